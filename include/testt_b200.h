@@ -1,0 +1,148 @@
+/*
+ * testt_b200 — C ABI of the B200 (sm_100a) kernels of the fused QLoRA hot path.
+ *
+ * Every entry point takes raw device pointers, 64-bit sizes, scalar parameters and a CUDA stream
+ * (passed as `void *`, a `cudaStream_t`; NULL means the legacy default stream). Nothing is
+ * allocated inside: the caller owns every buffer. Work is only enqueued; the call returns once
+ * the launch is queued. The return value is TB_OK (0) or a negative TB_E* code; the text of the
+ * last error on the calling host thread is returned by tb_last_error().
+ *
+ * fp16 tensors are passed as `uint16_t *` (IEEE binary16 bit patterns), so this header needs no
+ * CUDA include. Reference citations (file:line) are into the SalReII/testt repository.
+ */
+#ifndef TESTT_B200_H
+#define TESTT_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TB_OK 0
+#define TB_EINVAL (-1)   /* bad size, shape or missing required pointer            */
+#define TB_EALIGN (-2)   /* pointer alignment the kernel needs is not met           */
+#define TB_ELAUNCH (-3)  /* the CUDA launch (or a CUDA runtime call) failed         */
+#define TB_EDEVICE (-4)  /* the current device is not sm_100 / has no usable kernel */
+
+/* Text of the last error reported on this host thread ("" when none). */
+const char *tb_last_error(void);
+
+/* Library version, (major << 16) | (minor << 8) | patch. */
+int tb_version(void);
+
+/* ---------------------------------------------------------------------------------------------
+ * NF4 unpack (bitsandbytes 4-bit layout). Replaces nf4_unpack_kernel and its launch in
+ * unpack_into, solution/nf4.py:27-45 and :72-89.
+ *
+ *   nested:  absmax[b] = fp32(code2[absmax_u8[b]] * absmax2[b / qblock2]) + offset[0]
+ *   plain:   absmax[b] = absmax_f32[b]
+ *   out[2j]   = fp16(nf4[packed[j] >> 4]  * absmax[(2j) / qblock])   (high nibble first)
+ *   out[2j+1] = fp16(nf4[packed[j] & 15] * absmax[(2j) / qblock])
+ * Each product and sum is rounded on its own (no FMA), then rounded once to fp16, so the output
+ * is bit-exact with the reference for the same 16-entry nf4 table.
+ * qblock must be even; n_bytes counts packed bytes (= values / 2).
+ * ------------------------------------------------------------------------------------------- */
+int tb_nf4_unpack_nested(const uint8_t *packed, const uint8_t *absmax_u8, const float *code2,
+                         const float *absmax2, const float *offset, const float *nf4_table,
+                         uint16_t *out, int64_t n_bytes, int32_t qblock, int32_t qblock2,
+                         void *stream);
+
+int tb_nf4_unpack_plain(const uint8_t *packed, const float *absmax, const float *nf4_table,
+                        uint16_t *out, int64_t n_bytes, int32_t qblock, void *stream);
+
+/* One launch for up to TB_NF4_MAX_WEIGHTS weights (for example q|k|v or gate|up stacked into
+ * one GEMM operand). Replaces the per-weight loop of unpack_concat, solution/nf4.py:96-105.
+ * Arrays are HOST arrays of length n_weights. For weight i: absmax_f32[i] non-NULL selects the
+ * plain layout, else the nested fields (absmax_u8, code2, absmax2, offset, qblock2) are used. */
+#define TB_NF4_MAX_WEIGHTS 8
+int tb_nf4_unpack_multi(int32_t n_weights, const uint8_t *const *packed,
+                        const float *const *absmax_f32, const uint8_t *const *absmax_u8,
+                        const float *const *code2, const float *const *absmax2,
+                        const float *const *offset, const float *const *nf4_table,
+                        uint16_t *const *out, const int64_t *n_bytes, const int32_t *qblock,
+                        const int32_t *qblock2, void *stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Residual add + RMSNorm. Replaces rmsnorm_fwd_kernel / rmsnorm_bwd_kernel and their launches,
+ * solution/rmsnorm.py:24-69 and :76-112.
+ *
+ * forward, per row r of [rows, hidden]:
+ *   s = x (+ delta)           fp32, written to s_out only when delta != NULL
+ *   rstd = 1 / sqrt(sum(s*s) / hidden + eps)
+ *   y = fp16((s * rstd) * weight);  ypad[pad_idx[r]] = fp32 value of the same product
+ *   rstd_out[r] = rstd
+ * x fp32, delta fp16 (nullable), weight fp32, ypad fp32 [padded_rows, hidden] (nullable, together
+ * with pad_idx int64 [rows]). ypad rows that no pad_idx names are NOT touched (zero them first).
+ * ------------------------------------------------------------------------------------------- */
+int tb_add_rmsnorm_fwd(const float *x, const uint16_t *delta, const float *weight, float *s_out,
+                       uint16_t *y, float *ypad, const int64_t *pad_idx, float *rstd_out,
+                       int64_t rows, int64_t hidden, float eps, void *stream);
+
+/* backward, per row r:
+ *   g = (dy (+ dypad[pad_idx[r]])) * weight        dy fp16, dypad fp32; either may be NULL
+ *   n = s * rstd
+ *   dx = (g - n * sum(g*n) / hidden) * rstd (+ ds)  fp32 out; ddelta = fp16(dx) when non-NULL */
+int tb_add_rmsnorm_bwd(const float *s, const float *rstd, const float *weight, const uint16_t *dy,
+                       const float *dypad, const int64_t *pad_idx, const float *ds, float *dx,
+                       uint16_t *ddelta, int64_t rows, int64_t hidden, void *stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * QKV pack: LoRA add + rotary embedding + scatter into the padded attention layout. Replaces
+ * rope_pack_fwd_kernel / rope_pack_bwd_kernel and RopePack, solution/rope.py:24-128, :136-176.
+ *
+ * qkv fp16 [rows, (nh + 2 nkv) * d]; lora_q [rows, nh*d] and lora_v [rows, nkv*d] (nullable;
+ * lora_is_fp32 selects fp32, else fp16); cos/sin fp32 [seq, d]; pos_idx int64 [rows] (padded
+ * position b*seq + t of each token). Outputs q fp16 [batch, nh, seq, d], k/v [batch, nkv, seq, d].
+ *   q = rot(qkv_q + lq), k = rot(qkv_k), v = qkv_v + lv, rot(x)=(x1 c1 - x2 s1, x2 c2 + x1 s2)
+ * slot_tok (nullable) is int32 [batch*seq]: the token at each padded slot or -1. When given, the
+ * kernel covers every slot and writes the zero rows itself; when NULL it writes only the token
+ * rows and the caller must have zeroed q, k, v.
+ * ------------------------------------------------------------------------------------------- */
+int tb_rope_pack_fwd(const uint16_t *qkv, const void *lora_q, const void *lora_v,
+                     int32_t lora_is_fp32, const float *cos, const float *sin,
+                     const int64_t *pos_idx, const int32_t *slot_tok, uint16_t *q, uint16_t *k,
+                     uint16_t *v, int64_t rows, int64_t batch, int64_t seq, int32_t n_heads,
+                     int32_t n_kv, int32_t head_dim, void *stream);
+
+/* dqkv fp16 [rows, (nh + 2 nkv) * d] from dq/dk/dv fp16 in the padded layout (each nullable =
+ * zero gradient): inverse rotation (g1 c1 + g2 s2, g2 c2 - g1 s1) for q and k, copy for v. */
+int tb_rope_pack_bwd(const uint16_t *dq, const uint16_t *dk, const uint16_t *dv, const float *cos,
+                     const float *sin, const int64_t *pos_idx, uint16_t *dqkv, int64_t rows,
+                     int64_t batch, int64_t seq, int32_t n_heads, int32_t n_kv, int32_t head_dim,
+                     void *stream);
+
+/* slot_tok[b*seq+t] = token index at that padded slot, -1 for padding (the inverse of pos_idx).
+ * Helper for tb_rope_pack_fwd; a memset plus one scatter kernel. */
+int tb_slot_index(const int64_t *pos_idx, int64_t rows, int64_t slots, int32_t *slot_tok,
+                  void *stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Gated SiLU. Replaces gated_silu_fwd_kernel / gated_silu_bwd_inplace_kernel,
+ * solution/mlp.py:31-58 and :61-77.
+ *   gu fp16 [rows, 2*inter] = [gate | up];  act = fp16(gate / (1 + exp(-gate)) * up)
+ *   backward, IN PLACE over gu:  sig = 1/(1+exp(-g));  [g | u] <- [dact*u*sig*(1+g(1-sig)) |
+ *   dact*(g*sig)], dact fp16 [rows, inter].
+ * ------------------------------------------------------------------------------------------- */
+int tb_swiglu_fwd(const uint16_t *gu, uint16_t *act, int64_t rows, int64_t inter, void *stream);
+int tb_swiglu_bwd_inplace(const uint16_t *dact, uint16_t *gu, int64_t rows, int64_t inter,
+                          void *stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Vocabulary head statistics over a chunk of fp16 logits, IN PLACE. Replaces
+ * head_stats_grad_kernel, solution/head.py:34-76 (launch :108-110).
+ * logits fp16 [rows, vocab] with row stride ld (elements); targets int64 [rows] (-100 = none).
+ * Per row: lse, entropy = lse - sum(p z), loss = lse - z[target] (0 when unlabelled),
+ * correct = labelled & (first argmax == target); for labelled rows the logits are overwritten
+ * with fp16((exp(z - lse) - onehot) * grad_scale). Targets outside [0, vocab) other than -100
+ * are an error the caller must rule out (the row is then treated as unlabelled).
+ * ------------------------------------------------------------------------------------------- */
+int tb_head_stats_grad(uint16_t *logits, const int64_t *targets, float *entropy, float *loss,
+                       int32_t *correct, int64_t rows, int64_t vocab, int64_t ld,
+                       float grad_scale, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TESTT_B200_H */

@@ -1,0 +1,179 @@
+"""Eager-torch CPU restatements of the floating-point ops of the path. TEST INFRASTRUCTURE ONLY.
+
+Each function states the reference's arithmetic in fp32 (as its Triton kernel does), in the
+reference's operation order, on CPU tensors. The head is also given in fp64 (`head_stats_exact`)
+as the ground truth the loss/entropy tolerances are measured against.
+"""
+
+import torch
+
+IGNORE_INDEX = -100
+
+
+# ---- add + RMSNorm: solution/rmsnorm.py:24-69 --------------------------------------------------
+
+def add_rmsnorm_fwd(x, delta, w, eps, pad_idx=None, padded_rows=0):
+    """(s fp32, y fp16, ypad fp32, rstd fp32) — rmsnorm.py:31-43."""
+    s = x.float() + delta.float() if delta is not None else x.float()
+    hidden = s.shape[-1]
+    variance = (s * s).sum(-1) / hidden
+    rstd = 1.0 / torch.sqrt(variance + eps)
+    y32 = (s * rstd[:, None]) * w.float()
+    ypad = torch.zeros((padded_rows, hidden), dtype=torch.float32)
+    if pad_idx is not None:
+        ypad[pad_idx.long()] = y32
+    return s, y32.to(torch.float16), ypad, rstd
+
+
+def add_rmsnorm_bwd(s, rstd, w, pad_idx=None, ds=None, dy=None, dypad=None):
+    """(dx fp32, ddelta fp16) — rmsnorm.py:54-69."""
+    g = torch.zeros_like(s, dtype=torch.float32)
+    if dy is not None:
+        g = g + dy.float()
+    if dypad is not None and pad_idx is not None:
+        g = g + dypad.float()[pad_idx.long()]
+    g = g * w.float()
+    normed = s.float() * rstd[:, None]
+    proj = (g * normed).sum(-1) / s.shape[-1]
+    dx = (g - normed * proj[:, None]) * rstd[:, None]
+    if ds is not None:
+        dx = dx + ds.float()
+    return dx, dx.to(torch.float16)
+
+
+def add_rmsnorm_autograd_ref(x, delta, w, eps):
+    """The reference test's formula (solution/test_kernels.py:67-70), for autograd checks."""
+    s = x + delta.float() if delta is not None else x
+    return s, w * (s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + eps))
+
+
+# ---- QKV pack + RoPE: solution/rope.py:24-128 --------------------------------------------------
+
+def rope_tables(seq, head_dim, theta):
+    """cos/sin fp32 [seq, head_dim] as Qwen2's rotary embedding builds them."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim))
+    freqs = torch.arange(seq).float()[:, None] * inv[None]
+    emb = torch.cat([freqs, freqs], -1)
+    return emb.cos(), emb.sin()
+
+
+def rope_pack_fwd(qkv, lq, lv, cos, sin, pos_idx, batch, seq, nh, nkv, d):
+    """(q, k, v) fp16 in [batch, heads, seq, d], zeros at padding — rope.py:29-75."""
+    half = d // 2
+    x = qkv.float()
+    rows = x.shape[0]
+    fq = x[:, :nh * d].reshape(rows, nh, d)
+    fk = x[:, nh * d:(nh + nkv) * d].reshape(rows, nkv, d)
+    fv = x[:, (nh + nkv) * d:].reshape(rows, nkv, d)
+    if lq is not None:
+        fq = fq + lq.float().reshape(rows, nh, d)
+    if lv is not None:
+        fv = fv + lv.float().reshape(rows, nkv, d)
+    pos = pos_idx.long()
+    t = pos % seq
+    c1, c2 = cos[t, :half][:, None], cos[t, half:][:, None]
+    s1, s2 = sin[t, :half][:, None], sin[t, half:][:, None]
+
+    def rot(f):
+        x1, x2 = f[..., :half], f[..., half:]
+        return torch.cat([x1 * c1 - x2 * s1, x2 * c2 + x1 * s2], -1)
+
+    def scatter(f, heads):
+        out = torch.zeros(batch * seq, heads, d, dtype=torch.float32)
+        out[pos] = f
+        return out.view(batch, seq, heads, d).transpose(1, 2).contiguous().to(torch.float16)
+
+    return scatter(rot(fq), nh), scatter(rot(fk), nkv), scatter(fv, nkv)
+
+
+def rope_pack_bwd(dq, dk, dv, cos, sin, pos_idx, batch, seq, nh, nkv, d):
+    """dqkv fp16 [rows, (nh + 2 nkv) d] — rope.py:83-128."""
+    half = d // 2
+    pos = pos_idx.long()
+    rows = pos.numel()
+    t = pos % seq
+    b = pos // seq
+    c1, c2 = cos[t, :half][:, None], cos[t, half:][:, None]
+    s1, s2 = sin[t, :half][:, None], sin[t, half:][:, None]
+
+    def gather(g, heads):
+        if g is None:
+            return torch.zeros(rows, heads, d)
+        return g.float()[b, :, t, :]
+
+    def unrot(g):
+        g1, g2 = g[..., :half], g[..., half:]
+        return torch.cat([g1 * c1 + g2 * s2, g2 * c2 - g1 * s1], -1)
+
+    gq, gk, gv = gather(dq, nh), gather(dk, nkv), gather(dv, nkv)
+    out = torch.cat([unrot(gq).reshape(rows, -1), unrot(gk).reshape(rows, -1),
+                     gv.reshape(rows, -1)], -1)
+    return out.to(torch.float16)
+
+
+# ---- gated SiLU: solution/mlp.py:31-58 --------------------------------------------------------
+
+def swiglu_fwd(gu):
+    """act fp16 = fp16(g / (1 + exp(-g)) * u) — mlp.py:36-40."""
+    inter = gu.shape[1] // 2
+    g, u = gu[:, :inter].float(), gu[:, inter:].float()
+    return (g / (1.0 + torch.exp(-g)) * u).to(torch.float16)
+
+
+def swiglu_bwd(dact, gu):
+    """[dg | du] fp16 — mlp.py:50-58."""
+    inter = gu.shape[1] // 2
+    g, u = gu[:, :inter].float(), gu[:, inter:].float()
+    dact = dact.float()
+    sig = 1.0 / (1.0 + torch.exp(-g))
+    d_silu = dact * u
+    dg = d_silu * sig * (1.0 + g * (1.0 - sig))
+    du = dact * (g * sig)
+    return torch.cat([dg, du], 1).to(torch.float16)
+
+
+# ---- head: solution/head.py:34-137 -------------------------------------------------------------
+
+def head_stats_exact(logits16, targets, grad_scale):
+    """Per row (entropy, loss, correct, dlogits fp16) from fp16 logits, in fp64 (the exact values
+    the reference's online fp32 sweep approximates, head.py:54-76)."""
+    z = logits16.double()
+    lse = torch.logsumexp(z, -1)
+    p = torch.exp(z - lse[:, None])
+    entropy = lse - (p * z).sum(-1)
+    tgt = targets.long()
+    labelled = tgt != IGNORE_INDEX
+    safe = torch.where(labelled, tgt, torch.zeros_like(tgt))
+    zt = z.gather(1, safe[:, None]).squeeze(1)
+    loss = torch.where(labelled, lse - zt, torch.zeros_like(lse))
+    # first argmax: torch.argmax returns the first maximal index
+    correct = labelled & (z.argmax(-1) == tgt)
+    onehot = torch.zeros_like(z)
+    onehot[torch.arange(z.shape[0])[labelled], tgt[labelled]] = 1.0
+    grad = ((p - onehot) * grad_scale).to(torch.float16)
+    dlogits = torch.where(labelled[:, None], grad, logits16)
+    return entropy, loss, correct, dlogits
+
+
+def grad_unit(denominator):
+    """head.py:79-84."""
+    import math
+
+    exponent = int(round(math.log2(max(float(denominator), 1e-6)))) + 6
+    return float(2 ** max(0, min(16, exponent)))
+
+
+def fused_head_loss(h16, w16, targets, denominator):
+    """(loss, entropy, token_loss, correct, dh fp16 [rows, hidden] for a unit gradient of the
+    loss) — the chunked algorithm of head.py:89-137 on the CPU: logits rounded to fp16 as the
+    fp16 GEMM does, statistics in fp64, dlogits in fp16, dh = fp16(dlogits @ W) * (1/unit)."""
+    logits = (h16.float() @ w16.float().t()).to(torch.float16)
+    denom = float(denominator)
+    unit = grad_unit(denom)
+    entropy, token_loss, correct, dlogits = head_stats_exact(logits, targets, unit / denom)
+    labelled = targets.long() != IGNORE_INDEX
+    dh16 = (dlogits.float() @ w16.float()).to(torch.float16)
+    dh16[~labelled] = 0
+    dh = (dh16.float() * (1.0 / unit)).to(torch.float16)
+    loss = token_loss.sum() / denom
+    return loss, entropy, token_loss, correct, dh

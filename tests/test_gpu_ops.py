@@ -1,0 +1,370 @@
+"""CUDA kernels (through the C ABI and the op wrappers) against the reference's golden outputs
+and the CPU oracle, at the fixtures' small shapes and at the benchmark configurations' full
+shapes, plus the edge cases the reference's tests and layouts allow."""
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_bitexact, assert_rel, assert_ulp, golden, nf4_weight, t
+from oracle import cnf4, ops, synth
+from oracle import nf4 as onf4
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+# ---- NF4 unpack --------------------------------------------------------------------------------
+
+def _golden_weights(g):
+    ws = []
+    i = 0
+    while f"w{i}_packed" in g:
+        ws.append(dict(packed=g[f"w{i}_packed"], absmax=g[f"w{i}_absmax"],
+                       code2=g[f"w{i}_code2"], absmax2=g[f"w{i}_absmax2"],
+                       offset=g[f"w{i}_offset"], table=g["table"], nested=True,
+                       blocksize=int(g["blocksize"]), blocksize2=int(g["blocksize2"]),
+                       shape=g[f"w{i}_shape"]))
+        i += 1
+    return ws
+
+
+def test_nf4_nested_golden_stacked():
+    from testt_b200.nf4 import supports_fast_unpack, unpack_concat
+
+    g = golden("nf4_nested")
+    ws = [nf4_weight(q, DEV) for q in _golden_weights(g)]
+    assert all(supports_fast_unpack(w) for w in ws)
+    out = unpack_concat(ws, torch.device(DEV))
+    assert_bitexact(out.reshape(-1), g["out"].reshape(-1), "stacked nested unpack")
+
+
+def test_nf4_plain_golden():
+    from testt_b200.nf4 import unpack_into
+
+    g = golden("nf4_plain")
+    q = dict(packed=g["packed"], absmax=g["absmax"], table=g["table"], nested=False,
+             blocksize=int(g["blocksize"]), shape=g["shape"])
+    out = torch.empty(tuple(int(v) for v in g["shape"]), dtype=torch.float16, device=DEV)
+    unpack_into(nf4_weight(q, DEV), out)
+    assert_bitexact(out.reshape(-1), g["out"].reshape(-1), "plain unpack")
+
+
+@pytest.mark.parametrize("nested", [False, True])
+def test_nf4_config1_full_size_bitexact(nested):
+    """Config 1: the [8960, 1536] gate_proj weight, blocksize 64 (plain fp32 absmax is the
+    configuration's layout; nested is the reference's)."""
+    from testt_b200.nf4 import unpack_into
+
+    w = synth.config1_weight("cpu").numpy()
+    q = onf4.quantize(w, blocksize=64, nested=nested)
+    out = torch.empty(w.shape, dtype=torch.float16, device=DEV)
+    unpack_into(nf4_weight(q, DEV), out)
+    assert_bitexact(out.reshape(-1), cnf4.unpack(q), "config 1")
+
+
+@pytest.mark.parametrize("shape,blocksize", [((3, 10), 2), ((5, 6), 6), ((7, 64), 32),
+                                             ((1, 2), 2), ((130, 64), 128)])
+def test_nf4_odd_sizes_and_blocksizes(shape, blocksize):
+    """Sizes whose byte count is not a multiple of 4 or whose block is not a multiple of 8
+    values take the byte-granular kernel; results stay bit-exact."""
+    from testt_b200.nf4 import unpack_concat
+
+    rng = np.random.default_rng(sum(shape) + blocksize)
+    w = (rng.standard_normal(shape) * 0.05).astype(np.float16)
+    qs = [onf4.quantize(w, blocksize=blocksize, nested=n, blocksize2=4) for n in (False, True)]
+    out = unpack_concat([nf4_weight(q, DEV) for q in qs], torch.device(DEV))
+    ref = np.concatenate([cnf4.unpack(q) for q in qs])
+    assert_bitexact(out.reshape(-1), ref, f"{shape} bs{blocksize}")
+
+
+def test_nf4_more_weights_than_one_launch_and_misaligned_output():
+    from testt_b200 import nf4
+
+    rng = np.random.default_rng(7)
+    qs = [onf4.quantize((rng.standard_normal((rows, 64)) * 0.02).astype(np.float16), 64,
+                        nested=bool(i % 2)) for i, rows in enumerate([3, 8, 1, 5, 2, 9, 4, 6, 7,
+                                                                        2, 3])]
+    out = nf4.unpack_concat([nf4_weight(q, DEV) for q in qs], torch.device(DEV))
+    ref = np.concatenate([cnf4.unpack(q) for q in qs])
+    assert_bitexact(out.reshape(-1), ref, "11 weights")
+    # an output view that starts 2 bytes past a 16-byte boundary
+    buf = torch.empty(64 * 3 + 1, dtype=torch.float16, device=DEV)
+    view = buf[1:].view(3, 64)
+    nf4.unpack_into(nf4_weight(qs[0], DEV), view)
+    assert_bitexact(view.reshape(-1), cnf4.unpack(qs[0]), "misaligned out")
+
+
+def test_nf4_rejects_bad_blocksize_and_cpu_tensors():
+    from testt_b200 import _lib
+    from testt_b200.nf4 import unpack_into
+
+    packed = torch.zeros(16, dtype=torch.uint8, device=DEV)
+    absmax = torch.ones(16, device=DEV)
+    table = torch.zeros(16, device=DEV)
+    out = torch.empty(32, dtype=torch.float16, device=DEV)
+    with pytest.raises(_lib.KernelError, match="blocksize"):
+        _lib.call("tb_nf4_unpack_plain", _lib.ptr(packed), _lib.ptr(absmax), _lib.ptr(table),
+                  _lib.ptr(out), 16, 3, _lib.stream_of(out))
+    q = onf4.quantize(np.zeros((2, 64), np.float16), 64)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        unpack_into(nf4_weight(q, "cpu"), torch.empty(2, 64, dtype=torch.float16))
+
+
+# ---- add + RMSNorm -----------------------------------------------------------------------------
+
+@pytest.mark.parametrize("tag", ["dp", "d", "p", "wide"])
+def test_rmsnorm_golden(tag):
+    from testt_b200.rmsnorm import add_rmsnorm
+
+    g = golden(f"rmsnorm_{tag}")
+    x = t(g["x"], DEV).requires_grad_(True)
+    delta = t(g["delta"], DEV).requires_grad_(True) if "delta" in g else None
+    pad_idx = t(g["pad_idx"], DEV) if "pad_idx" in g else None
+    s, y, ypad = add_rmsnorm(x, delta, t(g["w"], DEV), 1e-6, pad_idx, int(g["padded_rows"]))
+    assert_ulp(y, g["y"], 1, "y")
+    if delta is not None:
+        assert np.array_equal(s.detach().cpu().numpy(), g["s"])
+    if pad_idx is not None:
+        assert_rel(ypad, g["ypad"], 1e-5, "ypad")
+    outs = [y] + ([ypad] if pad_idx is not None else []) + ([s] if delta is not None else [])
+    grads = [t(g["gy"], DEV)] + ([t(g["gpad"], DEV)] if pad_idx is not None else []) + \
+        ([t(g["gs"], DEV)] if delta is not None else [])
+    torch.autograd.backward(outs, grads)
+    assert_rel(x.grad, g["dx"], 1e-3, "dx")
+    if delta is not None:
+        assert_ulp(delta.grad, g["ddelta"], 1, "ddelta")
+
+
+def test_rmsnorm_config2_full_size():
+    from testt_b200 import rmsnorm
+
+    c = synth.config2("cpu")
+    cu = {k: (v.to(DEV) if torch.is_tensor(v) else v) for k, v in c.items()}
+    s, y, ypad, rstd = rmsnorm._launch_fwd(cu["x"], cu["delta"], cu["weight"], c["eps"],
+                                           cu["pad_idx"], c["padded_rows"])
+    rs, ry, rypad, rrstd = ops.add_rmsnorm_fwd(c["x"], c["delta"], c["weight"], c["eps"],
+                                               c["pad_idx"], c["padded_rows"])
+    assert torch.equal(s.cpu(), rs)
+    assert_ulp(y, ry, 1, "y")
+    assert_rel(ypad, rypad, 1e-5, "ypad")
+    assert_rel(rstd, rrstd, 1e-6, "rstd")
+    dx, ddelta = rmsnorm._launch_bwd(s, rstd, cu["weight"], cu["pad_idx"], cu["ds"], cu["dy"],
+                                     cu["dypad"], True)
+    rdx, rdd = ops.add_rmsnorm_bwd(rs, rrstd, c["weight"], c["pad_idx"], c["ds"], c["dy"],
+                                   c["dypad"])
+    assert_rel(dx, rdx, 1e-3, "dx")
+    assert_ulp(ddelta, rdd, 1, "ddelta")
+
+
+@pytest.mark.parametrize("rows,hidden", [(0, 1536), (1, 1536), (3, 100), (5, 4104), (2, 8)])
+def test_rmsnorm_edge_shapes(rows, hidden):
+    """Empty input, a single row, hidden sizes that are not a multiple of 8 (element kernel) and
+    wider than one chunk per thread."""
+    from testt_b200.rmsnorm import add_rmsnorm
+
+    gen = torch.Generator().manual_seed(rows * 7 + hidden)
+    x = torch.randn(rows, hidden, generator=gen)
+    d = torch.randn(rows, hidden, generator=gen).half()
+    w = torch.rand(hidden, generator=gen) + 0.5
+    pad = torch.randperm(rows + 3, generator=gen)[:rows]
+    s, y, ypad = add_rmsnorm(x.to(DEV), d.to(DEV), w.to(DEV), 1e-6, pad.to(DEV), rows + 3)
+    rs, ry, rypad, _ = ops.add_rmsnorm_fwd(x, d, w, 1e-6, pad, rows + 3)
+    assert_ulp(y, ry, 1, "y")
+    assert_rel(ypad, rypad, 1e-5, "ypad")
+
+
+# ---- gated SiLU --------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("tag", ["odd", "vec"])
+def test_swiglu_golden(tag):
+    from testt_b200.mlp import gated_silu, gated_silu_backward_
+
+    g = golden(f"swiglu_{tag}")
+    gu = t(g["gu"], DEV)
+    assert_ulp(gated_silu(gu), g["act"], 1, "act")
+    out = gated_silu_backward_(t(g["dact"], DEV), gu.clone())
+    assert_ulp(out, g["dgu"], 1, "dgu")
+
+
+def test_swiglu_config3_full_size():
+    from testt_b200.mlp import gated_silu, gated_silu_backward_
+
+    c = synth.config3("cpu")
+    gu = c["gu"].to(DEV)
+    assert_ulp(gated_silu(gu), ops.swiglu_fwd(c["gu"]), 1, "act")
+    work = gu.clone()
+    ret = gated_silu_backward_(c["dact"].to(DEV), work)
+    assert ret.data_ptr() == work.data_ptr(), "backward is in place"
+    assert_ulp(work, ops.swiglu_bwd(c["dact"], c["gu"]), 1, "dgu")
+
+
+def test_swiglu_empty_and_extreme_values():
+    from testt_b200.mlp import gated_silu, gated_silu_backward_
+
+    assert gated_silu(torch.empty(0, 16, dtype=torch.float16, device=DEV)).shape == (0, 8)
+    vals = torch.tensor([-65504.0, -100.0, -20.0, -1.0, 0.0, 1.0, 20.0, 65504.0],
+                        dtype=torch.float16)
+    gu = torch.cat([vals, torch.ones(8, dtype=torch.float16)]).reshape(1, 16)
+    assert_ulp(gated_silu(gu.to(DEV)), ops.swiglu_fwd(gu), 1, "act extremes")
+    d = torch.full((1, 8), 0.01, dtype=torch.float16)
+    assert_ulp(gated_silu_backward_(d.to(DEV), gu.to(DEV).clone()), ops.swiglu_bwd(d, gu), 1,
+               "dgu extremes")
+
+
+# ---- QKV pack + RoPE ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("tag", ["small", "d128"])
+def test_rope_golden(tag):
+    from testt_b200.rope import rope_pack
+
+    g = golden(f"rope_{tag}")
+    batch, seq, nh, nkv, d = [int(v) for v in g["dims"]]
+    qkv = t(g["qkv"], DEV).requires_grad_(True)
+    lq = t(g["lq"], DEV).requires_grad_(True)
+    lv = t(g["lv"], DEV).requires_grad_(True)
+    q, k, v = rope_pack(qkv, lq, lv, t(g["cos"], DEV), t(g["sin"], DEV), t(g["pos_idx"], DEV),
+                        batch, seq, nh, nkv, d)
+    for name, got in (("q", q), ("k", k), ("v", v)):
+        assert_ulp(got, g[name], 1, name)
+    torch.autograd.backward([q, k, v], [t(g["gq"], DEV), t(g["gk"], DEV), t(g["gv"], DEV)])
+    assert_ulp(qkv.grad, g["dqkv"], 1, "dqkv")
+    q_cols, v_start = nh * d, (nh + nkv) * d
+    assert_ulp(lq.grad.half(), g["dqkv"][:, :q_cols], 1, "dlq")
+    assert_ulp(lv.grad.half(), g["dqkv"][:, v_start:], 1, "dlv")
+
+
+@pytest.mark.parametrize("lora", ["fp32", "fp16", "none"])
+def test_rope_config3_full_size(lora):
+    from testt_b200.rope import RopePack, slot_index
+
+    c = synth.config3("cpu")
+    dims = (c["batch"], c["seq"], synth.N_HEADS, synth.N_KV, synth.HEAD_DIM)
+    lq = None if lora == "none" else c["lora_q"].to(getattr(torch, {"fp32": "float32",
+                                                                     "fp16": "float16"}[lora]))
+    lv = None if lora == "none" else c["lora_v"].to(lq.dtype)
+    dev = lambda x: None if x is None else x.to(DEV)  # noqa: E731
+    q, k, v = RopePack.apply(dev(c["qkv"]), dev(lq), dev(lv), dev(c["cos"]), dev(c["sin"]),
+                             dev(c["pos_idx"]), *dims, None)
+    rq, rk, rv = ops.rope_pack_fwd(c["qkv"], lq, lv, c["cos"], c["sin"], c["pos_idx"], *dims)
+    for name, got, ref in (("q", q, rq), ("k", k, rk), ("v", v, rv)):
+        assert_ulp(got, ref, 1, name)
+    slot = slot_index(dev(c["pos_idx"]), c["batch"] * c["seq"])
+    assert int((slot >= 0).sum()) == c["rows"]
+    from testt_b200 import _lib
+
+    dqkv = torch.empty_like(dev(c["qkv"]))
+    _lib.call("tb_rope_pack_bwd", _lib.ptr(dev(c["dq"])), _lib.ptr(dev(c["dk"])),
+              _lib.ptr(dev(c["dv"])), _lib.ptr(dev(c["cos"])), _lib.ptr(dev(c["sin"])),
+              _lib.ptr(dev(c["pos_idx"])), _lib.ptr(dqkv), c["rows"], c["batch"], c["seq"],
+              synth.N_HEADS, synth.N_KV, synth.HEAD_DIM, _lib.stream_of(dqkv))
+    ref = ops.rope_pack_bwd(c["dq"], c["dk"], c["dv"], c["cos"], c["sin"], c["pos_idx"], *dims)
+    assert_ulp(dqkv, ref, 1, "dqkv")
+
+
+def test_rope_unsorted_positions_and_token_grid():
+    """Positions in any order (and left padding): the slot map and the token-grid launch both
+    give the oracle's layout, zeros included."""
+    from testt_b200 import _lib
+    from testt_b200.rope import rope_pack
+
+    gen = torch.Generator().manual_seed(3)
+    batch, seq, nh, nkv, d = 3, 11, 4, 2, 64
+    pos = torch.randperm(batch * seq, generator=gen)[:17]
+    rows = pos.numel()
+    qkv = torch.randn(rows, (nh + 2 * nkv) * d, generator=gen).half()
+    lq = torch.randn(rows, nh * d, generator=gen).half()
+    lv = torch.randn(rows, nkv * d, generator=gen).half()
+    cos, sin = ops.rope_tables(seq, d, 1e6)
+    ref = ops.rope_pack_fwd(qkv, lq, lv, cos, sin, pos, batch, seq, nh, nkv, d)
+    got = rope_pack(qkv.to(DEV), lq.to(DEV), lv.to(DEV), cos.to(DEV), sin.to(DEV), pos.to(DEV),
+                    batch, seq, nh, nkv, d)
+    for a, b in zip(got, ref):
+        assert_ulp(a, b, 1, "slot grid")
+    outs = [torch.zeros(batch, h, seq, d, dtype=torch.float16, device=DEV) for h in (nh, nkv, nkv)]
+    _lib.call("tb_rope_pack_fwd", _lib.ptr(qkv.to(DEV)), _lib.ptr(lq.to(DEV)),
+              _lib.ptr(lv.to(DEV)), 0, _lib.ptr(cos.to(DEV)), _lib.ptr(sin.to(DEV)),
+              _lib.ptr(pos.to(DEV)), None, *[_lib.ptr(o) for o in outs], rows, batch, seq, nh,
+              nkv, d, _lib.stream_of(outs[0]))
+    torch.cuda.synchronize()
+    for a, b in zip(outs, ref):
+        assert_ulp(a, b, 1, "token grid")
+
+
+# ---- vocab head --------------------------------------------------------------------------------
+
+def test_head_stats_golden():
+    from testt_b200.head import head_stats_grad
+
+    g = golden("head_stats")
+    logits = t(g["logits"], DEV)
+    ent, loss, correct = head_stats_grad(logits, t(g["targets"], DEV), float(g["grad_scale"]))
+    assert_rel(loss, g["loss"], 1e-4, "loss", floor=0.0)
+    assert_rel(ent, g["entropy"], 1e-4, "entropy", floor=0.0)
+    assert np.array_equal(correct.cpu().numpy(), g["correct"])
+    assert_ulp(logits, g["dlogits"], 1, "dlogits in place")
+
+
+def test_head_loss_golden():
+    from testt_b200.head import fused_head_loss
+
+    g = golden("head_loss")
+    h = t(g["h"], DEV).requires_grad_(True)
+    loss, ent, tok, correct = fused_head_loss(h, t(g["w"], DEV), t(g["targets"], DEV),
+                                              t(g["denom"], DEV))
+    assert_rel(loss, g["loss"], 1e-4, "loss", floor=0.0)
+    assert_rel(ent, g["entropy"], 1e-4, "entropy", floor=0.0)
+    assert_rel(tok, g["token_loss"], 1e-4, "token loss", floor=0.0)
+    assert np.array_equal(correct.cpu().numpy(), g["correct"])
+    (loss * 1024.0).backward()
+    assert_rel(h.grad, g["dh"], 2e-2, "dh")
+
+
+def test_head_stats_config4_rows_vs_oracle():
+    """Config 4 vocabulary (151936) on 64 rows: the stats kernel over the fp16 logits against the
+    fp64 oracle; dlogits within 1 ulp."""
+    from testt_b200.head import _grad_unit, head_stats_grad
+
+    c = synth.config4("cpu", rows=64)
+    logits = (c["hidden"].float() @ c["weight"].float().t()).half()
+    scale = _grad_unit(c["n_labelled"]) / c["n_labelled"]
+    work = logits.to(DEV)
+    ent, loss, correct = head_stats_grad(work, c["targets"].to(DEV), scale)
+    rent, rloss, rcorrect, rdl = ops.head_stats_exact(logits, c["targets"], scale)
+    assert_rel(loss, rloss, 1e-4, "loss", floor=0.0)
+    assert_rel(ent, rent, 1e-4, "entropy", floor=0.0)
+    assert torch.equal(correct.cpu().bool(), rcorrect)
+    assert_ulp(work, rdl, 1, "dlogits")
+
+
+def test_head_full_config4_properties():
+    """Config 4 at full size (2048 rows, 1331 labelled): the fused head against an fp32 torch
+    computation of the same fp16 logits on the GPU; loss/entropy rtol 1e-4, hits exact."""
+    from testt_b200.head import fused_head_loss
+
+    c = synth.config4(DEV)
+    w, h, tg = c["weight"], c["hidden"], c["targets"]
+    hh = h.clone().requires_grad_(True)
+    denom = c["n_labelled"]
+    loss, ent, tok, correct = fused_head_loss(hh, w, tg, denom)
+    rows = h.shape[0]
+    r_ent = torch.empty(rows, device=DEV, dtype=torch.float64)
+    r_tok = torch.empty(rows, device=DEV, dtype=torch.float64)
+    r_cor = torch.empty(rows, device=DEV, dtype=torch.bool)
+    for s in range(0, rows, 256):
+        z = (h[s:s + 256] @ w.t()).double()
+        lse = torch.logsumexp(z, -1)
+        p = torch.exp(z - lse[:, None])
+        r_ent[s:s + 256] = lse - (p * z).sum(-1)
+        tt = tg[s:s + 256]
+        lab = tt != -100
+        zt = z.gather(1, torch.where(lab, tt, 0)[:, None]).squeeze(1)
+        r_tok[s:s + 256] = torch.where(lab, lse - zt, 0)
+        r_cor[s:s + 256] = lab & (z.argmax(-1) == tt)
+    assert_rel(ent, r_ent, 1e-4, "entropy", floor=0.0)
+    assert_rel(tok, r_tok, 1e-4, "token loss", floor=0.0)
+    assert torch.equal(correct, r_cor)
+    assert_rel(loss, r_tok.sum() / denom, 1e-4, "loss", floor=0.0)
+    loss.backward()
+    assert hh.grad is not None and torch.isfinite(hh.grad.float()).all()
+    assert int((hh.grad[tg == -100] != 0).sum()) == 0, "unlabelled rows get no gradient"

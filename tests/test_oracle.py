@@ -1,0 +1,125 @@
+"""The CPU oracle against the reference's own outputs (tests/golden, made by running the
+reference's Triton kernels through Triton's interpreter). No GPU needed."""
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_bitexact, assert_rel, assert_ulp, golden, t
+from oracle import cnf4, ops
+from oracle import nf4 as onf4
+
+
+def _weights(g):
+    ws = []
+    i = 0
+    while f"w{i}_packed" in g:
+        ws.append(dict(packed=g[f"w{i}_packed"], absmax=g[f"w{i}_absmax"],
+                       code2=g[f"w{i}_code2"], absmax2=g[f"w{i}_absmax2"],
+                       offset=g[f"w{i}_offset"], table=g["table"], nested=True,
+                       blocksize=int(g["blocksize"]), blocksize2=int(g["blocksize2"])))
+        i += 1
+    return ws
+
+
+def test_nf4_nested_oracle_is_bitexact_with_reference():
+    g = golden("nf4_nested")
+    ws = _weights(g)
+    got = np.concatenate([onf4.dequantize(q) for q in ws])
+    assert_bitexact(got, g["out"].reshape(-1), "numpy oracle")
+    got_c = np.concatenate([cnf4.unpack(q) for q in ws])
+    assert_bitexact(got_c, g["out"].reshape(-1), "C oracle")
+
+
+def test_nf4_plain_oracle_is_bitexact_with_reference():
+    g = golden("nf4_plain")
+    q = dict(packed=g["packed"], absmax=g["absmax"], table=g["table"], nested=False,
+             blocksize=int(g["blocksize"]))
+    assert_bitexact(onf4.dequantize(q), g["out"].reshape(-1), "numpy oracle")
+    assert_bitexact(cnf4.unpack(q), g["out"].reshape(-1), "C oracle")
+
+
+def test_nf4_quantiser_round_trip():
+    rng = np.random.default_rng(0)
+    w = (rng.standard_normal((64, 256)) * 0.02).astype(np.float16)
+    for nested in (False, True):
+        q = onf4.quantize(w, blocksize=64, nested=nested)
+        back = onf4.dequantize(q).astype(np.float32).reshape(w.shape)
+        # NF4 has 16 levels: the reconstruction error is bounded by half the widest level gap
+        # times the block absmax (plus the nested absmax error).
+        amax = np.abs(w.astype(np.float32)).reshape(-1, 64).max(1)
+        err = np.abs(back - w.astype(np.float32)).reshape(-1, 64).max(1)
+        assert (err <= amax * 0.2 + 1e-3).all()
+        assert_bitexact(cnf4.unpack(q), onf4.dequantize(q), "C vs numpy")
+
+
+def test_nf4_table_is_normalfloat():
+    tab = onf4.nf4_code_table()
+    assert tab.shape == (16,) and tab[0] == -1.0 and tab[-1] == 1.0 and tab[7] == 0.0
+    assert np.all(np.diff(tab) > 0)
+
+
+@pytest.mark.parametrize("tag", ["dp", "d", "p", "wide"])
+def test_rmsnorm_oracle_matches_reference(tag):
+    g = golden(f"rmsnorm_{tag}")
+    x, w = t(g["x"]), t(g["w"])
+    delta = t(g["delta"]) if "delta" in g else None
+    pad_idx = t(g["pad_idx"]) if "pad_idx" in g else None
+    padded = int(g["padded_rows"])
+    s, y, ypad, rstd = ops.add_rmsnorm_fwd(x, delta, w, 1e-6, pad_idx, padded)
+    assert_ulp(y, g["y"], 1, "y")
+    if delta is not None:
+        assert np.array_equal(s.numpy(), g["s"]), "s = x + delta is one fp32 add"
+    if pad_idx is not None:
+        assert_rel(ypad, g["ypad"], 1e-5, "ypad")
+    dx, ddelta = ops.add_rmsnorm_bwd(
+        s, rstd, w, pad_idx, ds=t(g["gs"]) if "gs" in g else None, dy=t(g["gy"]),
+        dypad=t(g["gpad"]) if "gpad" in g else None)
+    assert_rel(dx, g["dx"], 1e-3, "dx")
+    if "ddelta" in g:
+        assert_ulp(ddelta, g["ddelta"], 1, "ddelta")
+
+
+@pytest.mark.parametrize("tag", ["odd", "vec"])
+def test_swiglu_oracle_matches_reference(tag):
+    g = golden(f"swiglu_{tag}")
+    gu = t(g["gu"])
+    assert_ulp(ops.swiglu_fwd(gu), g["act"], 1, "act")
+    assert_ulp(ops.swiglu_bwd(t(g["dact"]), gu), g["dgu"], 1, "dgu")
+
+
+@pytest.mark.parametrize("tag", ["small", "d128"])
+def test_rope_oracle_matches_reference(tag):
+    g = golden(f"rope_{tag}")
+    batch, seq, nh, nkv, d = [int(v) for v in g["dims"]]
+    args = (t(g["cos"]), t(g["sin"]), t(g["pos_idx"]), batch, seq, nh, nkv, d)
+    q, k, v = ops.rope_pack_fwd(t(g["qkv"]), t(g["lq"]), t(g["lv"]), *args)
+    for name, got in (("q", q), ("k", k), ("v", v)):
+        assert_ulp(got, g[name], 1, name)
+    dqkv = ops.rope_pack_bwd(t(g["gq"]), t(g["gk"]), t(g["gv"]), *args)
+    assert_ulp(dqkv, g["dqkv"], 1, "dqkv")
+
+
+def test_head_stats_oracle_matches_reference():
+    g = golden("head_stats")
+    ent, loss, correct, dlogits = ops.head_stats_exact(t(g["logits"]), t(g["targets"]),
+                                                       float(g["grad_scale"]))
+    assert_rel(loss, g["loss"], 1e-4, "loss", floor=0.0)
+    assert_rel(ent, g["entropy"], 1e-4, "entropy", floor=0.0)
+    assert np.array_equal(correct.numpy().astype(np.int32), g["correct"])
+    assert_ulp(dlogits, g["dlogits"], 1, "dlogits")
+    # the tie rows: the first argmax decides
+    assert g["correct"][5] == 0 and g["correct"][6] == 1
+
+
+def test_head_loss_oracle_matches_reference():
+    g = golden("head_loss")
+    loss, ent, tok, correct, dh = ops.fused_head_loss(t(g["h"]), t(g["w"]), t(g["targets"]),
+                                                      int(g["denom"]))
+    assert_rel(loss, g["loss"], 1e-4, "loss", floor=0.0)
+    assert_rel(ent, g["entropy"], 1e-4, "entropy", floor=0.0)
+    assert_rel(tok, g["token_loss"], 1e-4, "token loss", floor=0.0)
+    assert np.array_equal(correct.numpy(), g["correct"])
+    # the golden dh is the gradient of loss * 1024
+    ref_dh = torch.from_numpy(g["dh"]).float()
+    assert_rel(dh.float() * 1024.0, ref_dh, 2e-2, "dh")

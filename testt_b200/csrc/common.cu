@@ -1,0 +1,43 @@
+// C-ABI error reporting and device queries shared by every kernel file.
+#include <cstring>
+
+#include "common.cuh"
+
+namespace tb {
+
+static thread_local char g_last_error[512] = "";
+
+int set_error(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char *what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    return set_error(TB_ELAUNCH, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  }
+  return TB_OK;
+}
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+}  // namespace tb
+
+extern "C" const char *tb_last_error(void) { return tb::g_last_error; }
+
+extern "C" int tb_version(void) { return (0 << 16) | (1 << 8) | 0; }

@@ -1,0 +1,395 @@
+// QKV pack: LoRA add + rotary embedding + scatter into the padded [batch, heads, seq, d] layout,
+// forward and backward, for sm_100a.
+//
+// Reference: solution/rope.py:24-75 (rope_pack_fwd_kernel), :78-128 (rope_pack_bwd_kernel),
+// :136-176 (RopePack). One warp per token (backward) or per padded slot (forward with a slot map).
+// Lane l owns 8 consecutive dims d0..d0+7 of one head half and the matching dims of the other
+// half (the rotation pairs x[d] with x[d + d/2]), so the cos/sin values of the slot are loaded
+// once per lane and reused for every head; all loads and stores are 16-byte vectors. With a slot
+// map (slot_tok) the forward kernel covers every padded slot and writes the zero rows of padding
+// itself, which removes the three zero-fills of the outputs the reference does before its launch
+// (solution/rope.py:141-143).
+#include "common.cuh"
+
+namespace tb {
+namespace {
+
+constexpr int kWarpsPerBlock = 4;
+
+struct RopeDims {
+  int64_t rows, batch, seq;
+  int nh, nkv, d, half;
+};
+
+template <bool kLoraFp32>
+__device__ __forceinline__ void load8_lora(const void *p, int64_t idx, float (&f)[8]) {
+  if (kLoraFp32) {
+    load8f(static_cast<const float *>(p) + idx, f);
+  } else {
+    load8h(static_cast<const uint16_t *>(p) + idx, f);
+  }
+}
+
+__device__ __forceinline__ void zero8(float (&f)[8]) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) f[k] = 0.f;
+}
+
+// kSlots: one warp per padded slot, tokens found through slot_tok, padding rows zero-filled.
+template <bool kSlots, bool kLoraFp32>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+    rope_fwd_vec(const uint16_t *__restrict__ qkv, const void *__restrict__ lq,
+                 const void *__restrict__ lv, const float *__restrict__ cosv,
+                 const float *__restrict__ sinv, const int64_t *__restrict__ pos_idx,
+                 const int32_t *__restrict__ slot_tok, uint16_t *__restrict__ q,
+                 uint16_t *__restrict__ k, uint16_t *__restrict__ v, RopeDims dm) {
+  const int lane = threadIdx.x & 31;
+  const int64_t unit = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int64_t slots = dm.batch * dm.seq;
+  int64_t tok, pos;
+  if (kSlots) {
+    if (unit >= slots) return;
+    pos = unit;
+    tok = __ldg(slot_tok + unit);
+  } else {
+    if (unit >= dm.rows) return;
+    tok = unit;
+    pos = __ldg(pos_idx + unit);
+    if (pos < 0 || pos >= slots) return;  // out-of-range position: nothing to write
+  }
+  const int64_t b = pos / dm.seq, t = pos % dm.seq;
+  const int D = dm.d, H = dm.half;
+  const int lph = H / 8;            // lanes per head
+  const int hps = 32 / lph;         // heads per warp step
+  const int hsub = lane / lph;
+  const int d0 = (lane % lph) * 8;
+  const int total = dm.nh + 2 * dm.nkv;
+  if (hsub >= hps) return;
+  const bool real = !kSlots || (tok >= 0 && tok < dm.rows);
+
+  float c1[8], c2[8], s1[8], s2[8];
+  if (real) {
+    load8f(cosv + t * D + d0, c1);
+    load8f(cosv + t * D + H + d0, c2);
+    load8f(sinv + t * D + d0, s1);
+    load8f(sinv + t * D + H + d0, s2);
+  }
+  const int64_t W = (int64_t)total * D;
+  for (int hr = hsub; hr < total; hr += hps) {
+    float x1[8], x2[8], o1[8], o2[8];
+    uint16_t *dst;
+    if (hr < dm.nh) {
+      dst = q + ((b * dm.nh + hr) * dm.seq + t) * D;
+    } else if (hr < dm.nh + dm.nkv) {
+      dst = k + ((b * dm.nkv + (hr - dm.nh)) * dm.seq + t) * D;
+    } else {
+      dst = v + ((b * dm.nkv + (hr - dm.nh - dm.nkv)) * dm.seq + t) * D;
+    }
+    if (!real) {
+      zero8(o1);
+      store8h(dst + d0, o1);
+      store8h(dst + H + d0, o1);
+      continue;
+    }
+    const uint16_t *row = qkv + tok * W + (int64_t)hr * D;
+    load8h(row + d0, x1);
+    load8h(row + H + d0, x2);
+    if (hr < dm.nh) {
+      if (lq != nullptr) {
+        float a[8], c[8];
+        const int64_t li = tok * ((int64_t)dm.nh * D) + (int64_t)hr * D;
+        load8_lora<kLoraFp32>(lq, li + d0, a);
+        load8_lora<kLoraFp32>(lq, li + H + d0, c);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) { x1[e] = x1[e] + a[e]; x2[e] = x2[e] + c[e]; }
+      }
+    } else if (hr >= dm.nh + dm.nkv) {
+      if (lv != nullptr) {
+        float a[8], c[8];
+        const int64_t li = tok * ((int64_t)dm.nkv * D) + (int64_t)(hr - dm.nh - dm.nkv) * D;
+        load8_lora<kLoraFp32>(lv, li + d0, a);
+        load8_lora<kLoraFp32>(lv, li + H + d0, c);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) { x1[e] = x1[e] + a[e]; x2[e] = x2[e] + c[e]; }
+      }
+      store8h(dst + d0, x1);
+      store8h(dst + H + d0, x2);
+      continue;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      o1[e] = x1[e] * c1[e] - x2[e] * s1[e];
+      o2[e] = x2[e] * c2[e] + x1[e] * s2[e];
+    }
+    store8h(dst + d0, o1);
+    store8h(dst + H + d0, o2);
+  }
+}
+
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+    rope_bwd_vec(const uint16_t *__restrict__ dq, const uint16_t *__restrict__ dk,
+                 const uint16_t *__restrict__ dv, const float *__restrict__ cosv,
+                 const float *__restrict__ sinv, const int64_t *__restrict__ pos_idx,
+                 uint16_t *__restrict__ dqkv, RopeDims dm) {
+  const int lane = threadIdx.x & 31;
+  const int64_t tok = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (tok >= dm.rows) return;
+  const int64_t slots = dm.batch * dm.seq;
+  const int64_t pos = __ldg(pos_idx + tok);
+  const bool inside = pos >= 0 && pos < slots;
+  const int64_t b = inside ? pos / dm.seq : 0, t = inside ? pos % dm.seq : 0;
+  const int D = dm.d, H = dm.half;
+  const int lph = H / 8, hps = 32 / lph, hsub = lane / lph, d0 = (lane % lph) * 8;
+  const int total = dm.nh + 2 * dm.nkv;
+  if (hsub >= hps) return;
+  float c1[8], c2[8], s1[8], s2[8];
+  load8f(cosv + t * D + d0, c1);
+  load8f(cosv + t * D + H + d0, c2);
+  load8f(sinv + t * D + d0, s1);
+  load8f(sinv + t * D + H + d0, s2);
+  const int64_t W = (int64_t)total * D;
+  uint16_t *row = dqkv + tok * W;
+  for (int hr = hsub; hr < total; hr += hps) {
+    const uint16_t *src;
+    bool rotate = true;
+    if (hr < dm.nh) {
+      src = dq ? dq + ((b * dm.nh + hr) * dm.seq + t) * D : nullptr;
+    } else if (hr < dm.nh + dm.nkv) {
+      src = dk ? dk + ((b * dm.nkv + (hr - dm.nh)) * dm.seq + t) * D : nullptr;
+    } else {
+      src = dv ? dv + ((b * dm.nkv + (hr - dm.nh - dm.nkv)) * dm.seq + t) * D : nullptr;
+      rotate = false;
+    }
+    float g1[8], g2[8], o1[8], o2[8];
+    if (src != nullptr && inside) {
+      load8h(src + d0, g1);
+      load8h(src + H + d0, g2);
+    } else {
+      zero8(g1);
+      zero8(g2);
+    }
+    if (rotate) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        o1[e] = g1[e] * c1[e] + g2[e] * s2[e];
+        o2[e] = g2[e] * c2[e] - g1[e] * s1[e];
+      }
+      store8h(row + (int64_t)hr * D + d0, o1);
+      store8h(row + (int64_t)hr * D + H + d0, o2);
+    } else {
+      store8h(row + (int64_t)hr * D + d0, g1);
+      store8h(row + (int64_t)hr * D + H + d0, g2);
+    }
+  }
+}
+
+// Element-granular versions for head sizes whose half is not a multiple of 8 (or unaligned
+// buffers): one thread per (unit, head row, j < d/2).
+__device__ __forceinline__ float lora_at(const void *p, bool fp32, int64_t i) {
+  return fp32 ? static_cast<const float *>(p)[i]
+              : __half2float(__ushort_as_half(static_cast<const uint16_t *>(p)[i]));
+}
+
+__device__ __forceinline__ uint16_t h16(float f) { return __half_as_ushort(__float2half_rn(f)); }
+__device__ __forceinline__ float f16(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+__global__ void rope_fwd_any(const uint16_t *qkv, const void *lq, const void *lv, bool lora_fp32,
+                             const float *cosv, const float *sinv, const int64_t *pos_idx,
+                             const int32_t *slot_tok, uint16_t *q, uint16_t *k, uint16_t *v,
+                             RopeDims dm) {
+  const int total = dm.nh + 2 * dm.nkv;
+  const int64_t slots = dm.batch * dm.seq;
+  const int64_t units = slot_tok ? slots : dm.rows;
+  const int64_t n = units * total * dm.half;
+  const int D = dm.d, H = dm.half;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int j = (int)(i % H);
+    const int hr = (int)((i / H) % total);
+    const int64_t unit = i / ((int64_t)H * total);
+    int64_t tok, pos;
+    if (slot_tok) {
+      pos = unit;
+      tok = slot_tok[unit];
+    } else {
+      tok = unit;
+      pos = pos_idx[unit];
+      if (pos < 0 || pos >= slots) continue;
+    }
+    const int64_t b = pos / dm.seq, t = pos % dm.seq;
+    uint16_t *dst;
+    if (hr < dm.nh) dst = q + ((b * dm.nh + hr) * dm.seq + t) * D;
+    else if (hr < dm.nh + dm.nkv) dst = k + ((b * dm.nkv + (hr - dm.nh)) * dm.seq + t) * D;
+    else dst = v + ((b * dm.nkv + (hr - dm.nh - dm.nkv)) * dm.seq + t) * D;
+    if (tok < 0 || tok >= dm.rows) {
+      dst[j] = 0;
+      dst[j + H] = 0;
+      continue;
+    }
+    const uint16_t *row = qkv + tok * (int64_t)total * D + (int64_t)hr * D;
+    float x1 = f16(row[j]), x2 = f16(row[j + H]);
+    if (hr < dm.nh && lq) {
+      const int64_t li = tok * ((int64_t)dm.nh * D) + (int64_t)hr * D;
+      x1 = x1 + lora_at(lq, lora_fp32, li + j);
+      x2 = x2 + lora_at(lq, lora_fp32, li + j + H);
+    }
+    if (hr >= dm.nh + dm.nkv) {
+      if (lv) {
+        const int64_t li = tok * ((int64_t)dm.nkv * D) + (int64_t)(hr - dm.nh - dm.nkv) * D;
+        x1 = x1 + lora_at(lv, lora_fp32, li + j);
+        x2 = x2 + lora_at(lv, lora_fp32, li + j + H);
+      }
+      dst[j] = h16(x1);
+      dst[j + H] = h16(x2);
+      continue;
+    }
+    const float c1 = cosv[t * D + j], c2 = cosv[t * D + H + j];
+    const float s1 = sinv[t * D + j], s2 = sinv[t * D + H + j];
+    dst[j] = h16(x1 * c1 - x2 * s1);
+    dst[j + H] = h16(x2 * c2 + x1 * s2);
+  }
+}
+
+__global__ void rope_bwd_any(const uint16_t *dq, const uint16_t *dk, const uint16_t *dv,
+                             const float *cosv, const float *sinv, const int64_t *pos_idx,
+                             uint16_t *dqkv, RopeDims dm) {
+  const int total = dm.nh + 2 * dm.nkv;
+  const int64_t slots = dm.batch * dm.seq;
+  const int64_t n = dm.rows * total * dm.half;
+  const int D = dm.d, H = dm.half;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int j = (int)(i % H);
+    const int hr = (int)((i / H) % total);
+    const int64_t tok = i / ((int64_t)H * total);
+    const int64_t pos = pos_idx[tok];
+    const bool inside = pos >= 0 && pos < slots;
+    const int64_t b = inside ? pos / dm.seq : 0, t = inside ? pos % dm.seq : 0;
+    const uint16_t *src;
+    bool rotate = true;
+    if (hr < dm.nh) src = dq ? dq + ((b * dm.nh + hr) * dm.seq + t) * D : nullptr;
+    else if (hr < dm.nh + dm.nkv) src = dk ? dk + ((b * dm.nkv + (hr - dm.nh)) * dm.seq + t) * D : nullptr;
+    else {
+      src = dv ? dv + ((b * dm.nkv + (hr - dm.nh - dm.nkv)) * dm.seq + t) * D : nullptr;
+      rotate = false;
+    }
+    const float g1 = (src && inside) ? f16(src[j]) : 0.f;
+    const float g2 = (src && inside) ? f16(src[j + H]) : 0.f;
+    uint16_t *row = dqkv + tok * (int64_t)total * D + (int64_t)hr * D;
+    if (rotate) {
+      const float c1 = cosv[t * D + j], c2 = cosv[t * D + H + j];
+      const float s1 = sinv[t * D + j], s2 = sinv[t * D + H + j];
+      row[j] = h16(g1 * c1 + g2 * s2);
+      row[j + H] = h16(g2 * c2 - g1 * s1);
+    } else {
+      row[j] = h16(g1);
+      row[j + H] = h16(g2);
+    }
+  }
+}
+
+__global__ void slot_scatter(const int64_t *pos_idx, int64_t rows, int64_t slots,
+                             int32_t *slot_tok) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t p = pos_idx[i];
+    if (p >= 0 && p < slots) slot_tok[p] = (int32_t)i;
+  }
+}
+
+int check_dims(const char *what, int64_t rows, int64_t batch, int64_t seq, int nh, int nkv, int d) {
+  if (rows < 0 || batch < 0 || seq <= 0 || nh <= 0 || nkv < 0 || d <= 0 || d % 2)
+    return set_error(TB_EINVAL, "%s: bad dims rows=%lld batch=%lld seq=%lld nh=%d nkv=%d d=%d",
+                     what, (long long)rows, (long long)batch, (long long)seq, nh, nkv, d);
+  if (rows > 0x7fffffffLL) return set_error(TB_EINVAL, "%s: too many rows", what);
+  return TB_OK;
+}
+
+unsigned grid_for(int64_t n, int threads) {
+  int64_t blocks = (n + threads - 1) / threads;
+  const int64_t cap = (int64_t)sm_count() * 32;
+  if (blocks > cap) blocks = cap;
+  return (unsigned)(blocks > 0 ? blocks : 1);
+}
+
+}  // namespace
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" int tb_rope_pack_fwd(const uint16_t *qkv, const void *lora_q, const void *lora_v,
+                                int32_t lora_is_fp32, const float *cos, const float *sin,
+                                const int64_t *pos_idx, const int32_t *slot_tok, uint16_t *q,
+                                uint16_t *k, uint16_t *v, int64_t rows, int64_t batch, int64_t seq,
+                                int32_t n_heads, int32_t n_kv, int32_t head_dim, void *stream) {
+  int rc = check_dims("rope_pack_fwd", rows, batch, seq, n_heads, n_kv, head_dim);
+  if (rc != TB_OK) return rc;
+  if (!cos || !sin || !q || (n_kv > 0 && (!k || !v)))
+    return set_error(TB_EINVAL, "rope_pack_fwd: cos, sin, q, k, v are required");
+  if (rows > 0 && (!qkv || !pos_idx))
+    return set_error(TB_EINVAL, "rope_pack_fwd: qkv and pos_idx are required");
+  const int64_t units = slot_tok ? batch * seq : rows;
+  if (units == 0) return TB_OK;
+  RopeDims dm{rows, batch, seq, n_heads, n_kv, head_dim, head_dim / 2};
+  const bool vec = dm.half % 8 == 0 && dm.half <= 256 && aligned(qkv, 16) && aligned(cos, 16) &&
+                   aligned(sin, 16) && aligned(q, 16) && (n_kv == 0 || (aligned(k, 16) && aligned(v, 16))) &&
+                   (!lora_q || aligned(lora_q, 16)) && (!lora_v || aligned(lora_v, 16));
+  cudaStream_t st = as_stream(stream);
+  if (vec) {
+    const unsigned blocks = (unsigned)((units + kWarpsPerBlock - 1) / kWarpsPerBlock);
+    const int threads = kWarpsPerBlock * 32;
+    if (slot_tok) {
+      if (lora_is_fp32)
+        rope_fwd_vec<true, true><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx, slot_tok, q, k, v, dm);
+      else
+        rope_fwd_vec<true, false><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx, slot_tok, q, k, v, dm);
+    } else {
+      if (lora_is_fp32)
+        rope_fwd_vec<false, true><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx, slot_tok, q, k, v, dm);
+      else
+        rope_fwd_vec<false, false><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx, slot_tok, q, k, v, dm);
+    }
+  } else {
+    const int64_t n = units * (n_heads + 2 * n_kv) * (int64_t)dm.half;
+    rope_fwd_any<<<grid_for(n, 256), 256, 0, st>>>(qkv, lora_q, lora_v, lora_is_fp32 != 0, cos, sin,
+                                                   pos_idx, slot_tok, q, k, v, dm);
+  }
+  return check_launch("rope_pack_fwd");
+}
+
+extern "C" int tb_rope_pack_bwd(const uint16_t *dq, const uint16_t *dk, const uint16_t *dv,
+                                const float *cos, const float *sin, const int64_t *pos_idx,
+                                uint16_t *dqkv, int64_t rows, int64_t batch, int64_t seq,
+                                int32_t n_heads, int32_t n_kv, int32_t head_dim, void *stream) {
+  int rc = check_dims("rope_pack_bwd", rows, batch, seq, n_heads, n_kv, head_dim);
+  if (rc != TB_OK) return rc;
+  if (rows == 0) return TB_OK;
+  if (!cos || !sin || !pos_idx || !dqkv)
+    return set_error(TB_EINVAL, "rope_pack_bwd: cos, sin, pos_idx, dqkv are required");
+  RopeDims dm{rows, batch, seq, n_heads, n_kv, head_dim, head_dim / 2};
+  const bool vec = dm.half % 8 == 0 && dm.half <= 256 && aligned(dqkv, 16) && aligned(cos, 16) &&
+                   aligned(sin, 16) && (!dq || aligned(dq, 16)) && (!dk || aligned(dk, 16)) &&
+                   (!dv || aligned(dv, 16));
+  cudaStream_t st = as_stream(stream);
+  if (vec) {
+    const unsigned blocks = (unsigned)((rows + kWarpsPerBlock - 1) / kWarpsPerBlock);
+    rope_bwd_vec<<<blocks, kWarpsPerBlock * 32, 0, st>>>(dq, dk, dv, cos, sin, pos_idx, dqkv, dm);
+  } else {
+    const int64_t n = rows * (n_heads + 2 * n_kv) * (int64_t)dm.half;
+    rope_bwd_any<<<grid_for(n, 256), 256, 0, st>>>(dq, dk, dv, cos, sin, pos_idx, dqkv, dm);
+  }
+  return check_launch("rope_pack_bwd");
+}
+
+extern "C" int tb_slot_index(const int64_t *pos_idx, int64_t rows, int64_t slots,
+                             int32_t *slot_tok, void *stream) {
+  if (rows < 0 || slots < 0) return set_error(TB_EINVAL, "slot_index: negative size");
+  if (slots == 0) return TB_OK;
+  if (!slot_tok || (rows > 0 && !pos_idx))
+    return set_error(TB_EINVAL, "slot_index: pos_idx and slot_tok are required");
+  cudaStream_t st = as_stream(stream);
+  if (cudaMemsetAsync(slot_tok, 0xff, (size_t)slots * sizeof(int32_t), st) != cudaSuccess)
+    return check_launch("slot_index memset");
+  if (rows > 0) slot_scatter<<<grid_for(rows, 256), 256, 0, st>>>(pos_idx, rows, slots, slot_tok);
+  return check_launch("slot_index");
+}

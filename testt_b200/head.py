@@ -1,0 +1,131 @@
+"""The output head and everything computed from its logits, without full logits, on B200
+(reference: solution/head.py).
+
+The head runs over the real (non-pad) tokens in chunks of CHUNK_ROWS rows, labelled rows first:
+1. logits = h @ W^T for the chunk, fp16 (cuBLAS through torch.matmul);
+2. tb_head_stats_grad, one CTA per row, two sweeps over the vocabulary: sweep 1 (online, fp32)
+   gives logsumexp, entropy = lse - sum(p z), the token loss lse - z[label] and whether the first
+   argmax is the label; sweep 2 (labelled rows only) overwrites the logits in place with
+   (softmax - onehot) * scale in fp16;
+3. dh = dlogits @ W for the labelled rows of the chunk (cuBLAS).
+The gradient is taken in forward (the head is frozen) and scaled by the loss scale in backward.
+"""
+
+import math
+
+import torch
+
+from . import _lib
+
+CHUNK_ROWS = 256
+IGNORE_INDEX = -100
+
+
+def head_stats_grad(logits, targets, grad_scale):
+    """(entropy, loss, correct int32) per row of fp16 `logits` [rows, vocab]; overwrites the
+    labelled rows with their scaled dlogits (reference kernel: head.py:34-76)."""
+    _lib.require_cuda(logits, targets, what="head_stats_grad")
+    if logits.dtype != torch.float16 or logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("head_stats_grad: logits must be fp16 [rows, vocab] with unit column stride")
+    rows, vocab = logits.shape
+    targets = targets if targets.dtype == torch.int64 else targets.to(torch.int64)
+    targets = targets.contiguous()
+    dev = logits.device
+    entropy = torch.empty(rows, dtype=torch.float32, device=dev)
+    loss = torch.empty(rows, dtype=torch.float32, device=dev)
+    correct = torch.empty(rows, dtype=torch.int32, device=dev)
+    if rows:
+        _lib.call("tb_head_stats_grad", _lib.ptr(logits), _lib.ptr(targets), _lib.ptr(entropy),
+                  _lib.ptr(loss), _lib.ptr(correct), rows, vocab, logits.stride(0),
+                  float(grad_scale), _lib.stream_of(logits))
+    return entropy, loss, correct
+
+
+def _grad_unit(denominator):
+    """A power of two G with G / denominator about 64: the fp16 head gradient is held at the
+    magnitude a GradScaler gives it (65536 / tokens), and rescaling by a power of two is exact
+    (reference: head.py:79-84)."""
+    exponent = int(round(math.log2(max(float(denominator), 1e-6)))) + 6
+    return float(2 ** max(0, min(16, exponent)))
+
+
+def _host_counts(labelled, denominator, device, targets=None, vocab=None):
+    """(labelled rows, loss denominator) on the host, with one synchronisation
+    (reference: head.py:140-148). Also rejects targets outside [0, vocab) other than
+    IGNORE_INDEX in the same synchronisation."""
+    parts = [labelled.sum().to(torch.float64)]
+    if torch.is_tensor(denominator):
+        parts.append(denominator.to(device=device, dtype=torch.float64).reshape(()))
+    if targets is not None:
+        bad = ((targets != IGNORE_INDEX) & ((targets < 0) | (targets >= vocab))).sum()
+        parts.append(bad.to(torch.float64))
+    vals = torch.stack(parts).tolist()
+    n_labelled = int(vals[0])
+    denom = float(vals[1]) if torch.is_tensor(denominator) else float(denominator)
+    if targets is not None and vals[-1]:
+        raise ValueError(f"fused_head_loss: {int(vals[-1])} targets outside [0, {vocab}) "
+                         f"that are not {IGNORE_INDEX}")
+    return n_labelled, denom
+
+
+class FusedHeadLoss(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, hidden, weight, targets, denominator):
+        _lib.require_cuda(hidden, weight, targets, what="fused_head_loss")
+        rows, width = hidden.shape
+        vocab = weight.shape[0]
+        dev = hidden.device
+        labelled = targets != IGNORE_INDEX
+        order = torch.argsort((~labelled).to(torch.int8), stable=True)
+        n_labelled, denom = _host_counts(labelled, denominator, dev, targets, vocab)
+        h = hidden.index_select(0, order)
+        tgt = targets.index_select(0, order).to(torch.int64).contiguous()
+        entropy = torch.empty(rows, dtype=torch.float32, device=dev)
+        token_loss = torch.empty(rows, dtype=torch.float32, device=dev)
+        correct = torch.empty(rows, dtype=torch.int32, device=dev)
+        want_grad = ctx.needs_input_grad[0]
+        unit = _grad_unit(denom)
+        grad_sorted = torch.empty((n_labelled, width), dtype=torch.float16, device=dev) \
+            if want_grad else None
+        stream = _lib.stream_of(hidden)
+        for start in range(0, rows, CHUNK_ROWS):
+            stop = min(rows, start + CHUNK_ROWS)
+            logits = torch.matmul(h[start:stop], weight.t())
+            _lib.call("tb_head_stats_grad", _lib.ptr(logits), _lib.ptr(tgt[start:stop]),
+                      _lib.ptr(entropy[start:]), _lib.ptr(token_loss[start:]),
+                      _lib.ptr(correct[start:]), stop - start, vocab, logits.stride(0),
+                      unit / max(denom, 1e-6), stream)
+            lab_stop = min(stop, n_labelled)
+            if want_grad and lab_stop > start:
+                torch.matmul(logits[:lab_stop - start], weight, out=grad_sorted[start:lab_stop])
+            del logits
+        total = token_loss.sum()
+        if torch.is_tensor(denominator):
+            loss = total / denominator.to(dev)
+        else:
+            loss = total / denominator
+        if want_grad:
+            grad = torch.zeros((rows, width), dtype=torch.float16, device=dev)
+            grad.index_copy_(0, order[:n_labelled], grad_sorted)
+            ctx.save_for_backward(grad)
+        ctx.unit = unit
+        unsort = torch.empty_like(order)
+        unsort[order] = torch.arange(rows, device=dev)
+        stats = (entropy[unsort], token_loss[unsort], correct[unsort].bool())
+        ctx.mark_non_differentiable(*stats)
+        return (loss, *stats)
+
+    @staticmethod
+    def backward(ctx, grad_loss, *_unused):
+        if not ctx.needs_input_grad[0]:
+            return None, None, None, None
+        (grad,) = ctx.saved_tensors
+        factor = grad_loss.to(torch.float32) / ctx.unit
+        return (grad.to(torch.float32) * factor).to(torch.float16), None, None, None
+
+
+def fused_head_loss(hidden16, weight16, targets, denominator):
+    """(loss, token entropy [M], token loss [M], token correct [M]) for rows of `hidden16`
+    (reference: head.py:151-156). `targets[i]` is the label row i predicts (IGNORE_INDEX for
+    none); `denominator` is what the summed loss is divided by."""
+    return FusedHeadLoss.apply(hidden16.contiguous(), weight16, targets.contiguous(), denominator)

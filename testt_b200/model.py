@@ -1,0 +1,291 @@
+"""The Qwen2 + LoRA training forward built from the B200 kernels, on real tokens only
+(reference: solution/model.py).
+
+`fused_forward` stands in for `Qwen2ForCausalLM.forward` in one case: a labelled training step
+that the trainer patch asked for, on a model whose decoder layers are 4-bit NF4 projections with
+at most one plain LoRA adapter on q_proj / v_proj, SDPA attention and fp16 autocast. Anything
+else runs the original forward.
+
+Per decoder layer, with s the fp32 residual stream of the M real tokens:
+    s, y, y_pad = add_rmsnorm(s, d)                 tb_add_rmsnorm_fwd (d: previous block, fp16)
+    qkv        = y @ [Wq; Wk; Wv]^T + b               tb_nf4_unpack_multi + one cuBLAS GEMM
+    lq, lv     = LoRA(dropout(y_pad))                 PyTorch, peft's math, same dropout draws
+    q, k, v    = rope_pack(qkv, lq, lv)               tb_rope_pack_fwd into padded [B, H, T, 128]
+    a          = SDPA(q, k, v, causal + pad mask)     PyTorch
+    o          = a[real tokens] @ Wo^T                tb_nf4_unpack_multi + cuBLAS
+    s, y2, _   = add_rmsnorm(s, o)                    tb_add_rmsnorm_fwd
+    d          = mlp(y2)                              NF4 + cuBLAS + tb_swiglu_fwd
+then the final norm and the fused head (head.py). Pad tokens never enter the projections, norms,
+MLP or head; attention runs on the padded layout, as in the unpatched model.
+"""
+
+import torch
+
+from .head import IGNORE_INDEX, fused_head_loss
+from .mlp import fused_mlp
+from .nf4 import frozen_linear
+from .rmsnorm import add_rmsnorm
+from .rope import rope_pack, slot_index
+
+_ALLOWED_KWARGS = {"num_items_in_batch", "output_attentions", "output_hidden_states",
+                   "return_dict"}
+
+
+class HeadStats:
+    """What TRL's metrics and Soup's rewind log read from one labelled forward, carried in
+    `outputs.logits` instead of [batch, seq, vocab] logits (reference: model.py:36-51)."""
+
+    def __init__(self, entropy_sum, correct, labelled, row_loss_sum, row_tokens):
+        self.entropy_sum = entropy_sum      # token entropies summed over attention_mask == 1
+        self.correct = correct              # labelled tokens whose first argmax is the label
+        self.labelled = labelled            # labelled tokens
+        self.row_loss_sum = row_loss_sum    # [batch] token cross-entropy summed per row
+        self.row_tokens = row_tokens        # [batch] labelled tokens per row
+
+    def row_losses(self):
+        """(per-row mean CE, per-row labelled tokens), as soup_cli's rewind_hf.row_losses."""
+        denom = self.row_tokens.clamp(min=1).to(self.row_loss_sum.dtype)
+        means = (self.row_loss_sum / denom).tolist()
+        return [float(m) for m in means], [int(n) for n in self.row_tokens.tolist()]
+
+
+def _base_layer(module):
+    get = getattr(module, "get_base_layer", None)
+    return get() if callable(get) else module
+
+
+def _is_4bit(module):
+    """A 4-bit NF4 projection: bitsandbytes' Linear4bit or any module whose weight carries the
+    same `.data` / `.quant_state` pair (all the kernel reads)."""
+    state = getattr(getattr(module, "weight", None), "quant_state", None)
+    return state is not None and getattr(state, "quant_type", None) == "nf4"
+
+
+def _lora_parts(module):
+    """None for a layer without an adapter; (dropout, A, B, scaling) for one active plain LoRA
+    adapter; False for anything else: merged, disabled, several adapters, DoRA, variants, bias
+    (reference: model.py:68-91)."""
+    if not hasattr(module, "lora_A"):
+        return None
+    try:
+        if getattr(module, "merged", False) or getattr(module, "disable_adapters", False):
+            return False
+        names = [n for n in module.active_adapters if n in module.lora_A.keys()]
+        if not names:
+            return None
+        if len(names) > 1:
+            return False
+        name = names[0]
+        if name in getattr(module, "lora_variant", {}) \
+                or getattr(module, "use_dora", {}).get(name, False) \
+                or getattr(module, "lora_bias", {}).get(name, False):
+            return False
+        dropout = module.lora_dropout[name]
+        if not isinstance(dropout, (torch.nn.Dropout, torch.nn.Identity)):
+            return False
+        return dropout, module.lora_A[name], module.lora_B[name], float(module.scaling[name])
+    except Exception:  # noqa: BLE001 - an unexpected adapter layout is not ours to run
+        return False
+
+
+class LayerPlan:
+    """The frozen weights and LoRA hooks of one decoder layer (reference: model.py:94-122)."""
+
+    __slots__ = ("layer", "attn", "q", "k", "v", "o", "gate", "up", "down", "qkv_bias",
+                 "o_bias", "lora_modules")
+
+    def __init__(self, layer):
+        self.layer = layer
+        attn, mlp = layer.self_attn, layer.mlp
+        self.attn = attn
+        self.lora_modules = (attn.q_proj, attn.v_proj)
+        projections = (attn.q_proj, attn.k_proj, attn.v_proj, attn.o_proj, mlp.gate_proj,
+                       mlp.up_proj, mlp.down_proj)
+        bases = [_base_layer(m) for m in projections]
+        if not all(_is_4bit(b) for b in bases):
+            raise ValueError("not a 4-bit NF4 layer")
+        q, k, v, o, gate, up, down = bases
+        self.q, self.k, self.v, self.o = q.weight, k.weight, v.weight, o.weight
+        self.gate, self.up, self.down = gate.weight, up.weight, down.weight
+        if any(getattr(b, "bias", None) is not None for b in (gate, up, down)):
+            raise ValueError("MLP bias")
+        qkv_bias = [getattr(b, "bias", None) for b in (q, k, v)]
+        if all(b is None for b in qkv_bias):
+            self.qkv_bias = None
+        elif all(b is not None for b in qkv_bias):
+            self.qkv_bias = torch.cat([b.detach().to(torch.float16) for b in qkv_bias])
+        else:
+            raise ValueError("q/k/v bias on some projections only")
+        o_bias = getattr(o, "bias", None)
+        self.o_bias = None if o_bias is None else o_bias.detach().to(torch.float16)
+        for m in (attn.k_proj, attn.o_proj, mlp.gate_proj, mlp.up_proj, mlp.down_proj):
+            if _lora_parts(m) is not None:
+                raise ValueError("LoRA outside q_proj/v_proj")
+
+
+class ModelPlan:
+    """The validated shape of a model the fused path runs (reference: model.py:125-149)."""
+
+    def __init__(self, causal_lm):
+        cfg = causal_lm.config
+        inner = causal_lm.model
+        if getattr(cfg, "_attn_implementation", None) != "sdpa":
+            raise ValueError("attention is not sdpa")
+        if getattr(inner, "has_sliding_layers", False) or \
+                any(kind != "full_attention" for kind in (getattr(cfg, "layer_types", None) or [])):
+            raise ValueError("sliding-window layers")
+        if getattr(cfg, "hidden_act", "silu") != "silu":
+            raise ValueError("activation is not silu")
+        self.n_heads = cfg.num_attention_heads
+        self.n_kv = cfg.num_key_value_heads
+        self.hidden = cfg.hidden_size
+        self.head_dim = getattr(cfg, "head_dim", None) or self.hidden // self.n_heads
+        if self.head_dim % 2:
+            raise ValueError("odd head_dim")
+        self.layers = [LayerPlan(layer) for layer in inner.layers[:cfg.num_hidden_layers]]
+        self.embed = inner.embed_tokens
+        self.head = causal_lm.lm_head
+        if self.embed.weight.requires_grad or self.head.weight.requires_grad or \
+                getattr(self.head, "bias", None) is not None:
+            raise ValueError("trainable or biased embedding/head")
+        if self.head.weight.shape[0] != cfg.vocab_size:
+            raise ValueError("vocab size")
+
+
+def model_plan(causal_lm):
+    """The model's plan, validated once and cached on it; None when the model is not one the
+    fused path runs (reference: model.py:152-162)."""
+    plan = causal_lm.__dict__.get("_soup_kernel_plan")
+    if plan is None:
+        try:
+            plan = ModelPlan(causal_lm)
+        except Exception as exc:  # noqa: BLE001
+            print(f"[testt_b200] fused path off for this model: {exc}", flush=True)
+            plan = False
+        causal_lm.__dict__["_soup_kernel_plan"] = plan
+    return plan or None
+
+
+def can_run(causal_lm, input_ids, attention_mask, labels, extra):
+    """Whether this forward call is one the fused path takes (reference: model.py:165-192)."""
+    from ._common import device_ok
+
+    if not (causal_lm.training and torch.is_grad_enabled() and labels is not None):
+        return False
+    if input_ids is None or attention_mask is None or input_ids.dim() != 2 \
+            or attention_mask.shape != input_ids.shape or labels.shape != input_ids.shape:
+        return False
+    if not device_ok(input_ids):
+        return False
+    for key, value in extra.items():
+        if key not in _ALLOWED_KWARGS:
+            return False
+        if key not in ("num_items_in_batch", "return_dict") and value:
+            return False
+    dev_type = input_ids.device.type
+    if not torch.is_autocast_enabled(dev_type) or \
+            torch.get_autocast_dtype(dev_type) != torch.float16:
+        return False
+    plan = model_plan(causal_lm)
+    if plan is None:
+        return False
+    for lp in plan.layers:
+        if _lora_parts(lp.attn.k_proj) is not None:
+            return False
+        if any(_lora_parts(m) is False for m in lp.lora_modules):
+            return False
+    return True
+
+
+def _lora_branch(module, y_pad, batch, seq, pos_idx):
+    """peft's lora_B(lora_A(dropout(x))) * scaling for the real tokens, where x is the padded
+    fp32 norm output the unpatched model feeds it (same shape and dtype, hence the same dropout
+    draws); A and B then run on the real tokens only (reference: model.py:195-206)."""
+    parts = _lora_parts(module)
+    if parts is None:
+        return None
+    dropout, lora_a, lora_b, scaling = parts
+    hidden = y_pad.shape[-1]
+    dropped = dropout(y_pad.view(batch, seq, hidden)).view(batch * seq, hidden)
+    return lora_b(lora_a(dropped.index_select(0, pos_idx))) * scaling
+
+
+def _attention(lp, q, k, v, mask):
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+
+    out, _ = sdpa_attention_forward(lp.attn, q, k, v, mask, dropout=0.0,
+                                    scaling=lp.attn.scaling, sliding_window=None)
+    return out
+
+
+def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_batch):
+    """The training forward of the fused path; returns CausalLMOutputWithPast whose `logits`
+    is a HeadStats (reference: model.py:209-279)."""
+    from transformers.masking_utils import create_causal_mask
+    from transformers.modeling_outputs import CausalLMOutputWithPast
+
+    plan = model_plan(causal_lm)
+    inner, cfg = causal_lm.model, causal_lm.config
+    batch, seq = input_ids.shape
+    dev = input_ids.device
+    padded = batch * seq
+    pos_idx = attention_mask.reshape(-1).nonzero().squeeze(1)   # sorted, one host sync
+    slot_tok = slot_index(pos_idx, padded)                      # shared by every layer's rope
+
+    # Embeddings of the real tokens (the table may be held in fp16 with exact values, see
+    # trainer_patch.prepare_model); the residual stream is fp32.
+    ids = input_ids.reshape(-1).index_select(0, pos_idx)
+    s = torch.nn.functional.embedding(ids, plan.embed.weight).float()
+
+    shape_ref = s.new_empty((1, 1, 1)).expand(batch, seq, plan.hidden)
+    position_ids = torch.arange(seq, device=dev).unsqueeze(0)
+    mask = create_causal_mask(config=cfg, inputs_embeds=shape_ref, attention_mask=attention_mask,
+                              past_key_values=None, position_ids=position_ids)
+    cos, sin = inner.rotary_emb(shape_ref, position_ids)
+    cos, sin = cos[0].float(), sin[0].float()
+
+    delta = None
+    for lp in plan.layers:
+        layer = lp.layer
+        s, y, y_pad = add_rmsnorm(s, delta, layer.input_layernorm.weight,
+                                  layer.input_layernorm.variance_epsilon, pos_idx, padded)
+        qkv = frozen_linear(y, (lp.q, lp.k, lp.v), lp.qkv_bias)
+        lora_q = _lora_branch(lp.attn.q_proj, y_pad, batch, seq, pos_idx)
+        lora_v = _lora_branch(lp.attn.v_proj, y_pad, batch, seq, pos_idx)
+        del y_pad
+        q, k, v = rope_pack(qkv, lora_q, lora_v, cos, sin, pos_idx, batch, seq, plan.n_heads,
+                            plan.n_kv, plan.head_dim, slot_tok=slot_tok)
+        del qkv, lora_q, lora_v
+        attn = _attention(lp, q, k, v, mask)
+        del q, k, v
+        attn = attn.reshape(padded, plan.n_heads * plan.head_dim).index_select(0, pos_idx)
+        o = frozen_linear(attn, (lp.o,), lp.o_bias)
+        del attn
+        s, y2, _ = add_rmsnorm(s, o, layer.post_attention_layernorm.weight,
+                               layer.post_attention_layernorm.variance_epsilon)
+        delta = fused_mlp(y2, lp.gate, lp.up, lp.down)
+        del y2, o
+
+    _, y, _ = add_rmsnorm(s, delta, inner.norm.weight, inner.norm.variance_epsilon)
+    del s, delta
+
+    # causal-LM targets as the loss shifts them: position t is scored against t + 1
+    targets = torch.nn.functional.pad(labels, (0, 1), value=IGNORE_INDEX)[:, 1:]
+    targets = targets.reshape(-1).index_select(0, pos_idx)
+    labelled = targets != IGNORE_INDEX
+    denominator = num_items_in_batch if num_items_in_batch is not None else labelled.sum()
+    weight = plan.head.weight
+    if weight.dtype != torch.float16:
+        weight = weight.to(torch.float16)
+    loss, entropy, token_loss, correct = fused_head_loss(y, weight, targets, denominator)
+
+    with torch.no_grad():
+        row = torch.div(pos_idx, seq, rounding_mode="floor")
+        row_loss_sum = torch.zeros(batch, dtype=torch.float32, device=dev) \
+            .index_add_(0, row, token_loss)
+        row_tokens = torch.zeros(batch, dtype=torch.long, device=dev) \
+            .index_add_(0, row, labelled.long())
+        stats = HeadStats(entropy_sum=entropy.sum(), correct=correct.sum(),
+                          labelled=labelled.sum(), row_loss_sum=row_loss_sum,
+                          row_tokens=row_tokens)
+    return CausalLMOutputWithPast(loss=loss, logits=stats)

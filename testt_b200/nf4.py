@@ -1,0 +1,183 @@
+"""NF4 (bitsandbytes 4-bit) weight unpacking on B200, and the frozen 4-bit linear that uses it.
+
+Reference: solution/nf4.py. A bitsandbytes NF4 weight holds two 4-bit codes per byte (high
+nibble first) and one absmax per `blocksize` values. The absmax is either fp32 ("plain") or, with
+double quant ("nested"), an 8-bit code into a 256-entry table, scaled per `state2.blocksize`
+absmax blocks and shifted by one offset:
+
+    absmax[b] = code2[absmax_u8[b]] * absmax2[b // blocksize2] + offset      (nested)
+    w[i]      = nf4[q[i]] * absmax[i // blocksize]    (fp32, rounded once to fp16)
+
+`tb_nf4_unpack_multi` unpacks every weight of a stacked GEMM operand (q|k|v, gate|up) in one
+launch, bit-exact with the reference for both layouts (the reference kernel takes only the
+nested one and sends the plain one to bitsandbytes, nf4.py:86-88).
+"""
+
+import torch
+
+from . import _lib
+
+MAX_WEIGHTS_PER_LAUNCH = 8
+
+
+def _quant_state(weight):
+    return getattr(weight, "quant_state", None)
+
+
+def supports_fast_unpack(weight):
+    """True for the layouts the kernel handles: NF4 with an even blocksize, plain fp32 absmax or
+    nested absmax, 2-D shape, uint8 contiguous packed data (reference: nf4.py:52-62)."""
+    state = _quant_state(weight)
+    if state is None or getattr(state, "quant_type", None) != "nf4":
+        return False
+    if state.blocksize % 2:
+        return False
+    if state.nested:
+        if state.state2 is None or state.absmax.dtype != torch.uint8:
+            return False
+    elif state.absmax.dtype != torch.float32:
+        return False
+    shape = tuple(state.shape)
+    if len(shape) != 2 or (shape[0] * shape[1]) % 2:
+        return False
+    data = weight.data
+    return data.dtype == torch.uint8 and data.is_contiguous() and \
+        data.numel() * 2 == shape[0] * shape[1]
+
+
+def _tensors(weight):
+    state = _quant_state(weight)
+    ts = [weight.data, state.absmax, state.code]
+    if state.nested:
+        ts += [state.state2.code, state.state2.absmax]
+        if torch.is_tensor(state.offset):
+            ts.append(state.offset)
+    return ts
+
+
+def _on_device(weight, device):
+    return all(t.device == device for t in _tensors(weight))
+
+
+def _offset_tensor(state, device):
+    """The nested offset as a 1-element fp32 device tensor (cached on the state: a Python float
+    offset would otherwise cost a host-to-device copy per call)."""
+    off = state.offset
+    if torch.is_tensor(off):
+        return off.reshape(1).to(torch.float32) if off.dtype != torch.float32 else off
+    cached = getattr(state, "_tb_offset", None)
+    if cached is None or cached.device != device:
+        cached = torch.tensor([float(off)], dtype=torch.float32, device=device)
+        try:
+            state._tb_offset = cached
+        except AttributeError:
+            pass
+    return cached
+
+
+def _job(weight, out):
+    state = _quant_state(weight)
+    entry = dict(packed=weight.data, table=state.code.to(torch.float32), out=out,
+                 n_bytes=weight.data.numel(), qblock=int(state.blocksize))
+    if state.nested:
+        entry.update(absmax_u8=state.absmax, code2=state.state2.code.to(torch.float32),
+                     absmax2=state.state2.absmax.to(torch.float32),
+                     offset=_offset_tensor(state, out.device), qblock2=int(state.state2.blocksize))
+    else:
+        entry.update(absmax_f32=state.absmax)
+    return entry
+
+
+def _launch(jobs, device):
+    """One tb_nf4_unpack_multi launch per MAX_WEIGHTS_PER_LAUNCH weights."""
+    stream = _lib.stream_of(jobs[0]["out"])
+    for start in range(0, len(jobs), MAX_WEIGHTS_PER_LAUNCH):
+        part = jobs[start:start + MAX_WEIGHTS_PER_LAUNCH]
+        n = len(part)
+        get = lambda key: [_lib.ptr(j.get(key)) for j in part]  # noqa: E731
+        call_args = [
+            n, _lib.ptr_array(get("packed")), _lib.ptr_array(get("absmax_f32")),
+            _lib.ptr_array(get("absmax_u8")), _lib.ptr_array(get("code2")),
+            _lib.ptr_array(get("absmax2")), _lib.ptr_array(get("offset")),
+            _lib.ptr_array(get("table")), _lib.ptr_array(get("out")),
+            (_lib._I64 * n)(*[j["n_bytes"] for j in part]),
+            (_lib._I32 * n)(*[j["qblock"] for j in part]),
+            (_lib._I32 * n)(*[j.get("qblock2", 1) for j in part]),
+            stream]
+        _lib.call("tb_nf4_unpack_multi", *call_args)
+
+
+def _check_out(weight, out):
+    shape = weight_shape(weight)
+    if out.dtype != torch.float16 or not out.is_contiguous() or out.numel() != shape[0] * shape[1]:
+        raise ValueError(f"unpack_into: out must be a contiguous fp16 tensor of {shape} values, "
+                         f"got {tuple(out.shape)} {out.dtype}")
+
+
+def unpack_into(weight, out):
+    """Write the fp16 values of one bitsandbytes 4-bit weight ([N, K]) into `out` ([N, K])
+    (reference: nf4.py:72-89)."""
+    _check_out(weight, out)
+    if out.is_cuda and supports_fast_unpack(weight) and \
+            _on_device(weight, out.device):
+        _launch([_job(weight, out)], out.device)
+        return out
+    if not out.is_cuda:
+        raise RuntimeError("unpack_into: testt_b200 unpacks on CUDA devices only")
+    # A layout the kernel does not cover (FP4, odd blocksize): bitsandbytes' own GPU path, as the
+    # reference does for layouts its kernel does not take.
+    import bitsandbytes.functional as bnb_functional
+
+    out.copy_(bnb_functional.dequantize_4bit(weight.data, _quant_state(weight))
+              .to(out.dtype).view_as(out))
+    return out
+
+
+def weight_shape(weight):
+    return tuple(_quant_state(weight).shape)
+
+
+def unpack_concat(weights, device):
+    """fp16 [sum N_i, K]: the weights stacked by rows, unpacked in one launch when every weight
+    has a layout the kernel takes (reference: nf4.py:96-105)."""
+    device = torch.device(device)
+    rows = [weight_shape(w)[0] for w in weights]
+    cols = weight_shape(weights[0])[1]
+    out = torch.empty((sum(rows), cols), dtype=torch.float16, device=device)
+    if device.type == "cuda" and all(supports_fast_unpack(w) and _on_device(w, device)
+                                     for w in weights):
+        jobs, start = [], 0
+        for weight, n in zip(weights, rows):
+            jobs.append(_job(weight, out[start:start + n]))
+            start += n
+        _launch(jobs, device)
+        return out
+    start = 0
+    for weight, n in zip(weights, rows):
+        unpack_into(weight, out[start:start + n])
+        start += n
+    return out
+
+
+class FrozenNF4Linear(torch.autograd.Function):
+    """y = x @ W^T (+ b) for frozen 4-bit weights stacked by rows, fp16 in and out
+    (reference: nf4.py:108-127). Nothing large is saved: W is unpacked again in backward."""
+
+    @staticmethod
+    def forward(ctx, x, bias, weights):
+        weight = unpack_concat(weights, x.device)
+        out = torch.nn.functional.linear(x, weight, bias)
+        ctx.weights = weights
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        grad_x = None
+        if ctx.needs_input_grad[0]:
+            weight = unpack_concat(ctx.weights, grad_out.device)
+            grad_x = grad_out.to(torch.float16) @ weight
+        return grad_x, None, None
+
+
+def frozen_linear(x, weights, bias=None):
+    return FrozenNF4Linear.apply(x, bias, tuple(weights))
