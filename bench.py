@@ -1,0 +1,598 @@
+"""Benchmark of the fused QLoRA hot path on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    (N > 1: python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...)
+
+Workload: a full QLoRA training step of a random-init Qwen2.5-1.5B-shaped
+model (28 layers, hidden 1536, MLP 8960, 12/2 heads, vocab 151936, tied embedding), every decoder
+projection NF4 (blocksize 64, double-quant absmax), LoRA r=16 alpha=32 on q/v, batch 4 per GPU
+with lognormal(median 140) lengths padded to 512. A step is forward + backward through the public
+path (apply()'s patched Qwen2 forward -> model.fused_forward, all five kernel pairs) under fp16
+autocast, the LoRA-gradient all-reduce (NCCL, N > 1), and an AdamW step. Data parallel: every
+rank runs its own batch, so per-GPU work is fixed (weak scaling).
+
+Printed on rank 0, one JSON line:
+  value      whole-job real tokens / s over the timed steps, inputs already on the device
+  e2e        the same step, the batch copied from pinned host memory every step and the loss
+             and statistics read back (the path a training loop takes)
+  hot_path   the fused memory-bound kernels of one step (NF4 unpack, add+RMSNorm, RoPE pack,
+             SwiGLU, fwd + bwd, 28 layers), replayed as a CUDA graph: GB/s against HBM peak
+  roofline   the dominant hot-path kernel (NF4 unpack): algorithmic bytes / measured time
+  head       the vocabulary head of config 4 (2048 rows, 1331 labelled): TFLOP/s
+  cpu_baseline  the same step on the host cores (oracle.step sample), rank 0 at N = 1
+The reference arm (--impl reference) times that CPU step alone.
+"""
+
+import argparse
+import datetime
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "fused hot-path GB/s (% HBM peak) + QLoRA step tokens/sec at 1/2/4/8 B200"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+# ---- process setup ---------------------------------------------------------------------------
+
+def setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        dist.init_process_group("nccl" if args.impl == "ours" else "gloo",
+                                timeout=datetime.timedelta(seconds=300))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+
+
+def max_over_ranks(x, world, device):
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clock and throttle reasons while a region runs."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+        return False
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.seek(0)
+        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sm, mx, reasons = [], None, set()
+        for r in rows:
+            r = [c.strip() for c in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---- the QLoRA step (value, e2e) -------------------------------------------------------------
+
+def make_batch(lengths, seq, vocab, seed, device):
+    """input_ids / attention_mask / labels [B, seq]: uniform ids, right padding, the first third
+    of every row masked as prompt."""
+    g = torch.Generator().manual_seed(seed)
+    b = len(lengths)
+    ids = torch.randint(0, vocab, (b, seq), generator=g)
+    mask = torch.zeros(b, seq, dtype=torch.int64)
+    labels = torch.full((b, seq), -100, dtype=torch.int64)
+    for r, n in enumerate(lengths):
+        mask[r, :n] = 1
+        labels[r, n // 3:n] = ids[r, n // 3:n]
+    ids[mask == 0] = 0
+    return ids.to(device), mask.to(device), labels.to(device)
+
+
+class TrainStep:
+    """forward (fused path) + backward + LoRA-gradient all-reduce + AdamW, loss scale 1024."""
+
+    LOSS_SCALE = 1024.0
+
+    def __init__(self, model, world):
+        from testt_b200.dist import GradBucket
+        from testt_b200.qlora import lora_parameters
+
+        self.model = model
+        self.params = lora_parameters(model)
+        self.bucket = GradBucket(self.params)
+        self.opt = torch.optim.AdamW(self.params, lr=1e-4, fused=True)
+        self.world = world
+
+    def __call__(self, ids, mask, labels):
+        from testt_b200.trainer_patch import _FusedRequest
+
+        n_items = (labels[:, 1:] != -100).sum()
+        with torch.autocast("cuda", dtype=torch.float16):
+            with _FusedRequest():
+                out = self.model(input_ids=ids, attention_mask=mask, labels=labels,
+                                 num_items_in_batch=n_items)
+        (out.loss * self.LOSS_SCALE).backward()
+        self.bucket.all_reduce(average=True)
+        self.bucket.flat.mul_(1.0 / self.LOSS_SCALE)
+        self.opt.step()
+        self.bucket.zero()
+        return out
+
+
+def time_region(fn, steps, world, device):
+    """Device time of `steps` calls of fn (CUDA events, barrier + synchronize on both sides),
+    max over ranks, in ms."""
+    barrier(world)
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    stop.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(start.elapsed_time(stop), world, device)
+
+
+# ---- the hot path as CUDA graphs (hot_path, roofline) ----------------------------------------
+
+class HotPath:
+    """Every fused memory-bound kernel launch of one training step at the step's shapes (M real
+    tokens, 28 layers), on per-layer buffers, with each launch's algorithmic bytes. Launches are
+    grouped by kernel so each group can be captured and replayed on its own."""
+
+    def __init__(self, model, lengths, seq, device):
+        from oracle import synth
+        from testt_b200 import _lib, nf4
+        from testt_b200.model import model_plan
+
+        self.lib = _lib
+        plan = model_plan(model)
+        self.plan = plan
+        dev = torch.device(device)
+        pos = synth.positions(lengths, seq).to(dev)
+        m, b, p = pos.numel(), len(lengths), len(lengths) * seq
+        h, inter = plan.hidden, model.config.intermediate_size
+        nh, nkv, d = plan.n_heads, plan.n_kv, plan.head_dim
+        width = (nh + 2 * nkv) * d
+        self.tokens = m
+        f32, f16 = torch.float32, torch.float16
+        g = torch.Generator(device=dev)
+        g.manual_seed(1)
+
+        def rnd(shape, dtype, std=1.0):
+            return (torch.randn(shape, generator=g, device=dev) * std).to(dtype)
+
+        self.groups = {k: [] for k in ("nf4_unpack", "rmsnorm_fwd", "rmsnorm_bwd", "rope_fwd",
+                                       "rope_bwd", "swiglu_fwd", "swiglu_bwd")}
+        self.bytes = {k: 0 for k in self.groups}
+        self.keep = []
+        cos, sin = (t.to(dev) for t in synth._rope(seq, dev))
+        slot = torch.empty(p, dtype=torch.int32, device=dev)
+        _lib.call("tb_slot_index", _lib.ptr(pos), m, p, _lib.ptr(slot),
+                  _lib.stream_of(pos))
+        self.keep += [pos, cos, sin, slot]
+        w_norm = torch.ones(h, device=dev)
+
+        def add(group, nbytes, name, *args):
+            self.groups[group].append((name, args))
+            self.bytes[group] += nbytes
+
+        # NF4: q|k|v, o, gate|up, down unpacked in forward and again in backward
+        def nf4_jobs(weights):
+            outs = []
+            for wt in weights:
+                shp = tuple(wt.quant_state.shape)
+                outs.append(torch.empty(shp, dtype=f16, device=dev))
+            self.keep.extend(outs)
+            jobs = [nf4._job(wt, o) for wt, o in zip(weights, outs)]
+            self.keep.append(jobs)
+            nb = sum(_nf4_bytes(wt) for wt in weights)
+            return jobs, nb
+
+        def nf4_launch(jobs):
+            n = len(jobs)
+            get = lambda key: [_lib.ptr(j.get(key)) for j in jobs]  # noqa: E731
+            return (n, _lib.ptr_array(get("packed")), _lib.ptr_array(get("absmax_f32")),
+                    _lib.ptr_array(get("absmax_u8")), _lib.ptr_array(get("code2")),
+                    _lib.ptr_array(get("absmax2")), _lib.ptr_array(get("offset")),
+                    _lib.ptr_array(get("table")), _lib.ptr_array(get("out")),
+                    (_lib._I64 * n)(*[j["n_bytes"] for j in jobs]),
+                    (_lib._I32 * n)(*[j["qblock"] for j in jobs]),
+                    (_lib._I32 * n)(*[j.get("qblock2", 1) for j in jobs]))
+
+        fwd_nf4, bwd_nf4 = [], []
+        for lp in plan.layers:
+            for ws in ((lp.q, lp.k, lp.v), (lp.o,), (lp.gate, lp.up), (lp.down,)):
+                jobs, nb = nf4_jobs(ws)
+                fwd_nf4.append((nf4_launch(jobs), nb))
+                bwd_nf4.insert(0, (nf4_launch(jobs), nb))
+        for args, nb in fwd_nf4 + bwd_nf4:
+            add("nf4_unpack", nb, "tb_nf4_unpack_multi", *args)
+
+        e = m * h
+        pad_b = 8 * m
+        for layer in range(len(plan.layers) + 1):
+            last = layer == len(plan.layers)
+            # input norm (with delta except on layer 0, with the padded fp32 copy) ...
+            x = rnd((m, h), f32)
+            delta = None if layer == 0 else rnd((m, h), f16, 0.5)
+            s = torch.empty((m, h), dtype=f32, device=dev)
+            y = torch.empty((m, h), dtype=f16, device=dev)
+            ypad = torch.zeros((p, h), dtype=f32, device=dev) if not last else None
+            rstd = torch.empty(m, dtype=f32, device=dev)
+            self.keep += [x, delta, s, y, ypad, rstd]
+            nb = e * (4 + 2 + (6 if delta is not None else 0) + (4 if ypad is not None else 0)) \
+                + 4 * h + 4 * m + (pad_b if ypad is not None else 0)
+            add("rmsnorm_fwd", nb, "tb_add_rmsnorm_fwd", _lib.ptr(x), _lib.ptr(delta),
+                _lib.ptr(w_norm), _lib.ptr(s) if delta is not None else None, _lib.ptr(y),
+                _lib.ptr(ypad), _lib.ptr(pos) if ypad is not None else None, _lib.ptr(rstd),
+                m, h, 1e-6)
+            dy = rnd((m, h), f16, 1e-2)
+            dypad = rnd((p, h), f32, 1e-3) if ypad is not None else None
+            ds = rnd((m, h), f32, 1e-2) if (layer > 0 and not last) else None
+            dx = torch.empty((m, h), dtype=f32, device=dev)
+            ddelta = torch.empty((m, h), dtype=f16, device=dev) if layer > 0 else None
+            self.keep += [dy, dypad, ds, dx, ddelta]
+            nb = e * (4 + 2 + 4 + (4 if dypad is not None else 0) + (4 if ds is not None else 0)
+                      + (2 if ddelta is not None else 0)) + 4 * h + 4 * m \
+                + (pad_b if dypad is not None else 0)
+            add("rmsnorm_bwd", nb, "tb_add_rmsnorm_bwd", _lib.ptr(s if delta is not None else x),
+                _lib.ptr(rstd), _lib.ptr(w_norm), _lib.ptr(dy), _lib.ptr(dypad),
+                _lib.ptr(pos) if dypad is not None else None, _lib.ptr(ds), _lib.ptr(dx),
+                _lib.ptr(ddelta), m, h)
+            if last:
+                break
+            # ... post-attention norm (delta, no padded copy)
+            x2, d2 = rnd((m, h), f32), rnd((m, h), f16, 0.5)
+            s2 = torch.empty((m, h), dtype=f32, device=dev)
+            y2 = torch.empty((m, h), dtype=f16, device=dev)
+            r2 = torch.empty(m, dtype=f32, device=dev)
+            dy2, ds2 = rnd((m, h), f16, 1e-2), rnd((m, h), f32, 1e-2)
+            dx2 = torch.empty((m, h), dtype=f32, device=dev)
+            dd2 = torch.empty((m, h), dtype=f16, device=dev)
+            self.keep += [x2, d2, s2, y2, r2, dy2, ds2, dx2, dd2]
+            add("rmsnorm_fwd", e * 12 + 4 * h + 4 * m, "tb_add_rmsnorm_fwd", _lib.ptr(x2),
+                _lib.ptr(d2), _lib.ptr(w_norm), _lib.ptr(s2), _lib.ptr(y2), None, None,
+                _lib.ptr(r2), m, h, 1e-6)
+            add("rmsnorm_bwd", e * 16 + 4 * h + 4 * m, "tb_add_rmsnorm_bwd", _lib.ptr(s2),
+                _lib.ptr(r2), _lib.ptr(w_norm), _lib.ptr(dy2), None, None, _lib.ptr(ds2),
+                _lib.ptr(dx2), _lib.ptr(dd2), m, h)
+            # QKV pack + RoPE (LoRA outputs fp16, as under autocast)
+            qkv = rnd((m, width), f16)
+            lq, lv = rnd((m, nh * d), f16, 1e-2), rnd((m, nkv * d), f16, 1e-2)
+            q = torch.empty((b, nh, seq, d), dtype=f16, device=dev)
+            k = torch.empty((b, nkv, seq, d), dtype=f16, device=dev)
+            v = torch.empty((b, nkv, seq, d), dtype=f16, device=dev)
+            self.keep += [qkv, lq, lv, q, k, v]
+            nb = m * (width * 2 + (nh + nkv) * d * 2) + p * width * 2 + 2 * seq * d * 4 + p * 4
+            add("rope_fwd", nb, "tb_rope_pack_fwd", _lib.ptr(qkv), _lib.ptr(lq), _lib.ptr(lv), 0,
+                _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(pos), _lib.ptr(slot), _lib.ptr(q),
+                _lib.ptr(k), _lib.ptr(v), m, b, seq, nh, nkv, d)
+            dq, dk, dv = rnd(q.shape, f16), rnd(k.shape, f16), rnd(v.shape, f16)
+            dqkv = torch.empty((m, width), dtype=f16, device=dev)
+            self.keep += [dq, dk, dv, dqkv]
+            nb = m * width * 2 * 2 + m * 8 + 2 * seq * d * 4
+            add("rope_bwd", nb, "tb_rope_pack_bwd", _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv),
+                _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(pos), _lib.ptr(dqkv), m, b, seq, nh, nkv, d)
+            # SwiGLU
+            gu = rnd((m, 2 * inter), f16)
+            act = torch.empty((m, inter), dtype=f16, device=dev)
+            dact = rnd((m, inter), f16, 1e-2)
+            gu2 = rnd((m, 2 * inter), f16)
+            self.keep += [gu, act, dact, gu2]
+            add("swiglu_fwd", m * inter * 6, "tb_swiglu_fwd", _lib.ptr(gu), _lib.ptr(act), m, inter)
+            add("swiglu_bwd", m * inter * 10, "tb_swiglu_bwd_inplace", _lib.ptr(dact),
+                _lib.ptr(gu2), m, inter)
+
+    def launches(self, group=None):
+        return sum(len(v) for k, v in self.groups.items() if group in (None, k))
+
+    def total_bytes(self, group=None):
+        return sum(v for k, v in self.bytes.items() if group in (None, k))
+
+    def _run(self, groups):
+        stream = self.lib.stream_of(self.keep[0])
+        for gname in groups:
+            for name, args in self.groups[gname]:
+                self.lib.call(name, *args, stream)
+
+    def graph(self, groups):
+        """A CUDA graph of the launches of `groups` (in step order within each group)."""
+        self._run(groups)  # eager warm-up outside capture
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._run(groups)
+        return g
+
+
+def _nf4_bytes(weight):
+    """Algorithmic bytes of one NF4 unpack: packed codes + absmax (+ nested tables) + fp16 out."""
+    st = weight.quant_state
+    n = weight.data.numel()
+    b = n + 4 * n  # packed bytes in, 2 fp16 values (4 bytes) out per byte
+    b += st.absmax.numel() * st.absmax.element_size() + 16 * 4
+    if st.nested:
+        b += st.state2.absmax.numel() * 4 + 256 * 4 + 4
+    return b
+
+
+def time_graph(graph, reps, world, device, flush=None):
+    """ms per replay of a captured graph (device time, max over ranks); the L2 is flushed before
+    every replay by writing `flush` (larger than L2) and the flush time is not counted."""
+    times = []
+    for _ in range(reps):
+        if flush is not None:
+            flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    times.sort()
+    med = times[len(times) // 2]
+    return max_over_ranks(med, world, device)
+
+
+# ---- the head (config 4) ---------------------------------------------------------------------
+
+def head_bench(device, reps, world):
+    from oracle import synth
+    from testt_b200.head import fused_head_loss
+
+    c = synth.config4(device)
+    h = c["hidden"].clone().requires_grad_(True)
+
+    def run():
+        loss, *_ = fused_head_loss(h, c["weight"], c["targets"], c["n_labelled"])
+        return loss
+
+    run()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(reps):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        run()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    times.sort()
+    ms = times[len(times) // 2]
+    rows, hidden, vocab = 2048, synth.HIDDEN, synth.VOCAB
+    flops = 2 * rows * hidden * vocab + 2 * c["n_labelled"] * hidden * vocab
+    return {"ms": ms, "tflops": flops / ms / 1e9, "flops": flops, "rows": rows,
+            "labelled": c["n_labelled"]}
+
+
+# ---- arms ------------------------------------------------------------------------------------
+
+def reference_arm(args, rank, world):
+    """The reference path on the host cores: the CPU QLoRA step sample (oracle.step)."""
+    if rank != 0:
+        return
+    from oracle import step, synth
+
+    lengths = synth.lengths(seed=0)
+    cpu = step.CpuStep(lengths, threads=os.cpu_count())
+    for _ in range(args.warmup):
+        cpu.seconds()
+    secs = [cpu.seconds() for _ in range(args.steps)]
+    s = sum(secs) / len(secs)
+    sample, thr, rows = cpu.sample, torch.get_num_threads(), cpu.rows
+    value = rows / s
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": s * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "QLoRA step, Qwen2.5-1.5B shape, batch 4/GPU, NF4 dq, "
+                                   "LoRA r16 q/v (CPU sample)", "tokens_per_gpu": rows},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": thr, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def ours_arm(args, rank, world, local):
+    from oracle import synth
+    from testt_b200 import _lib, trainer_patch
+    from testt_b200.qlora import build_qlora_model, qwen2_config
+
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    pk, pk_kind = peaks()
+    trainer_patch.patch_forward()
+    cfg = qwen2_config()
+    model = build_qlora_model(cfg, dev, seed=0)
+    lengths = synth.lengths(seed=0)
+    seq = synth.SEQ
+    ids, mask, labels = make_batch(lengths, seq, cfg.vocab_size, 100 + rank, dev)
+    tokens = sum(lengths)
+    step = TrainStep(model, world)
+
+    for _ in range(args.warmup):
+        step(ids, mask, labels)
+    torch.cuda.synchronize()
+
+    # value: the step with the batch already on the device
+    _lib.reset_call_count()
+    with Clocks(local) as clk:
+        ms = time_region(lambda: step(ids, mask, labels), args.steps, world, dev)
+    calls = _lib.call_count() // args.steps
+    clocks = clk.summary()
+    value = tokens * world * args.steps / (ms / 1e3)
+
+    # e2e: batch from pinned host memory every step, loss and statistics read back
+    host = [t.cpu().pin_memory() for t in (ids, mask, labels)]
+    h2d = sum(t.numel() * t.element_size() for t in host)
+
+    def e2e_step():
+        batch = [t.to(dev, non_blocking=True) for t in host]
+        out = step(*batch)
+        st = out.logits
+        vals = torch.stack([out.loss.detach().float(), st.entropy_sum.float(),
+                            st.correct.float(), st.labelled.float()]).cpu()
+        return vals
+
+    e2e_ms = time_region(e2e_step, args.steps, world, dev)
+    e2e_value = tokens * world * args.steps / (e2e_ms / 1e3)
+
+    # hot path: the fused memory-bound kernels of one step as CUDA graphs
+    hp = HotPath(model, lengths, seq, dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    reps = max(args.steps, 5)
+    full = hp.graph(list(hp.groups))
+    hp_ms = time_graph(full, reps, world, dev, flush)
+    hp_bytes = hp.total_bytes()
+    per_kernel = {}
+    for name in hp.groups:
+        g = hp.graph([name])
+        kms = time_graph(g, reps, world, dev, flush)
+        nb = hp.total_bytes(name)
+        per_kernel[name] = {"launches": hp.launches(name), "ms": kms, "bytes": nb,
+                            "gbps": nb / kms / 1e6, "frac": nb / kms / 1e6 / pk["hbm_gbs"]}
+        del g
+    del full
+    nf = per_kernel["nf4_unpack"]
+    n_launch = nf["launches"]
+    achieved = nf["gbps"]
+
+    head = head_bench(dev, max(args.steps, 5), world) if rank == 0 else None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import step as cstep
+
+        s, sample, thr, rows = cstep.cpu_step_seconds(lengths, repeats=1,
+                                                      threads=os.cpu_count())
+        cpu = {"value": rows / s, "unit": "tokens/s", "cores": thr, "kind": "port",
+               "sample": sample}
+
+    if rank != 0:
+        return
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "nf4_unpack_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get("bytes_per_launch")
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+        "data": "synthetic (random-init weights, uniform token ids, lognormal lengths)",
+        "config": {"workload": "config 5: QLoRA train step (fwd+bwd+LoRA all-reduce+AdamW), "
+                               "Qwen2.5-1.5B shape, NF4 bs64 double-quant, LoRA r16 a32 q/v",
+                   "global_batch": 4 * world, "seq_len": seq, "tokens_per_gpu": tokens,
+                   "lengths": lengths, "parallelism": f"dp{world}",
+                   "l2": "inputs larger than L2 (3.4 GB of NF4 weights streamed per step); "
+                         "hot-path graphs: L2 flushed (256 MB write) before each replay"},
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": 16},
+        "gpu_launches": calls,
+        "clocks": clocks,
+        "hot_path": {"gbps": hp_bytes / hp_ms / 1e6, "frac": hp_bytes / hp_ms / 1e6 / pk["hbm_gbs"],
+                     "ms_per_step": hp_ms, "bytes_per_step": hp_bytes,
+                     "launches_per_step": hp.launches(), "per_kernel": per_kernel,
+                     "peak": pk["hbm_gbs"], "peak_kind": pk_kind},
+        "roofline": {"kernel": "nf4_unpack (tb_nf4_unpack_multi)", "bound": "hbm",
+                     "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / pk["hbm_gbs"], "peak_kind": pk_kind,
+                     "launches": n_launch, "avg_launch_us": nf["ms"] * 1e3 / n_launch,
+                     "bytes_per_launch": nf["bytes"] / n_launch, "traffic": traffic},
+        "head": None if head is None else {
+            **head, "frac": head["tflops"] / pk["bf16_tflops"], "peak": pk["bf16_tflops"],
+            "bound": "tensor", "unit": "TFLOP/s"},
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, world, local = setup(args)
+    try:
+        if args.impl == "reference":
+            reference_arm(args, rank, world)
+        else:
+            ours_arm(args, rank, world, local)
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    t0 = time.time()
+    main()

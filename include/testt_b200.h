@@ -141,6 +141,33 @@ int tb_head_stats_grad(uint16_t *logits, const int64_t *targets, float *entropy,
                        int32_t *correct, int64_t rows, int64_t vocab, int64_t ld,
                        float grad_scale, void *stream);
 
+/* Split form of the same statistics, for rows spread over several CTAs or several GPUs (a
+ * vocabulary-sharded head). No counterpart kernel in the reference, whose one launch per chunk
+ * covers whole rows (solution/head.py:34-76); these three compute the same values.
+ *
+ * tb_head_partials: logits fp16 [rows, cols] (row stride ld) hold vocabulary columns
+ * col_offset .. col_offset+cols-1. Each row is cut into `splits` column ranges; for each range:
+ *   part fp32 [rows, splits, 6] = (max z, sum e^(z-max), sum e^(z-max) z, best z,
+ *                                  z[target] if the target column is in the range else 0,
+ *                                  1 if it is else 0)
+ *   part_idx int64 [rows, splits] = vocabulary index of the first maximum in the range.
+ * rows <= 65535 per call. */
+int tb_head_partials(const uint16_t *logits, const int64_t *targets, float *part,
+                     int64_t *part_idx, int64_t rows, int64_t cols, int64_t ld,
+                     int64_t col_offset, int32_t splits, void *stream);
+
+/* Merges n_groups x splits partial states per row, laid out [group][row][split] (for example the
+ * partials of every rank, gathered): lse, entropy = lse - sum(p z), loss = lse - z[target]
+ * (0 for unlabelled rows) and correct = first argmax == target. */
+int tb_head_merge(const float *part, const int64_t *part_idx, const int64_t *targets,
+                  int64_t rows, int32_t n_groups, int32_t splits, float *lse, float *entropy,
+                  float *loss, int32_t *correct, void *stream);
+
+/* In place over the labelled rows of a [rows, cols] slab (columns col_offset ..):
+ * logits <- fp16((exp(z - lse[row]) - [col == target]) * grad_scale); unlabelled rows untouched. */
+int tb_head_dlogits(uint16_t *logits, const int64_t *targets, const float *lse, int64_t rows,
+                    int64_t cols, int64_t ld, int64_t col_offset, float grad_scale, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -177,3 +177,60 @@ def fused_head_loss(h16, w16, targets, denominator):
     dh = (dh16.float() * (1.0 / unit)).to(torch.float16)
     loss = token_loss.sum() / denom
     return loss, entropy, token_loss, correct, dh
+
+
+# ---- head, split form (partials per column range, merge) ---------------------------------------
+
+def head_partials(logits16, targets, col_offset, splits):
+    """[rows, splits, 6] fp64 partial states and [rows, splits] first-argmax indices of a slab of
+    fp16 logits holding vocabulary columns col_offset.. — the per-range online-softmax state the
+    reference's sweep 1 accumulates (head.py:54-72), one state per column range."""
+    z = logits16.double()
+    rows, cols = z.shape
+    chunk = -(-cols // splits)
+    chunk = -(-chunk // 8) * 8
+    part = torch.zeros((rows, splits, 6), dtype=torch.float64)
+    idx = torch.full((rows, splits), 2 ** 63 - 1, dtype=torch.int64)
+    part[:, :, 0] = float("-inf")
+    part[:, :, 3] = float("-inf")
+    tgt = targets.long()
+    for s in range(splits):
+        lo, hi = s * chunk, min(cols, (s + 1) * chunk)
+        if lo >= hi:
+            continue
+        zz = z[:, lo:hi]
+        m = zz.max(-1).values
+        e = torch.exp(zz - m[:, None])
+        part[:, s, 0] = m
+        part[:, s, 1] = e.sum(-1)
+        part[:, s, 2] = (e * zz).sum(-1)
+        part[:, s, 3] = m
+        idx[:, s] = zz.argmax(-1) + lo + col_offset
+        inside = (tgt >= col_offset + lo) & (tgt < col_offset + hi)
+        rows_in = torch.nonzero(inside).squeeze(1)
+        part[rows_in, s, 4] = z[rows_in, tgt[rows_in] - col_offset]
+        part[rows_in, s, 5] = 1.0
+    return part, idx
+
+
+def head_merge(parts, idxs, targets):
+    """Merge [groups, rows, splits, 6] partial states -> (lse, entropy, loss, correct)."""
+    p = parts.double().permute(1, 0, 2, 3).reshape(parts.shape[1], -1, 6)
+    ix = idxs.permute(1, 0, 2).reshape(idxs.shape[1], -1)
+    m = p[:, :, 0].max(-1).values
+    w = torch.where(torch.isinf(p[:, :, 0]), torch.zeros_like(p[:, :, 0]),
+                    torch.exp(p[:, :, 0] - m[:, None]))
+    s = (p[:, :, 1] * w).sum(-1)
+    dz = (p[:, :, 2] * w).sum(-1)
+    lse = m + torch.log(s)
+    entropy = lse - dz / s
+    best = p[:, :, 3].max(-1).values
+    cand = torch.where(p[:, :, 3] == best[:, None], ix, torch.full_like(ix, 2 ** 63 - 1))
+    arg = cand.min(-1).values
+    found = p[:, :, 5] > 0
+    zt = (p[:, :, 4] * found).sum(-1)
+    tgt = targets.long()
+    labelled = (tgt != IGNORE_INDEX) & found.any(-1)
+    loss = torch.where(labelled, lse - zt, torch.zeros_like(lse))
+    correct = labelled & (arg == tgt)
+    return lse, entropy, loss, correct

@@ -1,0 +1,121 @@
+"""The fused training step against the unpatched model, on a small random 4-bit Qwen2 + LoRA
+(the check of the reference's solution/test_model.py): loss, every LoRA gradient, TRL's entropy
+and token accuracy, and the per-row losses of Soup's rewind log."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def lora_model():
+    from testt_b200.qlora import build_qlora_model, qwen2_config
+
+    cfg = qwen2_config(vocab=1000, hidden=256, inter=512, layers=2, heads=4, kv_heads=2,
+                       max_pos=256, theta=10000.0)
+    return build_qlora_model(cfg, DEV, seed=0, weight_std=0.05, lora_b_std=0.05, bias_std=0.1,
+                             norm_jitter=True)
+
+
+def batch(vocab=1000):
+    g = torch.Generator().manual_seed(1)
+    lengths = [24, 15, 6]
+    seq = max(lengths)
+    ids = torch.randint(0, vocab, (len(lengths), seq), generator=g)
+    mask = torch.zeros_like(ids)
+    labels = torch.full_like(ids, -100)
+    for row, n in enumerate(lengths):
+        mask[row, :n] = 1
+        labels[row, n // 3:n] = ids[row, n // 3:n]
+    ids[mask == 0] = 0
+    return ids.to(DEV), mask.to(DEV), labels.to(DEV)
+
+
+def _row_losses(logits, labels):
+    """Per-row mean cross-entropy of the shifted labelled tokens, and their counts."""
+    shift, tgt = logits[:, :-1].float(), labels[:, 1:]
+    ce = torch.nn.functional.cross_entropy(shift.transpose(1, 2), tgt, ignore_index=-100,
+                                           reduction="none")
+    n = (tgt != -100).sum(1)
+    return [float(v) for v in (ce.sum(1) / n.clamp(min=1))], [int(v) for v in n]
+
+
+def run(model, fused):
+    from testt_b200.model import HeadStats
+    from testt_b200.trainer_patch import _FusedRequest, patch_forward
+
+    patch_forward()
+    ids, mask, labels = batch()
+    n_items = (labels[:, 1:] != -100).sum()
+    for p in model.parameters():
+        p.grad = None
+    torch.manual_seed(123)
+    with torch.autocast(DEV, dtype=torch.float16):
+        if fused:
+            with _FusedRequest():
+                out = model(input_ids=ids, attention_mask=mask, labels=labels,
+                            num_items_in_batch=n_items)
+        else:
+            out = model(input_ids=ids, attention_mask=mask, labels=labels,
+                        num_items_in_batch=n_items)
+    (out.loss * 1024).backward()
+    grads = {n: p.grad.detach().float().clone() for n, p in model.named_parameters()
+             if p.grad is not None}
+    if fused:
+        stats = out.logits
+        assert isinstance(stats, HeadStats)
+        entropy = float(stats.entropy_sum / mask.sum())
+        accuracy = float(stats.correct / stats.labelled)
+        rows = stats.row_losses()
+    else:
+        logits = out.logits.detach().float()
+        logp = torch.log_softmax(logits, -1)
+        per_token = -(logp.exp() * logp).sum(-1)
+        entropy = float((per_token * mask).sum() / mask.sum())
+        pred = logits[:, :-1].argmax(-1)
+        tgt = labels[:, 1:]
+        accuracy = float(((pred == tgt) & (tgt != -100)).sum() / (tgt != -100).sum())
+        rows = _row_losses(logits, labels)
+    return float(out.loss), grads, entropy, accuracy, rows
+
+
+def test_fused_step_matches_unpatched_model(lora_model):
+    from testt_b200 import _lib
+
+    ref = run(lora_model, fused=False)
+    _lib.reset_call_count()
+    got = run(lora_model, fused=True)
+    assert _lib.call_count() > 0, "the fused step must run the native kernels"
+    assert abs(got[0] - ref[0]) / ref[0] < 2e-3, (got[0], ref[0])
+    assert set(got[1]) == set(ref[1]) and ref[1]
+    for name, grad in ref[1].items():
+        rel = (got[1][name] - grad).norm() / grad.norm().clamp(min=1e-12)
+        assert rel < 2e-2, (name, float(rel))
+    assert abs(got[2] - ref[2]) / ref[2] < 2e-3, (got[2], ref[2])
+    assert abs(got[3] - ref[3]) < 1e-6 + 0.02, (got[3], ref[3])
+    assert got[4][1] == ref[4][1]
+    for a, b in zip(got[4][0], ref[4][0]):
+        assert abs(a - b) / b < 2e-3, (got[4][0], ref[4][0])
+
+
+def test_fused_path_declines_what_it_does_not_run(lora_model):
+    """Eval mode, no autocast and extra kwargs fall through to the original forward."""
+    from testt_b200.model import HeadStats, can_run
+    from testt_b200.trainer_patch import _FusedRequest, patch_forward
+
+    patch_forward()
+    ids, mask, labels = batch()
+    with torch.autocast(DEV, dtype=torch.float16):
+        assert can_run(lora_model, ids, mask, labels, {})
+        assert not can_run(lora_model, ids, mask, labels, {"output_attentions": True})
+        assert not can_run(lora_model, ids, mask, None, {})
+    assert not can_run(lora_model, ids, mask, labels, {})  # no fp16 autocast
+    lora_model.eval()
+    try:
+        with torch.autocast(DEV, dtype=torch.float16), _FusedRequest(), torch.no_grad():
+            out = lora_model(input_ids=ids, attention_mask=mask, labels=labels)
+        assert not isinstance(out.logits, HeadStats)
+    finally:
+        lora_model.train()

@@ -253,11 +253,14 @@ def test_rope_config3_full_size(lora):
     assert int((slot >= 0).sum()) == c["rows"]
     from testt_b200 import _lib
 
-    dqkv = torch.empty_like(dev(c["qkv"]))
-    _lib.call("tb_rope_pack_bwd", _lib.ptr(dev(c["dq"])), _lib.ptr(dev(c["dk"])),
-              _lib.ptr(dev(c["dv"])), _lib.ptr(dev(c["cos"])), _lib.ptr(dev(c["sin"])),
-              _lib.ptr(dev(c["pos_idx"])), _lib.ptr(dqkv), c["rows"], c["batch"], c["seq"],
-              synth.N_HEADS, synth.N_KV, synth.HEAD_DIM, _lib.stream_of(dqkv))
+    # keep every device tensor referenced until the kernel has run
+    g = {k: dev(c[k]) for k in ("dq", "dk", "dv", "cos", "sin", "pos_idx", "qkv")}
+    dqkv = torch.empty_like(g["qkv"])
+    _lib.call("tb_rope_pack_bwd", _lib.ptr(g["dq"]), _lib.ptr(g["dk"]), _lib.ptr(g["dv"]),
+              _lib.ptr(g["cos"]), _lib.ptr(g["sin"]), _lib.ptr(g["pos_idx"]), _lib.ptr(dqkv),
+              c["rows"], c["batch"], c["seq"], synth.N_HEADS, synth.N_KV, synth.HEAD_DIM,
+              _lib.stream_of(dqkv))
+    torch.cuda.synchronize()
     ref = ops.rope_pack_bwd(c["dq"], c["dk"], c["dv"], c["cos"], c["sin"], c["pos_idx"], *dims)
     assert_ulp(dqkv, ref, 1, "dqkv")
 
@@ -282,10 +285,11 @@ def test_rope_unsorted_positions_and_token_grid():
     for a, b in zip(got, ref):
         assert_ulp(a, b, 1, "slot grid")
     outs = [torch.zeros(batch, h, seq, d, dtype=torch.float16, device=DEV) for h in (nh, nkv, nkv)]
-    _lib.call("tb_rope_pack_fwd", _lib.ptr(qkv.to(DEV)), _lib.ptr(lq.to(DEV)),
-              _lib.ptr(lv.to(DEV)), 0, _lib.ptr(cos.to(DEV)), _lib.ptr(sin.to(DEV)),
-              _lib.ptr(pos.to(DEV)), None, *[_lib.ptr(o) for o in outs], rows, batch, seq, nh,
-              nkv, d, _lib.stream_of(outs[0]))
+    ins = [x.to(DEV) for x in (qkv, lq, lv, cos, sin, pos)]
+    _lib.call("tb_rope_pack_fwd", _lib.ptr(ins[0]), _lib.ptr(ins[1]), _lib.ptr(ins[2]), 0,
+              _lib.ptr(ins[3]), _lib.ptr(ins[4]), _lib.ptr(ins[5]), None,
+              *[_lib.ptr(o) for o in outs], rows, batch, seq, nh, nkv, d,
+              _lib.stream_of(outs[0]))
     torch.cuda.synchronize()
     for a, b in zip(outs, ref):
         assert_ulp(a, b, 1, "token grid")
@@ -368,3 +372,60 @@ def test_head_full_config4_properties():
     loss.backward()
     assert hh.grad is not None and torch.isfinite(hh.grad.float()).all()
     assert int((hh.grad[tg == -100] != 0).sum()) == 0, "unlabelled rows get no gradient"
+
+
+def _split_head_on_one_gpu(logits16, targets, groups, splits, scale):
+    """The vocab-sharded head's three kernels with `groups` shards emulated on one GPU."""
+    from testt_b200 import _lib
+    from testt_b200.dist import PART_FIELDS, shard_range
+
+    rows, vocab = logits16.shape
+    work = logits16.clone()
+    tg = targets.to(torch.int64).contiguous()
+    part = torch.empty((groups, rows, splits, PART_FIELDS), dtype=torch.float32, device=DEV)
+    pidx = torch.empty((groups, rows, splits), dtype=torch.int64, device=DEV)
+    slabs = []
+    for r in range(groups):
+        lo, hi = shard_range(vocab, r, groups)
+        slab = work[:, lo:hi].contiguous()
+        slabs.append((lo, hi, slab))
+        _lib.call("tb_head_partials", _lib.ptr(slab), _lib.ptr(tg), _lib.ptr(part[r]),
+                  _lib.ptr(pidx[r]), rows, hi - lo, slab.stride(0), lo, splits,
+                  _lib.stream_of(slab))
+    lse = torch.empty(rows, dtype=torch.float32, device=DEV)
+    ent, loss = torch.empty_like(lse), torch.empty_like(lse)
+    cor = torch.empty(rows, dtype=torch.int32, device=DEV)
+    _lib.call("tb_head_merge", _lib.ptr(part), _lib.ptr(pidx), _lib.ptr(tg), rows, groups, splits,
+              _lib.ptr(lse), _lib.ptr(ent), _lib.ptr(loss), _lib.ptr(cor), _lib.stream_of(lse))
+    for lo, hi, slab in slabs:
+        _lib.call("tb_head_dlogits", _lib.ptr(slab), _lib.ptr(tg), _lib.ptr(lse), rows, hi - lo,
+                  slab.stride(0), lo, scale, _lib.stream_of(slab))
+        work[:, lo:hi] = slab
+    return ent, loss, cor, work
+
+
+@pytest.mark.parametrize("groups,splits", [(1, 1), (1, 7), (3, 4), (8, 2)])
+def test_split_head_kernels_golden(groups, splits):
+    g = golden("head_stats")
+    ent, loss, cor, dl = _split_head_on_one_gpu(t(g["logits"], DEV), t(g["targets"], DEV), groups,
+                                                splits, float(g["grad_scale"]))
+    assert_rel(loss, g["loss"], 1e-4, "loss", floor=0.0)
+    assert_rel(ent, g["entropy"], 1e-4, "entropy", floor=0.0)
+    assert np.array_equal(cor.cpu().numpy(), g["correct"])
+    assert_ulp(dl, g["dlogits"], 1, "dlogits")
+
+
+@pytest.mark.parametrize("groups", [2, 8])
+def test_split_head_kernels_config4_rows(groups):
+    from testt_b200.head import _grad_unit
+
+    c = synth.config4("cpu", rows=48)
+    logits = (c["hidden"].float() @ c["weight"].float().t()).half()
+    scale = _grad_unit(c["n_labelled"]) / c["n_labelled"]
+    ent, loss, cor, dl = _split_head_on_one_gpu(logits.to(DEV), c["targets"].to(DEV), groups, 4,
+                                                scale)
+    rent, rloss, rcor, rdl = ops.head_stats_exact(logits, c["targets"], scale)
+    assert_rel(loss, rloss, 1e-4, "loss", floor=0.0)
+    assert_rel(ent, rent, 1e-4, "entropy", floor=0.0)
+    assert torch.equal(cor.cpu().bool(), rcor)
+    assert_ulp(dl, rdl, 1, "dlogits")

@@ -123,3 +123,25 @@ def test_head_loss_oracle_matches_reference():
     # the golden dh is the gradient of loss * 1024
     ref_dh = torch.from_numpy(g["dh"]).float()
     assert_rel(dh.float() * 1024.0, ref_dh, 2e-2, "dh")
+
+
+@pytest.mark.parametrize("groups,splits", [(1, 1), (1, 5), (3, 2), (8, 4)])
+def test_split_head_oracle_equals_whole_row(groups, splits):
+    """Partials over any split of the vocabulary merge to the whole-row statistics (the property
+    the vocab-sharded head relies on), ties included."""
+    from testt_b200.dist import shard_range
+
+    g = golden("head_stats")
+    logits, targets = t(g["logits"]), t(g["targets"])
+    vocab = logits.shape[1]
+    parts, idxs = [], []
+    for r in range(groups):
+        lo, hi = shard_range(vocab, r, groups)
+        p, i = ops.head_partials(logits[:, lo:hi], targets, lo, splits)
+        parts.append(p)
+        idxs.append(i)
+    lse, ent, loss, correct = ops.head_merge(torch.stack(parts), torch.stack(idxs), targets)
+    rent, rloss, rcorrect, _ = ops.head_stats_exact(logits, targets, 1.0)
+    assert torch.allclose(ent, rent, rtol=1e-9)
+    assert torch.allclose(loss, rloss, rtol=1e-9, atol=1e-12)
+    assert torch.equal(correct, rcorrect)

@@ -33,9 +33,13 @@ SIGNATURES = {
     "tb_swiglu_fwd": [_P, _P, _I64, _I64, _P],
     "tb_swiglu_bwd_inplace": [_P, _P, _I64, _I64, _P],
     "tb_head_stats_grad": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P],
+    "tb_head_partials": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _P],
+    "tb_head_merge": [_P, _P, _P, _I64, _I32, _I32, _P, _P, _P, _P, _P],
+    "tb_head_dlogits": [_P, _P, _P, _I64, _I64, _I64, _I64, _F, _P],
 }
 
 _lib = None
+_calls = 0
 
 
 class KernelError(RuntimeError):
@@ -66,10 +70,22 @@ def load():
 
 def call(name, *args):
     """Calls entry point `name`; raises KernelError with the library's message on failure."""
+    global _calls
+    _calls += 1
     rc = getattr(load(), name)(*args)
     if rc != 0:
         msg = load().tb_last_error().decode(errors="replace")
         raise KernelError(f"{name} failed ({rc}): {msg}")
+
+
+def call_count():
+    """Entry-point calls (each one kernel launch) since the last reset_call_count()."""
+    return _calls
+
+
+def reset_call_count():
+    global _calls
+    _calls = 0
 
 
 def ptr(t):

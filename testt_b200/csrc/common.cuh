@@ -10,6 +10,7 @@
 #include <cstdio>
 
 #include "../../include/testt_b200.h"
+#include "fastdiv.h"
 
 namespace tb {
 

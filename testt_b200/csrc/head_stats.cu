@@ -162,6 +162,179 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+
+// ---- split form: partials over column ranges, a merge, and the dlogits sweep ----------------
+// The same two sweeps as head_stats_grad_rows, split so that one row can be spread over several
+// CTAs (more parallelism for short chunks) and over several GPUs (a vocabulary-sharded head):
+// each (row, column range) yields a partial online-softmax state, states of one row are merged
+// in any grouping (max, rescaled sums, first argmax on ties), and the dlogits sweep then needs
+// only the merged lse.
+
+constexpr int kPartThreads = 256;
+constexpr int kPartFields = 6;  // max, sum e, sum e z, best value, z[target], target found
+
+__device__ __forceinline__ void block_merge(Online &o, Online *sh) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) o = online_merge(o, shfl_online(o, off));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) sh[warp] = o;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    o = lane < nw ? sh[lane] : Online{-CUDART_INF_F, 0.f, 0.f, -CUDART_INF_F, 0x7fffffffffffffffLL};
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) o = online_merge(o, shfl_online(o, off));
+  }
+}
+
+__global__ void __launch_bounds__(kPartThreads)
+    head_partials_kernel(const uint16_t *__restrict__ logits, const int64_t *__restrict__ targets,
+                         float *__restrict__ part, int64_t *__restrict__ part_idx, int64_t cols,
+                         int64_t ld, int64_t col_offset, int64_t chunk, bool vec) {
+  __shared__ Online sh[kPartThreads / 32];
+  const int64_t row = blockIdx.y;
+  const int split = blockIdx.x, splits = gridDim.x;
+  const int64_t lo = (int64_t)split * chunk;
+  const int64_t hi = lo + chunk < cols ? lo + chunk : cols;
+  const uint16_t *base = logits + row * ld;
+  const int64_t target = __ldg(targets + row);
+  Online o{-CUDART_INF_F, 0.f, 0.f, -CUDART_INF_F, 0x7fffffffffffffffLL};
+  int64_t vlo = lo, vend = lo;
+  if (vec && lo < hi) {
+    vend = lo + ((hi - lo) / 8) * 8;
+    for (int64_t c0 = lo + threadIdx.x * 8; c0 < vend; c0 += (int64_t)kPartThreads * 8 * kUnroll) {
+      float z[kUnroll][8];
+#pragma unroll
+      for (int r = 0; r < kUnroll; ++r) {
+        const int64_t c = c0 + (int64_t)r * kPartThreads * 8;
+        if (c < vend) load8h(base + c, z[r]);
+      }
+#pragma unroll
+      for (int r = 0; r < kUnroll; ++r) {
+        const int64_t c = c0 + (int64_t)r * kPartThreads * 8;
+        if (c < vend) {
+          float lm = z[r][0];
+#pragma unroll
+          for (int k = 1; k < 8; ++k) lm = fmaxf(lm, z[r][k]);
+          if (lm > o.m) {
+            const float sc = __expf(o.m - lm);
+            o.s *= sc;
+            o.dz *= sc;
+            o.m = lm;
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float e = __expf(z[r][k] - o.m);
+            o.s += e;
+            o.dz += e * z[r][k];
+            if (z[r][k] > o.best) {
+              o.best = z[r][k];
+              o.idx = col_offset + c + k;
+            }
+          }
+        }
+      }
+    }
+    vlo = vend;
+  }
+  for (int64_t c = vlo + threadIdx.x; c < hi; c += kPartThreads)
+    online_add(o, __half2float(__ushort_as_half(base[c])), col_offset + c);
+  block_merge(o, sh);
+  if (threadIdx.x == 0) {
+    float *out = part + (row * splits + split) * kPartFields;
+    out[0] = o.m;
+    out[1] = o.s;
+    out[2] = o.dz;
+    out[3] = o.best;
+    const bool found = target >= col_offset + lo && target < col_offset + hi;
+    out[4] = found ? __half2float(__ushort_as_half(base[target - col_offset])) : 0.f;
+    out[5] = found ? 1.f : 0.f;
+    part_idx[row * splits + split] = o.idx;
+  }
+}
+
+// One warp per row over n_groups x splits partial states laid out [group][row][split].
+__global__ void head_merge_kernel(const float *__restrict__ part,
+                                  const int64_t *__restrict__ part_idx,
+                                  const int64_t *__restrict__ targets, int64_t rows, int n_groups,
+                                  int splits, float *__restrict__ lse_out,
+                                  float *__restrict__ entropy, float *__restrict__ loss,
+                                  int32_t *__restrict__ correct) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  Online o{-CUDART_INF_F, 0.f, 0.f, -CUDART_INF_F, 0x7fffffffffffffffLL};
+  float zt = 0.f, found = 0.f;
+  const int n = n_groups * splits;
+  for (int p = lane; p < n; p += 32) {
+    const int g = p / splits, sp = p - g * splits;
+    const int64_t at = ((int64_t)g * rows + row) * splits + sp;
+    const float *q = part + at * kPartFields;
+    Online b{q[0], q[1], q[2], q[3], part_idx[at]};
+    o = online_merge(o, b);
+    if (q[5] != 0.f && found == 0.f) {
+      zt = q[4];
+      found = 1.f;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    o = online_merge(o, shfl_online(o, off));
+    const float zo = __shfl_xor_sync(0xffffffffu, zt, off);
+    const float fo = __shfl_xor_sync(0xffffffffu, found, off);
+    if (found == 0.f && fo != 0.f) {
+      zt = zo;
+      found = fo;
+    }
+  }
+  if (lane == 0) {
+    const int64_t target = targets[row];
+    const bool labelled = target != -100 && found != 0.f;
+    const float lse = o.m + logf(o.s);
+    lse_out[row] = lse;
+    entropy[row] = lse - o.dz / o.s;
+    loss[row] = labelled ? lse - zt : 0.f;
+    correct[row] = (labelled && o.idx == target) ? 1 : 0;
+  }
+}
+
+// dlogits over labelled rows, in place: flat over 8-value vectors (n < 2^32 vectors).
+__global__ void __launch_bounds__(256)
+    head_dlogits_kernel(uint16_t *__restrict__ logits, const int64_t *__restrict__ targets,
+                        const float *__restrict__ lse, uint32_t n, FastDiv vpr, int64_t ld,
+                        int64_t col_offset, float grad_scale) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    uint32_t row, v;
+    vpr.divmod(i, row, v);
+    const int64_t target = __ldg(targets + row);
+    if (target == -100) continue;
+    const float l = __ldg(lse + row);
+    uint16_t *p = logits + (int64_t)row * ld + (int64_t)v * 8;
+    float z[8];
+    load8h_rw(p, z);
+    const int64_t c0 = col_offset + (int64_t)v * 8;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) z[k] = (__expf(z[k] - l) - (c0 + k == target ? 1.f : 0.f)) * grad_scale;
+    store8h(p, z);
+  }
+}
+
+__global__ void head_dlogits_any(uint16_t *logits, const int64_t *targets, const float *lse,
+                                 int64_t rows, int64_t cols, int64_t ld, int64_t col_offset,
+                                 float grad_scale) {
+  const int64_t n = rows * cols;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / cols, c = i - row * cols;
+    const int64_t target = targets[row];
+    if (target == -100) continue;
+    uint16_t *p = logits + row * ld + c;
+    const float z = __half2float(__ushort_as_half(*p));
+    const float g = (__expf(z - lse[row]) - (col_offset + c == target ? 1.f : 0.f)) * grad_scale;
+    *p = __half_as_ushort(__float2half_rn(g));
+  }
+}
+
 }  // namespace
 }  // namespace tb
 
@@ -181,4 +354,65 @@ extern "C" int tb_head_stats_grad(uint16_t *logits, const int64_t *targets, floa
   head_stats_grad_rows<<<(unsigned)rows, kThreads, 0, as_stream(stream)>>>(
       logits, targets, entropy, loss, correct, vocab, ld, grad_scale, vec);
   return check_launch("head_stats_grad");
+}
+
+extern "C" int tb_head_partials(const uint16_t *logits, const int64_t *targets, float *part,
+                                int64_t *part_idx, int64_t rows, int64_t cols, int64_t ld,
+                                int64_t col_offset, int32_t splits, void *stream) {
+  if (rows < 0 || cols <= 0 || ld < cols || splits < 1 || col_offset < 0)
+    return set_error(TB_EINVAL, "head_partials: rows %lld cols %lld ld %lld splits %d",
+                     (long long)rows, (long long)cols, (long long)ld, splits);
+  if (rows == 0) return TB_OK;
+  if (!logits || !targets || !part || !part_idx)
+    return set_error(TB_EINVAL, "head_partials: all pointers are required");
+  if (rows > 65535) return set_error(TB_EINVAL, "head_partials: at most 65535 rows per call");
+  const bool vec = aligned(logits, 16) && ld % 8 == 0;
+  int64_t chunk = (cols + splits - 1) / splits;
+  chunk = ((chunk + 7) / 8) * 8;
+  const dim3 grid((unsigned)splits, (unsigned)rows);
+  head_partials_kernel<<<grid, kPartThreads, 0, as_stream(stream)>>>(
+      logits, targets, part, part_idx, cols, ld, col_offset, chunk, vec);
+  return check_launch("head_partials");
+}
+
+extern "C" int tb_head_merge(const float *part, const int64_t *part_idx, const int64_t *targets,
+                             int64_t rows, int32_t n_groups, int32_t splits, float *lse,
+                             float *entropy, float *loss, int32_t *correct, void *stream) {
+  if (rows < 0 || n_groups < 1 || splits < 1)
+    return set_error(TB_EINVAL, "head_merge: rows %lld groups %d splits %d", (long long)rows,
+                     n_groups, splits);
+  if (rows == 0) return TB_OK;
+  if (!part || !part_idx || !targets || !lse || !entropy || !loss || !correct)
+    return set_error(TB_EINVAL, "head_merge: all pointers are required");
+  const int warps = 8;
+  const unsigned blocks = (unsigned)((rows + warps - 1) / warps);
+  head_merge_kernel<<<blocks, warps * 32, 0, as_stream(stream)>>>(
+      part, part_idx, targets, rows, n_groups, splits, lse, entropy, loss, correct);
+  return check_launch("head_merge");
+}
+
+extern "C" int tb_head_dlogits(uint16_t *logits, const int64_t *targets, const float *lse,
+                               int64_t rows, int64_t cols, int64_t ld, int64_t col_offset,
+                               float grad_scale, void *stream) {
+  if (rows < 0 || cols <= 0 || ld < cols || col_offset < 0)
+    return set_error(TB_EINVAL, "head_dlogits: rows %lld cols %lld ld %lld", (long long)rows,
+                     (long long)cols, (long long)ld);
+  if (rows == 0) return TB_OK;
+  if (!logits || !targets || !lse) return set_error(TB_EINVAL, "head_dlogits: all pointers are required");
+  cudaStream_t st = as_stream(stream);
+  const int64_t nvec = rows * (cols / 8);
+  const int64_t cap = (int64_t)sm_count() * 8;
+  if (cols % 8 == 0 && ld % 8 == 0 && aligned(logits, 16) && nvec < (1LL << 31)) {
+    int64_t blocks = (nvec + 255) / 256;
+    if (blocks > cap) blocks = cap;
+    head_dlogits_kernel<<<(unsigned)blocks, 256, 0, st>>>(logits, targets, lse, (uint32_t)nvec,
+                                                         FastDiv((uint32_t)(cols / 8)), ld,
+                                                         col_offset, grad_scale);
+  } else {
+    int64_t blocks = (rows * cols + 255) / 256;
+    if (blocks > cap) blocks = cap;
+    head_dlogits_any<<<(unsigned)blocks, 256, 0, st>>>(logits, targets, lse, rows, cols, ld,
+                                                      col_offset, grad_scale);
+  }
+  return check_launch("head_dlogits");
 }

@@ -8,8 +8,9 @@
 // Lane l of a warp handles words base + 32*k + l (k < kUnroll), so every 4-byte load and every
 // 16-byte store of a warp instruction is contiguous (128 B in, 512 B out). A word's 4 bytes lie
 // in one absmax block whenever the block holds a multiple of 8 values, so the scale is computed
-// once per word. Arithmetic is bit-exact with the reference: each mul/add rounded on its own
-// (__fmul_rn / __fadd_rn, no FMA contraction), then one round-to-nearest-even to fp16.
+// once per word; block indices use 32-bit invariant division (FastDiv), never 64-bit division.
+// Arithmetic is bit-exact with the reference: each mul/add rounded on its own (__fmul_rn /
+// __fadd_rn, no FMA contraction), then one round-to-nearest-even to fp16.
 #include "common.cuh"
 
 namespace tb {
@@ -30,8 +31,8 @@ struct Nf4Job {
   const float *table[kMaxW];
   uint16_t *out[kMaxW];
   int64_t start[kMaxW + 1];  // prefix sums of units (words for the vector kernel, else bytes)
-  int32_t half_qblock[kMaxW];  // packed bytes per absmax block
-  int32_t qblock2[kMaxW];
+  FastDiv block_div[kMaxW];  // packed byte index -> absmax block (divisor qblock / 2)
+  FastDiv nest_div[kMaxW];   // absmax block -> nested block (divisor qblock2)
 };
 
 __device__ __forceinline__ int find_weight(const Nf4Job &job, int64_t u) {
@@ -42,10 +43,10 @@ __device__ __forceinline__ int find_weight(const Nf4Job &job, int64_t u) {
   return j;
 }
 
-__device__ __forceinline__ float block_scale(const Nf4Job &job, int j, int64_t b) {
+__device__ __forceinline__ float block_scale(const Nf4Job &job, int j, uint32_t b) {
   if (job.absmax_f32[j] != nullptr) return __ldg(job.absmax_f32[j] + b);
   const int code = __ldg(job.absmax_u8[j] + b);
-  const float a = __fmul_rn(__ldg(job.code2[j] + code), __ldg(job.absmax2[j] + b / job.qblock2[j]));
+  const float a = __fmul_rn(__ldg(job.code2[j] + code), __ldg(job.absmax2[j] + job.nest_div[j].div(b)));
   return __fadd_rn(a, __ldg(job.offset[j]));
 }
 
@@ -60,32 +61,33 @@ __global__ void __launch_bounds__(kThreads) nf4_unpack_words(const __grid_consta
   const int64_t warps = (int64_t)gridDim.x * (kThreads / 32);
   for (int64_t w = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
        w * 32 * kUnroll < total; w += warps) {
-    uint32_t word[kUnroll];
-    int64_t unit[kUnroll];
+    uint32_t word[kUnroll], local[kUnroll];
+    int wj[kUnroll];
+    float scale[kUnroll];
 #pragma unroll
     for (int k = 0; k < kUnroll; ++k) {
-      unit[k] = (w * kUnroll + k) * 32 + lane;
-      word[k] = 0;
-      if (unit[k] < total) {
-        const int j = find_weight(job, unit[k]);
-        const int64_t local = unit[k] - job.start[j];
-        word[k] = __ldg(reinterpret_cast<const uint32_t *>(job.packed[j]) + local);
+      const int64_t unit = (w * kUnroll + k) * 32 + lane;
+      wj[k] = -1;
+      if (unit < total) {
+        const int j = find_weight(job, unit);
+        wj[k] = j;
+        local[k] = (uint32_t)(unit - job.start[j]);
+        word[k] = __ldg(reinterpret_cast<const uint32_t *>(job.packed[j]) + local[k]);
+        scale[k] = block_scale(job, j, job.block_div[j].div(local[k] * 4u));
       }
     }
 #pragma unroll
     for (int k = 0; k < kUnroll; ++k) {
-      if (unit[k] >= total) continue;
-      const int j = find_weight(job, unit[k]);
-      const int64_t local = unit[k] - job.start[j];
-      const float scale = block_scale(job, j, (local * 4) / job.half_qblock[j]);
+      const int j = wj[k];
+      if (j < 0) continue;
       float f[8];
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
         const uint32_t byte = (word[k] >> (8 * b)) & 0xffu;
-        f[2 * b] = __fmul_rn(table[j][byte >> 4], scale);
-        f[2 * b + 1] = __fmul_rn(table[j][byte & 15u], scale);
+        f[2 * b] = __fmul_rn(table[j][byte >> 4], scale[k]);
+        f[2 * b + 1] = __fmul_rn(table[j][byte & 15u], scale[k]);
       }
-      store8h_cs(job.out[j] + local * 8, f);
+      store8h_cs(job.out[j] + (size_t)local[k] * 8, f);
     }
   }
 }
@@ -96,20 +98,20 @@ __global__ void __launch_bounds__(kThreads) nf4_unpack_bytes(const __grid_consta
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < total; u += stride) {
     const int j = find_weight(job, u);
-    const int64_t local = u - job.start[j];
-    const float scale = block_scale(job, j, local / job.half_qblock[j]);
+    const uint32_t local = (uint32_t)(u - job.start[j]);
+    const float scale = block_scale(job, j, job.block_div[j].div(local));
     const uint32_t byte = __ldg(job.packed[j] + local);
     const float hi = __fmul_rn(__ldg(job.table[j] + (byte >> 4)), scale);
     const float lo = __fmul_rn(__ldg(job.table[j] + (byte & 15u)), scale);
-    job.out[j][2 * local] = __half_as_ushort(__float2half_rn(hi));
-    job.out[j][2 * local + 1] = __half_as_ushort(__float2half_rn(lo));
+    job.out[j][2 * (size_t)local] = __half_as_ushort(__float2half_rn(hi));
+    job.out[j][2 * (size_t)local + 1] = __half_as_ushort(__float2half_rn(lo));
   }
 }
 
-int launch(Nf4Job &job, const int64_t *n_bytes, cudaStream_t stream) {
+int launch(Nf4Job &job, const int64_t *n_bytes, const int32_t *half_qblock, cudaStream_t stream) {
   bool words = true;
   for (int j = 0; j < job.n; ++j) {
-    words = words && n_bytes[j] % 4 == 0 && job.half_qblock[j] % 4 == 0 &&
+    words = words && n_bytes[j] % 4 == 0 && half_qblock[j] % 4 == 0 &&
             aligned(job.packed[j], 4) && aligned(job.out[j], 16);
   }
   job.start[0] = 0;
@@ -117,7 +119,8 @@ int launch(Nf4Job &job, const int64_t *n_bytes, cudaStream_t stream) {
   for (int j = job.n; j < kMaxW; ++j) job.start[j + 1] = job.start[job.n];
   const int64_t total = job.start[job.n];
   if (total == 0) return TB_OK;
-  const int64_t cap = (int64_t)sm_count() * 16;
+  // enough resident warps to keep HBM busy, then a grid-stride loop
+  const int64_t cap = (int64_t)sm_count() * (2048 / kThreads);
   if (words) {
     const int64_t per_block = (int64_t)kThreads * kUnroll;
     int64_t blocks = (total + per_block - 1) / per_block;
@@ -133,38 +136,40 @@ int launch(Nf4Job &job, const int64_t *n_bytes, cudaStream_t stream) {
 
 int fill_common(Nf4Job &job, int j, const uint8_t *packed, const float *table, uint16_t *out,
                 int64_t n_bytes, int32_t qblock) {
-  if (packed == nullptr || table == nullptr || out == nullptr)
-    return set_error(TB_EINVAL, "nf4_unpack: weight %d: packed, nf4 table and out are required", j);
-  if (n_bytes < 0) return set_error(TB_EINVAL, "nf4_unpack: weight %d: n_bytes < 0", j);
   if (qblock <= 0 || qblock % 2)
     return set_error(TB_EINVAL, "nf4_unpack: weight %d: blocksize %d must be positive and even", j,
                      qblock);
+  if (n_bytes < 0 || n_bytes >= (1LL << 32))
+    return set_error(TB_EINVAL, "nf4_unpack: weight %d: n_bytes %lld out of range [0, 2^32)", j,
+                     (long long)n_bytes);
+  if (packed == nullptr || table == nullptr || out == nullptr)
+    return set_error(TB_EINVAL, "nf4_unpack: weight %d: packed, nf4 table and out are required", j);
   job.packed[j] = packed;
   job.table[j] = table;
   job.out[j] = out;
-  job.half_qblock[j] = qblock / 2;
+  job.block_div[j] = FastDiv((uint32_t)(qblock / 2));
   job.absmax_f32[j] = nullptr;
   job.absmax_u8[j] = nullptr;
   job.code2[j] = nullptr;
   job.absmax2[j] = nullptr;
   job.offset[j] = nullptr;
-  job.qblock2[j] = 1;
+  job.nest_div[j] = FastDiv(1);
   return TB_OK;
 }
 
 int fill_nested(Nf4Job &job, int j, const uint8_t *absmax_u8, const float *code2,
                 const float *absmax2, const float *offset, int32_t qblock2) {
+  if (qblock2 <= 0)
+    return set_error(TB_EINVAL, "nf4_unpack: weight %d: nested blocksize %d", j, qblock2);
   if (absmax_u8 == nullptr || code2 == nullptr || absmax2 == nullptr || offset == nullptr)
     return set_error(TB_EINVAL,
                      "nf4_unpack: weight %d: nested layout needs absmax_u8, code2, absmax2, offset",
                      j);
-  if (qblock2 <= 0)
-    return set_error(TB_EINVAL, "nf4_unpack: weight %d: nested blocksize %d", j, qblock2);
   job.absmax_u8[j] = absmax_u8;
   job.code2[j] = code2;
   job.absmax2[j] = absmax2;
   job.offset[j] = offset;
-  job.qblock2[j] = qblock2;
+  job.nest_div[j] = FastDiv((uint32_t)qblock2);
   return TB_OK;
 }
 
@@ -182,7 +187,8 @@ extern "C" int tb_nf4_unpack_nested(const uint8_t *packed, const uint8_t *absmax
   int rc = fill_common(job, 0, packed, nf4_table, out, n_bytes, qblock);
   if (rc == TB_OK) rc = fill_nested(job, 0, absmax_u8, code2, absmax2, offset, qblock2);
   if (rc != TB_OK) return rc;
-  return launch(job, &n_bytes, as_stream(stream));
+  const int32_t half = qblock / 2;
+  return launch(job, &n_bytes, &half, as_stream(stream));
 }
 
 extern "C" int tb_nf4_unpack_plain(const uint8_t *packed, const float *absmax,
@@ -194,7 +200,8 @@ extern "C" int tb_nf4_unpack_plain(const uint8_t *packed, const float *absmax,
   if (rc != TB_OK) return rc;
   if (absmax == nullptr) return set_error(TB_EINVAL, "nf4_unpack_plain: absmax is required");
   job.absmax_f32[0] = absmax;
-  return launch(job, &n_bytes, as_stream(stream));
+  const int32_t half = qblock / 2;
+  return launch(job, &n_bytes, &half, as_stream(stream));
 }
 
 extern "C" int tb_nf4_unpack_multi(int32_t n_weights, const uint8_t *const *packed,
@@ -211,9 +218,11 @@ extern "C" int tb_nf4_unpack_multi(int32_t n_weights, const uint8_t *const *pack
     return set_error(TB_EINVAL, "nf4_unpack_multi: packed, nf4_table, out, n_bytes, qblock required");
   Nf4Job job{};
   job.n = n_weights;
+  int32_t half[kMaxW];
   for (int j = 0; j < n_weights; ++j) {
     int rc = fill_common(job, j, packed[j], nf4_table[j], out[j], n_bytes[j], qblock[j]);
     if (rc != TB_OK) return rc;
+    half[j] = qblock[j] / 2;
     const float *plain = absmax_f32 ? absmax_f32[j] : nullptr;
     if (plain != nullptr) {
       job.absmax_f32[j] = plain;
@@ -224,5 +233,5 @@ extern "C" int tb_nf4_unpack_multi(int32_t n_weights, const uint8_t *const *pack
       if (rc != TB_OK) return rc;
     }
   }
-  return launch(job, n_bytes, as_stream(stream));
+  return launch(job, n_bytes, half, as_stream(stream));
 }

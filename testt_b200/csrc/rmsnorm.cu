@@ -25,35 +25,42 @@ __global__ void rmsnorm_fwd_vec(const float *__restrict__ x, const uint16_t *__r
   const int64_t row = blockIdx.x;
   const int nch = (int)(hidden / 8);
   const int64_t base = row * hidden;
-  float v[NCH][8];
-  float ss = 0.f;
+  // every load of the row is issued before the reduction: x, delta, weight and the pad row
+  const int64_t dest = ypad != nullptr ? __ldg(pad_idx + row) * hidden : 0;
+  float v[NCH][8], wv[NCH][8];
 #pragma unroll
   for (int i = 0; i < NCH; ++i) {
     const int c = threadIdx.x + i * blockDim.x;
     if (c < nch) {
       load8f(x + base + c * 8, v[i]);
+      load8f(w + c * 8, wv[i]);
       if (delta != nullptr) {
         float d[8];
         load8h(delta + base + c * 8, d);
 #pragma unroll
         for (int k = 0; k < 8; ++k) v[i][k] = v[i][k] + d[k];
-        store8f(s_out + base + c * 8, v[i]);
       }
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NCH; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (c < nch) {
+      if (delta != nullptr) store8f(s_out + base + c * 8, v[i]);
 #pragma unroll
       for (int k = 0; k < 8; ++k) ss += v[i][k] * v[i][k];
     }
   }
   const float total = block_sum(ss, red);
   const float rstd = 1.0f / sqrtf(total / (float)hidden + eps);
-  const int64_t dest = ypad != nullptr ? __ldg(pad_idx + row) * hidden : 0;
 #pragma unroll
   for (int i = 0; i < NCH; ++i) {
     const int c = threadIdx.x + i * blockDim.x;
     if (c < nch) {
-      float wv[8], o[8];
-      load8f(w + c * 8, wv);
+      float o[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) o[k] = __fmul_rn(__fmul_rn(v[i][k], rstd), wv[k]);
+      for (int k = 0; k < 8; ++k) o[k] = __fmul_rn(__fmul_rn(v[i][k], rstd), wv[i][k]);
       store8h(y + base + c * 8, o);
       if (ypad != nullptr) store8f(ypad + dest + c * 8, o);
     }
@@ -74,12 +81,14 @@ __global__ void rmsnorm_bwd_vec(const float *__restrict__ s, const float *__rest
   const int64_t base = row * hidden;
   const int64_t src = dypad != nullptr ? __ldg(pad_idx + row) * hidden : 0;
   const float rstd = __ldg(rstd_in + row);
-  float g[NCH][8], n[NCH][8];
+  // g, n and the residual gradient are all loaded before the reduction
+  float g[NCH][8], n[NCH][8], r[NCH][8];
   float dot = 0.f;
 #pragma unroll
   for (int i = 0; i < NCH; ++i) {
     const int c = threadIdx.x + i * blockDim.x;
     if (c < nch) {
+      float wv[8];
       if (dy != nullptr) {
         load8h(dy + base + c * 8, g[i]);
       } else {
@@ -92,13 +101,18 @@ __global__ void rmsnorm_bwd_vec(const float *__restrict__ s, const float *__rest
 #pragma unroll
         for (int k = 0; k < 8; ++k) g[i][k] = g[i][k] + p[k];
       }
-      float wv[8], sv[8];
+      if (ds != nullptr) {
+        load8f(ds + base + c * 8, r[i]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) r[i][k] = 0.f;
+      }
       load8f(w + c * 8, wv);
-      load8f(s + base + c * 8, sv);
+      load8f(s + base + c * 8, n[i]);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         g[i][k] = g[i][k] * wv[k];
-        n[i][k] = sv[k] * rstd;
+        n[i][k] = n[i][k] * rstd;
         dot += g[i][k] * n[i][k];
       }
     }
@@ -110,12 +124,9 @@ __global__ void rmsnorm_bwd_vec(const float *__restrict__ s, const float *__rest
     if (c < nch) {
       float o[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) o[k] = (g[i][k] - n[i][k] * proj) * rstd;
-      if (ds != nullptr) {
-        float d[8];
-        load8f(ds + base + c * 8, d);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) o[k] = o[k] + d[k];
+      for (int k = 0; k < 8; ++k) {
+        o[k] = (g[i][k] - n[i][k] * proj) * rstd;
+        if (ds != nullptr) o[k] = o[k] + r[i][k];
       }
       store8f(dx + base + c * 8, o);
       if (ddelta != nullptr) store8h(ddelta + base + c * 8, o);

@@ -2,10 +2,11 @@
 // forward and backward, for sm_100a.
 //
 // Reference: solution/rope.py:24-75 (rope_pack_fwd_kernel), :78-128 (rope_pack_bwd_kernel),
-// :136-176 (RopePack). One warp per token (backward) or per padded slot (forward with a slot map).
-// Lane l owns 8 consecutive dims d0..d0+7 of one head half and the matching dims of the other
-// half (the rotation pairs x[d] with x[d + d/2]), so the cos/sin values of the slot are loaded
-// once per lane and reused for every head; all loads and stores are 16-byte vectors. With a slot
+// :136-176 (RopePack). One CTA per token (backward) or per padded slot (forward with a slot map),
+// one thread per (head row, 8-dim group): thread t owns dims d0..d0+7 of one half of head row
+// t / (d/16) and the matching dims of the other half (the rotation pairs x[d] with x[d + d/2]).
+// For Qwen2.5-1.5B (12 q + 2 k + 2 v heads, d = 128) that is 128 threads whose loads are all
+// independent, so a slot costs one memory latency; all loads and stores are 16-byte vectors. With a slot
 // map (slot_tok) the forward kernel covers every padded slot and writes the zero rows of padding
 // itself, which removes the three zero-fills of the outputs the reference does before its launch
 // (solution/rope.py:141-143).
@@ -14,7 +15,7 @@
 namespace tb {
 namespace {
 
-constexpr int kWarpsPerBlock = 4;
+constexpr int kMaxThreads = 512;
 
 struct RopeDims {
   int64_t rows, batch, seq;
@@ -35,36 +36,34 @@ __device__ __forceinline__ void zero8(float (&f)[8]) {
   for (int k = 0; k < 8; ++k) f[k] = 0.f;
 }
 
-// kSlots: one warp per padded slot, tokens found through slot_tok, padding rows zero-filled.
+// kSlots: one CTA per padded slot, tokens found through slot_tok, padding rows zero-filled.
 template <bool kSlots, bool kLoraFp32>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+__global__ void __launch_bounds__(kMaxThreads)
     rope_fwd_vec(const uint16_t *__restrict__ qkv, const void *__restrict__ lq,
                  const void *__restrict__ lv, const float *__restrict__ cosv,
                  const float *__restrict__ sinv, const int64_t *__restrict__ pos_idx,
                  const int32_t *__restrict__ slot_tok, uint16_t *__restrict__ q,
-                 uint16_t *__restrict__ k, uint16_t *__restrict__ v, RopeDims dm) {
-  const int lane = threadIdx.x & 31;
-  const int64_t unit = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+                 uint16_t *__restrict__ k, uint16_t *__restrict__ v, RopeDims dm, FastDiv seq_div) {
+  const int64_t unit = blockIdx.x;
   const int64_t slots = dm.batch * dm.seq;
   int64_t tok, pos;
   if (kSlots) {
-    if (unit >= slots) return;
     pos = unit;
     tok = __ldg(slot_tok + unit);
   } else {
-    if (unit >= dm.rows) return;
     tok = unit;
     pos = __ldg(pos_idx + unit);
     if (pos < 0 || pos >= slots) return;  // out-of-range position: nothing to write
   }
-  const int64_t b = pos / dm.seq, t = pos % dm.seq;
+  uint32_t b32, t32;
+  seq_div.divmod((uint32_t)pos, b32, t32);
+  const int64_t b = b32, t = t32;
   const int D = dm.d, H = dm.half;
-  const int lph = H / 8;            // lanes per head
-  const int hps = 32 / lph;         // heads per warp step
-  const int hsub = lane / lph;
-  const int d0 = (lane % lph) * 8;
+  const int lph = H / 8;                    // threads per head row
+  const int rows_per_pass = blockDim.x / lph;
+  if ((int)threadIdx.x >= rows_per_pass * lph) return;  // no __syncthreads below
+  const int d0 = (threadIdx.x % lph) * 8;
   const int total = dm.nh + 2 * dm.nkv;
-  if (hsub >= hps) return;
   const bool real = !kSlots || (tok >= 0 && tok < dm.rows);
 
   float c1[8], c2[8], s1[8], s2[8];
@@ -75,7 +74,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     load8f(sinv + t * D + H + d0, s2);
   }
   const int64_t W = (int64_t)total * D;
-  for (int hr = hsub; hr < total; hr += hps) {
+  for (int hr = threadIdx.x / lph; hr < total; hr += rows_per_pass) {
     float x1[8], x2[8], o1[8], o2[8];
     uint16_t *dst;
     if (hr < dm.nh) {
@@ -126,22 +125,22 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
   }
 }
 
-__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+__global__ void __launch_bounds__(kMaxThreads)
     rope_bwd_vec(const uint16_t *__restrict__ dq, const uint16_t *__restrict__ dk,
                  const uint16_t *__restrict__ dv, const float *__restrict__ cosv,
                  const float *__restrict__ sinv, const int64_t *__restrict__ pos_idx,
-                 uint16_t *__restrict__ dqkv, RopeDims dm) {
-  const int lane = threadIdx.x & 31;
-  const int64_t tok = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
-  if (tok >= dm.rows) return;
+                 uint16_t *__restrict__ dqkv, RopeDims dm, FastDiv seq_div) {
+  const int64_t tok = blockIdx.x;
   const int64_t slots = dm.batch * dm.seq;
   const int64_t pos = __ldg(pos_idx + tok);
   const bool inside = pos >= 0 && pos < slots;
-  const int64_t b = inside ? pos / dm.seq : 0, t = inside ? pos % dm.seq : 0;
+  uint32_t b32 = 0, t32 = 0;
+  if (inside) seq_div.divmod((uint32_t)pos, b32, t32);
+  const int64_t b = b32, t = t32;
   const int D = dm.d, H = dm.half;
-  const int lph = H / 8, hps = 32 / lph, hsub = lane / lph, d0 = (lane % lph) * 8;
+  const int lph = H / 8, rows_per_pass = blockDim.x / lph, d0 = (threadIdx.x % lph) * 8;
+  if ((int)threadIdx.x >= rows_per_pass * lph) return;  // no __syncthreads below
   const int total = dm.nh + 2 * dm.nkv;
-  if (hsub >= hps) return;
   float c1[8], c2[8], s1[8], s2[8];
   load8f(cosv + t * D + d0, c1);
   load8f(cosv + t * D + H + d0, c2);
@@ -149,7 +148,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
   load8f(sinv + t * D + H + d0, s2);
   const int64_t W = (int64_t)total * D;
   uint16_t *row = dqkv + tok * W;
-  for (int hr = hsub; hr < total; hr += hps) {
+  for (int hr = threadIdx.x / lph; hr < total; hr += rows_per_pass) {
     const uint16_t *src;
     bool rotate = true;
     if (hr < dm.nh) {
@@ -301,8 +300,18 @@ int check_dims(const char *what, int64_t rows, int64_t batch, int64_t seq, int n
   if (rows < 0 || batch < 0 || seq <= 0 || nh <= 0 || nkv < 0 || d <= 0 || d % 2)
     return set_error(TB_EINVAL, "%s: bad dims rows=%lld batch=%lld seq=%lld nh=%d nkv=%d d=%d",
                      what, (long long)rows, (long long)batch, (long long)seq, nh, nkv, d);
-  if (rows > 0x7fffffffLL) return set_error(TB_EINVAL, "%s: too many rows", what);
+  if (rows > 0x7fffffffLL || batch * seq > 0x7fffffffLL)
+    return set_error(TB_EINVAL, "%s: too many rows or slots", what);
   return TB_OK;
+}
+
+// Threads of a per-unit CTA: one per (head row, 8-dim group), a warp multiple, at most
+// kMaxThreads (more head rows loop).
+int rope_threads(const RopeDims &dm) {
+  int64_t t = (int64_t)(dm.nh + 2 * dm.nkv) * (dm.half / 8);
+  t = ((t + 31) / 32) * 32;
+  if (t > kMaxThreads) t = (kMaxThreads / (dm.half / 8)) * (dm.half / 8);
+  return (int)t;
 }
 
 unsigned grid_for(int64_t n, int threads) {
@@ -331,23 +340,24 @@ extern "C" int tb_rope_pack_fwd(const uint16_t *qkv, const void *lora_q, const v
   const int64_t units = slot_tok ? batch * seq : rows;
   if (units == 0) return TB_OK;
   RopeDims dm{rows, batch, seq, n_heads, n_kv, head_dim, head_dim / 2};
-  const bool vec = dm.half % 8 == 0 && dm.half <= 256 && aligned(qkv, 16) && aligned(cos, 16) &&
+  const bool vec = dm.half % 8 == 0 && dm.half <= 8 * kMaxThreads && aligned(qkv, 16) && aligned(cos, 16) &&
                    aligned(sin, 16) && aligned(q, 16) && (n_kv == 0 || (aligned(k, 16) && aligned(v, 16))) &&
                    (!lora_q || aligned(lora_q, 16)) && (!lora_v || aligned(lora_v, 16));
   cudaStream_t st = as_stream(stream);
   if (vec) {
-    const unsigned blocks = (unsigned)((units + kWarpsPerBlock - 1) / kWarpsPerBlock);
-    const int threads = kWarpsPerBlock * 32;
+    const unsigned blocks = (unsigned)units;
+    const int threads = rope_threads(dm);
+    const FastDiv sd((uint32_t)seq);
     if (slot_tok) {
       if (lora_is_fp32)
-        rope_fwd_vec<true, true><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx, slot_tok, q, k, v, dm);
+        rope_fwd_vec<true, true><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx, slot_tok, q, k, v, dm, sd);
       else
-        rope_fwd_vec<true, false><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx, slot_tok, q, k, v, dm);
+        rope_fwd_vec<true, false><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx, slot_tok, q, k, v, dm, sd);
     } else {
       if (lora_is_fp32)
-        rope_fwd_vec<false, true><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx, slot_tok, q, k, v, dm);
+        rope_fwd_vec<false, true><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx, slot_tok, q, k, v, dm, sd);
       else
-        rope_fwd_vec<false, false><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx, slot_tok, q, k, v, dm);
+        rope_fwd_vec<false, false><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx, slot_tok, q, k, v, dm, sd);
     }
   } else {
     const int64_t n = units * (n_heads + 2 * n_kv) * (int64_t)dm.half;
@@ -367,13 +377,13 @@ extern "C" int tb_rope_pack_bwd(const uint16_t *dq, const uint16_t *dk, const ui
   if (!cos || !sin || !pos_idx || !dqkv)
     return set_error(TB_EINVAL, "rope_pack_bwd: cos, sin, pos_idx, dqkv are required");
   RopeDims dm{rows, batch, seq, n_heads, n_kv, head_dim, head_dim / 2};
-  const bool vec = dm.half % 8 == 0 && dm.half <= 256 && aligned(dqkv, 16) && aligned(cos, 16) &&
+  const bool vec = dm.half % 8 == 0 && dm.half <= 8 * kMaxThreads && aligned(dqkv, 16) && aligned(cos, 16) &&
                    aligned(sin, 16) && (!dq || aligned(dq, 16)) && (!dk || aligned(dk, 16)) &&
                    (!dv || aligned(dv, 16));
   cudaStream_t st = as_stream(stream);
   if (vec) {
-    const unsigned blocks = (unsigned)((rows + kWarpsPerBlock - 1) / kWarpsPerBlock);
-    rope_bwd_vec<<<blocks, kWarpsPerBlock * 32, 0, st>>>(dq, dk, dv, cos, sin, pos_idx, dqkv, dm);
+    rope_bwd_vec<<<(unsigned)rows, rope_threads(dm), 0, st>>>(dq, dk, dv, cos, sin, pos_idx, dqkv,
+                                                             dm, FastDiv((uint32_t)seq));
   } else {
     const int64_t n = rows * (n_heads + 2 * n_kv) * (int64_t)dm.half;
     rope_bwd_any<<<grid_for(n, 256), 256, 0, st>>>(dq, dk, dv, cos, sin, pos_idx, dqkv, dm);

@@ -23,63 +23,66 @@ __device__ __forceinline__ void swiglu_bwd_one(float dact, float g, float u, flo
   du = dact * (g * sig);
 }
 
+// Vector index i (8 values) -> (row, chunk) with one invariant division; n < 2^32 vectors.
 __global__ void __launch_bounds__(kThreads)
-    swiglu_fwd_vec(const uint16_t *__restrict__ gu, uint16_t *__restrict__ act, int64_t rows,
-                   int64_t inter) {
-  const int64_t vpr = inter / 8, n = rows * vpr;
-  const int64_t stride = (int64_t)gridDim.x * kThreads;
-  for (int64_t i0 = (int64_t)blockIdx.x * kThreads * kUnroll + threadIdx.x; i0 < n;
+    swiglu_fwd_vec(const uint16_t *__restrict__ gu, uint16_t *__restrict__ act, uint32_t n,
+                   FastDiv vpr, int64_t inter) {
+  const uint32_t stride = gridDim.x * kThreads;
+  for (uint32_t i0 = blockIdx.x * kThreads * kUnroll + threadIdx.x; i0 < n;
        i0 += stride * kUnroll) {
     float g[kUnroll][8], u[kUnroll][8];
 #pragma unroll
     for (int r = 0; r < kUnroll; ++r) {
-      const int64_t i = i0 + (int64_t)r * kThreads;
+      const uint32_t i = i0 + r * kThreads;
       if (i < n) {
-        const int64_t row = i / vpr, c = i - row * vpr;
-        const uint16_t *p = gu + row * 2 * inter + c * 8;
+        uint32_t row, c;
+        vpr.divmod(i, row, c);
+        const uint16_t *p = gu + (int64_t)row * 2 * inter + c * 8;
         load8h(p, g[r]);
         load8h(p + inter, u[r]);
       }
     }
 #pragma unroll
     for (int r = 0; r < kUnroll; ++r) {
-      const int64_t i = i0 + (int64_t)r * kThreads;
+      const uint32_t i = i0 + r * kThreads;
       if (i < n) {
-        const int64_t row = i / vpr, c = i - row * vpr;
+        uint32_t row, c;
+        vpr.divmod(i, row, c);
         float o[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) o[k] = silu(g[r][k]) * u[r][k];
-        store8h(act + row * inter + c * 8, o);
+        store8h(act + (int64_t)row * inter + c * 8, o);
       }
     }
   }
 }
 
 __global__ void __launch_bounds__(kThreads)
-    swiglu_bwd_vec(const uint16_t *__restrict__ dact, uint16_t *__restrict__ gu, int64_t rows,
-                   int64_t inter) {
-  const int64_t vpr = inter / 8, n = rows * vpr;
-  const int64_t stride = (int64_t)gridDim.x * kThreads;
-  for (int64_t i0 = (int64_t)blockIdx.x * kThreads * kUnroll + threadIdx.x; i0 < n;
+    swiglu_bwd_vec(const uint16_t *__restrict__ dact, uint16_t *__restrict__ gu, uint32_t n,
+                   FastDiv vpr, int64_t inter) {
+  const uint32_t stride = gridDim.x * kThreads;
+  for (uint32_t i0 = blockIdx.x * kThreads * kUnroll + threadIdx.x; i0 < n;
        i0 += stride * kUnroll) {
     float d[kUnroll][8], g[kUnroll][8], u[kUnroll][8];
 #pragma unroll
     for (int r = 0; r < kUnroll; ++r) {
-      const int64_t i = i0 + (int64_t)r * kThreads;
+      const uint32_t i = i0 + r * kThreads;
       if (i < n) {
-        const int64_t row = i / vpr, c = i - row * vpr;
-        uint16_t *p = gu + row * 2 * inter + c * 8;
-        load8h(dact + row * inter + c * 8, d[r]);
+        uint32_t row, c;
+        vpr.divmod(i, row, c);
+        uint16_t *p = gu + (int64_t)row * 2 * inter + c * 8;
+        load8h(dact + (int64_t)row * inter + c * 8, d[r]);
         load8h_rw(p, g[r]);
         load8h_rw(p + inter, u[r]);
       }
     }
 #pragma unroll
     for (int r = 0; r < kUnroll; ++r) {
-      const int64_t i = i0 + (int64_t)r * kThreads;
+      const uint32_t i = i0 + r * kThreads;
       if (i < n) {
-        const int64_t row = i / vpr, c = i - row * vpr;
-        uint16_t *p = gu + row * 2 * inter + c * 8;
+        uint32_t row, c;
+        vpr.divmod(i, row, c);
+        uint16_t *p = gu + (int64_t)row * 2 * inter + c * 8;
         float dg[8], du[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) swiglu_bwd_one(d[r][k], g[r][k], u[r][k], dg[k], du[k]);
@@ -135,8 +138,10 @@ extern "C" int tb_swiglu_fwd(const uint16_t *gu, uint16_t *act, int64_t rows, in
   if (rows == 0) return TB_OK;
   if (!gu || !act) return set_error(TB_EINVAL, "swiglu_fwd: gu and act are required");
   cudaStream_t st = as_stream(stream);
-  if (inter % 8 == 0 && aligned(gu, 16) && aligned(act, 16)) {
-    swiglu_fwd_vec<<<blocks_for(rows * (inter / 8), kThreads * kUnroll), kThreads, 0, st>>>(gu, act, rows, inter);
+  const int64_t nvec = rows * (inter / 8);
+  if (inter % 8 == 0 && nvec < (1LL << 31) && aligned(gu, 16) && aligned(act, 16)) {
+    swiglu_fwd_vec<<<blocks_for(nvec, kThreads * kUnroll), kThreads, 0, st>>>(
+        gu, act, (uint32_t)nvec, FastDiv((uint32_t)(inter / 8)), inter);
   } else {
     swiglu_fwd_any<<<blocks_for(rows * inter, kThreads), kThreads, 0, st>>>(gu, act, rows, inter);
   }
@@ -150,8 +155,10 @@ extern "C" int tb_swiglu_bwd_inplace(const uint16_t *dact, uint16_t *gu, int64_t
   if (rows == 0) return TB_OK;
   if (!gu || !dact) return set_error(TB_EINVAL, "swiglu_bwd: dact and gu are required");
   cudaStream_t st = as_stream(stream);
-  if (inter % 8 == 0 && aligned(gu, 16) && aligned(dact, 16)) {
-    swiglu_bwd_vec<<<blocks_for(rows * (inter / 8), kThreads * kUnroll), kThreads, 0, st>>>(dact, gu, rows, inter);
+  const int64_t nvec = rows * (inter / 8);
+  if (inter % 8 == 0 && nvec < (1LL << 31) && aligned(gu, 16) && aligned(dact, 16)) {
+    swiglu_bwd_vec<<<blocks_for(nvec, kThreads * kUnroll), kThreads, 0, st>>>(
+        dact, gu, (uint32_t)nvec, FastDiv((uint32_t)(inter / 8)), inter);
   } else {
     swiglu_bwd_any<<<blocks_for(rows * inter, kThreads), kThreads, 0, st>>>(dact, gu, rows, inter);
   }
