@@ -429,6 +429,102 @@ def head_bench(device, reps, world):
             "labelled": c["n_labelled"]}
 
 
+# ---- single kernels at configs 1-4 (--kernel) -------------------------------------------------
+
+def kernel_bench(name, steps, warmup, device):
+    """One kernel at its configuration's full size, `warmup` + `steps` launches, each timed with
+    CUDA events after an L2 flush; returns a dict (median us, algorithmic bytes, GB/s)."""
+    import numpy as np
+
+    from oracle import synth
+    from testt_b200 import _lib, head, mlp, nf4, rmsnorm, rope
+    from testt_b200.qlora import quantize_nf4
+
+    dev = torch.device(device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    fn, nbytes, info = None, 0, {}
+    if name in ("nf4", "nf4_nested"):
+        w = synth.config1_weight(dev)
+        packed, state = quantize_nf4(w, 64, nested=name == "nf4_nested")
+
+        class _W:
+            pass
+
+        wt = _W()
+        wt.data, wt.quant_state = packed, state
+        out = torch.empty(w.shape, dtype=torch.float16, device=dev)
+        jobs = [nf4._job(wt, out)]
+        fn = lambda: nf4._launch(jobs, dev)  # noqa: E731
+        nbytes = _nf4_bytes(wt)
+        info = {"config": "1", "shape": list(w.shape), "layout": "nested" if "nested" in name
+                else "plain fp32 absmax"}
+    elif name.startswith("rmsnorm"):
+        c = synth.config2(dev)
+        ypad = torch.zeros(2048, 1536, device=dev)
+        s, y, yp, rstd = rmsnorm._launch_fwd(c["x"], c["delta"], c["weight"], 1e-6, c["pad_idx"],
+                                             2048, ypad=ypad)
+        e = 2048 * 1536
+        if name == "rmsnorm_fwd":
+            fn = lambda: rmsnorm._launch_fwd(c["x"], c["delta"], c["weight"], 1e-6,  # noqa: E731
+                                             c["pad_idx"], 2048, ypad=ypad)
+            nbytes = 16 * e + 30720
+        else:
+            fn = lambda: rmsnorm._launch_bwd(s, rstd, c["weight"], c["pad_idx"], c["ds"],  # noqa
+                                             c["dy"], c["dypad"], True)
+            nbytes = 20 * e + 30720
+        info = {"config": "2", "rows": 2048, "hidden": 1536}
+    elif name.startswith("rope") or name.startswith("swiglu"):
+        c = synth.config3(dev)
+        m = c["rows"]
+        info = {"config": "3", "tokens": m, "lengths": c["lengths"]}
+        if name == "rope_fwd":
+            slot = rope.slot_index(c["pos_idx"], 2048)
+            args = (c["qkv"], c["lora_q"], c["lora_v"], c["cos"], c["sin"], c["pos_idx"], 4, 512,
+                    12, 2, 128, slot)
+            fn = lambda: rope.RopePack.apply(*args)  # noqa: E731
+            nbytes = m * 11272 + 8388608 + 524288 + 2048 * 4
+        elif name == "rope_bwd":
+            dqkv = torch.empty_like(c["qkv"])
+            fn = lambda: _lib.call(  # noqa: E731
+                "tb_rope_pack_bwd", _lib.ptr(c["dq"]), _lib.ptr(c["dk"]), _lib.ptr(c["dv"]),
+                _lib.ptr(c["cos"]), _lib.ptr(c["sin"]), _lib.ptr(c["pos_idx"]), _lib.ptr(dqkv),
+                m, 4, 512, 12, 2, 128, _lib.stream_of(dqkv))
+            nbytes = m * 8200 + 524288
+        elif name == "swiglu_fwd":
+            fn = lambda: mlp.gated_silu(c["gu"])  # noqa: E731
+            nbytes = m * 53760
+        else:
+            gu = c["gu"].clone()
+            fn = lambda: mlp.gated_silu_backward_(c["dact"], gu)  # noqa: E731
+            nbytes = m * 89600
+    elif name == "head_stats":
+        c = synth.config4(dev, rows=256)
+        logits = c["hidden"] @ c["weight"].t()
+        fn = lambda: head.head_stats_grad(logits, c["targets"], 1e-3)  # noqa: E731
+        lab = int((c["targets"] != -100).sum())
+        nbytes = logits.numel() * 2 + lab * 151936 * 4
+        info = {"config": "4", "rows": 256, "labelled": lab}
+    else:
+        raise SystemExit(f"unknown kernel {name}")
+    for _ in range(warmup):
+        fn()
+    times = []
+    for _ in range(steps):
+        flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b) * 1e3)
+    us = float(np.median(times))
+    pk, kind = peaks()
+    gbps = nbytes / us / 1e3
+    return {"kernel": name, "us": us, "us_min": float(min(times)), "bytes": nbytes,
+            "gbps": gbps, "frac": gbps / pk["hbm_gbs"], "peak_kind": kind, **info}
+
+
 # ---- arms ------------------------------------------------------------------------------------
 
 def reference_arm(args, rank, world):
@@ -480,9 +576,14 @@ def ours_arm(args, rank, world, local):
     torch.cuda.synchronize()
 
     # value: the step with the batch already on the device
+    def timed_step():
+        torch.cuda.nvtx.range_push("timed_step")
+        step(ids, mask, labels)
+        torch.cuda.nvtx.range_pop()
+
     _lib.reset_call_count()
     with Clocks(local) as clk:
-        ms = time_region(lambda: step(ids, mask, labels), args.steps, world, dev)
+        ms = time_region(timed_step, args.steps, world, dev)
     calls = _lib.call_count() // args.steps
     clocks = clk.summary()
     value = tokens * world * args.steps / (ms / 1e3)
@@ -579,7 +680,18 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    ap.add_argument("--kernel", default=None,
+                    help="time one kernel at its configuration instead (nf4, nf4_nested, "
+                         "rmsnorm_fwd, rmsnorm_bwd, rope_fwd, rope_bwd, swiglu_fwd, swiglu_bwd, "
+                         "head_stats, all)")
     args = ap.parse_args()
+    if args.kernel:
+        names = ["nf4", "nf4_nested", "rmsnorm_fwd", "rmsnorm_bwd", "rope_fwd", "rope_bwd",
+                 "swiglu_fwd", "swiglu_bwd", "head_stats"] if args.kernel == "all" \
+            else args.kernel.split(",")
+        for n in names:
+            print(json.dumps(kernel_bench(n, args.steps, args.warmup, "cuda:0")), flush=True)
+        return
     if args.warmup < 3:
         args.warmup = 3
     rank, world, local = setup(args)

@@ -19,8 +19,10 @@ def golden(name):
 
 
 def t(a, device="cpu"):
-    """numpy -> torch (keeps dtype)."""
-    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+    """numpy -> torch (keeps dtype and 0-d shapes)."""
+    a = np.asarray(a)
+    a = a.copy() if a.ndim == 0 else np.ascontiguousarray(a)
+    return torch.from_numpy(a).to(device)
 
 
 def _np16(x):

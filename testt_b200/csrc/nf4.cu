@@ -4,11 +4,15 @@
 // unpack_concat). The reference runs one Triton program per 1024 packed bytes and one launch per
 // weight; here one launch covers every weight of a stacked GEMM operand (q|k|v, gate|up).
 //
-// Layout of the work: the packed bytes of all weights form one virtual stream of 4-byte words.
-// Lane l of a warp handles words base + 32*k + l (k < kUnroll), so every 4-byte load and every
-// 16-byte store of a warp instruction is contiguous (128 B in, 512 B out). A word's 4 bytes lie
-// in one absmax block whenever the block holds a multiple of 8 values, so the scale is computed
-// once per word; block indices use 32-bit invariant division (FastDiv), never 64-bit division.
+// Layout of the work: a warp handles a span of 32 * kUnroll consecutive 4-byte words of one
+// weight; lane l takes words l, l + 32, l + 64, ... of the span, so every 4-byte load and every
+// 16-byte store of a warp instruction is contiguous (128 B in, 512 B out). Contiguous stores
+// matter most here (80 % of the bytes are the fp16 output): giving each thread 16 contiguous
+// packed bytes instead made every store instruction 64-byte strided and cost 1.5x on B200.
+// Each weight's range of words is padded to whole spans, so the weight of a span is uniform
+// across the warp and found once per span; the 256-entry nested code table, the offset and the
+// 16-entry NF4 table live in shared memory, block indices use 32-bit invariant division
+// (FastDiv). Sizes or alignments that do not fit take a byte-granular kernel.
 // Arithmetic is bit-exact with the reference: each mul/add rounded on its own (__fmul_rn /
 // __fadd_rn, no FMA contraction), then one round-to-nearest-even to fp16.
 #include "common.cuh"
@@ -30,7 +34,8 @@ struct Nf4Job {
   const float *offset[kMaxW];
   const float *table[kMaxW];
   uint16_t *out[kMaxW];
-  int64_t start[kMaxW + 1];  // prefix sums of units (words for the vector kernel, else bytes)
+  int64_t start[kMaxW + 1];  // prefix sums of units (padded words for the word kernel, else bytes)
+  uint32_t n_words[kMaxW];   // words of each weight (word kernel)
   FastDiv block_div[kMaxW];  // packed byte index -> absmax block (divisor qblock / 2)
   FastDiv nest_div[kMaxW];   // absmax block -> nested block (divisor qblock2)
 };
@@ -50,36 +55,54 @@ __device__ __forceinline__ float block_scale(const Nf4Job &job, int j, uint32_t 
   return __fadd_rn(a, __ldg(job.offset[j]));
 }
 
+constexpr int kSpan = 32 * kUnroll;  // words per warp span
+
 __global__ void __launch_bounds__(kThreads) nf4_unpack_words(const __grid_constant__ Nf4Job job) {
   __shared__ float table[kMaxW][16];
+  __shared__ float code2[kMaxW][256];
+  __shared__ float offs[kMaxW];
   for (int i = threadIdx.x; i < job.n * 16; i += blockDim.x)
     table[i >> 4][i & 15] = __ldg(job.table[i >> 4] + (i & 15));
+  for (int j = 0; j < job.n; ++j) {
+    if (job.absmax_f32[j] != nullptr) continue;
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) code2[j][i] = __ldg(job.code2[j] + i);
+    if (threadIdx.x == 0) offs[j] = __ldg(job.offset[j]);
+  }
   __syncthreads();
 
-  const int64_t total = job.start[job.n];
+  const int64_t spans = job.start[job.n] / kSpan;
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (kThreads / 32);
-  for (int64_t w = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
-       w * 32 * kUnroll < total; w += warps) {
-    uint32_t word[kUnroll], local[kUnroll];
-    int wj[kUnroll];
+  for (int64_t sp = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); sp < spans;
+       sp += warps) {
+    const int j = find_weight(job, sp * kSpan);  // uniform across the warp
+    const uint32_t first = (uint32_t)(sp * kSpan - job.start[j]);
+    const uint32_t nwords = job.n_words[j];
+    const uint32_t *src = reinterpret_cast<const uint32_t *>(job.packed[j]);
+    const bool plain = job.absmax_f32[j] != nullptr;
+    uint32_t word[kUnroll];
     float scale[kUnroll];
 #pragma unroll
     for (int k = 0; k < kUnroll; ++k) {
-      const int64_t unit = (w * kUnroll + k) * 32 + lane;
-      wj[k] = -1;
-      if (unit < total) {
-        const int j = find_weight(job, unit);
-        wj[k] = j;
-        local[k] = (uint32_t)(unit - job.start[j]);
-        word[k] = __ldg(reinterpret_cast<const uint32_t *>(job.packed[j]) + local[k]);
-        scale[k] = block_scale(job, j, job.block_div[j].div(local[k] * 4u));
+      const uint32_t local = first + k * 32 + lane;
+      word[k] = 0;
+      scale[k] = 0.f;
+      if (local < nwords) {
+        word[k] = __ldg(src + local);
+        const uint32_t b = job.block_div[j].div(local * 4u);
+        if (plain) {
+          scale[k] = __ldg(job.absmax_f32[j] + b);
+        } else {
+          const int code = __ldg(job.absmax_u8[j] + b);
+          const float a2 = __ldg(job.absmax2[j] + job.nest_div[j].div(b));
+          scale[k] = __fadd_rn(__fmul_rn(code2[j][code], a2), offs[j]);
+        }
       }
     }
 #pragma unroll
     for (int k = 0; k < kUnroll; ++k) {
-      const int j = wj[k];
-      if (j < 0) continue;
+      const uint32_t local = first + k * 32 + lane;
+      if (local >= nwords) continue;
       float f[8];
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
@@ -87,7 +110,7 @@ __global__ void __launch_bounds__(kThreads) nf4_unpack_words(const __grid_consta
         f[2 * b] = __fmul_rn(table[j][byte >> 4], scale[k]);
         f[2 * b + 1] = __fmul_rn(table[j][byte & 15u], scale[k]);
       }
-      store8h_cs(job.out[j] + (size_t)local[k] * 8, f);
+      store8h_cs(job.out[j] + (size_t)local * 8, f);
     }
   }
 }
@@ -115,20 +138,25 @@ int launch(Nf4Job &job, const int64_t *n_bytes, const int32_t *half_qblock, cuda
             aligned(job.packed[j], 4) && aligned(job.out[j], 16);
   }
   job.start[0] = 0;
-  for (int j = 0; j < job.n; ++j) job.start[j + 1] = job.start[j] + (words ? n_bytes[j] / 4 : n_bytes[j]);
+  for (int j = 0; j < job.n; ++j) {
+    int64_t units = n_bytes[j];
+    if (words) {
+      job.n_words[j] = (uint32_t)(n_bytes[j] / 4);
+      units = ((n_bytes[j] / 4 + kSpan - 1) / kSpan) * kSpan;  // whole warp spans
+    }
+    job.start[j + 1] = job.start[j] + units;
+  }
   for (int j = job.n; j < kMaxW; ++j) job.start[j + 1] = job.start[job.n];
   const int64_t total = job.start[job.n];
   if (total == 0) return TB_OK;
-  // enough resident warps to keep HBM busy, then a grid-stride loop
+  // one block per 8 warps of work, at most what is resident at once (8 per SM), grid-stride
   const int64_t cap = (int64_t)sm_count() * (2048 / kThreads);
+  const int64_t per_block = (int64_t)kThreads * (words ? kUnroll : 1);
+  int64_t blocks = (total + per_block - 1) / per_block;
+  if (blocks > cap) blocks = cap;
   if (words) {
-    const int64_t per_block = (int64_t)kThreads * kUnroll;
-    int64_t blocks = (total + per_block - 1) / per_block;
-    if (blocks > cap) blocks = cap;
     nf4_unpack_words<<<(unsigned)blocks, kThreads, 0, stream>>>(job);
   } else {
-    int64_t blocks = (total + kThreads - 1) / kThreads;
-    if (blocks > cap) blocks = cap;
     nf4_unpack_bytes<<<(unsigned)blocks, kThreads, 0, stream>>>(job);
   }
   return check_launch("nf4_unpack");

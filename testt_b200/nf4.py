@@ -92,19 +92,70 @@ def _launch(jobs, device):
     """One tb_nf4_unpack_multi launch per MAX_WEIGHTS_PER_LAUNCH weights."""
     stream = _lib.stream_of(jobs[0]["out"])
     for start in range(0, len(jobs), MAX_WEIGHTS_PER_LAUNCH):
-        part = jobs[start:start + MAX_WEIGHTS_PER_LAUNCH]
-        n = len(part)
-        get = lambda key: [_lib.ptr(j.get(key)) for j in part]  # noqa: E731
-        call_args = [
-            n, _lib.ptr_array(get("packed")), _lib.ptr_array(get("absmax_f32")),
+        _lib.call("tb_nf4_unpack_multi",
+                  *_job_arrays(jobs[start:start + MAX_WEIGHTS_PER_LAUNCH]), stream)
+
+
+def _job_arrays(jobs):
+    """The C arrays tb_nf4_unpack_multi takes for up to MAX_WEIGHTS_PER_LAUNCH jobs."""
+    n = len(jobs)
+    get = lambda key: [_lib.ptr(j.get(key)) for j in jobs]  # noqa: E731
+    return [n, _lib.ptr_array(get("packed")), _lib.ptr_array(get("absmax_f32")),
             _lib.ptr_array(get("absmax_u8")), _lib.ptr_array(get("code2")),
             _lib.ptr_array(get("absmax2")), _lib.ptr_array(get("offset")),
             _lib.ptr_array(get("table")), _lib.ptr_array(get("out")),
-            (_lib._I64 * n)(*[j["n_bytes"] for j in part]),
-            (_lib._I32 * n)(*[j["qblock"] for j in part]),
-            (_lib._I32 * n)(*[j.get("qblock2", 1) for j in part]),
-            stream]
-        _lib.call("tb_nf4_unpack_multi", *call_args)
+            (_lib._I64 * n)(*[j["n_bytes"] for j in jobs]),
+            (_lib._I32 * n)(*[j["qblock"] for j in jobs]),
+            (_lib._I32 * n)(*[j.get("qblock2", 1) for j in jobs])]
+
+
+class _Prepared:
+    """The launch arguments of one stacked weight tuple, built once: every input pointer is
+    fixed, only the output pointers change per call (the `out` C array is rewritten in place).
+    Valid while the weights keep their storage (checked by data pointer on every use)."""
+
+    def __init__(self, weights, device):
+        self.shapes = [weight_shape(w) for w in weights]
+        self.rows = [s[0] for s in self.shapes]
+        self.cols = self.shapes[0][1]
+        self.device = device
+        dummy = torch.empty(0, dtype=torch.float16, device=device)
+        self.jobs = [_job(w, dummy) for w in weights]  # keeps converted tables alive
+        self.parts = []
+        for start in range(0, len(weights), MAX_WEIGHTS_PER_LAUNCH):
+            part = self.jobs[start:start + MAX_WEIGHTS_PER_LAUNCH]
+            self.parts.append((start, len(part), _job_arrays(part)))
+        self.check = self._fingerprint(weights)
+
+    @staticmethod
+    def _fingerprint(weights):
+        return tuple((w.data.data_ptr(), _quant_state(w).absmax.data_ptr()) for w in weights)
+
+    def run(self, out):
+        base = out.data_ptr()
+        stride = self.cols * 2
+        stream = _lib.stream_of(out)
+        offsets = [0]
+        for r in self.rows:
+            offsets.append(offsets[-1] + r)
+        for start, n, args in self.parts:
+            arr = args[8]
+            for i in range(n):
+                arr[i] = base + offsets[start + i] * stride
+            _lib.call("tb_nf4_unpack_multi", *args, stream)
+        return out
+
+
+_prepared = {}
+
+
+def _prepared_for(weights, device):
+    key = (tuple(id(w) for w in weights), str(device))
+    prep = _prepared.get(key)
+    if prep is None or prep.check != _Prepared._fingerprint(weights):
+        prep = _Prepared(weights, device)
+        _prepared[key] = prep
+    return prep
 
 
 def _check_out(weight, out):
@@ -144,14 +195,13 @@ def unpack_concat(weights, device):
     rows = [weight_shape(w)[0] for w in weights]
     cols = weight_shape(weights[0])[1]
     out = torch.empty((sum(rows), cols), dtype=torch.float16, device=device)
+    weights = tuple(weights)
+    prep = _prepared.get((tuple(id(w) for w in weights), str(device)))
+    if prep is not None and prep.check == _Prepared._fingerprint(weights):
+        return prep.run(out)
     if device.type == "cuda" and all(supports_fast_unpack(w) and _on_device(w, device)
                                      for w in weights):
-        jobs, start = [], 0
-        for weight, n in zip(weights, rows):
-            jobs.append(_job(weight, out[start:start + n]))
-            start += n
-        _launch(jobs, device)
-        return out
+        return _prepared_for(weights, device).run(out)
     start = 0
     for weight, n in zip(weights, rows):
         unpack_into(weight, out[start:start + n])
