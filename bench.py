@@ -148,33 +148,37 @@ def make_batch(lengths, seq, vocab, seed, device):
 
 
 class TrainStep:
-    """forward (fused path) + backward + LoRA-gradient all-reduce + AdamW, loss scale 1024."""
+    """forward (fused path) + backward + LoRA-gradient all-reduce + AdamW, loss scale 1024,
+    run eagerly (every kernel launched from Python)."""
 
     LOSS_SCALE = 1024.0
 
-    def __init__(self, model, world):
+    def __init__(self, model, world, bucket=None, opt=None):
         from testt_b200.dist import GradBucket
         from testt_b200.qlora import lora_parameters
 
         self.model = model
         self.params = lora_parameters(model)
-        self.bucket = GradBucket(self.params)
-        self.opt = torch.optim.AdamW(self.params, lr=1e-4, fused=True)
+        self.bucket = bucket or GradBucket(self.params)
+        self.opt = opt or torch.optim.AdamW(self.params, lr=1e-4, fused=True, capturable=True)
         self.world = world
+
+    def post_backward(self):
+        self.bucket.all_reduce(average=True)
+        self.opt.step()
 
     def __call__(self, ids, mask, labels):
         from testt_b200.trainer_patch import _FusedRequest
 
         n_items = (labels[:, 1:] != -100).sum()
+        self.bucket.zero()
         with torch.autocast("cuda", dtype=torch.float16):
             with _FusedRequest():
                 out = self.model(input_ids=ids, attention_mask=mask, labels=labels,
                                  num_items_in_batch=n_items)
         (out.loss * self.LOSS_SCALE).backward()
-        self.bucket.all_reduce(average=True)
         self.bucket.flat.mul_(1.0 / self.LOSS_SCALE)
-        self.opt.step()
-        self.bucket.zero()
+        self.post_backward()
         return out
 
 
@@ -378,13 +382,19 @@ def _nf4_bytes(weight):
     return b
 
 
+def flush_l2(buf):
+    """Evict the L2 (126 MB on B200) by reading a larger buffer: the lines it leaves are clean,
+    so the next kernel does not pay for writing back dirty data of earlier work."""
+    return buf.sum()
+
+
 def time_graph(graph, reps, world, device, flush=None):
     """ms per replay of a captured graph (device time, max over ranks); the L2 is flushed before
-    every replay by writing `flush` (larger than L2) and the flush time is not counted."""
+    every replay (flush_l2, not counted)."""
     times = []
     for _ in range(reps):
         if flush is not None:
-            flush.zero_()
+            flush_l2(flush)
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record()
@@ -441,7 +451,7 @@ def kernel_bench(name, steps, warmup, device):
     from testt_b200.qlora import quantize_nf4
 
     dev = torch.device(device)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush = torch.zeros(64 << 20, dtype=torch.float32, device=dev)  # 256 MB
     fn, nbytes, info = None, 0, {}
     if name in ("nf4", "nf4_nested"):
         w = synth.config1_weight(dev)
@@ -510,7 +520,7 @@ def kernel_bench(name, steps, warmup, device):
         fn()
     times = []
     for _ in range(steps):
-        flush.zero_()
+        flush_l2(flush)
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record()
@@ -570,42 +580,56 @@ def ours_arm(args, rank, world, local):
     ids, mask, labels = make_batch(lengths, seq, cfg.vocab_size, 100 + rank, dev)
     tokens = sum(lengths)
     step = TrainStep(model, world)
+    from testt_b200.graphs import GraphedTrainStep
 
-    for _ in range(args.warmup):
-        step(ids, mask, labels)
-    torch.cuda.synchronize()
-
-    # value: the step with the batch already on the device
-    def timed_step():
-        torch.cuda.nvtx.range_push("timed_step")
-        step(ids, mask, labels)
-        torch.cuda.nvtx.range_pop()
-
-    _lib.reset_call_count()
-    with Clocks(local) as clk:
-        ms = time_region(timed_step, args.steps, world, dev)
-    calls = _lib.call_count() // args.steps
-    clocks = clk.summary()
-    value = tokens * world * args.steps / (ms / 1e3)
-
-    # e2e: batch from pinned host memory every step, loss and statistics read back
+    graphed = GraphedTrainStep(model, step.bucket, loss_scale=TrainStep.LOSS_SCALE,
+                               post_backward=step.post_backward)
     host = [t.cpu().pin_memory() for t in (ids, mask, labels)]
     h2d = sum(t.numel() * t.element_size() for t in host)
 
+    # eager step (reported beside the captured one)
+    for _ in range(args.warmup):
+        step(ids, mask, labels)
+    torch.cuda.synchronize()
+    eager_ms = time_region(lambda: step(ids, mask, labels), args.steps, world, dev)
+
+    # value: the captured step replayed on inputs already on the device
+    graphed(ids, mask, labels, host_mask=host[1], host_labels=host[2])  # capture
+    for _ in range(args.warmup):
+        graphed.replay()
+    torch.cuda.synchronize()
+
+    def timed_step():
+        torch.cuda.nvtx.range_push("timed_step")
+        graphed.replay()
+        torch.cuda.nvtx.range_pop()
+
+    _lib.reset_call_count()
+    _ = _lib.call_count()
+    with Clocks(local) as clk:
+        ms = time_region(timed_step, args.steps, world, dev)
+    clocks = clk.summary()
+    value = tokens * world * args.steps / (ms / 1e3)
+
+    # e2e: the public call with a host batch every step (plan from the host copy, H2D copies
+    # into the graph's buffers, replay) and the loss and statistics read back to the host
     def e2e_step():
-        batch = [t.to(dev, non_blocking=True) for t in host]
-        out = step(*batch)
-        st = out.logits
-        vals = torch.stack([out.loss.detach().float(), st.entropy_sum.float(),
-                            st.correct.float(), st.labelled.float()]).cpu()
-        return vals
+        loss, st = graphed(host[0], host[1], host[2], host_mask=host[1], host_labels=host[2])
+        return torch.stack([loss.detach().float(), st.entropy_sum.float(), st.correct.float(),
+                            st.labelled.float()]).cpu()
 
     e2e_ms = time_region(e2e_step, args.steps, world, dev)
     e2e_value = tokens * world * args.steps / (e2e_ms / 1e3)
 
+    # kernels launched per step: counted on one eager step (a replay launches the same kernels)
+    _lib.reset_call_count()
+    step(ids, mask, labels)
+    torch.cuda.synchronize()
+    calls = _lib.call_count()
+
     # hot path: the fused memory-bound kernels of one step as CUDA graphs
     hp = HotPath(model, lengths, seq, dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush = torch.zeros(64 << 20, dtype=torch.float32, device=dev)  # 256 MB
     reps = max(args.steps, 5)
     full = hp.graph(list(hp.groups))
     hp_ms = time_graph(full, reps, world, dev, flush)
@@ -647,13 +671,17 @@ def ours_arm(args, rank, world, local):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
         "data": "synthetic (random-init weights, uniform token ids, lognormal lengths)",
         "config": {"workload": "config 5: QLoRA train step (fwd+bwd+LoRA all-reduce+AdamW), "
-                               "Qwen2.5-1.5B shape, NF4 bs64 double-quant, LoRA r16 a32 q/v",
+                               "Qwen2.5-1.5B shape, NF4 bs64 double-quant, LoRA r16 a32 q/v, "
+                               "captured as one CUDA graph (testt_b200.graphs)",
                    "global_batch": 4 * world, "seq_len": seq, "tokens_per_gpu": tokens,
                    "lengths": lengths, "parallelism": f"dp{world}",
                    "l2": "inputs larger than L2 (3.4 GB of NF4 weights streamed per step); "
-                         "hot-path graphs: L2 flushed (256 MB write) before each replay"},
+                         "hot-path graphs: L2 flushed (256 MB read) before each replay"},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": 16},
+                "d2h_bytes_per_step": 16, "path": "GraphedTrainStep(host batch) -> replay"},
+        "eager": {"tokens_per_s": tokens * world * args.steps / (eager_ms / 1e3),
+                  "ms_per_step": eager_ms / args.steps,
+                  "note": "the same step launched op by op from Python (no CUDA graph)"},
         "gpu_launches": calls,
         "clocks": clocks,
         "hot_path": {"gbps": hp_bytes / hp_ms / 1e6, "frac": hp_bytes / hp_ms / 1e6 / pk["hbm_gbs"],

@@ -30,10 +30,22 @@ inline bool aligned(const void *p, uintptr_t a) {
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Blocks of `kernel` resident on the whole device at `threads` threads and `smem` dynamic shared
+// bytes per block (the occupancy calculator times the SM count; at least the SM count).
+template <typename Kernel>
+int resident_blocks(Kernel kernel, int threads, size_t smem = 0) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  return per_sm * sm_count();
+}
+
 // ---- fp16 packing --------------------------------------------------------------------------
 
+// Two floats rounded to nearest-even fp16 and packed (one cvt.rn.f16x2.f32).
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-  __half2 h = __halves2half2(__float2half_rn(lo), __float2half_rn(hi));
+  __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t *>(&h);
 }
 

@@ -57,8 +57,38 @@ __device__ __forceinline__ float block_scale(const Nf4Job &job, int j, uint32_t 
 
 constexpr int kSpan = 32 * kUnroll;  // words per warp span
 
+// fp16 values of the 8 nibbles of `word` (high nibble of each byte first) times `scale`, packed.
+// `tab` is the byte address of the 16-entry table in shared memory (64-byte aligned), so a
+// nibble's entry is tab | ((word >> s) & 0x3c): one shift and one logic op per lookup.
+__device__ __forceinline__ uint4 decode_word(uint32_t word, float scale, uint32_t tab) {
+  float f[8];
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    const uint32_t hi_off = (word >> (8 * b + 2)) & 0x3cu;
+    const uint32_t lo_off = (b == 0 ? (word << 2) : (word >> (8 * b - 2))) & 0x3cu;
+    float hi, lo;
+    asm("ld.shared.f32 %0, [%1];" : "=f"(hi) : "r"(tab | hi_off));
+    asm("ld.shared.f32 %0, [%1];" : "=f"(lo) : "r"(tab | lo_off));
+    // two products per instruction (sm_100 packed fp32 multiply, each lane rounded to nearest
+    // even exactly like __fmul_rn)
+    asm("{\n\t.reg .b64 a, s, p;\n\t"
+        "mov.b64 a, {%2, %3};\n\t"
+        "mov.b64 s, {%4, %4};\n\t"
+        "mul.rn.f32x2 p, a, s;\n\t"
+        "mov.b64 {%0, %1}, p;\n\t}"
+        : "=f"(f[2 * b]), "=f"(f[2 * b + 1])
+        : "f"(hi), "f"(lo), "f"(scale));
+  }
+  return make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]),
+                    pack_half2(f[6], f[7]));
+}
+
+// kBlock64: blocksize 64 (8 words per absmax block). A span of 32 * kUnroll words holds 4 *
+// kUnroll blocks: lane l < 4 * kUnroll computes the scale of block l once and word k of lane l
+// (block 4k + l/8) takes it by shuffle.
+template <bool kBlock64>
 __global__ void __launch_bounds__(kThreads) nf4_unpack_words(const __grid_constant__ Nf4Job job) {
-  __shared__ float table[kMaxW][16];
+  __shared__ __align__(64) float table[kMaxW][16];
   __shared__ float code2[kMaxW][256];
   __shared__ float offs[kMaxW];
   for (int i = threadIdx.x; i < job.n * 16; i += blockDim.x)
@@ -80,37 +110,51 @@ __global__ void __launch_bounds__(kThreads) nf4_unpack_words(const __grid_consta
     const uint32_t nwords = job.n_words[j];
     const uint32_t *src = reinterpret_cast<const uint32_t *>(job.packed[j]);
     const bool plain = job.absmax_f32[j] != nullptr;
+    const uint32_t tab = (uint32_t)__cvta_generic_to_shared(&table[j][0]);
     uint32_t word[kUnroll];
-    float scale[kUnroll];
 #pragma unroll
     for (int k = 0; k < kUnroll; ++k) {
       const uint32_t local = first + k * 32 + lane;
-      word[k] = 0;
-      scale[k] = 0.f;
-      if (local < nwords) {
-        word[k] = __ldg(src + local);
-        const uint32_t b = job.block_div[j].div(local * 4u);
+      word[k] = local < nwords ? __ldg(src + local) : 0u;
+    }
+    float scale[kUnroll];
+    if (kBlock64) {
+      // lane l: block first/8 + l (exists when its first word does)
+      const uint32_t b = (first >> 3) + lane;
+      float mine = 0.f;
+      if (lane < 4 * kUnroll && b * 8 < nwords) {
         if (plain) {
-          scale[k] = __ldg(job.absmax_f32[j] + b);
+          mine = __ldg(job.absmax_f32[j] + b);
         } else {
           const int code = __ldg(job.absmax_u8[j] + b);
           const float a2 = __ldg(job.absmax2[j] + job.nest_div[j].div(b));
-          scale[k] = __fadd_rn(__fmul_rn(code2[j][code], a2), offs[j]);
+          mine = __fadd_rn(__fmul_rn(code2[j][code], a2), offs[j]);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k) scale[k] = __shfl_sync(0xffffffffu, mine, 4 * k + (lane >> 3));
+    } else {
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k) {
+        const uint32_t local = first + k * 32 + lane;
+        scale[k] = 0.f;
+        if (local < nwords) {
+          const uint32_t b = job.block_div[j].div(local * 4u);
+          if (plain) {
+            scale[k] = __ldg(job.absmax_f32[j] + b);
+          } else {
+            const int code = __ldg(job.absmax_u8[j] + b);
+            const float a2 = __ldg(job.absmax2[j] + job.nest_div[j].div(b));
+            scale[k] = __fadd_rn(__fmul_rn(code2[j][code], a2), offs[j]);
+          }
         }
       }
     }
+    uint4 *dst = reinterpret_cast<uint4 *>(job.out[j]);
 #pragma unroll
     for (int k = 0; k < kUnroll; ++k) {
       const uint32_t local = first + k * 32 + lane;
-      if (local >= nwords) continue;
-      float f[8];
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const uint32_t byte = (word[k] >> (8 * b)) & 0xffu;
-        f[2 * b] = __fmul_rn(table[j][byte >> 4], scale[k]);
-        f[2 * b + 1] = __fmul_rn(table[j][byte & 15u], scale[k]);
-      }
-      store8h_cs(job.out[j] + (size_t)local * 8, f);
+      if (local < nwords) __stcs(dst + local, decode_word(word[k], scale[k], tab));
     }
   }
 }
@@ -149,14 +193,23 @@ int launch(Nf4Job &job, const int64_t *n_bytes, const int32_t *half_qblock, cuda
   for (int j = job.n; j < kMaxW; ++j) job.start[j + 1] = job.start[job.n];
   const int64_t total = job.start[job.n];
   if (total == 0) return TB_OK;
-  // one block per 8 warps of work, at most what is resident at once (8 per SM), grid-stride
-  const int64_t cap = (int64_t)sm_count() * (2048 / kThreads);
+  // one block per 8 spans (words) or 256 bytes of work, at most what is resident at once,
+  // then a grid-stride loop
+  bool block64 = true;
+  for (int j = 0; j < job.n; ++j) block64 = block64 && half_qblock[j] == 32;
   const int64_t per_block = (int64_t)kThreads * (words ? kUnroll : 1);
   int64_t blocks = (total + per_block - 1) / per_block;
-  if (blocks > cap) blocks = cap;
-  if (words) {
-    nf4_unpack_words<<<(unsigned)blocks, kThreads, 0, stream>>>(job);
+  if (words && block64) {
+    static int cap = resident_blocks(nf4_unpack_words<true>, kThreads);
+    if (blocks > cap) blocks = cap;
+    nf4_unpack_words<true><<<(unsigned)blocks, kThreads, 0, stream>>>(job);
+  } else if (words) {
+    static int cap = resident_blocks(nf4_unpack_words<false>, kThreads);
+    if (blocks > cap) blocks = cap;
+    nf4_unpack_words<false><<<(unsigned)blocks, kThreads, 0, stream>>>(job);
   } else {
+    static int cap = resident_blocks(nf4_unpack_bytes, kThreads);
+    if (blocks > cap) blocks = cap;
     nf4_unpack_bytes<<<(unsigned)blocks, kThreads, 0, stream>>>(job);
   }
   return check_launch("nf4_unpack");

@@ -70,14 +70,17 @@ def _host_counts(labelled, denominator, device, targets=None, vocab=None):
 
 class FusedHeadLoss(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, hidden, weight, targets, denominator):
+    def forward(ctx, hidden, weight, targets, denominator, counts=None):
         _lib.require_cuda(hidden, weight, targets, what="fused_head_loss")
         rows, width = hidden.shape
         vocab = weight.shape[0]
         dev = hidden.device
         labelled = targets != IGNORE_INDEX
         order = torch.argsort((~labelled).to(torch.int8), stable=True)
-        n_labelled, denom = _host_counts(labelled, denominator, dev, targets, vocab)
+        if counts is None:
+            n_labelled, denom = _host_counts(labelled, denominator, dev, targets, vocab)
+        else:  # known on the host already (a captured step): no synchronisation here
+            n_labelled, denom = int(counts[0]), float(counts[1])
         h = hidden.index_select(0, order)
         tgt = targets.index_select(0, order).to(torch.int64).contiguous()
         entropy = torch.empty(rows, dtype=torch.float32, device=dev)
@@ -118,14 +121,17 @@ class FusedHeadLoss(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_loss, *_unused):
         if not ctx.needs_input_grad[0]:
-            return None, None, None, None
+            return None, None, None, None, None
         (grad,) = ctx.saved_tensors
         factor = grad_loss.to(torch.float32) / ctx.unit
-        return (grad.to(torch.float32) * factor).to(torch.float16), None, None, None
+        return (grad.to(torch.float32) * factor).to(torch.float16), None, None, None, None
 
 
-def fused_head_loss(hidden16, weight16, targets, denominator):
+def fused_head_loss(hidden16, weight16, targets, denominator, counts=None):
     """(loss, token entropy [M], token loss [M], token correct [M]) for rows of `hidden16`
     (reference: head.py:151-156). `targets[i]` is the label row i predicts (IGNORE_INDEX for
-    none); `denominator` is what the summed loss is divided by."""
-    return FusedHeadLoss.apply(hidden16.contiguous(), weight16, targets.contiguous(), denominator)
+    none); `denominator` is what the summed loss is divided by. `counts` = (labelled rows,
+    denominator as a float), when the caller knows them on the host, skips the one
+    synchronisation the head otherwise makes (the targets are then trusted to be in range)."""
+    return FusedHeadLoss.apply(hidden16.contiguous(), weight16, targets.contiguous(), denominator,
+                               counts)

@@ -19,6 +19,8 @@ then the final norm and the fused head (head.py). Pad tokens never enter the pro
 MLP or head; attention runs on the padded layout, as in the unpatched model.
 """
 
+import threading
+
 import torch
 
 from .head import IGNORE_INDEX, fused_head_loss
@@ -29,6 +31,31 @@ from .rope import rope_pack, slot_index
 
 _ALLOWED_KWARGS = {"num_items_in_batch", "output_attentions", "output_hidden_states",
                    "return_dict"}
+
+_static = threading.local()
+
+
+class StaticBatch:
+    """Host-side facts of one batch, computed before a captured step is replayed so that the
+    step itself makes no host synchronisation: the real-token positions (and their slot map),
+    the attention mask SDPA takes, and the head's (labelled rows, loss denominator). While a
+    StaticBatch is active (`with batch:`), fused_forward uses these instead of deriving them."""
+
+    def __init__(self, pos_idx, slot_tok, mask, counts):
+        self.pos_idx, self.slot_tok, self.mask, self.counts = pos_idx, slot_tok, mask, counts
+
+    def __enter__(self):
+        self._prev = getattr(_static, "batch", None)
+        _static.batch = self
+        return self
+
+    def __exit__(self, *exc):
+        _static.batch = self._prev
+        return False
+
+
+def active_static_batch():
+    return getattr(_static, "batch", None)
 
 
 class HeadStats:
@@ -229,8 +256,12 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
     batch, seq = input_ids.shape
     dev = input_ids.device
     padded = batch * seq
-    pos_idx = attention_mask.reshape(-1).nonzero().squeeze(1)   # sorted, one host sync
-    slot_tok = slot_index(pos_idx, padded)                      # shared by every layer's rope
+    static = active_static_batch()
+    if static is None:
+        pos_idx = attention_mask.reshape(-1).nonzero().squeeze(1)   # sorted, one host sync
+        slot_tok = slot_index(pos_idx, padded)                      # shared by every layer
+    else:
+        pos_idx, slot_tok = static.pos_idx, static.slot_tok
 
     # Embeddings of the real tokens (the table may be held in fp16 with exact values, see
     # trainer_patch.prepare_model); the residual stream is fp32.
@@ -239,8 +270,12 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
 
     shape_ref = s.new_empty((1, 1, 1)).expand(batch, seq, plan.hidden)
     position_ids = torch.arange(seq, device=dev).unsqueeze(0)
-    mask = create_causal_mask(config=cfg, inputs_embeds=shape_ref, attention_mask=attention_mask,
-                              past_key_values=None, position_ids=position_ids)
+    if static is None:
+        mask = create_causal_mask(config=cfg, inputs_embeds=shape_ref,
+                                  attention_mask=attention_mask, past_key_values=None,
+                                  position_ids=position_ids)
+    else:
+        mask = static.mask
     cos, sin = inner.rotary_emb(shape_ref, position_ids)
     cos, sin = cos[0].float(), sin[0].float()
 
@@ -277,7 +312,8 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
     weight = plan.head.weight
     if weight.dtype != torch.float16:
         weight = weight.to(torch.float16)
-    loss, entropy, token_loss, correct = fused_head_loss(y, weight, targets, denominator)
+    loss, entropy, token_loss, correct = fused_head_loss(
+        y, weight, targets, denominator, counts=None if static is None else static.counts)
 
     with torch.no_grad():
         row = torch.div(pos_idx, seq, rounding_mode="floor")
