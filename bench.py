@@ -658,6 +658,10 @@ def ours_arm(args, rank, world, local):
         cpu = {"value": rows / s, "unit": "tokens/s", "cores": thr, "kind": "port",
                "sample": sample}
 
+    # graphs that hold NCCL calls are released before the process group goes away
+    graphed.entries.clear()
+    del graphed, hp
+    torch.cuda.synchronize()
     if rank != 0:
         return
     traffic = None
