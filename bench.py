@@ -659,6 +659,7 @@ def ours_arm(args, rank, world, local):
                "sample": sample}
 
     # graphs that hold NCCL calls are released before the process group goes away
+    hp_launches = hp.launches()
     graphed.entries.clear()
     del graphed, hp
     torch.cuda.synchronize()
@@ -690,7 +691,7 @@ def ours_arm(args, rank, world, local):
         "clocks": clocks,
         "hot_path": {"gbps": hp_bytes / hp_ms / 1e6, "frac": hp_bytes / hp_ms / 1e6 / pk["hbm_gbs"],
                      "ms_per_step": hp_ms, "bytes_per_step": hp_bytes,
-                     "launches_per_step": hp.launches(), "per_kernel": per_kernel,
+                     "launches_per_step": hp_launches, "per_kernel": per_kernel,
                      "peak": pk["hbm_gbs"], "peak_kind": pk_kind},
         "roofline": {"kernel": "nf4_unpack (tb_nf4_unpack_multi)", "bound": "hbm",
                      "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
