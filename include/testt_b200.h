@@ -31,6 +31,12 @@ const char *tb_last_error(void);
 /* Library version, (major << 16) | (minor << 8) | patch. */
 int tb_version(void);
 
+/* Bounded waits (on mbarriers of bulk copies) that gave up on `device` (-1: the current one)
+ * since the library was loaded; each such kernel returned early instead of hanging, so a
+ * nonzero count means its output is incomplete. Synchronising. No counterpart in the
+ * reference (its Triton kernels do not wait on barriers). */
+int tb_wait_timeouts(int32_t device, uint32_t *count);
+
 /* ---------------------------------------------------------------------------------------------
  * NF4 unpack (bitsandbytes 4-bit layout). Replaces nf4_unpack_kernel and its launch in
  * unpack_into, solution/nf4.py:27-45 and :72-89.

@@ -64,10 +64,12 @@ def test_nf4_config1_full_size_bitexact(nested):
 
 
 @pytest.mark.parametrize("shape,blocksize", [((3, 10), 2), ((5, 6), 6), ((7, 64), 32),
-                                             ((1, 2), 2), ((130, 64), 128)])
+                                             ((1, 2), 2), ((130, 64), 128), ((5, 64), 64),
+                                             ((24, 64), 64), ((96, 1536), 64), ((33, 4096), 64)])
 def test_nf4_odd_sizes_and_blocksizes(shape, blocksize):
-    """Sizes whose byte count is not a multiple of 4 or whose block is not a multiple of 8
-    values take the byte-granular kernel; results stay bit-exact."""
+    """Every launch path gives bit-exact values: the bulk-copy pipeline (blocksize 64, sizes in
+    whole 16-byte units), the register path for other blocksize-64 sizes, the word kernel for
+    other blocksizes, and the byte kernel for sizes that are not a multiple of 4 bytes."""
     from testt_b200.nf4 import unpack_concat
 
     rng = np.random.default_rng(sum(shape) + blocksize)
@@ -93,6 +95,13 @@ def test_nf4_more_weights_than_one_launch_and_misaligned_output():
     view = buf[1:].view(3, 64)
     nf4.unpack_into(nf4_weight(qs[0], DEV), view)
     assert_bitexact(view.reshape(-1), cnf4.unpack(qs[0]), "misaligned out")
+
+
+def test_nf4_no_wait_timed_out():
+    """The bulk-copy kernel's bounded waits never gave up in the runs above."""
+    from testt_b200 import _lib
+
+    assert _lib.wait_timeouts() == 0
 
 
 def test_nf4_rejects_bad_blocksize_and_cpu_tensors():

@@ -12,7 +12,8 @@ import os
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libtestt_b200.so")
+# TESTT_B200_LIB points at another build of the same library (for example a debug build)
+LIB_PATH = os.environ.get("TESTT_B200_LIB") or os.path.join(HERE, "libtestt_b200.so")
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -36,6 +37,7 @@ SIGNATURES = {
     "tb_head_partials": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _P],
     "tb_head_merge": [_P, _P, _P, _I64, _I32, _I32, _P, _P, _P, _P, _P],
     "tb_head_dlogits": [_P, _P, _P, _I64, _I64, _I64, _I64, _F, _P],
+    "tb_wait_timeouts": [_I32, _P],
 }
 
 _lib = None
@@ -111,6 +113,13 @@ def ptr_array(values):
     for i, v in enumerate(values):
         arr[i] = None if v is None else (v.value if isinstance(v, ctypes.c_void_p) else v)
     return arr
+
+
+def wait_timeouts(device=-1):
+    """Bounded device-side waits that gave up (see tb_wait_timeouts); synchronising."""
+    count = ctypes.c_uint32(0)
+    call("tb_wait_timeouts", int(device), ctypes.byref(count))
+    return count.value
 
 
 def exported_symbols():

@@ -36,8 +36,35 @@ int sm_count() {
   return cached[dev];
 }
 
+static TimeoutReader g_readers[16];
+static int g_n_readers = 0;
+
+int register_timeout_reader(TimeoutReader reader) {
+  if (g_n_readers < 16) g_readers[g_n_readers++] = reader;
+  return g_n_readers;
+}
+
 }  // namespace tb
 
 extern "C" const char *tb_last_error(void) { return tb::g_last_error; }
+
+extern "C" int tb_wait_timeouts(int32_t device, uint32_t *count) {
+  if (count == nullptr) return tb::set_error(TB_EINVAL, "wait_timeouts: count is required");
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return tb::check_launch("wait_timeouts");
+  if (device >= 0 && cudaSetDevice(device) != cudaSuccess) return tb::check_launch("wait_timeouts");
+  uint32_t total = 0;
+  cudaError_t e = cudaSuccess;
+  for (int i = 0; i < tb::g_n_readers && e == cudaSuccess; ++i) {
+    unsigned int c = 0;
+    e = tb::g_readers[i](&c);
+    total += c;
+  }
+  if (device >= 0) cudaSetDevice(prev);
+  if (e != cudaSuccess)
+    return tb::set_error(TB_ELAUNCH, "wait_timeouts: %s", cudaGetErrorString(e));
+  *count = total;
+  return TB_OK;
+}
 
 extern "C" int tb_version(void) { return (0 << 16) | (1 << 8) | 0; }

@@ -103,6 +103,75 @@ __device__ __forceinline__ void store8h_cs(uint16_t *p, const float (&f)[8]) {
   __stcs(reinterpret_cast<uint4 *>(p), v);
 }
 
+// ---- bulk async copies and mbarriers (sm_90+ PTX, used on sm_100a) -------------------------
+// 1-D bulk copy global -> shared completing on an mbarrier (no multicast). Every wait on an
+// mbarrier is bounded: after kWaitLimit polls the waiter gives up, counts a timeout in
+// g_wait_timeouts (read by tb_wait_timeouts) and the kernel returns instead of hanging.
+
+constexpr uint32_t kWaitLimit = 1u << 24;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// true once the phase with the given parity has completed; false after kWaitLimit polls
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+// Bounded waits that gave up, on the current device since the library was loaded. One counter
+// per translation unit (no relocatable device code); a file whose kernels wait registers a
+// reader with TB_REGISTER_TIMEOUT_READER and tb_wait_timeouts sums them.
+static __device__ unsigned int g_wait_timeouts = 0;
+
+typedef cudaError_t (*TimeoutReader)(unsigned int *);
+int register_timeout_reader(TimeoutReader reader);
+
+#define TB_REGISTER_TIMEOUT_READER(tag)                                             \
+  static cudaError_t tag##_read_timeouts(unsigned int *out) {                       \
+    return cudaMemcpyFromSymbol(out, ::tb::g_wait_timeouts, sizeof(unsigned int));  \
+  }                                                                                 \
+  static const int tag##_timeout_reader = ::tb::register_timeout_reader(tag##_read_timeouts);
+
 // ---- reductions ----------------------------------------------------------------------------
 
 __device__ __forceinline__ float warp_sum(float v) {
