@@ -169,6 +169,22 @@ int tb_head_merge(const float *part, const int64_t *part_idx, const int64_t *tar
                   int64_t rows, int32_t n_groups, int32_t splits, float *lse, float *entropy,
                   float *loss, int32_t *correct, void *stream);
 
+/* tb_head_stats_grad's contract (the same outputs, the same in-place dlogits) with nothing
+ * allocated anywhere, for callers that cannot allocate device memory themselves: a host binding
+ * that only ever receives buffers owned by someone else (a plain C FFI from another language
+ * runtime), a process whose framework allocator has reserved all device memory so that a
+ * cudaMalloc here would fail or fragment it, or a latency-critical loop that cannot afford the
+ * device synchronisation cudaMalloc implies. No counterpart in the reference (its head kernel,
+ * solution/head.py:34-76, needs no scratch). The scratch it uses (partial states of the split
+ * form, 1,179,648 bytes) is a fixed array inside the library: each GPU that loads the library
+ * holds it until the process exits. At most 32768 rows per call (larger calls are rejected with
+ * TB_EINVAL). The first call on a device looks up the array's device address (once per
+ * device), so make that first call before any stream capture. Calls share the array: calls
+ * whose kernels overlap on the GPU (different streams, no ordering) race and must not be made. */
+int tb_head_stats_grad_noalloc(uint16_t *logits, const int64_t *targets, float *entropy,
+                               float *loss, int32_t *correct, int64_t rows, int64_t vocab,
+                               int64_t ld, float grad_scale, void *stream);
+
 /* In place over the labelled rows of a [rows, cols] slab (columns col_offset ..):
  * logits <- fp16((exp(z - lse[row]) - [col == target]) * grad_scale); unlabelled rows untouched. */
 int tb_head_dlogits(uint16_t *logits, const int64_t *targets, const float *lse, int64_t rows,

@@ -10,6 +10,8 @@
 // reference's tl.exp lowers to.
 #include <math_constants.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace tb {
@@ -415,4 +417,82 @@ extern "C" int tb_head_dlogits(uint16_t *logits, const int64_t *targets, const f
                                                       col_offset, grad_scale);
   }
   return check_launch("head_dlogits");
+}
+
+// ---- the same statistics with no allocation anywhere (tb_head_stats_grad_noalloc) -----------
+// Scratch of the split form (partial states, their argmax indices, the merged lse) lives in one
+// file-scope device array instead of caller-provided buffers. Each GPU that loads the library
+// holds it (1,179,648 bytes) until the process exits. Every call shares it and leaves the last
+// call's contents behind; nothing in it needs to start at zero (the partials kernel writes every
+// (row, split) state before the merge reads it, the merge writes every lse before the dlogits
+// sweep reads it). Calls whose kernels overlap on the GPU (on different streams) race on it.
+namespace tb {
+namespace {
+
+constexpr int64_t kNoAllocMaxRows = 32768;   // rows per call
+constexpr int64_t kNoAllocMaxParts = 32768;  // rows x splits per call
+constexpr size_t kNoAllocPartBytes = (size_t)kNoAllocMaxParts * kPartFields * sizeof(float);
+constexpr size_t kNoAllocIdxBytes = (size_t)kNoAllocMaxParts * sizeof(int64_t);
+constexpr size_t kNoAllocLseBytes = (size_t)kNoAllocMaxRows * sizeof(float);
+constexpr size_t kNoAllocBytes = kNoAllocPartBytes + kNoAllocIdxBytes + kNoAllocLseBytes;
+
+static __device__ __align__(256) unsigned char g_head_scratch[kNoAllocBytes];
+
+// Device address of g_head_scratch on the current device, taken once per device (the host-side
+// name of the array is not a device address).
+int head_scratch(unsigned char **out) {
+  static std::mutex lock;
+  static unsigned char *cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return set_error(TB_EDEVICE, "head_stats_grad_noalloc: no usable current device");
+  std::lock_guard<std::mutex> guard(lock);
+  if (cached[dev] == nullptr) {
+    void *ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_head_scratch);
+    if (e != cudaSuccess || ptr == nullptr)
+      return set_error(TB_ELAUNCH, "head_stats_grad_noalloc: scratch address: %s",
+                       cudaGetErrorString(e));
+    cached[dev] = static_cast<unsigned char *>(ptr);
+  }
+  *out = cached[dev];
+  return TB_OK;
+}
+
+}  // namespace
+}  // namespace tb
+
+extern "C" int tb_head_stats_grad_noalloc(uint16_t *logits, const int64_t *targets,
+                                          float *entropy, float *loss, int32_t *correct,
+                                          int64_t rows, int64_t vocab, int64_t ld,
+                                          float grad_scale, void *stream) {
+  if (rows < 0 || vocab <= 0 || ld < vocab)
+    return set_error(TB_EINVAL, "head_stats_grad_noalloc: rows %lld vocab %lld ld %lld",
+                     (long long)rows, (long long)vocab, (long long)ld);
+  if (rows > kNoAllocMaxRows)
+    return set_error(TB_EINVAL,
+                     "head_stats_grad_noalloc: %lld rows exceed the fixed scratch (at most %lld "
+                     "rows per call; split the call or use tb_head_stats_grad)",
+                     (long long)rows, (long long)kNoAllocMaxRows);
+  if (rows == 0) return TB_OK;
+  if (!logits || !targets || !entropy || !loss || !correct)
+    return set_error(TB_EINVAL, "head_stats_grad_noalloc: all pointers are required");
+  unsigned char *scratch = nullptr;
+  int rc = head_scratch(&scratch);
+  if (rc != TB_OK) return rc;
+  float *part = reinterpret_cast<float *>(scratch);
+  int64_t *part_idx = reinterpret_cast<int64_t *>(scratch + kNoAllocPartBytes);
+  float *lse = reinterpret_cast<float *>(scratch + kNoAllocPartBytes + kNoAllocIdxBytes);
+  // enough (row, split) CTAs to fill the GPU, within the scratch
+  int64_t splits = (4LL * sm_count() + rows - 1) / rows;
+  if (splits > 16) splits = 16;
+  if (splits > kNoAllocMaxParts / rows) splits = kNoAllocMaxParts / rows;
+  if (splits < 1) splits = 1;
+  rc = tb_head_partials(logits, targets, part, part_idx, rows, vocab, ld, 0, (int32_t)splits,
+                        stream);
+  if (rc != TB_OK) return rc;
+  rc = tb_head_merge(part, part_idx, targets, rows, 1, (int32_t)splits, lse, entropy, loss,
+                     correct, stream);
+  if (rc != TB_OK) return rc;
+  return tb_head_dlogits(logits, targets, lse, rows, vocab, ld, 0, grad_scale, stream);
 }
