@@ -169,6 +169,20 @@ int tb_head_merge(const float *part, const int64_t *part_idx, const int64_t *tar
                   int64_t rows, int32_t n_groups, int32_t splits, float *lse, float *entropy,
                   float *loss, int32_t *correct, void *stream);
 
+/* The head's logits GEMM on the tensor cores with sweep 1 fused into its epilogue. For rows of
+ * hidden fp16 [rows, hidden_dim] and the head weight fp16 [vocab, hidden_dim] (both row-major,
+ * hidden_dim a multiple of 64, 16-byte aligned): z = fp16(hidden . weight^T) (tcgen05.mma, fp32
+ * accumulation in TMEM, rounded to fp16 as the reference's fp16 GEMM output,
+ * solution/head.py:107) and, per row and 256-column vocabulary tile, the partial state of
+ * tb_head_partials: part fp32 [rows, ceil(vocab/256), 6], part_idx int64 [rows, ceil(vocab/256)]
+ * (merge them with tb_head_merge, n_groups 1, splits ceil(vocab/256)). When logits is non-NULL
+ * the fp16 logits of the first logits_rows rows are written to it ([logits_rows, vocab]) for
+ * the dlogits pass. Replaces the cuBLAS logits GEMM + sweep 1 of the
+ * reference's head (solution/head.py:107-110, :54-72). sm_100 only. */
+int tb_head_logits_stats(const uint16_t *hidden, const uint16_t *weight, const int64_t *targets,
+                         uint16_t *logits, int64_t logits_rows, float *part, int64_t *part_idx,
+                         int64_t rows, int64_t vocab, int64_t hidden_dim, void *stream);
+
 /* tb_head_stats_grad's contract (the same outputs, the same in-place dlogits) with nothing
  * allocated anywhere, for callers that cannot allocate device memory themselves: a host binding
  * that only ever receives buffers owned by someone else (a plain C FFI from another language

@@ -1,0 +1,91 @@
+"""The tensor-core head (tb_head_logits_stats: tcgen05 GEMM with the statistics epilogue): its
+fp16 logits against an fp32 GEMM rounded to fp16 (within 1 ulp: only the fp32 accumulation order
+differs), and its partials, merged by tb_head_merge, against the fp64 oracle and the reference
+path (cuBLAS logits + tb_head_stats_grad): loss and entropy rtol 1e-4, first-argmax hits exact."""
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_rel
+from oracle import ops
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _case(rows, vocab, hidden, seed, std=1.0):
+    g = torch.Generator().manual_seed(seed)
+    h = torch.randn(rows, hidden, generator=g).half()
+    w = (torch.randn(vocab, hidden, generator=g) * (std / hidden ** 0.5) * 4).half()
+    tg = torch.randint(0, vocab, (rows,), generator=g)
+    tg[torch.rand(rows, generator=g) < 0.35] = -100
+    return h.to(DEV), w.to(DEV), tg.to(DEV)
+
+
+def assert_logits(got, ref):
+    """Within 1 fp16 ulp, or within 1e-4 of the tensor's rms where a sum cancels to near zero
+    (there an accumulation-order difference of the fp32 sums spans several tiny ulps)."""
+    from helpers import fp16_ulp_diff
+
+    d = fp16_ulp_diff(got, ref)
+    diff = (got.float() - ref.float()).abs().cpu().numpy()
+    rms = float(ref.float().pow(2).mean().sqrt())
+    bad = (d > 1) & (diff > 1e-4 * rms)
+    assert not bad.any(), f"logits: {int(bad.sum())} values beyond 1 ulp and 1e-4 rms"
+    assert (d <= 1).mean() > 0.998
+
+
+def tc_head(h, w, tg, logits_rows):
+    from testt_b200 import _lib
+
+    rows, hidden = h.shape
+    vocab = w.shape[0]
+    vt = -(-vocab // 256)
+    part = torch.empty((rows, vt, 6), dtype=torch.float32, device=DEV)
+    idx = torch.empty((rows, vt), dtype=torch.int64, device=DEV)
+    logits = torch.empty((max(logits_rows, 1), vocab), dtype=torch.float16, device=DEV)
+    _lib.call("tb_head_logits_stats", _lib.ptr(h), _lib.ptr(w), _lib.ptr(tg),
+              _lib.ptr(logits) if logits_rows else None, logits_rows, _lib.ptr(part),
+              _lib.ptr(idx), rows, vocab, hidden, _lib.stream_of(h))
+    lse = torch.empty(rows, device=DEV)
+    ent, loss = torch.empty_like(lse), torch.empty_like(lse)
+    cor = torch.empty(rows, dtype=torch.int32, device=DEV)
+    _lib.call("tb_head_merge", _lib.ptr(part), _lib.ptr(idx), _lib.ptr(tg), rows, 1, vt,
+              _lib.ptr(lse), _lib.ptr(ent), _lib.ptr(loss), _lib.ptr(cor), _lib.stream_of(h))
+    torch.cuda.synchronize()
+    assert _lib.wait_timeouts() == 0
+    return logits[:logits_rows], lse, ent, loss, cor
+
+
+@pytest.mark.parametrize("rows,vocab,hidden", [(128, 256, 64), (300, 1000, 128),
+                                               (7, 5003, 192), (129, 512, 1536)])
+def test_tc_head_small_shapes(rows, vocab, hidden):
+    h, w, tg = _case(rows, vocab, hidden, rows + vocab)
+    logits, lse, ent, loss, cor = tc_head(h, w, tg, rows)
+    ref16 = (h.float() @ w.float().t()).half()
+    assert_logits(logits, ref16)
+    rent, rloss, rcor, _ = ops.head_stats_exact(logits.cpu(), tg.cpu(), 1.0)
+    assert_rel(loss, rloss, 1e-4, "loss", floor=0.0)
+    assert_rel(ent, rent, 1e-4, "entropy", floor=0.0)
+    assert torch.equal(cor.cpu().bool(), rcor)
+
+
+def test_tc_head_config4_against_reference_path():
+    """Config 4 (2048 rows, vocab 151936, hidden 1536): the fused statistics against cuBLAS
+    logits + tb_head_stats_grad, on the same inputs."""
+    from oracle import synth
+    from testt_b200.head import head_stats_grad
+
+    c = synth.config4(DEV)
+    h, w, tg = c["hidden"], c["weight"], c["targets"]
+    logits, lse, ent, loss, cor = tc_head(h, w, tg, 256)
+    ref = (h[:256].float() @ w.float().t()).half()
+    assert_logits(logits, ref)
+    full = torch.empty(2048, w.shape[0], dtype=torch.float16, device=DEV)
+    torch.matmul(h, w.t(), out=full)
+    rent, rloss, rcor = head_stats_grad(full, tg, 1.0)
+    assert_rel(loss, rloss, 1e-4, "loss", floor=0.0)
+    assert_rel(ent, rent, 1e-4, "entropy", floor=0.0)
+    # a hit can flip only where cuBLAS and the tensor-core GEMM round a near-tie differently
+    assert int((cor != rcor).sum()) == 0

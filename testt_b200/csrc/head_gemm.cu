@@ -1,0 +1,413 @@
+// Vocabulary head on the 5th-generation tensor cores: logits = h . W^T with tcgen05.mma (TMEM
+// accumulators, TMA-fed shared-memory operands) and the online-softmax partial statistics of
+// each (row, 256-column vocabulary tile) computed in the epilogue, so the logits never have to be
+// read back for sweep 1 of the reference's head kernel (solution/head.py:54-72).
+//
+// One persistent CTA per SM, warp-specialised:
+//   warp 0       TMA producer: per K block of 64, a 128x64 tile of h and a 256x64 tile of W
+//                (fp16, K-major, 128-byte swizzle) into a 4-stage shared-memory ring
+//   warp 1       MMA issuer: 4 x tcgen05.mma.kind::f16 (M128 N256 K16) per stage into one of two
+//                TMEM accumulators (2 x 256 fp32 columns, double-buffered across tiles)
+//   warps 2..5   epilogue: tcgen05.ld of the tile's rows (warp w reads TMEM lanes 32*(w%4)..),
+//                logits rounded to fp16 exactly as the reference's fp16 GEMM output, then per row
+//                (max, sum e, sum e z, first argmax, z[target]) -> part[row][vtile], and
+//                optionally the fp16 logits for the dlogits / dh pass.
+// tb_head_merge then merges the vocabulary tiles into lse, entropy, loss and the argmax hit.
+// Tiles are ordered so concurrent CTAs share vocabulary tiles (W streamed from HBM about once).
+// Every mbarrier wait is bounded (mbar_wait); a role that gives up leaves its loop, all roles
+// meet at the final barrier and TMEM is always deallocated. No multicast is used.
+#include <cuda.h>
+
+#include <math_constants.h>
+
+#include "common.cuh"
+
+namespace tb {
+namespace {
+
+constexpr int kBM = 128, kBN = 256, kBK = 64;   // tile; kBK fp16 = 128 bytes = one swizzle row
+constexpr int kStages = 4;
+constexpr int kABytes = kBM * kBK * 2;          // 16 KB
+constexpr int kBBytes = kBN * kBK * 2;          // 32 KB
+constexpr int kStageBytes = kABytes + kBBytes;  // 48 KB
+constexpr int kThreads = 192;                   // 6 warps
+constexpr int kTmemCols = 2 * kBN;              // two fp32 accumulators
+constexpr int kPartFields = 6;
+
+// M=128, N=256, A=B=f16 (K-major), D=f32: the kind::f16 instruction descriptor
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+
+struct Smem {
+  alignas(1024) uint8_t stage[kStages][kStageBytes];  // A then B per stage (1024-aligned atoms)
+  uint64_t full[kStages], empty[kStages];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  volatile int error;  // a role gave up waiting: every role leaves its loop
+};
+
+// K-major, 128-byte-swizzle operand descriptor: start address, LBO 1 (ignored for swizzled
+// K-major), SBO 1024 bytes between 8-row atoms, version 1 (sm_100), layout SWIZZLE_128B.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3fff);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+      "l"(a), "l"(b), "r"(kIdesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::
+                   "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct HeadArgs {
+  const int64_t *targets;
+  uint16_t *logits;  // optional fp16 [logits_rows, vocab] output
+  float *part;       // [rows, n_vtiles, 6]
+  int64_t *part_idx; // [rows, n_vtiles]
+  int rows, logits_rows, vocab, k_blocks, m_tiles, v_tiles;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    head_logits_stats(const __grid_constant__ CUtensorMap map_h,
+                      const __grid_constant__ CUtensorMap map_w, const HeadArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem &sm = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                        ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t tiles = (int64_t)args.m_tiles * args.v_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&sm.acc_full[a], 1);
+      mbar_init(&sm.acc_empty[a], 4);
+    }
+    mbar_init(&sm.mma_done, 1);
+    sm.error = 0;
+    mbar_init_fence();
+  }
+  if (warp == 1) {  // TMEM: two 256-column fp32 accumulators
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&sm.tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    // ---- TMA producer -------------------------------------------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      for (int64_t t = blockIdx.x; t < tiles && !sm.error; t += gridDim.x) {
+        const int mt = (int)(t % args.m_tiles), vt = (int)(t / args.m_tiles);
+        for (int kb = 0; kb < args.k_blocks; ++kb) {
+          if (!mbar_wait(&sm.empty[stage], phase ^ 1)) {
+            sm.error = 1;
+            break;
+          }
+          mbar_expect_tx(&sm.full[stage], kStageBytes);
+          tma_load_2d(sm.stage[stage], &map_h, kb * kBK, mt * kBM, &sm.full[stage]);
+          tma_load_2d(sm.stage[stage] + kABytes, &map_w, kb * kBK, vt * kBN, &sm.full[stage]);
+          ++issued;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // every copy issued must have landed before the CTA may leave (bounded)
+      for (int s = 0; s < kStages && s < (int)issued; ++s) {
+        if (stage == 0) {
+          stage = kStages;
+          phase ^= 1;
+        }
+        --stage;
+        mbar_wait(&sm.full[stage], phase);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ---------------------------------------------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t it = 0;
+      for (int64_t t = blockIdx.x; t < tiles && !sm.error; t += gridDim.x, ++it) {
+        const int acc = (int)(it & 1);
+        const uint32_t acc_phase = (uint32_t)((it >> 1) & 1);
+        if (!mbar_wait(&sm.acc_empty[acc], acc_phase ^ 1)) {
+          sm.error = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(acc * kBN);
+        for (int kb = 0; kb < args.k_blocks; ++kb) {
+          if (!mbar_wait(&sm.full[stage], phase)) {
+            sm.error = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sm.stage[stage]);
+          const uint32_t b0 = a0 + kABytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)  // K = 16 per MMA: 32 bytes along the swizzled row
+            mma_f16(d, smem_desc(a0 + k * 32), smem_desc(b0 + k * 32), (kb | k) != 0);
+          mma_commit(&sm.empty[stage]);  // the stage is free once these MMAs have read it
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        mma_commit(&sm.acc_full[acc]);  // the accumulator is ready once all its MMAs are done
+      }
+      mma_commit(&sm.mma_done);
+      mbar_wait(&sm.mma_done, 0);  // no MMA in flight before TMEM is released
+    }
+  } else {
+    // ---- epilogue: 4 warps, thread = one row of the tile ----------------------------------
+    const int quarter = warp & 3;                // TMEM lanes 32*quarter .. 32*quarter+31
+    const int row_in_tile = quarter * 32 + lane;
+    int64_t it = 0;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+      const int acc = (int)(it & 1);
+      const uint32_t acc_phase = (uint32_t)((it >> 1) & 1);
+      const int ok = mbar_wait(&sm.acc_full[acc], acc_phase) ? 1 : 0;
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) sm.error = 1;
+        break;
+      }
+      tc_fence_after();
+      const int mt = (int)(t % args.m_tiles), vt = (int)(t / args.m_tiles);
+      const int row = mt * kBM + row_in_tile;
+      const bool live = row < args.rows;
+      const int64_t target = live ? __ldg(args.targets + row) : -1;
+      const int col0 = vt * kBN;
+      float m = -CUDART_INF_F, s = 0.f, dz = 0.f, best = -CUDART_INF_F, zt = 0.f;
+      int64_t best_idx = 0x7fffffffffffffffLL;
+      bool found = false;
+      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kBN);
+#pragma unroll 1
+      for (int c = 0; c < kBN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + (uint32_t)c, r);
+        float z[32];
+        uint32_t h16[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const __half2 hh = __floats2half2_rn(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+          const float2 zz = __half22float2(hh);
+          z[i] = zz.x;
+          z[i + 1] = zz.y;
+          h16[i / 2] = *reinterpret_cast<const uint32_t *>(&hh);
+        }
+        const int cbase = col0 + c;
+        const int nvalid = min(32, args.vocab - cbase);
+        if (nvalid <= 0) continue;
+        const bool keep = live && args.logits != nullptr && row < args.logits_rows;
+        if (keep && nvalid == 32 && (args.vocab & 7) == 0) {
+          uint4 *dst = reinterpret_cast<uint4 *>(args.logits + (int64_t)row * args.vocab + cbase);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(h16[4 * q], h16[4 * q + 1], h16[4 * q + 2], h16[4 * q + 3]);
+        } else if (keep) {
+          for (int i = 0; i < nvalid; ++i)
+            args.logits[(int64_t)row * args.vocab + cbase + i] =
+                (uint16_t)(h16[i / 2] >> (16 * (i & 1)));
+        }
+        float lm = -CUDART_INF_F;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < nvalid) lm = fmaxf(lm, z[i]);
+        if (lm > m) {
+          const float sc = __expf(m - lm);
+          s *= sc;
+          dz *= sc;
+          m = lm;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (i < nvalid) {
+            const float e = __expf(z[i] - m);
+            s += e;
+            dz += e * z[i];
+            if (z[i] > best) {
+              best = z[i];
+              best_idx = cbase + i;
+            }
+            if (cbase + i == target) {
+              zt = z[i];
+              found = true;
+            }
+          }
+        }
+      }
+      // the accumulator may be overwritten once every epilogue warp has read it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
+      if (live) {
+        const int64_t at = (int64_t)row * args.v_tiles + vt;
+        float *out = args.part + at * kPartFields;
+        out[0] = m;
+        out[1] = s;
+        out[2] = dz;
+        out[3] = best;
+        out[4] = found ? zt : 0.f;
+        out[5] = found ? 1.f : 0.f;
+        args.part_idx[at] = best_idx;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && sm.error) atomicAdd(&g_wait_timeouts, 1u);
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// ---- host: TMA descriptors through the driver entry point (no libcuda link) ---------------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D fp16 row-major [rows, cols] -> box [box_rows, 64] with 128-byte swizzle
+int make_map(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return set_error(TB_EDEVICE, "head: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims,
+                        strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(TB_EINVAL, "head: tensor map encode failed (%d)", (int)r);
+  return TB_OK;
+}
+
+}  // namespace
+
+TB_REGISTER_TIMEOUT_READER(head_gemm)
+
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" int tb_head_logits_stats(const uint16_t *hidden, const uint16_t *weight,
+                                    const int64_t *targets, uint16_t *logits, int64_t logits_rows,
+                                    float *part, int64_t *part_idx, int64_t rows, int64_t vocab,
+                                    int64_t hidden_dim, void *stream) {
+  if (rows < 0 || vocab <= 0 || hidden_dim <= 0)
+    return set_error(TB_EINVAL, "head_logits_stats: rows %lld vocab %lld hidden %lld",
+                     (long long)rows, (long long)vocab, (long long)hidden_dim);
+  if (rows == 0) return TB_OK;
+  if (!hidden || !weight || !targets || !part || !part_idx)
+    return set_error(TB_EINVAL, "head_logits_stats: hidden, weight, targets, part, part_idx required");
+  if (hidden_dim % kBK != 0)
+    return set_error(TB_EINVAL, "head_logits_stats: hidden size %lld is not a multiple of %d",
+                     (long long)hidden_dim, kBK);
+  if (!aligned(hidden, 16) || !aligned(weight, 16) || (logits && !aligned(logits, 16)))
+    return set_error(TB_EALIGN, "head_logits_stats: 16-byte aligned buffers are required");
+  if (rows > (1LL << 30) || vocab > (1LL << 30))
+    return set_error(TB_EINVAL, "head_logits_stats: sizes too large");
+  int dev = 0, major = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (major != 10) return set_error(TB_EDEVICE, "head_logits_stats: needs an sm_100 GPU");
+  CUtensorMap map_h, map_w;
+  int rc = make_map(&map_h, hidden, rows, hidden_dim, kBM);
+  if (rc == TB_OK) rc = make_map(&map_w, weight, vocab, hidden_dim, kBN);
+  if (rc != TB_OK) return rc;
+  HeadArgs a;
+  a.targets = targets;
+  a.logits = logits;
+  a.part = part;
+  a.part_idx = part_idx;
+  a.rows = (int)rows;
+  a.logits_rows = logits ? (int)(logits_rows < rows ? logits_rows : rows) : 0;
+  a.vocab = (int)vocab;
+  a.k_blocks = (int)(hidden_dim / kBK);
+  a.m_tiles = (int)((rows + kBM - 1) / kBM);
+  a.v_tiles = (int)((vocab + kBN - 1) / kBN);
+  const size_t smem = sizeof(Smem) + 1024;
+  if (cudaFuncSetAttribute(head_logits_stats, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return check_launch("head_logits_stats attribute");
+  const int64_t tiles = (int64_t)a.m_tiles * a.v_tiles;
+  const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
+  head_logits_stats<<<grid, kThreads, smem, as_stream(stream)>>>(map_h, map_w, a);
+  return check_launch("head_logits_stats");
+}
