@@ -382,6 +382,26 @@ def _nf4_bytes(weight):
     return b
 
 
+def _nf4_traffic(bytes_per_launch):
+    """DRAM bytes (read + write) per NF4 launch from the committed ncu summary of config 1
+    (profiles/nf4_unpack_config1.md), scaled to a launch of `bytes_per_launch` algorithmic bytes
+    (traffic grows in proportion to the values unpacked). None if the summary is absent."""
+    import re
+
+    path = os.path.join(ROOT, "profiles", "nf4_unpack_config1.md")
+    if not os.path.exists(path):
+        return None
+    text = open(path).read()
+    scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}
+    total = 0.0
+    for what in ("read", "write"):
+        m = re.search(rf"DRAM {what} during the kernel \| ([0-9.]+) (\w+)", text)
+        if not m:
+            return None
+        total += float(m.group(1)) * scale.get(m.group(2), 1)
+    return total * bytes_per_launch / 35266624
+
+
 def flush_l2(buf):
     """Evict the L2 (126 MB on B200) by reading a larger buffer: the lines it leaves are clean,
     so the next kernel does not pay for writing back dirty data of earlier work."""
@@ -507,6 +527,18 @@ def kernel_bench(name, steps, warmup, device):
             gu = c["gu"].clone()
             fn = lambda: mlp.gated_silu_backward_(c["dact"], gu)  # noqa: E731
             nbytes = m * 89600
+    elif name == "head_tc":
+        c = synth.config4(dev)
+        rows, hidden, vocab = 2048, synth.HIDDEN, synth.VOCAB
+        vt = -(-vocab // 256)
+        part = torch.empty((rows, vt, 6), device=dev)
+        pidx = torch.empty((rows, vt), dtype=torch.int64, device=dev)
+        fn = lambda: _lib.call(  # noqa: E731
+            "tb_head_logits_stats", _lib.ptr(c["hidden"]), _lib.ptr(c["weight"]),
+            _lib.ptr(c["targets"]), None, 0, _lib.ptr(part), _lib.ptr(pidx), rows, vocab, hidden,
+            _lib.stream_of(part))
+        nbytes = 0
+        info = {"config": "4", "rows": rows, "flops": 2 * rows * hidden * vocab}
     elif name == "head_stats":
         c = synth.config4(dev, rows=256)
         logits = c["hidden"] @ c["weight"].t()
@@ -530,6 +562,10 @@ def kernel_bench(name, steps, warmup, device):
         times.append(a.elapsed_time(b) * 1e3)
     us = float(np.median(times))
     pk, kind = peaks()
+    if "flops" in info:
+        tf = info["flops"] / us / 1e6
+        return {"kernel": name, "us": us, "us_min": float(min(times)), "tflops": tf,
+                "frac": tf / pk["bf16_tflops"], "peak_kind": kind, **info}
     gbps = nbytes / us / 1e3
     return {"kernel": name, "us": us, "us_min": float(min(times)), "bytes": nbytes,
             "gbps": gbps, "frac": gbps / pk["hbm_gbs"], "peak_kind": kind, **info}
@@ -665,11 +701,7 @@ def ours_arm(args, rank, world, local):
     torch.cuda.synchronize()
     if rank != 0:
         return
-    traffic = None
-    tpath = os.path.join(ROOT, "profiles", "nf4_unpack_traffic.json")
-    if os.path.exists(tpath):
-        with open(tpath) as f:
-            traffic = json.load(f).get("bytes_per_launch")
+    traffic = _nf4_traffic(nf["bytes"] / n_launch)
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -697,7 +729,11 @@ def ours_arm(args, rank, world, local):
                      "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / pk["hbm_gbs"], "peak_kind": pk_kind,
                      "launches": n_launch, "avg_launch_us": nf["ms"] * 1e3 / n_launch,
-                     "bytes_per_launch": nf["bytes"] / n_launch, "traffic": traffic},
+                     "bytes_per_launch": nf["bytes"] / n_launch, "traffic": traffic,
+                     "traffic_note": "ncu capture of one config-1 launch (profiles/"
+                                     "nf4_unpack_config1.md) scaled to the step's average launch; "
+                                     "its fp16 output stays in L2 during a single launch, so the "
+                                     "captured DRAM traffic is the reads only"},
         "head": None if head is None else {
             **head, "frac": head["tflops"] / pk["bf16_tflops"], "peak": pk["bf16_tflops"],
             "bound": "tensor", "unit": "TFLOP/s"},
@@ -716,11 +752,11 @@ def main():
     ap.add_argument("--kernel", default=None,
                     help="time one kernel at its configuration instead (nf4, nf4_nested, "
                          "rmsnorm_fwd, rmsnorm_bwd, rope_fwd, rope_bwd, swiglu_fwd, swiglu_bwd, "
-                         "head_stats, all)")
+                         "head_stats, head_tc, all)")
     args = ap.parse_args()
     if args.kernel:
         names = ["nf4", "nf4_nested", "rmsnorm_fwd", "rmsnorm_bwd", "rope_fwd", "rope_bwd",
-                 "swiglu_fwd", "swiglu_bwd", "head_stats"] if args.kernel == "all" \
+                 "swiglu_fwd", "swiglu_bwd", "head_stats", "head_tc"] if args.kernel == "all" \
             else args.kernel.split(",")
         for n in names:
             print(json.dumps(kernel_bench(n, args.steps, args.warmup, "cuda:0")), flush=True)

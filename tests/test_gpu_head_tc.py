@@ -89,3 +89,30 @@ def test_tc_head_config4_against_reference_path():
     assert_rel(ent, rent, 1e-4, "entropy", floor=0.0)
     # a hit can flip only where cuBLAS and the tensor-core GEMM round a near-tie differently
     assert int((cor != rcor).sum()) == 0
+
+
+def test_fused_head_loss_tensor_core_path_equals_chunked_path():
+    """fused_head_loss through the tensor-core head and through the reference's chunked
+    structure: same loss, statistics and (within fp16 rounding) gradient."""
+    from oracle import synth
+    from testt_b200 import head
+
+    c = synth.config4(DEV, rows=512)
+    outs = []
+    for tc in (True, False):
+        head.USE_TENSOR_CORE_HEAD = tc
+        try:
+            hh = c["hidden"].clone().requires_grad_(True)
+            loss, ent, tok, cor = head.fused_head_loss(hh, c["weight"], c["targets"],
+                                                       int((c["targets"] != -100).sum()))
+            loss.backward()
+            outs.append((loss.detach(), ent, tok, cor, hh.grad))
+        finally:
+            head.USE_TENSOR_CORE_HEAD = True
+    (l1, e1, t1, c1, g1), (l2, e2, t2, c2, g2) = outs
+    assert_rel(l1, l2, 1e-4, "loss", floor=0.0)
+    assert_rel(e1, e2, 1e-4, "entropy", floor=0.0)
+    assert_rel(t1, t2, 1e-4, "token loss", floor=0.0)
+    assert torch.equal(c1, c2)
+    rel = (g1.float() - g2.float()).norm() / g2.float().norm()
+    assert rel < 1e-2, float(rel)

@@ -1,14 +1,19 @@
 """The output head and everything computed from its logits, without full logits, on B200
 (reference: solution/head.py).
 
-The head runs over the real (non-pad) tokens in chunks of CHUNK_ROWS rows, labelled rows first:
-1. logits = h @ W^T for the chunk, fp16 (cuBLAS through torch.matmul);
-2. tb_head_stats_grad, one CTA per row, two sweeps over the vocabulary: sweep 1 (online, fp32)
-   gives logsumexp, entropy = lse - sum(p z), the token loss lse - z[label] and whether the first
-   argmax is the label; sweep 2 (labelled rows only) overwrites the logits in place with
-   (softmax - onehot) * scale in fp16;
-3. dh = dlogits @ W for the labelled rows of the chunk (cuBLAS).
-The gradient is taken in forward (the head is frozen) and scaled by the loss scale in backward.
+The head runs over the real (non-pad) tokens, labelled rows first. On B200 (sm_100):
+1. tb_head_logits_stats: logits = h @ W^T on the tensor cores (tcgen05, TMEM accumulators),
+   rounded to fp16, with sweep 1 in the GEMM's epilogue: per row and 256-column vocabulary tile
+   the online-softmax state (max, sum of exp, sum of exp * z, first argmax, z[label]); the fp16
+   logits are kept only for labelled rows;
+2. tb_head_merge: logsumexp, entropy = lse - sum(p z), token loss lse - z[label] and whether the
+   first argmax is the label;
+3. tb_head_dlogits (labelled rows): (softmax - onehot) * scale in fp16, in place; then
+   dh = dlogits @ W (cuBLAS).
+Otherwise (hidden not a multiple of 64) the reference's structure runs, in chunks of CHUNK_ROWS
+rows: cuBLAS logits, tb_head_stats_grad (one CTA per row, two sweeps, dlogits in place) and the
+dh GEMM per chunk. The gradient is taken in forward (the head is frozen) and scaled by the loss
+scale in backward.
 """
 
 import math
@@ -39,6 +44,46 @@ def head_stats_grad(logits, targets, grad_scale):
                   _lib.ptr(loss), _lib.ptr(correct), rows, vocab, logits.stride(0),
                   float(grad_scale), _lib.stream_of(logits))
     return entropy, loss, correct
+
+
+# The head runs its logits GEMM on the tensor cores with sweep 1 in the GEMM's epilogue
+# (tb_head_logits_stats) when the shapes allow (hidden a multiple of 64, sm_100); otherwise the
+# reference's structure: cuBLAS logits per CHUNK_ROWS chunk + tb_head_stats_grad.
+USE_TENSOR_CORE_HEAD = True
+VOCAB_TILE = 256
+
+
+def _tensor_core_ok(h, weight):
+    if h.shape[1] % 64 or weight.dtype != torch.float16 or h.dtype != torch.float16:
+        return False
+    if not (h.is_contiguous() and weight.is_contiguous()):
+        return False
+    if h.data_ptr() % 16 or weight.data_ptr() % 16:
+        return False
+    return torch.cuda.get_device_capability(h.device)[0] == 10
+
+
+def _tc_head(h, weight, tgt, entropy, token_loss, correct, grad_sorted, n_labelled, scale,
+             stream):
+    """All rows at once: tensor-core logits + partials, merge, then (labelled rows) dlogits in
+    place over the fp16 logits the GEMM kept and dh = dlogits . W (cuBLAS)."""
+    rows, width = h.shape
+    vocab = weight.shape[0]
+    dev = h.device
+    vt = -(-vocab // VOCAB_TILE)
+    part = torch.empty((rows, vt, 6), dtype=torch.float32, device=dev)
+    pidx = torch.empty((rows, vt), dtype=torch.int64, device=dev)
+    keep = n_labelled if grad_sorted is not None else 0
+    logits = torch.empty((keep, vocab), dtype=torch.float16, device=dev) if keep else None
+    _lib.call("tb_head_logits_stats", _lib.ptr(h), _lib.ptr(weight), _lib.ptr(tgt),
+              _lib.ptr(logits), keep, _lib.ptr(part), _lib.ptr(pidx), rows, vocab, width, stream)
+    lse = torch.empty(rows, dtype=torch.float32, device=dev)
+    _lib.call("tb_head_merge", _lib.ptr(part), _lib.ptr(pidx), _lib.ptr(tgt), rows, 1, vt,
+              _lib.ptr(lse), _lib.ptr(entropy), _lib.ptr(token_loss), _lib.ptr(correct), stream)
+    if keep:
+        _lib.call("tb_head_dlogits", _lib.ptr(logits), _lib.ptr(tgt), _lib.ptr(lse), keep, vocab,
+                  vocab, 0, float(scale), stream)
+        torch.matmul(logits, weight, out=grad_sorted)
 
 
 def _grad_unit(denominator):
@@ -91,7 +136,13 @@ class FusedHeadLoss(torch.autograd.Function):
         grad_sorted = torch.empty((n_labelled, width), dtype=torch.float16, device=dev) \
             if want_grad else None
         stream = _lib.stream_of(hidden)
-        for start in range(0, rows, CHUNK_ROWS):
+        if USE_TENSOR_CORE_HEAD and _tensor_core_ok(h, weight):
+            _tc_head(h, weight, tgt, entropy, token_loss, correct, grad_sorted, n_labelled,
+                     unit / max(denom, 1e-6), stream)
+            rows_loop = range(0)
+        else:
+            rows_loop = range(0, rows, CHUNK_ROWS)
+        for start in rows_loop:
             stop = min(rows, start + CHUNK_ROWS)
             logits = torch.matmul(h[start:stop], weight.t())
             _lib.call("tb_head_stats_grad", _lib.ptr(logits), _lib.ptr(tgt[start:stop]),
