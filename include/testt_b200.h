@@ -183,6 +183,11 @@ int tb_head_logits_stats(const uint16_t *hidden, const uint16_t *weight, const i
                          uint16_t *logits, int64_t logits_rows, float *part, int64_t *part_idx,
                          int64_t rows, int64_t vocab, int64_t hidden_dim, void *stream);
 
+/* Which tensor-core kernel tb_head_logits_stats uses, process-wide: 0 automatic, 1 the 1-SM
+ * kernel (128x256 tiles, tcgen05.mma.cta_group::1), 2 the 2-SM kernel (256x256 tiles per CTA
+ * pair, tcgen05.mma.cta_group::2). Same results either way. No counterpart in the reference. */
+int tb_head_gemm_variant(int32_t variant);
+
 /* tb_head_stats_grad's contract (the same outputs, the same in-place dlogits) with nothing
  * allocated anywhere, for callers that cannot allocate device memory themselves: a host binding
  * that only ever receives buffers owned by someone else (a plain C FFI from another language

@@ -58,20 +58,32 @@ def tc_head(h, w, tg, logits_rows):
     return logits[:logits_rows], lse, ent, loss, cor
 
 
-@pytest.mark.parametrize("rows,vocab,hidden", [(128, 256, 64), (300, 1000, 128),
+@pytest.fixture(params=[1, 2], ids=["1sm", "2sm"])
+def variant(request):
+    """Run a test with the 1-SM and with the 2-SM tensor-core kernel."""
+    from testt_b200 import _lib
+
+    _lib.call("tb_head_gemm_variant", request.param)
+    yield request.param
+    _lib.call("tb_head_gemm_variant", 0)
+
+
+@pytest.mark.parametrize("rows,vocab,hidden", [(128, 256, 64), (256, 256, 64), (300, 1000, 128),
                                                (7, 5003, 192), (129, 512, 1536)])
-def test_tc_head_small_shapes(rows, vocab, hidden):
+def test_tc_head_small_shapes(rows, vocab, hidden, variant):
     h, w, tg = _case(rows, vocab, hidden, rows + vocab)
     logits, lse, ent, loss, cor = tc_head(h, w, tg, rows)
     ref16 = (h.float() @ w.float().t()).half()
     assert_logits(logits, ref16)
     rent, rloss, rcor, _ = ops.head_stats_exact(logits.cpu(), tg.cpu(), 1.0)
     assert_rel(loss, rloss, 1e-4, "loss", floor=0.0)
-    assert_rel(ent, rent, 1e-4, "entropy", floor=0.0)
+    # entropy = lse - sum(p z) cancels for peaked rows (entropy near 0): hold it to rtol 1e-4 of
+    # the entropies' rms there, not of its own tiny value
+    assert_rel(ent, rent, 1e-4, "entropy")
     assert torch.equal(cor.cpu().bool(), rcor)
 
 
-def test_tc_head_config4_against_reference_path():
+def test_tc_head_config4_against_reference_path(variant):
     """Config 4 (2048 rows, vocab 151936, hidden 1536): the fused statistics against cuBLAS
     logits + tb_head_stats_grad, on the same inputs."""
     from oracle import synth

@@ -40,6 +40,7 @@ SIGNATURES = {
     "tb_wait_timeouts": [_I32, _P],
     "tb_head_stats_grad_noalloc": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P],
     "tb_head_logits_stats": [_P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _P],
+    "tb_head_gemm_variant": [_I32],
 }
 
 _lib = None

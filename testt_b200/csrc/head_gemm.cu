@@ -322,6 +322,292 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---- 2-SM version: a CTA pair computes a 256x256 tile with tcgen05.mma.cta_group::2 ------------
+// CTA rank r of the pair loads rows [256*mt + 128 r, +128) of h and rows [256*vt + 128 r, +128) of
+// W into its own shared memory (6 stages of 32 KB); both CTAs' TMA loads complete on the leader's
+// (rank 0) full barrier, which the leader alone arms for 64 KB. The leader's MMA thread issues
+// M256 N256 K16 MMAs: each CTA's TMEM receives its own 128 rows x 256 columns (double-buffered).
+// Commits are multicast to the same barrier in both CTAs (stage empty, accumulator full); each
+// CTA's epilogue drains its own TMEM and arrives on the leader's accumulator-empty barrier
+// (8 arrivals). Operand reuse is 131 FLOP per byte loaded, against 87 for the 1-SM tile.
+constexpr int kStages2 = 6;
+constexpr int kA2Bytes = 128 * kBK * 2;            // 16 KB: this CTA's rows of h
+constexpr int kB2Bytes = 128 * kBK * 2;            // 16 KB: this CTA's half of the W tile
+constexpr int kStage2Bytes = kA2Bytes + kB2Bytes;  // 32 KB
+constexpr uint32_t kPeerMask = 0xFEFFFFFFu;        // shared::cluster address -> rank 0 of the pair
+constexpr uint32_t kIdesc2 =
+    (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+
+struct Smem2 {
+  alignas(1024) uint8_t stage[kStages2][kStage2Bytes];
+  uint64_t full[kStages2], empty[kStages2];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  volatile int error;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, int c0, int c1,
+                                                 uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar) & kPeerMask)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_f16_pair(uint32_t tmem, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+      "l"(a), "l"(b), "r"(kIdesc2), "r"(acc)
+      : "memory");
+}
+
+// arrive on the barrier at this offset in both CTAs of the pair once prior MMAs complete
+__device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\t"
+      "mov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], m;\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_leader(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                   smem_u32(bar) & kPeerMask)
+               : "memory");
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    head_logits_stats_2sm(const __grid_constant__ CUtensorMap map_h,
+                          const __grid_constant__ CUtensorMap map_w, const HeadArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem2 &sm = *reinterpret_cast<Smem2 *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                          ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int64_t pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const int m_tiles2 = (args.rows + 255) / 256;
+  const int64_t tiles = (int64_t)m_tiles2 * args.v_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages2; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&sm.acc_full[a], 1);
+      mbar_init(&sm.acc_empty[a], 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    mbar_init(&sm.mma_done, 1);
+    sm.error = 0;
+    mbar_init_fence();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&sm.tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated in both
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, issued = 0;
+      for (int64_t t = pair; t < tiles && !sm.error; t += pairs) {
+        const int mt = (int)(t % m_tiles2), vt = (int)(t / m_tiles2);
+        for (int kb = 0; kb < args.k_blocks; ++kb) {
+          if (!mbar_wait(&sm.empty[stage], phase ^ 1)) {
+            sm.error = 1;
+            break;
+          }
+          if (leader) mbar_expect_tx(&sm.full[stage], 2 * kStage2Bytes);
+          tma_load_2d_pair(sm.stage[stage], &map_h, kb * kBK, mt * 256 + (int)rank * 128,
+                           &sm.full[stage]);
+          tma_load_2d_pair(sm.stage[stage] + kA2Bytes, &map_w, kb * kBK,
+                           vt * kBN + (int)rank * 128, &sm.full[stage]);
+          ++issued;
+          if (++stage == kStages2) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // this CTA's copies have landed once the stages it filled are freed again (bounded)
+      for (int s = 0; s < kStages2 && s < (int)issued; ++s) {
+        if (stage == 0) {
+          stage = kStages2;
+          phase ^= 1;
+        }
+        --stage;
+        mbar_wait(&sm.empty[stage], phase);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t it = 0;
+      for (int64_t t = pair; t < tiles && !sm.error; t += pairs, ++it) {
+        const int acc = (int)(it & 1);
+        const uint32_t acc_phase = (uint32_t)((it >> 1) & 1);
+        if (!mbar_wait(&sm.acc_empty[acc], acc_phase ^ 1)) {
+          sm.error = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(acc * kBN);
+        for (int kb = 0; kb < args.k_blocks; ++kb) {
+          if (!mbar_wait(&sm.full[stage], phase)) {
+            sm.error = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sm.stage[stage]);
+          const uint32_t b0 = a0 + kA2Bytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            mma_f16_pair(d, smem_desc(a0 + k * 32), smem_desc(b0 + k * 32), (kb | k) != 0);
+          mma_commit_pair(&sm.empty[stage]);
+          if (++stage == kStages2) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        mma_commit_pair(&sm.acc_full[acc]);
+      }
+      asm volatile(
+          "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+              smem_u32(&sm.mma_done))
+          : "memory");
+      mbar_wait(&sm.mma_done, 0);
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row_in_tile = (int)rank * 128 + quarter * 32 + lane;
+    int64_t it = 0;
+    for (int64_t t = pair; t < tiles; t += pairs, ++it) {
+      const int acc = (int)(it & 1);
+      const uint32_t acc_phase = (uint32_t)((it >> 1) & 1);
+      const int ok = mbar_wait(&sm.acc_full[acc], acc_phase) ? 1 : 0;
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) sm.error = 1;
+        break;
+      }
+      tc_fence_after();
+      const int mt = (int)(t % m_tiles2), vt = (int)(t / m_tiles2);
+      const int row = mt * 256 + row_in_tile;
+      const bool live = row < args.rows;
+      const int64_t target = live ? __ldg(args.targets + row) : -1;
+      const int col0 = vt * kBN;
+      float m = -CUDART_INF_F, s = 0.f, dz = 0.f, best = -CUDART_INF_F, zt = 0.f;
+      int64_t best_idx = 0x7fffffffffffffffLL;
+      bool found = false;
+      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kBN);
+#pragma unroll 1
+      for (int c = 0; c < kBN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + (uint32_t)c, r);
+        float z[32];
+        uint32_t h16[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const __half2 hh = __floats2half2_rn(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+          const float2 zz = __half22float2(hh);
+          z[i] = zz.x;
+          z[i + 1] = zz.y;
+          h16[i / 2] = *reinterpret_cast<const uint32_t *>(&hh);
+        }
+        const int cbase = col0 + c;
+        const int nvalid = min(32, args.vocab - cbase);
+        if (nvalid <= 0) continue;
+        const bool keep = live && args.logits != nullptr && row < args.logits_rows;
+        if (keep && nvalid == 32 && (args.vocab & 7) == 0) {
+          uint4 *dst = reinterpret_cast<uint4 *>(args.logits + (int64_t)row * args.vocab + cbase);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(h16[4 * q], h16[4 * q + 1], h16[4 * q + 2], h16[4 * q + 3]);
+        } else if (keep) {
+          for (int i = 0; i < nvalid; ++i)
+            args.logits[(int64_t)row * args.vocab + cbase + i] =
+                (uint16_t)(h16[i / 2] >> (16 * (i & 1)));
+        }
+        float lm = -CUDART_INF_F;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < nvalid) lm = fmaxf(lm, z[i]);
+        if (lm > m) {
+          const float sc = __expf(m - lm);
+          s *= sc;
+          dz *= sc;
+          m = lm;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (i < nvalid) {
+            const float e = __expf(z[i] - m);
+            s += e;
+            dz += e * z[i];
+            if (z[i] > best) {
+              best = z[i];
+              best_idx = cbase + i;
+            }
+            if (cbase + i == target) {
+              zt = z[i];
+              found = true;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_leader(&sm.acc_empty[acc]);
+      if (live) {
+        const int64_t at = (int64_t)row * args.v_tiles + vt;
+        float *out = args.part + at * kPartFields;
+        out[0] = m;
+        out[1] = s;
+        out[2] = dz;
+        out[3] = best;
+        out[4] = found ? zt : 0.f;
+        out[5] = found ? 1.f : 0.f;
+        args.part_idx[at] = best_idx;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA leaves while its pair may still reach its shared memory
+  if (threadIdx.x == 0 && sm.error) atomicAdd(&g_wait_timeouts, 1u);
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
 // ---- host: TMA descriptors through the driver entry point (no libcuda link) ---------------
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -357,6 +643,10 @@ int make_map(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, int
   if (r != CUDA_SUCCESS) return set_error(TB_EINVAL, "head: tensor map encode failed (%d)", (int)r);
   return TB_OK;
 }
+
+// 0: automatic, 1: the 1-SM kernel, 2: the 2-SM kernel (process-wide; tb_head_gemm_variant)
+int g_head_variant = 0;
+constexpr bool kAutoTwoSm = false;
 
 }  // namespace
 
@@ -402,6 +692,32 @@ extern "C" int tb_head_logits_stats(const uint16_t *hidden, const uint16_t *weig
   a.k_blocks = (int)(hidden_dim / kBK);
   a.m_tiles = (int)((rows + kBM - 1) / kBM);
   a.v_tiles = (int)((vocab + kBN - 1) / kBN);
+  const int variant = g_head_variant;
+  const bool two_sm = variant == 2 || (variant == 0 && kAutoTwoSm && rows > kBM);
+  if (two_sm) {
+    CUtensorMap map_h2, map_w2;  // boxes of 128 rows for both operands
+    rc = make_map(&map_h2, hidden, rows, hidden_dim, 128);
+    if (rc == TB_OK) rc = make_map(&map_w2, weight, vocab, hidden_dim, 128);
+    if (rc != TB_OK) return rc;
+    const size_t smem2 = sizeof(Smem2) + 1024;
+    if (cudaFuncSetAttribute(head_logits_stats_2sm, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem2) != cudaSuccess)
+      return check_launch("head_logits_stats_2sm attribute");
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem2;
+    cfg.stream = as_stream(stream);
+    cfg.gridDim = dim3(2 * (unsigned)sm_count());
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, head_logits_stats_2sm, &cfg) != cudaSuccess ||
+        clusters < 1)
+      return check_launch("head_logits_stats_2sm occupancy");
+    const int64_t tiles2 = (int64_t)((rows + 255) / 256) * a.v_tiles;
+    const int64_t pairs = tiles2 < clusters ? tiles2 : clusters;
+    head_logits_stats_2sm<<<(unsigned)(2 * pairs), kThreads, smem2, as_stream(stream)>>>(
+        map_h2, map_w2, a);
+    return check_launch("head_logits_stats_2sm");
+  }
   const size_t smem = sizeof(Smem) + 1024;
   if (cudaFuncSetAttribute(head_logits_stats, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem) != cudaSuccess)
@@ -410,4 +726,11 @@ extern "C" int tb_head_logits_stats(const uint16_t *hidden, const uint16_t *weig
   const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
   head_logits_stats<<<grid, kThreads, smem, as_stream(stream)>>>(map_h, map_w, a);
   return check_launch("head_logits_stats");
+}
+
+extern "C" int tb_head_gemm_variant(int32_t variant) {
+  if (variant < 0 || variant > 2)
+    return set_error(TB_EINVAL, "head_gemm_variant: %d (0 auto, 1 one-SM, 2 two-SM)", variant);
+  g_head_variant = variant;
+  return TB_OK;
 }
