@@ -83,6 +83,38 @@ def test_tc_head_small_shapes(rows, vocab, hidden, variant):
     assert torch.equal(cor.cpu().bool(), rcor)
 
 
+def test_tc_head_first_argmax_ties(variant):
+    """Integer logits (entries of h and W in {-1, 0, 1}: exact sums) tie often; the hit must be
+    the reference's first argmax: targets on the first maximum, on a later tied maximum, on a
+    maximum in another vocabulary tile and at random."""
+    from testt_b200 import _lib  # noqa: F401
+
+    rows, vocab, hidden = 384, 1000, 64
+    g = torch.Generator().manual_seed(7)
+    h = torch.randint(-1, 2, (rows, hidden), generator=g).half()
+    w = torch.randint(-1, 2, (vocab, hidden), generator=g).half()
+    z = h.float() @ w.float().t()
+    tg = torch.randint(0, vocab, (rows,), generator=g)
+    for r in range(rows):
+        ties = torch.nonzero(z[r] == z[r].max()).squeeze(1)
+        kind = r % 4
+        if kind == 0:
+            tg[r] = ties[0]
+        elif kind == 1:
+            tg[r] = ties[-1]
+        elif kind == 2:
+            tg[r] = ties[len(ties) // 2]
+    tg[5::17] = -100
+    logits, lse, ent, loss, cor = tc_head(h.to(DEV), w.to(DEV), tg.to(DEV), rows)
+    assert torch.equal(logits.cpu(), z.half())
+    rent, rloss, rcor, _ = ops.head_stats_exact(logits.cpu(), tg, 1.0)
+    assert torch.equal(cor.cpu().bool(), rcor)
+    assert int(rcor.sum()) > rows // 4
+    # integer logits make lse - z[target] cancel to ~1e-3 on rows whose target is a clear
+    # maximum (fp32 lse near 30 carries ulps of 4e-6): rtol 1e-4 of the losses' rms there
+    assert_rel(loss, rloss, 1e-4, "loss")
+
+
 def test_tc_head_config4_against_reference_path(variant):
     """Config 4 (2048 rows, vocab 151936, hidden 1536): the fused statistics against cuBLAS
     logits + tb_head_stats_grad, on the same inputs."""

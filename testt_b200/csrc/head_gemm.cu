@@ -103,6 +103,84 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+constexpr float kLog2e = 1.4426950408889634f;
+
+// 2^x on the MUFU (PTX ex2.approx); e^x is computed as 2^(x log2 e)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// One row's online state over one 256-column vocabulary tile, built 32 columns at a time.
+struct RowTile {
+  float m, s, dz;  // running max; sum of e = exp(z - m); sum of e z
+  float zt, pm;    // the target's logit; max of the target chunk's columns before the target
+  int fm_chunk;    // column offset of the first chunk that reached the running max
+  bool found;      // the target lies in this tile
+  bool first;      // ... and is the tile's first maximum
+};
+
+// Folds 32 fp16 logits (packed in pairs, column c.. of the tile) into the state. The chunk max
+// is taken on the packed halves; the argmax is not tracked per element: only whether the
+// target is the tile's first maximum matters (tb_head_merge compares the winning index with
+// the target), which needs the target's chunk alone (t_off = target - tile column 0, or
+// negative when the target is elsewhere). kFull false: only the first nvalid columns exist.
+template <bool kFull>
+__device__ __forceinline__ void fold_chunk(RowTile &st, uint32_t (&h)[16], int c, int nvalid,
+                                           int t_off) {
+  if (!kFull) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {  // columns past the vocabulary: -inf (no max, e = 0)
+      if (2 * j >= nvalid) h[j] = (h[j] & 0xffff0000u) | 0xfc00u;
+      if (2 * j + 1 >= nvalid) h[j] = (h[j] & 0x0000ffffu) | 0xfc000000u;
+    }
+  }
+  __half2 v[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    v[j] = __hmax2(*reinterpret_cast<const __half2 *>(&h[j]),
+                   *reinterpret_cast<const __half2 *>(&h[j + 8]));
+#pragma unroll
+  for (int w = 4; w > 0; w >>= 1)
+#pragma unroll
+    for (int j = 0; j < w; ++j) v[j] = __hmax2(v[j], v[j + w]);
+  const float lm = fmaxf(__low2float(v[0]), __high2float(v[0]));
+  if (lm > st.m) {
+    const float sc = ex2_approx((st.m - lm) * kLog2e);  // 0 while m is -inf
+    st.s *= sc;
+    st.dz *= sc;
+    st.m = lm;
+    st.fm_chunk = c;
+  }
+  const float ml = st.m * kLog2e;
+  float s0 = 0.f, s1 = 0.f, d0 = 0.f, d1 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float2 z = __half22float2(*reinterpret_cast<const __half2 *>(&h[j]));
+    const float e0 = ex2_approx(fmaf(z.x, kLog2e, -ml));
+    const float e1 = ex2_approx(fmaf(z.y, kLog2e, -ml));
+    s0 += e0;
+    s1 += e1;
+    d0 = fmaf(e0, kFull || 2 * j < nvalid ? z.x : 0.f, d0);
+    d1 = fmaf(e1, kFull || 2 * j + 1 < nvalid ? z.y : 0.f, d1);
+  }
+  st.s += s0 + s1;
+  st.dz += d0 + d1;
+  const int o = t_off - c;
+  if ((unsigned)o < 32u) {  // the target's chunk (one per labelled row)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float2 z = __half22float2(*reinterpret_cast<const __half2 *>(&h[j]));
+      if (2 * j < o) st.pm = fmaxf(st.pm, z.x);
+      if (2 * j == o) st.zt = z.x;
+      if (2 * j + 1 < o) st.pm = fmaxf(st.pm, z.y);
+      if (2 * j + 1 == o) st.zt = z.y;
+    }
+    st.found = true;
+  }
+}
+
 struct HeadArgs {
   const int64_t *targets;
   uint16_t *logits;  // optional fp16 [logits_rows, vocab] output
@@ -110,6 +188,68 @@ struct HeadArgs {
   int64_t *part_idx; // [rows, n_vtiles]
   int rows, logits_rows, vocab, k_blocks, m_tiles, v_tiles;
 };
+
+// The epilogue of one tile for one row (one thread): reads the row's 256 fp32 accumulator
+// columns from TMEM (taddr: this warp's lane quarter and the accumulator), rounds them to fp16
+// as the reference's fp16 GEMM output, optionally stores them (kept rows) and returns the
+// tile's state. Every thread of the warp calls it (tcgen05.ld is warp-wide).
+__device__ __forceinline__ RowTile tile_rows(const HeadArgs &args, uint32_t taddr, int row,
+                                             bool live, int64_t target, int col0) {
+  RowTile st{-CUDART_INF_F, 0.f, 0.f, 0.f, -CUDART_INF_F, -1, false, false};
+  const int64_t dt = target - col0;
+  const int t_off = (dt >= 0 && dt < kBN) ? (int)dt : -1024;
+  const bool keep = live && args.logits != nullptr && row < args.logits_rows;
+#pragma unroll 1
+  for (int c = 0; c < kBN; c += 32) {
+    const int nvalid = min(32, args.vocab - (col0 + c));
+    if (nvalid <= 0) break;  // warp-uniform: the rest of the tile is past the vocabulary
+    uint32_t r[32];
+    tmem_ld32(taddr + (uint32_t)c, r);
+    uint32_t h[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const __half2 hh = __floats2half2_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+      h[j] = *reinterpret_cast<const uint32_t *>(&hh);
+    }
+    if (keep) {
+      uint16_t *dst = args.logits + (int64_t)row * args.vocab + col0 + c;
+      if (nvalid == 32 && (args.vocab & 7) == 0) {
+        uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          d4[q] = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < nvalid) dst[i] = (uint16_t)(h[i / 2] >> (16 * (i & 1)));
+      }
+    }
+    if (nvalid == 32)
+      fold_chunk<true>(st, h, c, 32, t_off);
+    else
+      fold_chunk<false>(st, h, c, nvalid, t_off);
+  }
+  // the target is the tile's first maximum: it reaches the max, its chunk is the first chunk
+  // that does, and no column of that chunk before it does
+  st.first = st.found && st.zt == st.m && st.fm_chunk == (t_off & ~31) && st.pm < st.m;
+  return st;
+}
+
+// part[row][vt] = (m, s, dz, m, zt, found) and an index that tb_head_merge orders tiles by and
+// that equals the target exactly when the target is this tile's first maximum (any other
+// column of the tile otherwise)
+__device__ __forceinline__ void store_partial(const HeadArgs &args, int row, int vt, int col0,
+                                              int64_t target, const RowTile &st) {
+  const int64_t at = (int64_t)row * args.v_tiles + vt;
+  float *out = args.part + at * kPartFields;
+  out[0] = st.m;
+  out[1] = st.s;
+  out[2] = st.dz;
+  out[3] = st.m;
+  out[4] = st.found ? st.zt : 0.f;
+  out[5] = st.found ? 1.f : 0.f;
+  args.part_idx[at] = st.first ? target : (int64_t)col0 + (target == col0 ? 1 : 0);
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
     head_logits_stats(const __grid_constant__ CUtensorMap map_h,
@@ -234,80 +374,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool live = row < args.rows;
       const int64_t target = live ? __ldg(args.targets + row) : -1;
       const int col0 = vt * kBN;
-      float m = -CUDART_INF_F, s = 0.f, dz = 0.f, best = -CUDART_INF_F, zt = 0.f;
-      int64_t best_idx = 0x7fffffffffffffffLL;
-      bool found = false;
       const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kBN);
-#pragma unroll 1
-      for (int c = 0; c < kBN; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(taddr + (uint32_t)c, r);
-        float z[32];
-        uint32_t h16[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const __half2 hh = __floats2half2_rn(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-          const float2 zz = __half22float2(hh);
-          z[i] = zz.x;
-          z[i + 1] = zz.y;
-          h16[i / 2] = *reinterpret_cast<const uint32_t *>(&hh);
-        }
-        const int cbase = col0 + c;
-        const int nvalid = min(32, args.vocab - cbase);
-        if (nvalid <= 0) continue;
-        const bool keep = live && args.logits != nullptr && row < args.logits_rows;
-        if (keep && nvalid == 32 && (args.vocab & 7) == 0) {
-          uint4 *dst = reinterpret_cast<uint4 *>(args.logits + (int64_t)row * args.vocab + cbase);
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            dst[q] = make_uint4(h16[4 * q], h16[4 * q + 1], h16[4 * q + 2], h16[4 * q + 3]);
-        } else if (keep) {
-          for (int i = 0; i < nvalid; ++i)
-            args.logits[(int64_t)row * args.vocab + cbase + i] =
-                (uint16_t)(h16[i / 2] >> (16 * (i & 1)));
-        }
-        float lm = -CUDART_INF_F;
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < nvalid) lm = fmaxf(lm, z[i]);
-        if (lm > m) {
-          const float sc = __expf(m - lm);
-          s *= sc;
-          dz *= sc;
-          m = lm;
-        }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (i < nvalid) {
-            const float e = __expf(z[i] - m);
-            s += e;
-            dz += e * z[i];
-            if (z[i] > best) {
-              best = z[i];
-              best_idx = cbase + i;
-            }
-            if (cbase + i == target) {
-              zt = z[i];
-              found = true;
-            }
-          }
-        }
-      }
+      const RowTile st = tile_rows(args, taddr, row, live, target, col0);
       // the accumulator may be overwritten once every epilogue warp has read it
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
-      if (live) {
-        const int64_t at = (int64_t)row * args.v_tiles + vt;
-        float *out = args.part + at * kPartFields;
-        out[0] = m;
-        out[1] = s;
-        out[2] = dz;
-        out[3] = best;
-        out[4] = found ? zt : 0.f;
-        out[5] = found ? 1.f : 0.f;
-        args.part_idx[at] = best_idx;
-      }
+      if (live) store_partial(args, row, vt, col0, target, st);
     }
   }
 
@@ -520,79 +593,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const bool live = row < args.rows;
       const int64_t target = live ? __ldg(args.targets + row) : -1;
       const int col0 = vt * kBN;
-      float m = -CUDART_INF_F, s = 0.f, dz = 0.f, best = -CUDART_INF_F, zt = 0.f;
-      int64_t best_idx = 0x7fffffffffffffffLL;
-      bool found = false;
       const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kBN);
-#pragma unroll 1
-      for (int c = 0; c < kBN; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(taddr + (uint32_t)c, r);
-        float z[32];
-        uint32_t h16[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const __half2 hh = __floats2half2_rn(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-          const float2 zz = __half22float2(hh);
-          z[i] = zz.x;
-          z[i + 1] = zz.y;
-          h16[i / 2] = *reinterpret_cast<const uint32_t *>(&hh);
-        }
-        const int cbase = col0 + c;
-        const int nvalid = min(32, args.vocab - cbase);
-        if (nvalid <= 0) continue;
-        const bool keep = live && args.logits != nullptr && row < args.logits_rows;
-        if (keep && nvalid == 32 && (args.vocab & 7) == 0) {
-          uint4 *dst = reinterpret_cast<uint4 *>(args.logits + (int64_t)row * args.vocab + cbase);
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            dst[q] = make_uint4(h16[4 * q], h16[4 * q + 1], h16[4 * q + 2], h16[4 * q + 3]);
-        } else if (keep) {
-          for (int i = 0; i < nvalid; ++i)
-            args.logits[(int64_t)row * args.vocab + cbase + i] =
-                (uint16_t)(h16[i / 2] >> (16 * (i & 1)));
-        }
-        float lm = -CUDART_INF_F;
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < nvalid) lm = fmaxf(lm, z[i]);
-        if (lm > m) {
-          const float sc = __expf(m - lm);
-          s *= sc;
-          dz *= sc;
-          m = lm;
-        }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (i < nvalid) {
-            const float e = __expf(z[i] - m);
-            s += e;
-            dz += e * z[i];
-            if (z[i] > best) {
-              best = z[i];
-              best_idx = cbase + i;
-            }
-            if (cbase + i == target) {
-              zt = z[i];
-              found = true;
-            }
-          }
-        }
-      }
+      const RowTile st = tile_rows(args, taddr, row, live, target, col0);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_leader(&sm.acc_empty[acc]);
-      if (live) {
-        const int64_t at = (int64_t)row * args.v_tiles + vt;
-        float *out = args.part + at * kPartFields;
-        out[0] = m;
-        out[1] = s;
-        out[2] = dz;
-        out[3] = best;
-        out[4] = found ? zt : 0.f;
-        out[5] = found ? 1.f : 0.f;
-        args.part_idx[at] = best_idx;
-      }
+      if (live) store_partial(args, row, vt, col0, target, st);
     }
   }
 
