@@ -208,6 +208,7 @@ class HotPath:
     def __init__(self, model, lengths, seq, device):
         from oracle import synth
         from testt_b200 import _lib, nf4
+        from testt_b200.model import USE_VARLEN_ATTENTION as varlen
         from testt_b200.model import model_plan
 
         self.lib = _lib
@@ -322,23 +323,34 @@ class HotPath:
             add("rmsnorm_bwd", e * 16 + 4 * h + 4 * m, "tb_add_rmsnorm_bwd", _lib.ptr(s2),
                 _lib.ptr(r2), _lib.ptr(w_norm), _lib.ptr(dy2), None, None, _lib.ptr(ds2),
                 _lib.ptr(dx2), _lib.ptr(dd2), m, h)
-            # QKV pack + RoPE (LoRA outputs fp16, as under autocast)
+            # QKV pack + RoPE (LoRA outputs fp16, as under autocast), token-major as the step
+            # runs it (model.USE_VARLEN_ATTENTION), else into the padded layout
             qkv = rnd((m, width), f16)
             lq, lv = rnd((m, nh * d), f16, 1e-2), rnd((m, nkv * d), f16, 1e-2)
-            q = torch.empty((b, nh, seq, d), dtype=f16, device=dev)
-            k = torch.empty((b, nkv, seq, d), dtype=f16, device=dev)
-            v = torch.empty((b, nkv, seq, d), dtype=f16, device=dev)
+            if varlen:
+                shapes = ((m, nh, d), (m, nkv, d), (m, nkv, d))
+            else:
+                shapes = ((b, nh, seq, d), (b, nkv, seq, d), (b, nkv, seq, d))
+            q, k, v = (torch.empty(sh, dtype=f16, device=dev) for sh in shapes)
             self.keep += [qkv, lq, lv, q, k, v]
-            nb = m * (width * 2 + (nh + nkv) * d * 2) + p * width * 2 + 2 * seq * d * 4 + p * 4
-            add("rope_fwd", nb, "tb_rope_pack_fwd", _lib.ptr(qkv), _lib.ptr(lq), _lib.ptr(lv), 0,
-                _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(pos), _lib.ptr(slot), _lib.ptr(q),
-                _lib.ptr(k), _lib.ptr(v), m, b, seq, nh, nkv, d)
+            if varlen:
+                nb = m * (width * 2 + (nh + nkv) * d * 2 + width * 2 + 8) + 2 * seq * d * 4
+                add("rope_fwd", nb, "tb_rope_tokens_fwd", _lib.ptr(qkv), _lib.ptr(lq),
+                    _lib.ptr(lv), 0, _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(pos), _lib.ptr(q),
+                    _lib.ptr(k), _lib.ptr(v), m, b, seq, nh, nkv, d)
+            else:
+                nb = m * (width * 2 + (nh + nkv) * d * 2) + p * width * 2 + 2 * seq * d * 4 \
+                    + p * 4
+                add("rope_fwd", nb, "tb_rope_pack_fwd", _lib.ptr(qkv), _lib.ptr(lq),
+                    _lib.ptr(lv), 0, _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(pos),
+                    _lib.ptr(slot), _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), m, b, seq, nh, nkv, d)
             dq, dk, dv = rnd(q.shape, f16), rnd(k.shape, f16), rnd(v.shape, f16)
             dqkv = torch.empty((m, width), dtype=f16, device=dev)
             self.keep += [dq, dk, dv, dqkv]
             nb = m * width * 2 * 2 + m * 8 + 2 * seq * d * 4
-            add("rope_bwd", nb, "tb_rope_pack_bwd", _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv),
-                _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(pos), _lib.ptr(dqkv), m, b, seq, nh, nkv, d)
+            add("rope_bwd", nb, "tb_rope_tokens_bwd" if varlen else "tb_rope_pack_bwd",
+                _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv), _lib.ptr(cos), _lib.ptr(sin),
+                _lib.ptr(pos), _lib.ptr(dqkv), m, b, seq, nh, nkv, d)
             # SwiGLU
             gu = rnd((m, 2 * inter), f16)
             act = torch.empty((m, inter), dtype=f16, device=dev)
@@ -624,10 +636,12 @@ def ours_arm(args, rank, world, local):
     h2d = sum(t.numel() * t.element_size() for t in host)
 
     # eager step (reported beside the captured one)
-    for _ in range(args.warmup):
-        step(ids, mask, labels)
-    torch.cuda.synchronize()
-    eager_ms = time_region(lambda: step(ids, mask, labels), args.steps, world, dev)
+    eager_ms = None
+    if not args.step_only:
+        for _ in range(args.warmup):
+            step(ids, mask, labels)
+        torch.cuda.synchronize()
+        eager_ms = time_region(lambda: step(ids, mask, labels), args.steps, world, dev)
 
     # value: the captured step replayed on inputs already on the device
     graphed(ids, mask, labels, host_mask=host[1], host_labels=host[2])  # capture
@@ -646,6 +660,16 @@ def ours_arm(args, rank, world, local):
         ms = time_region(timed_step, args.steps, world, dev)
     clocks = clk.summary()
     value = tokens * world * args.steps / (ms / 1e3)
+    if args.step_only:  # the captured step alone (for launch lists): no other measurement
+        graphed.entries.clear()
+        del graphed
+        torch.cuda.synchronize()
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": value, "unit": "tokens/s",
+                              "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                              "ms_per_step": ms / args.steps, "step_only": True,
+                              "clocks": clocks}), flush=True)
+        return
 
     # e2e: the public call with a host batch every step (plan from the host copy, H2D copies
     # into the graph's buffers, replay) and the loss and statistics read back to the host
@@ -749,6 +773,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    ap.add_argument("--step-only", action="store_true",
+                    help="time the captured training step only (for ncu launch lists)")
     ap.add_argument("--kernel", default=None,
                     help="time one kernel at its configuration instead (nf4, nf4_nested, "
                          "rmsnorm_fwd, rmsnorm_bwd, rope_fwd, rope_bwd, swiglu_fwd, swiglu_bwd, "

@@ -118,6 +118,24 @@ int tb_rope_pack_bwd(const uint16_t *dq, const uint16_t *dk, const uint16_t *dv,
                      int64_t batch, int64_t seq, int32_t n_heads, int32_t n_kv, int32_t head_dim,
                      void *stream);
 
+/* The same QKV pack with token-major outputs: q fp16 [rows, nh, d], k and v [rows, nkv, d], the
+ * packed layout of variable-length attention (cumulative sequence offsets instead of padding);
+ * pos_idx still gives each token's position b*seq + t (its rotary row t). No padded slot is
+ * written. No counterpart in the reference, whose attention runs on the padded layout
+ * (solution/model.py:242-246). */
+int tb_rope_tokens_fwd(const uint16_t *qkv, const void *lora_q, const void *lora_v,
+                       int32_t lora_is_fp32, const float *cos, const float *sin,
+                       const int64_t *pos_idx, uint16_t *q, uint16_t *k, uint16_t *v,
+                       int64_t rows, int64_t batch, int64_t seq, int32_t n_heads, int32_t n_kv,
+                       int32_t head_dim, void *stream);
+
+/* Backward of tb_rope_tokens_fwd: dqkv fp16 [rows, (nh + 2 nkv) * d] from token-major dq, dk,
+ * dv (each nullable = zero gradient). */
+int tb_rope_tokens_bwd(const uint16_t *dq, const uint16_t *dk, const uint16_t *dv,
+                       const float *cos, const float *sin, const int64_t *pos_idx,
+                       uint16_t *dqkv, int64_t rows, int64_t batch, int64_t seq, int32_t n_heads,
+                       int32_t n_kv, int32_t head_dim, void *stream);
+
 /* slot_tok[b*seq+t] = token index at that padded slot, -1 for padding (the inverse of pos_idx).
  * Helper for tb_rope_pack_fwd; a memset plus one scatter kernel. */
 int tb_slot_index(const int64_t *pos_idx, int64_t rows, int64_t slots, int32_t *slot_tok,

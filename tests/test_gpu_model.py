@@ -81,12 +81,20 @@ def run(model, fused):
     return float(out.loss), grads, entropy, accuracy, rows
 
 
-def test_fused_step_matches_unpatched_model(lora_model):
-    from testt_b200 import _lib
+@pytest.mark.parametrize("varlen", [True, False], ids=["varlen_attention", "padded_attention"])
+def test_fused_step_matches_unpatched_model(lora_model, varlen):
+    """Both attention layouts of the fused path: token-major variable-length attention (the
+    default) and the reference's padded layout with the causal + padding mask."""
+    from testt_b200 import _lib, model
 
     ref = run(lora_model, fused=False)
     _lib.reset_call_count()
-    got = run(lora_model, fused=True)
+    saved = model.USE_VARLEN_ATTENTION
+    model.USE_VARLEN_ATTENTION = varlen and saved
+    try:
+        got = run(lora_model, fused=True)
+    finally:
+        model.USE_VARLEN_ATTENTION = saved
     assert _lib.call_count() > 0, "the fused step must run the native kernels"
     assert abs(got[0] - ref[0]) / ref[0] < 2e-3, (got[0], ref[0])
     assert set(got[1]) == set(ref[1]) and ref[1]

@@ -304,6 +304,73 @@ def test_rope_unsorted_positions_and_token_grid():
         assert_ulp(a, b, 1, "token grid")
 
 
+def _to_tokens(padded, pos, seq):
+    """[batch, heads, seq, d] -> token-major [rows, heads, d] at the padded positions pos."""
+    b, t = pos // seq, pos % seq
+    return padded[b, :, t, :]
+
+
+@pytest.mark.parametrize("lora", ["fp32", "fp16", "none"])
+def test_rope_tokens_config3_full_size(lora):
+    """The token-major pack (variable-length attention's layout): the oracle's padded outputs
+    at each token's slot, within 1 ulp, and the backward from token-major gradients."""
+    from testt_b200 import _lib
+    from testt_b200.rope import RopeTokens
+
+    c = synth.config3("cpu")
+    dims = (c["batch"], c["seq"], synth.N_HEADS, synth.N_KV, synth.HEAD_DIM)
+    lq = None if lora == "none" else c["lora_q"].to(getattr(torch, {"fp32": "float32",
+                                                                     "fp16": "float16"}[lora]))
+    lv = None if lora == "none" else c["lora_v"].to(lq.dtype)
+    dev = lambda x: None if x is None else x.to(DEV)  # noqa: E731
+    q, k, v = RopeTokens.apply(dev(c["qkv"]), dev(lq), dev(lv), dev(c["cos"]), dev(c["sin"]),
+                               dev(c["pos_idx"]), *dims)
+    rq, rk, rv = ops.rope_pack_fwd(c["qkv"], lq, lv, c["cos"], c["sin"], c["pos_idx"], *dims)
+    pos = c["pos_idx"]
+    for name, got, ref in (("q", q, rq), ("k", k, rk), ("v", v, rv)):
+        assert got.shape == (c["rows"], ref.shape[1], synth.HEAD_DIM)
+        assert_ulp(got, _to_tokens(ref, pos, c["seq"]), 1, name)
+    g = {k: dev(c[k]) for k in ("cos", "sin", "pos_idx", "qkv")}
+    grads = [dev(_to_tokens(c[n], pos, c["seq"]).contiguous()) for n in ("dq", "dk", "dv")]
+    dqkv = torch.empty_like(g["qkv"])
+    _lib.call("tb_rope_tokens_bwd", *[_lib.ptr(x) for x in grads], _lib.ptr(g["cos"]),
+              _lib.ptr(g["sin"]), _lib.ptr(g["pos_idx"]), _lib.ptr(dqkv), c["rows"], c["batch"],
+              c["seq"], synth.N_HEADS, synth.N_KV, synth.HEAD_DIM, _lib.stream_of(dqkv))
+    torch.cuda.synchronize()
+    ref = ops.rope_pack_bwd(c["dq"], c["dk"], c["dv"], c["cos"], c["sin"], c["pos_idx"], *dims)
+    assert_ulp(dqkv, ref, 1, "dqkv")
+
+
+@pytest.mark.parametrize("d", [64, 36])
+def test_rope_tokens_autograd_and_element_path(d):
+    """Token-major pack through autograd (LoRA grads are views of dqkv), with unsorted
+    positions; d = 36 (half 18) takes the element-granular kernels."""
+    from testt_b200.rope import rope_tokens
+
+    gen = torch.Generator().manual_seed(5)
+    batch, seq, nh, nkv = 3, 13, 4, 2
+    pos = torch.randperm(batch * seq, generator=gen)[:19]
+    rows = pos.numel()
+    qkv = torch.randn(rows, (nh + 2 * nkv) * d, generator=gen).half()
+    lq = torch.randn(rows, nh * d, generator=gen).half()
+    lv = torch.randn(rows, nkv * d, generator=gen).half()
+    cos, sin = ops.rope_tables(seq, d, 1e6)
+    ref = ops.rope_pack_fwd(qkv, lq, lv, cos, sin, pos, batch, seq, nh, nkv, d)
+    ins = [x.to(DEV).requires_grad_(x.dtype == torch.float16) for x in (qkv, lq, lv)]
+    got = rope_tokens(*ins, cos.to(DEV), sin.to(DEV), pos.to(DEV), batch, seq, nh, nkv, d)
+    for a, b, name in zip(got, ref, "qkv"):
+        assert_ulp(a, _to_tokens(b, pos, seq), 1, name)
+    gq = torch.randn(batch, nh, seq, d, generator=gen).half()
+    gk = torch.randn(batch, nkv, seq, d, generator=gen).half()
+    gv = torch.randn(batch, nkv, seq, d, generator=gen).half()
+    torch.autograd.backward(list(got), [_to_tokens(x, pos, seq).contiguous().to(DEV)
+                                        for x in (gq, gk, gv)])
+    dref = ops.rope_pack_bwd(gq, gk, gv, cos, sin, pos, batch, seq, nh, nkv, d)
+    assert_ulp(ins[0].grad, dref, 1, "dqkv")
+    assert_ulp(ins[1].grad, dref[:, :nh * d], 1, "dlq")
+    assert_ulp(ins[2].grad, dref[:, (nh + nkv) * d:], 1, "dlv")
+
+
 # ---- vocab head --------------------------------------------------------------------------------
 
 def test_head_stats_golden():

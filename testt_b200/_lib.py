@@ -30,6 +30,9 @@ SIGNATURES = {
     "tb_rope_pack_fwd": [_P, _P, _P, _I32, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32,
                          _I32, _I32, _P],
     "tb_rope_pack_bwd": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _P],
+    "tb_rope_tokens_fwd": [_P, _P, _P, _I32, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32,
+                           _I32, _I32, _P],
+    "tb_rope_tokens_bwd": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _P],
     "tb_slot_index": [_P, _I64, _I64, _P, _P],
     "tb_swiglu_fwd": [_P, _P, _I64, _I64, _P],
     "tb_swiglu_bwd_inplace": [_P, _P, _I64, _I64, _P],

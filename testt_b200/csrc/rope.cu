@@ -10,6 +10,10 @@
 // map (slot_tok) the forward kernel covers every padded slot and writes the zero rows of padding
 // itself, which removes the three zero-fills of the outputs the reference does before its launch
 // (solution/rope.py:141-143).
+//
+// Token-major mode (tb_rope_tokens_fwd / _bwd, no counterpart in the reference): the same
+// arithmetic with q, k, v laid out [rows, heads, d], the packed layout of variable-length
+// attention, so no padded slot is written or read.
 #include "common.cuh"
 
 namespace tb {
@@ -36,8 +40,16 @@ __device__ __forceinline__ void zero8(float (&f)[8]) {
   for (int k = 0; k < 8; ++k) f[k] = 0.f;
 }
 
+// Element offset of head row h (of `heads`) of token tok at slot (b, t): the padded
+// [batch, heads, seq, d] layout, or token-major [rows, heads, d].
+__device__ __forceinline__ int64_t head_row(bool tokens, int64_t tok, int64_t b, int64_t t,
+                                            int heads, int h, int64_t seq, int D) {
+  return tokens ? (tok * heads + h) * (int64_t)D : ((b * heads + h) * seq + t) * (int64_t)D;
+}
+
 // kSlots: one CTA per padded slot, tokens found through slot_tok, padding rows zero-filled.
-template <bool kSlots, bool kLoraFp32>
+// kTokens (with kSlots false): token-major outputs.
+template <bool kSlots, bool kLoraFp32, bool kTokens>
 __global__ void __launch_bounds__(kMaxThreads)
     rope_fwd_vec(const uint16_t *__restrict__ qkv, const void *__restrict__ lq,
                  const void *__restrict__ lv, const float *__restrict__ cosv,
@@ -78,11 +90,11 @@ __global__ void __launch_bounds__(kMaxThreads)
     float x1[8], x2[8], o1[8], o2[8];
     uint16_t *dst;
     if (hr < dm.nh) {
-      dst = q + ((b * dm.nh + hr) * dm.seq + t) * D;
+      dst = q + head_row(kTokens, tok, b, t, dm.nh, hr, dm.seq, D);
     } else if (hr < dm.nh + dm.nkv) {
-      dst = k + ((b * dm.nkv + (hr - dm.nh)) * dm.seq + t) * D;
+      dst = k + head_row(kTokens, tok, b, t, dm.nkv, hr - dm.nh, dm.seq, D);
     } else {
-      dst = v + ((b * dm.nkv + (hr - dm.nh - dm.nkv)) * dm.seq + t) * D;
+      dst = v + head_row(kTokens, tok, b, t, dm.nkv, hr - dm.nh - dm.nkv, dm.seq, D);
     }
     if (!real) {
       zero8(o1);
@@ -125,6 +137,7 @@ __global__ void __launch_bounds__(kMaxThreads)
   }
 }
 
+template <bool kTokens>
 __global__ void __launch_bounds__(kMaxThreads)
     rope_bwd_vec(const uint16_t *__restrict__ dq, const uint16_t *__restrict__ dk,
                  const uint16_t *__restrict__ dv, const float *__restrict__ cosv,
@@ -152,11 +165,12 @@ __global__ void __launch_bounds__(kMaxThreads)
     const uint16_t *src;
     bool rotate = true;
     if (hr < dm.nh) {
-      src = dq ? dq + ((b * dm.nh + hr) * dm.seq + t) * D : nullptr;
+      src = dq ? dq + head_row(kTokens, tok, b, t, dm.nh, hr, dm.seq, D) : nullptr;
     } else if (hr < dm.nh + dm.nkv) {
-      src = dk ? dk + ((b * dm.nkv + (hr - dm.nh)) * dm.seq + t) * D : nullptr;
+      src = dk ? dk + head_row(kTokens, tok, b, t, dm.nkv, hr - dm.nh, dm.seq, D) : nullptr;
     } else {
-      src = dv ? dv + ((b * dm.nkv + (hr - dm.nh - dm.nkv)) * dm.seq + t) * D : nullptr;
+      src = dv ? dv + head_row(kTokens, tok, b, t, dm.nkv, hr - dm.nh - dm.nkv, dm.seq, D)
+               : nullptr;
       rotate = false;
     }
     float g1[8], g2[8], o1[8], o2[8];
@@ -195,7 +209,7 @@ __device__ __forceinline__ float f16(uint16_t h) { return __half2float(__ushort_
 __global__ void rope_fwd_any(const uint16_t *qkv, const void *lq, const void *lv, bool lora_fp32,
                              const float *cosv, const float *sinv, const int64_t *pos_idx,
                              const int32_t *slot_tok, uint16_t *q, uint16_t *k, uint16_t *v,
-                             RopeDims dm) {
+                             RopeDims dm, bool tokens) {
   const int total = dm.nh + 2 * dm.nkv;
   const int64_t slots = dm.batch * dm.seq;
   const int64_t units = slot_tok ? slots : dm.rows;
@@ -217,9 +231,9 @@ __global__ void rope_fwd_any(const uint16_t *qkv, const void *lq, const void *lv
     }
     const int64_t b = pos / dm.seq, t = pos % dm.seq;
     uint16_t *dst;
-    if (hr < dm.nh) dst = q + ((b * dm.nh + hr) * dm.seq + t) * D;
-    else if (hr < dm.nh + dm.nkv) dst = k + ((b * dm.nkv + (hr - dm.nh)) * dm.seq + t) * D;
-    else dst = v + ((b * dm.nkv + (hr - dm.nh - dm.nkv)) * dm.seq + t) * D;
+    if (hr < dm.nh) dst = q + head_row(tokens, tok, b, t, dm.nh, hr, dm.seq, D);
+    else if (hr < dm.nh + dm.nkv) dst = k + head_row(tokens, tok, b, t, dm.nkv, hr - dm.nh, dm.seq, D);
+    else dst = v + head_row(tokens, tok, b, t, dm.nkv, hr - dm.nh - dm.nkv, dm.seq, D);
     if (tok < 0 || tok >= dm.rows) {
       dst[j] = 0;
       dst[j + H] = 0;
@@ -251,7 +265,7 @@ __global__ void rope_fwd_any(const uint16_t *qkv, const void *lq, const void *lv
 
 __global__ void rope_bwd_any(const uint16_t *dq, const uint16_t *dk, const uint16_t *dv,
                              const float *cosv, const float *sinv, const int64_t *pos_idx,
-                             uint16_t *dqkv, RopeDims dm) {
+                             uint16_t *dqkv, RopeDims dm, bool tokens) {
   const int total = dm.nh + 2 * dm.nkv;
   const int64_t slots = dm.batch * dm.seq;
   const int64_t n = dm.rows * total * dm.half;
@@ -266,10 +280,12 @@ __global__ void rope_bwd_any(const uint16_t *dq, const uint16_t *dk, const uint1
     const int64_t b = inside ? pos / dm.seq : 0, t = inside ? pos % dm.seq : 0;
     const uint16_t *src;
     bool rotate = true;
-    if (hr < dm.nh) src = dq ? dq + ((b * dm.nh + hr) * dm.seq + t) * D : nullptr;
-    else if (hr < dm.nh + dm.nkv) src = dk ? dk + ((b * dm.nkv + (hr - dm.nh)) * dm.seq + t) * D : nullptr;
+    if (hr < dm.nh) src = dq ? dq + head_row(tokens, tok, b, t, dm.nh, hr, dm.seq, D) : nullptr;
+    else if (hr < dm.nh + dm.nkv)
+      src = dk ? dk + head_row(tokens, tok, b, t, dm.nkv, hr - dm.nh, dm.seq, D) : nullptr;
     else {
-      src = dv ? dv + ((b * dm.nkv + (hr - dm.nh - dm.nkv)) * dm.seq + t) * D : nullptr;
+      src = dv ? dv + head_row(tokens, tok, b, t, dm.nkv, hr - dm.nh - dm.nkv, dm.seq, D)
+               : nullptr;
       rotate = false;
     }
     const float g1 = (src && inside) ? f16(src[j]) : 0.f;
@@ -326,17 +342,20 @@ unsigned grid_for(int64_t n, int threads) {
 
 using namespace tb;
 
-extern "C" int tb_rope_pack_fwd(const uint16_t *qkv, const void *lora_q, const void *lora_v,
-                                int32_t lora_is_fp32, const float *cos, const float *sin,
-                                const int64_t *pos_idx, const int32_t *slot_tok, uint16_t *q,
-                                uint16_t *k, uint16_t *v, int64_t rows, int64_t batch, int64_t seq,
-                                int32_t n_heads, int32_t n_kv, int32_t head_dim, void *stream) {
-  int rc = check_dims("rope_pack_fwd", rows, batch, seq, n_heads, n_kv, head_dim);
+namespace tb {
+namespace {
+
+int rope_fwd_launch(const char *what, bool tokens, const uint16_t *qkv, const void *lora_q,
+                    const void *lora_v, int32_t lora_is_fp32, const float *cos, const float *sin,
+                    const int64_t *pos_idx, const int32_t *slot_tok, uint16_t *q, uint16_t *k,
+                    uint16_t *v, int64_t rows, int64_t batch, int64_t seq, int32_t n_heads,
+                    int32_t n_kv, int32_t head_dim, void *stream) {
+  int rc = check_dims(what, rows, batch, seq, n_heads, n_kv, head_dim);
   if (rc != TB_OK) return rc;
   if (!cos || !sin || !q || (n_kv > 0 && (!k || !v)))
-    return set_error(TB_EINVAL, "rope_pack_fwd: cos, sin, q, k, v are required");
+    return set_error(TB_EINVAL, "%s: cos, sin, q, k, v are required", what);
   if (rows > 0 && (!qkv || !pos_idx))
-    return set_error(TB_EINVAL, "rope_pack_fwd: qkv and pos_idx are required");
+    return set_error(TB_EINVAL, "%s: qkv and pos_idx are required", what);
   const int64_t units = slot_tok ? batch * seq : rows;
   if (units == 0) return TB_OK;
   RopeDims dm{rows, batch, seq, n_heads, n_kv, head_dim, head_dim / 2};
@@ -348,47 +367,95 @@ extern "C" int tb_rope_pack_fwd(const uint16_t *qkv, const void *lora_q, const v
     const unsigned blocks = (unsigned)units;
     const int threads = rope_threads(dm);
     const FastDiv sd((uint32_t)seq);
-    if (slot_tok) {
-      if (lora_is_fp32)
-        rope_fwd_vec<true, true><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx, slot_tok, q, k, v, dm, sd);
-      else
-        rope_fwd_vec<true, false><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx, slot_tok, q, k, v, dm, sd);
+#define TB_ROPE_FWD(S, F, T)                                                                    \
+  rope_fwd_vec<S, F, T><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx,  \
+                                                     slot_tok, q, k, v, dm, sd)
+    if (tokens) {
+      if (lora_is_fp32) TB_ROPE_FWD(false, true, true);
+      else TB_ROPE_FWD(false, false, true);
+    } else if (slot_tok) {
+      if (lora_is_fp32) TB_ROPE_FWD(true, true, false);
+      else TB_ROPE_FWD(true, false, false);
     } else {
-      if (lora_is_fp32)
-        rope_fwd_vec<false, true><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx, slot_tok, q, k, v, dm, sd);
-      else
-        rope_fwd_vec<false, false><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx, slot_tok, q, k, v, dm, sd);
+      if (lora_is_fp32) TB_ROPE_FWD(false, true, false);
+      else TB_ROPE_FWD(false, false, false);
     }
+#undef TB_ROPE_FWD
   } else {
     const int64_t n = units * (n_heads + 2 * n_kv) * (int64_t)dm.half;
     rope_fwd_any<<<grid_for(n, 256), 256, 0, st>>>(qkv, lora_q, lora_v, lora_is_fp32 != 0, cos, sin,
-                                                   pos_idx, slot_tok, q, k, v, dm);
+                                                   pos_idx, slot_tok, q, k, v, dm, tokens);
   }
-  return check_launch("rope_pack_fwd");
+  return check_launch(what);
 }
 
-extern "C" int tb_rope_pack_bwd(const uint16_t *dq, const uint16_t *dk, const uint16_t *dv,
-                                const float *cos, const float *sin, const int64_t *pos_idx,
-                                uint16_t *dqkv, int64_t rows, int64_t batch, int64_t seq,
-                                int32_t n_heads, int32_t n_kv, int32_t head_dim, void *stream) {
-  int rc = check_dims("rope_pack_bwd", rows, batch, seq, n_heads, n_kv, head_dim);
+int rope_bwd_launch(const char *what, bool tokens, const uint16_t *dq, const uint16_t *dk,
+                    const uint16_t *dv, const float *cos, const float *sin, const int64_t *pos_idx,
+                    uint16_t *dqkv, int64_t rows, int64_t batch, int64_t seq, int32_t n_heads,
+                    int32_t n_kv, int32_t head_dim, void *stream) {
+  int rc = check_dims(what, rows, batch, seq, n_heads, n_kv, head_dim);
   if (rc != TB_OK) return rc;
   if (rows == 0) return TB_OK;
   if (!cos || !sin || !pos_idx || !dqkv)
-    return set_error(TB_EINVAL, "rope_pack_bwd: cos, sin, pos_idx, dqkv are required");
+    return set_error(TB_EINVAL, "%s: cos, sin, pos_idx, dqkv are required", what);
   RopeDims dm{rows, batch, seq, n_heads, n_kv, head_dim, head_dim / 2};
   const bool vec = dm.half % 8 == 0 && dm.half <= 8 * kMaxThreads && aligned(dqkv, 16) && aligned(cos, 16) &&
                    aligned(sin, 16) && (!dq || aligned(dq, 16)) && (!dk || aligned(dk, 16)) &&
                    (!dv || aligned(dv, 16));
   cudaStream_t st = as_stream(stream);
   if (vec) {
-    rope_bwd_vec<<<(unsigned)rows, rope_threads(dm), 0, st>>>(dq, dk, dv, cos, sin, pos_idx, dqkv,
-                                                             dm, FastDiv((uint32_t)seq));
+    const FastDiv sd((uint32_t)seq);
+    if (tokens)
+      rope_bwd_vec<true><<<(unsigned)rows, rope_threads(dm), 0, st>>>(dq, dk, dv, cos, sin,
+                                                                     pos_idx, dqkv, dm, sd);
+    else
+      rope_bwd_vec<false><<<(unsigned)rows, rope_threads(dm), 0, st>>>(dq, dk, dv, cos, sin,
+                                                                      pos_idx, dqkv, dm, sd);
   } else {
     const int64_t n = rows * (n_heads + 2 * n_kv) * (int64_t)dm.half;
-    rope_bwd_any<<<grid_for(n, 256), 256, 0, st>>>(dq, dk, dv, cos, sin, pos_idx, dqkv, dm);
+    rope_bwd_any<<<grid_for(n, 256), 256, 0, st>>>(dq, dk, dv, cos, sin, pos_idx, dqkv, dm,
+                                                   tokens);
   }
-  return check_launch("rope_pack_bwd");
+  return check_launch(what);
+}
+
+}  // namespace
+}  // namespace tb
+
+extern "C" int tb_rope_pack_fwd(const uint16_t *qkv, const void *lora_q, const void *lora_v,
+                                int32_t lora_is_fp32, const float *cos, const float *sin,
+                                const int64_t *pos_idx, const int32_t *slot_tok, uint16_t *q,
+                                uint16_t *k, uint16_t *v, int64_t rows, int64_t batch, int64_t seq,
+                                int32_t n_heads, int32_t n_kv, int32_t head_dim, void *stream) {
+  return rope_fwd_launch("rope_pack_fwd", false, qkv, lora_q, lora_v, lora_is_fp32, cos, sin,
+                         pos_idx, slot_tok, q, k, v, rows, batch, seq, n_heads, n_kv, head_dim,
+                         stream);
+}
+
+extern "C" int tb_rope_pack_bwd(const uint16_t *dq, const uint16_t *dk, const uint16_t *dv,
+                                const float *cos, const float *sin, const int64_t *pos_idx,
+                                uint16_t *dqkv, int64_t rows, int64_t batch, int64_t seq,
+                                int32_t n_heads, int32_t n_kv, int32_t head_dim, void *stream) {
+  return rope_bwd_launch("rope_pack_bwd", false, dq, dk, dv, cos, sin, pos_idx, dqkv, rows, batch,
+                         seq, n_heads, n_kv, head_dim, stream);
+}
+
+extern "C" int tb_rope_tokens_fwd(const uint16_t *qkv, const void *lora_q, const void *lora_v,
+                                  int32_t lora_is_fp32, const float *cos, const float *sin,
+                                  const int64_t *pos_idx, uint16_t *q, uint16_t *k, uint16_t *v,
+                                  int64_t rows, int64_t batch, int64_t seq, int32_t n_heads,
+                                  int32_t n_kv, int32_t head_dim, void *stream) {
+  return rope_fwd_launch("rope_tokens_fwd", true, qkv, lora_q, lora_v, lora_is_fp32, cos, sin,
+                         pos_idx, nullptr, q, k, v, rows, batch, seq, n_heads, n_kv, head_dim,
+                         stream);
+}
+
+extern "C" int tb_rope_tokens_bwd(const uint16_t *dq, const uint16_t *dk, const uint16_t *dv,
+                                  const float *cos, const float *sin, const int64_t *pos_idx,
+                                  uint16_t *dqkv, int64_t rows, int64_t batch, int64_t seq,
+                                  int32_t n_heads, int32_t n_kv, int32_t head_dim, void *stream) {
+  return rope_bwd_launch("rope_tokens_bwd", true, dq, dk, dv, cos, sin, pos_idx, dqkv, rows,
+                         batch, seq, n_heads, n_kv, head_dim, stream);
 }
 
 extern "C" int tb_slot_index(const int64_t *pos_idx, int64_t rows, int64_t slots,

@@ -8,7 +8,7 @@ that the eager path reads back from the GPU (the real-token positions, the atten
 takes, the head's labelled-row count and denominator) are computed before the replay from host
 copies of the batch (model.StaticBatch) and the graph is keyed by them:
 
-    key = (batch, seq, real tokens, labelled tokens, loss denominator, mask kind)
+    key = (batch, seq, real tokens, labelled tokens, loss denominator, longest row)
 
 A key seen before replays its graph after copying the batch into the graph's input buffers; a new
 key is captured once (after `warmup` eager steps on a side stream). Every trainable gradient must
@@ -21,14 +21,14 @@ import torch.nn.functional as F
 
 from .dist import GradBucket
 from .head import IGNORE_INDEX
-from .model import HeadStats, StaticBatch
+from .model import USE_VARLEN_ATTENTION, HeadStats, StaticBatch, sequence_offsets
 from .rope import slot_index
 from .trainer_patch import _FusedRequest
 
 
 class _Entry:
-    __slots__ = ("graph", "ids", "mask", "labels", "n_items", "pos", "mask4d", "loss", "stats",
-                 "tokens")
+    __slots__ = ("graph", "ids", "mask", "labels", "n_items", "pos", "mask4d", "cu", "max_len",
+                 "loss", "stats", "tokens")
 
 
 def host_plan(attention_mask, labels, num_items_in_batch=None):
@@ -67,8 +67,8 @@ class GraphedTrainStep:
 
     def _step(self, e, counts):
         self.bucket.zero()
-        slot = slot_index(e.pos, e.ids.numel())
-        with StaticBatch(e.pos, slot, e.mask4d, counts), \
+        slot = None if e.cu is not None else slot_index(e.pos, e.ids.numel())
+        with StaticBatch(e.pos, slot, e.mask4d, counts, e.cu, e.max_len), \
                 torch.autocast("cuda", dtype=torch.float16), _FusedRequest():
             out = self.model(input_ids=e.ids, attention_mask=e.mask, labels=e.labels,
                              num_items_in_batch=e.n_items)
@@ -78,13 +78,14 @@ class GraphedTrainStep:
             self.post_backward()
         return out
 
-    def _capture(self, key, ids, mask, labels, n_items, pos, counts):
+    def _capture(self, key, ids, mask, labels, n_items, pos, counts, cu, max_len):
         e = _Entry()
         e.ids, e.mask, e.labels = ids.clone(), mask.clone(), labels.clone()
         e.n_items = n_items.clone()
         e.pos = pos.clone()
         e.tokens = pos.numel()
-        m4 = self._mask4d(e)
+        e.cu, e.max_len = (cu.clone(), max_len) if cu is not None else (None, None)
+        m4 = self._mask4d(e) if e.cu is None else None
         e.mask4d = None if m4 is None else m4.clone()
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
@@ -115,19 +116,23 @@ class GraphedTrainStep:
             num_items_in_batch = int((hl[:, 1:] != IGNORE_INDEX).sum())
         n_items_f = float(num_items_in_batch)
         pos, n_lab, denom = host_plan(hm, hl, n_items_f)
+        cu, max_len = sequence_offsets(hm) if USE_VARLEN_ATTENTION else (None, None)
         batch, seq = tuple(input_ids.shape)
-        key = (batch, seq, pos.numel(), n_lab, denom)
+        key = (batch, seq, pos.numel(), n_lab, denom, max_len)
         e = self.entries.get(key)
         n_items = torch.tensor(n_items_f, device=dev) if e is None else None
         if e is None:
             e = self._capture(key, input_ids.to(dev), attention_mask.to(dev), labels.to(dev),
-                              n_items, pos.to(dev), (n_lab, denom))
+                              n_items, pos.to(dev), (n_lab, denom),
+                              None if cu is None else cu.to(dev), max_len)
             e.graph.replay()
         else:
             e.ids.copy_(input_ids, non_blocking=True)
             e.mask.copy_(attention_mask, non_blocking=True)
             e.labels.copy_(labels, non_blocking=True)
             e.pos.copy_(pos, non_blocking=True)
+            if e.cu is not None:
+                e.cu.copy_(cu, non_blocking=True)
             if e.mask4d is not None:
                 e.mask4d.copy_(self._mask4d(e))
             e.graph.replay()

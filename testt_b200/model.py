@@ -10,13 +10,17 @@ Per decoder layer, with s the fp32 residual stream of the M real tokens:
     s, y, y_pad = add_rmsnorm(s, d)                 tb_add_rmsnorm_fwd (d: previous block, fp16)
     qkv        = y @ [Wq; Wk; Wv]^T + b               tb_nf4_unpack_multi + one cuBLAS GEMM
     lq, lv     = LoRA(dropout(y_pad))                 PyTorch, peft's math, same dropout draws
-    q, k, v    = rope_pack(qkv, lq, lv)               tb_rope_pack_fwd into padded [B, H, T, 128]
-    a          = SDPA(q, k, v, causal + pad mask)     PyTorch
-    o          = a[real tokens] @ Wo^T                tb_nf4_unpack_multi + cuBLAS
+    q, k, v    = rope_tokens(qkv, lq, lv)             tb_rope_tokens_fwd, token-major [M, H, 128]
+    a          = varlen causal attention(q, k, v)     PyTorch's flash kernels, GQA, per sequence
+    o          = a @ Wo^T                             tb_nf4_unpack_multi + cuBLAS
     s, y2, _   = add_rmsnorm(s, o)                    tb_add_rmsnorm_fwd
     d          = mlp(y2)                              NF4 + cuBLAS + tb_swiglu_fwd
 then the final norm and the fused head (head.py). Pad tokens never enter the projections, norms,
-MLP or head; attention runs on the padded layout, as in the unpatched model.
+MLP, attention or head. Causal attention over each row's real tokens in column order is the
+unpatched model's causal + padding-mask attention restricted to the real query rows (the only
+rows whose outputs are used), with the padded positions never computed. Without
+torch.nn.attention.varlen, attention runs as in the reference: rope_pack into the padded
+[B, H, T, 128] layout and SDPA with the causal + padding mask.
 """
 
 import threading
@@ -27,7 +31,15 @@ from .head import IGNORE_INDEX, fused_head_loss
 from .mlp import fused_mlp
 from .nf4 import frozen_linear
 from .rmsnorm import add_rmsnorm
-from .rope import rope_pack, slot_index
+from .rope import rope_pack, rope_tokens, slot_index
+
+try:
+    from torch.nn.attention.varlen import varlen_attn as _varlen_attn
+except ImportError:  # torch < 2.9: attention on the padded layout
+    _varlen_attn = None
+
+# causal attention over each sequence's real tokens (token-major) when available
+USE_VARLEN_ATTENTION = _varlen_attn is not None
 
 _ALLOWED_KWARGS = {"num_items_in_batch", "output_attentions", "output_hidden_states",
                    "return_dict"}
@@ -38,11 +50,14 @@ _static = threading.local()
 class StaticBatch:
     """Host-side facts of one batch, computed before a captured step is replayed so that the
     step itself makes no host synchronisation: the real-token positions (and their slot map),
-    the attention mask SDPA takes, and the head's (labelled rows, loss denominator). While a
-    StaticBatch is active (`with batch:`), fused_forward uses these instead of deriving them."""
+    the attention mask SDPA takes, the head's (labelled rows, loss denominator) and, for
+    variable-length attention, the cumulative sequence offsets (int32 [batch + 1], on the
+    device) with the longest sequence. While a StaticBatch is active (`with batch:`),
+    fused_forward uses these instead of deriving them."""
 
-    def __init__(self, pos_idx, slot_tok, mask, counts):
+    def __init__(self, pos_idx, slot_tok, mask, counts, cu_seqlens=None, max_len=None):
         self.pos_idx, self.slot_tok, self.mask, self.counts = pos_idx, slot_tok, mask, counts
+        self.cu_seqlens, self.max_len = cu_seqlens, max_len
 
     def __enter__(self):
         self._prev = getattr(_static, "batch", None)
@@ -237,6 +252,16 @@ def _lora_branch(module, y_pad, batch, seq, pos_idx):
     return lora_b(lora_a(dropped.index_select(0, pos_idx))) * scaling
 
 
+def sequence_offsets(attention_mask):
+    """(cu_seqlens int32 [batch + 1], longest row) of the real tokens of each row: the packed
+    sequences of variable-length attention, in pos_idx order. The offsets stay on the mask's
+    device; reading the longest row back synchronises once when that is a GPU."""
+    lengths = attention_mask.reshape(attention_mask.shape[0], -1).ne(0).sum(1)
+    cu = torch.zeros(lengths.numel() + 1, dtype=torch.int32, device=lengths.device)
+    cu[1:] = lengths.cumsum(0)
+    return cu, int(lengths.max()) if lengths.numel() else 0
+
+
 def _attention(lp, q, k, v, mask):
     from transformers.integrations.sdpa_attention import sdpa_attention_forward
 
@@ -257,11 +282,17 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
     dev = input_ids.device
     padded = batch * seq
     static = active_static_batch()
+    varlen = USE_VARLEN_ATTENTION and (static is None or static.cu_seqlens is not None)
     if static is None:
         pos_idx = attention_mask.reshape(-1).nonzero().squeeze(1)   # sorted, one host sync
-        slot_tok = slot_index(pos_idx, padded)                      # shared by every layer
+        if varlen:
+            cu_seqlens, max_len = sequence_offsets(attention_mask)  # one more host sync
+        else:
+            slot_tok = slot_index(pos_idx, padded)                  # shared by every layer
     else:
         pos_idx, slot_tok = static.pos_idx, static.slot_tok
+        cu_seqlens, max_len = static.cu_seqlens, static.max_len
+    tokens = pos_idx.numel()
 
     # Embeddings of the real tokens (the table may be held in fp16 with exact values, see
     # trainer_patch.prepare_model); the residual stream is fp32.
@@ -270,7 +301,9 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
 
     shape_ref = s.new_empty((1, 1, 1)).expand(batch, seq, plan.hidden)
     position_ids = torch.arange(seq, device=dev).unsqueeze(0)
-    if static is None:
+    if varlen:
+        mask = None
+    elif static is None:
         mask = create_causal_mask(config=cfg, inputs_embeds=shape_ref,
                                   attention_mask=attention_mask, past_key_values=None,
                                   position_ids=position_ids)
@@ -288,12 +321,21 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
         lora_q = _lora_branch(lp.attn.q_proj, y_pad, batch, seq, pos_idx)
         lora_v = _lora_branch(lp.attn.v_proj, y_pad, batch, seq, pos_idx)
         del y_pad
-        q, k, v = rope_pack(qkv, lora_q, lora_v, cos, sin, pos_idx, batch, seq, plan.n_heads,
-                            plan.n_kv, plan.head_dim, slot_tok=slot_tok)
-        del qkv, lora_q, lora_v
-        attn = _attention(lp, q, k, v, mask)
-        del q, k, v
-        attn = attn.reshape(padded, plan.n_heads * plan.head_dim).index_select(0, pos_idx)
+        if varlen:
+            q, k, v = rope_tokens(qkv, lora_q, lora_v, cos, sin, pos_idx, batch, seq,
+                                  plan.n_heads, plan.n_kv, plan.head_dim)
+            del qkv, lora_q, lora_v
+            attn = _varlen_attn(q, k, v, cu_seqlens, cu_seqlens, max_len, max_len,
+                                scale=lp.attn.scaling, window_size=(-1, 0))
+            del q, k, v
+            attn = attn.reshape(tokens, plan.n_heads * plan.head_dim)
+        else:
+            q, k, v = rope_pack(qkv, lora_q, lora_v, cos, sin, pos_idx, batch, seq,
+                                plan.n_heads, plan.n_kv, plan.head_dim, slot_tok=slot_tok)
+            del qkv, lora_q, lora_v
+            attn = _attention(lp, q, k, v, mask)
+            del q, k, v
+            attn = attn.reshape(padded, plan.n_heads * plan.head_dim).index_select(0, pos_idx)
         o = frozen_linear(attn, (lp.o,), lp.o_bias)
         del attn
         s, y2, _ = add_rmsnorm(s, o, layer.post_attention_layernorm.weight,
