@@ -266,12 +266,12 @@ class HotPath:
                     (_lib._I32 * n)(*[j["qblock"] for j in jobs]),
                     (_lib._I32 * n)(*[j.get("qblock2", 1) for j in jobs]))
 
+        # every NF4 weight of a layer in one launch (nf4.LayerWeights), forward and backward
         fwd_nf4, bwd_nf4 = [], []
         for lp in plan.layers:
-            for ws in ((lp.q, lp.k, lp.v), (lp.o,), (lp.gate, lp.up), (lp.down,)):
-                jobs, nb = nf4_jobs(ws)
-                fwd_nf4.append((nf4_launch(jobs), nb))
-                bwd_nf4.insert(0, (nf4_launch(jobs), nb))
+            jobs, nb = nf4_jobs(lp.weights.flat)
+            fwd_nf4.append((nf4_launch(jobs), nb))
+            bwd_nf4.insert(0, (nf4_launch(jobs), nb))
         for args, nb in fwd_nf4 + bwd_nf4:
             add("nf4_unpack", nb, "tb_nf4_unpack_multi", *args)
 
@@ -562,16 +562,25 @@ def kernel_bench(name, steps, warmup, device):
         raise SystemExit(f"unknown kernel {name}")
     for _ in range(warmup):
         fn()
+    torch.cuda.synchronize()
+    # the launch replayed from a CUDA graph: the event pair then brackets the kernel alone (an
+    # eager call's host-side work can outlast the L2 flush queued before it and idle the GPU
+    # inside the timed region)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    graph.replay()
     times = []
     for _ in range(steps):
         flush_l2(flush)
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record()
-        fn()
+        graph.replay()
         b.record()
         torch.cuda.synchronize()
         times.append(a.elapsed_time(b) * 1e3)
+    del graph
     us = float(np.median(times))
     pk, kind = peaks()
     if "flops" in info:

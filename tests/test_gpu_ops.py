@@ -97,6 +97,45 @@ def test_nf4_more_weights_than_one_launch_and_misaligned_output():
     assert_bitexact(view.reshape(-1), cnf4.unpack(qs[0]), "misaligned out")
 
 
+def test_layer_weights_one_launch_operands_and_grads():
+    """LayerWeights: the operands of a layer (groups of different widths, plain and nested) in
+    one launch equal the oracle bit for bit, and layer_linear / layer_mlp give what
+    frozen_linear / fused_mlp give, forward and backward, releasing the buffer in backward."""
+    from testt_b200 import _lib, mlp, nf4
+
+    rng = np.random.default_rng(11)
+    shapes = [(96, 128), (32, 128), (32, 128), (128, 128), (160, 128), (160, 128), (128, 160)]
+    qs = [onf4.quantize((rng.standard_normal(sh) * 0.05).astype(np.float16), 64,
+                        nested=bool(i % 2)) for i, sh in enumerate(shapes)]
+    ws = [nf4_weight(q, DEV) for q in qs]
+    groups = ((ws[0], ws[1], ws[2]), (ws[3],), (ws[4], ws[5]), (ws[6],))
+    lw = nf4.LayerWeights(groups)
+    _lib.reset_call_count()
+    ops = lw.operands(torch.device(DEV))
+    assert _lib.call_count() == 1
+    i = 0
+    for g, op in zip(groups, ops):
+        ref = np.concatenate([cnf4.unpack(qs[i + k]) for k in range(len(g))])
+        assert_bitexact(op.reshape(-1), ref, f"group of {len(g)}")
+        i += len(g)
+    x = torch.randn(40, 128, device=DEV, dtype=torch.float16, requires_grad=True)
+    x2 = x.detach().clone().requires_grad_(True)
+    y = nf4.layer_linear(x, lw, 0, last=True)
+    z = mlp.layer_mlp(y[:, :128].contiguous(), lw, 2, 3)
+    lw.release()
+    y2 = nf4.frozen_linear(x2, groups[0])
+    z2 = mlp.fused_mlp(y2[:, :128].contiguous(), ws[4], ws[5], ws[6])
+    # the same GEMMs on the same values (cuBLAS may pick another algorithm for another operand
+    # address, hence a tolerance rather than equality)
+    torch.testing.assert_close(y, y2, rtol=1e-3, atol=1e-3)
+    torch.testing.assert_close(z, z2, rtol=1e-3, atol=1e-3)
+    gz = torch.randn_like(z)
+    (z * gz).sum().backward()
+    (z2 * gz).sum().backward()
+    torch.testing.assert_close(x.grad, x2.grad, rtol=1e-3, atol=1e-3)
+    assert lw._ops is None, "the last backward operation releases the layer's weights"
+
+
 def test_nf4_no_wait_timed_out():
     """The bulk-copy kernel's bounded waits never gave up in the runs above."""
     from testt_b200 import _lib

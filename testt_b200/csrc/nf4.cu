@@ -20,9 +20,14 @@
 namespace tb {
 namespace {
 
+#ifndef TB_NF4_UNROLL
+#define TB_NF4_UNROLL 8
+#endif
+
 constexpr int kMaxW = TB_NF4_MAX_WEIGHTS;
-constexpr int kUnroll = 4;
+constexpr int kUnroll = TB_NF4_UNROLL;  // words per lane per warp span (4 or 8)
 constexpr int kThreads = 256;
+static_assert(kUnroll == 4 || kUnroll == 8, "a span's blocks of 64 must fit one lane each");
 
 struct Nf4Job {
   int n;
@@ -57,38 +62,125 @@ __device__ __forceinline__ float block_scale(const Nf4Job &job, int j, uint32_t 
 
 constexpr int kSpan = 32 * kUnroll;  // words per warp span
 
+// Shared-memory address tab | byte b of x: byte b of x moved to byte 0 and bytes 1..3 taken from
+// tab (256-byte aligned, so its byte 0 is zero), one byte permute.
+__device__ __forceinline__ uint32_t table_addr(uint32_t x, uint32_t tab, int b) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(x), "r"(tab), "r"(0x7650u | (uint32_t)b));
+  return r;
+}
+
 // fp16 values of the 8 nibbles of `word` (high nibble of each byte first) times `scale`, packed.
-// `tab` is the byte address of the 16-entry table in shared memory (64-byte aligned), so a
-// nibble's entry is tab | ((word >> s) & 0x3c): one shift and one logic op per lookup.
+// `tab` is the shared-memory address of the 16-entry table (256-byte aligned). The byte offsets
+// 4 * nibble of all eight nibbles come from two shift-and-mask operations (each byte of lo4 /
+// hi4 holds one), and each lookup address from one byte permute.
 __device__ __forceinline__ uint4 decode_word(uint32_t word, float scale, uint32_t tab) {
+  const uint32_t lo4 = (word << 2) & 0x3c3c3c3cu;
+  const uint32_t hi4 = (word >> 2) & 0x3c3c3c3cu;
   float f[8];
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
-    const uint32_t hi_off = (word >> (8 * b + 2)) & 0x3cu;
-    const uint32_t lo_off = (b == 0 ? (word << 2) : (word >> (8 * b - 2))) & 0x3cu;
     float hi, lo;
-    asm("ld.shared.f32 %0, [%1];" : "=f"(hi) : "r"(tab | hi_off));
-    asm("ld.shared.f32 %0, [%1];" : "=f"(lo) : "r"(tab | lo_off));
+    asm("ld.shared.f32 %0, [%1];" : "=f"(hi) : "r"(table_addr(hi4, tab, b)));
+    asm("ld.shared.f32 %0, [%1];" : "=f"(lo) : "r"(table_addr(lo4, tab, b)));
     // two products per instruction (sm_100 packed fp32 multiply, each lane rounded to nearest
     // even exactly like __fmul_rn)
-    asm("{\n\t.reg .b64 a, s, p;\n\t"
-        "mov.b64 a, {%2, %3};\n\t"
-        "mov.b64 s, {%4, %4};\n\t"
-        "mul.rn.f32x2 p, a, s;\n\t"
-        "mov.b64 {%0, %1}, p;\n\t}"
-        : "=f"(f[2 * b]), "=f"(f[2 * b + 1])
-        : "f"(hi), "f"(lo), "f"(scale));
+    const float2 p = __fmul2_rn(make_float2(hi, lo), make_float2(scale, scale));
+    f[2 * b] = p.x;
+    f[2 * b + 1] = p.y;
   }
   return make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]),
                     pack_half2(f[6], f[7]));
 }
 
-// kBlock64: blocksize 64 (8 words per absmax block). A span of 32 * kUnroll words holds 4 *
-// kUnroll blocks: lane l < 4 * kUnroll computes the scale of block l once and word k of lane l
-// (block 4k + l/8) takes it by shuffle.
-template <bool kBlock64>
-__global__ void __launch_bounds__(kThreads) nf4_unpack_words(const __grid_constant__ Nf4Job job) {
-  __shared__ __align__(64) float table[kMaxW][16];
+#ifndef TB_NF4_SPANS
+#define TB_NF4_SPANS 4
+#endif
+constexpr int kSpansPerWarp = TB_NF4_SPANS;  // spans a warp is sized to take (grid sizing)
+
+// One warp span of blocksize-64 weights, loaded ahead of its decode: the span's words and the
+// absmax of lane l's block (block first/8 + l): the fp32 absmax (plain) or the u8 code and the
+// fp32 absmax2 it scales (nested).
+struct Span64 {
+  int j;
+  uint32_t first, nwords;
+  uint32_t word[kUnroll];
+  float a;
+  int code;  // -1: plain absmax (or no block for this lane)
+};
+
+__device__ __forceinline__ void fetch_span64(const Nf4Job &job, int64_t sp, int lane, Span64 &s) {
+  s.j = find_weight(job, sp * kSpan);  // uniform across the warp
+  s.first = (uint32_t)(sp * kSpan - job.start[s.j]);
+  s.nwords = job.n_words[s.j];
+  const uint32_t *src = reinterpret_cast<const uint32_t *>(job.packed[s.j]);
+#pragma unroll
+  for (int k = 0; k < kUnroll; ++k) {
+    const uint32_t local = s.first + k * 32 + lane;
+    s.word[k] = local < s.nwords ? __ldg(src + local) : 0u;
+  }
+  const uint32_t b = (s.first >> 3) + lane;
+  s.a = 0.f;
+  s.code = -1;
+  if (lane < 4 * kUnroll && b * 8 < s.nwords) {
+    if (job.absmax_f32[s.j] != nullptr) {
+      s.a = __ldg(job.absmax_f32[s.j] + b);
+    } else {
+      s.code = __ldg(job.absmax_u8[s.j] + b);
+      s.a = __ldg(job.absmax2[s.j] + job.nest_div[s.j].div(b));
+    }
+  }
+}
+
+// Blocksize 64 with the next span's loads issued before the current span's decode, so a warp
+// keeps its memory latency behind its own arithmetic. A span of 32 * kUnroll words holds
+// 4 * kUnroll blocks: lane l computes the scale of block l once and word k of lane l (block
+// 4k + l/8) takes it by shuffle.
+__global__ void __launch_bounds__(kThreads) nf4_unpack_words64(const __grid_constant__ Nf4Job job) {
+  __shared__ __align__(256) float table[kMaxW][64];  // 16 entries used, 256-byte stride
+  __shared__ float code2[kMaxW][256];
+  __shared__ float offs[kMaxW];
+  for (int i = threadIdx.x; i < job.n * 16; i += blockDim.x)
+    table[i >> 4][i & 15] = __ldg(job.table[i >> 4] + (i & 15));
+  for (int j = 0; j < job.n; ++j) {
+    if (job.absmax_f32[j] != nullptr) continue;
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) code2[j][i] = __ldg(job.code2[j] + i);
+    if (threadIdx.x == 0) offs[j] = __ldg(job.offset[j]);
+  }
+  __syncthreads();
+
+  const int64_t spans = job.start[job.n] / kSpan;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (kThreads / 32);
+  const uint32_t table_base = (uint32_t)__cvta_generic_to_shared(&table[0][0]);
+  int64_t sp = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
+  if (sp >= spans) return;
+  Span64 cur, nxt;
+  fetch_span64(job, sp, lane, cur);
+  while (true) {
+    const int64_t nsp = sp + warps;
+    const bool more = nsp < spans;  // uniform across the warp
+    if (more) fetch_span64(job, nsp, lane, nxt);
+    float mine = cur.a;
+    if (cur.code >= 0) mine = __fadd_rn(__fmul_rn(code2[cur.j][cur.code], cur.a), offs[cur.j]);
+    const uint32_t tab = table_base + (uint32_t)cur.j * 256u;
+    uint4 *dst = reinterpret_cast<uint4 *>(job.out[cur.j]);
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) {
+      const float scale = __shfl_sync(0xffffffffu, mine, 4 * k + (lane >> 3));
+      const uint32_t local = cur.first + k * 32 + lane;
+      if (local < cur.nwords) __stcs(dst + local, decode_word(cur.word[k], scale, tab));
+    }
+    if (!more) break;
+    cur = nxt;
+    sp = nsp;
+  }
+}
+
+// Any even blocksize: each word's absmax block is found by invariant division and its scale
+// computed by the lane itself.
+__global__ void __launch_bounds__(kThreads) nf4_unpack_words_any(const __grid_constant__ Nf4Job job) {
+  __shared__ __align__(256) float table[kMaxW][64];  // 16 entries used, 256-byte stride
   __shared__ float code2[kMaxW][256];
   __shared__ float offs[kMaxW];
   for (int i = threadIdx.x; i < job.n * 16; i += blockDim.x)
@@ -111,50 +203,22 @@ __global__ void __launch_bounds__(kThreads) nf4_unpack_words(const __grid_consta
     const uint32_t *src = reinterpret_cast<const uint32_t *>(job.packed[j]);
     const bool plain = job.absmax_f32[j] != nullptr;
     const uint32_t tab = (uint32_t)__cvta_generic_to_shared(&table[j][0]);
-    uint32_t word[kUnroll];
-#pragma unroll
-    for (int k = 0; k < kUnroll; ++k) {
-      const uint32_t local = first + k * 32 + lane;
-      word[k] = local < nwords ? __ldg(src + local) : 0u;
-    }
-    float scale[kUnroll];
-    if (kBlock64) {
-      // lane l: block first/8 + l (exists when its first word does)
-      const uint32_t b = (first >> 3) + lane;
-      float mine = 0.f;
-      if (lane < 4 * kUnroll && b * 8 < nwords) {
-        if (plain) {
-          mine = __ldg(job.absmax_f32[j] + b);
-        } else {
-          const int code = __ldg(job.absmax_u8[j] + b);
-          const float a2 = __ldg(job.absmax2[j] + job.nest_div[j].div(b));
-          mine = __fadd_rn(__fmul_rn(code2[j][code], a2), offs[j]);
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < kUnroll; ++k) scale[k] = __shfl_sync(0xffffffffu, mine, 4 * k + (lane >> 3));
-    } else {
-#pragma unroll
-      for (int k = 0; k < kUnroll; ++k) {
-        const uint32_t local = first + k * 32 + lane;
-        scale[k] = 0.f;
-        if (local < nwords) {
-          const uint32_t b = job.block_div[j].div(local * 4u);
-          if (plain) {
-            scale[k] = __ldg(job.absmax_f32[j] + b);
-          } else {
-            const int code = __ldg(job.absmax_u8[j] + b);
-            const float a2 = __ldg(job.absmax2[j] + job.nest_div[j].div(b));
-            scale[k] = __fadd_rn(__fmul_rn(code2[j][code], a2), offs[j]);
-          }
-        }
-      }
-    }
     uint4 *dst = reinterpret_cast<uint4 *>(job.out[j]);
 #pragma unroll
     for (int k = 0; k < kUnroll; ++k) {
       const uint32_t local = first + k * 32 + lane;
-      if (local < nwords) __stcs(dst + local, decode_word(word[k], scale[k], tab));
+      if (local >= nwords) continue;
+      const uint32_t word = __ldg(src + local);
+      const uint32_t b = job.block_div[j].div(local * 4u);
+      float scale;
+      if (plain) {
+        scale = __ldg(job.absmax_f32[j] + b);
+      } else {
+        const int code = __ldg(job.absmax_u8[j] + b);
+        const float a2 = __ldg(job.absmax2[j] + job.nest_div[j].div(b));
+        scale = __fadd_rn(__fmul_rn(code2[j][code], a2), offs[j]);
+      }
+      __stcs(dst + local, decode_word(word, scale, tab));
     }
   }
 }
@@ -200,13 +264,17 @@ int launch(Nf4Job &job, const int64_t *n_bytes, const int32_t *half_qblock, cuda
   const int64_t per_block = (int64_t)kThreads * (words ? kUnroll : 1);
   int64_t blocks = (total + per_block - 1) / per_block;
   if (words && block64) {
-    static int cap = resident_blocks(nf4_unpack_words<true>, kThreads);
+    // about kSpansPerWarp spans per warp, but at least one block per SM
+    static int cap = resident_blocks(nf4_unpack_words64, kThreads);
+    const int64_t per = (int64_t)(kThreads / 32) * kSpansPerWarp;
+    blocks = (total / kSpan + per - 1) / per;
+    if (blocks < sm_count()) blocks = sm_count();
     if (blocks > cap) blocks = cap;
-    nf4_unpack_words<true><<<(unsigned)blocks, kThreads, 0, stream>>>(job);
+    nf4_unpack_words64<<<(unsigned)blocks, kThreads, 0, stream>>>(job);
   } else if (words) {
-    static int cap = resident_blocks(nf4_unpack_words<false>, kThreads);
+    static int cap = resident_blocks(nf4_unpack_words_any, kThreads);
     if (blocks > cap) blocks = cap;
-    nf4_unpack_words<false><<<(unsigned)blocks, kThreads, 0, stream>>>(job);
+    nf4_unpack_words_any<<<(unsigned)blocks, kThreads, 0, stream>>>(job);
   } else {
     static int cap = resident_blocks(nf4_unpack_bytes, kThreads);
     if (blocks > cap) blocks = cap;

@@ -4,9 +4,9 @@
 - gate and up are one GEMM against both weights unpacked into one [2*inter, hidden] buffer
   (one tb_nf4_unpack_multi launch);
 - tb_swiglu_fwd reads the fp16 [tokens, 2*inter] result and writes silu(g)*u in fp16;
-- nothing of size [tokens, inter] is saved: backward recomputes gate/up from the saved fp16 input
-  (one GEMM) and tb_swiglu_bwd_inplace turns the incoming gradient into the gate/up gradients in
-  place, so the input gradient is again a single GEMM.
+- the fp16 gate|up output is saved for backward (RECOMPUTE_GATE_UP = False; the reference
+  recomputes it from the saved input), and tb_swiglu_bwd_inplace turns the incoming gradient into
+  the gate/up gradients in place, so the input gradient is again a single GEMM.
 """
 
 import torch
@@ -14,7 +14,11 @@ import torch
 from . import _lib
 from .nf4 import unpack_concat
 
-RECOMPUTE_GATE_UP = True  # keep only the [tokens, hidden] input; recompute gate/up in backward
+# Save the fp16 gate|up GEMM output [tokens, 2*inter] for backward (22 MB per Qwen2.5-1.5B
+# layer at 621 tokens) instead of recomputing it there as the reference does to save memory:
+# on a 180 GB B200 the memory is free and the recompute is a third of the layer's MLP GEMMs.
+# True restores the reference's recompute.
+RECOMPUTE_GATE_UP = False
 
 
 def _check_gu(gu, what):
@@ -86,6 +90,45 @@ class FusedNF4MLP(torch.autograd.Function):
         del dact
         grad_x = torch.matmul(gu, gate_up)
         return grad_x, None, None, None
+
+
+class LayerMLP(torch.autograd.Function):
+    """FusedNF4MLP on the operands of a LayerWeights: gate|up is operand g_gu, down g_down."""
+
+    @staticmethod
+    def forward(ctx, x, lw, g_gu, g_down):
+        ops = lw.operands(x.device)
+        gu = torch.matmul(x, ops[g_gu].t())
+        act = gated_silu(gu)
+        if RECOMPUTE_GATE_UP:
+            del gu
+            ctx.save_for_backward(x)
+        else:
+            ctx.save_for_backward(x, gu)
+        out = torch.matmul(act, ops[g_down].t())
+        ctx.lw, ctx.groups = lw, (g_gu, g_down)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        if not ctx.needs_input_grad[0]:
+            return None, None, None, None
+        ops = ctx.lw.operands(grad_out.device)
+        g_gu, g_down = ctx.groups
+        saved = ctx.saved_tensors
+        x = saved[0]
+        grad_out = grad_out.to(torch.float16)
+        dact = torch.matmul(grad_out, ops[g_down])
+        gu = torch.matmul(x, ops[g_gu].t()) if RECOMPUTE_GATE_UP else saved[1]
+        gated_silu_backward_(dact, gu)
+        del dact
+        grad_x = torch.matmul(gu, ops[g_gu])
+        return grad_x, None, None, None
+
+
+def layer_mlp(x, lw, g_gu, g_down):
+    _lib.require_cuda(x, what="layer_mlp")
+    return LayerMLP.apply(x.contiguous(), lw, g_gu, g_down)
 
 
 def fused_mlp(x, gate_w, up_w, down_w):

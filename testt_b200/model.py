@@ -8,13 +8,15 @@ else runs the original forward.
 
 Per decoder layer, with s the fp32 residual stream of the M real tokens:
     s, y, y_pad = add_rmsnorm(s, d)                 tb_add_rmsnorm_fwd (d: previous block, fp16)
-    qkv        = y @ [Wq; Wk; Wv]^T + b               tb_nf4_unpack_multi + one cuBLAS GEMM
+    W          = unpack(q|k|v, o, gate|up, down)      tb_nf4_unpack_multi, one launch per layer
+    qkv        = y @ [Wq; Wk; Wv]^T + b               cuBLAS
     lq, lv     = LoRA(dropout(y_pad))                 PyTorch, peft's math, same dropout draws
     q, k, v    = rope_tokens(qkv, lq, lv)             tb_rope_tokens_fwd, token-major [M, H, 128]
     a          = varlen causal attention(q, k, v)     PyTorch's flash kernels, GQA, per sequence
-    o          = a @ Wo^T                             tb_nf4_unpack_multi + cuBLAS
+    o          = a @ Wo^T                             cuBLAS
     s, y2, _   = add_rmsnorm(s, o)                    tb_add_rmsnorm_fwd
-    d          = mlp(y2)                              NF4 + cuBLAS + tb_swiglu_fwd
+    d          = mlp(y2)                              cuBLAS + tb_swiglu_fwd
+(backward unpacks the layer's weights again, once, in its first operation)
 then the final norm and the fused head (head.py). Pad tokens never enter the projections, norms,
 MLP, attention or head. Causal attention over each row's real tokens in column order is the
 unpatched model's causal + padding-mask attention restricted to the real query rows (the only
@@ -28,8 +30,8 @@ import threading
 import torch
 
 from .head import IGNORE_INDEX, fused_head_loss
-from .mlp import fused_mlp
-from .nf4 import frozen_linear
+from .mlp import layer_mlp
+from .nf4 import LayerWeights, layer_linear
 from .rmsnorm import add_rmsnorm
 from .rope import rope_pack, rope_tokens, slot_index
 
@@ -134,7 +136,7 @@ class LayerPlan:
     """The frozen weights and LoRA hooks of one decoder layer (reference: model.py:94-122)."""
 
     __slots__ = ("layer", "attn", "q", "k", "v", "o", "gate", "up", "down", "qkv_bias",
-                 "o_bias", "lora_modules")
+                 "o_bias", "lora_modules", "weights")
 
     def __init__(self, layer):
         self.layer = layer
@@ -149,6 +151,9 @@ class LayerPlan:
         q, k, v, o, gate, up, down = bases
         self.q, self.k, self.v, self.o = q.weight, k.weight, v.weight, o.weight
         self.gate, self.up, self.down = gate.weight, up.weight, down.weight
+        # the layer's GEMM operands, unpacked by one launch: 0 q|k|v, 1 o, 2 gate|up, 3 down
+        self.weights = LayerWeights(((self.q, self.k, self.v), (self.o,), (self.gate, self.up),
+                                     (self.down,)))
         if any(getattr(b, "bias", None) is not None for b in (gate, up, down)):
             raise ValueError("MLP bias")
         qkv_bias = [getattr(b, "bias", None) for b in (q, k, v)]
@@ -317,7 +322,10 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
         layer = lp.layer
         s, y, y_pad = add_rmsnorm(s, delta, layer.input_layernorm.weight,
                                   layer.input_layernorm.variance_epsilon, pos_idx, padded)
-        qkv = frozen_linear(y, (lp.q, lp.k, lp.v), lp.qkv_bias)
+        lw = lp.weights
+        lw.release()
+        lw.operands(dev)  # every NF4 weight of the layer, one unpack launch
+        qkv = layer_linear(y, lw, 0, lp.qkv_bias, last=True)
         lora_q = _lora_branch(lp.attn.q_proj, y_pad, batch, seq, pos_idx)
         lora_v = _lora_branch(lp.attn.v_proj, y_pad, batch, seq, pos_idx)
         del y_pad
@@ -336,11 +344,12 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
             attn = _attention(lp, q, k, v, mask)
             del q, k, v
             attn = attn.reshape(padded, plan.n_heads * plan.head_dim).index_select(0, pos_idx)
-        o = frozen_linear(attn, (lp.o,), lp.o_bias)
+        o = layer_linear(attn, lw, 1, lp.o_bias)
         del attn
         s, y2, _ = add_rmsnorm(s, o, layer.post_attention_layernorm.weight,
                                layer.post_attention_layernorm.variance_epsilon)
-        delta = fused_mlp(y2, lp.gate, lp.up, lp.down)
+        delta = layer_mlp(y2, lw, 2, 3)
+        lw.release()  # backward unpacks the layer again
         del y2, o
 
     _, y, _ = add_rmsnorm(s, delta, inner.norm.weight, inner.norm.variance_epsilon)

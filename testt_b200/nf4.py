@@ -55,6 +55,14 @@ def _tensors(weight):
     return ts
 
 
+def _norm_device(device):
+    """torch.device with its index ("cuda" means the current CUDA device)."""
+    device = torch.device(device)
+    if device.type == "cuda" and device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    return device
+
+
 def _on_device(weight, device):
     return all(t.device == device for t in _tensors(weight))
 
@@ -191,7 +199,7 @@ def weight_shape(weight):
 def unpack_concat(weights, device):
     """fp16 [sum N_i, K]: the weights stacked by rows, unpacked in one launch when every weight
     has a layout the kernel takes (reference: nf4.py:96-105)."""
-    device = torch.device(device)
+    device = _norm_device(device)
     rows = [weight_shape(w)[0] for w in weights]
     cols = weight_shape(weights[0])[1]
     out = torch.empty((sum(rows), cols), dtype=torch.float16, device=device)
@@ -207,6 +215,103 @@ def unpack_concat(weights, device):
         unpack_into(weight, out[start:start + n])
         start += n
     return out
+
+
+class _PreparedFlat:
+    """Launch arguments for weights of any shapes unpacked back to back into one flat fp16
+    buffer (weight i at element offset offsets[i]); built once, like _Prepared."""
+
+    def __init__(self, weights, device):
+        self.shapes = [weight_shape(w) for w in weights]
+        self.offsets = [0]
+        for r, c in self.shapes:
+            self.offsets.append(self.offsets[-1] + r * c)
+        self.total = self.offsets[-1]
+        dummy = torch.empty(0, dtype=torch.float16, device=device)
+        self.jobs = [_job(w, dummy) for w in weights]
+        self.parts = []
+        for start in range(0, len(weights), MAX_WEIGHTS_PER_LAUNCH):
+            part = self.jobs[start:start + MAX_WEIGHTS_PER_LAUNCH]
+            self.parts.append((start, len(part), _job_arrays(part)))
+        self.check = _Prepared._fingerprint(weights)
+
+    def run(self, buf):
+        base = buf.data_ptr()
+        stream = _lib.stream_of(buf)
+        for start, n, args in self.parts:
+            arr = args[8]
+            for i in range(n):
+                arr[i] = base + self.offsets[start + i] * 2
+            _lib.call("tb_nf4_unpack_multi", *args, stream)
+        return buf
+
+
+class LayerWeights:
+    """The frozen NF4 weights of one decoder layer as GEMM operands stacked by rows, e.g.
+    ((q, k, v), (o,), (gate, up), (down,)), unpacked together into one fp16 buffer by a single
+    tb_nf4_unpack_multi launch (up to MAX_WEIGHTS_PER_LAUNCH weights) and held until release().
+    One launch per layer instead of one per operand: the unpack of a 1.5B layer (94 MB of fp16)
+    runs as one long kernel instead of four short ones, each paying its launch, ramp and tail.
+    The forward of the layer unpacks and releases it; in backward the first operation that needs
+    an operand unpacks the whole layer again and the last one releases it."""
+
+    def __init__(self, groups):
+        self.groups = tuple(tuple(g) for g in groups)
+        self.flat = tuple(w for g in self.groups for w in g)
+        self._ops = None
+        self._prep = None
+
+    def _fast(self, device):
+        return device.type == "cuda" and len(self.flat) <= MAX_WEIGHTS_PER_LAUNCH and \
+            all(supports_fast_unpack(w) and _on_device(w, device) for w in self.flat)
+
+    def operands(self, device):
+        """fp16 [sum N, K] per group (views of one buffer), unpacked on first use."""
+        if self._ops is not None:
+            return self._ops
+        device = _norm_device(device)
+        if not self._fast(device):
+            self._ops = [unpack_concat(g, device) for g in self.groups]
+            return self._ops
+        prep = self._prep
+        if prep is None or prep.check != _Prepared._fingerprint(self.flat):
+            prep = self._prep = _PreparedFlat(self.flat, device)
+        buf = prep.run(torch.empty(prep.total, dtype=torch.float16, device=device))
+        ops, i = [], 0
+        for g in self.groups:
+            rows = sum(prep.shapes[i + k][0] for k in range(len(g)))
+            cols = prep.shapes[i][1]
+            ops.append(buf[prep.offsets[i]:prep.offsets[i] + rows * cols].view(rows, cols))
+            i += len(g)
+        self._ops = ops
+        return ops
+
+    def release(self):
+        self._ops = None
+
+
+class LayerLinear(torch.autograd.Function):
+    """y = x @ W^T (+ b) with W operand `group` of a LayerWeights; `last` marks the layer's
+    operation that runs last in backward (it releases the layer's unpacked weights)."""
+
+    @staticmethod
+    def forward(ctx, x, bias, lw, group, last):
+        out = torch.nn.functional.linear(x, lw.operands(x.device)[group], bias)
+        ctx.lw, ctx.group, ctx.last = lw, group, last
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        grad_x = None
+        if ctx.needs_input_grad[0]:
+            grad_x = grad_out.to(torch.float16) @ ctx.lw.operands(grad_out.device)[ctx.group]
+        if ctx.last:
+            ctx.lw.release()
+        return grad_x, None, None, None, None
+
+
+def layer_linear(x, lw, group, bias=None, last=False):
+    return LayerLinear.apply(x, bias, lw, group, last)
 
 
 class FrozenNF4Linear(torch.autograd.Function):
