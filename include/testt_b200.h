@@ -142,6 +142,29 @@ int tb_slot_index(const int64_t *pos_idx, int64_t rows, int64_t slots, int32_t *
                   void *stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * LoRA branches of q_proj / v_proj around PyTorch's dropout (the reference's _lora_branch,
+ * solution/model.py:195-206: lora_B(lora_A(dropout(x_pad))) * scaling on the real tokens; no
+ * kernel of its own there: index_select, casts, index_add and dropout backward in PyTorch).
+ * ------------------------------------------------------------------------------------------- */
+
+/* x16[r] = fp16(dropped[pos_idx[r]]) for each of q and v (either pair nullable): the real rows of
+ * the fp32 dropout outputs [slots, hidden] gathered and cast to fp16 [rows, hidden], the input
+ * lora_A reads under fp16 autocast. */
+int tb_lora_gather(const float *dropped_q, const float *dropped_v, const int64_t *pos_idx,
+                   uint16_t *xq, uint16_t *xv, int64_t rows, int64_t hidden, void *stream);
+
+/* The padded gradient of the dropout input both adapters share, fp32 [slots, hidden]:
+ * grad[p] = fp32(dxq[t]) * scale_q * mask_q[p] + fp32(dxv[t]) * scale_v * mask_v[p] for the token
+ * t = slot_tok[p], 0 where slot_tok[p] < 0. dxq / dxv: fp16 [rows, hidden] gradients of the fp16
+ * lora_A inputs (nullable: that adapter is absent); mask_q / mask_v: the dropout keep masks
+ * (bool bytes [slots, hidden]; nullable: no dropout, the gradient passes unscaled); scale =
+ * 1 / (1 - p) as the dropout backward takes it. Each product and the sum rounded on its own. */
+int tb_lora_dropout_grad(const uint16_t *dxq, const uint16_t *dxv, const uint8_t *mask_q,
+                         const uint8_t *mask_v, const int32_t *slot_tok, float *grad,
+                         int64_t slots, int64_t hidden, float scale_q, float scale_v,
+                         void *stream);
+
+/* ---------------------------------------------------------------------------------------------
  * Gated SiLU. Replaces gated_silu_fwd_kernel / gated_silu_bwd_inplace_kernel,
  * solution/mlp.py:31-58 and :61-77.
  *   gu fp16 [rows, 2*inter] = [gate | up];  act = fp16(gate / (1 + exp(-gate)) * up)

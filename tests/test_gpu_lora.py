@@ -1,0 +1,101 @@
+"""The LoRA pair node (lora.lora_pair: PyTorch dropout + tb_lora_gather + cuBLAS, backward through
+tb_lora_dropout_grad) against the reference's per-adapter composition (solution/model.py:195-206:
+dropout on the padded fp32 norm output, index_select of the real rows, lora_A, lora_B, scaling,
+under fp16 autocast): the same dropout draws, outputs and gradients of the padded input and of
+both adapters' weights."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _adapters(hidden, outs, r, seed):
+    g = torch.Generator().manual_seed(seed)
+    mods = []
+    for out, scaling in zip(outs, (2.0, 0.5)):
+        a = torch.nn.Linear(hidden, r, bias=False)
+        b = torch.nn.Linear(r, out, bias=False)
+        with torch.no_grad():
+            a.weight.copy_(torch.randn(r, hidden, generator=g) * 0.05)
+            b.weight.copy_(torch.randn(out, r, generator=g) * 0.05)
+        mods.append((torch.nn.Dropout(0.05), a.to(DEV), b.to(DEV), scaling))
+    return mods
+
+
+def _reference(parts, x_pad, pos_idx, batch, seq):
+    outs = []
+    for dropout, a, b, scaling in parts:
+        hidden = x_pad.shape[-1]
+        dropped = dropout(x_pad.view(batch, seq, hidden)).view(batch * seq, hidden)
+        outs.append(b(a(dropped.index_select(0, pos_idx))) * scaling)
+    return outs
+
+
+@pytest.mark.parametrize("dropout_on", [True, False])
+def test_lora_pair_matches_per_adapter_composition(dropout_on):
+    from testt_b200.lora import lora_pair
+    from testt_b200.rope import slot_index
+
+    batch, seq, hidden, r = 3, 40, 256, 16
+    gen = torch.Generator().manual_seed(2)
+    lengths = [33, 7, 40]
+    pos = torch.cat([torch.arange(n) + i * seq for i, n in enumerate(lengths)]).to(DEV)
+    slot = slot_index(pos, batch * seq)
+    x0 = torch.randn(batch * seq, hidden, generator=gen).to(DEV)
+    parts = _adapters(hidden, (hidden, 64), r, 3)
+    for d, *_ in parts:
+        d.train(dropout_on)
+    gq = (torch.randn(pos.numel(), hidden, generator=gen) * 0.1).half().to(DEV)
+    gv = (torch.randn(pos.numel(), 64, generator=gen) * 0.1).half().to(DEV)
+
+    results = []
+    for fused in (False, True):
+        x = x0.clone().requires_grad_(True)
+        for _, a, b, _ in parts:
+            a.weight.grad = None
+            b.weight.grad = None
+        torch.manual_seed(77)
+        with torch.autocast(DEV, dtype=torch.float16):
+            if fused:
+                lq, lv = lora_pair(parts[0], parts[1], x, pos, slot)
+            else:
+                lq, lv = _reference(parts, x, pos, batch, seq)
+        torch.autograd.backward([lq, lv], [gq, gv])
+        results.append((lq.detach(), lv.detach(), x.grad.clone(),
+                        [t.weight.grad.clone() for _, a, b, _ in parts for t in (a, b)]))
+    (rq, rv, rx, rw), (fq, fv, fx, fw) = results
+    assert fq.dtype == torch.float16 and fv.dtype == torch.float16
+    torch.testing.assert_close(fq, rq, rtol=1e-3, atol=1e-4)
+    torch.testing.assert_close(fv, rv, rtol=1e-3, atol=1e-4)
+    torch.testing.assert_close(fx, rx, rtol=1e-3, atol=1e-5)
+    pad = torch.ones(batch * seq, dtype=torch.bool, device=DEV)
+    pad[pos] = False
+    assert torch.all(fx[pad] == 0)
+    for f, ref in zip(fw, rw):
+        torch.testing.assert_close(f, ref, rtol=1e-3, atol=1e-5)
+
+
+def test_lora_pair_one_adapter_only():
+    """LoRA on q_proj only: the v output is None and the padded gradient is q's alone."""
+    from testt_b200.lora import lora_pair
+    from testt_b200.rope import slot_index
+
+    batch, seq, hidden = 2, 16, 128
+    pos = torch.tensor([0, 1, 2, 16, 17], device=DEV)
+    slot = slot_index(pos, batch * seq)
+    parts = _adapters(hidden, (hidden, hidden), 8, 4)
+    x = torch.randn(batch * seq, hidden, device=DEV, requires_grad=True)
+    torch.manual_seed(5)
+    with torch.autocast(DEV, dtype=torch.float16):
+        lq, lv = lora_pair(parts[0], None, x, pos, slot)
+    assert lv is None and lq.shape == (5, hidden)
+    lq.float().sum().backward()
+    x2 = x.detach().clone().requires_grad_(True)
+    torch.manual_seed(5)
+    with torch.autocast(DEV, dtype=torch.float16):
+        (rq,) = _reference(parts[:1], x2, pos, batch, seq)
+    rq.float().sum().backward()
+    torch.testing.assert_close(lq, rq, rtol=1e-3, atol=1e-4)
+    torch.testing.assert_close(x.grad, x2.grad, rtol=1e-3, atol=1e-5)

@@ -94,7 +94,7 @@ __device__ __forceinline__ uint4 decode_word(uint32_t word, float scale, uint32_
 }
 
 #ifndef TB_NF4_SPANS
-#define TB_NF4_SPANS 4
+#define TB_NF4_SPANS 2
 #endif
 constexpr int kSpansPerWarp = TB_NF4_SPANS;  // spans a warp is sized to take (grid sizing)
 

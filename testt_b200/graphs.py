@@ -67,7 +67,7 @@ class GraphedTrainStep:
 
     def _step(self, e, counts):
         self.bucket.zero()
-        slot = None if e.cu is not None else slot_index(e.pos, e.ids.numel())
+        slot = slot_index(e.pos, e.ids.numel())
         with StaticBatch(e.pos, slot, e.mask4d, counts, e.cu, e.max_len), \
                 torch.autocast("cuda", dtype=torch.float16), _FusedRequest():
             out = self.model(input_ids=e.ids, attention_mask=e.mask, labels=e.labels,

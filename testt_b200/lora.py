@@ -1,0 +1,128 @@
+"""The LoRA branches of q_proj and v_proj as one autograd node (reference: solution/model.py:195-206,
+_lora_branch).
+
+peft computes lora_B(lora_A(dropout(x))) * scaling per adapter. On the fused path x is the
+padded fp32 norm output [batch * seq, hidden], the tensor the unpatched model feeds the adapter,
+so PyTorch's dropout draws the same mask; only the real tokens go on to lora_A. Under fp16
+autocast lora_A's input and both adapter weights are cast to fp16. This node keeps exactly those
+operations and their roundings, and replaces the glue around the dropout with two kernels:
+
+    forward   dq, mq = dropout_q(x); dv, mv = dropout_v(x)       PyTorch (same random draws)
+              xq16, xv16 = fp16(dq[pos_idx]), fp16(dv[pos_idx])   tb_lora_gather (one launch)
+              lora_q = (xq16 @ Aq16^T) @ Bq16^T * scaling_q         cuBLAS, fp16 (same for v)
+    backward  the adapter GEMM gradients as autograd computes them, then
+              dx_pad = dropout_q'(dxq) + dropout_v'(dxv) at the real rows, 0 at padding
+                                                                   tb_lora_dropout_grad
+instead of (per adapter) index_select + cast in forward and zero-fill + index_add + dropout
+backward + the sum of the two in backward.
+"""
+
+import torch
+
+from . import _lib
+
+_F16 = torch.float16
+
+
+def _dropout_of(module_dropout):
+    """(p, training) of a peft dropout module (nn.Dropout or nn.Identity)."""
+    if isinstance(module_dropout, torch.nn.Dropout):
+        return float(module_dropout.p), bool(module_dropout.training)
+    return 0.0, False
+
+
+class LoraPair(torch.autograd.Function):
+    """(lora_q, lora_v) fp16 [rows, out] for the real rows of x_pad; either adapter may be
+    absent (its weights None)."""
+
+    @staticmethod
+    def forward(ctx, x_pad, aq, bq, av, bv, pos_idx, slot_tok, cfg):
+        (pq, on_q, sq), (pv, on_v, sv) = cfg
+        rows = pos_idx.numel()
+        hidden = x_pad.shape[1]
+        with torch.autocast("cuda", enabled=False):
+            drops = []
+            for a, p, on in ((aq, pq, on_q), (av, pv, on_v)):
+                if a is None:
+                    drops.append((None, None))
+                elif on and p > 0.0:
+                    drops.append(torch.ops.aten.native_dropout(x_pad, p, True))
+                else:
+                    drops.append((x_pad, None))
+            (dq, mq), (dv, mv) = drops
+            xq = torch.empty((rows, hidden), dtype=_F16, device=x_pad.device) \
+                if aq is not None else None
+            xv = torch.empty((rows, hidden), dtype=_F16, device=x_pad.device) \
+                if av is not None else None
+            if rows and (xq is not None or xv is not None):
+                _lib.call("tb_lora_gather", _lib.ptr(dq), _lib.ptr(dv), _lib.ptr(pos_idx),
+                          _lib.ptr(xq), _lib.ptr(xv), rows, hidden, _lib.stream_of(x_pad))
+            del dq, dv
+            outs, saved = [], []
+            for x16, a, b, s in ((xq, aq, bq, sq), (xv, av, bv, sv)):
+                if a is None:
+                    outs.append(None)
+                    saved += [None, None, None, None]
+                    continue
+                a16, b16 = a.to(_F16), b.to(_F16)
+                h = x16 @ a16.t()
+                outs.append((h @ b16.t()) * s)
+                saved += [x16, h, a16, b16]
+        ctx.save_for_backward(pos_idx, slot_tok, mq, mv, *saved)
+        ctx.cfg = cfg
+        ctx.slots = x_pad.shape[0]
+        ctx.hidden = hidden
+        return outs[0], outs[1]
+
+    @staticmethod
+    def backward(ctx, gq_out, gv_out):
+        pos_idx, slot_tok, mq, mv, xq, hq, aq16, bq16, xv, hv, av16, bv16 = ctx.saved_tensors
+        (pq, on_q, sq), (pv, on_v, sv) = ctx.cfg
+        need = ctx.needs_input_grad
+        with torch.autocast("cuda", enabled=False):
+            grads = []
+            dxs = []
+            for g_out, x16, h, a16, b16, s in ((gq_out, xq, hq, aq16, bq16, sq),
+                                               (gv_out, xv, hv, av16, bv16, sv)):
+                if x16 is None:
+                    grads += [None, None]
+                    dxs.append(None)
+                    continue
+                if g_out is None:
+                    g_out = torch.zeros((x16.shape[0], b16.shape[0]), dtype=_F16,
+                                        device=x16.device)
+                g = g_out.to(_F16) * s          # backward of "* scaling"
+                db = (g.t() @ h).float()        # lora_B weight gradient (fp16 GEMM, cast back)
+                dh = g @ b16
+                da = (dh.t() @ x16).float()     # lora_A weight gradient
+                dxs.append(dh @ a16 if need[0] else None)
+                grads += [da, db]
+            gx = None
+            if need[0]:
+                gx = torch.empty((ctx.slots, ctx.hidden), dtype=torch.float32,
+                                 device=slot_tok.device)
+                scale_q = float(1.0 / (1.0 - pq)) if mq is not None else 1.0
+                scale_v = float(1.0 / (1.0 - pv)) if mv is not None else 1.0
+                _lib.call("tb_lora_dropout_grad", _lib.ptr(dxs[0]), _lib.ptr(dxs[1]),
+                          _lib.ptr(mq), _lib.ptr(mv), _lib.ptr(slot_tok), _lib.ptr(gx),
+                          ctx.slots, ctx.hidden, scale_q, scale_v, _lib.stream_of(gx))
+        return (gx, grads[0], grads[1], grads[2], grads[3], None, None, None)
+
+
+def lora_pair(parts_q, parts_v, x_pad, pos_idx, slot_tok):
+    """(lora_q, lora_v) for peft adapter parts (dropout, lora_A, lora_B, scaling) or None per
+    projection; None when neither projection has an adapter."""
+    if parts_q is None and parts_v is None:
+        return None, None
+    _lib.require_cuda(x_pad, pos_idx, slot_tok, what="lora_pair")
+    cfg, weights = [], []
+    for parts in (parts_q, parts_v):
+        if parts is None:
+            cfg.append((0.0, False, 1.0))
+            weights += [None, None]
+            continue
+        dropout, lora_a, lora_b, scaling = parts
+        p, on = _dropout_of(dropout)
+        cfg.append((p, on, float(scaling)))
+        weights += [lora_a.weight, lora_b.weight]
+    return LoraPair.apply(x_pad.contiguous(), *weights, pos_idx, slot_tok, tuple(cfg))

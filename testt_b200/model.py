@@ -10,7 +10,8 @@ Per decoder layer, with s the fp32 residual stream of the M real tokens:
     s, y, y_pad = add_rmsnorm(s, d)                 tb_add_rmsnorm_fwd (d: previous block, fp16)
     W          = unpack(q|k|v, o, gate|up, down)      tb_nf4_unpack_multi, one launch per layer
     qkv        = y @ [Wq; Wk; Wv]^T + b               cuBLAS
-    lq, lv     = LoRA(dropout(y_pad))                 PyTorch, peft's math, same dropout draws
+    lq, lv     = LoRA(dropout(y_pad))                 lora.lora_pair: PyTorch dropout (same draws),
+                                                      tb_lora_gather, cuBLAS; tb_lora_dropout_grad
     q, k, v    = rope_tokens(qkv, lq, lv)             tb_rope_tokens_fwd, token-major [M, H, 128]
     a          = varlen causal attention(q, k, v)     PyTorch's flash kernels, GQA, per sequence
     o          = a @ Wo^T                             cuBLAS
@@ -33,6 +34,7 @@ from .head import IGNORE_INDEX, fused_head_loss
 from .mlp import layer_mlp
 from .nf4 import LayerWeights, layer_linear
 from .rmsnorm import add_rmsnorm
+from .lora import lora_pair
 from .rope import rope_pack, rope_tokens, slot_index
 
 try:
@@ -244,19 +246,6 @@ def can_run(causal_lm, input_ids, attention_mask, labels, extra):
     return True
 
 
-def _lora_branch(module, y_pad, batch, seq, pos_idx):
-    """peft's lora_B(lora_A(dropout(x))) * scaling for the real tokens, where x is the padded
-    fp32 norm output the unpatched model feeds it (same shape and dtype, hence the same dropout
-    draws); A and B then run on the real tokens only (reference: model.py:195-206)."""
-    parts = _lora_parts(module)
-    if parts is None:
-        return None
-    dropout, lora_a, lora_b, scaling = parts
-    hidden = y_pad.shape[-1]
-    dropped = dropout(y_pad.view(batch, seq, hidden)).view(batch * seq, hidden)
-    return lora_b(lora_a(dropped.index_select(0, pos_idx))) * scaling
-
-
 def sequence_offsets(attention_mask):
     """(cu_seqlens int32 [batch + 1], longest row) of the real tokens of each row: the packed
     sequences of variable-length attention, in pos_idx order. The offsets stay on the mask's
@@ -290,10 +279,9 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
     varlen = USE_VARLEN_ATTENTION and (static is None or static.cu_seqlens is not None)
     if static is None:
         pos_idx = attention_mask.reshape(-1).nonzero().squeeze(1)   # sorted, one host sync
+        slot_tok = slot_index(pos_idx, padded)                      # shared by every layer
         if varlen:
             cu_seqlens, max_len = sequence_offsets(attention_mask)  # one more host sync
-        else:
-            slot_tok = slot_index(pos_idx, padded)                  # shared by every layer
     else:
         pos_idx, slot_tok = static.pos_idx, static.slot_tok
         cu_seqlens, max_len = static.cu_seqlens, static.max_len
@@ -320,14 +308,16 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
     delta = None
     for lp in plan.layers:
         layer = lp.layer
+        # y_pad's padding rows only reach dropout outputs that are never gathered: not zeroed
         s, y, y_pad = add_rmsnorm(s, delta, layer.input_layernorm.weight,
-                                  layer.input_layernorm.variance_epsilon, pos_idx, padded)
+                                  layer.input_layernorm.variance_epsilon, pos_idx, padded,
+                                  zero_padding=False)
         lw = lp.weights
         lw.release()
         lw.operands(dev)  # every NF4 weight of the layer, one unpack launch
         qkv = layer_linear(y, lw, 0, lp.qkv_bias, last=True)
-        lora_q = _lora_branch(lp.attn.q_proj, y_pad, batch, seq, pos_idx)
-        lora_v = _lora_branch(lp.attn.v_proj, y_pad, batch, seq, pos_idx)
+        lora_q, lora_v = lora_pair(_lora_parts(lp.attn.q_proj), _lora_parts(lp.attn.v_proj),
+                                   y_pad, pos_idx, slot_tok)
         del y_pad
         if varlen:
             q, k, v = rope_tokens(qkv, lora_q, lora_v, cos, sin, pos_idx, batch, seq,

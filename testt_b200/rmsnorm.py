@@ -69,8 +69,8 @@ class AddRMSNorm(torch.autograd.Function):
     """(s, y16, ypad32) = (x + delta, norm(x + delta) in fp16, the same in fp32 at padded rows)."""
 
     @staticmethod
-    def forward(ctx, x, delta, weight, eps, pad_idx, padded_rows):
-        s, y, ypad, rstd = _launch_fwd(x, delta, weight, eps, pad_idx, padded_rows)
+    def forward(ctx, x, delta, weight, eps, pad_idx, padded_rows, ypad=None):
+        s, y, ypad, rstd = _launch_fwd(x, delta, weight, eps, pad_idx, padded_rows, ypad)
         ctx.save_for_backward(s, rstd, weight, pad_idx)
         return s, y, ypad
 
@@ -79,17 +79,17 @@ class AddRMSNorm(torch.autograd.Function):
         s, rstd, weight, pad_idx = ctx.saved_tensors
         need_x, need_delta = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
         if not (need_x or need_delta):
-            return None, None, None, None, None, None
+            return None, None, None, None, None, None, None
         dx, ddelta = _launch_bwd(s, rstd, weight, pad_idx, grad_s, grad_y, grad_ypad, need_delta)
-        return (dx if need_x else None), ddelta, None, None, None, None
+        return (dx if need_x else None), ddelta, None, None, None, None, None
 
 
 class RMSNormNoAdd(torch.autograd.Function):
     """(y16, ypad32) = norm(x) without a residual add (the first layer's input norm)."""
 
     @staticmethod
-    def forward(ctx, x, weight, eps, pad_idx, padded_rows):
-        _s, y, ypad, rstd = _launch_fwd(x, None, weight, eps, pad_idx, padded_rows)
+    def forward(ctx, x, weight, eps, pad_idx, padded_rows, ypad=None):
+        _s, y, ypad, rstd = _launch_fwd(x, None, weight, eps, pad_idx, padded_rows, ypad)
         ctx.save_for_backward(x, rstd, weight, pad_idx)
         return y, ypad
 
@@ -97,15 +97,20 @@ class RMSNormNoAdd(torch.autograd.Function):
     def backward(ctx, grad_y, grad_ypad):
         x, rstd, weight, pad_idx = ctx.saved_tensors
         if not ctx.needs_input_grad[0]:
-            return None, None, None, None, None
+            return None, None, None, None, None, None
         dx, _ = _launch_bwd(x, rstd, weight, pad_idx, None, grad_y, grad_ypad, False)
-        return dx, None, None, None, None
+        return dx, None, None, None, None, None
 
 
-def add_rmsnorm(x, delta, weight, eps, pad_idx=None, padded_rows=0):
-    """Returns (s, y16, ypad32); with delta=None, s is x itself (reference: rmsnorm.py:152-158)."""
+def add_rmsnorm(x, delta, weight, eps, pad_idx=None, padded_rows=0, zero_padding=True):
+    """Returns (s, y16, ypad32); with delta=None, s is x itself (reference: rmsnorm.py:152-158).
+    zero_padding=False leaves the rows of ypad that pad_idx does not name unwritten (for a
+    caller that never reads them)."""
     x = x.contiguous()
+    ypad = None
+    if pad_idx is not None and not zero_padding:
+        ypad = torch.empty((padded_rows, x.shape[1]), dtype=torch.float32, device=x.device)
     if delta is None:
-        y, ypad = RMSNormNoAdd.apply(x, weight, eps, pad_idx, padded_rows)
+        y, ypad = RMSNormNoAdd.apply(x, weight, eps, pad_idx, padded_rows, ypad)
         return x, y, ypad
-    return AddRMSNorm.apply(x, delta.contiguous(), weight, eps, pad_idx, padded_rows)
+    return AddRMSNorm.apply(x, delta.contiguous(), weight, eps, pad_idx, padded_rows, ypad)
