@@ -551,6 +551,13 @@ def kernel_bench(name, steps, warmup, device):
             _lib.stream_of(part))
         nbytes = 0
         info = {"config": "4", "rows": rows, "flops": 2 * rows * hidden * vocab}
+    elif name == "head_cublas":  # the plain cuBLAS logits GEMM of config 4, for comparison
+        c = synth.config4(dev)
+        rows, hidden, vocab = 2048, synth.HIDDEN, synth.VOCAB
+        logits = torch.empty((rows, vocab), dtype=torch.float16, device=dev)
+        fn = lambda: torch.matmul(c["hidden"], c["weight"].t(), out=logits)  # noqa: E731
+        nbytes = 0
+        info = {"config": "4", "rows": rows, "flops": 2 * rows * hidden * vocab}
     elif name == "head_stats":
         c = synth.config4(dev, rows=256)
         logits = c["hidden"] @ c["weight"].t()
@@ -787,7 +794,7 @@ def main():
     ap.add_argument("--kernel", default=None,
                     help="time one kernel at its configuration instead (nf4, nf4_nested, "
                          "rmsnorm_fwd, rmsnorm_bwd, rope_fwd, rope_bwd, swiglu_fwd, swiglu_bwd, "
-                         "head_stats, head_tc, all)")
+                         "head_stats, head_tc, head_cublas, all)")
     args = ap.parse_args()
     if args.kernel:
         names = ["nf4", "nf4_nested", "rmsnorm_fwd", "rmsnorm_bwd", "rope_fwd", "rope_bwd",
