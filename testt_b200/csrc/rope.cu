@@ -47,47 +47,106 @@ __device__ __forceinline__ int64_t head_row(bool tokens, int64_t tok, int64_t b,
   return tokens ? (tok * heads + h) * (int64_t)D : ((b * heads + h) * seq + t) * (int64_t)D;
 }
 
-// kSlots: one CTA per padded slot, tokens found through slot_tok, padding rows zero-filled.
-// kTokens (with kSlots false): token-major outputs.
-template <bool kSlots, bool kLoraFp32, bool kTokens>
+// The token's q/k/v inputs of head row hr (qkv row, plus the LoRA row for q and v), in fp32.
+template <bool kLoraFp32>
+__device__ __forceinline__ void load_head_row(const uint16_t *qkv, const void *lq, const void *lv,
+                                              const RopeDims &dm, int64_t tok, int hr, int d0,
+                                              float (&x1)[8], float (&x2)[8]) {
+  const int D = dm.d, H = dm.half;
+  const uint16_t *row = qkv + tok * (int64_t)(dm.nh + 2 * dm.nkv) * D + (int64_t)hr * D;
+  load8h(row + d0, x1);
+  load8h(row + H + d0, x2);
+  const void *l = nullptr;
+  int64_t li = 0;
+  if (hr < dm.nh) {
+    l = lq;
+    li = tok * ((int64_t)dm.nh * D) + (int64_t)hr * D;
+  } else if (hr >= dm.nh + dm.nkv) {
+    l = lv;
+    li = tok * ((int64_t)dm.nkv * D) + (int64_t)(hr - dm.nh - dm.nkv) * D;
+  }
+  if (l != nullptr) {
+    float a[8], c[8];
+    load8_lora<kLoraFp32>(l, li + d0, a);
+    load8_lora<kLoraFp32>(l, li + H + d0, c);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) { x1[e] = x1[e] + a[e]; x2[e] = x2[e] + c[e]; }
+  }
+}
+
+// Zero rows of the padding slots (slot_tok < 0) among slots [p0, p1): a warp per slot, the
+// warp's slots p0 + warp + i * nwarps; lane i reads slot i's token, so memory is waited on once.
+__device__ __forceinline__ void zero_padding(const int32_t *__restrict__ slot_tok, uint16_t *q,
+                                             uint16_t *k, uint16_t *v, const RopeDims &dm,
+                                             const FastDiv &seq_div, int64_t p0, int64_t p1) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const int D = dm.d, total = dm.nh + 2 * dm.nkv, vpr = D / 8;  // 16-byte stores per head row
+  float zero[8];
+  zero8(zero);
+  for (int64_t base = p0 + warp; base < p1; base += 32LL * nwarps) {
+    const int64_t mine = base + (int64_t)lane * nwarps;
+    const int32_t tok_l = mine < p1 ? __ldg(slot_tok + mine) : 0;
+    for (int i = 0; i < 32; ++i) {
+      const int64_t p = base + (int64_t)i * nwarps;
+      if (p >= p1) break;
+      if (__shfl_sync(0xffffffffu, tok_l, i) >= 0) continue;  // a token's slot: its CTA writes it
+      uint32_t b32, t32;
+      seq_div.divmod((uint32_t)p, b32, t32);
+      const int64_t b = b32, t = t32;
+      for (int j = lane; j < total * vpr; j += 32) {
+        const int hr = j / vpr, c = (j - hr * vpr) * 8;
+        uint16_t *dst;
+        if (hr < dm.nh) dst = q + head_row(false, 0, b, t, dm.nh, hr, dm.seq, D);
+        else if (hr < dm.nh + dm.nkv) dst = k + head_row(false, 0, b, t, dm.nkv, hr - dm.nh, dm.seq, D);
+        else dst = v + head_row(false, 0, b, t, dm.nkv, hr - dm.nh - dm.nkv, dm.seq, D);
+        store8h(dst + c, zero);
+      }
+    }
+  }
+}
+
+// One CTA per token (blockIdx < rows). Its input rows do not depend on its position, so they
+// are loaded before the position arrives; the rotary rows of the position come after (a 512 KB
+// table, L2-resident after the first tokens). With a slot map every CTA also zeroes the padding
+// slots of its own range of zero_chunk slots (the grid covers them when there are more ranges
+// than tokens), so the padding costs no CTAs or waves of its own. kTokens: token-major outputs.
+template <bool kLoraFp32, bool kTokens>
 __global__ void __launch_bounds__(kMaxThreads)
     rope_fwd_vec(const uint16_t *__restrict__ qkv, const void *__restrict__ lq,
                  const void *__restrict__ lv, const float *__restrict__ cosv,
                  const float *__restrict__ sinv, const int64_t *__restrict__ pos_idx,
                  const int32_t *__restrict__ slot_tok, uint16_t *__restrict__ q,
-                 uint16_t *__restrict__ k, uint16_t *__restrict__ v, RopeDims dm, FastDiv seq_div) {
-  const int64_t unit = blockIdx.x;
+                 uint16_t *__restrict__ k, uint16_t *__restrict__ v, RopeDims dm, FastDiv seq_div,
+                 int64_t zero_chunk) {
   const int64_t slots = dm.batch * dm.seq;
-  int64_t tok, pos;
-  if (kSlots) {
-    pos = unit;
-    tok = __ldg(slot_tok + unit);
-  } else {
-    tok = unit;
-    pos = __ldg(pos_idx + unit);
-    if (pos < 0 || pos >= slots) return;  // out-of-range position: nothing to write
-  }
-  uint32_t b32, t32;
-  seq_div.divmod((uint32_t)pos, b32, t32);
-  const int64_t b = b32, t = t32;
   const int D = dm.d, H = dm.half;
+  const int total = dm.nh + 2 * dm.nkv;
+  if (slot_tok != nullptr) {
+    const int64_t p0 = (int64_t)blockIdx.x * zero_chunk;
+    if (p0 < slots) zero_padding(slot_tok, q, k, v, dm, seq_div, p0,
+                                 p0 + zero_chunk < slots ? p0 + zero_chunk : slots);
+  }
+  if ((int64_t)blockIdx.x >= dm.rows) return;
   const int lph = H / 8;                    // threads per head row
   const int rows_per_pass = blockDim.x / lph;
   if ((int)threadIdx.x >= rows_per_pass * lph) return;  // no __syncthreads below
+  const int64_t tok = blockIdx.x;
   const int d0 = (threadIdx.x % lph) * 8;
-  const int total = dm.nh + 2 * dm.nkv;
-  const bool real = !kSlots || (tok >= 0 && tok < dm.rows);
-
+  const int hr0 = threadIdx.x / lph;
+  const int64_t pos = __ldg(pos_idx + tok);
+  float x1[8], x2[8];
+  if (hr0 < total) load_head_row<kLoraFp32>(qkv, lq, lv, dm, tok, hr0, d0, x1, x2);
+  if (pos < 0 || pos >= slots) return;  // out-of-range position: nothing to write
+  uint32_t b32, t32;
+  seq_div.divmod((uint32_t)pos, b32, t32);
+  const int64_t b = b32, t = t32;
   float c1[8], c2[8], s1[8], s2[8];
-  if (real) {
-    load8f(cosv + t * D + d0, c1);
-    load8f(cosv + t * D + H + d0, c2);
-    load8f(sinv + t * D + d0, s1);
-    load8f(sinv + t * D + H + d0, s2);
-  }
-  const int64_t W = (int64_t)total * D;
-  for (int hr = threadIdx.x / lph; hr < total; hr += rows_per_pass) {
-    float x1[8], x2[8], o1[8], o2[8];
+  load8f(cosv + t * D + d0, c1);
+  load8f(cosv + t * D + H + d0, c2);
+  load8f(sinv + t * D + d0, s1);
+  load8f(sinv + t * D + H + d0, s2);
+  for (int hr = hr0; hr < total; hr += rows_per_pass) {
+    if (hr != hr0) load_head_row<kLoraFp32>(qkv, lq, lv, dm, tok, hr, d0, x1, x2);
     uint16_t *dst;
     if (hr < dm.nh) {
       dst = q + head_row(kTokens, tok, b, t, dm.nh, hr, dm.seq, D);
@@ -95,38 +154,11 @@ __global__ void __launch_bounds__(kMaxThreads)
       dst = k + head_row(kTokens, tok, b, t, dm.nkv, hr - dm.nh, dm.seq, D);
     } else {
       dst = v + head_row(kTokens, tok, b, t, dm.nkv, hr - dm.nh - dm.nkv, dm.seq, D);
-    }
-    if (!real) {
-      zero8(o1);
-      store8h(dst + d0, o1);
-      store8h(dst + H + d0, o1);
-      continue;
-    }
-    const uint16_t *row = qkv + tok * W + (int64_t)hr * D;
-    load8h(row + d0, x1);
-    load8h(row + H + d0, x2);
-    if (hr < dm.nh) {
-      if (lq != nullptr) {
-        float a[8], c[8];
-        const int64_t li = tok * ((int64_t)dm.nh * D) + (int64_t)hr * D;
-        load8_lora<kLoraFp32>(lq, li + d0, a);
-        load8_lora<kLoraFp32>(lq, li + H + d0, c);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) { x1[e] = x1[e] + a[e]; x2[e] = x2[e] + c[e]; }
-      }
-    } else if (hr >= dm.nh + dm.nkv) {
-      if (lv != nullptr) {
-        float a[8], c[8];
-        const int64_t li = tok * ((int64_t)dm.nkv * D) + (int64_t)(hr - dm.nh - dm.nkv) * D;
-        load8_lora<kLoraFp32>(lv, li + d0, a);
-        load8_lora<kLoraFp32>(lv, li + H + d0, c);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) { x1[e] = x1[e] + a[e]; x2[e] = x2[e] + c[e]; }
-      }
-      store8h(dst + d0, x1);
+      store8h(dst + d0, x1);  // v: LoRA-added, not rotated
       store8h(dst + H + d0, x2);
       continue;
     }
+    float o1[8], o2[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       o1[e] = x1[e] * c1[e] - x2[e] * s1[e];
@@ -145,15 +177,32 @@ __global__ void __launch_bounds__(kMaxThreads)
                  uint16_t *__restrict__ dqkv, RopeDims dm, FastDiv seq_div) {
   const int64_t tok = blockIdx.x;
   const int64_t slots = dm.batch * dm.seq;
-  const int64_t pos = __ldg(pos_idx + tok);
-  const bool inside = pos >= 0 && pos < slots;
-  uint32_t b32 = 0, t32 = 0;
-  if (inside) seq_div.divmod((uint32_t)pos, b32, t32);
-  const int64_t b = b32, t = t32;
   const int D = dm.d, H = dm.half;
   const int lph = H / 8, rows_per_pass = blockDim.x / lph, d0 = (threadIdx.x % lph) * 8;
   if ((int)threadIdx.x >= rows_per_pass * lph) return;  // no __syncthreads below
   const int total = dm.nh + 2 * dm.nkv;
+  const int hr0 = threadIdx.x / lph;
+  const int64_t pos = __ldg(pos_idx + tok);
+  // token-major gradients do not depend on the position: the first head row's are loaded
+  // while the position is in flight
+  float g1[8], g2[8];
+  bool have = false;
+  if (kTokens && hr0 < total) {
+    const uint16_t *src = hr0 < dm.nh ? (dq ? dq + head_row(true, tok, 0, 0, dm.nh, hr0, 0, D) : nullptr)
+                          : hr0 < dm.nh + dm.nkv
+                              ? (dk ? dk + head_row(true, tok, 0, 0, dm.nkv, hr0 - dm.nh, 0, D) : nullptr)
+                              : (dv ? dv + head_row(true, tok, 0, 0, dm.nkv, hr0 - dm.nh - dm.nkv, 0, D)
+                                    : nullptr);
+    if (src != nullptr) {
+      load8h(src + d0, g1);
+      load8h(src + H + d0, g2);
+      have = true;
+    }
+  }
+  const bool inside = pos >= 0 && pos < slots;
+  uint32_t b32 = 0, t32 = 0;
+  if (inside) seq_div.divmod((uint32_t)pos, b32, t32);
+  const int64_t b = b32, t = t32;
   float c1[8], c2[8], s1[8], s2[8];
   load8f(cosv + t * D + d0, c1);
   load8f(cosv + t * D + H + d0, c2);
@@ -161,7 +210,7 @@ __global__ void __launch_bounds__(kMaxThreads)
   load8f(sinv + t * D + H + d0, s2);
   const int64_t W = (int64_t)total * D;
   uint16_t *row = dqkv + tok * W;
-  for (int hr = threadIdx.x / lph; hr < total; hr += rows_per_pass) {
+  for (int hr = hr0; hr < total; hr += rows_per_pass) {
     const uint16_t *src;
     bool rotate = true;
     if (hr < dm.nh) {
@@ -173,10 +222,12 @@ __global__ void __launch_bounds__(kMaxThreads)
                : nullptr;
       rotate = false;
     }
-    float g1[8], g2[8], o1[8], o2[8];
+    float o1[8], o2[8];
     if (src != nullptr && inside) {
-      load8h(src + d0, g1);
-      load8h(src + H + d0, g2);
+      if (!(kTokens && hr == hr0 && have)) {
+        load8h(src + d0, g1);
+        load8h(src + H + d0, g2);
+      }
     } else {
       zero8(g1);
       zero8(g2);
@@ -364,21 +415,29 @@ int rope_fwd_launch(const char *what, bool tokens, const uint16_t *qkv, const vo
                    (!lora_q || aligned(lora_q, 16)) && (!lora_v || aligned(lora_v, 16));
   cudaStream_t st = as_stream(stream);
   if (vec) {
-    const unsigned blocks = (unsigned)units;
+    // one CTA per token; with a slot map each CTA also zeroes the padding of an equal range of
+    // slots (the grid grows past the tokens only when the ranges would exceed 32 slots a warp)
     const int threads = rope_threads(dm);
+    int64_t ctas = rows, zero_chunk = 1;
+    if (!tokens && slot_tok) {
+      const int64_t slots = batch * seq, cap = 32LL * (threads / 32);
+      zero_chunk = (slots + (rows > 0 ? rows : 1) - 1) / (rows > 0 ? rows : 1);
+      if (zero_chunk > cap) zero_chunk = cap;
+      const int64_t ranges = (slots + zero_chunk - 1) / zero_chunk;
+      if (ranges > ctas) ctas = ranges;
+    }
+    const unsigned blocks = (unsigned)ctas;
     const FastDiv sd((uint32_t)seq);
-#define TB_ROPE_FWD(S, F, T)                                                                    \
-  rope_fwd_vec<S, F, T><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx,  \
-                                                     slot_tok, q, k, v, dm, sd)
+    const int32_t *slots_map = tokens ? nullptr : slot_tok;
+#define TB_ROPE_FWD(F, T)                                                                       \
+  rope_fwd_vec<F, T><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx,     \
+                                                  slots_map, q, k, v, dm, sd, zero_chunk)
     if (tokens) {
-      if (lora_is_fp32) TB_ROPE_FWD(false, true, true);
-      else TB_ROPE_FWD(false, false, true);
-    } else if (slot_tok) {
-      if (lora_is_fp32) TB_ROPE_FWD(true, true, false);
-      else TB_ROPE_FWD(true, false, false);
+      if (lora_is_fp32) TB_ROPE_FWD(true, true);
+      else TB_ROPE_FWD(false, true);
     } else {
-      if (lora_is_fp32) TB_ROPE_FWD(false, true, false);
-      else TB_ROPE_FWD(false, false, false);
+      if (lora_is_fp32) TB_ROPE_FWD(true, false);
+      else TB_ROPE_FWD(false, false);
     }
 #undef TB_ROPE_FWD
   } else {
