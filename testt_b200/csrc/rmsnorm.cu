@@ -188,7 +188,9 @@ __global__ void rmsnorm_bwd_any(const float *s, const float *rstd_in, const floa
 }
 
 // Threads per row and chunks per thread for the vector kernels; NCH 0 = use the scalar kernel.
-void plan_rows(int64_t hidden, bool vec_ok, int &threads, int &nch) {
+// Rows get more chunks per thread while the grid would not fit in one wave of resident
+// threads (a second, partial wave costs a whole row-latency of its own).
+void plan_rows(int64_t hidden, int64_t rows, bool vec_ok, int &threads, int &nch) {
   if (!vec_ok || hidden % 8 != 0 || hidden > 8 * 8 * 1024) {
     threads = 256;
     nch = 0;
@@ -205,6 +207,11 @@ void plan_rows(int64_t hidden, bool vec_ok, int &threads, int &nch) {
     threads = 256;
     nch = 0;
     return;
+  }
+  const int64_t resident = (int64_t)sm_count() * 2048 * 7 / 8;
+  while (nch < 8 && rows * t > resident && (chunks + 2 * nch - 1) / (2 * nch) >= 32) {
+    nch *= 2;
+    t = (((chunks + nch - 1) / nch + 31) / 32) * 32;
   }
   threads = (int)t;
 }
@@ -230,7 +237,7 @@ extern "C" int tb_add_rmsnorm_fwd(const float *x, const uint16_t *delta, const f
                       (!delta || (aligned(delta, 16) && aligned(s_out, 16))) &&
                       (!ypad || aligned(ypad, 16));
   int threads, nch;
-  plan_rows(hidden, vec_ok, threads, nch);
+  plan_rows(hidden, rows, vec_ok, threads, nch);
   cudaStream_t st = as_stream(stream);
   const dim3 grid((unsigned)rows);
   switch (nch) {
@@ -258,7 +265,7 @@ extern "C" int tb_add_rmsnorm_bwd(const float *s, const float *rstd, const float
                       (!dy || aligned(dy, 16)) && (!dypad || aligned(dypad, 16)) &&
                       (!ds || aligned(ds, 16)) && (!ddelta || aligned(ddelta, 16));
   int threads, nch;
-  plan_rows(hidden, vec_ok, threads, nch);
+  plan_rows(hidden, rows, vec_ok, threads, nch);
   cudaStream_t st = as_stream(stream);
   const dim3 grid((unsigned)rows);
   switch (nch) {
