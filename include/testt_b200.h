@@ -153,6 +153,23 @@ int tb_slot_index(const int64_t *pos_idx, int64_t rows, int64_t slots, int32_t *
 int tb_lora_gather(const float *dropped_q, const float *dropped_v, const int64_t *pos_idx,
                    uint16_t *xq, uint16_t *xv, int64_t rows, int64_t hidden, void *stream);
 
+/* Both adapters' forward for rank-16 LoRA, per real row m (either adapter's pointers NULL when
+ * absent): x16[m] = fp16(dropped[pos_idx[m]]); h16[m] = fp16(x16[m] . a^T);
+ * out[m] = fp16(fp32(fp16(h16[m] . b^T)) * scale), fp32 accumulation. dropped: fp32
+ * [slots, hidden] dropout outputs; a: fp16 lora_A weight [16, hidden]; b: fp16 lora_B weight
+ * [hout, 16] (the autocast casts); x16 [rows, hidden], h16 [rows, 16] (kept for backward), out
+ * [rows, hout], fp16.
+ * hidden and hout multiples of 8 (at most 8192); 16-byte aligned buffers. Replaces lora_A,
+ * lora_B and "* scaling" under fp16 autocast with their weight casts (peft, called from
+ * solution/model.py:205), and the index_select + cast of tb_lora_gather. */
+int tb_lora_forward(const float *dropped_q, const uint16_t *a_q, const uint16_t *b_q,
+                    uint16_t *x16_q, uint16_t *h16_q, uint16_t *out_q, int64_t hout_q,
+                    float scale_q, const float *dropped_v, const uint16_t *a_v,
+                    const uint16_t *b_v, uint16_t *x16_v,
+                    uint16_t *h16_v, uint16_t *out_v, int64_t hout_v, float scale_v,
+                    const int64_t *pos_idx, int64_t rows, int64_t hidden, int32_t rank,
+                    void *stream);
+
 /* The padded gradient of the dropout input both adapters share, fp32 [slots, hidden]:
  * grad[p] = fp32(dxq[t]) * scale_q * mask_q[p] + fp32(dxv[t]) * scale_v * mask_v[p] for the token
  * t = slot_tok[p], 0 where slot_tok[p] < 0. dxq / dxv: fp16 [rows, hidden] gradients of the fp16

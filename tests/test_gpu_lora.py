@@ -67,14 +67,21 @@ def test_lora_pair_matches_per_adapter_composition(dropout_on):
                         [t.weight.grad.clone() for _, a, b, _ in parts for t in (a, b)]))
     (rq, rv, rx, rw), (fq, fv, fx, fw) = results
     assert fq.dtype == torch.float16 and fv.dtype == torch.float16
-    torch.testing.assert_close(fq, rq, rtol=1e-3, atol=1e-4)
-    torch.testing.assert_close(fv, rv, rtol=1e-3, atol=1e-4)
-    torch.testing.assert_close(fx, rx, rtol=1e-3, atol=1e-5)
+    # the same roundings (fp16 casts, fp16 GEMM outputs, the scaling product); only the fp32
+    # accumulation order of the rank-16 kernel differs from cuBLAS's, which can move an fp16
+    # result by an ulp (1e-3 relative): a few ulps of tolerance, and a mask mismatch would show
+    # as O(1) differences
+    torch.testing.assert_close(fq, rq, rtol=5e-3, atol=2e-4)
+    torch.testing.assert_close(fv, rv, rtol=5e-3, atol=2e-4)
+    torch.testing.assert_close(fx, rx, rtol=5e-3, atol=1e-5)
     pad = torch.ones(batch * seq, dtype=torch.bool, device=DEV)
     pad[pos] = False
     assert torch.all(fx[pad] == 0)
+    # weight gradients sum over the rows: an ulp of h16 in one row moves an element that
+    # cancels to near zero by more than its own rtol, so the absolute floor scales with the
+    # gradient's largest element
     for f, ref in zip(fw, rw):
-        torch.testing.assert_close(f, ref, rtol=1e-3, atol=1e-5)
+        torch.testing.assert_close(f, ref, rtol=5e-3, atol=float(ref.abs().max()) * 2e-3)
 
 
 def test_lora_pair_one_adapter_only():

@@ -8,8 +8,9 @@ autocast lora_A's input and both adapter weights are cast to fp16. This node kee
 operations and their roundings, and replaces the glue around the dropout with two kernels:
 
     forward   dq, mq = dropout_q(x); dv, mv = dropout_v(x)       PyTorch (same random draws)
-              xq16, xv16 = fp16(dq[pos_idx]), fp16(dv[pos_idx])   tb_lora_gather (one launch)
-              lora_q = (xq16 @ Aq16^T) @ Bq16^T * scaling_q         cuBLAS, fp16 (same for v)
+              xq16, xv16 = fp16(dq[pos_idx]), fp16(dv[pos_idx])
+              lora_q = (xq16 @ Aq16^T) @ Bq16^T * scaling_q         (same for v)
+              all of it one launch for rank 16 (tb_lora_forward), else tb_lora_gather + cuBLAS
     backward  the adapter GEMM gradients as autograd computes them, then
               dx_pad = dropout_q'(dxq) + dropout_v'(dxv) at the real rows, 0 at padding
                                                                    tb_lora_dropout_grad
@@ -22,6 +23,23 @@ import torch
 from . import _lib
 
 _F16 = torch.float16
+
+
+_RANK = 16  # the rank tb_lora_forward takes
+
+
+def _fused_ok(aq, bq, av, bv, hidden):
+    """Whether tb_lora_forward takes these adapters (rank 16, widths multiples of 8)."""
+    if hidden % 8 or hidden > 8192:
+        return False
+    for a, b in ((aq, bq), (av, bv)):
+        if a is None:
+            continue
+        if a.dim() != 2 or a.shape != (_RANK, hidden) or b.dim() != 2 or b.shape[1] != _RANK \
+                or b.shape[0] % 8 or b.shape[0] > 8192 or a.dtype != torch.float32 \
+                or b.dtype != torch.float32 or not (a.is_contiguous() and b.is_contiguous()):
+            return False
+    return True
 
 
 def _dropout_of(module_dropout):
@@ -50,24 +68,42 @@ class LoraPair(torch.autograd.Function):
                 else:
                     drops.append((x_pad, None))
             (dq, mq), (dv, mv) = drops
-            xq = torch.empty((rows, hidden), dtype=_F16, device=x_pad.device) \
-                if aq is not None else None
-            xv = torch.empty((rows, hidden), dtype=_F16, device=x_pad.device) \
-                if av is not None else None
-            if rows and (xq is not None or xv is not None):
-                _lib.call("tb_lora_gather", _lib.ptr(dq), _lib.ptr(dv), _lib.ptr(pos_idx),
-                          _lib.ptr(xq), _lib.ptr(xv), rows, hidden, _lib.stream_of(x_pad))
+            dev = x_pad.device
+            xq = torch.empty((rows, hidden), dtype=_F16, device=dev) if aq is not None else None
+            xv = torch.empty((rows, hidden), dtype=_F16, device=dev) if av is not None else None
+            if _fused_ok(aq, bq, av, bv, hidden):
+                # both adapters in one kernel: gather + cast, lora_A, lora_B, * scaling
+                outs, hs, w16 = [], [], []
+                for a, b in ((aq, bq), (av, bv)):
+                    outs.append(None if a is None else
+                                torch.empty((rows, b.shape[0]), dtype=_F16, device=dev))
+                    hs.append(None if a is None else
+                              torch.empty((rows, a.shape[0]), dtype=_F16, device=dev))
+                    w16 += [None, None] if a is None else [a.to(_F16), b.to(_F16)]
+                if rows:
+                    _lib.call("tb_lora_forward", _lib.ptr(dq), _lib.ptr(w16[0]),
+                              _lib.ptr(w16[1]), _lib.ptr(xq), _lib.ptr(hs[0]),
+                              _lib.ptr(outs[0]), bq.shape[0] if bq is not None else 0, sq,
+                              _lib.ptr(dv), _lib.ptr(w16[2]), _lib.ptr(w16[3]), _lib.ptr(xv),
+                              _lib.ptr(hs[1]), _lib.ptr(outs[1]),
+                              bv.shape[0] if bv is not None else 0, sv, _lib.ptr(pos_idx), rows,
+                              hidden, _RANK, _lib.stream_of(x_pad))
+                saved = [xq, hs[0], w16[0], w16[1], xv, hs[1], w16[2], w16[3]]
+            else:
+                if rows and (xq is not None or xv is not None):
+                    _lib.call("tb_lora_gather", _lib.ptr(dq), _lib.ptr(dv), _lib.ptr(pos_idx),
+                              _lib.ptr(xq), _lib.ptr(xv), rows, hidden, _lib.stream_of(x_pad))
+                outs, saved = [], []
+                for x16, a, b, s in ((xq, aq, bq, sq), (xv, av, bv, sv)):
+                    if a is None:
+                        outs.append(None)
+                        saved += [None, None, None, None]
+                        continue
+                    a16, b16 = a.to(_F16), b.to(_F16)
+                    h = x16 @ a16.t()
+                    outs.append((h @ b16.t()) * s)
+                    saved += [x16, h, a16, b16]
             del dq, dv
-            outs, saved = [], []
-            for x16, a, b, s in ((xq, aq, bq, sq), (xv, av, bv, sv)):
-                if a is None:
-                    outs.append(None)
-                    saved += [None, None, None, None]
-                    continue
-                a16, b16 = a.to(_F16), b.to(_F16)
-                h = x16 @ a16.t()
-                outs.append((h @ b16.t()) * s)
-                saved += [x16, h, a16, b16]
         ctx.save_for_backward(pos_idx, slot_tok, mq, mv, *saved)
         ctx.cfg = cfg
         ctx.slots = x_pad.shape[0]
