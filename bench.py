@@ -266,12 +266,16 @@ class HotPath:
                     (_lib._I32 * n)(*[j["qblock"] for j in jobs]),
                     (_lib._I32 * n)(*[j.get("qblock2", 1) for j in jobs]))
 
-        # every NF4 weight of a layer in one launch (nf4.LayerWeights), forward and backward
+        # every NF4 weight of a layer in one launch (nf4.LayerWeights), in the forward, and again
+        # in the backward unless the step keeps the forward's copies (model.KEEP_UNPACKED_WEIGHTS)
+        from testt_b200.model import KEEP_UNPACKED_WEIGHTS
+
         fwd_nf4, bwd_nf4 = [], []
         for lp in plan.layers:
             jobs, nb = nf4_jobs(lp.weights.flat)
             fwd_nf4.append((nf4_launch(jobs), nb))
-            bwd_nf4.insert(0, (nf4_launch(jobs), nb))
+            if not KEEP_UNPACKED_WEIGHTS:
+                bwd_nf4.insert(0, (nf4_launch(jobs), nb))
         for args, nb in fwd_nf4 + bwd_nf4:
             add("nf4_unpack", nb, "tb_nf4_unpack_multi", *args)
 

@@ -108,6 +108,25 @@ def test_fused_step_matches_unpatched_model(lora_model, varlen):
         assert abs(a - b) / b < 2e-3, (got[4][0], ref[4][0])
 
 
+def test_kept_weights_give_the_same_step(lora_model):
+    """Reusing the forward's unpacked weights in the backward (KEEP_UNPACKED_WEIGHTS) gives the
+    same loss and gradients as unpacking them again, step after step."""
+    from testt_b200 import model
+
+    saved = model.KEEP_UNPACKED_WEIGHTS
+    try:
+        model.KEEP_UNPACKED_WEIGHTS = False
+        ref = run(lora_model, fused=True)
+        model.KEEP_UNPACKED_WEIGHTS = True
+        got = [run(lora_model, fused=True) for _ in range(2)]
+    finally:
+        model.KEEP_UNPACKED_WEIGHTS = saved
+    for g in got:
+        assert g[0] == ref[0]
+        for name, grad in ref[1].items():
+            torch.testing.assert_close(g[1][name], grad, rtol=1e-6, atol=1e-7)
+
+
 def test_fused_path_declines_what_it_does_not_run(lora_model):
     """Eval mode, no autocast and extra kwargs fall through to the original forward."""
     from testt_b200.model import HeadStats, can_run

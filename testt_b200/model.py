@@ -17,7 +17,8 @@ Per decoder layer, with s the fp32 residual stream of the M real tokens:
     o          = a @ Wo^T                             cuBLAS
     s, y2, _   = add_rmsnorm(s, o)                    tb_add_rmsnorm_fwd
     d          = mlp(y2)                              cuBLAS + tb_swiglu_fwd
-(backward unpacks the layer's weights again, once, in its first operation)
+(the backward reuses the layer's unpacked weights, KEEP_UNPACKED_WEIGHTS, or unpacks them again,
+once, in its first operation)
 then the final norm and the fused head (head.py). Pad tokens never enter the projections, norms,
 MLP, attention or head. Causal attention over each row's real tokens in column order is the
 unpatched model's causal + padding-mask attention restricted to the real query rows (the only
@@ -44,6 +45,13 @@ except ImportError:  # torch < 2.9: attention on the padded layout
 
 # causal attention over each sequence's real tokens (token-major) when available
 USE_VARLEN_ATTENTION = _varlen_attn is not None
+
+# Keep each layer's fp16 weights, unpacked once per step in the forward, for the backward (2.6 GB
+# for Qwen2.5-1.5B, released layer by layer as the backward passes), instead of unpacking them
+# again in the backward as the reference does to keep device memory down. Every step still
+# unpacks every weight from NF4 (the forward releases the previous step's copies first).
+# False restores the reference's second unpack.
+KEEP_UNPACKED_WEIGHTS = True
 
 _ALLOWED_KWARGS = {"num_items_in_batch", "output_attentions", "output_hidden_states",
                    "return_dict"}
@@ -339,7 +347,8 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
         s, y2, _ = add_rmsnorm(s, o, layer.post_attention_layernorm.weight,
                                layer.post_attention_layernorm.variance_epsilon)
         delta = layer_mlp(y2, lw, 2, 3)
-        lw.release()  # backward unpacks the layer again
+        if not KEEP_UNPACKED_WEIGHTS:
+            lw.release()  # backward unpacks the layer again
         del y2, o
 
     _, y, _ = add_rmsnorm(s, delta, inner.norm.weight, inner.norm.variance_epsilon)
