@@ -11,7 +11,7 @@ operations and their roundings, and replaces the glue around the dropout with tw
               xq16, xv16 = fp16(dq[pos_idx]), fp16(dv[pos_idx])
               lora_q = (xq16 @ Aq16^T) @ Bq16^T * scaling_q         (same for v)
               all of it one launch for rank 16 (tb_lora_forward), else tb_lora_gather + cuBLAS
-    backward  the adapter GEMM gradients as autograd computes them, then
+    backward  the adapter GEMMs (the scaling in their fp32 epilogue, weight gradients in fp32),
               dx_pad = dropout_q'(dxq) + dropout_v'(dxv) at the real rows, 0 at padding
                                                                    tb_lora_dropout_grad
 instead of (per adapter) index_select + cast in forward and zero-fill + index_add + dropout
@@ -127,10 +127,17 @@ class LoraPair(torch.autograd.Function):
                 if g_out is None:
                     g_out = torch.zeros((x16.shape[0], b16.shape[0]), dtype=_F16,
                                         device=x16.device)
-                g = g_out.to(_F16) * s          # backward of "* scaling"
-                db = (g.t() @ h).float()        # lora_B weight gradient (fp16 GEMM, cast back)
-                dh = g @ b16
-                da = (dh.t() @ x16).float()     # lora_A weight gradient
+                g_out = g_out.to(_F16)
+                rank, rows_ = h.shape[1], h.shape[0]
+                # "* scaling" is taken into the GEMMs' fp32 epilogue (alpha) and the weight
+                # gradients come out of cuBLAS in fp32 (peft under autocast rounds them to fp16
+                # first, then casts): two GEMMs per gradient and no separate scale or cast kernels
+                db = torch.addmm(torch.empty((b16.shape[0], rank), dtype=torch.float32,
+                                             device=h.device),
+                                 g_out.t(), h, beta=0.0, alpha=s, out_dtype=torch.float32)
+                dh = torch.addmm(torch.empty((rows_, rank), dtype=_F16, device=h.device),
+                                 g_out, b16, beta=0.0, alpha=s)
+                da = torch.mm(dh.t(), x16, out_dtype=torch.float32)   # lora_A weight gradient
                 dxs.append(dh @ a16 if need[0] else None)
                 grads += [da, db]
             gx = None
