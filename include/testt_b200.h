@@ -153,19 +153,19 @@ int tb_slot_index(const int64_t *pos_idx, int64_t rows, int64_t slots, int32_t *
 int tb_lora_gather(const float *dropped_q, const float *dropped_v, const int64_t *pos_idx,
                    uint16_t *xq, uint16_t *xv, int64_t rows, int64_t hidden, void *stream);
 
-/* Both adapters' forward for rank-16 LoRA, per real row m (either adapter's pointers NULL when
- * absent): x16[m] = fp16(dropped[pos_idx[m]]); h16[m] = fp16(x16[m] . a^T);
- * out[m] = fp16(fp32(fp16(h16[m] . b^T)) * scale), fp32 accumulation. dropped: fp32
- * [slots, hidden] dropout outputs; a: fp16 lora_A weight [16, hidden]; b: fp16 lora_B weight
- * [hout, 16] (the autocast casts); x16 [rows, hidden], h16 [rows, 16] (kept for backward), out
- * [rows, hout], fp16.
- * hidden and hout multiples of 8 (at most 8192); 16-byte aligned buffers. Replaces lora_A,
- * lora_B and "* scaling" under fp16 autocast with their weight casts (peft, called from
- * solution/model.py:205), and the index_select + cast of tb_lora_gather. */
-int tb_lora_forward(const float *dropped_q, const uint16_t *a_q, const uint16_t *b_q,
-                    uint16_t *x16_q, uint16_t *h16_q, uint16_t *out_q, int64_t hout_q,
-                    float scale_q, const float *dropped_v, const uint16_t *a_v,
-                    const uint16_t *b_v, uint16_t *x16_v,
+/* Both adapters' forward for rank-16 LoRA, per real row m (either adapter's weights NULL when
+ * absent): x16[m] = fp16(dropped[pos_idx[m]]); h16[m] = fp16(x16[m] . fp16(a)^T);
+ * out[m] = fp16(fp32(fp16(h16[m] . fp16(b)^T)) * scale), fp32 accumulation on the tensor cores.
+ * dropped: fp32 [slots, hidden] dropout outputs; a: lora_A weight fp32 [16, hidden]; b: lora_B
+ * weight fp32 [hout, 16]; a16 / b16: their fp16 casts, written here for the backward GEMMs; x16
+ * [rows, hidden], h16 [rows, 16] (kept for backward), out [rows, hout], fp16. hidden a multiple
+ * of 16, hout of 8. Replaces lora_A, lora_B and "* scaling" under fp16 autocast with their
+ * weight casts (peft, called from solution/model.py:205), and the index_select + cast of
+ * tb_lora_gather. */
+int tb_lora_forward(const float *dropped_q, const float *a_q, const float *b_q, uint16_t *a16_q,
+                    uint16_t *b16_q, uint16_t *x16_q, uint16_t *h16_q, uint16_t *out_q,
+                    int64_t hout_q, float scale_q, const float *dropped_v, const float *a_v,
+                    const float *b_v, uint16_t *a16_v, uint16_t *b16_v, uint16_t *x16_v,
                     uint16_t *h16_v, uint16_t *out_v, int64_t hout_v, float scale_v,
                     const int64_t *pos_idx, int64_t rows, int64_t hidden, int32_t rank,
                     void *stream);

@@ -36,8 +36,8 @@ SIGNATURES = {
     "tb_slot_index": [_P, _I64, _I64, _P, _P],
     "tb_lora_gather": [_P, _P, _P, _P, _P, _I64, _I64, _P],
     "tb_lora_dropout_grad": [_P, _P, _P, _P, _P, _P, _I64, _I64, _F, _F, _P],
-    "tb_lora_forward": [_P, _P, _P, _P, _P, _P, _I64, _F, _P, _P, _P, _P, _P, _P, _I64, _F, _P,
-                        _I64, _I64, _I32, _P],
+    "tb_lora_forward": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _F, _P, _P, _P, _P, _P, _P, _P,
+                        _P, _I64, _F, _P, _I64, _I64, _I32, _P],
     "tb_swiglu_fwd": [_P, _P, _I64, _I64, _P],
     "tb_swiglu_bwd_inplace": [_P, _P, _I64, _I64, _P],
     "tb_head_stats_grad": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P],

@@ -126,19 +126,25 @@ __global__ void lora_dropout_grad_any(const uint16_t *dxq, const uint16_t *dxv, 
 }
 
 // ---- the adapters' forward in one kernel (rank 16) -------------------------------------------
-// Per real row m and adapter (blockIdx.y: 0 = q, 1 = v), one warp:
+// Per tile of 16 real rows and adapter (blockIdx.y: 0 = q, 1 = v):
 //   x16 = fp16(dropped[pos_idx[m]])                         (index_select + the autocast cast)
 //   h16 = fp16(x16 . fp16(A)^T)                               (lora_A, fp16 GEMM output)
 //   out = fp16(fp32(fp16(h16 . fp16(B)^T)) * scaling)          (lora_B, then * scaling)
-// with fp32 accumulation, the fp16 weights (the autocast casts, made by the caller) staged in
-// shared memory (B transposed), the 16 sums of h reduced across the warp by a butterfly (every
-// lane ends with all of them). x16 and h16 are written for the backward GEMMs.
+// on the tensor cores (mma.sync m16n8k16, fp16 inputs, fp32 accumulation). The CTA's 8 warps
+// split lora_A's K (hidden) and add their partial 16x16 sums in shared memory in a fixed order;
+// h16 then feeds lora_B as the A operand of every 16x8 output tile, the tiles split over the
+// warps. Operands are read straight from global memory (the weights are L2-resident after the
+// first tiles) and rounded to fp16 in registers, so the autocast casts cost no kernel of their
+// own; the CTAs of tile 0 write those fp16 weights, with x16 and h16, for the backward GEMMs.
 constexpr int kRank = 16;
+constexpr int kFwdWarps = 8;
 
 struct LoraFwdAdapter {
   const float *dropped;  // fp32 [slots, hidden]
-  const uint16_t *a;     // fp16(lora_A weight) [16, hidden]
-  const uint16_t *b;     // fp16(lora_B weight) [hout, 16]
+  const float *a;        // lora_A weight fp32 [16, hidden]
+  const float *b;        // lora_B weight fp32 [hout, 16]
+  uint16_t *a16;         // fp16(a), written by tile 0
+  uint16_t *b16;         // fp16(b), written by tile 0
   uint16_t *x16;         // fp16 [rows, hidden]
   uint16_t *h16;         // fp16 [rows, 16]
   uint16_t *out;         // fp16 [rows, hout]
@@ -149,99 +155,119 @@ struct LoraFwdAdapter {
 struct LoraFwdArgs {
   LoraFwdAdapter ad[2];
   const int64_t *pos_idx;
-  int64_t rows, rows_per_cta;
+  int64_t rows;
   int hidden;
 };
 
-__device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
-  const float2 a = unpack_half2(v.x), b = unpack_half2(v.y), c = unpack_half2(v.z),
-               d = unpack_half2(v.w);
-  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+__device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__global__ void __launch_bounds__(kThreads) lora_fwd_kernel(const __grid_constant__ LoraFwdArgs a) {
-  extern __shared__ __align__(16) uint8_t lora_smem[];
+// two consecutive fp32 values as one fp16x2 (lower address in the lower half)
+__device__ __forceinline__ uint32_t ld_f16x2(const float *p) {
+  const float2 v = __ldg(reinterpret_cast<const float2 *>(p));
+  return pack_half2(v.x, v.y);
+}
+
+__global__ void __launch_bounds__(kFwdWarps * 32)
+    lora_fwd_kernel(const __grid_constant__ LoraFwdArgs a) {
+  __shared__ float part[kFwdWarps][16][kRank + 1];
+  __shared__ uint32_t h_sh[16][kRank / 2];  // h16 of the tile, fp16x2 pairs
   const LoraFwdAdapter &p = a.ad[blockIdx.y];
   if (p.a == nullptr) return;
   const int H = a.hidden, HO = p.hout;
-  uint16_t *a16 = reinterpret_cast<uint16_t *>(lora_smem);  // [16][H]
-  uint16_t *bt16 = a16 + kRank * H;                          // [16][HO]: B transposed
-  {
-    const uint4 *src = reinterpret_cast<const uint4 *>(p.a);
-    uint4 *dst = reinterpret_cast<uint4 *>(a16);
-#pragma unroll 4
-    for (int i = threadIdx.x; i < kRank * H / 8; i += blockDim.x) dst[i] = __ldg(src + i);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;  // mma fragment row group / column pair
+  const bool writer = blockIdx.x == 0;
+  const int64_t m0 = (int64_t)blockIdx.x * 16;
+  const bool r0 = m0 + g < a.rows, r1 = m0 + g + 8 < a.rows;
+  const float *x0 = r0 ? p.dropped + __ldg(a.pos_idx + m0 + g) * H : nullptr;
+  const float *x1 = r1 ? p.dropped + __ldg(a.pos_idx + m0 + g + 8) * H : nullptr;
+
+  // lora_A: this warp's k-steps of 16 columns
+  float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+  const int ksteps = H / 16;
+  uint32_t *x16 = reinterpret_cast<uint32_t *>(p.x16);
+  for (int ks = warp; ks < ksteps; ks += kFwdWarps) {
+    const int k = ks * 16 + 2 * t;
+    const uint32_t a0 = r0 ? ld_f16x2(x0 + k) : 0u, a1 = r1 ? ld_f16x2(x1 + k) : 0u;
+    const uint32_t a2 = r0 ? ld_f16x2(x0 + k + 8) : 0u, a3 = r1 ? ld_f16x2(x1 + k + 8) : 0u;
+    // B = A^T: column n of B is row n of A; n-tile 0 = ranks 0..7, n-tile 1 = 8..15
+    const uint32_t b00 = ld_f16x2(p.a + (int64_t)g * H + k);
+    const uint32_t b01 = ld_f16x2(p.a + (int64_t)g * H + k + 8);
+    const uint32_t b10 = ld_f16x2(p.a + (int64_t)(g + 8) * H + k);
+    const uint32_t b11 = ld_f16x2(p.a + (int64_t)(g + 8) * H + k + 8);
+    mma_16816(c0, a0, a1, a2, a3, b00, b01);
+    mma_16816(c1, a0, a1, a2, a3, b10, b11);
+    if (r0) {
+      x16[((m0 + g) * H + k) / 2] = a0;
+      x16[((m0 + g) * H + k + 8) / 2] = a2;
+    }
+    if (r1) {
+      x16[((m0 + g + 8) * H + k) / 2] = a1;
+      x16[((m0 + g + 8) * H + k + 8) / 2] = a3;
+    }
+    if (writer) {
+      uint32_t *w = reinterpret_cast<uint32_t *>(p.a16);
+      w[((int64_t)g * H + k) / 2] = b00;
+      w[((int64_t)g * H + k + 8) / 2] = b01;
+      w[((int64_t)(g + 8) * H + k) / 2] = b10;
+      w[((int64_t)(g + 8) * H + k + 8) / 2] = b11;
+    }
   }
-#pragma unroll 2
-  for (int n = threadIdx.x; n < HO; n += blockDim.x) {  // row n of B: 16 halves, 2 loads
-    const uint4 lo = __ldg(reinterpret_cast<const uint4 *>(p.b + (int64_t)n * kRank));
-    const uint4 hi = __ldg(reinterpret_cast<const uint4 *>(p.b + (int64_t)n * kRank + 8));
-    const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+  part[warp][g][2 * t] = c0[0];
+  part[warp][g][2 * t + 1] = c0[1];
+  part[warp][g + 8][2 * t] = c0[2];
+  part[warp][g + 8][2 * t + 1] = c0[3];
+  part[warp][g][8 + 2 * t] = c1[0];
+  part[warp][g][8 + 2 * t + 1] = c1[1];
+  part[warp][g + 8][8 + 2 * t] = c1[2];
+  part[warp][g + 8][8 + 2 * t + 1] = c1[3];
+  __syncthreads();
+  if (threadIdx.x < 16 * kRank / 2) {  // 128 threads: one fp16x2 pair of h each
+    const int row = threadIdx.x / (kRank / 2), pr = threadIdx.x % (kRank / 2);
+    float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-    for (int j = 0; j < kRank; ++j)
-      bt16[j * HO + n] = (uint16_t)(w[j / 2] >> (16 * (j & 1)));
+    for (int w = 0; w < kFwdWarps; ++w) {
+      s0 += part[w][row][2 * pr];
+      s1 += part[w][row][2 * pr + 1];
+    }
+    const uint32_t hv = pack_half2(s0, s1);
+    h_sh[row][pr] = hv;
+    if (m0 + row < a.rows) reinterpret_cast<uint32_t *>(p.h16)[(m0 + row) * (kRank / 2) + pr] = hv;
   }
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  const int64_t m0 = (int64_t)blockIdx.x * a.rows_per_cta;
-  const int64_t m1 = m0 + a.rows_per_cta < a.rows ? m0 + a.rows_per_cta : a.rows;
-  for (int64_t m = m0 + warp; m < m1; m += nwarps) {
-    const float *xrow = p.dropped + __ldg(a.pos_idx + m) * H;
-    float acc[kRank];
-#pragma unroll
-    for (int j = 0; j < kRank; ++j) acc[j] = 0.f;
-    for (int v = lane; v < H / 8; v += 32) {
-      float x[8];
-      load8f(xrow + v * 8, x);
-      uint4 xv;
-      xv.x = pack_half2(x[0], x[1]);
-      xv.y = pack_half2(x[2], x[3]);
-      xv.z = pack_half2(x[4], x[5]);
-      xv.w = pack_half2(x[6], x[7]);
-      *reinterpret_cast<uint4 *>(p.x16 + m * H + v * 8) = xv;
-      unpack8(xv, x);
-#pragma unroll
-      for (int j = 0; j < kRank; ++j) {
-        float w[8];
-        unpack8(*reinterpret_cast<const uint4 *>(a16 + j * H + v * 8), w);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[j] = fmaf(x[e], w[e], acc[j]);
-      }
+
+  // lora_B: A operand = h16 (16 x 16), one 16 x 8 output tile per mma, tiles over the warps
+  const uint32_t ha0 = h_sh[g][t], ha1 = h_sh[g + 8][t], ha2 = h_sh[g][4 + t],
+                 ha3 = h_sh[g + 8][4 + t];
+  for (int nt = warp; nt < HO / 8; nt += kFwdWarps) {
+    const int n = nt * 8 + g;  // B[k][n] = lora_B[n][k]
+    const uint32_t b0 = ld_f16x2(p.b + (int64_t)n * kRank + 2 * t);
+    const uint32_t b1 = ld_f16x2(p.b + (int64_t)n * kRank + 2 * t + 8);
+    if (writer) {
+      uint32_t *w = reinterpret_cast<uint32_t *>(p.b16);
+      w[((int64_t)n * kRank + 2 * t) / 2] = b0;
+      w[((int64_t)n * kRank + 2 * t + 8) / 2] = b1;
     }
-#pragma unroll
-    for (int j = 0; j < kRank; ++j) {
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], off);
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_16816(c, ha0, ha1, ha2, ha3, b0, b1);
+    // the GEMM's fp16 output, then * scaling, rounded to fp16 again
+    const int col = nt * 8 + 2 * t;
+    if (r0) {
+      const float2 o = unpack_half2(pack_half2(c[0], c[1]));
+      reinterpret_cast<uint32_t *>(p.out)[((m0 + g) * HO + col) / 2] =
+          pack_half2(o.x * p.scale, o.y * p.scale);
     }
-    float h[kRank];
-    uint32_t hp[kRank / 2];
-#pragma unroll
-    for (int j = 0; j < kRank; j += 2) {
-      hp[j / 2] = pack_half2(acc[j], acc[j + 1]);
-      const float2 r = unpack_half2(hp[j / 2]);
-      h[j] = r.x;
-      h[j + 1] = r.y;
-    }
-    if (lane < 2) {
-      const uint4 hv = lane == 0 ? make_uint4(hp[0], hp[1], hp[2], hp[3])
-                                 : make_uint4(hp[4], hp[5], hp[6], hp[7]);
-      *reinterpret_cast<uint4 *>(p.h16 + m * kRank + lane * 8) = hv;
-    }
-    for (int v = lane; v < HO / 8; v += 32) {
-      float o[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = 0.f;
-#pragma unroll
-      for (int j = 0; j < kRank; ++j) {
-        float w[8];
-        unpack8(*reinterpret_cast<const uint4 *>(bt16 + j * HO + v * 8), w);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = fmaf(h[j], w[e], o[e]);
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e)  // the GEMM's fp16 output, then * scaling (rounded on store)
-        o[e] = __half2float(__float2half_rn(o[e])) * p.scale;
-      store8h(p.out + m * HO + v * 8, o);
+    if (r1) {
+      const float2 o = unpack_half2(pack_half2(c[2], c[3]));
+      reinterpret_cast<uint32_t *>(p.out)[((m0 + g + 8) * HO + col) / 2] =
+          pack_half2(o.x * p.scale, o.y * p.scale);
     }
   }
 }
@@ -305,53 +331,48 @@ extern "C" int tb_lora_dropout_grad(const uint16_t *dxq, const uint16_t *dxv,
   return check_launch("lora_dropout_grad");
 }
 
-extern "C" int tb_lora_forward(const float *dropped_q, const uint16_t *a_q, const uint16_t *b_q,
-                               uint16_t *x16_q, uint16_t *h16_q, uint16_t *out_q, int64_t hout_q,
-                               float scale_q, const float *dropped_v, const uint16_t *a_v,
-                               const uint16_t *b_v, uint16_t *x16_v, uint16_t *h16_v,
-                               uint16_t *out_v, int64_t hout_v, float scale_v,
+extern "C" int tb_lora_forward(const float *dropped_q, const float *a_q, const float *b_q,
+                               uint16_t *a16_q, uint16_t *b16_q, uint16_t *x16_q,
+                               uint16_t *h16_q, uint16_t *out_q, int64_t hout_q, float scale_q,
+                               const float *dropped_v, const float *a_v, const float *b_v,
+                               uint16_t *a16_v, uint16_t *b16_v, uint16_t *x16_v,
+                               uint16_t *h16_v, uint16_t *out_v, int64_t hout_v, float scale_v,
                                const int64_t *pos_idx, int64_t rows, int64_t hidden, int32_t rank,
                                void *stream) {
   if (rank != kRank)
     return set_error(TB_EINVAL, "lora_forward: rank %d (the fused kernel takes rank %d)", rank,
                      kRank);
-  if (rows < 0 || hidden <= 0 || hidden % 8 || hout_q % 8 || hout_v % 8 || hout_q < 0 ||
-      hout_v < 0 || hidden > 8192 || hout_q > 8192 || hout_v > 8192)
+  if (rows < 0 || hidden <= 0 || hidden % 16 || hout_q % 8 || hout_v % 8 || hout_q < 0 ||
+      hout_v < 0)
     return set_error(TB_EINVAL, "lora_forward: rows %lld hidden %lld hout %lld/%lld",
                      (long long)rows, (long long)hidden, (long long)hout_q, (long long)hout_v);
-  if (rows == 0 || (!a_q && !a_v)) return TB_OK;
-  if (!pos_idx) return set_error(TB_EINVAL, "lora_forward: pos_idx is required");
+  if (!a_q && !a_v) return TB_OK;
+  if (rows > (1LL << 31) / (hidden > 16 ? hidden : 16))
+    return set_error(TB_EINVAL, "lora_forward: too many rows");
   LoraFwdArgs args{};
-  const float *dr[2] = {dropped_q, dropped_v};
-  const uint16_t *aa[2] = {a_q, a_v}, *bb[2] = {b_q, b_v};
+  const float *dr[2] = {dropped_q, dropped_v}, *aa[2] = {a_q, a_v}, *bb[2] = {b_q, b_v};
+  uint16_t *a16[2] = {a16_q, a16_v}, *b16[2] = {b16_q, b16_v};
   uint16_t *xx[2] = {x16_q, x16_v}, *hh[2] = {h16_q, h16_v}, *oo[2] = {out_q, out_v};
   const int64_t ho[2] = {hout_q, hout_v};
   const float sc[2] = {scale_q, scale_v};
-  int64_t max_hout = 0;
   for (int i = 0; i < 2; ++i) {
     if (aa[i] == nullptr) continue;
-    if (!dr[i] || !bb[i] || !xx[i] || !hh[i] || !oo[i])
-      return set_error(TB_EINVAL, "lora_forward: adapter %d needs dropped, a, b, x16, h16, out", i);
-    if (!aligned(dr[i], 16) || !aligned(xx[i], 16) || !aligned(hh[i], 16) || !aligned(oo[i], 16) ||
-        !aligned(aa[i], 16) || !aligned(bb[i], 16))
-      return set_error(TB_EALIGN, "lora_forward: 16-byte aligned buffers are required");
-    args.ad[i] = LoraFwdAdapter{dr[i], aa[i], bb[i], xx[i], hh[i], oo[i], (int)ho[i], sc[i]};
-    if (ho[i] > max_hout) max_hout = ho[i];
+    if (!bb[i] || !a16[i] || !b16[i] || (rows > 0 && (!dr[i] || !xx[i] || !hh[i] || !oo[i])))
+      return set_error(TB_EINVAL,
+                       "lora_forward: adapter %d needs dropped, a, b, a16, b16, x16, h16, out", i);
+    if (!aligned(aa[i], 8) || !aligned(bb[i], 8) || !aligned(a16[i], 4) || !aligned(b16[i], 4) ||
+        (rows > 0 && (!aligned(dr[i], 8) || !aligned(xx[i], 4) || !aligned(hh[i], 4) ||
+                      !aligned(oo[i], 4))))
+      return set_error(TB_EALIGN, "lora_forward: misaligned buffer");
+    args.ad[i] = LoraFwdAdapter{dr[i], aa[i], bb[i], a16[i], b16[i], xx[i], hh[i], oo[i],
+                                (int)ho[i], sc[i]};
   }
+  if (rows > 0 && !pos_idx) return set_error(TB_EINVAL, "lora_forward: pos_idx is required");
   args.pos_idx = pos_idx;
   args.rows = rows;
   args.hidden = (int)hidden;
-  // about one CTA per SM over both adapters, 8 warps each
-  int64_t ctas = sm_count() / 2;
-  if (ctas * (kThreads / 32) > rows) ctas = (rows + kThreads / 32 - 1) / (kThreads / 32);
-  if (ctas < 1) ctas = 1;
-  args.rows_per_cta = (rows + ctas - 1) / ctas;
-  ctas = (rows + args.rows_per_cta - 1) / args.rows_per_cta;
-  const size_t smem = (size_t)kRank * (hidden + max_hout) * 2;
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(lora_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem) != cudaSuccess)
-    return check_launch("lora_forward attribute");
-  lora_fwd_kernel<<<dim3((unsigned)ctas, 2), kThreads, smem, as_stream(stream)>>>(args);
+  // one CTA per 16 rows and adapter (tile 0 also writes the fp16 weights, so at least one)
+  const int64_t tiles = rows > 0 ? (rows + 15) / 16 : 1;
+  lora_fwd_kernel<<<dim3((unsigned)tiles, 2), kFwdWarps * 32, 0, as_stream(stream)>>>(args);
   return check_launch("lora_forward");
 }

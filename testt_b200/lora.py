@@ -29,15 +29,17 @@ _RANK = 16  # the rank tb_lora_forward takes
 
 
 def _fused_ok(aq, bq, av, bv, hidden):
-    """Whether tb_lora_forward takes these adapters (rank 16, widths multiples of 8)."""
-    if hidden % 8 or hidden > 8192:
+    """Whether tb_lora_forward takes these adapters (rank 16, hidden a multiple of 16, output
+    widths of 8)."""
+    if hidden % 16:
         return False
     for a, b in ((aq, bq), (av, bv)):
         if a is None:
             continue
         if a.dim() != 2 or a.shape != (_RANK, hidden) or b.dim() != 2 or b.shape[1] != _RANK \
-                or b.shape[0] % 8 or b.shape[0] > 8192 or a.dtype != torch.float32 \
-                or b.dtype != torch.float32 or not (a.is_contiguous() and b.is_contiguous()):
+                or b.shape[0] % 8 or a.dtype != torch.float32 or b.dtype != torch.float32 \
+                or not (a.is_contiguous() and b.is_contiguous()) \
+                or a.data_ptr() % 8 or b.data_ptr() % 8:
             return False
     return True
 
@@ -79,15 +81,16 @@ class LoraPair(torch.autograd.Function):
                                 torch.empty((rows, b.shape[0]), dtype=_F16, device=dev))
                     hs.append(None if a is None else
                               torch.empty((rows, a.shape[0]), dtype=_F16, device=dev))
-                    w16 += [None, None] if a is None else [a.to(_F16), b.to(_F16)]
-                if rows:
-                    _lib.call("tb_lora_forward", _lib.ptr(dq), _lib.ptr(w16[0]),
-                              _lib.ptr(w16[1]), _lib.ptr(xq), _lib.ptr(hs[0]),
-                              _lib.ptr(outs[0]), bq.shape[0] if bq is not None else 0, sq,
-                              _lib.ptr(dv), _lib.ptr(w16[2]), _lib.ptr(w16[3]), _lib.ptr(xv),
-                              _lib.ptr(hs[1]), _lib.ptr(outs[1]),
-                              bv.shape[0] if bv is not None else 0, sv, _lib.ptr(pos_idx), rows,
-                              hidden, _RANK, _lib.stream_of(x_pad))
+                    w16 += [None, None] if a is None else \
+                        [torch.empty_like(a, dtype=_F16), torch.empty_like(b, dtype=_F16)]
+                # the kernel also writes the fp16 weights (the autocast casts) for backward
+                _lib.call("tb_lora_forward", _lib.ptr(dq), _lib.ptr(aq), _lib.ptr(bq),
+                          _lib.ptr(w16[0]), _lib.ptr(w16[1]), _lib.ptr(xq), _lib.ptr(hs[0]),
+                          _lib.ptr(outs[0]), bq.shape[0] if bq is not None else 0, sq,
+                          _lib.ptr(dv), _lib.ptr(av), _lib.ptr(bv), _lib.ptr(w16[2]),
+                          _lib.ptr(w16[3]), _lib.ptr(xv), _lib.ptr(hs[1]), _lib.ptr(outs[1]),
+                          bv.shape[0] if bv is not None else 0, sv, _lib.ptr(pos_idx), rows,
+                          hidden, _RANK, _lib.stream_of(x_pad))
                 saved = [xq, hs[0], w16[0], w16[1], xv, hs[1], w16[2], w16[3]]
             else:
                 if rows and (xq is not None or xv is not None):
