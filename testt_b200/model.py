@@ -13,7 +13,8 @@ Per decoder layer, with s the fp32 residual stream of the M real tokens:
     lq, lv     = LoRA(dropout(y_pad))                 lora.lora_pair: PyTorch dropout (same draws),
                                                       tb_lora_gather, cuBLAS; tb_lora_dropout_grad
     q, k, v    = rope_tokens(qkv, lq, lv)             tb_rope_tokens_fwd, token-major [M, H, 128]
-    a          = varlen causal attention(q, k, v)     PyTorch's flash kernels, GQA, per sequence
+    a          = varlen causal attention(q, k, v)     FlashAttention 2 varlen (GQA in-kernel),
+                                                      else PyTorch's varlen flash kernels
     o          = a @ Wo^T                             cuBLAS
     s, y2, _   = add_rmsnorm(s, o)                    tb_add_rmsnorm_fwd
     d          = mlp(y2)                              cuBLAS + tb_swiglu_fwd
@@ -39,12 +40,28 @@ from .lora import lora_pair
 from .rope import rope_pack, rope_tokens, slot_index
 
 try:
-    from torch.nn.attention.varlen import varlen_attn as _varlen_attn
-except ImportError:  # torch < 2.9: attention on the padded layout
-    _varlen_attn = None
+    from torch.nn.attention.varlen import varlen_attn as _torch_varlen
+except ImportError:  # torch < 2.9
+    _torch_varlen = None
+try:  # FlashAttention 2 (library): GQA handled inside its backward, no separate dK/dV sums
+    from flash_attn import flash_attn_varlen_func as _flash_varlen
+except ImportError:
+    _flash_varlen = None
+
+
+def _varlen_attn(q, k, v, cu_seqlens, max_len, scale):
+    """Causal attention over the packed sequences of cu_seqlens (token-major q, k, v)."""
+    if _flash_varlen is not None and USE_FLASH_ATTN:
+        return _flash_varlen(q, k, v, cu_seqlens, cu_seqlens, max_len, max_len,
+                             softmax_scale=scale, causal=True)
+    return _torch_varlen(q, k, v, cu_seqlens, cu_seqlens, max_len, max_len, scale=scale,
+                         window_size=(-1, 0))
+
+
+USE_FLASH_ATTN = True
 
 # causal attention over each sequence's real tokens (token-major) when available
-USE_VARLEN_ATTENTION = _varlen_attn is not None
+USE_VARLEN_ATTENTION = _torch_varlen is not None or _flash_varlen is not None
 
 # Keep each layer's fp16 weights, unpacked once per step in the forward, for the backward (2.6 GB
 # for Qwen2.5-1.5B, released layer by layer as the backward passes), instead of unpacking them
@@ -331,8 +348,7 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
             q, k, v = rope_tokens(qkv, lora_q, lora_v, cos, sin, pos_idx, batch, seq,
                                   plan.n_heads, plan.n_kv, plan.head_dim)
             del qkv, lora_q, lora_v
-            attn = _varlen_attn(q, k, v, cu_seqlens, cu_seqlens, max_len, max_len,
-                                scale=lp.attn.scaling, window_size=(-1, 0))
+            attn = _varlen_attn(q, k, v, cu_seqlens, max_len, lp.attn.scaling)
             del q, k, v
             attn = attn.reshape(tokens, plan.n_heads * plan.head_dim)
         else:
