@@ -81,20 +81,26 @@ def run(model, fused):
     return float(out.loss), grads, entropy, accuracy, rows
 
 
-@pytest.mark.parametrize("varlen", [True, False], ids=["varlen_attention", "padded_attention"])
-def test_fused_step_matches_unpatched_model(lora_model, varlen):
-    """Both attention layouts of the fused path: token-major variable-length attention (the
-    default) and the reference's padded layout with the causal + padding mask."""
+@pytest.mark.parametrize("attention", ["flash_varlen", "torch_varlen", "padded"])
+def test_fused_step_matches_unpatched_model(lora_model, attention):
+    """Every attention form of the fused path: token-major variable-length attention through
+    FlashAttention 2 (the default) or PyTorch's varlen kernels, and the reference's padded layout
+    with the causal + padding mask."""
     from testt_b200 import _lib, model
 
+    if attention == "flash_varlen" and model._flash_varlen is None:
+        pytest.skip("flash_attn is not installed")
+    if attention == "torch_varlen" and model._torch_varlen is None:
+        pytest.skip("torch.nn.attention.varlen is not available")
     ref = run(lora_model, fused=False)
     _lib.reset_call_count()
-    saved = model.USE_VARLEN_ATTENTION
-    model.USE_VARLEN_ATTENTION = varlen and saved
+    saved = model.USE_VARLEN_ATTENTION, model.USE_FLASH_ATTN
+    model.USE_VARLEN_ATTENTION = attention != "padded" and saved[0]
+    model.USE_FLASH_ATTN = attention == "flash_varlen"
     try:
         got = run(lora_model, fused=True)
     finally:
-        model.USE_VARLEN_ATTENTION = saved
+        model.USE_VARLEN_ATTENTION, model.USE_FLASH_ATTN = saved
     assert _lib.call_count() > 0, "the fused step must run the native kernels"
     assert abs(got[0] - ref[0]) / ref[0] < 2e-3, (got[0], ref[0])
     assert set(got[1]) == set(ref[1]) and ref[1]
