@@ -117,6 +117,11 @@ class GraphedTrainStep:
         n_items_f = float(num_items_in_batch)
         pos, n_lab, denom = host_plan(hm, hl, n_items_f)
         cu, max_len = sequence_offsets(hm) if USE_VARLEN_ATTENTION else (None, None)
+        if torch.cuda.is_available():
+            # page-locked, so the copies into the graph's buffers below are asynchronous (a copy
+            # from pageable memory would first wait for everything queued on the stream)
+            pos = pos.pin_memory()
+            cu = None if cu is None else cu.pin_memory()
         batch, seq = tuple(input_ids.shape)
         key = (batch, seq, pos.numel(), n_lab, denom, max_len)
         e = self.entries.get(key)
