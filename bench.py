@@ -477,17 +477,14 @@ def head_bench(device, reps, world):
 
 # ---- single kernels at configs 1-4 (--kernel) -------------------------------------------------
 
-def kernel_bench(name, steps, warmup, device):
-    """One kernel at its configuration's full size, `warmup` + `steps` launches, each timed with
-    CUDA events after an L2 flush; returns a dict (median us, algorithmic bytes, GB/s)."""
-    import numpy as np
-
+def _kernel_case(name, device):
+    """(launch closure, algorithmic bytes, info) of one kernel at its configuration, on buffers
+    of its own (nbytes 0 for the tensor-core kernels, whose info holds their FLOPs)."""
     from oracle import synth
     from testt_b200 import _lib, head, mlp, nf4, rmsnorm, rope
     from testt_b200.qlora import quantize_nf4
 
     dev = torch.device(device)
-    flush = torch.zeros(64 << 20, dtype=torch.float32, device=dev)  # 256 MB
     fn, nbytes, info = None, 0, {}
     if name in ("nf4", "nf4_nested"):
         w = synth.config1_weight(dev)
@@ -571,18 +568,15 @@ def kernel_bench(name, steps, warmup, device):
         info = {"config": "4", "rows": 256, "labelled": lab}
     else:
         raise SystemExit(f"unknown kernel {name}")
-    for _ in range(warmup):
-        fn()
-    torch.cuda.synchronize()
-    # the launch replayed from a CUDA graph: the event pair then brackets the kernel alone (an
-    # eager call's host-side work can outlast the L2 flush queued before it and idle the GPU
-    # inside the timed region)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        fn()
-    graph.replay()
+    return fn, nbytes, info
+
+
+def _graph_us(graph, reps, flush):
+    """Median device time (us) of `reps` replays of `graph`, the L2 flushed before each."""
+    import numpy as np
+
     times = []
-    for _ in range(steps):
+    for _ in range(reps):
         flush_l2(flush)
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
@@ -591,16 +585,71 @@ def kernel_bench(name, steps, warmup, device):
         b.record()
         torch.cuda.synchronize()
         times.append(a.elapsed_time(b) * 1e3)
+    return float(np.median(times)), float(min(times))
+
+
+def _capture(fns):
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for fn in fns:
+            fn()
+    graph.replay()
+    torch.cuda.synchronize()
+    return graph
+
+
+CHAIN_BYTES = 384 << 20  # buffer sets of a chain together exceed the 126 MB L2 three times
+
+
+def kernel_bench(name, steps, warmup, device):
+    """One kernel at its configuration's full size. Two timings, each of a CUDA graph replayed
+    after a 256 MB L2 flush (an eager call's host work could outlast the flush and leave the GPU
+    idle inside the timed region):
+    - single: one launch (the CUDA event pair resolves about 2 us on these GPUs, a large part of
+      a 5-15 us launch);
+    - chain (memory-bound kernels): back-to-back launches, each on its own set of buffers, the
+      sets rotating with more than 3x the L2 between two uses of a set, as the step's per-layer
+      launches run; time per launch = graph time / launches. GB/s and frac come from it.
+    Beside the chain, the same chain of device-to-device cudaMemcpyAsync copies moving the same
+    bytes (half read, half written per copy) is timed (`memcpy_gbps`): what the copy path of
+    the runtime reaches at this transfer size (not a ceiling: the kernels beat it)."""
+    dev = torch.device(device)
+    flush = torch.zeros(64 << 20, dtype=torch.float32, device=dev)  # 256 MB
+    fn, nbytes, info = _kernel_case(name, dev)
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    graph = _capture([fn])
+    us, us_min = _graph_us(graph, steps, flush)
     del graph
-    us = float(np.median(times))
     pk, kind = peaks()
     if "flops" in info:
         tf = info["flops"] / us / 1e6
-        return {"kernel": name, "us": us, "us_min": float(min(times)), "tflops": tf,
+        return {"kernel": name, "us": us, "us_min": us_min, "tflops": tf,
                 "frac": tf / pk["bf16_tflops"], "peak_kind": kind, **info}
-    gbps = nbytes / us / 1e3
-    return {"kernel": name, "us": us, "us_min": float(min(times)), "bytes": nbytes,
-            "gbps": gbps, "frac": gbps / pk["hbm_gbs"], "peak_kind": kind, **info}
+    n_sets = max(3, min(80, -(-CHAIN_BYTES // nbytes)))
+    fns = [fn] + [_kernel_case(name, dev)[0] for _ in range(n_sets - 1)]
+    for f in fns[1:]:
+        for _ in range(warmup):
+            f()
+    launches = n_sets * max(1, -(-32 // n_sets))
+    chain = [fns[i % n_sets] for i in range(launches)]
+    graph = _capture(chain)
+    chain_us = _graph_us(graph, max(3, steps // 2), flush)[0] / launches
+    del graph, fns, chain
+    half = (nbytes // 2) // 16 * 16
+    bufs = [(torch.empty(half, dtype=torch.uint8, device=dev),
+             torch.empty(half, dtype=torch.uint8, device=dev)) for _ in range(n_sets)]
+    copies = [(lambda s=s, d=d: d.copy_(s)) for s, d in bufs]
+    graph = _capture([copies[i % n_sets] for i in range(launches)])
+    copy_us = _graph_us(graph, max(3, steps // 2), flush)[0] / launches
+    del graph, bufs, copies
+    gbps = nbytes / chain_us / 1e3
+    memcpy_gbps = 2 * half / copy_us / 1e3
+    return {"kernel": name, "us": chain_us, "gbps": gbps, "frac": gbps / pk["hbm_gbs"],
+            "bytes": nbytes, "chain_launches": launches, "buffer_sets": n_sets,
+            "single_us": us, "single_us_min": us_min, "single_gbps": nbytes / us / 1e3,
+            "memcpy_gbps": memcpy_gbps, "peak_kind": kind, **info}
 
 
 # ---- arms ------------------------------------------------------------------------------------

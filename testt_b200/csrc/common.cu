@@ -1,4 +1,5 @@
 // C-ABI error reporting and device queries shared by every kernel file.
+#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
@@ -34,6 +35,14 @@ int sm_count() {
     cached[dev] = n;
   }
   return cached[dev];
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *v = std::getenv("TESTT_B200_PDL");
+    return v == nullptr || std::strcmp(v, "0") != 0;
+  }();
+  return on;
 }
 
 static TimeoutReader g_readers[16];

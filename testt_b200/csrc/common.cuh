@@ -41,6 +41,47 @@ int resident_blocks(Kernel kernel, int threads, size_t smem = 0) {
   return per_sm * sm_count();
 }
 
+// ---- launches with programmatic dependent launch -------------------------------------------
+// The memory-bound kernels are launched with programmatic dependent launch (PDL) allowed: the
+// GPU may schedule a kernel's CTAs while the previous kernel of the stream is still draining,
+// so the launch latency (about 0.8 us between back-to-back launches on B200, 0.2-0.6 us less
+// with PDL) overlaps that kernel's tail. Such a kernel starts with pdl_wait()
+// (griddepcontrol.wait: returns once the previous kernel has completed and its memory is
+// visible) before it touches global memory, then pdl_release() (griddepcontrol.launch_dependents)
+// lets the next PDL kernel be scheduled; the next kernel waits for this one's completion all
+// the same. Without the launch attribute both instructions do nothing. TESTT_B200_PDL=0 in the
+// environment launches without the attribute (plain stream ordering).
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_release() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+bool pdl_enabled();
+
+// Launches `kernel` (whose first statements are pdl_wait(); pdl_release();) on `stream`;
+// TB_OK or TB_ELAUNCH with the CUDA message.
+template <typename... KArgs, typename... Args>
+int launch(const char *what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+           cudaStream_t stream, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return set_error(TB_ELAUNCH, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  }
+  return TB_OK;
+}
+
 // ---- fp16 packing --------------------------------------------------------------------------
 
 // Two floats rounded to nearest-even fp16 and packed (one cvt.rn.f16x2.f32).

@@ -69,6 +69,8 @@ __global__ void __launch_bounds__(kThreads)
                          float *__restrict__ entropy, float *__restrict__ loss,
                          int32_t *__restrict__ correct, int64_t vocab, int64_t ld,
                          float grad_scale, bool vec) {
+  pdl_wait();
+  pdl_release();
   __shared__ Online part[kThreads / 32];
   __shared__ float lse_sh;
   const int64_t row = blockIdx.x;
@@ -193,6 +195,8 @@ __global__ void __launch_bounds__(kPartThreads)
     head_partials_kernel(const uint16_t *__restrict__ logits, const int64_t *__restrict__ targets,
                          float *__restrict__ part, int64_t *__restrict__ part_idx, int64_t cols,
                          int64_t ld, int64_t col_offset, int64_t chunk, bool vec) {
+  pdl_wait();
+  pdl_release();
   __shared__ Online sh[kPartThreads / 32];
   const int64_t row = blockIdx.y;
   const int split = blockIdx.x, splits = gridDim.x;
@@ -262,6 +266,8 @@ __global__ void head_merge_kernel(const float *__restrict__ part,
                                   int splits, float *__restrict__ lse_out,
                                   float *__restrict__ entropy, float *__restrict__ loss,
                                   int32_t *__restrict__ correct) {
+  pdl_wait();
+  pdl_release();
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -305,6 +311,8 @@ __global__ void __launch_bounds__(256)
     head_dlogits_kernel(uint16_t *__restrict__ logits, const int64_t *__restrict__ targets,
                         const float *__restrict__ lse, uint32_t n, FastDiv vpr, int64_t ld,
                         int64_t col_offset, float grad_scale) {
+  pdl_wait();
+  pdl_release();
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     uint32_t row, v;
     vpr.divmod(i, row, v);
@@ -324,6 +332,8 @@ __global__ void __launch_bounds__(256)
 __global__ void head_dlogits_any(uint16_t *logits, const int64_t *targets, const float *lse,
                                  int64_t rows, int64_t cols, int64_t ld, int64_t col_offset,
                                  float grad_scale) {
+  pdl_wait();
+  pdl_release();
   const int64_t n = rows * cols;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -353,9 +363,9 @@ extern "C" int tb_head_stats_grad(uint16_t *logits, const int64_t *targets, floa
     return set_error(TB_EINVAL, "head_stats_grad: all pointers are required");
   if (rows > 0x7fffffffLL) return set_error(TB_EINVAL, "head_stats_grad: too many rows");
   const bool vec = aligned(logits, 16) && ld % 8 == 0;
-  head_stats_grad_rows<<<(unsigned)rows, kThreads, 0, as_stream(stream)>>>(
-      logits, targets, entropy, loss, correct, vocab, ld, grad_scale, vec);
-  return check_launch("head_stats_grad");
+  return launch("head_stats_grad", head_stats_grad_rows, (unsigned)rows, kThreads, 0,
+                as_stream(stream), logits, targets, entropy, loss, correct, vocab, ld, grad_scale,
+                vec);
 }
 
 extern "C" int tb_head_partials(const uint16_t *logits, const int64_t *targets, float *part,
@@ -372,9 +382,8 @@ extern "C" int tb_head_partials(const uint16_t *logits, const int64_t *targets, 
   int64_t chunk = (cols + splits - 1) / splits;
   chunk = ((chunk + 7) / 8) * 8;
   const dim3 grid((unsigned)splits, (unsigned)rows);
-  head_partials_kernel<<<grid, kPartThreads, 0, as_stream(stream)>>>(
-      logits, targets, part, part_idx, cols, ld, col_offset, chunk, vec);
-  return check_launch("head_partials");
+  return launch("head_partials", head_partials_kernel, grid, kPartThreads, 0, as_stream(stream),
+                logits, targets, part, part_idx, cols, ld, col_offset, chunk, vec);
 }
 
 extern "C" int tb_head_merge(const float *part, const int64_t *part_idx, const int64_t *targets,
@@ -388,9 +397,8 @@ extern "C" int tb_head_merge(const float *part, const int64_t *part_idx, const i
     return set_error(TB_EINVAL, "head_merge: all pointers are required");
   const int warps = 8;
   const unsigned blocks = (unsigned)((rows + warps - 1) / warps);
-  head_merge_kernel<<<blocks, warps * 32, 0, as_stream(stream)>>>(
-      part, part_idx, targets, rows, n_groups, splits, lse, entropy, loss, correct);
-  return check_launch("head_merge");
+  return launch("head_merge", head_merge_kernel, blocks, warps * 32, 0, as_stream(stream), part,
+                part_idx, targets, rows, n_groups, splits, lse, entropy, loss, correct);
 }
 
 extern "C" int tb_head_dlogits(uint16_t *logits, const int64_t *targets, const float *lse,
@@ -407,16 +415,14 @@ extern "C" int tb_head_dlogits(uint16_t *logits, const int64_t *targets, const f
   if (cols % 8 == 0 && ld % 8 == 0 && aligned(logits, 16) && nvec < (1LL << 31)) {
     int64_t blocks = (nvec + 255) / 256;
     if (blocks > cap) blocks = cap;
-    head_dlogits_kernel<<<(unsigned)blocks, 256, 0, st>>>(logits, targets, lse, (uint32_t)nvec,
-                                                         FastDiv((uint32_t)(cols / 8)), ld,
-                                                         col_offset, grad_scale);
-  } else {
-    int64_t blocks = (rows * cols + 255) / 256;
-    if (blocks > cap) blocks = cap;
-    head_dlogits_any<<<(unsigned)blocks, 256, 0, st>>>(logits, targets, lse, rows, cols, ld,
-                                                      col_offset, grad_scale);
+    return launch("head_dlogits", head_dlogits_kernel, (unsigned)blocks, 256, 0, st, logits,
+                  targets, lse, (uint32_t)nvec, FastDiv((uint32_t)(cols / 8)), ld, col_offset,
+                  grad_scale);
   }
-  return check_launch("head_dlogits");
+  int64_t blocks = (rows * cols + 255) / 256;
+  if (blocks > cap) blocks = cap;
+  return launch("head_dlogits", head_dlogits_any, (unsigned)blocks, 256, 0, st, logits, targets,
+                lse, rows, cols, ld, col_offset, grad_scale);
 }
 
 // ---- the same statistics with no allocation anywhere (tb_head_stats_grad_noalloc) -----------

@@ -26,6 +26,8 @@ __global__ void __launch_bounds__(kThreads)
     lora_gather_vec(const float *__restrict__ dq, const float *__restrict__ dv,
                     const int64_t *__restrict__ pos_idx, uint16_t *__restrict__ xq,
                     uint16_t *__restrict__ xv, int64_t rows, int64_t vec_per_row) {
+  pdl_wait();
+  pdl_release();
   const int64_t n = rows * vec_per_row;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -46,6 +48,8 @@ __global__ void __launch_bounds__(kThreads)
 
 __global__ void lora_gather_any(const float *dq, const float *dv, const int64_t *pos_idx,
                                 uint16_t *xq, uint16_t *xv, int64_t rows, int64_t hidden) {
+  pdl_wait();
+  pdl_release();
   const int64_t n = rows * hidden;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -70,6 +74,8 @@ __global__ void __launch_bounds__(kThreads)
                           const uint8_t *__restrict__ mq, const uint8_t *__restrict__ mv,
                           const int32_t *__restrict__ slot_tok, float *__restrict__ g,
                           int64_t slots, int64_t vec_per_row, float sq, float sv) {
+  pdl_wait();
+  pdl_release();
   const int64_t n = slots * vec_per_row;
   const int64_t hidden = vec_per_row * 8;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -111,6 +117,8 @@ __global__ void __launch_bounds__(kThreads)
 __global__ void lora_dropout_grad_any(const uint16_t *dxq, const uint16_t *dxv, const uint8_t *mq,
                                       const uint8_t *mv, const int32_t *slot_tok, float *g,
                                       int64_t slots, int64_t hidden, float sq, float sv) {
+  pdl_wait();
+  pdl_release();
   const int64_t n = slots * hidden;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -176,6 +184,8 @@ __device__ __forceinline__ uint32_t ld_f16x2(const float *p) {
 
 __global__ void __launch_bounds__(kFwdWarps * 32)
     lora_fwd_kernel(const __grid_constant__ LoraFwdArgs a) {
+  pdl_wait();
+  pdl_release();
   __shared__ float part[kFwdWarps][16][kRank + 1];
   __shared__ uint32_t h_sh[16][kRank / 2];  // h16 of the tile, fp16x2 pairs
   const LoraFwdAdapter &p = a.ad[blockIdx.y];
@@ -297,14 +307,11 @@ extern "C" int tb_lora_gather(const float *dropped_q, const float *dropped_v,
   const bool vec = hidden % 8 == 0 && (!dropped_q || (aligned(dropped_q, 16) && aligned(xq, 16))) &&
                    (!dropped_v || (aligned(dropped_v, 16) && aligned(xv, 16)));
   if (vec) {
-    lora_gather_vec<<<grid_for(rows * hidden / 8), kThreads, 0, st>>>(dropped_q, dropped_v,
-                                                                       pos_idx, xq, xv, rows,
-                                                                       hidden / 8);
-  } else {
-    lora_gather_any<<<grid_for(rows * hidden), kThreads, 0, st>>>(dropped_q, dropped_v, pos_idx,
-                                                                  xq, xv, rows, hidden);
+    return launch("lora_gather", lora_gather_vec, grid_for(rows * hidden / 8), kThreads, 0, st,
+                  dropped_q, dropped_v, pos_idx, xq, xv, rows, hidden / 8);
   }
-  return check_launch("lora_gather");
+  return launch("lora_gather", lora_gather_any, grid_for(rows * hidden), kThreads, 0, st,
+                dropped_q, dropped_v, pos_idx, xq, xv, rows, hidden);
 }
 
 extern "C" int tb_lora_dropout_grad(const uint16_t *dxq, const uint16_t *dxv,
@@ -322,13 +329,12 @@ extern "C" int tb_lora_dropout_grad(const uint16_t *dxq, const uint16_t *dxv,
                    (!dxv || aligned(dxv, 16)) && (!mask_q || aligned(mask_q, 8)) &&
                    (!mask_v || aligned(mask_v, 8));
   if (vec) {
-    lora_dropout_grad_vec<<<grid_for(slots * hidden / 8), kThreads, 0, st>>>(
-        dxq, dxv, mask_q, mask_v, slot_tok, grad, slots, hidden / 8, scale_q, scale_v);
-  } else {
-    lora_dropout_grad_any<<<grid_for(slots * hidden), kThreads, 0, st>>>(
-        dxq, dxv, mask_q, mask_v, slot_tok, grad, slots, hidden, scale_q, scale_v);
+    return launch("lora_dropout_grad", lora_dropout_grad_vec, grid_for(slots * hidden / 8),
+                  kThreads, 0, st, dxq, dxv, mask_q, mask_v, slot_tok, grad, slots, hidden / 8,
+                  scale_q, scale_v);
   }
-  return check_launch("lora_dropout_grad");
+  return launch("lora_dropout_grad", lora_dropout_grad_any, grid_for(slots * hidden), kThreads, 0,
+                st, dxq, dxv, mask_q, mask_v, slot_tok, grad, slots, hidden, scale_q, scale_v);
 }
 
 extern "C" int tb_lora_forward(const float *dropped_q, const float *a_q, const float *b_q,
@@ -373,6 +379,6 @@ extern "C" int tb_lora_forward(const float *dropped_q, const float *a_q, const f
   args.hidden = (int)hidden;
   // one CTA per 16 rows and adapter (tile 0 also writes the fp16 weights, so at least one)
   const int64_t tiles = rows > 0 ? (rows + 15) / 16 : 1;
-  lora_fwd_kernel<<<dim3((unsigned)tiles, 2), kFwdWarps * 32, 0, as_stream(stream)>>>(args);
-  return check_launch("lora_forward");
+  return launch("lora_forward", lora_fwd_kernel, dim3((unsigned)tiles, 2), kFwdWarps * 32, 0,
+                as_stream(stream), args);
 }

@@ -97,6 +97,10 @@ __device__ __forceinline__ uint4 decode_word(uint32_t word, float scale, uint32_
 #define TB_NF4_SPANS 2
 #endif
 constexpr int kSpansPerWarp = TB_NF4_SPANS;  // spans a warp is sized to take (grid sizing)
+#ifndef TB_NF4_WAVES
+#define TB_NF4_WAVES 1
+#endif
+constexpr int kWavesCap = TB_NF4_WAVES;  // grid at most this many waves of resident blocks
 
 // One warp span of blocksize-64 weights, loaded ahead of its decode: the span's words and the
 // absmax of lane l's block (block first/8 + l): the fp32 absmax (plain) or the u8 code and the
@@ -137,6 +141,8 @@ __device__ __forceinline__ void fetch_span64(const Nf4Job &job, int64_t sp, int 
 // 4 * kUnroll blocks: lane l computes the scale of block l once and word k of lane l (block
 // 4k + l/8) takes it by shuffle.
 __global__ void __launch_bounds__(kThreads) nf4_unpack_words64(const __grid_constant__ Nf4Job job) {
+  pdl_wait();
+  pdl_release();
   __shared__ __align__(256) float table[kMaxW][64];  // 16 entries used, 256-byte stride
   __shared__ float code2[kMaxW][256];
   __shared__ float offs[kMaxW];
@@ -180,6 +186,8 @@ __global__ void __launch_bounds__(kThreads) nf4_unpack_words64(const __grid_cons
 // Any even blocksize: each word's absmax block is found by invariant division and its scale
 // computed by the lane itself.
 __global__ void __launch_bounds__(kThreads) nf4_unpack_words_any(const __grid_constant__ Nf4Job job) {
+  pdl_wait();
+  pdl_release();
   __shared__ __align__(256) float table[kMaxW][64];  // 16 entries used, 256-byte stride
   __shared__ float code2[kMaxW][256];
   __shared__ float offs[kMaxW];
@@ -225,6 +233,8 @@ __global__ void __launch_bounds__(kThreads) nf4_unpack_words_any(const __grid_co
 
 // Byte-granular path for sizes or alignments the word kernel cannot take.
 __global__ void __launch_bounds__(kThreads) nf4_unpack_bytes(const __grid_constant__ Nf4Job job) {
+  pdl_wait();
+  pdl_release();
   const int64_t total = job.start[job.n];
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < total; u += stride) {
@@ -239,7 +249,7 @@ __global__ void __launch_bounds__(kThreads) nf4_unpack_bytes(const __grid_consta
   }
 }
 
-int launch(Nf4Job &job, const int64_t *n_bytes, const int32_t *half_qblock, cudaStream_t stream) {
+int launch_job(Nf4Job &job, const int64_t *n_bytes, const int32_t *half_qblock, cudaStream_t stream) {
   bool words = true;
   for (int j = 0; j < job.n; ++j) {
     words = words && n_bytes[j] % 4 == 0 && half_qblock[j] % 4 == 0 &&
@@ -265,22 +275,21 @@ int launch(Nf4Job &job, const int64_t *n_bytes, const int32_t *half_qblock, cuda
   int64_t blocks = (total + per_block - 1) / per_block;
   if (words && block64) {
     // about kSpansPerWarp spans per warp, but at least one block per SM
-    static int cap = resident_blocks(nf4_unpack_words64, kThreads);
+    static int cap = resident_blocks(nf4_unpack_words64, kThreads) * kWavesCap;
     const int64_t per = (int64_t)(kThreads / 32) * kSpansPerWarp;
     blocks = (total / kSpan + per - 1) / per;
     if (blocks < sm_count()) blocks = sm_count();
     if (blocks > cap) blocks = cap;
-    nf4_unpack_words64<<<(unsigned)blocks, kThreads, 0, stream>>>(job);
-  } else if (words) {
+    return launch("nf4_unpack", nf4_unpack_words64, (unsigned)blocks, kThreads, 0, stream, job);
+  }
+  if (words) {
     static int cap = resident_blocks(nf4_unpack_words_any, kThreads);
     if (blocks > cap) blocks = cap;
-    nf4_unpack_words_any<<<(unsigned)blocks, kThreads, 0, stream>>>(job);
-  } else {
-    static int cap = resident_blocks(nf4_unpack_bytes, kThreads);
-    if (blocks > cap) blocks = cap;
-    nf4_unpack_bytes<<<(unsigned)blocks, kThreads, 0, stream>>>(job);
+    return launch("nf4_unpack", nf4_unpack_words_any, (unsigned)blocks, kThreads, 0, stream, job);
   }
-  return check_launch("nf4_unpack");
+  static int cap = resident_blocks(nf4_unpack_bytes, kThreads);
+  if (blocks > cap) blocks = cap;
+  return launch("nf4_unpack", nf4_unpack_bytes, (unsigned)blocks, kThreads, 0, stream, job);
 }
 
 int fill_common(Nf4Job &job, int j, const uint8_t *packed, const float *table, uint16_t *out,
@@ -337,7 +346,7 @@ extern "C" int tb_nf4_unpack_nested(const uint8_t *packed, const uint8_t *absmax
   if (rc == TB_OK) rc = fill_nested(job, 0, absmax_u8, code2, absmax2, offset, qblock2);
   if (rc != TB_OK) return rc;
   const int32_t half = qblock / 2;
-  return launch(job, &n_bytes, &half, as_stream(stream));
+  return launch_job(job, &n_bytes, &half, as_stream(stream));
 }
 
 extern "C" int tb_nf4_unpack_plain(const uint8_t *packed, const float *absmax,
@@ -350,7 +359,7 @@ extern "C" int tb_nf4_unpack_plain(const uint8_t *packed, const float *absmax,
   if (absmax == nullptr) return set_error(TB_EINVAL, "nf4_unpack_plain: absmax is required");
   job.absmax_f32[0] = absmax;
   const int32_t half = qblock / 2;
-  return launch(job, &n_bytes, &half, as_stream(stream));
+  return launch_job(job, &n_bytes, &half, as_stream(stream));
 }
 
 extern "C" int tb_nf4_unpack_multi(int32_t n_weights, const uint8_t *const *packed,
@@ -382,5 +391,5 @@ extern "C" int tb_nf4_unpack_multi(int32_t n_weights, const uint8_t *const *pack
       if (rc != TB_OK) return rc;
     }
   }
-  return launch(job, n_bytes, half, as_stream(stream));
+  return launch_job(job, n_bytes, half, as_stream(stream));
 }

@@ -21,6 +21,8 @@ __global__ void rmsnorm_fwd_vec(const float *__restrict__ x, const uint16_t *__r
                                 uint16_t *__restrict__ y, float *__restrict__ ypad,
                                 const int64_t *__restrict__ pad_idx, float *__restrict__ rstd_out,
                                 int64_t hidden, float eps) {
+  pdl_wait();
+  pdl_release();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const int nch = (int)(hidden / 8);
@@ -75,6 +77,8 @@ __global__ void rmsnorm_bwd_vec(const float *__restrict__ s, const float *__rest
                                 const int64_t *__restrict__ pad_idx, const float *__restrict__ ds,
                                 float *__restrict__ dx, uint16_t *__restrict__ ddelta,
                                 int64_t hidden) {
+  pdl_wait();
+  pdl_release();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const int nch = (int)(hidden / 8);
@@ -138,6 +142,8 @@ __global__ void rmsnorm_bwd_vec(const float *__restrict__ s, const float *__rest
 __global__ void rmsnorm_fwd_any(const float *x, const uint16_t *delta, const float *w,
                                 float *s_out, uint16_t *y, float *ypad, const int64_t *pad_idx,
                                 float *rstd_out, int64_t hidden, float eps) {
+  pdl_wait();
+  pdl_release();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const int64_t base = row * hidden;
@@ -165,6 +171,8 @@ __global__ void rmsnorm_fwd_any(const float *x, const uint16_t *delta, const flo
 __global__ void rmsnorm_bwd_any(const float *s, const float *rstd_in, const float *w,
                                 const uint16_t *dy, const float *dypad, const int64_t *pad_idx,
                                 const float *ds, float *dx, uint16_t *ddelta, int64_t hidden) {
+  pdl_wait();
+  pdl_release();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const int64_t base = row * hidden;
@@ -240,14 +248,15 @@ extern "C" int tb_add_rmsnorm_fwd(const float *x, const uint16_t *delta, const f
   plan_rows(hidden, rows, vec_ok, threads, nch);
   cudaStream_t st = as_stream(stream);
   const dim3 grid((unsigned)rows);
+  int rc;
   switch (nch) {
-    case 1: rmsnorm_fwd_vec<1><<<grid, threads, 0, st>>>(x, delta, weight, s_out, y, ypad, pad_idx, rstd_out, hidden, eps); break;
-    case 2: rmsnorm_fwd_vec<2><<<grid, threads, 0, st>>>(x, delta, weight, s_out, y, ypad, pad_idx, rstd_out, hidden, eps); break;
-    case 4: rmsnorm_fwd_vec<4><<<grid, threads, 0, st>>>(x, delta, weight, s_out, y, ypad, pad_idx, rstd_out, hidden, eps); break;
-    case 8: rmsnorm_fwd_vec<8><<<grid, threads, 0, st>>>(x, delta, weight, s_out, y, ypad, pad_idx, rstd_out, hidden, eps); break;
-    default: rmsnorm_fwd_any<<<grid, threads, 0, st>>>(x, delta, weight, s_out, y, ypad, pad_idx, rstd_out, hidden, eps); break;
+    case 1: rc = launch("add_rmsnorm_fwd", rmsnorm_fwd_vec<1>, grid, threads, 0, st, x, delta, weight, s_out, y, ypad, pad_idx, rstd_out, hidden, eps); break;
+    case 2: rc = launch("add_rmsnorm_fwd", rmsnorm_fwd_vec<2>, grid, threads, 0, st, x, delta, weight, s_out, y, ypad, pad_idx, rstd_out, hidden, eps); break;
+    case 4: rc = launch("add_rmsnorm_fwd", rmsnorm_fwd_vec<4>, grid, threads, 0, st, x, delta, weight, s_out, y, ypad, pad_idx, rstd_out, hidden, eps); break;
+    case 8: rc = launch("add_rmsnorm_fwd", rmsnorm_fwd_vec<8>, grid, threads, 0, st, x, delta, weight, s_out, y, ypad, pad_idx, rstd_out, hidden, eps); break;
+    default: rc = launch("add_rmsnorm_fwd", rmsnorm_fwd_any, grid, threads, 0, st, x, delta, weight, s_out, y, ypad, pad_idx, rstd_out, hidden, eps); break;
   }
-  return check_launch("add_rmsnorm_fwd");
+  return rc;
 }
 
 extern "C" int tb_add_rmsnorm_bwd(const float *s, const float *rstd, const float *weight,
@@ -268,12 +277,13 @@ extern "C" int tb_add_rmsnorm_bwd(const float *s, const float *rstd, const float
   plan_rows(hidden, rows, vec_ok, threads, nch);
   cudaStream_t st = as_stream(stream);
   const dim3 grid((unsigned)rows);
+  int rc;
   switch (nch) {
-    case 1: rmsnorm_bwd_vec<1><<<grid, threads, 0, st>>>(s, rstd, weight, dy, dypad, pad_idx, ds, dx, ddelta, hidden); break;
-    case 2: rmsnorm_bwd_vec<2><<<grid, threads, 0, st>>>(s, rstd, weight, dy, dypad, pad_idx, ds, dx, ddelta, hidden); break;
-    case 4: rmsnorm_bwd_vec<4><<<grid, threads, 0, st>>>(s, rstd, weight, dy, dypad, pad_idx, ds, dx, ddelta, hidden); break;
-    case 8: rmsnorm_bwd_vec<8><<<grid, threads, 0, st>>>(s, rstd, weight, dy, dypad, pad_idx, ds, dx, ddelta, hidden); break;
-    default: rmsnorm_bwd_any<<<grid, threads, 0, st>>>(s, rstd, weight, dy, dypad, pad_idx, ds, dx, ddelta, hidden); break;
+    case 1: rc = launch("add_rmsnorm_bwd", rmsnorm_bwd_vec<1>, grid, threads, 0, st, s, rstd, weight, dy, dypad, pad_idx, ds, dx, ddelta, hidden); break;
+    case 2: rc = launch("add_rmsnorm_bwd", rmsnorm_bwd_vec<2>, grid, threads, 0, st, s, rstd, weight, dy, dypad, pad_idx, ds, dx, ddelta, hidden); break;
+    case 4: rc = launch("add_rmsnorm_bwd", rmsnorm_bwd_vec<4>, grid, threads, 0, st, s, rstd, weight, dy, dypad, pad_idx, ds, dx, ddelta, hidden); break;
+    case 8: rc = launch("add_rmsnorm_bwd", rmsnorm_bwd_vec<8>, grid, threads, 0, st, s, rstd, weight, dy, dypad, pad_idx, ds, dx, ddelta, hidden); break;
+    default: rc = launch("add_rmsnorm_bwd", rmsnorm_bwd_any, grid, threads, 0, st, s, rstd, weight, dy, dypad, pad_idx, ds, dx, ddelta, hidden); break;
   }
-  return check_launch("add_rmsnorm_bwd");
+  return rc;
 }

@@ -118,6 +118,8 @@ __global__ void __launch_bounds__(kMaxThreads)
                  const int32_t *__restrict__ slot_tok, uint16_t *__restrict__ q,
                  uint16_t *__restrict__ k, uint16_t *__restrict__ v, RopeDims dm, FastDiv seq_div,
                  int64_t zero_chunk) {
+  pdl_wait();
+  pdl_release();
   const int64_t slots = dm.batch * dm.seq;
   const int D = dm.d, H = dm.half;
   const int total = dm.nh + 2 * dm.nkv;
@@ -175,6 +177,8 @@ __global__ void __launch_bounds__(kMaxThreads)
                  const uint16_t *__restrict__ dv, const float *__restrict__ cosv,
                  const float *__restrict__ sinv, const int64_t *__restrict__ pos_idx,
                  uint16_t *__restrict__ dqkv, RopeDims dm, FastDiv seq_div) {
+  pdl_wait();
+  pdl_release();
   const int64_t tok = blockIdx.x;
   const int64_t slots = dm.batch * dm.seq;
   const int D = dm.d, H = dm.half;
@@ -261,6 +265,8 @@ __global__ void rope_fwd_any(const uint16_t *qkv, const void *lq, const void *lv
                              const float *cosv, const float *sinv, const int64_t *pos_idx,
                              const int32_t *slot_tok, uint16_t *q, uint16_t *k, uint16_t *v,
                              RopeDims dm, bool tokens) {
+  pdl_wait();
+  pdl_release();
   const int total = dm.nh + 2 * dm.nkv;
   const int64_t slots = dm.batch * dm.seq;
   const int64_t units = slot_tok ? slots : dm.rows;
@@ -317,6 +323,8 @@ __global__ void rope_fwd_any(const uint16_t *qkv, const void *lq, const void *lv
 __global__ void rope_bwd_any(const uint16_t *dq, const uint16_t *dk, const uint16_t *dv,
                              const float *cosv, const float *sinv, const int64_t *pos_idx,
                              uint16_t *dqkv, RopeDims dm, bool tokens) {
+  pdl_wait();
+  pdl_release();
   const int total = dm.nh + 2 * dm.nkv;
   const int64_t slots = dm.batch * dm.seq;
   const int64_t n = dm.rows * total * dm.half;
@@ -356,6 +364,8 @@ __global__ void rope_bwd_any(const uint16_t *dq, const uint16_t *dk, const uint1
 
 __global__ void slot_scatter(const int64_t *pos_idx, int64_t rows, int64_t slots,
                              int32_t *slot_tok) {
+  pdl_wait();
+  pdl_release();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t p = pos_idx[i];
@@ -429,23 +439,16 @@ int rope_fwd_launch(const char *what, bool tokens, const uint16_t *qkv, const vo
     const unsigned blocks = (unsigned)ctas;
     const FastDiv sd((uint32_t)seq);
     const int32_t *slots_map = tokens ? nullptr : slot_tok;
-#define TB_ROPE_FWD(F, T)                                                                       \
-  rope_fwd_vec<F, T><<<blocks, threads, 0, st>>>(qkv, lora_q, lora_v, cos, sin, pos_idx,     \
-                                                  slots_map, q, k, v, dm, sd, zero_chunk)
-    if (tokens) {
-      if (lora_is_fp32) TB_ROPE_FWD(true, true);
-      else TB_ROPE_FWD(false, true);
-    } else {
-      if (lora_is_fp32) TB_ROPE_FWD(true, false);
-      else TB_ROPE_FWD(false, false);
-    }
+#define TB_ROPE_FWD(F, T)                                                                      \
+  launch(what, rope_fwd_vec<F, T>, blocks, threads, 0, st, qkv, lora_q, lora_v, cos, sin,      \
+         pos_idx, slots_map, q, k, v, dm, sd, zero_chunk)
+    if (tokens) return lora_is_fp32 ? TB_ROPE_FWD(true, true) : TB_ROPE_FWD(false, true);
+    return lora_is_fp32 ? TB_ROPE_FWD(true, false) : TB_ROPE_FWD(false, false);
 #undef TB_ROPE_FWD
-  } else {
-    const int64_t n = units * (n_heads + 2 * n_kv) * (int64_t)dm.half;
-    rope_fwd_any<<<grid_for(n, 256), 256, 0, st>>>(qkv, lora_q, lora_v, lora_is_fp32 != 0, cos, sin,
-                                                   pos_idx, slot_tok, q, k, v, dm, tokens);
   }
-  return check_launch(what);
+  const int64_t n = units * (n_heads + 2 * n_kv) * (int64_t)dm.half;
+  return launch(what, rope_fwd_any, grid_for(n, 256), 256, 0, st, qkv, lora_q, lora_v,
+                lora_is_fp32 != 0, cos, sin, pos_idx, slot_tok, q, k, v, dm, tokens);
 }
 
 int rope_bwd_launch(const char *what, bool tokens, const uint16_t *dq, const uint16_t *dk,
@@ -465,17 +468,14 @@ int rope_bwd_launch(const char *what, bool tokens, const uint16_t *dq, const uin
   if (vec) {
     const FastDiv sd((uint32_t)seq);
     if (tokens)
-      rope_bwd_vec<true><<<(unsigned)rows, rope_threads(dm), 0, st>>>(dq, dk, dv, cos, sin,
-                                                                     pos_idx, dqkv, dm, sd);
-    else
-      rope_bwd_vec<false><<<(unsigned)rows, rope_threads(dm), 0, st>>>(dq, dk, dv, cos, sin,
-                                                                      pos_idx, dqkv, dm, sd);
-  } else {
-    const int64_t n = rows * (n_heads + 2 * n_kv) * (int64_t)dm.half;
-    rope_bwd_any<<<grid_for(n, 256), 256, 0, st>>>(dq, dk, dv, cos, sin, pos_idx, dqkv, dm,
-                                                   tokens);
+      return launch(what, rope_bwd_vec<true>, (unsigned)rows, rope_threads(dm), 0, st, dq, dk, dv,
+                    cos, sin, pos_idx, dqkv, dm, sd);
+    return launch(what, rope_bwd_vec<false>, (unsigned)rows, rope_threads(dm), 0, st, dq, dk, dv,
+                  cos, sin, pos_idx, dqkv, dm, sd);
   }
-  return check_launch(what);
+  const int64_t n = rows * (n_heads + 2 * n_kv) * (int64_t)dm.half;
+  return launch(what, rope_bwd_any, grid_for(n, 256), 256, 0, st, dq, dk, dv, cos, sin, pos_idx,
+                dqkv, dm, tokens);
 }
 
 }  // namespace
@@ -526,6 +526,7 @@ extern "C" int tb_slot_index(const int64_t *pos_idx, int64_t rows, int64_t slots
   cudaStream_t st = as_stream(stream);
   if (cudaMemsetAsync(slot_tok, 0xff, (size_t)slots * sizeof(int32_t), st) != cudaSuccess)
     return check_launch("slot_index memset");
-  if (rows > 0) slot_scatter<<<grid_for(rows, 256), 256, 0, st>>>(pos_idx, rows, slots, slot_tok);
-  return check_launch("slot_index");
+  if (rows == 0) return TB_OK;
+  return launch("slot_index", slot_scatter, grid_for(rows, 256), 256, 0, st, pos_idx, rows, slots,
+                slot_tok);
 }

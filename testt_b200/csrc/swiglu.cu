@@ -12,7 +12,6 @@ namespace tb {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kUnroll = 2;
 
 __device__ __forceinline__ float silu(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
@@ -23,73 +22,87 @@ __device__ __forceinline__ void swiglu_bwd_one(float dact, float g, float u, flo
   du = dact * (g * sig);
 }
 
+__device__ __forceinline__ void unpack8(const uint4 &v, float (&f)[8]) {
+  const float2 a = unpack_half2(v.x), b = unpack_half2(v.y), c = unpack_half2(v.z),
+               d = unpack_half2(v.w);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+  f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+}
+
 // Vector index i (8 values) -> (row, chunk) with one invariant division; n < 2^32 vectors.
+// Grid-stride with the next vector's 16-byte loads issued before the current vector's math
+// (one vector in flight ahead per thread, raw in registers). The forward is launched with a
+// grid that covers every vector (one per thread, the most loads in flight at the start), the
+// backward with one wave of resident blocks (measured fastest for each at 621 and 2048 rows).
 __global__ void __launch_bounds__(kThreads)
     swiglu_fwd_vec(const uint16_t *__restrict__ gu, uint16_t *__restrict__ act, uint32_t n,
                    FastDiv vpr, int64_t inter) {
+  pdl_wait();
+  pdl_release();
   const uint32_t stride = gridDim.x * kThreads;
-  for (uint32_t i0 = blockIdx.x * kThreads * kUnroll + threadIdx.x; i0 < n;
-       i0 += stride * kUnroll) {
-    float g[kUnroll][8], u[kUnroll][8];
-#pragma unroll
-    for (int r = 0; r < kUnroll; ++r) {
-      const uint32_t i = i0 + r * kThreads;
-      if (i < n) {
-        uint32_t row, c;
-        vpr.divmod(i, row, c);
-        const uint16_t *p = gu + (int64_t)row * 2 * inter + c * 8;
-        load8h(p, g[r]);
-        load8h(p + inter, u[r]);
-      }
+  uint32_t i = blockIdx.x * kThreads + threadIdx.x;
+  if (i >= n) return;
+  uint32_t row, c;
+  vpr.divmod(i, row, c);
+  const uint16_t *p = gu + (int64_t)row * 2 * inter + c * 8;
+  uint4 gb = __ldg(reinterpret_cast<const uint4 *>(p));
+  uint4 ub = __ldg(reinterpret_cast<const uint4 *>(p + inter));
+  while (true) {
+    float g[8], u[8], o[8];
+    unpack8(gb, g);
+    unpack8(ub, u);
+    const uint32_t r0 = row, c0 = c;
+    const uint32_t next = i + stride;
+    const bool more = next < n && next > i;
+    if (more) {
+      vpr.divmod(next, row, c);
+      p = gu + (int64_t)row * 2 * inter + c * 8;
+      gb = __ldg(reinterpret_cast<const uint4 *>(p));
+      ub = __ldg(reinterpret_cast<const uint4 *>(p + inter));
     }
 #pragma unroll
-    for (int r = 0; r < kUnroll; ++r) {
-      const uint32_t i = i0 + r * kThreads;
-      if (i < n) {
-        uint32_t row, c;
-        vpr.divmod(i, row, c);
-        float o[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) o[k] = silu(g[r][k]) * u[r][k];
-        store8h(act + (int64_t)row * inter + c * 8, o);
-      }
-    }
+    for (int k = 0; k < 8; ++k) o[k] = silu(g[k]) * u[k];
+    store8h(act + (int64_t)r0 * inter + c0 * 8, o);
+    if (!more) break;
+    i = next;
   }
 }
 
 __global__ void __launch_bounds__(kThreads)
     swiglu_bwd_vec(const uint16_t *__restrict__ dact, uint16_t *__restrict__ gu, uint32_t n,
                    FastDiv vpr, int64_t inter) {
+  pdl_wait();
+  pdl_release();
   const uint32_t stride = gridDim.x * kThreads;
-  for (uint32_t i0 = blockIdx.x * kThreads * kUnroll + threadIdx.x; i0 < n;
-       i0 += stride * kUnroll) {
-    float d[kUnroll][8], g[kUnroll][8], u[kUnroll][8];
-#pragma unroll
-    for (int r = 0; r < kUnroll; ++r) {
-      const uint32_t i = i0 + r * kThreads;
-      if (i < n) {
-        uint32_t row, c;
-        vpr.divmod(i, row, c);
-        uint16_t *p = gu + (int64_t)row * 2 * inter + c * 8;
-        load8h(dact + (int64_t)row * inter + c * 8, d[r]);
-        load8h_rw(p, g[r]);
-        load8h_rw(p + inter, u[r]);
-      }
+  uint32_t i = blockIdx.x * kThreads + threadIdx.x;
+  if (i >= n) return;
+  uint32_t row, c;
+  vpr.divmod(i, row, c);
+  uint16_t *p = gu + (int64_t)row * 2 * inter + c * 8;
+  uint4 db = __ldg(reinterpret_cast<const uint4 *>(dact + (int64_t)row * inter + c * 8));
+  uint4 gb = *reinterpret_cast<const uint4 *>(p);
+  uint4 ub = *reinterpret_cast<const uint4 *>(p + inter);
+  while (true) {
+    float d[8], g[8], u[8], dg[8], du[8];
+    unpack8(db, d);
+    unpack8(gb, g);
+    unpack8(ub, u);
+    uint16_t *const out = p;
+    const uint32_t next = i + stride;
+    const bool more = next < n && next > i;
+    if (more) {
+      vpr.divmod(next, row, c);
+      p = gu + (int64_t)row * 2 * inter + c * 8;
+      db = __ldg(reinterpret_cast<const uint4 *>(dact + (int64_t)row * inter + c * 8));
+      gb = *reinterpret_cast<const uint4 *>(p);
+      ub = *reinterpret_cast<const uint4 *>(p + inter);
     }
 #pragma unroll
-    for (int r = 0; r < kUnroll; ++r) {
-      const uint32_t i = i0 + r * kThreads;
-      if (i < n) {
-        uint32_t row, c;
-        vpr.divmod(i, row, c);
-        uint16_t *p = gu + (int64_t)row * 2 * inter + c * 8;
-        float dg[8], du[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) swiglu_bwd_one(d[r][k], g[r][k], u[r][k], dg[k], du[k]);
-        store8h(p, dg);
-        store8h(p + inter, du);
-      }
-    }
+    for (int k = 0; k < 8; ++k) swiglu_bwd_one(d[k], g[k], u[k], dg[k], du[k]);
+    store8h(out, dg);
+    store8h(out + inter, du);
+    if (!more) break;
+    i = next;
   }
 }
 
@@ -97,6 +110,8 @@ __device__ __forceinline__ float f16(uint16_t h) { return __half2float(__ushort_
 __device__ __forceinline__ uint16_t h16(float f) { return __half_as_ushort(__float2half_rn(f)); }
 
 __global__ void swiglu_fwd_any(const uint16_t *gu, uint16_t *act, int64_t rows, int64_t inter) {
+  pdl_wait();
+  pdl_release();
   const int64_t n = rows * inter;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -107,6 +122,8 @@ __global__ void swiglu_fwd_any(const uint16_t *gu, uint16_t *act, int64_t rows, 
 }
 
 __global__ void swiglu_bwd_any(const uint16_t *dact, uint16_t *gu, int64_t rows, int64_t inter) {
+  pdl_wait();
+  pdl_release();
   const int64_t n = rows * inter;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -119,9 +136,9 @@ __global__ void swiglu_bwd_any(const uint16_t *dact, uint16_t *gu, int64_t rows,
   }
 }
 
-unsigned blocks_for(int64_t n, int per_block) {
-  int64_t b = (n + per_block - 1) / per_block;
-  const int64_t cap = (int64_t)sm_count() * 16;
+// Blocks of kThreads for n work items, at most `cap` (a grid-stride loop covers the rest).
+unsigned blocks_for(int64_t n, int64_t cap) {
+  int64_t b = (n + kThreads - 1) / kThreads;
   if (b > cap) b = cap;
   return (unsigned)(b > 0 ? b : 1);
 }
@@ -140,12 +157,11 @@ extern "C" int tb_swiglu_fwd(const uint16_t *gu, uint16_t *act, int64_t rows, in
   cudaStream_t st = as_stream(stream);
   const int64_t nvec = rows * (inter / 8);
   if (inter % 8 == 0 && nvec < (1LL << 31) && aligned(gu, 16) && aligned(act, 16)) {
-    swiglu_fwd_vec<<<blocks_for(nvec, kThreads * kUnroll), kThreads, 0, st>>>(
-        gu, act, (uint32_t)nvec, FastDiv((uint32_t)(inter / 8)), inter);
-  } else {
-    swiglu_fwd_any<<<blocks_for(rows * inter, kThreads), kThreads, 0, st>>>(gu, act, rows, inter);
+    return launch("swiglu_fwd", swiglu_fwd_vec, blocks_for(nvec, 1LL << 24), kThreads, 0, st, gu,
+                  act, (uint32_t)nvec, FastDiv((uint32_t)(inter / 8)), inter);
   }
-  return check_launch("swiglu_fwd");
+  return launch("swiglu_fwd", swiglu_fwd_any, blocks_for(rows * inter, (int64_t)sm_count() * 16),
+                kThreads, 0, st, gu, act, rows, inter);
 }
 
 extern "C" int tb_swiglu_bwd_inplace(const uint16_t *dact, uint16_t *gu, int64_t rows,
@@ -157,10 +173,10 @@ extern "C" int tb_swiglu_bwd_inplace(const uint16_t *dact, uint16_t *gu, int64_t
   cudaStream_t st = as_stream(stream);
   const int64_t nvec = rows * (inter / 8);
   if (inter % 8 == 0 && nvec < (1LL << 31) && aligned(gu, 16) && aligned(dact, 16)) {
-    swiglu_bwd_vec<<<blocks_for(nvec, kThreads * kUnroll), kThreads, 0, st>>>(
-        dact, gu, (uint32_t)nvec, FastDiv((uint32_t)(inter / 8)), inter);
-  } else {
-    swiglu_bwd_any<<<blocks_for(rows * inter, kThreads), kThreads, 0, st>>>(dact, gu, rows, inter);
+    static const int wave = resident_blocks(swiglu_bwd_vec, kThreads);
+    return launch("swiglu_bwd", swiglu_bwd_vec, blocks_for(nvec, wave), kThreads, 0, st, dact, gu,
+                  (uint32_t)nvec, FastDiv((uint32_t)(inter / 8)), inter);
   }
-  return check_launch("swiglu_bwd");
+  return launch("swiglu_bwd", swiglu_bwd_any, blocks_for(rows * inter, (int64_t)sm_count() * 16),
+                kThreads, 0, st, dact, gu, rows, inter);
 }
