@@ -19,6 +19,7 @@ Printed on rank 0, one JSON line:
              SwiGLU, fwd + bwd, 28 layers), replayed as a CUDA graph: GB/s against HBM peak
   roofline   the dominant hot-path kernel (NF4 unpack): algorithmic bytes / measured time
   head       the vocabulary head of config 4 (2048 rows, 1331 labelled): TFLOP/s
+  head_sharded  (N > 1) config 4 with the head weight vocabulary-sharded over the N GPUs
   cpu_baseline  the same step on the host cores (oracle.step sample), rank 0 at N = 1
 The reference arm (--impl reference) times that CPU step alone.
 """
@@ -475,6 +476,34 @@ def head_bench(device, reps, world):
             "labelled": c["n_labelled"]}
 
 
+def sharded_head_bench(device, reps, world, rank):
+    """Config 4 with the head weight vocabulary-sharded over the ranks (dist.ShardedHead: each
+    rank's tensor-core logits + statistics over its shard, one all-gather of the folded
+    per-row states, dlogits and dh on its shard, one all-reduce of dh): device time per call,
+    max over ranks. Every rank holds the same hidden rows and targets (same seed)."""
+    from oracle import synth
+    from testt_b200.dist import ShardedHead, shard_range
+
+    c = synth.config4(device)
+    lo, hi = shard_range(synth.VOCAB, rank, world)
+    shard = c.pop("weight")[lo:hi].contiguous()
+    torch.cuda.empty_cache()
+    head = ShardedHead(shard, synth.VOCAB)
+    n_lab = c["n_labelled"]
+
+    def run():
+        head.forward(c["hidden"], c["targets"], n_lab, counts=(n_lab, float(n_lab)))
+
+    for _ in range(2):
+        run()
+    torch.cuda.synchronize()
+    ms = time_region(run, reps, world, device) / reps
+    rows, hidden, vocab = 2048, synth.HIDDEN, synth.VOCAB
+    flops = 2 * rows * hidden * vocab + 2 * n_lab * hidden * vocab
+    return {"ms": ms, "tflops": flops / ms / 1e9, "flops": flops, "rows": rows,
+            "labelled": n_lab, "n_gpus": world, "shard_rows": hi - lo}
+
+
 # ---- single kernels at configs 1-4 (--kernel) -------------------------------------------------
 
 def _kernel_case(name, device):
@@ -788,6 +817,8 @@ def ours_arm(args, rank, world, local):
     achieved = nf["gbps"]
 
     head = head_bench(dev, max(args.steps, 5), world) if rank == 0 else None
+    # config 4 vocabulary-sharded over the N GPUs (every rank takes part)
+    sharded = sharded_head_bench(dev, max(args.steps, 5), world, rank) if world > 1 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -843,6 +874,10 @@ def ours_arm(args, rank, world, local):
         "head": None if head is None else {
             **head, "frac": head["tflops"] / pk["bf16_tflops"], "peak": pk["bf16_tflops"],
             "bound": "tensor", "unit": "TFLOP/s"},
+        "head_sharded": None if sharded is None else {
+            **sharded, "frac": sharded["tflops"] / (world * pk["bf16_tflops"]),
+            "peak": world * pk["bf16_tflops"], "bound": "tensor", "unit": "TFLOP/s",
+            "note": "config 4 with the head weight split over the N GPUs' vocabulary shards"},
         "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)

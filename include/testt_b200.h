@@ -227,6 +227,18 @@ int tb_head_merge(const float *part, const int64_t *part_idx, const int64_t *tar
                   int64_t rows, int32_t n_groups, int32_t splits, float *lse, float *entropy,
                   float *loss, int32_t *correct, void *stream);
 
+/* Folds partial states: for each row, its splits_in states (part [rows, splits_in, 6],
+ * part_idx [rows, splits_in], the layout tb_head_partials and tb_head_logits_stats write) are
+ * merged in splits_out contiguous groups into part_out [rows, splits_out, 6] and idx_out
+ * [rows, splits_out], every argmax index shifted by col_offset. A vocabulary shard folds its
+ * per-tile states to one per row (indices made global with its first column) before the
+ * exchange between GPUs; tb_head_merge of the folded states gives what it gives unfolded. No
+ * counterpart in the reference (its head is one GPU, solution/head.py:54-72 merges inside one
+ * kernel). */
+int tb_head_fold(const float *part, const int64_t *part_idx, int64_t rows, int32_t splits_in,
+                 int64_t col_offset, int32_t splits_out, float *part_out, int64_t *idx_out,
+                 void *stream);
+
 /* The head's logits GEMM on the tensor cores with sweep 1 fused into its epilogue. For rows of
  * hidden fp16 [rows, hidden_dim] and the head weight fp16 [vocab, hidden_dim] (both row-major,
  * hidden_dim a multiple of 64, 16-byte aligned): z = fp16(hidden . weight^T) (tcgen05.mma, fp32
@@ -235,8 +247,9 @@ int tb_head_merge(const float *part, const int64_t *part_idx, const int64_t *tar
  * tb_head_partials: part fp32 [rows, ceil(vocab/256), 6], part_idx int64 [rows, ceil(vocab/256)]
  * (merge them with tb_head_merge, n_groups 1, splits ceil(vocab/256)). When logits is non-NULL
  * the fp16 logits of the first logits_rows rows are written to it ([logits_rows, vocab]) for
- * the dlogits pass. Replaces the cuBLAS logits GEMM + sweep 1 of the
- * reference's head (solution/head.py:107-110, :54-72). sm_100 only. */
+ * the dlogits pass. A target outside [0, vocab) (IGNORE_INDEX, or on a vocabulary shard a
+ * label another shard holds, passed as -1) matches no column. Replaces the cuBLAS logits GEMM +
+ * sweep 1 of the reference's head (solution/head.py:107-110, :54-72). sm_100 only. */
 int tb_head_logits_stats(const uint16_t *hidden, const uint16_t *weight, const int64_t *targets,
                          uint16_t *logits, int64_t logits_rows, float *part, int64_t *part_idx,
                          int64_t rows, int64_t vocab, int64_t hidden_dim, void *stream);

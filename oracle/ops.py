@@ -213,6 +213,36 @@ def head_partials(logits16, targets, col_offset, splits):
     return part, idx
 
 
+def head_fold(part, idx, col_offset, splits_out):
+    """Fold each row's [rows, splits_in, 6] partial states into splits_out contiguous groups of
+    states (fp64), every argmax index shifted by col_offset: the merge step of the reference's
+    online softmax (head.py:54-72, the running max rescaling the sums) stopped before lse."""
+    p = part.double()
+    rows, splits_in, _ = p.shape
+    per = -(-splits_in // splits_out)
+    out = torch.zeros((rows, splits_out, 6), dtype=torch.float64)
+    out_idx = torch.full((rows, splits_out), 2 ** 63 - 1, dtype=torch.int64)
+    none = idx == 2 ** 63 - 1
+    shifted = torch.where(none, idx, idx + col_offset)
+    for o in range(splits_out):
+        lo, hi = o * per, min(splits_in, (o + 1) * per)
+        q, ix = p[:, lo:hi], shifted[:, lo:hi]
+        m = q[:, :, 0].max(-1).values
+        w = torch.where(torch.isinf(q[:, :, 0]), torch.zeros_like(q[:, :, 0]),
+                        torch.exp(q[:, :, 0] - m[:, None]))
+        out[:, o, 0] = m
+        out[:, o, 1] = (q[:, :, 1] * w).sum(-1)
+        out[:, o, 2] = (q[:, :, 2] * w).sum(-1)
+        best = q[:, :, 3].max(-1).values
+        out[:, o, 3] = best
+        cand = torch.where(q[:, :, 3] == best[:, None], ix, torch.full_like(ix, 2 ** 63 - 1))
+        out_idx[:, o] = cand.min(-1).values
+        found = q[:, :, 5] > 0
+        out[:, o, 4] = (q[:, :, 4] * found).sum(-1)
+        out[:, o, 5] = found.any(-1).double()
+    return out, out_idx
+
+
 def head_merge(parts, idxs, targets):
     """Merge [groups, rows, splits, 6] partial states -> (lse, entropy, loss, correct)."""
     p = parts.double().permute(1, 0, 2, 3).reshape(parts.shape[1], -1, 6)

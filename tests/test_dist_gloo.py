@@ -58,7 +58,11 @@ def _sharded_head(rank, world, port, out):
     targets = torch.randint(0, vocab, (rows,), generator=gen)
     targets[::4] = -100
     lo, hi = shard_range(vocab, rank, world)
-    part, idx = ops.head_partials(logits[:, lo:hi], targets, lo, splits=3)
+    # the shard's states with local columns and labels (another shard's label: -1), folded to
+    # one state per row with global indices, as dist.shard_states does on the GPU
+    local = torch.where((targets >= lo) & (targets < hi), targets - lo, torch.full_like(targets, -1))
+    part, idx = ops.head_partials(logits[:, lo:hi], local, 0, splits=3)
+    part, idx = ops.head_fold(part, idx, lo, 1)
     gp, gi = exchange_partials(part.float(), idx)
     lse, ent, loss, correct = ops.head_merge(gp, gi, targets)
     # each rank's dlogits slab times its weight rows, summed over ranks = the full product

@@ -160,3 +160,82 @@ def test_fused_head_loss_tensor_core_path_equals_chunked_path():
     assert torch.equal(c1, c2)
     rel = (g1.float() - g2.float()).norm() / g2.float().norm()
     assert rel < 1e-2, float(rel)
+
+
+def test_fold_kernel_matches_oracle():
+    """tb_head_fold on the partials of a tensor-core launch: each row's tile states folded to 1
+    and to 3 states, indices shifted, against the fp64 oracle fold of the same states."""
+    from testt_b200 import _lib
+
+    h, w, tg = _case(300, 5003, 128, 11)
+    rows, vocab = 300, 5003
+    vt = -(-vocab // 256)
+    part = torch.empty((rows, vt, 6), dtype=torch.float32, device=DEV)
+    idx = torch.empty((rows, vt), dtype=torch.int64, device=DEV)
+    _lib.call("tb_head_logits_stats", _lib.ptr(h), _lib.ptr(w), _lib.ptr(tg), None, 0,
+              _lib.ptr(part), _lib.ptr(idx), rows, vocab, 128, _lib.stream_of(h))
+    for splits_out, offset in ((1, 0), (3, 70000)):
+        out = torch.empty((rows, splits_out, 6), dtype=torch.float32, device=DEV)
+        oidx = torch.empty((rows, splits_out), dtype=torch.int64, device=DEV)
+        _lib.call("tb_head_fold", _lib.ptr(part), _lib.ptr(idx), rows, vt, offset, splits_out,
+                  _lib.ptr(out), _lib.ptr(oidx), _lib.stream_of(h))
+        torch.cuda.synchronize()
+        ref, ridx = ops.head_fold(part.cpu(), idx.cpu(), offset, splits_out)
+        assert torch.equal(oidx.cpu(), ridx)
+        for f in (0, 3, 4, 5):  # max, best, target logit, found: exact
+            assert torch.equal(out[..., f].cpu().double(), ref[..., f])
+        # rescaled sums (fast exponential on the GPU); sum(e z) may cancel: held to its rms
+        assert_rel(out[..., 1], ref[..., 1].float(), 1e-5, "sum e", floor=0.0)
+        assert_rel(out[..., 2], ref[..., 2].float(), 1e-5, "sum e z")
+
+
+@pytest.mark.parametrize("groups", [2, 3, 8])
+def test_vocab_shards_on_one_gpu_equal_the_whole_head(groups):
+    """dist.shard_states (tensor-core logits + statistics per shard, labels of other shards
+    passed as -1, tiles folded to one state with global indices) for `groups` vocabulary shards
+    emulated on one GPU, merged as the ranks' gathered states: the statistics of the whole-vocab
+    head (loss, entropy rtol 1e-4, hits exact); each shard's dlogits times its weight rows,
+    summed, gives the whole head's dh."""
+    from oracle import synth
+    from testt_b200 import _lib
+    from testt_b200.dist import shard_range, shard_states
+
+    c = synth.config4(DEV, rows=384)
+    h, w, tg = c["hidden"], c["weight"], c["targets"]
+    labelled = tg != -100
+    order = torch.argsort((~labelled).to(torch.int8), stable=True)
+    hs, ts = h.index_select(0, order).contiguous(), tg.index_select(0, order).contiguous()
+    n_lab = int(labelled.sum())
+    rows = hs.shape[0]
+    stream = _lib.stream_of(hs)
+    parts, idxs, slabs = [], [], []
+    for r in range(groups):
+        lo, hi = shard_range(w.shape[0], r, groups)
+        shard = w[lo:hi].contiguous()
+        p, i, logits = shard_states(hs, ts, shard, lo, n_lab, stream)
+        parts.append(p)
+        idxs.append(i)
+        slabs.append((lo, shard, logits))
+    gp, gi = torch.stack(parts), torch.stack(idxs)
+    lse = torch.empty(rows, device=DEV)
+    ent, loss = torch.empty_like(lse), torch.empty_like(lse)
+    cor = torch.empty(rows, dtype=torch.int32, device=DEV)
+    _lib.call("tb_head_merge", _lib.ptr(gp), _lib.ptr(gi), _lib.ptr(ts), rows, groups, 1,
+              _lib.ptr(lse), _lib.ptr(ent), _lib.ptr(loss), _lib.ptr(cor), stream)
+    logits_full, rlse, rent, rloss, rcor = tc_head(hs, w, ts, rows)
+    assert_rel(loss, rloss, 1e-4, "loss", floor=0.0)
+    assert_rel(ent, rent, 1e-4, "entropy", floor=0.0)
+    assert torch.equal(cor, rcor)
+    scale = 64.0 / n_lab
+    dh = torch.zeros((n_lab, h.shape[1]), device=DEV)
+    for lo, shard, logits in slabs:
+        _lib.call("tb_head_dlogits", _lib.ptr(logits), _lib.ptr(ts), _lib.ptr(lse), n_lab,
+                  shard.shape[0], shard.shape[0], lo, scale, stream)
+        dh += torch.mm(logits, shard, out_dtype=torch.float32)
+    full = logits_full[:n_lab].clone()
+    _lib.call("tb_head_dlogits", _lib.ptr(full), _lib.ptr(ts), _lib.ptr(rlse), n_lab, w.shape[0],
+              w.shape[0], 0, scale, stream)
+    rdh = torch.mm(full, w, out_dtype=torch.float32)
+    rel = (dh - rdh).norm() / rdh.norm()
+    assert rel < 1e-3, float(rel)
+    assert _lib.wait_timeouts() == 0

@@ -145,3 +145,32 @@ def test_split_head_oracle_equals_whole_row(groups, splits):
     assert torch.allclose(ent, rent, rtol=1e-9)
     assert torch.allclose(loss, rloss, rtol=1e-9, atol=1e-12)
     assert torch.equal(correct, rcorrect)
+
+
+def test_oracle_fold_then_merge_equals_merge():
+    """Folding each row's partial states (some groups, indices shifted by a shard offset) and
+    merging the folded states gives the statistics of merging them all (tb_head_fold's
+    contract)."""
+    import torch
+
+    from oracle import ops
+
+    g = torch.Generator().manual_seed(3)
+    logits = (torch.randn(9, 2001, generator=g) * 3).half()
+    t = torch.randint(0, 2001, (9,), generator=g)
+    t[::4] = -100
+    t[1] = int(torch.argmax(logits[1].float()))
+    part, idx = ops.head_partials(logits, t, 0, splits=11)
+    whole = ops.head_merge(part[None], idx[None], t)
+    for splits_out in (1, 2, 11):
+        fp, fi = ops.head_fold(part, idx, 0, splits_out)
+        folded = ops.head_merge(fp[None], fi[None], t)
+        for a, b in zip(whole, folded):
+            if a.dtype == torch.bool:
+                assert torch.equal(a, b)
+            else:
+                assert torch.allclose(a, b, rtol=1e-12, atol=1e-12)
+    # indices shifted by a shard offset: the hit test against global targets
+    fp, fi = ops.head_fold(part, idx, 1000, 1)
+    shifted = ops.head_merge(fp[None], fi[None], torch.where(t >= 0, t + 1000, t))
+    assert torch.equal(shifted[3], whole[3])

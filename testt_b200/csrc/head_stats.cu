@@ -306,6 +306,58 @@ __global__ void head_merge_kernel(const float *__restrict__ part,
   }
 }
 
+// One warp per (row, output split): the row's input partial states [lo, hi) of its splits_in
+// states (contiguous per row) merged into one, every argmax index shifted by col_offset (a
+// vocabulary shard's first column); the target field is taken from the state that holds it.
+__global__ void head_fold_kernel(const float *__restrict__ part,
+                                 const int64_t *__restrict__ part_idx, int64_t rows,
+                                 int splits_in, int splits_out, int64_t col_offset,
+                                 float *__restrict__ out, int64_t *__restrict__ out_idx) {
+  pdl_wait();
+  pdl_release();
+  const int lane = threadIdx.x & 31;
+  const int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (w >= rows * splits_out) return;
+  const int64_t row = w / splits_out;
+  const int o = (int)(w - row * splits_out);
+  const int per = (splits_in + splits_out - 1) / splits_out;
+  const int lo = o * per, hi = min(splits_in, lo + per);
+  constexpr int64_t kNone = 0x7fffffffffffffffLL;
+  Online acc{-CUDART_INF_F, 0.f, 0.f, -CUDART_INF_F, kNone};
+  float zt = 0.f, found = 0.f;
+  for (int p = lo + lane; p < hi; p += 32) {
+    const int64_t at = row * splits_in + p;
+    const float *q = part + at * kPartFields;
+    const int64_t ix = part_idx[at];
+    const Online b{q[0], q[1], q[2], q[3], ix == kNone ? kNone : ix + col_offset};
+    acc = online_merge(acc, b);
+    if (q[5] != 0.f && found == 0.f) {
+      zt = q[4];
+      found = 1.f;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    acc = online_merge(acc, shfl_online(acc, off));
+    const float zo = __shfl_xor_sync(0xffffffffu, zt, off);
+    const float fo = __shfl_xor_sync(0xffffffffu, found, off);
+    if (found == 0.f && fo != 0.f) {
+      zt = zo;
+      found = fo;
+    }
+  }
+  if (lane == 0) {
+    float *q = out + w * kPartFields;
+    q[0] = acc.m;
+    q[1] = acc.s;
+    q[2] = acc.dz;
+    q[3] = acc.best;
+    q[4] = found != 0.f ? zt : 0.f;
+    q[5] = found;
+    out_idx[w] = acc.idx;
+  }
+}
+
 // dlogits over labelled rows, in place: flat over 8-value vectors (n < 2^32 vectors).
 __global__ void __launch_bounds__(256)
     head_dlogits_kernel(uint16_t *__restrict__ logits, const int64_t *__restrict__ targets,
@@ -399,6 +451,24 @@ extern "C" int tb_head_merge(const float *part, const int64_t *part_idx, const i
   const unsigned blocks = (unsigned)((rows + warps - 1) / warps);
   return launch("head_merge", head_merge_kernel, blocks, warps * 32, 0, as_stream(stream), part,
                 part_idx, targets, rows, n_groups, splits, lse, entropy, loss, correct);
+}
+
+extern "C" int tb_head_fold(const float *part, const int64_t *part_idx, int64_t rows,
+                            int32_t splits_in, int64_t col_offset, int32_t splits_out,
+                            float *part_out, int64_t *idx_out, void *stream) {
+  if (rows < 0 || splits_in < 1 || splits_out < 1 || splits_out > splits_in || col_offset < 0)
+    return set_error(TB_EINVAL, "head_fold: rows %lld splits %d -> %d offset %lld",
+                     (long long)rows, splits_in, splits_out, (long long)col_offset);
+  if (rows == 0) return TB_OK;
+  if (!part || !part_idx || !part_out || !idx_out)
+    return set_error(TB_EINVAL, "head_fold: all pointers are required");
+  const int64_t warps = rows * splits_out;
+  const int per_block = 8;
+  if ((warps + per_block - 1) / per_block > 0x7fffffffLL)
+    return set_error(TB_EINVAL, "head_fold: too many rows");
+  return launch("head_fold", head_fold_kernel, (unsigned)((warps + per_block - 1) / per_block),
+                per_block * 32, 0, as_stream(stream), part, part_idx, rows, (int)splits_in,
+                (int)splits_out, col_offset, part_out, idx_out);
 }
 
 extern "C" int tb_head_dlogits(uint16_t *logits, const int64_t *targets, const float *lse,

@@ -8,19 +8,21 @@ here are this build's:
    as a view into one flat fp32 buffer (autograd accumulates into the views in place), so the
    exchange is a single NCCL all-reduce of 8.7 MB for Qwen2.5-1.5B with r=16 on q/v.
 
-2. A vocabulary-sharded head. Rank r holds rows [lo_r, hi_r) of the tied head weight. Per chunk
-   of rows, each rank computes its logits slab, the per-row online-softmax partials of that slab
-   (tb_head_partials), all-gathers the partials (rows x splits x 6 floats + indices), merges
-   them (tb_head_merge, identical on every rank: lse, entropy, token loss, first-argmax hit),
-   turns its slab into dlogits (tb_head_dlogits) and multiplies by its weight shard; one
-   all-reduce of dh (fp32) finishes the chunk. No rank ever holds full logits or the full head.
+2. A vocabulary-sharded head. Rank r holds rows [lo_r, hi_r) of the tied head weight. Each rank
+   computes its logits slab on the tensor cores with the per-row online-softmax state of every
+   256-column tile in the GEMM's epilogue (tb_head_logits_stats), folds those to one state per
+   row (tb_head_fold), all-gathers them (rows x 6 floats + an index per rank), merges them
+   (tb_head_merge, identical on every rank: lse, entropy, token loss, first-argmax hit), turns
+   its labelled rows' slab into dlogits (tb_head_dlogits) and multiplies by its weight shard;
+   one all-reduce of dh (fp32) finishes. No rank ever holds full logits or the full head.
 """
 
 import torch
 import torch.distributed as dist
 
 from . import _lib
-from .head import IGNORE_INDEX, _grad_unit, _host_counts
+from .head import IGNORE_INDEX, USE_TENSOR_CORE_HEAD, VOCAB_TILE, _grad_unit, _host_counts, \
+    _tensor_core_ok
 
 PART_FIELDS = 6
 
@@ -87,12 +89,44 @@ def reduce_dh(dh32, group=None):
     return dh32
 
 
+def shard_states(hidden16, targets, weight_shard, lo, keep_rows, stream):
+    """One vocabulary shard's share of the head on the tensor cores: the logits of rows x
+    (weight rows lo ..) with their online-softmax state per 256-column tile
+    (tb_head_logits_stats; a label outside the shard is passed as -1 and matches no column),
+    folded to one state per row with global argmax indices (tb_head_fold). Returns the folded
+    states [rows, 1, 6], their indices [rows, 1] and the fp16 logits of the first `keep_rows`
+    rows (None when 0), kept for the dlogits pass."""
+    rows, width = hidden16.shape
+    cols = weight_shard.shape[0]
+    dev = hidden16.device
+    local = torch.where((targets >= lo) & (targets < lo + cols), targets - lo,
+                        torch.full_like(targets, -1))
+    vt = -(-cols // VOCAB_TILE)
+    part = torch.empty((rows, vt, PART_FIELDS), dtype=torch.float32, device=dev)
+    pidx = torch.empty((rows, vt), dtype=torch.int64, device=dev)
+    logits = torch.empty((keep_rows, cols), dtype=torch.float16, device=dev) if keep_rows else None
+    _lib.call("tb_head_logits_stats", _lib.ptr(hidden16), _lib.ptr(weight_shard), _lib.ptr(local),
+              _lib.ptr(logits), keep_rows, _lib.ptr(part), _lib.ptr(pidx), rows, cols, width,
+              stream)
+    folded = torch.empty((rows, 1, PART_FIELDS), dtype=torch.float32, device=dev)
+    fidx = torch.empty((rows, 1), dtype=torch.int64, device=dev)
+    _lib.call("tb_head_fold", _lib.ptr(part), _lib.ptr(pidx), rows, vt, lo, 1, _lib.ptr(folded),
+              _lib.ptr(fidx), stream)
+    return folded, fidx, logits
+
+
 class ShardedHead:
     """The fused head over a vocabulary-sharded weight (see the module docstring).
 
     weight_shard: fp16 [hi - lo, hidden] rows [lo, hi) of the head weight on this rank's GPU.
     forward(hidden16, targets, denominator) returns (loss, entropy, token_loss, correct, dh) with
     dh the fp16 gradient of the loss for a unit upstream gradient, the same on every rank.
+
+    On sm_100 with hidden a multiple of 64 every rank runs its shard through the tensor-core
+    logits GEMM with the statistics in its epilogue (shard_states) for all rows at once, folds
+    its tiles to one state per row and all-gathers those (rows x 6 floats + an index per rank);
+    otherwise chunks of `chunk_rows` go through cuBLAS logits and tb_head_partials (`splits`
+    column ranges per row). Either way tb_head_merge gives every rank the same statistics.
     """
 
     def __init__(self, weight_shard, vocab, group=None, chunk_rows=2048, splits=4):
@@ -108,14 +142,19 @@ class ShardedHead:
         self.chunk_rows = chunk_rows
         self.splits = splits
 
-    def forward(self, hidden16, targets, denominator):
+    def forward(self, hidden16, targets, denominator, counts=None):
+        """`counts` = (labelled rows, denominator as a float) when the caller knows them on the
+        host: skips the one synchronisation (the targets are then trusted to be in range)."""
         _lib.require_cuda(hidden16, targets, self.weight, what="ShardedHead")
         rows, width = hidden16.shape
         dev = hidden16.device
         targets = targets.to(torch.int64)
         labelled = targets != IGNORE_INDEX
         order = torch.argsort((~labelled).to(torch.int8), stable=True)
-        n_labelled, denom = _host_counts(labelled, denominator, dev, targets, self.vocab)
+        if counts is None:
+            n_labelled, denom = _host_counts(labelled, denominator, dev, targets, self.vocab)
+        else:
+            n_labelled, denom = int(counts[0]), float(counts[1])
         h = hidden16.index_select(0, order).contiguous()
         tgt = targets.index_select(0, order).contiguous()
         unit = _grad_unit(denom)
@@ -127,7 +166,20 @@ class ShardedHead:
         dh_sorted = torch.zeros((n_labelled, width), dtype=torch.float32, device=dev)
         cols = self.hi - self.lo
         stream = _lib.stream_of(hidden16)
-        for start in range(0, rows, self.chunk_rows):
+        if USE_TENSOR_CORE_HEAD and _tensor_core_ok(h, self.weight):
+            folded, fidx, logits = shard_states(h, tgt, self.weight, self.lo, n_labelled, stream)
+            gp, gi = exchange_partials(folded, fidx, self.group)
+            _lib.call("tb_head_merge", _lib.ptr(gp), _lib.ptr(gi), _lib.ptr(tgt), rows,
+                      self.world, 1, _lib.ptr(lse), _lib.ptr(entropy), _lib.ptr(token_loss),
+                      _lib.ptr(correct), stream)
+            if n_labelled:
+                _lib.call("tb_head_dlogits", _lib.ptr(logits), _lib.ptr(tgt), _lib.ptr(lse),
+                          n_labelled, cols, cols, self.lo, scale, stream)
+                dh_sorted = torch.mm(logits, self.weight, out_dtype=torch.float32)
+            chunks = range(0)
+        else:
+            chunks = range(0, rows, self.chunk_rows)
+        for start in chunks:
             stop = min(rows, start + self.chunk_rows)
             n = stop - start
             logits = torch.matmul(h[start:stop], self.weight.t())
