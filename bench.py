@@ -581,6 +581,16 @@ def _kernel_case(name, device):
             _lib.stream_of(part))
         nbytes = 0
         info = {"config": "4", "rows": rows, "flops": 2 * rows * hidden * vocab}
+    elif name == "head_full":  # fused_head_loss of config 4: statistics, dlogits and dh
+        c = synth.config4(dev)
+        rows, hidden, vocab = 2048, synth.HIDDEN, synth.VOCAB
+        hh = c["hidden"].clone().requires_grad_(True)
+        n_lab = c["n_labelled"]
+        fn = lambda: head.fused_head_loss(hh, c["weight"], c["targets"], n_lab,  # noqa: E731
+                                          counts=(n_lab, float(n_lab)))
+        nbytes = 0
+        info = {"config": "4", "rows": rows, "labelled": n_lab,
+                "flops": 2 * rows * hidden * vocab + 2 * n_lab * hidden * vocab}
     elif name == "head_cublas":  # the plain cuBLAS logits GEMM of config 4, for comparison
         c = synth.config4(dev)
         rows, hidden, vocab = 2048, synth.HIDDEN, synth.VOCAB
@@ -895,7 +905,7 @@ def main():
     ap.add_argument("--kernel", default=None,
                     help="time one kernel at its configuration instead (nf4, nf4_nested, "
                          "rmsnorm_fwd, rmsnorm_bwd, rope_fwd, rope_bwd, swiglu_fwd, swiglu_bwd, "
-                         "head_stats, head_tc, head_cublas, all)")
+                         "head_stats, head_tc, head_full, head_cublas, all)")
     args = ap.parse_args()
     if args.kernel:
         names = ["nf4", "nf4_nested", "rmsnorm_fwd", "rmsnorm_bwd", "rope_fwd", "rope_bwd",

@@ -138,14 +138,21 @@ __global__ void lora_dropout_grad_any(const uint16_t *dxq, const uint16_t *dxv, 
 //   x16 = fp16(dropped[pos_idx[m]])                         (index_select + the autocast cast)
 //   h16 = fp16(x16 . fp16(A)^T)                               (lora_A, fp16 GEMM output)
 //   out = fp16(fp32(fp16(h16 . fp16(B)^T)) * scaling)          (lora_B, then * scaling)
-// on the tensor cores (mma.sync m16n8k16, fp16 inputs, fp32 accumulation). The CTA's 8 warps
-// split lora_A's K (hidden) and add their partial 16x16 sums in shared memory in a fixed order;
-// h16 then feeds lora_B as the A operand of every 16x8 output tile, the tiles split over the
-// warps. Operands are read straight from global memory (the weights are L2-resident after the
-// first tiles) and rounded to fp16 in registers, so the autocast casts cost no kernel of their
-// own; the CTAs of tile 0 write those fp16 weights, with x16 and h16, for the backward GEMMs.
+// on the tensor cores (mma.sync m16n8k16, fp16 inputs, fp32 accumulation). A thread-block
+// cluster of kCluster CTAs takes one tile: CTA r of the cluster takes the r-th 1/kCluster of
+// lora_A's K (hidden), its 8 warps split those k-steps and add their partial 16x16 sums in
+// shared memory in a fixed order; the cluster then adds the CTAs' sums through distributed
+// shared memory, in rank order in every CTA (the same h16 everywhere, deterministic), and CTA r
+// computes the r-th interleaved share of lora_B's 16x8 output tiles with h16 as the A operand.
+// So a tile's serial chain is 1/kCluster of K and of the output columns, and 621 rows give
+// 39 x 2 clusters = 624 CTAs (one wave) instead of 78 CTAs that each walk all of K. Operands
+// are read straight from global memory (the weights are L2-resident after the first tiles) and
+// rounded to fp16 in registers, so the autocast casts cost no kernel of their own; the cluster
+// of tile 0 writes those fp16 weights, and every CTA its share of x16 (h16: rank 0), for the
+// backward GEMMs.
 constexpr int kRank = 16;
 constexpr int kFwdWarps = 8;
+constexpr int kCluster = 8;
 
 struct LoraFwdAdapter {
   const float *dropped;  // fp32 [slots, hidden]
@@ -182,28 +189,55 @@ __device__ __forceinline__ uint32_t ld_f16x2(const float *p) {
   return pack_half2(v.x, v.y);
 }
 
-__global__ void __launch_bounds__(kFwdWarps * 32)
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// every thread of every CTA of the cluster; release/acquire orders shared-memory writes before
+// the barrier with reads (local or remote) after it
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+
+// a float of CTA `rank`'s shared memory at the address `p` has in this CTA
+__device__ __forceinline__ float ld_cluster(const float *p, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(p)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kFwdWarps * 32)
     lora_fwd_kernel(const __grid_constant__ LoraFwdArgs a) {
   pdl_wait();
   pdl_release();
   __shared__ float part[kFwdWarps][16][kRank + 1];
+  __shared__ float cta_sum[16][kRank];      // this CTA's share of x . A^T (read by the cluster)
   __shared__ uint32_t h_sh[16][kRank / 2];  // h16 of the tile, fp16x2 pairs
   const LoraFwdAdapter &p = a.ad[blockIdx.y];
-  if (p.a == nullptr) return;
+  if (p.a == nullptr) return;  // the whole cluster (one blockIdx.y)
+  const uint32_t rank = cluster_ctarank();
   const int H = a.hidden, HO = p.hout;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;  // mma fragment row group / column pair
-  const bool writer = blockIdx.x == 0;
-  const int64_t m0 = (int64_t)blockIdx.x * 16;
+  const int64_t tile = blockIdx.x / kCluster;
+  const bool writer = tile == 0;
+  const int64_t m0 = tile * 16;
   const bool r0 = m0 + g < a.rows, r1 = m0 + g + 8 < a.rows;
   const float *x0 = r0 ? p.dropped + __ldg(a.pos_idx + m0 + g) * H : nullptr;
   const float *x1 = r1 ? p.dropped + __ldg(a.pos_idx + m0 + g + 8) * H : nullptr;
 
-  // lora_A: this warp's k-steps of 16 columns
+  // lora_A: this CTA's k-steps of 16 columns, over its warps
   float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
   const int ksteps = H / 16;
+  const int kper = (ksteps + kCluster - 1) / kCluster;
+  const int kbeg = (int)rank * kper, kend = min(ksteps, kbeg + kper);
   uint32_t *x16 = reinterpret_cast<uint32_t *>(p.x16);
-  for (int ks = warp; ks < ksteps; ks += kFwdWarps) {
+  for (int ks = kbeg + warp; ks < kend; ks += kFwdWarps) {
     const int k = ks * 16 + 2 * t;
     const uint32_t a0 = r0 ? ld_f16x2(x0 + k) : 0u, a1 = r1 ? ld_f16x2(x1 + k) : 0u;
     const uint32_t a2 = r0 ? ld_f16x2(x0 + k + 8) : 0u, a3 = r1 ? ld_f16x2(x1 + k + 8) : 0u;
@@ -239,24 +273,34 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
   part[warp][g + 8][8 + 2 * t] = c1[2];
   part[warp][g + 8][8 + 2 * t + 1] = c1[3];
   __syncthreads();
+  {  // 256 threads: one element of the CTA's 16 x 16 sum each, warps added in order
+    const int row = threadIdx.x / kRank, col = threadIdx.x % kRank;
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kFwdWarps; ++w) s += part[w][row][col];
+    cta_sum[row][col] = s;
+  }
+  cluster_sync();  // every CTA's sum is written
   if (threadIdx.x < 16 * kRank / 2) {  // 128 threads: one fp16x2 pair of h each
     const int row = threadIdx.x / (kRank / 2), pr = threadIdx.x % (kRank / 2);
     float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-    for (int w = 0; w < kFwdWarps; ++w) {
-      s0 += part[w][row][2 * pr];
-      s1 += part[w][row][2 * pr + 1];
+    for (uint32_t r = 0; r < (uint32_t)kCluster; ++r) {  // rank order: the same h16 in every CTA
+      s0 += ld_cluster(&cta_sum[row][2 * pr], r);
+      s1 += ld_cluster(&cta_sum[row][2 * pr + 1], r);
     }
     const uint32_t hv = pack_half2(s0, s1);
     h_sh[row][pr] = hv;
-    if (m0 + row < a.rows) reinterpret_cast<uint32_t *>(p.h16)[(m0 + row) * (kRank / 2) + pr] = hv;
+    if (rank == 0 && m0 + row < a.rows)
+      reinterpret_cast<uint32_t *>(p.h16)[(m0 + row) * (kRank / 2) + pr] = hv;
   }
-  __syncthreads();
+  cluster_sync();  // no CTA leaves while another reads its sums; h_sh complete
 
-  // lora_B: A operand = h16 (16 x 16), one 16 x 8 output tile per mma, tiles over the warps
+  // lora_B: A operand = h16 (16 x 16), one 16 x 8 output tile per mma; tile nt goes to CTA
+  // nt % kCluster, and within it to warp (nt / kCluster) % kFwdWarps
   const uint32_t ha0 = h_sh[g][t], ha1 = h_sh[g + 8][t], ha2 = h_sh[g][4 + t],
                  ha3 = h_sh[g + 8][4 + t];
-  for (int nt = warp; nt < HO / 8; nt += kFwdWarps) {
+  for (int nt = (int)rank + kCluster * warp; nt < HO / 8; nt += kCluster * kFwdWarps) {
     const int n = nt * 8 + g;  // B[k][n] = lora_B[n][k]
     const uint32_t b0 = ld_f16x2(p.b + (int64_t)n * kRank + 2 * t);
     const uint32_t b1 = ld_f16x2(p.b + (int64_t)n * kRank + 2 * t + 8);
@@ -377,8 +421,10 @@ extern "C" int tb_lora_forward(const float *dropped_q, const float *a_q, const f
   args.pos_idx = pos_idx;
   args.rows = rows;
   args.hidden = (int)hidden;
-  // one CTA per 16 rows and adapter (tile 0 also writes the fp16 weights, so at least one)
+  // one cluster of kCluster CTAs per 16 rows and adapter (tile 0 also writes the fp16
+  // weights, so at least one)
   const int64_t tiles = rows > 0 ? (rows + 15) / 16 : 1;
-  return launch("lora_forward", lora_fwd_kernel, dim3((unsigned)tiles, 2), kFwdWarps * 32, 0,
-                as_stream(stream), args);
+  if (tiles * kCluster > 0x7fffffffLL) return set_error(TB_EINVAL, "lora_forward: too many rows");
+  return launch("lora_forward", lora_fwd_kernel, dim3((unsigned)(tiles * kCluster), 2),
+                kFwdWarps * 32, 0, as_stream(stream), args);
 }
