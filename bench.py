@@ -569,6 +569,35 @@ def _kernel_case(name, device):
             gu = c["gu"].clone()
             fn = lambda: mlp.gated_silu_backward_(c["dact"], gu)  # noqa: E731
             nbytes = m * 89600
+    elif name == "lora_fwd":  # both rank-16 adapters of a layer at config 3's 621 tokens
+        c = synth.config3(dev)
+        m, hidden, r = c["rows"], 1536, 16
+        g = torch.Generator(device=dev).manual_seed(5)
+        f32, f16 = torch.float32, torch.float16
+
+        def rnd(*shape):
+            return torch.randn(shape, generator=g, device=dev) * 0.05
+
+        slots = 2048
+        dq, dv = rnd(slots, hidden), rnd(slots, hidden)
+        aq, av, bq, bv = rnd(r, hidden), rnd(r, hidden), rnd(hidden, r), rnd(256, r)
+        w16 = [torch.empty(t.shape, dtype=f16, device=dev) for t in (aq, bq, av, bv)]
+        xq, xv = (torch.empty((m, hidden), dtype=f16, device=dev) for _ in range(2))
+        hq, hv = (torch.empty((m, r), dtype=f16, device=dev) for _ in range(2))
+        oq = torch.empty((m, hidden), dtype=f16, device=dev)
+        ov = torch.empty((m, 256), dtype=f16, device=dev)
+        pos = c["pos_idx"]
+        fn = lambda: _lib.call(  # noqa: E731
+            "tb_lora_forward", _lib.ptr(dq), _lib.ptr(aq), _lib.ptr(bq), _lib.ptr(w16[0]),
+            _lib.ptr(w16[1]), _lib.ptr(xq), _lib.ptr(hq), _lib.ptr(oq), hidden, 2.0, _lib.ptr(dv),
+            _lib.ptr(av), _lib.ptr(bv), _lib.ptr(w16[2]), _lib.ptr(w16[3]), _lib.ptr(xv),
+            _lib.ptr(hv), _lib.ptr(ov), 256, 2.0, _lib.ptr(pos), m, hidden, r,
+            _lib.stream_of(oq))
+        # x read (fp32) and written (fp16) for both adapters, h16, outputs, weights (fp32 in, fp16 out)
+        nbytes = 2 * m * hidden * (4 + 2) + 2 * m * r * 2 + m * (hidden + 256) * 2 \
+            + (2 * r * hidden + (hidden + 256) * r) * (4 + 2) + m * 8
+        info = {"config": "3", "tokens": m, "hidden": hidden, "rank": r,
+                "outputs": [hidden, 256]}
     elif name == "head_tc":
         c = synth.config4(dev)
         rows, hidden, vocab = 2048, synth.HIDDEN, synth.VOCAB
@@ -905,11 +934,13 @@ def main():
     ap.add_argument("--kernel", default=None,
                     help="time one kernel at its configuration instead (nf4, nf4_nested, "
                          "rmsnorm_fwd, rmsnorm_bwd, rope_fwd, rope_bwd, swiglu_fwd, swiglu_bwd, "
+                         "lora_fwd, "
                          "head_stats, head_tc, head_full, head_cublas, all)")
     args = ap.parse_args()
     if args.kernel:
         names = ["nf4", "nf4_nested", "rmsnorm_fwd", "rmsnorm_bwd", "rope_fwd", "rope_bwd",
-                 "swiglu_fwd", "swiglu_bwd", "head_stats", "head_tc"] if args.kernel == "all" \
+                 "swiglu_fwd", "swiglu_bwd", "lora_fwd", "head_stats", "head_tc"] \
+            if args.kernel == "all" \
             else args.kernel.split(",")
         for n in names:
             print(json.dumps(kernel_bench(n, args.steps, args.warmup, "cuda:0")), flush=True)

@@ -153,6 +153,8 @@ __global__ void lora_dropout_grad_any(const uint16_t *dxq, const uint16_t *dxv, 
 constexpr int kRank = 16;
 constexpr int kFwdWarps = 8;
 constexpr int kCluster = 8;
+constexpr int kTileRows = 32;  // rows per cluster: two m16 tiles sharing every A fragment
+constexpr int kBPre = 3;       // lora_B output tiles per warp whose operands are loaded early
 
 struct LoraFwdAdapter {
   const float *dropped;  // fp32 [slots, hidden]
@@ -211,13 +213,61 @@ __device__ __forceinline__ float ld_cluster(const float *p, uint32_t rank) {
   return v;
 }
 
-__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kFwdWarps * 32)
+// lora_A's work for one k-step of 16 columns: the fp16 x fragments of both 16-row m-tiles
+// (rows m0 + 16 mt + g, + 8), the fp16 A fragments of both 8-rank n-tiles, four mma
+struct KStep {
+  uint32_t x[2][4];  // [m-tile][a0..a3]
+  uint32_t w[4];     // b00, b01, b10, b11
+};
+
+__device__ __forceinline__ void lora_a_step(const float *const (&xr)[2][2], const float *A, int H,
+                                            int k, float (&c)[2][2][4], KStep &st) {
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    st.x[mt][0] = xr[mt][0] ? ld_f16x2(xr[mt][0] + k) : 0u;
+    st.x[mt][1] = xr[mt][1] ? ld_f16x2(xr[mt][1] + k) : 0u;
+    st.x[mt][2] = xr[mt][0] ? ld_f16x2(xr[mt][0] + k + 8) : 0u;
+    st.x[mt][3] = xr[mt][1] ? ld_f16x2(xr[mt][1] + k + 8) : 0u;
+  }
+  const int g = (threadIdx.x & 31) >> 2;
+  // B = A^T: column n of B is row n of A; n-tile 0 = ranks 0..7, n-tile 1 = 8..15
+  st.w[0] = ld_f16x2(A + (int64_t)g * H + k);
+  st.w[1] = ld_f16x2(A + (int64_t)g * H + k + 8);
+  st.w[2] = ld_f16x2(A + (int64_t)(g + 8) * H + k);
+  st.w[3] = ld_f16x2(A + (int64_t)(g + 8) * H + k + 8);
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    mma_16816(c[mt][0], st.x[mt][0], st.x[mt][1], st.x[mt][2], st.x[mt][3], st.w[0], st.w[1]);
+    mma_16816(c[mt][1], st.x[mt][0], st.x[mt][1], st.x[mt][2], st.x[mt][3], st.w[2], st.w[3]);
+  }
+}
+
+// x16 of one k-step's valid rows for the backward
+__device__ __forceinline__ void lora_x16_store(const LoraFwdAdapter &p, const bool (&rv)[2][2],
+                                               int64_t m0, int H, int k, const KStep &st) {
+  const int g = (threadIdx.x & 31) >> 2;
+  uint32_t *x16 = reinterpret_cast<uint32_t *>(p.x16);
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    const int64_t r = m0 + 16 * mt + g;
+    if (rv[mt][0]) {
+      x16[(r * H + k) / 2] = st.x[mt][0];
+      x16[(r * H + k + 8) / 2] = st.x[mt][2];
+    }
+    if (rv[mt][1]) {
+      x16[((r + 8) * H + k) / 2] = st.x[mt][1];
+      x16[((r + 8) * H + k + 8) / 2] = st.x[mt][3];
+    }
+  }
+}
+
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kFwdWarps * 32, 3)
     lora_fwd_kernel(const __grid_constant__ LoraFwdArgs a) {
   pdl_wait();
   pdl_release();
-  __shared__ float part[kFwdWarps][16][kRank + 1];
-  __shared__ float cta_sum[16][kRank];      // this CTA's share of x . A^T (read by the cluster)
-  __shared__ uint32_t h_sh[16][kRank / 2];  // h16 of the tile, fp16x2 pairs
+  __shared__ float part[kFwdWarps][kTileRows][kRank + 1];
+  __shared__ float cta_sum[kTileRows][kRank];      // this CTA's share of x . A^T (cluster-read)
+  __shared__ uint32_t h_sh[kTileRows][kRank / 2];  // h16 of the tile, fp16x2 pairs
   const LoraFwdAdapter &p = a.ad[blockIdx.y];
   if (p.a == nullptr) return;  // the whole cluster (one blockIdx.y)
   const uint32_t rank = cluster_ctarank();
@@ -226,102 +276,141 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kFwdWarps * 3
   const int g = lane >> 2, t = lane & 3;  // mma fragment row group / column pair
   const int64_t tile = blockIdx.x / kCluster;
   const bool writer = tile == 0;
-  const int64_t m0 = tile * 16;
-  const bool r0 = m0 + g < a.rows, r1 = m0 + g + 8 < a.rows;
-  const float *x0 = r0 ? p.dropped + __ldg(a.pos_idx + m0 + g) * H : nullptr;
-  const float *x1 = r1 ? p.dropped + __ldg(a.pos_idx + m0 + g + 8) * H : nullptr;
+  const int64_t m0 = tile * kTileRows;
+  bool rv[2][2];
+  const float *xr[2][2];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int64_t r = m0 + 16 * mt + 8 * hf + g;
+      rv[mt][hf] = r < a.rows;
+      xr[mt][hf] = rv[mt][hf] ? p.dropped + __ldg(a.pos_idx + r) * H : nullptr;
+    }
+  // lora_B's operand fragments of this warp's first kBPre output tiles, loaded now (they do
+  // not depend on h): n-tile nt goes to CTA nt % kCluster, within it to warp nt / kCluster %
+  // kFwdWarps
+  const int nt0 = (int)rank + kCluster * warp;
+  constexpr int kStride = kCluster * kFwdWarps;
+  uint32_t bpre[kBPre][2];
+#pragma unroll
+  for (int i = 0; i < kBPre; ++i) {
+    const int nt = nt0 + i * kStride;
+    if (nt < HO / 8) {
+      const int n = nt * 8 + g;  // B[k][n] = lora_B[n][k]
+      bpre[i][0] = ld_f16x2(p.b + (int64_t)n * kRank + 2 * t);
+      bpre[i][1] = ld_f16x2(p.b + (int64_t)n * kRank + 2 * t + 8);
+    }
+  }
 
-  // lora_A: this CTA's k-steps of 16 columns, over its warps
-  float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+  // lora_A: this CTA's k-steps of 16 columns over its warps. Nothing is stored to global
+  // memory before the cluster barriers (a barrier's release would wait for it): the x16 copies
+  // of a warp's first two k-steps wait in registers; further k-steps (hidden > 2048) store as
+  // they go.
+  float c[2][2][4] = {};
   const int ksteps = H / 16;
   const int kper = (ksteps + kCluster - 1) / kCluster;
   const int kbeg = (int)rank * kper, kend = min(ksteps, kbeg + kper);
-  uint32_t *x16 = reinterpret_cast<uint32_t *>(p.x16);
-  for (int ks = kbeg + warp; ks < kend; ks += kFwdWarps) {
-    const int k = ks * 16 + 2 * t;
-    const uint32_t a0 = r0 ? ld_f16x2(x0 + k) : 0u, a1 = r1 ? ld_f16x2(x1 + k) : 0u;
-    const uint32_t a2 = r0 ? ld_f16x2(x0 + k + 8) : 0u, a3 = r1 ? ld_f16x2(x1 + k + 8) : 0u;
-    // B = A^T: column n of B is row n of A; n-tile 0 = ranks 0..7, n-tile 1 = 8..15
-    const uint32_t b00 = ld_f16x2(p.a + (int64_t)g * H + k);
-    const uint32_t b01 = ld_f16x2(p.a + (int64_t)g * H + k + 8);
-    const uint32_t b10 = ld_f16x2(p.a + (int64_t)(g + 8) * H + k);
-    const uint32_t b11 = ld_f16x2(p.a + (int64_t)(g + 8) * H + k + 8);
-    mma_16816(c0, a0, a1, a2, a3, b00, b01);
-    mma_16816(c1, a0, a1, a2, a3, b10, b11);
-    if (r0) {
-      x16[((m0 + g) * H + k) / 2] = a0;
-      x16[((m0 + g) * H + k + 8) / 2] = a2;
-    }
-    if (r1) {
-      x16[((m0 + g + 8) * H + k) / 2] = a1;
-      x16[((m0 + g + 8) * H + k + 8) / 2] = a3;
-    }
-    if (writer) {
-      uint32_t *w = reinterpret_cast<uint32_t *>(p.a16);
-      w[((int64_t)g * H + k) / 2] = b00;
-      w[((int64_t)g * H + k + 8) / 2] = b01;
-      w[((int64_t)(g + 8) * H + k) / 2] = b10;
-      w[((int64_t)(g + 8) * H + k + 8) / 2] = b11;
-    }
+  const int ks0 = kbeg + warp, ks1 = ks0 + kFwdWarps;
+  KStep s0, s1;
+  if (ks0 < kend) lora_a_step(xr, p.a, H, ks0 * 16 + 2 * t, c, s0);
+  if (ks1 < kend) lora_a_step(xr, p.a, H, ks1 * 16 + 2 * t, c, s1);
+  for (int ks = ks1 + kFwdWarps; ks < kend; ks += kFwdWarps) {
+    KStep st;
+    lora_a_step(xr, p.a, H, ks * 16 + 2 * t, c, st);
+    lora_x16_store(p, rv, m0, H, ks * 16 + 2 * t, st);
   }
-  part[warp][g][2 * t] = c0[0];
-  part[warp][g][2 * t + 1] = c0[1];
-  part[warp][g + 8][2 * t] = c0[2];
-  part[warp][g + 8][2 * t + 1] = c0[3];
-  part[warp][g][8 + 2 * t] = c1[0];
-  part[warp][g][8 + 2 * t + 1] = c1[1];
-  part[warp][g + 8][8 + 2 * t] = c1[2];
-  part[warp][g + 8][8 + 2 * t + 1] = c1[3];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      part[warp][16 * mt + g][8 * nt + 2 * t] = c[mt][nt][0];
+      part[warp][16 * mt + g][8 * nt + 2 * t + 1] = c[mt][nt][1];
+      part[warp][16 * mt + g + 8][8 * nt + 2 * t] = c[mt][nt][2];
+      part[warp][16 * mt + g + 8][8 * nt + 2 * t + 1] = c[mt][nt][3];
+    }
   __syncthreads();
-  {  // 256 threads: one element of the CTA's 16 x 16 sum each, warps added in order
-    const int row = threadIdx.x / kRank, col = threadIdx.x % kRank;
+  for (int e = threadIdx.x; e < kTileRows * kRank; e += kFwdWarps * 32) {
+    // the CTA's 32 x 16 sum, warps added in order
+    const int row = e / kRank, col = e % kRank;
     float s = 0.f;
 #pragma unroll
     for (int w = 0; w < kFwdWarps; ++w) s += part[w][row][col];
     cta_sum[row][col] = s;
   }
   cluster_sync();  // every CTA's sum is written
-  if (threadIdx.x < 16 * kRank / 2) {  // 128 threads: one fp16x2 pair of h each
-    const int row = threadIdx.x / (kRank / 2), pr = threadIdx.x % (kRank / 2);
-    float s0 = 0.f, s1 = 0.f;
+  uint32_t hv = 0;
+  const int hrow = threadIdx.x / (kRank / 2), hpr = threadIdx.x % (kRank / 2);
+  if (threadIdx.x < kTileRows * kRank / 2) {  // one fp16x2 pair of h each
+    float h0 = 0.f, h1 = 0.f;
 #pragma unroll
-    for (uint32_t r = 0; r < (uint32_t)kCluster; ++r) {  // rank order: the same h16 in every CTA
-      s0 += ld_cluster(&cta_sum[row][2 * pr], r);
-      s1 += ld_cluster(&cta_sum[row][2 * pr + 1], r);
+    for (uint32_t r = 0; r < (uint32_t)kCluster; ++r) {  // rank order: the same h16 everywhere
+      h0 += ld_cluster(&cta_sum[hrow][2 * hpr], r);
+      h1 += ld_cluster(&cta_sum[hrow][2 * hpr + 1], r);
     }
-    const uint32_t hv = pack_half2(s0, s1);
-    h_sh[row][pr] = hv;
-    if (rank == 0 && m0 + row < a.rows)
-      reinterpret_cast<uint32_t *>(p.h16)[(m0 + row) * (kRank / 2) + pr] = hv;
+    hv = pack_half2(h0, h1);
+    h_sh[hrow][hpr] = hv;
   }
   cluster_sync();  // no CTA leaves while another reads its sums; h_sh complete
 
-  // lora_B: A operand = h16 (16 x 16), one 16 x 8 output tile per mma; tile nt goes to CTA
-  // nt % kCluster, and within it to warp (nt / kCluster) % kFwdWarps
-  const uint32_t ha0 = h_sh[g][t], ha1 = h_sh[g + 8][t], ha2 = h_sh[g][4 + t],
-                 ha3 = h_sh[g + 8][4 + t];
-  for (int nt = (int)rank + kCluster * warp; nt < HO / 8; nt += kCluster * kFwdWarps) {
-    const int n = nt * 8 + g;  // B[k][n] = lora_B[n][k]
-    const uint32_t b0 = ld_f16x2(p.b + (int64_t)n * kRank + 2 * t);
-    const uint32_t b1 = ld_f16x2(p.b + (int64_t)n * kRank + 2 * t + 8);
+  // lora_B: A operand = h16 (two 16 x 16 m-tiles), one 16 x 8 output tile per mma
+  uint32_t ha[2][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    ha[mt][0] = h_sh[16 * mt + g][t];
+    ha[mt][1] = h_sh[16 * mt + g + 8][t];
+    ha[mt][2] = h_sh[16 * mt + g][4 + t];
+    ha[mt][3] = h_sh[16 * mt + g + 8][4 + t];
+  }
+  for (int i = 0, nt = nt0; nt < HO / 8; ++i, nt += kStride) {
+    const int n = nt * 8 + g;
+    uint32_t b0, b1;
+    if (i < kBPre) {
+#pragma unroll
+      for (int j = 0; j < kBPre; ++j)
+        if (j == i) {
+          b0 = bpre[j][0];
+          b1 = bpre[j][1];
+        }
+    } else {
+      b0 = ld_f16x2(p.b + (int64_t)n * kRank + 2 * t);
+      b1 = ld_f16x2(p.b + (int64_t)n * kRank + 2 * t + 8);
+    }
     if (writer) {
       uint32_t *w = reinterpret_cast<uint32_t *>(p.b16);
       w[((int64_t)n * kRank + 2 * t) / 2] = b0;
       w[((int64_t)n * kRank + 2 * t + 8) / 2] = b1;
     }
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-    mma_16816(c, ha0, ha1, ha2, ha3, b0, b1);
-    // the GEMM's fp16 output, then * scaling, rounded to fp16 again
     const int col = nt * 8 + 2 * t;
-    if (r0) {
-      const float2 o = unpack_half2(pack_half2(c[0], c[1]));
-      reinterpret_cast<uint32_t *>(p.out)[((m0 + g) * HO + col) / 2] =
-          pack_half2(o.x * p.scale, o.y * p.scale);
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      float o[4] = {0.f, 0.f, 0.f, 0.f};
+      mma_16816(o, ha[mt][0], ha[mt][1], ha[mt][2], ha[mt][3], b0, b1);
+      // the GEMM's fp16 output, then * scaling, rounded to fp16 again
+      const int64_t r = m0 + 16 * mt + g;
+      if (rv[mt][0]) {
+        const float2 v = unpack_half2(pack_half2(o[0], o[1]));
+        reinterpret_cast<uint32_t *>(p.out)[(r * HO + col) / 2] =
+            pack_half2(v.x * p.scale, v.y * p.scale);
+      }
+      if (rv[mt][1]) {
+        const float2 v = unpack_half2(pack_half2(o[2], o[3]));
+        reinterpret_cast<uint32_t *>(p.out)[((r + 8) * HO + col) / 2] =
+            pack_half2(v.x * p.scale, v.y * p.scale);
+      }
     }
-    if (r1) {
-      const float2 o = unpack_half2(pack_half2(c[2], c[3]));
-      reinterpret_cast<uint32_t *>(p.out)[((m0 + g + 8) * HO + col) / 2] =
-          pack_half2(o.x * p.scale, o.y * p.scale);
+  }
+  // the copies for the backward
+  if (rank == 0 && threadIdx.x < kTileRows * kRank / 2 && m0 + hrow < a.rows)
+    reinterpret_cast<uint32_t *>(p.h16)[(m0 + hrow) * (kRank / 2) + hpr] = hv;
+  if (ks0 < kend) lora_x16_store(p, rv, m0, H, ks0 * 16 + 2 * t, s0);
+  if (ks1 < kend) lora_x16_store(p, rv, m0, H, ks1 * 16 + 2 * t, s1);
+  if (writer) {  // fp16(A) of this CTA's k-range (re-read: L2-resident)
+    uint32_t *w = reinterpret_cast<uint32_t *>(p.a16);
+    const int k0 = kbeg * 16, k1 = kend * 16;
+    for (int e = threadIdx.x; e < kRank * (k1 - k0) / 2; e += kFwdWarps * 32) {
+      const int row = e / ((k1 - k0) / 2), k = k0 + 2 * (e % ((k1 - k0) / 2));
+      w[((int64_t)row * H + k) / 2] = ld_f16x2(p.a + (int64_t)row * H + k);
     }
   }
 }
@@ -421,9 +510,9 @@ extern "C" int tb_lora_forward(const float *dropped_q, const float *a_q, const f
   args.pos_idx = pos_idx;
   args.rows = rows;
   args.hidden = (int)hidden;
-  // one cluster of kCluster CTAs per 16 rows and adapter (tile 0 also writes the fp16
+  // one cluster of kCluster CTAs per kTileRows rows and adapter (tile 0 also writes the fp16
   // weights, so at least one)
-  const int64_t tiles = rows > 0 ? (rows + 15) / 16 : 1;
+  const int64_t tiles = rows > 0 ? (rows + kTileRows - 1) / kTileRows : 1;
   if (tiles * kCluster > 0x7fffffffLL) return set_error(TB_EINVAL, "lora_forward: too many rows");
   return launch("lora_forward", lora_fwd_kernel, dim3((unsigned)(tiles * kCluster), 2),
                 kFwdWarps * 32, 0, as_stream(stream), args);
