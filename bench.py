@@ -760,6 +760,9 @@ def ours_arm(args, rank, world, local):
     trainer_patch.patch_forward()
     cfg = qwen2_config()
     model = build_qlora_model(cfg, dev, seed=0)
+    # what the patched trainer setup does once the model is loaded (reference:
+    # trainer_patch.py:181-202): the frozen tied embedding / head table held in fp16
+    trainer_patch.prepare_model(model)
     lengths = synth.lengths(seed=0)
     seq = synth.SEQ
     ids, mask, labels = make_batch(lengths, seq, cfg.vocab_size, 100 + rank, dev)

@@ -106,3 +106,43 @@ def test_lora_pair_one_adapter_only():
     rq.float().sum().backward()
     torch.testing.assert_close(lq, rq, rtol=1e-3, atol=1e-4)
     torch.testing.assert_close(x.grad, x2.grad, rtol=1e-3, atol=1e-5)
+
+
+def test_lora_pair_accumulates_into_grad_bucket_views():
+    """Parameters whose .grad are GradBucket views get their weight gradients added into those
+    views by the gradient GEMMs (beta 1) instead of being returned to autograd: after two
+    backward passes the bucket holds twice the gradients the returned-gradient path gives
+    (the same dropout draws each time), and no parameter's .grad left the bucket."""
+    from testt_b200.dist import GradBucket
+    from testt_b200.lora import GRAD_IN_BUCKET, lora_pair
+    from testt_b200.rope import slot_index
+
+    batch, seq, hidden = 3, 40, 256
+    lengths = [33, 7, 40]
+    pos = torch.cat([torch.arange(n) + i * seq for i, n in enumerate(lengths)]).to(DEV)
+    slot = slot_index(pos, batch * seq)
+    x0 = torch.randn(batch * seq, hidden, device=DEV)
+    gq = (torch.randn(pos.numel(), hidden, device=DEV) * 0.1).half()
+    gv = (torch.randn(pos.numel(), 64, device=DEV) * 0.1).half()
+
+    def run(parts):
+        torch.manual_seed(11)
+        x = x0.clone().requires_grad_(True)
+        with torch.autocast(DEV, dtype=torch.float16):
+            lq, lv = lora_pair(parts[0], parts[1], x, pos, slot)
+        torch.autograd.backward([lq, lv], [gq, gv])
+
+    ref_parts = _adapters(hidden, (hidden, 64), 16, 3)
+    run(ref_parts)
+    ref = [t.weight.grad.clone() for _, a, b, _ in ref_parts for t in (a, b)]
+
+    parts = _adapters(hidden, (hidden, 64), 16, 3)
+    params = [t.weight for _, a, b, _ in parts for t in (a, b)]
+    bucket = GradBucket(params)
+    assert all(getattr(p, GRAD_IN_BUCKET, False) for p in params)
+    for _ in range(2):
+        run(parts)
+    for p, r in zip(params, ref):
+        assert p.grad.data_ptr() >= bucket.flat.data_ptr()
+        assert p.grad.data_ptr() < bucket.flat.data_ptr() + bucket.flat.numel() * 4
+        torch.testing.assert_close(p.grad, 2 * r, rtol=1e-4, atol=float(r.abs().max()) * 1e-5)

@@ -46,13 +46,18 @@ class GradBucket:
         self.attach()
 
     def attach(self):
-        """(Re)point every param.grad at its slice of the flat buffer."""
+        """(Re)point every param.grad at its slice of the flat buffer. The parameters are marked
+        (lora.GRAD_IN_BUCKET) so the LoRA node accumulates their gradients into these views
+        inside its gradient GEMMs."""
+        from .lora import GRAD_IN_BUCKET
+
         off = 0
         for p in self.params:
             if p.dtype != torch.float32:
                 raise TypeError("GradBucket holds fp32 trainable parameters only")
             n = p.numel()
             p.grad = self.flat[off:off + n].view_as(p)
+            setattr(p, GRAD_IN_BUCKET, True)
             off += n
 
     def zero(self):

@@ -11,7 +11,8 @@ operations and their roundings, and replaces the glue around the dropout with tw
               xq16, xv16 = fp16(dq[pos_idx]), fp16(dv[pos_idx])
               lora_q = (xq16 @ Aq16^T) @ Bq16^T * scaling_q         (same for v)
               all of it one launch for rank 16 (tb_lora_forward), else tb_lora_gather + cuBLAS
-    backward  the adapter GEMMs (the scaling in their fp32 epilogue, weight gradients in fp32),
+    backward  the adapter GEMMs (the scaling in their fp32 epilogue, weight gradients in fp32,
+              added straight into a GradBucket's .grad views when the parameters have them),
               dx_pad = dropout_q'(dxq) + dropout_v'(dxv) at the real rows, 0 at padding
                                                                    tb_lora_dropout_grad
 instead of (per adapter) index_select + cast in forward and zero-fill + index_add + dropout
@@ -42,6 +43,22 @@ def _fused_ok(aq, bq, av, bv, hidden):
                 or a.data_ptr() % 8 or b.data_ptr() % 8:
             return False
     return True
+
+
+# Attribute dist.GradBucket sets on the parameters whose .grad it holds as views of its flat
+# buffer. For those the backward adds each weight gradient into .grad inside the gradient GEMM
+# (beta 1, fp32) and returns None for it, which is what autograd's accumulation would do with a
+# returned gradient, without its separate add kernel (4 per layer). Hooks registered on such a
+# parameter's gradient do not see these gradients.
+GRAD_IN_BUCKET = "_testt_grad_in_bucket"
+
+
+def _in_bucket(param):
+    if param is None or not getattr(param, GRAD_IN_BUCKET, False):
+        return False
+    g = param.grad
+    return g is not None and g.dtype == torch.float32 and g.shape == param.shape \
+        and g.is_contiguous() and g.device == param.device
 
 
 def _dropout_of(module_dropout):
@@ -108,6 +125,7 @@ class LoraPair(torch.autograd.Function):
                     saved += [x16, h, a16, b16]
             del dq, dv
         ctx.save_for_backward(pos_idx, slot_tok, mq, mv, *saved)
+        ctx.params = (aq, bq, av, bv)  # leaves: for gradients accumulated in place
         ctx.cfg = cfg
         ctx.slots = x_pad.shape[0]
         ctx.hidden = hidden
@@ -121,8 +139,10 @@ class LoraPair(torch.autograd.Function):
         with torch.autocast("cuda", enabled=False):
             grads = []
             dxs = []
-            for g_out, x16, h, a16, b16, s in ((gq_out, xq, hq, aq16, bq16, sq),
-                                               (gv_out, xv, hv, av16, bv16, sv)):
+            pa_q, pb_q, pa_v, pb_v = ctx.params
+            for g_out, x16, h, a16, b16, s, pa, pb in (
+                    (gq_out, xq, hq, aq16, bq16, sq, pa_q, pb_q),
+                    (gv_out, xv, hv, av16, bv16, sv, pa_v, pb_v)):
                 if x16 is None:
                     grads += [None, None]
                     dxs.append(None)
@@ -135,12 +155,22 @@ class LoraPair(torch.autograd.Function):
                 # "* scaling" is taken into the GEMMs' fp32 epilogue (alpha) and the weight
                 # gradients come out of cuBLAS in fp32 (peft under autocast rounds them to fp16
                 # first, then casts): two GEMMs per gradient and no separate scale or cast kernels
-                db = torch.addmm(torch.empty((b16.shape[0], rank), dtype=torch.float32,
-                                             device=h.device),
-                                 g_out.t(), h, beta=0.0, alpha=s, out_dtype=torch.float32)
+                if _in_bucket(pb):  # accumulated by the GEMM itself (beta 1), nothing returned
+                    torch.addmm(pb.grad, g_out.t(), h, beta=1.0, alpha=s,
+                                out_dtype=torch.float32, out=pb.grad)
+                    db = None
+                else:
+                    db = torch.addmm(torch.empty((b16.shape[0], rank), dtype=torch.float32,
+                                                 device=h.device),
+                                     g_out.t(), h, beta=0.0, alpha=s, out_dtype=torch.float32)
                 dh = torch.addmm(torch.empty((rows_, rank), dtype=_F16, device=h.device),
                                  g_out, b16, beta=0.0, alpha=s)
-                da = torch.mm(dh.t(), x16, out_dtype=torch.float32)   # lora_A weight gradient
+                if _in_bucket(pa):  # lora_A weight gradient
+                    torch.addmm(pa.grad, dh.t(), x16, beta=1.0, alpha=1.0,
+                                out_dtype=torch.float32, out=pa.grad)
+                    da = None
+                else:
+                    da = torch.mm(dh.t(), x16, out_dtype=torch.float32)
                 dxs.append(dh @ a16 if need[0] else None)
                 grads += [da, db]
             gx = None
