@@ -181,6 +181,19 @@ int tb_lora_dropout_grad(const uint16_t *dxq, const uint16_t *dxv, const uint8_t
                          int64_t slots, int64_t hidden, float scale_q, float scale_v,
                          void *stream);
 
+/* tb_lora_dropout_grad with the adapters' lora_A input gradients computed inside it: for rank 16,
+ * dx = fp16(dh . a16) (dh fp16 [rows, 16], a16 = fp16(lora_A) [16, hidden], fp32 sums in rank
+ * order, as the fp16 GEMM `dh @ a16` under autocast gives it) for each adapter, then the same
+ * dropout backward and sum into grad fp32 [slots, hidden] (0 at padding slots). Replaces the
+ * two dx GEMMs and the dropout backward of _lora_branch's backward (solution/model.py:195-206).
+ * hidden a multiple of 8; 16-byte aligned dh, a16 and grad. Either adapter may be absent (NULL
+ * dh). */
+int tb_lora_dropout_grad_expand(const uint16_t *dh_q, const uint16_t *a16_q, const uint16_t *dh_v,
+                                const uint16_t *a16_v, const uint8_t *mask_q,
+                                const uint8_t *mask_v, const int32_t *slot_tok, float *grad,
+                                int64_t slots, int64_t hidden, int32_t rank, float scale_q,
+                                float scale_v, void *stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Gated SiLU. Replaces gated_silu_fwd_kernel / gated_silu_bwd_inplace_kernel,
  * solution/mlp.py:31-58 and :61-77.

@@ -146,3 +146,52 @@ def test_lora_pair_accumulates_into_grad_bucket_views():
         assert p.grad.data_ptr() >= bucket.flat.data_ptr()
         assert p.grad.data_ptr() < bucket.flat.data_ptr() + bucket.flat.numel() * 4
         torch.testing.assert_close(p.grad, 2 * r, rtol=1e-4, atol=float(r.abs().max()) * 1e-5)
+
+
+@pytest.mark.parametrize("adapters", ["both", "q", "v"])
+def test_dropout_grad_expand_matches_dx_gemm_then_dropout_grad(adapters):
+    """tb_lora_dropout_grad_expand (dx = fp16(dh . fp16(A)) computed inside the dropout
+    backward) against fp16(dh @ A16) from an fp64 product followed by tb_lora_dropout_grad:
+    within one fp16 ulp of dx (the fp32 sum order of the 16 products may round differently),
+    exact zeros at padding slots and where the mask drops."""
+    from testt_b200 import _lib
+    from testt_b200.rope import slot_index
+
+    g = torch.Generator(device=DEV).manual_seed(9)
+    batch, seq, hidden = 3, 40, 1536
+    lengths = [33, 7, 40]
+    pos = torch.cat([torch.arange(n) + i * seq for i, n in enumerate(lengths)]).to(DEV)
+    slots, rows = batch * seq, pos.numel()
+    slot = slot_index(pos, slots)
+    use = {"both": (True, True), "q": (True, False), "v": (False, True)}[adapters]
+    dh, a16, masks, dxs = [], [], [], []
+    for on in use:
+        if not on:
+            dh.append(None), a16.append(None), masks.append(None), dxs.append(None)
+            continue
+        d = (torch.randn(rows, 16, device=DEV, generator=g) * 0.3).half()
+        a = (torch.randn(16, hidden, device=DEV, generator=g) * 0.05).half()
+        m = torch.rand(slots, hidden, device=DEV, generator=g) > 0.1
+        dh.append(d), a16.append(a), masks.append(m)
+        dxs.append((d.double() @ a.double()).half())
+    scale_q, scale_v = 1 / 0.9, 1 / 0.95
+    got = torch.full((slots, hidden), float("nan"), device=DEV)
+    ref = torch.empty_like(got)
+    st = _lib.stream_of(got)
+    _lib.call("tb_lora_dropout_grad_expand", _lib.ptr(dh[0]), _lib.ptr(a16[0]), _lib.ptr(dh[1]),
+              _lib.ptr(a16[1]), _lib.ptr(masks[0]), _lib.ptr(masks[1]), _lib.ptr(slot),
+              _lib.ptr(got), slots, hidden, 16, scale_q, scale_v, st)
+    _lib.call("tb_lora_dropout_grad", _lib.ptr(dxs[0]), _lib.ptr(dxs[1]), _lib.ptr(masks[0]),
+              _lib.ptr(masks[1]), _lib.ptr(slot), _lib.ptr(ref), slots, hidden, scale_q,
+              scale_v, st)
+    torch.cuda.synchronize()
+    pad = torch.ones(slots, dtype=torch.bool, device=DEV)
+    pad[pos] = False
+    assert torch.all(got[pad] == 0)
+    if adapters != "both":  # one adapter: exactly zero wherever its mask drops
+        m = masks[0] if use[0] else masks[1]
+        assert torch.all(got[(~pad)[:, None] & ~m] == 0)
+    # one fp16 ulp of dx (relative 2^-11), times the dropout scale, per adapter
+    tol = sum(dx.abs().float().max().item() for dx in dxs if dx is not None) * 2 ** -10 * 1.2
+    assert (got - ref).abs().max().item() <= tol
+    assert torch.isfinite(got).all()

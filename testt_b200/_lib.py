@@ -36,6 +36,7 @@ SIGNATURES = {
     "tb_slot_index": [_P, _I64, _I64, _P, _P],
     "tb_lora_gather": [_P, _P, _P, _P, _P, _I64, _I64, _P],
     "tb_lora_dropout_grad": [_P, _P, _P, _P, _P, _P, _I64, _I64, _F, _F, _P],
+    "tb_lora_dropout_grad_expand": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _F, _F, _P],
     "tb_lora_forward": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _F, _P, _P, _P, _P, _P, _P, _P,
                         _P, _I64, _F, _P, _I64, _I64, _I32, _P],
     "tb_swiglu_fwd": [_P, _P, _I64, _I64, _P],

@@ -133,6 +133,97 @@ __global__ void lora_dropout_grad_any(const uint16_t *dxq, const uint16_t *dxv, 
   }
 }
 
+// ---- dropout backward with the rank-16 expansion folded in -----------------------------------
+// dx = fp16(dh . fp16(A)) of each adapter (the lora_A input gradient, an fp16 GEMM output under
+// autocast, K = 16) is computed where the dropout backward needs it instead of being written by
+// two GEMMs and read back: per padded slot p with token tok and column c,
+//   grad[p, c] = drop_q'(dx_q[tok, c]) + drop_v'(dx_v[tok, c])      (0 for padding slots)
+// with drop'(g) = mask ? g * scale : 0 (g when the adapter has no dropout), each product and the
+// sum rounded on their own as in tb_lora_dropout_grad. A CTA holds a 256-column slice of both
+// fp16(A) in shared memory; each warp takes rows, lane l its 8 columns of the slice, the
+// sixteen products of a column summed in rank order in fp32.
+constexpr int kExpandCols = 256;
+constexpr int kExpandRowsPerWarp = 4;
+
+__global__ void __launch_bounds__(kThreads)
+    lora_dropout_grad_expand(const uint16_t *__restrict__ dhq, const uint16_t *__restrict__ aq,
+                             const uint16_t *__restrict__ dhv, const uint16_t *__restrict__ av,
+                             const uint8_t *__restrict__ mq, const uint8_t *__restrict__ mv,
+                             const int32_t *__restrict__ slot_tok, float *__restrict__ g,
+                             int64_t slots, int hidden, float sq, float sv) {
+  pdl_wait();
+  pdl_release();
+  __shared__ uint4 a_sh[2][16][kExpandCols / 8];  // fp16(A) slices: [adapter][rank][8 cols]
+  const int c0 = blockIdx.x * kExpandCols;
+  const int ncols = min(kExpandCols, hidden - c0);
+  for (int e = threadIdx.x; e < 2 * 16 * (kExpandCols / 8); e += blockDim.x) {
+    const int ad = e / (16 * (kExpandCols / 8)), rem = e % (16 * (kExpandCols / 8));
+    const int r = rem / (kExpandCols / 8), v = rem % (kExpandCols / 8);
+    const uint16_t *a = ad == 0 ? aq : av;
+    uint4 val = make_uint4(0u, 0u, 0u, 0u);
+    if (a != nullptr && v * 8 < ncols)
+      val = __ldg(reinterpret_cast<const uint4 *>(a + (int64_t)r * hidden + c0 + v * 8));
+    a_sh[ad][r][v] = val;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = c0 + lane * 8;
+  const bool live = lane * 8 < ncols;
+  const int64_t p0 = ((int64_t)blockIdx.y * (blockDim.x >> 5) + warp) * kExpandRowsPerWarp;
+  for (int i = 0; i < kExpandRowsPerWarp; ++i) {
+    const int64_t p = p0 + i;
+    if (p >= slots) break;
+    const int64_t tok = __ldg(slot_tok + p);
+    float out[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) out[k] = 0.f;
+    if (tok >= 0 && live) {
+#pragma unroll
+      for (int ad = 0; ad < 2; ++ad) {
+        const uint16_t *dh = ad == 0 ? dhq : dhv;
+        if (dh == nullptr) continue;
+        const uint8_t *m = ad == 0 ? mq : mv;
+        const float scale = ad == 0 ? sq : sv;
+        // the token's 16 dh values (the same for the whole warp: one broadcast load)
+        const uint4 h0 = __ldg(reinterpret_cast<const uint4 *>(dh + tok * 16));
+        const uint4 h1 = __ldg(reinterpret_cast<const uint4 *>(dh + tok * 16 + 8));
+        float hf[16];
+        const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float2 f = unpack_half2(hw[j]);
+          hf[2 * j] = f.x;
+          hf[2 * j + 1] = f.y;
+        }
+        float acc[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+          const uint4 av4 = a_sh[ad][r][lane];
+          const uint32_t aw[4] = {av4.x, av4.y, av4.z, av4.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = unpack_half2(aw[j]);
+            acc[2 * j] = fmaf(hf[r], f.x, acc[2 * j]);
+            acc[2 * j + 1] = fmaf(hf[r], f.y, acc[2 * j + 1]);
+          }
+        }
+        uint2 mk = make_uint2(0x01010101u, 0x01010101u);
+        if (m != nullptr) mk = __ldg(reinterpret_cast<const uint2 *>(m + p * hidden + c));
+        const uint8_t *mb = reinterpret_cast<const uint8_t *>(&mk);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float dx = __half2float(__float2half_rn(acc[k]));  // the fp16 GEMM output
+          const float gk = m == nullptr ? dx : (mb[k] ? __fmul_rn(dx, scale) : 0.f);
+          out[k] = ad == 0 ? gk : __fadd_rn(out[k], gk);
+        }
+      }
+    }
+    if (live) store8f(g + p * hidden + c, out);
+  }
+}
+
 // ---- the adapters' forward in one kernel (rank 16) -------------------------------------------
 // Per tile of 16 real rows and adapter (blockIdx.y: 0 = q, 1 = v):
 //   x16 = fp16(dropped[pos_idx[m]])                         (index_select + the autocast cast)
@@ -468,6 +559,35 @@ extern "C" int tb_lora_dropout_grad(const uint16_t *dxq, const uint16_t *dxv,
   }
   return launch("lora_dropout_grad", lora_dropout_grad_any, grid_for(slots * hidden), kThreads, 0,
                 st, dxq, dxv, mask_q, mask_v, slot_tok, grad, slots, hidden, scale_q, scale_v);
+}
+
+extern "C" int tb_lora_dropout_grad_expand(const uint16_t *dh_q, const uint16_t *a16_q,
+                                           const uint16_t *dh_v, const uint16_t *a16_v,
+                                           const uint8_t *mask_q, const uint8_t *mask_v,
+                                           const int32_t *slot_tok, float *grad, int64_t slots,
+                                           int64_t hidden, int32_t rank, float scale_q,
+                                           float scale_v, void *stream) {
+  if (rank != 16)
+    return set_error(TB_EINVAL, "lora_dropout_grad_expand: rank %d (the kernel takes rank 16)",
+                     rank);
+  if (slots < 0 || hidden <= 0 || hidden % 8 || hidden > (1 << 30))
+    return set_error(TB_EINVAL, "lora_dropout_grad_expand: slots %lld hidden %lld",
+                     (long long)slots, (long long)hidden);
+  if (slots == 0) return TB_OK;
+  if (!slot_tok || !grad) return set_error(TB_EINVAL, "lora_dropout_grad_expand: slot_tok, grad required");
+  if ((dh_q && !a16_q) || (dh_v && !a16_v))
+    return set_error(TB_EINVAL, "lora_dropout_grad_expand: an adapter's dh needs its fp16 A");
+  if (!aligned(grad, 16) || (dh_q && (!aligned(dh_q, 16) || !aligned(a16_q, 16))) ||
+      (dh_v && (!aligned(dh_v, 16) || !aligned(a16_v, 16))) || (mask_q && !aligned(mask_q, 8)) ||
+      (mask_v && !aligned(mask_v, 8)))
+    return set_error(TB_EALIGN, "lora_dropout_grad_expand: misaligned buffer");
+  const int64_t rows_per_cta = (int64_t)(kThreads / 32) * kExpandRowsPerWarp;
+  const int64_t ys = (slots + rows_per_cta - 1) / rows_per_cta;
+  if (ys > 65535) return set_error(TB_EINVAL, "lora_dropout_grad_expand: too many slots");
+  const dim3 grid((unsigned)((hidden + kExpandCols - 1) / kExpandCols), (unsigned)ys);
+  return launch("lora_dropout_grad_expand", lora_dropout_grad_expand, grid, kThreads, 0,
+                as_stream(stream), dh_q, a16_q, dh_v, a16_v, mask_q, mask_v, slot_tok, grad, slots,
+                (int)hidden, scale_q, scale_v);
 }
 
 extern "C" int tb_lora_forward(const float *dropped_q, const float *a_q, const float *b_q,

@@ -13,8 +13,9 @@ operations and their roundings, and replaces the glue around the dropout with tw
               all of it one launch for rank 16 (tb_lora_forward), else tb_lora_gather + cuBLAS
     backward  the adapter GEMMs (the scaling in their fp32 epilogue, weight gradients in fp32,
               added straight into a GradBucket's .grad views when the parameters have them),
-              dx_pad = dropout_q'(dxq) + dropout_v'(dxv) at the real rows, 0 at padding
-                                                                   tb_lora_dropout_grad
+              dx_pad = dropout_q'(dh_q . Aq16) + dropout_v'(dh_v . Av16) at the real rows, 0 at
+              padding                            tb_lora_dropout_grad_expand (rank 16; else the
+                                                 dx GEMMs + tb_lora_dropout_grad)
 instead of (per adapter) index_select + cast in forward and zero-fill + index_add + dropout
 backward + the sum of the two in backward.
 """
@@ -138,7 +139,11 @@ class LoraPair(torch.autograd.Function):
         need = ctx.needs_input_grad
         with torch.autocast("cuda", enabled=False):
             grads = []
-            dxs = []
+            dxs, dhs, a16s = [], [], []
+            # rank 16: the lora_A input gradients dh . fp16(A) are computed inside the dropout
+            # backward (tb_lora_dropout_grad_expand), not by two GEMMs
+            expand = need[0] and ctx.hidden % 8 == 0 and \
+                all(h is None or h.shape[1] == _RANK for h in (hq, hv))
             pa_q, pb_q, pa_v, pb_v = ctx.params
             for g_out, x16, h, a16, b16, s, pa, pb in (
                     (gq_out, xq, hq, aq16, bq16, sq, pa_q, pb_q),
@@ -146,6 +151,8 @@ class LoraPair(torch.autograd.Function):
                 if x16 is None:
                     grads += [None, None]
                     dxs.append(None)
+                    dhs.append(None)
+                    a16s.append(None)
                     continue
                 if g_out is None:
                     g_out = torch.zeros((x16.shape[0], b16.shape[0]), dtype=_F16,
@@ -171,7 +178,9 @@ class LoraPair(torch.autograd.Function):
                     da = None
                 else:
                     da = torch.mm(dh.t(), x16, out_dtype=torch.float32)
-                dxs.append(dh @ a16 if need[0] else None)
+                dxs.append(dh @ a16 if need[0] and not expand else None)
+                dhs.append(dh)
+                a16s.append(a16.contiguous())
                 grads += [da, db]
             gx = None
             if need[0]:
@@ -179,9 +188,15 @@ class LoraPair(torch.autograd.Function):
                                  device=slot_tok.device)
                 scale_q = float(1.0 / (1.0 - pq)) if mq is not None else 1.0
                 scale_v = float(1.0 / (1.0 - pv)) if mv is not None else 1.0
-                _lib.call("tb_lora_dropout_grad", _lib.ptr(dxs[0]), _lib.ptr(dxs[1]),
-                          _lib.ptr(mq), _lib.ptr(mv), _lib.ptr(slot_tok), _lib.ptr(gx),
-                          ctx.slots, ctx.hidden, scale_q, scale_v, _lib.stream_of(gx))
+                if expand:
+                    _lib.call("tb_lora_dropout_grad_expand", _lib.ptr(dhs[0]), _lib.ptr(a16s[0]),
+                              _lib.ptr(dhs[1]), _lib.ptr(a16s[1]), _lib.ptr(mq), _lib.ptr(mv),
+                              _lib.ptr(slot_tok), _lib.ptr(gx), ctx.slots, ctx.hidden, _RANK,
+                              scale_q, scale_v, _lib.stream_of(gx))
+                else:
+                    _lib.call("tb_lora_dropout_grad", _lib.ptr(dxs[0]), _lib.ptr(dxs[1]),
+                              _lib.ptr(mq), _lib.ptr(mv), _lib.ptr(slot_tok), _lib.ptr(gx),
+                              ctx.slots, ctx.hidden, scale_q, scale_v, _lib.stream_of(gx))
         return (gx, grads[0], grads[1], grads[2], grads[3], None, None, None)
 
 
