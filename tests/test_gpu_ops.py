@@ -456,6 +456,36 @@ def test_head_stats_config4_rows_vs_oracle():
     assert_ulp(work, rdl, 1, "dlogits")
 
 
+@pytest.mark.parametrize("rows", [40, 1300])
+def test_head_stats_first_argmax_ties_both_kernels(rows):
+    """Integer-valued logits tie often, also across the column ranges that the cluster kernel
+    (few rows: a row over up to 8 CTAs) gives to different CTAs; 1300 rows take the
+    one-CTA-per-row kernel. Hits exact (first argmax), loss/entropy rtol 1e-4, dlogits 1 ulp."""
+    from testt_b200.head import head_stats_grad
+
+    vocab = 20000
+    g = torch.Generator().manual_seed(rows)
+    logits = torch.randint(-6, 7, (rows, vocab), generator=g).half()
+    targets = torch.randint(0, vocab, (rows,), generator=g)
+    for r in range(rows):
+        ties = torch.nonzero(logits[r] == logits[r].max()).squeeze(1)
+        kind = r % 3
+        if kind == 0:
+            targets[r] = ties[0]
+        elif kind == 1:
+            targets[r] = ties[-1]
+    targets[5::11] = -100
+    scale = 64.0 / rows
+    work = logits.to(DEV)
+    ent, loss, correct = head_stats_grad(work, targets.to(DEV), scale)
+    rent, rloss, rcorrect, rdl = ops.head_stats_exact(logits, targets, scale)
+    assert torch.equal(correct.cpu().bool(), rcorrect)
+    assert int(rcorrect.sum()) >= rows // 4
+    assert_rel(loss, rloss, 1e-4, "loss")
+    assert_rel(ent, rent, 1e-4, "entropy")
+    assert_ulp(work, rdl, 1, "dlogits")
+
+
 def test_head_full_config4_properties():
     """Config 4 at full size (2048 rows, 1331 labelled): the fused head against an fp32 torch
     computation of the same fp16 logits on the GPU; loss/entropy rtol 1e-4, hits exact."""

@@ -6,8 +6,11 @@
 // vectors of 8 logits, four vectors in flight per thread, followed by a shuffle + shared-memory
 // merge of the per-thread states. Sweep 2 (labelled rows only) rewrites the row in place with
 // fp16((exp(z - lse) - [c == target]) * grad_scale). Rounding: z are the fp16 logits widened to
-// fp32, exactly as the reference reads them; exponentials use the fast __expf that the
-// reference's tl.exp lowers to.
+// fp32, exactly as the reference reads them; exponentials are the MUFU 2^x that the fast exp of
+// the reference's tl.exp lowers to, with the max (or lse) shift folded into the FFMA forming its
+// argument. Per logit: one max, one FFMA + ex2, one add, one FFMA in sweep 1 (the first argmax
+// is searched only in a vector that raises the running max), one FFMA + ex2 + multiply in sweep
+// 2 (the one-hot term only in the vector holding the target).
 #include <math_constants.h>
 
 #include <mutex>
@@ -64,6 +67,66 @@ __device__ __forceinline__ Online shfl_online(const Online &a, int off) {
   return b;
 }
 
+constexpr float kLog2e = 1.4426950408889634f;
+
+// 2^x on the MUFU (PTX ex2.approx); e^x is taken as 2^(x log2 e), with the shift by the
+// running max folded into one FFMA: e^(z - m) = 2^(z log2e - m log2e)
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Folds 8 consecutive logits (columns c0 .. c0 + 7) into the state. The running max is also the
+// best value; the first index of a new maximum is searched only when the max grows (a tie with
+// an earlier maximum keeps the earlier index: the first argmax).
+__device__ __forceinline__ void online_add8(Online &o, const float (&z)[8], int64_t c0) {
+  float lm = z[0];
+#pragma unroll
+  for (int k = 1; k < 8; ++k) lm = fmaxf(lm, z[k]);
+  if (lm > o.m) {
+    const float sc = ex2f((o.m - lm) * kLog2e);  // 0 while m is -inf
+    o.s *= sc;
+    o.dz *= sc;
+    o.m = lm;
+    o.best = lm;
+    int first = 7;
+#pragma unroll
+    for (int k = 6; k >= 0; --k)
+      if (z[k] == lm) first = k;
+    o.idx = c0 + first;
+  }
+  const float ml = o.m * kLog2e;
+  float s0 = 0.f, s1 = 0.f, d0 = 0.f, d1 = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; k += 2) {
+    const float e0 = ex2f(fmaf(z[k], kLog2e, -ml));
+    const float e1 = ex2f(fmaf(z[k + 1], kLog2e, -ml));
+    s0 += e0;
+    s1 += e1;
+    d0 = fmaf(e0, z[k], d0);
+    d1 = fmaf(e1, z[k + 1], d1);
+  }
+  o.s += s0 + s1;
+  o.dz += d0 + d1;
+}
+
+// fp16((e^(z - lse) - [column == target]) * scale) of 8 consecutive logits (columns c0 ..),
+// in place; nl = -lse log2 e. The target test runs only in the one vector that holds it.
+__device__ __forceinline__ void dlogits8(uint16_t *p, const float (&z)[8], float nl,
+                                         int64_t c0, int64_t target, float scale) {
+  float g[8];
+  if ((uint64_t)(target - c0) < 8u) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      g[k] = (ex2f(fmaf(z[k], kLog2e, nl)) - (c0 + k == target ? 1.f : 0.f)) * scale;
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) g[k] = ex2f(fmaf(z[k], kLog2e, nl)) * scale;
+  }
+  store8h(p, g);
+}
+
 __global__ void __launch_bounds__(kThreads)
     head_stats_grad_rows(uint16_t *__restrict__ logits, const int64_t *__restrict__ targets,
                          float *__restrict__ entropy, float *__restrict__ loss,
@@ -90,27 +153,7 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
     for (int r = 0; r < kUnroll; ++r) {
       const int64_t v = v0 + (int64_t)r * kThreads;
-      if (v < nvec) {
-        float lm = z[r][0];
-#pragma unroll
-        for (int k = 1; k < 8; ++k) lm = fmaxf(lm, z[r][k]);
-        if (lm > o.m) {
-          const float sc = __expf(o.m - lm);
-          o.s *= sc;
-          o.dz *= sc;
-          o.m = lm;
-        }
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float e = __expf(z[r][k] - o.m);
-          o.s += e;
-          o.dz += e * z[r][k];
-          if (z[r][k] > o.best) {
-            o.best = z[r][k];
-            o.idx = v * 8 + k;
-          }
-        }
-      }
+      if (v < nvec) online_add8(o, z[r], v * 8);
     }
   }
   for (int64_t c = nvec * 8 + threadIdx.x; c < vocab; c += kThreads)
@@ -138,6 +181,7 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
   if (!labelled) return;
   const float lse = lse_sh;
+  const float nl = -lse * kLog2e;
   for (int64_t v0 = threadIdx.x; v0 < nvec; v0 += (int64_t)kThreads * kUnroll) {
     float z[kUnroll][8];
 #pragma unroll
@@ -148,15 +192,7 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
     for (int r = 0; r < kUnroll; ++r) {
       const int64_t v = v0 + (int64_t)r * kThreads;
-      if (v < nvec) {
-        float g[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float hot = (v * 8 + k == target) ? 1.f : 0.f;
-          g[k] = (__expf(z[r][k] - lse) - hot) * grad_scale;
-        }
-        store8h(base + v * 8, g);
-      }
+      if (v < nvec) dlogits8(base + v * 8, z[r], nl, v * 8, target, grad_scale);
     }
   }
   for (int64_t c = nvec * 8 + threadIdx.x; c < vocab; c += kThreads) {
@@ -218,27 +254,7 @@ __global__ void __launch_bounds__(kPartThreads)
 #pragma unroll
       for (int r = 0; r < kUnroll; ++r) {
         const int64_t c = c0 + (int64_t)r * kPartThreads * 8;
-        if (c < vend) {
-          float lm = z[r][0];
-#pragma unroll
-          for (int k = 1; k < 8; ++k) lm = fmaxf(lm, z[r][k]);
-          if (lm > o.m) {
-            const float sc = __expf(o.m - lm);
-            o.s *= sc;
-            o.dz *= sc;
-            o.m = lm;
-          }
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const float e = __expf(z[r][k] - o.m);
-            o.s += e;
-            o.dz += e * z[r][k];
-            if (z[r][k] > o.best) {
-              o.best = z[r][k];
-              o.idx = col_offset + c + k;
-            }
-          }
-        }
+        if (c < vend) online_add8(o, z[r], col_offset + c);
       }
     }
     vlo = vend;
@@ -370,14 +386,11 @@ __global__ void __launch_bounds__(256)
     vpr.divmod(i, row, v);
     const int64_t target = __ldg(targets + row);
     if (target == -100) continue;
-    const float l = __ldg(lse + row);
+    const float nl = -__ldg(lse + row) * kLog2e;
     uint16_t *p = logits + (int64_t)row * ld + (int64_t)v * 8;
     float z[8];
     load8h_rw(p, z);
-    const int64_t c0 = col_offset + (int64_t)v * 8;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) z[k] = (__expf(z[k] - l) - (c0 + k == target ? 1.f : 0.f)) * grad_scale;
-    store8h(p, z);
+    dlogits8(p, z, nl, col_offset + (int64_t)v * 8, target, grad_scale);
   }
 }
 
