@@ -195,6 +195,34 @@ int tb_lora_dropout_grad_expand(const uint16_t *dh_q, const uint16_t *a16_q, con
                                 float scale_v, void *stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * Causal attention over packed variable-length sequences with grouped key/value heads. Replaces
+ * the decoder layer's SDPA over the padded layout (solution/model.py:242-247) for the real rows:
+ * q fp16 [total, n_heads, head_dim], k, v fp16 [total, n_kv, head_dim] (token-major, the
+ * sequences packed back to back), cu_seqlens int32 [batch + 1] (sequence b holds tokens
+ * cu[b] .. cu[b+1]-1, no longer than max_len); query i of a sequence attends to its keys 0..i;
+ * query head h uses key/value head h / (n_heads / n_kv). head_dim 128.
+ * tb_attn_varlen_fwd: out fp16 [total, n_heads, head_dim] = softmax(scale q k^T) v, and
+ *   lse fp32 [n_heads, total], the base-2 log-sum-exp of scale * log2(e) * q k^T per query (what
+ *   the backward recomputes the probabilities from).
+ * ------------------------------------------------------------------------------------------- */
+int tb_attn_varlen_fwd(const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                       const int32_t *cu_seqlens, uint16_t *out, float *lse, int64_t batch,
+                       int64_t total, int64_t max_len, int32_t n_heads, int32_t n_kv,
+                       int32_t head_dim, float scale, void *stream);
+
+/* tb_attn_varlen_bwd: from the forward's q, k, v, out, lse and the output gradient dout
+ *   (fp16 [total, n_heads, head_dim]): dq fp16 [total, n_heads, head_dim], dk, dv fp16
+ *   [total, n_kv, head_dim] (the query heads of a group summed in head order in fp32, rounded
+ *   once). Scratch the caller provides: delta fp32 [n_heads, total] (rowsum(dout o out)),
+ *   dk_part, dv_part fp32 [total, n_heads, head_dim] (per-query-head partials). Deterministic. */
+int tb_attn_varlen_bwd(const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                       const uint16_t *out, const uint16_t *dout, const float *lse,
+                       const int32_t *cu_seqlens, uint16_t *dq, uint16_t *dk, uint16_t *dv,
+                       float *delta, float *dk_part, float *dv_part, int64_t batch, int64_t total,
+                       int64_t max_len, int32_t n_heads, int32_t n_kv, int32_t head_dim,
+                       float scale, void *stream);
+
+/* ---------------------------------------------------------------------------------------------
  * Gated SiLU. Replaces gated_silu_fwd_kernel / gated_silu_bwd_inplace_kernel,
  * solution/mlp.py:31-58 and :61-77.
  *   gu fp16 [rows, 2*inter] = [gate | up];  act = fp16(gate / (1 + exp(-gate)) * up)

@@ -1,0 +1,92 @@
+"""Causal variable-length GQA attention (tb_attn_varlen_fwd / _bwd) against an fp64 PyTorch
+restatement of the reference's attention restricted to the real rows (solution/model.py:242-247:
+softmax(q k^T * scale + causal/padding mask) v per sequence, key/value heads shared by groups of
+query heads). Outputs within fp16 rounding of the fp16 operands' exact result."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _case(lengths, nh, nkv, seed, d=128):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    total = sum(lengths)
+    q = torch.randn(total, nh, d, device=DEV, generator=g).half()
+    k = torch.randn(total, nkv, d, device=DEV, generator=g).half()
+    v = torch.randn(total, nkv, d, device=DEV, generator=g).half()
+    cu = torch.zeros(len(lengths) + 1, dtype=torch.int32, device=DEV)
+    cu[1:] = torch.tensor(lengths, device=DEV).cumsum(0)
+    return q, k, v, cu
+
+
+def _reference(q, k, v, cu, scale):
+    """fp64 attention per sequence: (out [T, H, D], lse2 [H, T])."""
+    nh, nkv = q.shape[1], k.shape[1]
+    outs, lses = [], []
+    for b in range(cu.numel() - 1):
+        s, e = int(cu[b]), int(cu[b + 1])
+        qq = q[s:e].double().transpose(0, 1)                                   # [H, L, D]
+        kk = k[s:e].double().transpose(0, 1).repeat_interleave(nh // nkv, 0)   # [H, L, D]
+        vv = v[s:e].double().transpose(0, 1).repeat_interleave(nh // nkv, 0)
+        sc = qq @ kk.transpose(1, 2) * scale
+        mask = torch.ones(e - s, e - s, dtype=torch.bool, device=q.device).tril()
+        sc = sc.masked_fill(~mask, float("-inf"))
+        lses.append(torch.logsumexp(sc, -1) / math.log(2.0))                   # [H, L]
+        outs.append((torch.softmax(sc, -1) @ vv).transpose(0, 1))               # [L, H, D]
+    return torch.cat(outs, 0), torch.cat(lses, 1)
+
+
+@pytest.mark.parametrize("lengths", [[149, 131, 193, 148], [1, 64, 65, 7, 200], [512]])
+def test_attention_forward_matches_reference(lengths):
+    from testt_b200.attention import attn_forward
+
+    q, k, v, cu = _case(lengths, 12, 2, sum(lengths))
+    scale = 1.0 / math.sqrt(128)
+    out, lse = attn_forward(q, k, v, cu, max(lengths), scale)
+    ref, rlse = _reference(q, k, v, cu, scale)
+    torch.testing.assert_close(out.double(), ref, rtol=0, atol=4e-3)
+    torch.testing.assert_close(lse.double(), rlse, rtol=0, atol=1e-3)
+
+
+@pytest.mark.parametrize("lengths", [[149, 131, 193, 148], [1, 64, 65, 7, 200], [512]])
+def test_attention_backward_matches_reference(lengths):
+    """dq, dk, dv against autograd of the fp64 restatement (grouped heads summed exactly):
+    within 2 % of each gradient's largest element (fp16 operands of P, dS and the outputs)."""
+    from testt_b200.attention import varlen_attention
+
+    nh, nkv = 12, 2
+    q, k, v, cu = _case(lengths, nh, nkv, 7 + sum(lengths))
+    g = torch.Generator(device=DEV).manual_seed(3)
+    dout = torch.randn(q.shape, device=DEV, generator=g).half()
+    scale = 1.0 / math.sqrt(128)
+    qq, kk, vv = (x.clone().requires_grad_(True) for x in (q, k, v))
+    out = varlen_attention(qq, kk, vv, cu, max(lengths), scale)
+    out.backward(dout)
+    rq, rk, rv = (x.double().requires_grad_(True) for x in (q, k, v))
+    ref, _ = _reference(rq, rk, rv, cu, scale)
+    ref.backward(dout.double())
+    for got, want, name in ((qq.grad, rq.grad, "dq"), (kk.grad, rk.grad, "dk"),
+                            (vv.grad, rv.grad, "dv")):
+        assert got.dtype == torch.float16 and got.shape == want.shape
+        err = (got.double() - want).abs().max().item()
+        assert err <= 2e-2 * want.abs().max().item(), (name, err, want.abs().max().item())
+        rel = (got.double() - want).norm() / want.norm()
+        assert rel < 3e-3, (name, float(rel))
+
+
+def test_attention_backward_is_deterministic():
+    from testt_b200.attention import varlen_attention
+
+    q, k, v, cu = _case([149, 131, 193, 148], 12, 2, 5)
+    dout = torch.randn(q.shape, device=DEV).half()
+    grads = []
+    for _ in range(2):
+        qq, kk, vv = (x.clone().requires_grad_(True) for x in (q, k, v))
+        varlen_attention(qq, kk, vv, cu, 193, 0.088).backward(dout)
+        grads.append((qq.grad, kk.grad, vv.grad))
+    for a, b in zip(*grads):
+        assert torch.equal(a, b)

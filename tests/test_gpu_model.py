@@ -94,14 +94,21 @@ def test_fused_step_matches_unpatched_model(lora_model, attention):
         pytest.skip("torch.nn.attention.varlen is not available")
     ref = run(lora_model, fused=False)
     _lib.reset_call_count()
-    saved = model.USE_VARLEN_ATTENTION, model.USE_FLASH_ATTN
+    saved = model.USE_VARLEN_ATTENTION, model.USE_FLASH_ATTN, model.USE_OWN_ATTENTION
     model.USE_VARLEN_ATTENTION = attention != "padded" and saved[0]
     model.USE_FLASH_ATTN = attention == "flash_varlen"
+    model.USE_OWN_ATTENTION = False
     try:
         got = run(lora_model, fused=True)
     finally:
-        model.USE_VARLEN_ATTENTION, model.USE_FLASH_ATTN = saved
+        model.USE_VARLEN_ATTENTION, model.USE_FLASH_ATTN, model.USE_OWN_ATTENTION = saved
     assert _lib.call_count() > 0, "the fused step must run the native kernels"
+    _assert_same_step(got, ref)
+
+
+def _assert_same_step(got, ref):
+    """The fused step's loss, LoRA gradients, entropy, accuracy and rewind rows against the
+    unpatched model's (the tolerances of the reference's solution/test_model.py)."""
     assert abs(got[0] - ref[0]) / ref[0] < 2e-3, (got[0], ref[0])
     assert set(got[1]) == set(ref[1]) and ref[1]
     for name, grad in ref[1].items():
@@ -112,6 +119,41 @@ def test_fused_step_matches_unpatched_model(lora_model, attention):
     assert got[4][1] == ref[4][1]
     for a, b in zip(got[4][0], ref[4][0]):
         assert abs(a - b) / b < 2e-3, (got[4][0], ref[4][0])
+
+
+@pytest.fixture(scope="module")
+def lora_model_d128():
+    """The same small model with head dimension 128 (4 query heads of 128 over 2 key/value
+    heads), the shape the library's own attention kernels take."""
+    from testt_b200.qlora import build_qlora_model, qwen2_config
+
+    cfg = qwen2_config(vocab=1000, hidden=512, inter=512, layers=2, heads=4, kv_heads=2,
+                       max_pos=256, theta=10000.0)
+    return build_qlora_model(cfg, DEV, seed=0, weight_std=0.05, lora_b_std=0.05, bias_std=0.1,
+                             norm_jitter=True)
+
+
+def test_fused_step_with_own_attention_matches_unpatched_model(lora_model_d128):
+    """Head dimension 128: the variable-length attention runs through tb_attn_varlen_fwd / _bwd
+    (checked), and the step matches the unpatched model as with the other attention forms."""
+    from testt_b200 import attention, model
+
+    calls = []
+    original = attention.varlen_attention
+
+    def counted(*args):
+        calls.append(1)
+        return original(*args)
+
+    ref = run(lora_model_d128, fused=False)
+    attention.varlen_attention = counted
+    try:
+        assert model.USE_OWN_ATTENTION and model.USE_VARLEN_ATTENTION
+        got = run(lora_model_d128, fused=True)
+    finally:
+        attention.varlen_attention = original
+    assert len(calls) == 2, "each layer's attention must run the library's kernels"
+    _assert_same_step(got, ref)
 
 
 def test_kept_weights_give_the_same_step(lora_model):

@@ -39,6 +39,9 @@ SIGNATURES = {
     "tb_lora_dropout_grad_expand": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _F, _F, _P],
     "tb_lora_forward": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _F, _P, _P, _P, _P, _P, _P, _P,
                         _P, _I64, _F, _P, _I64, _I64, _I32, _P],
+    "tb_attn_varlen_fwd": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _F, _P],
+    "tb_attn_varlen_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64,
+                           _I32, _I32, _I32, _F, _P],
     "tb_swiglu_fwd": [_P, _P, _I64, _I64, _P],
     "tb_swiglu_bwd_inplace": [_P, _P, _I64, _I64, _P],
     "tb_head_stats_grad": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P],

@@ -13,7 +13,8 @@ Per decoder layer, with s the fp32 residual stream of the M real tokens:
     lq, lv     = LoRA(dropout(y_pad))                 lora.lora_pair: PyTorch dropout (same draws),
                                                       tb_lora_gather, cuBLAS; tb_lora_dropout_grad
     q, k, v    = rope_tokens(qkv, lq, lv)             tb_rope_tokens_fwd, token-major [M, H, 128]
-    a          = varlen causal attention(q, k, v)     FlashAttention 2 varlen (GQA in-kernel),
+    a          = varlen causal attention(q, k, v)     tb_attn_varlen_fwd / _bwd (sm_100, head
+                                                      dim 128), else FlashAttention 2 varlen,
                                                       else PyTorch's varlen flash kernels
     o          = a @ Wo^T                             cuBLAS
     s, y2, _   = add_rmsnorm(s, o)                    tb_add_rmsnorm_fwd
@@ -32,6 +33,7 @@ import threading
 
 import torch
 
+from . import attention as _own_attn
 from .head import IGNORE_INDEX, fused_head_loss
 from .mlp import layer_mlp
 from .nf4 import LayerWeights, layer_linear
@@ -50,7 +52,11 @@ except ImportError:
 
 
 def _varlen_attn(q, k, v, cu_seqlens, max_len, scale):
-    """Causal attention over the packed sequences of cu_seqlens (token-major q, k, v)."""
+    """Causal attention over the packed sequences of cu_seqlens (token-major q, k, v): this
+    library's kernels (attention.varlen_attention) on sm_100 with head dim 128, else
+    FlashAttention 2's varlen kernels or PyTorch's."""
+    if USE_OWN_ATTENTION and _own_attn.supported(q, k, v):
+        return _own_attn.varlen_attention(q, k, v, cu_seqlens, max_len, scale)
     if _flash_varlen is not None and USE_FLASH_ATTN:
         return _flash_varlen(q, k, v, cu_seqlens, cu_seqlens, max_len, max_len,
                              softmax_scale=scale, causal=True)
@@ -58,10 +64,21 @@ def _varlen_attn(q, k, v, cu_seqlens, max_len, scale):
                          window_size=(-1, 0))
 
 
+USE_OWN_ATTENTION = True  # tb_attn_varlen_fwd / _bwd
+
+
+def _varlen_available(head_dim, device):
+    """Whether some variable-length attention runs here: the library's kernels (sm_100, head
+    dim 128) or one of the fallbacks."""
+    if USE_OWN_ATTENTION and head_dim == _own_attn.HEAD_DIM and \
+            torch.cuda.get_device_capability(device)[0] == 10:
+        return True
+    return (_flash_varlen is not None and USE_FLASH_ATTN) or _torch_varlen is not None
 USE_FLASH_ATTN = True
 
-# causal attention over each sequence's real tokens (token-major) when available
-USE_VARLEN_ATTENTION = _torch_varlen is not None or _flash_varlen is not None
+# causal attention over each sequence's real tokens (token-major); the library's own kernels
+# need no optional package, the fallbacks for other GPUs or head sizes do
+USE_VARLEN_ATTENTION = True
 
 # Keep each layer's fp16 weights, unpacked once per step in the forward, for the backward (2.6 GB
 # for Qwen2.5-1.5B, released layer by layer as the backward passes), instead of unpacking them
@@ -301,7 +318,8 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
     dev = input_ids.device
     padded = batch * seq
     static = active_static_batch()
-    varlen = USE_VARLEN_ATTENTION and (static is None or static.cu_seqlens is not None)
+    varlen = USE_VARLEN_ATTENTION and _varlen_available(plan.head_dim, dev) and \
+        (static is None or static.cu_seqlens is not None)
     if static is None:
         pos_idx = attention_mask.reshape(-1).nonzero().squeeze(1)   # sorted, one host sync
         slot_tok = slot_index(pos_idx, padded)                      # shared by every layer
