@@ -9,8 +9,10 @@
 // At the step's sizes (4 sequences of 131-193 tokens, 12 query heads over 2 key/value heads,
 // head dim 128) the work is small (about 0.3 GFLOP forward per layer) and latency-bound, so the
 // kernels are plain tensor-core tiles (mma.sync m16n8k16, fp16 operands, fp32 accumulation)
-// staged through shared memory (cp.async, the next key block copied while one is used) and
-// read with ldmatrix, one CTA per (64-query block, head, sequence):
+// staged through shared memory (cp.async, the next block copied while one is used) and read
+// with ldmatrix, one CTA per (64-query block, head, sequence), two warp groups per CTA taking
+// alternate key (or query) blocks and merging their partial results at the end, so a CTA's
+// serial chain is half its blocks:
 //   forward   S = Q K^T, online softmax in base 2 (the scale folded with log2 e), O += P V;
 //             writes O (fp16) and the base-2 log-sum-exp per (head, query) for the backward.
 // Rows of a sequence's last block past its length are computed but never stored.
@@ -24,7 +26,8 @@ namespace {
 constexpr int kD = 128;       // head dimension the kernels take
 constexpr int kBlock = 64;    // queries per CTA, keys per step
 constexpr int kLd = kD + 8;   // shared-memory row stride in halves (272 B: conflict-free ldmatrix)
-constexpr int kWarps = 4;     // 16 query rows each
+constexpr int kWarps = 4;     // per warp group: 16 rows each
+constexpr int kCtaThreads = 2 * kWarps * 32;  // two warp groups take alternate blocks
 constexpr int kTileHalves = kBlock * kLd;
 
 __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
@@ -56,12 +59,11 @@ __device__ __forceinline__ float attn_ex2(float x) {
 }
 
 // rows [0, nrows) of a 64 x 128 tile from a token-major tensor (row stride ld halves) into
-// shared memory, asynchronously (cp.async, 16 bytes a copy; rows past nrows are zero-filled)
+// shared memory, asynchronously (cp.async, 16 bytes a copy, threads tid of nthr; rows past
+// nrows are zero-filled)
 __device__ __forceinline__ void load_tile_async(uint16_t *sm, const uint16_t *g, int64_t ld,
-                                                int nrows) {
-#pragma unroll
-  for (int j = 0; j < kBlock * (kD / 8) / (kWarps * 32); ++j) {
-    const int i = threadIdx.x + j * kWarps * 32;
+                                                int nrows, int tid, int nthr) {
+  for (int i = tid; i < kBlock * (kD / 8); i += nthr) {
     const int r = i >> 4, c = (i & 15) * 8;
     const bool in = r < nrows;
     const uint16_t *src = g + (in ? r * ld + c : 0);
@@ -69,6 +71,11 @@ __device__ __forceinline__ void load_tile_async(uint16_t *sm, const uint16_t *g,
                  "l"(src), "r"(in ? 16 : 0)
                  : "memory");
   }
+}
+
+// barrier of one warp group (4 warps) of the CTA
+__device__ __forceinline__ void wg_sync(int wg) {
+  asm volatile("bar.sync %0, %1;" ::"r"(wg + 1), "r"(kWarps * 32) : "memory");
 }
 
 __device__ __forceinline__ void cp_async_commit() {
@@ -99,12 +106,13 @@ struct FwdArgs {
   float scale_log2;  // softmax scale * log2(e)
 };
 
-__global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const __grid_constant__ FwdArgs a) {
+__global__ void __launch_bounds__(kCtaThreads) attn_fwd_kernel(const __grid_constant__ FwdArgs a) {
   pdl_wait();
   pdl_release();
   extern __shared__ __align__(16) uint16_t smem[];
-  // Q, then two (K, V) buffers: the next key block is copied while this one is used
-  uint16_t *Qs = smem;
+  // tile 0: Q; warp group w: tiles 1 + 4w .. 4 + 4w, (K, V) twice: its next key block is
+  // copied while it uses one. Group w takes key blocks w, w + 2, ...; the two online-softmax
+  // states are merged at the end.
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int start = __ldg(a.cu + b), len = __ldg(a.cu + b + 1) - start;
   const int q0 = qb * kBlock;
@@ -114,33 +122,44 @@ __global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const __grid_cons
   const int nkb = min(qb, (len - 1) / kBlock) + 1;  // causal: key blocks up to this one
   const uint16_t *kg = a.k + (int64_t)start * ldk + hk * kD;
   const uint16_t *vg = a.v + (int64_t)start * ldk + hk * kD;
-  load_tile_async(Qs, a.q + (int64_t)(start + q0) * ldq + h * kD, ldq, min(kBlock, len - q0));
-  load_tile_async(smem + kTileHalves, kg, ldk, min(kBlock, len));
-  load_tile_async(smem + 2 * kTileHalves, vg, ldk, min(kBlock, len));
-  cp_async_commit();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int wg = warp >> 2, w4 = warp & 3, wtid = threadIdx.x & (kWarps * 32 - 1);
+  uint16_t *wbuf = smem + (1 + 4 * wg) * kTileHalves;
+  load_tile_async(smem, a.q + (int64_t)(start + q0) * ldq + h * kD, ldq, min(kBlock, len - q0),
+                  threadIdx.x, kCtaThreads);
+  if (wg < nkb) {
+    const int k0 = wg * kBlock;
+    load_tile_async(wbuf, kg + (int64_t)k0 * ldk, ldk, min(kBlock, len - k0), wtid, kWarps * 32);
+    load_tile_async(wbuf + kTileHalves, vg + (int64_t)k0 * ldk, ldk, min(kBlock, len - k0), wtid,
+                    kWarps * 32);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
   uint32_t qa[8][4];
+  load_a_frags(qa, smem, 16 * w4);
 
   float o[16][4];
 #pragma unroll
   for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
-  const int row0 = q0 + 16 * warp + g, row1 = row0 + 8;  // query positions in the sequence
-  for (int kb = 0; kb < nkb; ++kb) {
+  const int row0 = q0 + 16 * w4 + g, row1 = row0 + 8;  // query positions in the sequence
+  int it = 0;
+  for (int kb = wg; kb < nkb; kb += 2, ++it) {
     const int k0 = kb * kBlock;
-    if (kb + 1 < nkb) {  // the next block into the other buffer (read two iterations ago)
-      const int k1 = k0 + kBlock;
-      uint16_t *nb = smem + (1 + 2 * ((kb + 1) & 1)) * kTileHalves;
-      load_tile_async(nb, kg + (int64_t)k1 * ldk, ldk, min(kBlock, len - k1));
-      load_tile_async(nb + kTileHalves, vg + (int64_t)k1 * ldk, ldk, min(kBlock, len - k1));
+    if (kb + 2 < nkb) {  // this group's next block into its other buffer
+      const int k1 = k0 + 2 * kBlock;
+      uint16_t *nb = wbuf + 2 * ((it + 1) & 1) * kTileHalves;
+      load_tile_async(nb, kg + (int64_t)k1 * ldk, ldk, min(kBlock, len - k1), wtid, kWarps * 32);
+      load_tile_async(nb + kTileHalves, vg + (int64_t)k1 * ldk, ldk, min(kBlock, len - k1), wtid,
+                      kWarps * 32);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
-    __syncthreads();  // this block's tiles (and Q) are in shared memory for every warp
-    if (kb == 0) load_a_frags(qa, Qs, 16 * warp);
-    const uint16_t *Ks = smem + (1 + 2 * (kb & 1)) * kTileHalves;
+    wg_sync(wg);  // this block's tiles are in shared memory for the group's warps
+    const uint16_t *Ks = wbuf + 2 * (it & 1) * kTileHalves;
     const uint16_t *Vs = Ks + kTileHalves;
 
     // S = Q K^T for this warp's 16 rows x 64 keys
@@ -216,7 +235,40 @@ __global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const __grid_cons
         mma16816(o[2 * dp + 1], pa[kc2], bb[2], bb[3]);
       }
     }
-    __syncthreads();  // every warp is done with this buffer before it is refilled
+    wg_sync(wg);  // the group's warps are done with this buffer before it is refilled
+  }
+  // group 1's state (m, l and O of the same rows) through its now free buffers into group 0
+  __syncthreads();
+  float *mg = reinterpret_cast<float *>(smem + 5 * kTileHalves);
+  const int slot = w4 * 32 + lane;
+  if (wg == 1) {
+    mg[slot] = m0;
+    mg[128 + slot] = m1;
+    mg[256 + slot] = l0;
+    mg[384 + slot] = l1;
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) mg[512 + (nt * 4 + e) * 128 + slot] = o[nt][e];
+  }
+  __syncthreads();
+  if (wg == 1) return;
+  {
+    const float pm0 = mg[slot], pm1 = mg[128 + slot];
+    const float n0 = fmaxf(m0, pm0), n1 = fmaxf(m1, pm1);
+    const float a0 = attn_ex2(m0 - n0), b0 = attn_ex2(pm0 - n0);  // 0 for a -inf state
+    const float a1 = attn_ex2(m1 - n1), b1 = attn_ex2(pm1 - n1);
+    l0 = l0 * a0 + mg[256 + slot] * b0;
+    l1 = l1 * a1 + mg[384 + slot] * b1;
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      o[nt][0] = o[nt][0] * a0 + mg[512 + (nt * 4 + 0) * 128 + slot] * b0;
+      o[nt][1] = o[nt][1] * a0 + mg[512 + (nt * 4 + 1) * 128 + slot] * b0;
+      o[nt][2] = o[nt][2] * a1 + mg[512 + (nt * 4 + 2) * 128 + slot] * b1;
+      o[nt][3] = o[nt][3] * a1 + mg[512 + (nt * 4 + 3) * 128 + slot] * b1;
+    }
+    m0 = n0;
+    m1 = n1;
   }
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
@@ -261,12 +313,14 @@ struct BwdArgs {
   float scale, scale_log2;
 };
 
-__global__ void __launch_bounds__(kWarps * 32) attn_bwd_dq_kernel(const __grid_constant__ BwdArgs a) {
+__global__ void __launch_bounds__(kCtaThreads) attn_bwd_dq_kernel(const __grid_constant__ BwdArgs a) {
   pdl_wait();
   pdl_release();
   extern __shared__ __align__(16) uint16_t smem[];
   __shared__ float d_sh[kBlock];
-  uint16_t *Qs = smem, *dOs = smem + kTileHalves;  // then two (K, V) buffers
+  // tiles 0, 1: Q, dO; warp group w: tiles 2 + 4w .. 5 + 4w, (K, V) twice. Group w takes key
+  // blocks w, w + 2, ...; the two dQ partials are added at the end (group 0's first).
+  uint16_t *Qs = smem, *dOs = smem + kTileHalves;
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int start = __ldg(a.cu + b), len = __ldg(a.cu + b + 1) - start;
   const int q0 = qb * kBlock;
@@ -277,19 +331,28 @@ __global__ void __launch_bounds__(kWarps * 32) attn_bwd_dq_kernel(const __grid_c
   const int nkb = min(qb, (len - 1) / kBlock) + 1;
   const uint16_t *kg = a.k + (int64_t)start * ldk + hk * kD;
   const uint16_t *vg = a.v + (int64_t)start * ldk + hk * kD;
-  load_tile_async(Qs, a.q + (int64_t)(start + q0) * ldq + h * kD, ldq, nq);
-  load_tile_async(dOs, a.dout + (int64_t)(start + q0) * ldq + h * kD, ldq, nq);
-  load_tile_async(smem + 2 * kTileHalves, kg, ldk, min(kBlock, len));
-  load_tile_async(smem + 3 * kTileHalves, vg, ldk, min(kBlock, len));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int wg = warp >> 2, w4 = warp & 3, wtid = threadIdx.x & (kWarps * 32 - 1);
+  uint16_t *wbuf = smem + (2 + 4 * wg) * kTileHalves;
+  load_tile_async(Qs, a.q + (int64_t)(start + q0) * ldq + h * kD, ldq, nq, threadIdx.x,
+                  kCtaThreads);
+  load_tile_async(dOs, a.dout + (int64_t)(start + q0) * ldq + h * kD, ldq, nq, threadIdx.x,
+                  kCtaThreads);
+  if (wg < nkb) {
+    const int k0 = wg * kBlock;
+    load_tile_async(wbuf, kg + (int64_t)k0 * ldk, ldk, min(kBlock, len - k0), wtid, kWarps * 32);
+    load_tile_async(wbuf + kTileHalves, vg + (int64_t)k0 * ldk, ldk, min(kBlock, len - k0), wtid,
+                    kWarps * 32);
+  }
   cp_async_commit();
-  // D = rowsum(dO o O) of this block's queries: two threads per row, 64 dims each
+  // D = rowsum(dO o O) of this block's queries: four threads per row, 32 dims each
   {
-    const int r = threadIdx.x >> 1, half = threadIdx.x & 1;
+    const int r = threadIdx.x >> 2, part = threadIdx.x & 3;
     float d = 0.f;
     if (r < nq) {
-      const int64_t off = (int64_t)(start + q0 + r) * ldq + h * kD + half * 64;
+      const int64_t off = (int64_t)(start + q0 + r) * ldq + h * kD + part * 32;
 #pragma unroll
-      for (int c = 0; c < 64; c += 8) {
+      for (int c = 0; c < 32; c += 8) {
         float x[8], y[8];
         load8h(a.dout + off + c, x);
         load8h(a.out + off + c, y);
@@ -298,34 +361,38 @@ __global__ void __launch_bounds__(kWarps * 32) attn_bwd_dq_kernel(const __grid_c
       }
     }
     d += __shfl_xor_sync(0xffffffffu, d, 1);
-    if (half == 0) {
+    d += __shfl_xor_sync(0xffffffffu, d, 2);
+    if (part == 0) {
       d_sh[r] = d;
       if (r < nq) a.delta[(int64_t)h * a.total + start + q0 + r] = d;
     }
   }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int row0 = q0 + 16 * warp + g, row1 = row0 + 8;
+  cp_async_wait<0>();
+  __syncthreads();
+  const int row0 = q0 + 16 * w4 + g, row1 = row0 + 8;
   const float lse0 = row0 < len ? __ldg(a.lse + (int64_t)h * a.total + start + row0) : 0.f;
   const float lse1 = row1 < len ? __ldg(a.lse + (int64_t)h * a.total + start + row1) : 0.f;
+  const float d0 = d_sh[16 * w4 + g], d1 = d_sh[16 * w4 + g + 8];
   float dq[16][4];
 #pragma unroll
   for (int i = 0; i < 16; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.f;
-  const int ar = 16 * warp + (lane & 7) + ((lane >> 3) & 1) * 8, ac = (lane >> 4) * 8;
-  for (int kb = 0; kb < nkb; ++kb) {
+  const int ar = 16 * w4 + (lane & 7) + ((lane >> 3) & 1) * 8, ac = (lane >> 4) * 8;
+  int it = 0;
+  for (int kb = wg; kb < nkb; kb += 2, ++it) {
     const int k0 = kb * kBlock;
-    if (kb + 1 < nkb) {
-      const int k1 = k0 + kBlock;
-      uint16_t *nb = smem + (2 + 2 * ((kb + 1) & 1)) * kTileHalves;
-      load_tile_async(nb, kg + (int64_t)k1 * ldk, ldk, min(kBlock, len - k1));
-      load_tile_async(nb + kTileHalves, vg + (int64_t)k1 * ldk, ldk, min(kBlock, len - k1));
+    if (kb + 2 < nkb) {
+      const int k1 = k0 + 2 * kBlock;
+      uint16_t *nb = wbuf + 2 * ((it + 1) & 1) * kTileHalves;
+      load_tile_async(nb, kg + (int64_t)k1 * ldk, ldk, min(kBlock, len - k1), wtid, kWarps * 32);
+      load_tile_async(nb + kTileHalves, vg + (int64_t)k1 * ldk, ldk, min(kBlock, len - k1), wtid,
+                      kWarps * 32);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
-    __syncthreads();
-    const float d0 = d_sh[16 * warp + g], d1 = d_sh[16 * warp + g + 8];
-    const uint16_t *Ks = smem + (2 + 2 * (kb & 1)) * kTileHalves;
+    wg_sync(wg);
+    const uint16_t *Ks = wbuf + 2 * (it & 1) * kTileHalves;
     const uint16_t *Vs = Ks + kTileHalves;
     float s[8][4], dp[8][4];
 #pragma unroll
@@ -381,8 +448,24 @@ __global__ void __launch_bounds__(kWarps * 32) attn_bwd_dq_kernel(const __grid_c
         mma16816(dq[2 * dpi + 1], dsa[kc2], bb[2], bb[3]);
       }
     }
-    __syncthreads();
+    wg_sync(wg);
   }
+  // group 1's dQ partial through its now free buffers, added to group 0's
+  __syncthreads();
+  float *mg = reinterpret_cast<float *>(smem + 6 * kTileHalves);
+  const int slot = w4 * 32 + lane;
+  if (wg == 1) {
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) mg[(nt * 4 + e) * 128 + slot] = dq[nt][e];
+  }
+  __syncthreads();
+  if (wg == 1) return;
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) dq[nt][e] += mg[(nt * 4 + e) * 128 + slot];
   if (row0 < len) {
     uint32_t *op = reinterpret_cast<uint32_t *>(a.dq + (int64_t)(start + row0) * ldq + h * kD);
 #pragma unroll
@@ -397,12 +480,15 @@ __global__ void __launch_bounds__(kWarps * 32) attn_bwd_dq_kernel(const __grid_c
   }
 }
 
-__global__ void __launch_bounds__(kWarps * 32) attn_bwd_dkv_kernel(const __grid_constant__ BwdArgs a) {
+__global__ void __launch_bounds__(kCtaThreads) attn_bwd_dkv_kernel(const __grid_constant__ BwdArgs a) {
   pdl_wait();
   pdl_release();
   extern __shared__ __align__(16) uint16_t smem[];
-  __shared__ float lse_sh[2][kBlock], d_sh[2][kBlock];
-  uint16_t *Ks = smem, *Vs = smem + kTileHalves;  // then two (Q, dO) buffers
+  __shared__ float lse_sh[2][2][kBlock], d_sh[2][2][kBlock];  // [group][buffer][query]
+  // tiles 0, 1: K, V; warp group w: tiles 2 + 4w .. 5 + 4w, (Q, dO) twice. Group w takes query
+  // blocks kb + w, kb + w + 2, ...; the two dK / dV partials are added at the end (group 0's
+  // first).
+  uint16_t *Ks = smem, *Vs = smem + kTileHalves;
   const int kb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int start = __ldg(a.cu + b), len = __ldg(a.cu + b + 1) - start;
   const int k0 = kb * kBlock;
@@ -412,48 +498,60 @@ __global__ void __launch_bounds__(kWarps * 32) attn_bwd_dkv_kernel(const __grid_
   const int nqb = (len - 1) / kBlock + 1;  // query blocks kb .. nqb - 1 see these keys
   const uint16_t *qg = a.q + (int64_t)start * ldq + h * kD;
   const uint16_t *dog = a.dout + (int64_t)start * ldq + h * kD;
-  load_tile_async(Ks, a.k + (int64_t)(start + k0) * ldk + hk * kD, ldk, min(kBlock, len - k0));
-  load_tile_async(Vs, a.v + (int64_t)(start + k0) * ldk + hk * kD, ldk, min(kBlock, len - k0));
-  load_tile_async(smem + 2 * kTileHalves, qg + (int64_t)k0 * ldq, ldq, min(kBlock, len - k0));
-  load_tile_async(smem + 3 * kTileHalves, dog + (int64_t)k0 * ldq, ldq, min(kBlock, len - k0));
-  cp_async_commit();
-  if (threadIdx.x < kBlock) {
-    const int qi = k0 + threadIdx.x;
-    lse_sh[0][threadIdx.x] = qi < len ? __ldg(a.lse + (int64_t)h * a.total + start + qi) : 0.f;
-    d_sh[0][threadIdx.x] = qi < len ? __ldg(a.delta + (int64_t)h * a.total + start + qi) : 0.f;
-  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int key0 = k0 + 16 * warp + g, key1 = key0 + 8;
+  const int wg = warp >> 2, w4 = warp & 3, wtid = threadIdx.x & (kWarps * 32 - 1);
+  uint16_t *wbuf = smem + (2 + 4 * wg) * kTileHalves;
+  load_tile_async(Ks, a.k + (int64_t)(start + k0) * ldk + hk * kD, ldk, min(kBlock, len - k0),
+                  threadIdx.x, kCtaThreads);
+  load_tile_async(Vs, a.v + (int64_t)(start + k0) * ldk + hk * kD, ldk, min(kBlock, len - k0),
+                  threadIdx.x, kCtaThreads);
+  if (kb + wg < nqb) {
+    const int q0 = (kb + wg) * kBlock;
+    load_tile_async(wbuf, qg + (int64_t)q0 * ldq, ldq, min(kBlock, len - q0), wtid, kWarps * 32);
+    load_tile_async(wbuf + kTileHalves, dog + (int64_t)q0 * ldq, ldq, min(kBlock, len - q0), wtid,
+                    kWarps * 32);
+    if (wtid < kBlock) {
+      const int qi = q0 + wtid;
+      lse_sh[wg][0][wtid] = qi < len ? __ldg(a.lse + (int64_t)h * a.total + start + qi) : 0.f;
+      d_sh[wg][0][wtid] = qi < len ? __ldg(a.delta + (int64_t)h * a.total + start + qi) : 0.f;
+    }
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+  const int key0 = k0 + 16 * w4 + g, key1 = key0 + 8;
   float dk[16][4], dv[16][4];
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     dk[i][0] = dk[i][1] = dk[i][2] = dk[i][3] = 0.f;
     dv[i][0] = dv[i][1] = dv[i][2] = dv[i][3] = 0.f;
   }
-  const int ar = 16 * warp + (lane & 7) + ((lane >> 3) & 1) * 8, ac = (lane >> 4) * 8;
-  for (int qb = kb, it = 0; qb < nqb; ++qb, ++it) {
+  const int ar = 16 * w4 + (lane & 7) + ((lane >> 3) & 1) * 8, ac = (lane >> 4) * 8;
+  int it = 0;
+  for (int qb = kb + wg; qb < nqb; qb += 2, ++it) {
     const int q0 = qb * kBlock;
-    if (qb + 1 < nqb) {
-      const int q1 = q0 + kBlock;
-      uint16_t *nb = smem + (2 + 2 * ((it + 1) & 1)) * kTileHalves;
-      load_tile_async(nb, qg + (int64_t)q1 * ldq, ldq, min(kBlock, len - q1));
-      load_tile_async(nb + kTileHalves, dog + (int64_t)q1 * ldq, ldq, min(kBlock, len - q1));
+    if (qb + 2 < nqb) {  // this group's next query block into its other buffer
+      const int q1 = q0 + 2 * kBlock;
+      uint16_t *nb = wbuf + 2 * ((it + 1) & 1) * kTileHalves;
+      load_tile_async(nb, qg + (int64_t)q1 * ldq, ldq, min(kBlock, len - q1), wtid, kWarps * 32);
+      load_tile_async(nb + kTileHalves, dog + (int64_t)q1 * ldq, ldq, min(kBlock, len - q1), wtid,
+                      kWarps * 32);
       cp_async_commit();
-      if (threadIdx.x < kBlock) {
-        const int qi = q1 + threadIdx.x;
-        lse_sh[(it + 1) & 1][threadIdx.x] =
+      if (wtid < kBlock) {
+        const int qi = q1 + wtid;
+        lse_sh[wg][(it + 1) & 1][wtid] =
             qi < len ? __ldg(a.lse + (int64_t)h * a.total + start + qi) : 0.f;
-        d_sh[(it + 1) & 1][threadIdx.x] =
+        d_sh[wg][(it + 1) & 1][wtid] =
             qi < len ? __ldg(a.delta + (int64_t)h * a.total + start + qi) : 0.f;
       }
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
-    __syncthreads();
-    const uint16_t *Qs = smem + (2 + 2 * (it & 1)) * kTileHalves;
+    wg_sync(wg);
+    const uint16_t *Qs = wbuf + 2 * (it & 1) * kTileHalves;
     const uint16_t *dOs = Qs + kTileHalves;
-    const float *lse = lse_sh[it & 1], *dd = d_sh[it & 1];
+    const float *lse = lse_sh[wg][it & 1], *dd = d_sh[wg][it & 1];
     // S^T = K Q^T and dP^T = V dO^T: 16 keys x 64 queries per warp
     float st[8][4], dpt[8][4];
 #pragma unroll
@@ -513,8 +611,30 @@ __global__ void __launch_bounds__(kWarps * 32) attn_bwd_dkv_kernel(const __grid_
         mma16816(dk[2 * dpi + 1], dsa[kc2], bq[2], bq[3]);
       }
     }
-    __syncthreads();
+    wg_sync(wg);
   }
+  // group 1's dK / dV partials through its now free buffers, added to group 0's
+  __syncthreads();
+  float *mg = reinterpret_cast<float *>(smem + 6 * kTileHalves);
+  const int slot = w4 * 32 + lane;
+  if (wg == 1) {
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        mg[(nt * 4 + e) * 128 + slot] = dk[nt][e];
+        mg[8192 + (nt * 4 + e) * 128 + slot] = dv[nt][e];
+      }
+  }
+  __syncthreads();
+  if (wg == 1) return;
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      dk[nt][e] += mg[(nt * 4 + e) * 128 + slot];
+      dv[nt][e] += mg[8192 + (nt * 4 + e) * 128 + slot];
+    }
   // fp32 partials of this query head: rows key0 / key1, 8 columns per n-tile pair
 #pragma unroll
   for (int hf = 0; hf < 2; ++hf) {
@@ -531,7 +651,11 @@ __global__ void __launch_bounds__(kWarps * 32) attn_bwd_dkv_kernel(const __grid_
   }
 }
 
-// dK, dV fp16 [total, n_kv, 128] = sums of the fp32 partials of each group's query heads
+// dK, dV fp16 [total, n_kv, 128] = sums of the fp32 partials of each group's query heads, in
+// head order. A thread takes 4 columns of one (token, key/value head) and issues every group
+// member's loads before adding (groups of up to kMaxGroup heads; larger groups loop).
+constexpr int kMaxGroup = 8;
+
 __global__ void __launch_bounds__(256) attn_bwd_gsum_kernel(const float *__restrict__ dk_part,
                                                             const float *__restrict__ dv_part,
                                                             uint16_t *__restrict__ dk,
@@ -540,29 +664,34 @@ __global__ void __launch_bounds__(256) attn_bwd_gsum_kernel(const float *__restr
   pdl_wait();
   pdl_release();
   const int group = n_heads / n_kv;
-  const int64_t nvec = total * n_kv * (kD / 8);  // 8 outputs per thread
+  const int64_t nvec = total * n_kv * (kD / 4);
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t tok = i / (n_kv * (kD / 8));
-    const int rem = (int)(i - tok * (n_kv * (kD / 8)));
-    const int hk = rem / (kD / 8), c = (rem % (kD / 8)) * 8;
+    const int64_t tok = i / (n_kv * (kD / 4));
+    const int rem = (int)(i - tok * (n_kv * (kD / 4)));
+    const int hk = rem / (kD / 4), c = (rem % (kD / 4)) * 4;
     const int64_t src = tok * (int64_t)n_heads * kD + (int64_t)hk * group * kD + c;
-    float sk[8], sv[8];
+    float4 sk = make_float4(0.f, 0.f, 0.f, 0.f), sv = sk;
+    for (int j0 = 0; j0 < group; j0 += kMaxGroup) {
+      float4 xk[kMaxGroup], xv[kMaxGroup];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) sk[e] = sv[e] = 0.f;
-    for (int j = 0; j < group; ++j) {
-      float x[8], y[8];
-      load8f(dk_part + src + (int64_t)j * kD, x);
-      load8f(dv_part + src + (int64_t)j * kD, y);
+      for (int j = 0; j < kMaxGroup; ++j) {
+        if (j0 + j < group) {
+          xk[j] = __ldg(reinterpret_cast<const float4 *>(dk_part + src + (int64_t)(j0 + j) * kD));
+          xv[j] = __ldg(reinterpret_cast<const float4 *>(dv_part + src + (int64_t)(j0 + j) * kD));
+        }
+      }
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        sk[e] += x[e];
-        sv[e] += y[e];
+      for (int j = 0; j < kMaxGroup; ++j) {
+        if (j0 + j < group) {
+          sk.x += xk[j].x; sk.y += xk[j].y; sk.z += xk[j].z; sk.w += xk[j].w;
+          sv.x += xv[j].x; sv.y += xv[j].y; sv.z += xv[j].z; sv.w += xv[j].w;
+        }
       }
     }
     const int64_t dst = tok * (int64_t)n_kv * kD + (int64_t)hk * kD + c;
-    store8h(dk + dst, sk);
-    store8h(dv + dst, sv);
+    *reinterpret_cast<uint2 *>(dk + dst) = make_uint2(pack_half2(sk.x, sk.y), pack_half2(sk.z, sk.w));
+    *reinterpret_cast<uint2 *>(dv + dst) = make_uint2(pack_half2(sv.x, sv.y), pack_half2(sv.z, sv.w));
   }
 }
 
@@ -597,7 +726,7 @@ extern "C" int tb_attn_varlen_fwd(const uint16_t *q, const uint16_t *k, const ui
   if (!out || !lse) return set_error(TB_EINVAL, "attn_varlen_fwd: out and lse required");
   if (!aligned(out, 16)) return set_error(TB_EALIGN, "attn_varlen_fwd: out must be 16-byte aligned");
   if (batch == 0 || total == 0 || max_len == 0) return TB_OK;
-  const size_t smem = 5 * kTileHalves * sizeof(uint16_t);
+  const size_t smem = 9 * kTileHalves * sizeof(uint16_t);
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -607,7 +736,7 @@ extern "C" int tb_attn_varlen_fwd(const uint16_t *q, const uint16_t *k, const ui
   }
   FwdArgs a{q, k, v, cu_seqlens, out, lse, total, n_heads, n_kv, scale * 1.4426950408889634f};
   const dim3 grid((unsigned)((max_len + kBlock - 1) / kBlock), (unsigned)n_heads, (unsigned)batch);
-  return launch("attn_varlen_fwd", attn_fwd_kernel, grid, kWarps * 32, smem, as_stream(stream), a);
+  return launch("attn_varlen_fwd", attn_fwd_kernel, grid, kCtaThreads, smem, as_stream(stream), a);
 }
 
 extern "C" int tb_attn_varlen_bwd(const uint16_t *q, const uint16_t *k, const uint16_t *v,
@@ -625,7 +754,7 @@ extern "C" int tb_attn_varlen_bwd(const uint16_t *q, const uint16_t *k, const ui
       !aligned(dv, 16) || !aligned(dk_part, 16) || !aligned(dv_part, 16))
     return set_error(TB_EALIGN, "attn_varlen_bwd: 16-byte aligned buffers are required");
   if (batch == 0 || total == 0 || max_len == 0) return TB_OK;
-  const size_t smem = 6 * kTileHalves * sizeof(uint16_t);
+  const size_t smem = 10 * kTileHalves * sizeof(uint16_t);
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -640,11 +769,11 @@ extern "C" int tb_attn_varlen_bwd(const uint16_t *q, const uint16_t *k, const ui
             scale, scale * 1.4426950408889634f};
   const dim3 grid((unsigned)((max_len + kBlock - 1) / kBlock), (unsigned)n_heads, (unsigned)batch);
   cudaStream_t st = as_stream(stream);
-  rc = launch("attn_varlen_bwd dq", attn_bwd_dq_kernel, grid, kWarps * 32, smem, st, a);
+  rc = launch("attn_varlen_bwd dq", attn_bwd_dq_kernel, grid, kCtaThreads, smem, st, a);
   if (rc != TB_OK) return rc;
-  rc = launch("attn_varlen_bwd dkv", attn_bwd_dkv_kernel, grid, kWarps * 32, smem, st, a);
+  rc = launch("attn_varlen_bwd dkv", attn_bwd_dkv_kernel, grid, kCtaThreads, smem, st, a);
   if (rc != TB_OK) return rc;
-  const int64_t nvec = total * n_kv * (kD / 8);
+  const int64_t nvec = total * n_kv * (kD / 4);
   int64_t blocks = (nvec + 255) / 256;
   if (blocks > (int64_t)sm_count() * 8) blocks = (int64_t)sm_count() * 8;
   return launch("attn_varlen_bwd gsum", attn_bwd_gsum_kernel, (unsigned)blocks, 256, 0, st,
