@@ -264,3 +264,25 @@ def head_merge(parts, idxs, targets):
     loss = torch.where(labelled, lse - zt, torch.zeros_like(lse))
     correct = labelled & (arg == tgt)
     return lse, entropy, loss, correct
+
+
+def attention_varlen(q, k, v, cu_seqlens, scale):
+    """Causal attention over packed sequences with grouped key/value heads, fp64: the decoder
+    layer's SDPA with the causal + padding mask (solution/model.py:242-247) restricted to the
+    real query rows. q [T, H, D], k, v [T, Hkv, D] token-major, sequence b = tokens
+    cu[b] .. cu[b+1]-1. Returns (out [T, H, D], base-2 log-sum-exp [H, T] of scale q k^T)."""
+    import math
+
+    nh, nkv = q.shape[1], k.shape[1]
+    outs, lses = [], []
+    for b in range(cu_seqlens.numel() - 1):
+        s, e = int(cu_seqlens[b]), int(cu_seqlens[b + 1])
+        qq = q[s:e].double().transpose(0, 1)
+        kk = k[s:e].double().transpose(0, 1).repeat_interleave(nh // nkv, 0)
+        vv = v[s:e].double().transpose(0, 1).repeat_interleave(nh // nkv, 0)
+        sc = qq @ kk.transpose(1, 2) * scale
+        keep = torch.ones(e - s, e - s, dtype=torch.bool, device=q.device).tril()
+        sc = sc.masked_fill(~keep, float("-inf"))
+        lses.append(torch.logsumexp(sc, -1) / math.log(2.0))
+        outs.append((torch.softmax(sc, -1) @ vv).transpose(0, 1))
+    return torch.cat(outs, 0), torch.cat(lses, 1)

@@ -57,3 +57,18 @@ def test_version_and_error_text_work_without_gpu():
     rc = lib.tb_swiglu_fwd(None, None, -1, 8, None)
     assert rc == -1
     assert b"swiglu_fwd" in lib.tb_last_error()
+
+
+def test_attention_rejects_unsupported_shapes_without_gpu():
+    """Argument checks run before any CUDA call: head_dim other than 128, heads not a multiple of
+    the key/value heads."""
+    import ctypes
+
+    from testt_b200 import _lib
+
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    rc = lib.tb_attn_varlen_fwd(p, p, p, p, p, p, 1, 4, 4, 12, 2, 64, 0.125, None)
+    assert rc == -1 and b"head_dim" in lib.tb_last_error()
+    rc = lib.tb_attn_varlen_fwd(p, p, p, p, p, p, 1, 4, 4, 12, 5, 128, 0.125, None)
+    assert rc == -1 and b"heads" in lib.tb_last_error()

@@ -1,7 +1,8 @@
-"""Causal variable-length GQA attention (tb_attn_varlen_fwd / _bwd) against an fp64 PyTorch
-restatement of the reference's attention restricted to the real rows (solution/model.py:242-247:
-softmax(q k^T * scale + causal/padding mask) v per sequence, key/value heads shared by groups of
-query heads). Outputs within fp16 rounding of the fp16 operands' exact result."""
+"""Causal variable-length GQA attention (tb_attn_varlen_fwd / _bwd) against the fp64 oracle
+(oracle.ops.attention_varlen: the reference's attention restricted to the real rows,
+solution/model.py:242-247: softmax(q k^T * scale + causal/padding mask) v per sequence, key/value
+heads shared by groups of query heads). Outputs within fp16 rounding of the fp16 operands'
+exact result."""
 
 import math
 
@@ -24,20 +25,10 @@ def _case(lengths, nh, nkv, seed, d=128):
 
 
 def _reference(q, k, v, cu, scale):
-    """fp64 attention per sequence: (out [T, H, D], lse2 [H, T])."""
-    nh, nkv = q.shape[1], k.shape[1]
-    outs, lses = [], []
-    for b in range(cu.numel() - 1):
-        s, e = int(cu[b]), int(cu[b + 1])
-        qq = q[s:e].double().transpose(0, 1)                                   # [H, L, D]
-        kk = k[s:e].double().transpose(0, 1).repeat_interleave(nh // nkv, 0)   # [H, L, D]
-        vv = v[s:e].double().transpose(0, 1).repeat_interleave(nh // nkv, 0)
-        sc = qq @ kk.transpose(1, 2) * scale
-        mask = torch.ones(e - s, e - s, dtype=torch.bool, device=q.device).tril()
-        sc = sc.masked_fill(~mask, float("-inf"))
-        lses.append(torch.logsumexp(sc, -1) / math.log(2.0))                   # [H, L]
-        outs.append((torch.softmax(sc, -1) @ vv).transpose(0, 1))               # [L, H, D]
-    return torch.cat(outs, 0), torch.cat(lses, 1)
+    """fp64 attention per sequence (oracle.ops.attention_varlen): (out [T, H, D], lse2 [H, T])."""
+    from oracle import ops
+
+    return ops.attention_varlen(q, k, v, cu, scale)
 
 
 @pytest.mark.parametrize("lengths", [[149, 131, 193, 148], [1, 64, 65, 7, 200], [512]])

@@ -174,3 +174,43 @@ def test_oracle_fold_then_merge_equals_merge():
     fp, fi = ops.head_fold(part, idx, 1000, 1)
     shifted = ops.head_merge(fp[None], fi[None], torch.where(t >= 0, t + 1000, t))
     assert torch.equal(shifted[3], whole[3])
+
+
+def test_oracle_attention_equals_padded_sdpa_real_rows():
+    """The varlen attention oracle against what the reference runs: PyTorch SDPA over the padded
+    [batch, heads, seq, dim] layout with the causal + padding mask (solution/model.py:242-247,
+    transformers' sdpa path with repeat_kv for the grouped heads), on the real query rows."""
+    import math
+
+    import torch
+
+    from oracle import ops
+
+    g = torch.Generator().manual_seed(4)
+    lengths, nh, nkv, d, seq = [5, 9, 1, 7], 4, 2, 16, 9
+    total = sum(lengths)
+    q = torch.randn(total, nh, d, generator=g)
+    k = torch.randn(total, nkv, d, generator=g)
+    v = torch.randn(total, nkv, d, generator=g)
+    cu = torch.zeros(len(lengths) + 1, dtype=torch.int32)
+    cu[1:] = torch.tensor(lengths).cumsum(0)
+    scale = 1.0 / math.sqrt(d)
+    out, lse = ops.attention_varlen(q, k, v, cu, scale)
+
+    def pad(x):
+        p = torch.zeros(len(lengths), seq, x.shape[1], d, dtype=torch.float64)
+        for b, n in enumerate(lengths):
+            p[b, :n] = x[int(cu[b]):int(cu[b]) + n].double()
+        return p.transpose(1, 2)  # [B, H, T, D]
+
+    qp, kp, vp = pad(q), pad(k).repeat_interleave(nh // nkv, 1), pad(v).repeat_interleave(nh // nkv, 1)
+    real = torch.zeros(len(lengths), seq, dtype=torch.bool)
+    for b, n in enumerate(lengths):
+        real[b, :n] = True
+    mask = torch.ones(seq, seq, dtype=torch.bool).tril()[None, None] & real[:, None, None, :]
+    ref = torch.nn.functional.scaled_dot_product_attention(qp, kp, vp, attn_mask=mask, scale=scale)
+    ref = ref.transpose(1, 2)  # [B, T, H, D]
+    for b, n in enumerate(lengths):
+        torch.testing.assert_close(out[int(cu[b]):int(cu[b]) + n], ref[b, :n], rtol=1e-10,
+                                   atol=1e-12)
+    assert torch.isfinite(lse).all() and lse.shape == (nh, total)
