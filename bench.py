@@ -598,6 +598,31 @@ def _kernel_case(name, device):
             + (2 * r * hidden + (hidden + 256) * r) * (4 + 2) + m * 8
         info = {"config": "3", "tokens": m, "hidden": hidden, "rank": r,
                 "outputs": [hidden, 256]}
+    elif name in ("attn_fwd", "attn_fwd_bwd"):  # a layer's attention at config 5's lengths
+        import math
+
+        from testt_b200.attention import varlen_attention
+
+        lengths = synth.lengths(seed=0)
+        total = sum(lengths)
+        g = torch.Generator(device=dev).manual_seed(6)
+        q, k, v = (torch.randn((total, hh, 128), generator=g, device=dev).half()
+                   .requires_grad_(name == "attn_fwd_bwd") for hh in (12, 2, 2))
+        cu = torch.zeros(len(lengths) + 1, dtype=torch.int32, device=dev)
+        cu[1:] = torch.tensor(lengths, device=dev).cumsum(0)
+        dout = torch.randn((total, 12, 128), generator=g, device=dev).half()
+        scale, top = 1.0 / math.sqrt(128), max(lengths)
+        if name == "attn_fwd":
+            fn = lambda: varlen_attention(q, k, v, cu, top, scale)  # noqa: E731
+        else:
+            fn = lambda: torch.autograd.grad(  # noqa: E731
+                varlen_attention(q, k, v, cu, top, scale), (q, k, v), dout)
+        # causal score and value products: 2 * (L (L + 1) / 2) * heads * 128 * 2 per sequence;
+        # the backward recomputes the scores and forms dV, dP, dQ, dK (2.5 x the forward)
+        fwd = sum(2 * n * (n + 1) // 2 * 12 * 128 * 2 for n in lengths)
+        nbytes = 0
+        info = {"config": "5 (one layer)", "lengths": lengths, "heads": [12, 2], "head_dim": 128,
+                "flops": fwd if name == "attn_fwd" else int(3.5 * fwd)}
     elif name == "head_tc":
         c = synth.config4(dev)
         rows, hidden, vocab = 2048, synth.HIDDEN, synth.VOCAB
@@ -937,7 +962,7 @@ def main():
     ap.add_argument("--kernel", default=None,
                     help="time one kernel at its configuration instead (nf4, nf4_nested, "
                          "rmsnorm_fwd, rmsnorm_bwd, rope_fwd, rope_bwd, swiglu_fwd, swiglu_bwd, "
-                         "lora_fwd, "
+                         "lora_fwd, attn_fwd, attn_fwd_bwd, "
                          "head_stats, head_tc, head_full, head_cublas, all)")
     args = ap.parse_args()
     if args.kernel:
