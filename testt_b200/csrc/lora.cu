@@ -143,7 +143,7 @@ __global__ void lora_dropout_grad_any(const uint16_t *dxq, const uint16_t *dxv, 
 // fp16(A) in shared memory; each warp takes rows, lane l its 8 columns of the slice, the
 // sixteen products of a column summed in rank order in fp32.
 constexpr int kExpandCols = 256;
-constexpr int kExpandRowsPerWarp = 4;
+constexpr int kExpandRowsPerWarp = 2;
 
 __global__ void __launch_bounds__(kThreads)
     lora_dropout_grad_expand(const uint16_t *__restrict__ dhq, const uint16_t *__restrict__ aq,
@@ -170,25 +170,45 @@ __global__ void __launch_bounds__(kThreads)
   const int c = c0 + lane * 8;
   const bool live = lane * 8 < ncols;
   const int64_t p0 = ((int64_t)blockIdx.y * (blockDim.x >> 5) + warp) * kExpandRowsPerWarp;
+  // every row's slot lookup, dh rows and mask bytes are loaded before the math
+  int64_t tok[kExpandRowsPerWarp];
+#pragma unroll
+  for (int i = 0; i < kExpandRowsPerWarp; ++i)
+    tok[i] = p0 + i < slots ? __ldg(slot_tok + p0 + i) : -1;
+  uint4 hv4[kExpandRowsPerWarp][2][2];  // [row][adapter][half of the 16 dh values]
+  uint2 mk[kExpandRowsPerWarp][2];
+#pragma unroll
+  for (int i = 0; i < kExpandRowsPerWarp; ++i)
+#pragma unroll
+    for (int ad = 0; ad < 2; ++ad) {
+      const uint16_t *dh = ad == 0 ? dhq : dhv;
+      const uint8_t *m = ad == 0 ? mq : mv;
+      hv4[i][ad][0] = hv4[i][ad][1] = make_uint4(0u, 0u, 0u, 0u);
+      mk[i][ad] = make_uint2(0x01010101u, 0x01010101u);
+      if (tok[i] >= 0 && live && dh != nullptr) {
+        hv4[i][ad][0] = __ldg(reinterpret_cast<const uint4 *>(dh + tok[i] * 16));
+        hv4[i][ad][1] = __ldg(reinterpret_cast<const uint4 *>(dh + tok[i] * 16 + 8));
+        if (m != nullptr)
+          mk[i][ad] = __ldg(reinterpret_cast<const uint2 *>(m + (p0 + i) * hidden + c));
+      }
+    }
+#pragma unroll
   for (int i = 0; i < kExpandRowsPerWarp; ++i) {
     const int64_t p = p0 + i;
-    if (p >= slots) break;
-    const int64_t tok = __ldg(slot_tok + p);
+    if (p >= slots || !live) continue;
     float out[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) out[k] = 0.f;
-    if (tok >= 0 && live) {
+    if (tok[i] >= 0) {
 #pragma unroll
       for (int ad = 0; ad < 2; ++ad) {
         const uint16_t *dh = ad == 0 ? dhq : dhv;
         if (dh == nullptr) continue;
         const uint8_t *m = ad == 0 ? mq : mv;
         const float scale = ad == 0 ? sq : sv;
-        // the token's 16 dh values (the same for the whole warp: one broadcast load)
-        const uint4 h0 = __ldg(reinterpret_cast<const uint4 *>(dh + tok * 16));
-        const uint4 h1 = __ldg(reinterpret_cast<const uint4 *>(dh + tok * 16 + 8));
         float hf[16];
-        const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+        const uint32_t hw[8] = {hv4[i][ad][0].x, hv4[i][ad][0].y, hv4[i][ad][0].z, hv4[i][ad][0].w,
+                                hv4[i][ad][1].x, hv4[i][ad][1].y, hv4[i][ad][1].z, hv4[i][ad][1].w};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float2 f = unpack_half2(hw[j]);
@@ -209,9 +229,7 @@ __global__ void __launch_bounds__(kThreads)
             acc[2 * j + 1] = fmaf(hf[r], f.y, acc[2 * j + 1]);
           }
         }
-        uint2 mk = make_uint2(0x01010101u, 0x01010101u);
-        if (m != nullptr) mk = __ldg(reinterpret_cast<const uint2 *>(m + p * hidden + c));
-        const uint8_t *mb = reinterpret_cast<const uint8_t *>(&mk);
+        const uint8_t *mb = reinterpret_cast<const uint8_t *>(&mk[i][ad]);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const float dx = __half2float(__float2half_rn(acc[k]));  // the fp16 GEMM output
@@ -220,7 +238,7 @@ __global__ void __launch_bounds__(kThreads)
         }
       }
     }
-    if (live) store8f(g + p * hidden + c, out);
+    store8f(g + p * hidden + c, out);
   }
 }
 
