@@ -727,13 +727,10 @@ extern "C" int tb_attn_varlen_fwd(const uint16_t *q, const uint16_t *k, const ui
   if (!aligned(out, 16)) return set_error(TB_EALIGN, "attn_varlen_fwd: out must be 16-byte aligned");
   if (batch == 0 || total == 0 || max_len == 0) return TB_OK;
   const size_t smem = 9 * kTileHalves * sizeof(uint16_t);
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
-      return check_launch("attn_varlen_fwd attribute");
-    attr = true;
-  }
+  // set on every call: the attribute belongs to the current device
+  if (cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return check_launch("attn_varlen_fwd attribute");
   FwdArgs a{q, k, v, cu_seqlens, out, lse, total, n_heads, n_kv, scale * 1.4426950408889634f};
   const dim3 grid((unsigned)((max_len + kBlock - 1) / kBlock), (unsigned)n_heads, (unsigned)batch);
   return launch("attn_varlen_fwd", attn_fwd_kernel, grid, kCtaThreads, smem, as_stream(stream), a);
@@ -755,15 +752,11 @@ extern "C" int tb_attn_varlen_bwd(const uint16_t *q, const uint16_t *k, const ui
     return set_error(TB_EALIGN, "attn_varlen_bwd: 16-byte aligned buffers are required");
   if (batch == 0 || total == 0 || max_len == 0) return TB_OK;
   const size_t smem = 10 * kTileHalves * sizeof(uint16_t);
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_bwd_dkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
-      return check_launch("attn_varlen_bwd attribute");
-    attr = true;
-  }
+  if (cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess ||
+      cudaFuncSetAttribute(attn_bwd_dkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return check_launch("attn_varlen_bwd attribute");
   BwdArgs a{q,     k,      v,       out,     dout,    lse,     cu_seqlens,
             delta, dq,     dk_part, dv_part, total,   n_heads, n_kv,
             scale, scale * 1.4426950408889634f};
