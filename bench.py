@@ -94,10 +94,14 @@ class Clocks:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=self.file, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+        else:
+            # nvidia-smi takes a few hundred ms to start sampling: the timed region (often under
+            # a second) begins once it runs
+            time.sleep(0.5)
         return self
 
     def __exit__(self, *exc):
