@@ -78,9 +78,11 @@ def max_over_ranks(x, world, device):
 
 
 class Clocks:
-    """nvidia-smi sampling of SM clock and throttle reasons while a region runs."""
+    """nvidia-smi sampling of SM clock and throttle reasons while a region runs. The sampler
+    starts before the region (nvidia-smi takes a few hundred ms to start); the summary keeps the
+    samples whose timestamps fall inside the region (all of them if none does)."""
 
-    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
+    FIELDS = "timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
 
@@ -88,6 +90,7 @@ class Clocks:
         self.gpu = gpu_index
         self.proc = None
         self.file = None
+        self.start = self.stop = None
 
     def __enter__(self):
         self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
@@ -99,16 +102,45 @@ class Clocks:
         except OSError:
             self.proc = None
         else:
-            # nvidia-smi takes a few hundred ms to start sampling: the timed region (often under
-            # a second) begins once it runs
             time.sleep(0.5)
+        self.start = datetime.datetime.now()
         return self
 
     def __exit__(self, *exc):
+        self.stop = datetime.datetime.now()
         if self.proc is not None:
+            time.sleep(0.06)  # one more sample interval: the region's last sample is written
             self.proc.terminate()
             self.proc.wait(timeout=10)
         return False
+
+    @staticmethod
+    def parse(rows, start=None, stop=None):
+        """(SM MHz samples, max MHz, active throttle reasons) of nvidia-smi CSV rows, only the
+        rows stamped within [start, stop] when any is."""
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        parsed = []
+        for r in rows:
+            r = [c.strip() for c in r]
+            if len(r) < 10:
+                continue
+            try:
+                ts = datetime.datetime.strptime(r[0], "%Y/%m/%d %H:%M:%S.%f")
+            except ValueError:
+                ts = None
+            try:
+                sm, mx = float(r[2]), float(r[3])
+            except ValueError:
+                continue
+            active = [n for n, v in zip(names, r[6:10]) if v.lower().startswith("active")]
+            parsed.append((ts, sm, mx, active))
+        inside = [p for p in parsed
+                  if p[0] is not None and start is not None and start <= p[0] <= stop]
+        use = inside or parsed
+        sm = sorted(p[1] for p in use)
+        mx = use[-1][2] if use else None
+        reasons = sorted({a for p in use for a in p[3]})
+        return sm, mx, reasons, len(inside)
 
     def summary(self):
         if self.proc is None:
@@ -116,23 +148,9 @@ class Clocks:
         self.file.seek(0)
         rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
         os.unlink(self.file.name)
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        sm, mx, reasons = [], None, set()
-        for r in rows:
-            r = [c.strip() for c in r]
-            if len(r) < 9:
-                continue
-            try:
-                sm.append(float(r[1]))
-                mx = float(r[2])
-            except ValueError:
-                continue
-            for name, val in zip(names, r[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        sm.sort()
+        sm, mx, reasons, n_inside = self.parse(rows, self.start, self.stop)
         return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": reasons, "samples": len(sm), "samples_in_region": n_inside}
 
 
 # ---- the QLoRA step (value, e2e) -------------------------------------------------------------
