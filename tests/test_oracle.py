@@ -214,3 +214,50 @@ def test_oracle_attention_equals_padded_sdpa_real_rows():
         torch.testing.assert_close(out[int(cu[b]):int(cu[b]) + n], ref[b, :n], rtol=1e-10,
                                    atol=1e-12)
     assert torch.isfinite(lse).all() and lse.shape == (nh, total)
+
+
+def test_sequence_offsets_and_varlen_attention_for_any_padding_pattern():
+    """Right padding, left padding, holes and an empty row: sequence_offsets packs each row's
+    real tokens in column order (pos_idx order), and causal attention over the packed sequences
+    (the oracle) equals the reference's padded SDPA with the causal + padding mask on the real
+    query rows, so the variable-length path holds for any padding pattern."""
+    import math
+
+    import torch
+
+    from oracle import ops
+    from testt_b200.model import sequence_offsets
+
+    seq, nh, nkv, d = 8, 4, 2, 16
+    mask = torch.tensor([[1, 1, 1, 1, 1, 0, 0, 0],     # right padding
+                         [0, 0, 0, 1, 1, 1, 1, 1],     # left padding
+                         [1, 0, 1, 1, 0, 1, 0, 1],     # holes
+                         [0, 0, 0, 0, 0, 0, 0, 0]])    # no real token
+    cu, max_len = sequence_offsets(mask)
+    assert cu.dtype == torch.int32 and cu.tolist() == [0, 5, 10, 15, 15] and max_len == 5
+    pos = mask.reshape(-1).nonzero().squeeze(1)
+    g = torch.Generator().manual_seed(8)
+    qp = torch.randn(mask.shape[0], seq, nh, d, generator=g, dtype=torch.float64)
+    kp = torch.randn(mask.shape[0], seq, nkv, d, generator=g, dtype=torch.float64)
+    vp = torch.randn(mask.shape[0], seq, nkv, d, generator=g, dtype=torch.float64)
+    pack = lambda x: x.reshape(-1, *x.shape[2:]).index_select(0, pos)  # noqa: E731
+    scale = 1.0 / math.sqrt(d)
+    out, _ = ops.attention_varlen(pack(qp), pack(kp), pack(vp), cu, scale)
+    keep = torch.ones(seq, seq, dtype=torch.bool).tril()[None, None] & \
+        mask.bool()[:, None, None, :]
+    ref = torch.nn.functional.scaled_dot_product_attention(
+        qp.transpose(1, 2), kp.transpose(1, 2).repeat_interleave(nh // nkv, 1),
+        vp.transpose(1, 2).repeat_interleave(nh // nkv, 1), attn_mask=keep, scale=scale)
+    ref = ref.transpose(1, 2).reshape(-1, nh, d).index_select(0, pos)
+    torch.testing.assert_close(out, ref, rtol=1e-10, atol=1e-12)
+
+
+@pytest.mark.parametrize("blocksize", [64, 128, 256])
+@pytest.mark.parametrize("nested", [False, True])
+def test_nf4_c_oracle_equals_numpy_oracle(blocksize, nested):
+    """The C restatement (the timed CPU baseline's unpack) and the numpy one agree bit for bit
+    on other blocksizes and on a weight whose size is not a multiple of the nested block."""
+    rng = np.random.default_rng(blocksize + nested)
+    w = (rng.standard_normal((40, 3 * blocksize)) * 0.05).astype(np.float16)
+    q = onf4.quantize(w, blocksize=blocksize, nested=nested)
+    assert_bitexact(cnf4.unpack(q), onf4.dequantize(q), f"C vs numpy, blocksize {blocksize}")
