@@ -84,5 +84,16 @@ def build(verbose=False, force=False):
     return LIB_PATH
 
 
+def compile_staged(out_dir):
+    """Compile every `csrc/next/*.cu` (kernels not linked into the library until their parity
+    tests have run on a B200) to objects in `out_dir` with the library's flags; returns
+    {file name: ptxas log}."""
+    logs = {}
+    for src in sorted(glob.glob(os.path.join(CSRC, "next", "*.cu"))):
+        obj = os.path.join(out_dir, os.path.basename(src)[:-3] + ".o")
+        logs[os.path.basename(src)] = _compile(src, obj, verbose=True)
+    return logs
+
+
 if __name__ == "__main__":
     print(build(verbose="-v" in sys.argv, force="-f" in sys.argv))
