@@ -286,3 +286,22 @@ def attention_varlen(q, k, v, cu_seqlens, scale):
         lses.append(torch.logsumexp(sc, -1) / math.log(2.0))
         outs.append((torch.softmax(sc, -1) @ vv).transpose(0, 1))
     return torch.cat(outs, 0), torch.cat(lses, 1)
+
+
+def nf4_matmul(x16, quantized, bias16=None, transpose=False):
+    """FrozenNF4Linear (solution/nf4.py:115-127) on the CPU: the NF4 weights (oracle.nf4
+    quantize dicts, stacked by rows into W [N, K]) dequantised bit-exactly, then
+    fp16(x W^T + bias) (forward) or fp16(x W) (transpose: dX from dY), the products summed in
+    fp64 and rounded once to fp16, as a GEMM with an fp32 accumulator and a bias epilogue would
+    up to the order of its sums."""
+    import numpy as np
+
+    from . import nf4 as onf4
+
+    w = np.concatenate([onf4.dequantize(q).reshape(q["shape"]) for q in quantized], axis=0)
+    wt = torch.from_numpy(w.astype(np.float64))
+    x = x16.detach().cpu().double()
+    y = x @ wt if transpose else x @ wt.t()
+    if bias16 is not None:
+        y = y + bias16.detach().cpu().double()
+    return y.to(torch.float16)

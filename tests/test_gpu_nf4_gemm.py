@@ -1,0 +1,106 @@
+"""The NF4 GEMM with the decode in the tensor-core kernel (tb_nf4_gemm) against the oracle
+(bit-exact dequantisation, fp64 sums) and against cuBLAS over the unpacked weight, in both
+directions. The kernel is staged (not linked into the library yet): these tests skip while the
+loaded library does not export it."""
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_rel, nf4_weight
+from oracle import nf4 as onf4
+from oracle import ops
+
+pytestmark = pytest.mark.gpu
+
+# fp16 output of an fp32-accumulated sum: half an fp16 ulp of rounding plus the sum's order
+RTOL = 1e-3
+
+
+def _available():
+    if not torch.cuda.is_available():
+        return False
+    from testt_b200 import nf4_gemm
+
+    return nf4_gemm.available()
+
+
+requires_kernel = pytest.mark.skipif(not _available(),
+                                     reason="tb_nf4_gemm is not in the loaded library (staged)")
+
+
+def _weights(rows, cols, nested, seed):
+    rng = np.random.default_rng(seed)
+    qs = [onf4.quantize((rng.standard_normal((r, cols)) * 0.05).astype(np.float16),
+                        blocksize=64, nested=nested) for r in rows]
+    return qs, [nf4_weight(q, "cuda") for q in qs]
+
+
+def _x(rows, cols, seed, std=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(rows, cols, generator=g) * std).half().cuda()
+
+
+@requires_kernel
+@pytest.mark.parametrize("nested", [False, True])
+@pytest.mark.parametrize("tokens", [1, 37, 621, 1000])
+def test_forward_stacked_with_bias_matches_oracle(nested, tokens):
+    """q|k|v-shaped stack (the reduction split over several CTAs at these sizes), with bias."""
+    from testt_b200 import nf4_gemm
+
+    qs, ws = _weights((512, 128, 128), 1536, nested, seed=tokens)
+    x = _x(tokens, 1536, seed=1)
+    bias = _x(1, 768, seed=2, std=0.1)[0]
+    out = nf4_gemm.nf4_matmul(x, ws, bias)
+    torch.cuda.synchronize()
+    assert_rel(out.cpu(), ops.nf4_matmul(x.cpu(), qs, bias.cpu()), RTOL, "forward")
+    assert_rel(nf4_gemm.nf4_matmul(x, ws).cpu(), ops.nf4_matmul(x.cpu(), qs), RTOL, "no bias")
+
+
+@requires_kernel
+@pytest.mark.parametrize("nested", [False, True])
+@pytest.mark.parametrize("tokens", [1, 300, 621])
+def test_backward_stacked_matches_oracle(nested, tokens):
+    """dX = dY W over a stack of three weights (the reduction split over several CTAs, the
+    splits' ranges crossing from one weight to the next)."""
+    from testt_b200 import nf4_gemm
+
+    qs, ws = _weights((640, 384, 512), 256, nested, seed=10 + tokens)
+    dy = _x(tokens, 1536, seed=3, std=0.01)
+    out = nf4_gemm.nf4_matmul(dy, ws, transpose=True)
+    torch.cuda.synchronize()
+    assert_rel(out.cpu(), ops.nf4_matmul(dy.cpu(), qs, transpose=True), RTOL, "backward")
+
+
+@requires_kernel
+@pytest.mark.parametrize("which", ["gate_up", "down"])
+def test_config5_shapes_match_cublas_over_unpacked(which):
+    """The step's MLP GEMMs at 621 tokens, both directions, against torch.matmul (cuBLAS) over
+    tb_nf4_unpack's bit-exact fp16 weight."""
+    from testt_b200 import _lib, nf4_gemm
+    from testt_b200.nf4 import unpack_concat
+
+    rows, cols = ((8960, 8960), 1536) if which == "gate_up" else ((1536,), 8960)
+    _, ws = _weights(rows, cols, True, seed=7)
+    w16 = unpack_concat(ws, "cuda")
+    x = _x(621, cols, seed=4)
+    dy = _x(621, sum(rows), seed=5, std=0.01)
+    fwd = nf4_gemm.nf4_matmul(x, ws)
+    bwd = nf4_gemm.nf4_matmul(dy, ws, transpose=True)
+    ref_f = (x.float() @ w16.float().t()).half()
+    ref_b = (dy.float() @ w16.float()).half()
+    torch.cuda.synchronize()
+    assert_rel(fwd.cpu(), ref_f.cpu(), RTOL, f"{which} forward")
+    assert_rel(bwd.cpu(), ref_b.cpu(), RTOL, f"{which} backward")
+    assert_rel(fwd.cpu(), torch.matmul(x, w16.t()).cpu(), RTOL, f"{which} vs cuBLAS")
+    assert _lib.wait_timeouts() == 0
+
+
+@requires_kernel
+def test_rejects_shapes_it_does_not_take():
+    from testt_b200 import nf4_gemm
+
+    _, ws = _weights((64, 64), 256, False, seed=9)   # forward tiles of 128 rows would straddle
+    with pytest.raises(ValueError):
+        nf4_gemm.nf4_matmul(_x(4, 256, seed=6), ws)
+    assert nf4_gemm.nf4_matmul(_x(0, 128, seed=6), ws, transpose=True).shape == (0, 256)

@@ -261,3 +261,33 @@ def test_nf4_c_oracle_equals_numpy_oracle(blocksize, nested):
     w = (rng.standard_normal((40, 3 * blocksize)) * 0.05).astype(np.float16)
     q = onf4.quantize(w, blocksize=blocksize, nested=nested)
     assert_bitexact(cnf4.unpack(q), onf4.dequantize(q), f"C vs numpy, blocksize {blocksize}")
+
+
+@pytest.mark.parametrize("nested", [False, True])
+def test_nf4_gemm_host_absmax_and_oracle(nested):
+    """The staged NF4 GEMM's host side on the CPU: the fp32 absmax it expands from a nested
+    state equals the dequantiser's bit for bit, `supported` follows the kernel's shape rules,
+    and the GEMM oracle equals fp64 products of the dequantised weights in both directions."""
+    from helpers import nf4_weight
+    from testt_b200 import nf4_gemm
+
+    rng = np.random.default_rng(5 + nested)
+    qs = [onf4.quantize((rng.standard_normal((r, 192)) * 0.05).astype(np.float16),
+                        blocksize=64, nested=nested) for r in (128, 256)]
+    ws = [nf4_weight(q, "cpu") for q in qs]
+    for q, w in zip(qs, ws):
+        a = nf4_gemm.fp32_absmax(w).numpy()
+        assert a.dtype == np.float32
+        assert np.array_equal(a.view(np.uint32), onf4.block_absmax(q).view(np.uint32))
+    assert nf4_gemm.supported(ws) and not nf4_gemm.supported(ws, transpose=True)  # 192 % 128
+    # 64 rows: a forward tile of 128 rows would straddle two weights; the backward takes it
+    odd = nf4_weight(onf4.quantize(np.zeros((64, 256), np.float16), nested=nested), "cpu")
+    assert not nf4_gemm.supported([odd, odd]) and nf4_gemm.supported([odd, odd], transpose=True)
+    x = torch.from_numpy((rng.standard_normal((5, 192))).astype(np.float16))
+    bias = torch.from_numpy((rng.standard_normal(384) * 0.1).astype(np.float16))
+    w = torch.from_numpy(np.concatenate([onf4.dequantize(q).reshape(q["shape"]) for q in qs]))
+    y = ops.nf4_matmul(x, qs, bias)
+    assert y.dtype == torch.float16 and y.shape == (5, 384)
+    assert torch.equal(y, (x.double() @ w.double().t() + bias.double()).half())
+    dy = torch.from_numpy((rng.standard_normal((3, 384))).astype(np.float16))
+    assert torch.equal(ops.nf4_matmul(dy, qs, transpose=True), (dy.double() @ w.double()).half())

@@ -1,0 +1,127 @@
+"""Frozen NF4 linear layers with the NF4 decode inside the tensor-core GEMM: the fp16 weight is
+never written to memory (reference: solution/nf4.py:108-127, FrozenNF4Linear, which unpacks
+the weight and calls cuBLAS in both directions).
+
+    nf4_matmul(x, weights, bias)                  fp16 [T, N] = x [T, K] . W^T (+ bias)
+    nf4_matmul(dy, weights, transpose=True)       fp16 [T, K] = dy [T, N] . W
+
+W is the weights stacked by rows (q|k|v, gate|up), each with bitsandbytes' NF4 layout and
+blocksize 64. The kernel, tb_nf4_gemm, is staged: it is built from csrc/next/nf4_gemm.cu and is
+not linked into libtestt_b200.so until its parity tests have run on a B200. `available()` is
+therefore False with the shipped library, and no training path calls this module yet.
+"""
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .nf4 import _quant_state, supports_fast_unpack, weight_shape
+
+MAX_WEIGHTS = 4
+BLOCKSIZE = 64
+
+_SIG = [_lib._I32, _lib._P, _lib._I64, _lib._I64, _lib._I32, _lib._P, _lib._P, _lib._P, _lib._P,
+        _lib._I64, _lib._P, _lib._P, _lib._I64, _lib._P, _lib._I64, _lib._P]
+_WS_SIG = [_lib._I32, _lib._I64, _lib._I32, _lib._P, _lib._I64]
+
+
+def _entry():
+    """(tb_nf4_gemm, tb_nf4_gemm_workspace) of the loaded library, or None without them."""
+    lib = _lib.load()
+    fn = getattr(lib, "tb_nf4_gemm", None)
+    ws = getattr(lib, "tb_nf4_gemm_workspace", None)
+    if fn is None or ws is None:
+        return None
+    fn.restype, fn.argtypes = ctypes.c_int, _SIG
+    ws.restype, ws.argtypes = ctypes.c_int64, _WS_SIG
+    return fn, ws
+
+
+def available():
+    return _entry() is not None
+
+
+def supported(weights, transpose=False):
+    """True when tb_nf4_gemm takes these weights: 1-4 NF4 weights with blocksize 64, the same
+    column count, rows a multiple of 128 (forward) or 64 (backward), columns a multiple of 64
+    (forward) or 128 (backward)."""
+    if not 1 <= len(weights) <= MAX_WEIGHTS:
+        return False
+    if not all(supports_fast_unpack(w) and _quant_state(w).blocksize == BLOCKSIZE for w in weights):
+        return False
+    shapes = [weight_shape(w) for w in weights]
+    cols = shapes[0][1]
+    row_mult, col_mult = (64, 128) if transpose else (128, 64)
+    return all(s[1] == cols and s[0] % row_mult == 0 for s in shapes) and cols % col_mult == 0
+
+
+def fp32_absmax(weight):
+    """The weight's per-block absmax in fp32. A nested state's absmax is expanded once and kept
+    on the state: code2[c] * absmax2[b // blocksize2] + offset, the product and the sum each
+    rounded to fp32 (two kernels, no fused multiply-add), as the unpack kernel computes it."""
+    state = _quant_state(weight)
+    if not state.nested:
+        return state.absmax
+    cached = getattr(state, "_tb_absmax_f32", None)
+    if cached is not None and cached.device == state.absmax.device:
+        return cached
+    dev = state.absmax.device
+    code2 = state.state2.code.to(torch.float32)
+    absmax2 = state.state2.absmax.to(torch.float32)
+    blocks = torch.arange(state.absmax.numel(), device=dev) // int(state.state2.blocksize)
+    prod = code2[state.absmax.long()] * absmax2[blocks]
+    off = state.offset
+    off = off.to(device=dev, dtype=torch.float32) if torch.is_tensor(off) else float(off)
+    absmax = (prod + off).contiguous()
+    try:
+        state._tb_absmax_f32 = absmax
+    except AttributeError:
+        pass
+    return absmax
+
+
+def nf4_matmul(x, weights, bias=None, transpose=False):
+    """fp16 x [T, K] . W^T (+ bias) -> [T, N], or with transpose fp16 dy [T, N] . W -> [T, K],
+    W = the weights stacked by rows [N, K]."""
+    entry = _entry()
+    if entry is None:
+        raise RuntimeError("nf4_matmul: tb_nf4_gemm is not in the loaded library (staged kernel)")
+    fn, ws_fn = entry
+    _lib.require_cuda(x, bias, what="nf4_matmul")
+    weights = tuple(weights)
+    if not supported(weights, transpose):
+        raise ValueError("nf4_matmul: weights the kernel does not take")
+    if x.dtype != torch.float16 or x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("nf4_matmul: x must be fp16 [tokens, features] with unit column stride")
+    shapes = [weight_shape(w) for w in weights]
+    rows = [s[0] for s in shapes]
+    cols = shapes[0][1]
+    red = sum(rows) if transpose else cols
+    if x.shape[1] != red:
+        raise ValueError(f"nf4_matmul: x has {x.shape[1]} features, the weights take {red}")
+    tokens = x.shape[0]
+    out_cols = cols if transpose else sum(rows)
+    out = torch.empty((tokens, out_cols), dtype=torch.float16, device=x.device)
+    if tokens == 0:
+        return out
+    if x.stride(0) % 8 or x.data_ptr() % 16:
+        x = x.contiguous()
+    bias = None if bias is None else bias.to(torch.float16).contiguous()
+    absmax = [fp32_absmax(w) for w in weights]
+    tables = [_quant_state(w).code.to(torch.float32).contiguous() for w in weights]
+    n = len(weights)
+    rows_arr = (ctypes.c_int64 * n)(*rows)
+    ws_bytes = ws_fn(int(transpose), tokens, n, rows_arr, cols)
+    ws = torch.empty(max(ws_bytes, 0) // 4, dtype=torch.float32, device=x.device) \
+        if ws_bytes > 0 else None
+    rc = fn(int(transpose), _lib.ptr(x), tokens, x.stride(0), n,
+            _lib.ptr_array([_lib.ptr(w.data) for w in weights]),
+            _lib.ptr_array([_lib.ptr(a) for a in absmax]),
+            _lib.ptr_array([_lib.ptr(t) for t in tables]), rows_arr, cols, _lib.ptr(bias),
+            _lib.ptr(out), out.stride(0), _lib.ptr(ws), ws_bytes if ws is not None else 0,
+            _lib.stream_of(x))
+    if rc != 0:
+        msg = _lib.load().tb_last_error().decode(errors="replace")
+        raise _lib.KernelError(f"tb_nf4_gemm failed ({rc}): {msg}")
+    return out
