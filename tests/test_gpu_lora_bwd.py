@@ -1,0 +1,95 @@
+"""The rank-16 LoRA backward in two launches (tb_lora_backward: dh, dB, dA of both adapters)
+against fp32 products of the same fp16 operands, with and without in-place accumulation, one
+adapter absent, deterministic. The kernels are staged (not linked into the library yet): these
+tests skip while the loaded library does not export the entry point."""
+
+import ctypes
+
+import pytest
+import torch
+
+from helpers import assert_rel
+
+pytestmark = pytest.mark.gpu
+
+_P, _I64, _I32, _F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float
+_SIG = [_P, _P, _P, _P, _P, _P, _P, _I64, _F, _P, _P, _P, _P, _P, _P, _P, _I64, _F, _I64, _I64,
+        _I32, _I32, _P]
+
+
+def _entry():
+    if not torch.cuda.is_available():
+        return None
+    from testt_b200 import _lib
+
+    fn = getattr(_lib.load(), "tb_lora_backward", None)
+    if fn is not None:
+        fn.restype, fn.argtypes = ctypes.c_int, _SIG
+    return fn
+
+
+requires_kernel = pytest.mark.skipif(_entry() is None,
+                                     reason="tb_lora_backward is not in the loaded library (staged)")
+
+
+def _adapter(rows, width, hidden, scale, seed):
+    g = torch.Generator().manual_seed(seed)
+    r = lambda *s, std=1.0: (torch.randn(*s, generator=g) * std).half().cuda()  # noqa: E731
+    return dict(g=r(rows, width, std=1e-2), h=r(rows, 16), b16=r(width, 16, std=0.02),
+                x16=r(rows, hidden), scale=scale,
+                db=(torch.randn(width, 16, generator=g) * 1e-3).cuda(),
+                da=(torch.randn(16, hidden, generator=g) * 1e-3).cuda(),
+                dh=torch.empty(rows, 16, dtype=torch.float16, device="cuda"))
+
+
+def _reference(ad, acc_db, acc_da):
+    s = ad["scale"]
+    dh = (s * (ad["g"].float() @ ad["b16"].float())).half()
+    db = s * (ad["g"].float().t() @ ad["h"].float())
+    da = dh.float().t() @ ad["x16"].float()
+    return dh, db + ad["db"] if acc_db else db, da + ad["da"] if acc_da else da
+
+
+def _run(q, v, rows, hidden, accumulate):
+    from testt_b200 import _lib
+
+    def parts(ad):
+        if ad is None:
+            return [None] * 7 + [0, 0.0]
+        return [_lib.ptr(ad[k]) for k in ("g", "h", "b16", "x16", "dh", "db", "da")] + \
+            [ad["g"].shape[1], ad["scale"]]
+
+    rc = _entry()(*parts(q), *parts(v), rows, hidden, 16, accumulate, _lib.stream_of(
+        torch.empty(0, device="cuda")))
+    assert rc == 0, _lib.load().tb_last_error()
+    torch.cuda.synchronize()
+
+
+@requires_kernel
+@pytest.mark.parametrize("rows", [1, 37, 621])
+@pytest.mark.parametrize("accumulate", [0, 0b1111])
+def test_both_adapters_match_fp32_products(rows, accumulate):
+    q = _adapter(rows, 1536, 1536, 2.0, seed=rows)
+    v = _adapter(rows, 256, 1536, 2.0, seed=rows + 1)
+    refs = [_reference(ad, accumulate & 1, accumulate & 2) for ad in (q, v)]
+    _run(q, v, rows, 1536, accumulate)
+    for ad, (dh, db, da), name in zip((q, v), refs, "qv"):
+        assert_rel(ad["dh"].float().cpu(), dh.float().cpu(), 1e-3, f"dh {name}")
+        assert_rel(ad["db"].cpu(), db.cpu(), 1e-4, f"dB {name}")
+        assert_rel(ad["da"].cpu(), da.cpu(), 1e-4, f"dA {name}")
+
+
+@requires_kernel
+@pytest.mark.parametrize("present", ["q", "v"])
+def test_one_adapter_and_determinism(present):
+    ad = _adapter(300, 1536 if present == "q" else 256, 1536, 2.0, seed=3)
+    dh, db, da = _reference(ad, False, False)
+    args = (ad, None) if present == "q" else (None, ad)
+    _run(*args, 300, 1536, 0)
+    first = [ad[k].clone() for k in ("dh", "db", "da")]
+    _run(*args, 300, 1536, 0)
+    for a, b in zip(first, [ad[k] for k in ("dh", "db", "da")]):
+        assert torch.equal(a, b)
+    assert_rel(ad["dh"].float().cpu(), dh.float().cpu(), 1e-3, "dh")
+    assert_rel(ad["db"].cpu(), db.cpu(), 1e-4, "dB")
+    assert_rel(ad["da"].cpu(), da.cpu(), 1e-4, "dA")
