@@ -25,6 +25,7 @@ The reference arm (--impl reference) times that CPU step alone.
 """
 
 import argparse
+import ctypes
 import datetime
 import json
 import os
@@ -32,6 +33,7 @@ import subprocess
 import sys
 import tempfile
 import time
+from types import SimpleNamespace
 
 import torch
 import torch.distributed as dist
@@ -674,6 +676,72 @@ def _kernel_case(name, device):
         fn = lambda: torch.matmul(c["hidden"], c["weight"].t(), out=logits)  # noqa: E731
         nbytes = 0
         info = {"config": "4", "rows": rows, "flops": 2 * rows * hidden * vocab}
+    elif name.startswith("gate_up_"):  # the step's largest NF4 linear at 621 tokens, both ways
+        from testt_b200 import nf4_gemm
+
+        tokens, hidden, inter = 621, synth.HIDDEN, synth.INTER
+        g = torch.Generator(device=dev).manual_seed(8)
+        weights = []
+        for _ in range(2):
+            w = torch.randn((inter, hidden), generator=g, device=dev) * 0.02
+            packed, state = quantize_nf4(w, 64, nested=True)
+            weights.append(SimpleNamespace(data=packed, quant_state=state))
+        x = torch.randn((tokens, hidden), generator=g, device=dev).half()
+        dy = (torch.randn((tokens, 2 * inter), generator=g, device=dev) * 0.01).half()
+        if name in ("gate_up_fused_fwd", "gate_up_fused_bwd"):
+            if not nf4_gemm.available():
+                raise SystemExit(f"{name}: tb_nf4_gemm is not in the library (staged kernel)")
+            if name.endswith("fwd"):
+                fn = lambda: nf4_gemm.nf4_matmul(x, weights)  # noqa: E731
+            else:
+                fn = lambda: nf4_gemm.nf4_matmul(dy, weights, transpose=True)  # noqa: E731
+        elif name == "gate_up_unpack_fwd":  # the step's way: unpack, then cuBLAS
+            fn = lambda: torch.matmul(x, nf4.unpack_concat(weights, dev).t())  # noqa: E731
+        elif name == "gate_up_unpack_bwd":
+            fn = lambda: torch.matmul(dy, nf4.unpack_concat(weights, dev))  # noqa: E731
+        else:
+            raise SystemExit(f"unknown kernel {name}")
+        nbytes = 0
+        info = {"config": "5 (one layer's gate|up)", "tokens": tokens,
+                "shape": [2 * inter, hidden], "flops": 2 * tokens * 2 * inter * hidden}
+    elif name in ("lora_bwd", "lora_bwd_cublas"):  # both adapters' weight and dh gradients
+        tokens, hidden, r = 621, synth.HIDDEN, 16
+        g = torch.Generator(device=dev).manual_seed(9)
+        ads = []
+        for width in (hidden, 256):
+            ads.append(dict(
+                g=(torch.randn((tokens, width), generator=g, device=dev) * 0.01).half(),
+                h=torch.randn((tokens, r), generator=g, device=dev).half(),
+                b16=(torch.randn((width, r), generator=g, device=dev) * 0.02).half(),
+                x16=torch.randn((tokens, hidden), generator=g, device=dev).half(),
+                dh=torch.empty((tokens, r), dtype=torch.float16, device=dev),
+                db=torch.zeros((width, r), device=dev), da=torch.zeros((r, hidden), device=dev)))
+        if name == "lora_bwd":
+            lib = _lib.load()
+            entry = getattr(lib, "tb_lora_backward", None)
+            if entry is None:
+                raise SystemExit("lora_bwd: tb_lora_backward is not in the library (staged)")
+            P, I64, I32, F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float
+            entry.restype = ctypes.c_int
+            entry.argtypes = [P] * 7 + [I64, F] + [P] * 7 + [I64, F, I64, I64, I32, I32, P]
+
+            def parts(ad):
+                return [_lib.ptr(ad[k]) for k in ("g", "h", "b16", "x16", "dh", "db", "da")] \
+                    + [ad["g"].shape[1], 2.0]
+
+            fn = lambda: entry(*parts(ads[0]), *parts(ads[1]), tokens, hidden, r,  # noqa: E731
+                               0b1111, _lib.stream_of(ads[0]["dh"]))
+        else:  # the current backward's six GEMMs (lora.LoraPair.backward, bucket accumulation)
+            def fn():
+                for ad in ads:
+                    torch.addmm(ad["db"], ad["g"].t(), ad["h"], beta=1.0, alpha=2.0,
+                                out_dtype=torch.float32, out=ad["db"])
+                    torch.addmm(ad["dh"], ad["g"], ad["b16"], beta=0.0, alpha=2.0, out=ad["dh"])
+                    torch.addmm(ad["da"], ad["dh"].t(), ad["x16"], beta=1.0, alpha=1.0,
+                                out_dtype=torch.float32, out=ad["da"])
+        nbytes = 0
+        info = {"config": "5 (one layer's q and v adapters)", "tokens": tokens, "rank": r,
+                "flops": sum(2 * tokens * r * (2 * ad["g"].shape[1] + hidden) for ad in ads)}
     elif name == "head_stats":
         c = synth.config4(dev, rows=256)
         logits = c["hidden"] @ c["weight"].t()
@@ -985,7 +1053,9 @@ def main():
                     help="time one kernel at its configuration instead (nf4, nf4_nested, "
                          "rmsnorm_fwd, rmsnorm_bwd, rope_fwd, rope_bwd, swiglu_fwd, swiglu_bwd, "
                          "lora_fwd, attn_fwd, attn_fwd_bwd, "
-                         "head_stats, head_tc, head_full, head_cublas, all)")
+                         "head_stats, head_tc, head_full, head_cublas, all; staged kernels, "
+                         "with what they replace: gate_up_fused_fwd, gate_up_fused_bwd, "
+                         "gate_up_unpack_fwd, gate_up_unpack_bwd, lora_bwd, lora_bwd_cublas)")
     args = ap.parse_args()
     if args.kernel:
         names = ["nf4", "nf4_nested", "rmsnorm_fwd", "rmsnorm_bwd", "rope_fwd", "rope_bwd",
