@@ -41,10 +41,20 @@ def _x(rows, cols, seed, std=1.0):
     return (torch.randn(rows, cols, generator=g) * std).half().cuda()
 
 
+@pytest.fixture(params=[1, 2], ids=["workspace", "cluster"])
+def split_variant(request):
+    """Both ways of summing a split reduction; the automatic choice restored afterwards."""
+    from testt_b200 import nf4_gemm
+
+    nf4_gemm.set_variant(request.param)
+    yield request.param
+    nf4_gemm.set_variant(0)
+
+
 @requires_kernel
 @pytest.mark.parametrize("nested", [False, True])
 @pytest.mark.parametrize("tokens", [1, 37, 621, 1000])
-def test_forward_stacked_with_bias_matches_oracle(nested, tokens):
+def test_forward_stacked_with_bias_matches_oracle(nested, tokens, split_variant):
     """q|k|v-shaped stack (the reduction split over several CTAs at these sizes), with bias."""
     from testt_b200 import nf4_gemm
 
@@ -60,7 +70,7 @@ def test_forward_stacked_with_bias_matches_oracle(nested, tokens):
 @requires_kernel
 @pytest.mark.parametrize("nested", [False, True])
 @pytest.mark.parametrize("tokens", [1, 300, 621])
-def test_backward_stacked_matches_oracle(nested, tokens):
+def test_backward_stacked_matches_oracle(nested, tokens, split_variant):
     """dX = dY W over a stack of three weights (the reduction split over several CTAs, the
     splits' ranges crossing from one weight to the next)."""
     from testt_b200 import nf4_gemm

@@ -27,13 +27,19 @@
 //   warps 2..5  decoders: NF4 words and absmax read from global memory two stages ahead,
 //               decoded to fp16 and stored into the stage's A tile in the swizzled layout the
 //               MMA descriptor reads (fence.proxy.async, then an arrive on the stage's A
-//               barrier); afterwards the epilogue: TMEM -> fp16 output (one split) or fp32
-//               partials [split, token, row], which nf4_gemm_reduce sums in split order with
-//               the bias.
+//               barrier); afterwards the epilogue: TMEM -> fp16 output (one split).
+// A split reduction (small projections: the grid is filled by splitting the reduction) sums
+// its splits' accumulators either within a thread-block cluster of the splits (the default):
+// each CTA parks its fp32 accumulator in its now idle stage buffers, and CTA r of the cluster
+// adds column slice r of all of them through distributed shared memory in split order, with
+// the bias; or through fp32 partials [split, token, row] in a caller's workspace, summed in
+// split order by nf4_gemm_reduce (tb_nf4_gemm_variant(1)).
 // Every mbarrier wait is bounded (mbar_wait); a role that gives up sets the CTA's error flag
 // and leaves its loop, every role meets at the final barrier and TMEM is always released.
 // No multicast is used.
 #include <cuda.h>
+
+#include <cstddef>
 
 #include "../common.cuh"
 
@@ -60,6 +66,10 @@ struct Smem {
   uint32_t tmem_base;
   volatile int error;
 };
+// the cluster reduction keeps a CTA's fp32 accumulator [span][128] in the stage buffers a, b
+static_assert(offsetof(Smem, b) == sizeof(Smem::a), "stage buffers a and b are contiguous");
+static_assert(sizeof(Smem::a) + sizeof(Smem::b) >= (size_t)kMaxSpan * kBM * 4,
+              "the stage buffers hold a whole accumulator");
 
 struct GemmArgs {
   const uint8_t *packed[kMaxW];
@@ -76,7 +86,9 @@ struct GemmArgs {
   const uint16_t *bias;      // forward with one split only (else nf4_gemm_reduce adds it)
   uint16_t *out;
   int64_t ld_out;
-  float *part;               // [splits, tokens, a_rows] fp32 when splits > 1
+  float *part;               // [splits, tokens, a_rows] fp32 when splits > 1 (not cluster)
+  int cluster;               // splits > 1: the splits are one thread-block cluster and sum
+                             // their accumulators through distributed shared memory
 };
 
 // ---- tcgen05 / TMA helpers (PTX ISA: tcgen05.mma, cp.async.bulk.tensor) --------------------
@@ -171,6 +183,28 @@ __device__ __forceinline__ uint4 decode_word(uint32_t word, float scale, uint32_
   }
   return make_uint4(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]), pack_half2(f[4], f[5]),
                     pack_half2(f[6], f[7]));
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// every thread of every CTA of the cluster; orders shared-memory writes before the barrier
+// with the reads (local or remote) after it
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+
+// the float at the address `p` has in this CTA, in the shared memory of cluster CTA `rank`
+__device__ __forceinline__ float ld_cluster(const float *p, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(p)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -418,7 +452,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t v[32];
           tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(j * args.bn + c), v);
           const int ne = args.tokens - tb < 32 ? args.tokens - tb : 32;
-          if (args.splits == 1) {
+          if (args.cluster) {
+            // the stage buffers are free once every MMA has completed: the accumulator goes
+            // to red[column][row] (a warp's lanes are consecutive rows: conflict-free)
+            float *red = reinterpret_cast<float *>(&sm.a[0][0]);
+            const int col0 = j * args.bn + c;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) red[(col0 + e) * kBM + quarter * 32 + lane] = __uint_as_float(v[e]);
+          } else if (args.splits == 1) {
             uint16_t *o = args.out + (int64_t)tb * args.ld_out + row;
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
@@ -438,6 +479,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+  }
+
+  if (args.cluster) {
+    // the splits' sums: cluster CTA r finishes columns [r * per, (r + 1) * per) of the tile,
+    // adding the CTAs' accumulators in rank (= split) order, then the bias; the second barrier
+    // keeps every CTA's shared memory alive until all have read it
+    cluster_sync();
+    const int per = (args.span + args.splits - 1) / args.splits;
+    const int c_lo = (int)cluster_ctarank() * per;
+    const int c_hi = c_lo + per < args.span ? c_lo + per : args.span;
+    const float *red = reinterpret_cast<const float *>(&sm.a[0][0]);
+    for (int e = threadIdx.x; e < (c_hi - c_lo) * kBM; e += kThreads) {
+      const int col = c_lo + e / kBM, r = e % kBM;
+      const int t = t0 + col;
+      if (t >= args.tokens) break;  // columns ascend with e
+      float sum = 0.f;
+      for (int q = 0; q < args.splits; ++q)
+        sum = __fadd_rn(sum, ld_cluster(red + col * kBM + r, (uint32_t)q));
+      if (args.bias != nullptr)
+        sum = __fadd_rn(sum, __half2float(__ushort_as_half(__ldg(args.bias + a0 + r))));
+      args.out[(int64_t)t * args.ld_out + a0 + r] = __half_as_ushort(__float2half_rn(sum));
+    }
+    cluster_sync();
   }
 
   tc_fence_before();
@@ -521,8 +585,13 @@ int make_map(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, int
 }
 
 struct Plan {
-  int bn, nsub, span, groups, splits;
+  int bn, nsub, span, groups, splits, cluster;
 };
+
+// 0: automatic (split partials summed within a cluster), 1: split partials through the
+// workspace and nf4_gemm_reduce, 2: cluster always (process-wide; tb_nf4_gemm_variant)
+int g_variant = 0;
+constexpr int kMaxCluster = 8;  // portable cluster size
 
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
@@ -530,7 +599,7 @@ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // split until the grid reaches one CTA per SM (at least 4 blocks of 64 a split), within the
 // workspace.
 Plan make_plan(int64_t tokens, int a_tiles, int red_blocks, int64_t a_rows, int64_t ws_bytes,
-               int sms) {
+               int sms, int variant) {
   Plan p;
   p.groups = (int)ceil_div(tokens, kMaxSpan);
   const int64_t tg = ceil_div(tokens, p.groups);
@@ -550,8 +619,14 @@ Plan make_plan(int64_t tokens, int a_tiles, int red_blocks, int64_t a_rows, int6
     if (splits > most) splits = most;
     if (splits > 16) splits = 16;
   }
-  while (splits > 1 && (int64_t)splits * tokens * a_rows * 4 > ws_bytes) --splits;
+  const bool cluster = variant != 1;
+  if (cluster) {
+    if (splits > kMaxCluster) splits = kMaxCluster;
+  } else {
+    while (splits > 1 && (int64_t)splits * tokens * a_rows * 4 > ws_bytes) --splits;
+  }
   p.splits = splits;
+  p.cluster = cluster && splits > 1;
   return p;
 }
 
@@ -620,8 +695,9 @@ extern "C" int64_t tb_nf4_gemm_workspace(int32_t transpose, int64_t tokens, int3
   for (int j = 0; j < n_weights; ++j) total += rows[j];
   const int64_t a_rows = transpose ? k_dim : total;
   const int red_blocks = (int)((transpose ? total : k_dim) / kBK);
-  const Plan p = make_plan(tokens, (int)(a_rows / kBM), red_blocks, a_rows, INT64_MAX, sm_count());
-  return p.splits > 1 ? (int64_t)p.splits * tokens * a_rows * 4 : 0;
+  const Plan p = make_plan(tokens, (int)(a_rows / kBM), red_blocks, a_rows, INT64_MAX, sm_count(),
+                           g_variant);
+  return p.splits > 1 && !p.cluster ? (int64_t)p.splits * tokens * a_rows * 4 : 0;
 }
 
 extern "C" int tb_nf4_gemm(int32_t transpose, const uint16_t *tokens_in, int64_t tokens,
@@ -651,7 +727,7 @@ extern "C" int tb_nf4_gemm(int32_t transpose, const uint16_t *tokens_in, int64_t
 
   const int a_tiles = a.a_rows / kBM;
   const Plan p = make_plan(tokens, a_tiles, a.red_blocks, a.a_rows,
-                           workspace ? workspace_bytes : 0, sm_count());
+                           workspace ? workspace_bytes : 0, sm_count(), g_variant);
   a.bn = p.bn;
   a.nsub = p.nsub;
   a.span = p.span;
@@ -660,7 +736,8 @@ extern "C" int tb_nf4_gemm(int32_t transpose, const uint16_t *tokens_in, int64_t
   a.bias = bias;
   a.out = out;
   a.ld_out = ld_out;
-  a.part = p.splits > 1 ? workspace : nullptr;
+  a.part = p.splits > 1 && !p.cluster ? workspace : nullptr;
+  a.cluster = p.cluster;
 
   CUtensorMap map_b;
   rc = make_map(&map_b, tokens_in, tokens, red_dim, ld_in, p.bn);
@@ -670,10 +747,24 @@ extern "C" int tb_nf4_gemm(int32_t transpose, const uint16_t *tokens_in, int64_t
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return check_launch("nf4_gemm attribute");
-  const dim3 grid((unsigned)a_tiles, (unsigned)p.groups, (unsigned)p.splits);
-  kernel<<<grid, kThreads, smem, as_stream(stream)>>>(map_b, a);
-  rc = check_launch("nf4_gemm");
-  if (rc != TB_OK || p.splits == 1) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)a_tiles, (unsigned)p.groups, (unsigned)p.splits);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;  // the splits of one (tile, token group) form a cluster
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = (unsigned)p.splits;
+  cfg.attrs = attr;
+  cfg.numAttrs = p.cluster ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, map_b, a);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return set_error(TB_ELAUNCH, "nf4_gemm: launch failed: %s", cudaGetErrorString(e));
+  }
+  if (p.splits == 1 || p.cluster) return TB_OK;
   const int64_t vecs = tokens * (a.a_rows / 8);
   const int64_t blocks64 = (vecs + 255) / 256;
   const int cap = resident_blocks(nf4_gemm_reduce, 256);
@@ -681,4 +772,11 @@ extern "C" int tb_nf4_gemm(int32_t transpose, const uint16_t *tokens_in, int64_t
   return launch("nf4_gemm_reduce", nf4_gemm_reduce, dim3((unsigned)blocks), dim3(256), 0,
                 as_stream(stream), (const float *)workspace, p.splits, tokens, a.a_rows, bias, out,
                 ld_out);
+}
+
+extern "C" int tb_nf4_gemm_variant(int32_t variant) {
+  if (variant < 0 || variant > 2)
+    return set_error(TB_EINVAL, "nf4_gemm_variant: %d (0 auto, 1 workspace, 2 cluster)", variant);
+  g_variant = variant;
+  return TB_OK;
 }

@@ -42,6 +42,17 @@ def available():
     return _entry() is not None
 
 
+def set_variant(variant):
+    """How a split reduction is summed, process-wide: 0 automatic (within a thread-block cluster
+    of the splits), 1 fp32 partials in a workspace + a summing kernel, 2 cluster always."""
+    fn = getattr(_lib.load(), "tb_nf4_gemm_variant", None)
+    if fn is None:
+        raise RuntimeError("nf4_gemm: tb_nf4_gemm_variant is not in the loaded library")
+    fn.restype, fn.argtypes = ctypes.c_int, [_lib._I32]
+    if fn(int(variant)) != 0:
+        raise ValueError(_lib.load().tb_last_error().decode(errors="replace"))
+
+
 def supported(weights, transpose=False):
     """True when tb_nf4_gemm takes these weights: 1-4 NF4 weights with blocksize 64, the same
     column count, rows a multiple of 128 (forward) or 64 (backward), columns a multiple of 64
