@@ -192,10 +192,10 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 }
 
 // every thread of every CTA of the cluster; orders shared-memory writes before the barrier
-// with the reads (local or remote) after it
+// with the reads (local or remote) after it. The non-.aligned form: the lanes of the producer
+// and MMA warps reach it at different times.
 __device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
-               ::: "memory");
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
 // the float at the address `p` has in this CTA, in the shared memory of cluster CTA `rank`
