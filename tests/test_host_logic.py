@@ -1,8 +1,10 @@
 """Host-side logic that needs no GPU: which parameters the LoRA node accumulates into in place
-(GradBucket views), and the bench's filtering of nvidia-smi clock samples to the timed region."""
+(GradBucket views), the bench's filtering of nvidia-smi clock samples to the timed region, and
+the batch facts a captured step is planned from."""
 
 import datetime
 
+import pytest
 import torch
 
 
@@ -46,3 +48,31 @@ def test_clock_samples_are_filtered_to_the_region():
     sm, _, _, inside = bench.Clocks.parse(rows, stop, stop)
     assert len(sm) == 4 and inside == 0
     assert bench.Clocks.parse([["not", "a", "row"]], start, stop) == ([], None, [], 0)
+
+
+@pytest.mark.parametrize("num_items", [None, 7])
+def test_host_plan_matches_the_shifted_causal_lm_targets(num_items):
+    """graphs.host_plan (the captured step's batch facts, from host copies) against a loop over
+    the batch: real positions in row-major order, each scored against the next position's label
+    in the same row (the last column against nothing), labelled count, loss denominator."""
+    from testt_b200.graphs import host_plan
+
+    mask = torch.tensor([[1, 1, 1, 1, 0, 0],
+                         [0, 0, 1, 1, 1, 1],
+                         [1, 0, 1, 1, 0, 1],
+                         [0, 0, 0, 0, 0, 0]])
+    labels = torch.tensor([[-100, 11, 12, 13, -100, -100],
+                           [-100, -100, -100, 21, 22, 23],
+                           [30, -100, 32, -100, -100, 35],
+                           [-100, -100, -100, -100, -100, -100]])
+    pos, n_labelled, denom = host_plan(mask, labels, num_items)
+    want_pos, want_targets = [], []
+    for b in range(mask.shape[0]):
+        for t in range(mask.shape[1]):
+            if mask[b, t]:
+                want_pos.append(b * mask.shape[1] + t)
+                want_targets.append(int(labels[b, t + 1]) if t + 1 < mask.shape[1] else -100)
+    assert pos.tolist() == want_pos
+    labelled = sum(1 for y in want_targets if y != -100)
+    assert n_labelled == labelled == 6
+    assert denom == (float(num_items) if num_items is not None else float(labelled))
