@@ -291,3 +291,17 @@ def test_nf4_gemm_host_absmax_and_oracle(nested):
     assert torch.equal(y, (x.double() @ w.double().t() + bias.double()).half())
     dy = torch.from_numpy((rng.standard_normal((3, 384))).astype(np.float16))
     assert torch.equal(ops.nf4_matmul(dy, qs, transpose=True), (dy.double() @ w.double()).half())
+
+
+def test_cpu_step_sample_runs_at_small_shapes():
+    """The timed CPU baseline (oracle.step) end to end at small dimensions: one decoder layer
+    forward and backward with its NF4 weights unpacked by the C oracle, and the head sample."""
+    import math
+
+    from oracle import step
+
+    layer = step.CpuLayerSample([5, 9], hidden=128, inter=256, heads=4, kv=2, head_dim=32, seq=16)
+    assert layer.rows == 14
+    assert math.isfinite(layer.run()) and layer.run() > 0
+    head = step.CpuHeadSample(rows=8, vocab=300, hidden=128)
+    assert math.isfinite(head.run())
