@@ -114,3 +114,34 @@ def test_rejects_shapes_it_does_not_take():
     with pytest.raises(ValueError):
         nf4_gemm.nf4_matmul(_x(4, 256, seed=6), ws)
     assert nf4_gemm.nf4_matmul(_x(0, 128, seed=6), ws, transpose=True).shape == (0, 256)
+
+
+@requires_kernel
+def test_fused_layer_nodes_match_the_unpacking_nodes():
+    """fused_layer.layer_linear / layer_mlp (the GEMM decodes NF4 itself) against
+    nf4.layer_linear / mlp.layer_mlp (one unpack launch, cuBLAS) on the same LayerWeights, forward
+    and input gradient, at the Qwen2.5 layer's widths scaled down (q|k|v, o, gate|up, down)."""
+    from testt_b200 import fused_layer, mlp, nf4
+
+    rng = np.random.default_rng(12)
+    shapes = [(512, 512), (128, 512), (128, 512), (512, 512), (1024, 512), (1024, 512), (512, 1024)]
+    qs = [onf4.quantize((rng.standard_normal(sh) * 0.05).astype(np.float16), 64, nested=True)
+          for sh in shapes]
+    ws = [nf4_weight(q, "cuda") for q in qs]
+    lw = nf4.LayerWeights(((ws[0], ws[1], ws[2]), (ws[3],), (ws[4], ws[5]), (ws[6],)))
+    assert fused_layer.usable(lw)
+    bias = _x(1, 768, seed=13, std=0.1)[0]
+    x = _x(300, 512, seed=14).requires_grad_(True)
+    x2 = x.detach().clone().requires_grad_(True)
+    y = fused_layer.layer_linear(x, lw, 0, bias)
+    z = fused_layer.layer_mlp(y[:, :512], lw, 2, 3)
+    y2 = nf4.layer_linear(x2, lw, 0, bias)
+    z2 = mlp.layer_mlp(y2[:, :512], lw, 2, 3)
+    gz = _x(300, 512, seed=15, std=0.01)
+    (z.float() * gz.float()).sum().backward()
+    (z2.float() * gz.float()).sum().backward()
+    lw.release()
+    torch.cuda.synchronize()
+    assert_rel(y.detach().cpu(), y2.detach().cpu(), 2e-3, "qkv")
+    assert_rel(z.detach().cpu(), z2.detach().cpu(), 2e-3, "mlp")
+    assert_rel(x.grad.cpu(), x2.grad.cpu(), 2e-3, "dx")

@@ -1,0 +1,79 @@
+"""The decoder layer's frozen NF4 projections through the NF4-decoding tensor-core GEMM
+(nf4_gemm.nf4_matmul): the autograd nodes that replace nf4.LayerLinear and mlp.LayerMLP when
+every operand of a layer is supported, so the step unpacks no weight at all
+(reference: solution/nf4.py:108-127 FrozenNF4Linear, solution/mlp.py:80-113 FusedNF4MLP).
+
+Staged with the kernel: nothing imports this module until tb_nf4_gemm is linked into the
+library; `usable(lw)` is False before that.
+
+Same operations and roundings as the unpacking path: each GEMM takes fp16 operands, sums in fp32
+and rounds once to fp16 (the bias added before that rounding, as cuBLAS's bias epilogue does),
+the gate|up output is kept for the backward (mlp.RECOMPUTE_GATE_UP False) and SwiGLU runs
+through the same kernels.
+"""
+
+import torch
+
+from . import nf4_gemm
+from .mlp import gated_silu, gated_silu_backward_
+
+
+def usable(lw):
+    """True when tb_nf4_gemm is loaded and takes every operand group of the LayerWeights `lw`
+    in both directions."""
+    if not nf4_gemm.available():
+        return False
+    return all(nf4_gemm.supported(g) and nf4_gemm.supported(g, transpose=True)
+               for g in lw.groups)
+
+
+class FusedLayerLinear(torch.autograd.Function):
+    """y = x W^T (+ b) with W operand `group` of a LayerWeights, decoded inside the GEMM."""
+
+    @staticmethod
+    def forward(ctx, x, bias, lw, group):
+        ctx.weights = lw.groups[group]
+        return nf4_gemm.nf4_matmul(x.contiguous(), ctx.weights, bias)
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        grad_x = None
+        if ctx.needs_input_grad[0]:
+            grad_x = nf4_gemm.nf4_matmul(grad_out.to(torch.float16).contiguous(), ctx.weights,
+                                         transpose=True)
+        return grad_x, None, None, None
+
+
+class FusedLayerMLP(torch.autograd.Function):
+    """down(SwiGLU(x [gate|up]^T)) with both GEMMs and their dX decoded inside the GEMM."""
+
+    @staticmethod
+    def forward(ctx, x, lw, g_gu, g_down):
+        x = x.contiguous()
+        gate_up, down = lw.groups[g_gu], lw.groups[g_down]
+        gu = nf4_gemm.nf4_matmul(x, gate_up)
+        act = gated_silu(gu)
+        out = nf4_gemm.nf4_matmul(act, down)
+        ctx.save_for_backward(gu)
+        ctx.weights = (gate_up, down)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        if not ctx.needs_input_grad[0]:
+            return None, None, None, None
+        (gu,) = ctx.saved_tensors
+        gate_up, down = ctx.weights
+        dact = nf4_gemm.nf4_matmul(grad_out.to(torch.float16).contiguous(), down, transpose=True)
+        gated_silu_backward_(dact, gu)  # gu now holds d(gate|up)
+        del dact
+        grad_x = nf4_gemm.nf4_matmul(gu, gate_up, transpose=True)
+        return grad_x, None, None, None
+
+
+def layer_linear(x, lw, group, bias=None):
+    return FusedLayerLinear.apply(x, bias, lw, group)
+
+
+def layer_mlp(x, lw, g_gu, g_down):
+    return FusedLayerMLP.apply(x, lw, g_gu, g_down)
