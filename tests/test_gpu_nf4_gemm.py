@@ -145,3 +145,31 @@ def test_fused_layer_nodes_match_the_unpacking_nodes():
     assert_rel(y.detach().cpu(), y2.detach().cpu(), 2e-3, "qkv")
     assert_rel(z.detach().cpu(), z2.detach().cpu(), 2e-3, "mlp")
     assert_rel(x.grad.cpu(), x2.grad.cpu(), 2e-3, "dx")
+
+
+@requires_kernel
+@pytest.mark.parametrize("tokens", [1, 300, 621])
+def test_swiglu_epilogues_match_gemm_then_swiglu_kernels(tokens):
+    """tb_nf4_gemm_swiglu: gate|up forward with act formed in the epilogue, and down's dX with
+    the in-place SwiGLU backward in the epilogue, against the plain GEMM followed by the SwiGLU
+    kernels (mlp.gated_silu / gated_silu_backward_)."""
+    from testt_b200 import mlp, nf4_gemm
+
+    inter, hidden = 1024, 512
+    _, gate_up = _weights((inter, inter), hidden, True, seed=20)
+    _, down = _weights((hidden,), inter, True, seed=21)
+    x = _x(tokens, hidden, seed=22)
+    gu, act = nf4_gemm.gate_up_swiglu(x, gate_up)
+    gu_ref = nf4_gemm.nf4_matmul(x, gate_up)
+    torch.cuda.synchronize()
+    assert_rel(gu.cpu(), gu_ref.cpu(), RTOL, "gu")
+    from helpers import assert_ulp
+
+    assert_ulp(act.cpu(), mlp.gated_silu(gu).cpu(), 1, "act from the epilogue's own gu")
+    dy = _x(tokens, hidden, seed=23, std=0.01)
+    g1, g2 = gu.clone(), gu.clone()
+    nf4_gemm.down_swiglu_backward_(dy, down[0], g1)
+    dact = nf4_gemm.nf4_matmul(dy, down, transpose=True)
+    mlp.gated_silu_backward_(dact, g2)
+    torch.cuda.synchronize()
+    assert_rel(g1.float().cpu(), g2.float().cpu(), 2e-3, "d(gate|up)")

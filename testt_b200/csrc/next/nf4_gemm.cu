@@ -34,6 +34,9 @@
 // adds column slice r of all of them through distributed shared memory in split order, with
 // the bias; or through fp32 partials [split, token, row] in a caller's workspace, summed in
 // split order by nf4_gemm_reduce (tb_nf4_gemm_variant(1)).
+// tb_nf4_gemm_swiglu runs the MLP's GEMMs with SwiGLU in the epilogue: the gate|up forward
+// (tiles of 64 gate and 64 up rows, act formed from both halves through shared memory) and
+// down's dX (dact never written: the epilogue applies the in-place SwiGLU backward to gu).
 // Every mbarrier wait is bounded (mbar_wait); a role that gives up sets the CTA's error flag
 // and leaves its loop, every role meets at the final barrier and TMEM is always released.
 // No multicast is used.
@@ -89,7 +92,18 @@ struct GemmArgs {
   float *part;               // [splits, tokens, a_rows] fp32 when splits > 1 (not cluster)
   int cluster;               // splits > 1: the splits are one thread-block cluster and sum
                              // their accumulators through distributed shared memory
+  int mode;                  // kPlain, kSwigluFwd, kSwigluBwd (one split)
+  uint16_t *gu;              // SwiGLU modes: fp16 [tokens, 2 * inter] gate | up (row stride ld_gu)
+  int64_t ld_gu;
+  int inter;
 };
+
+// kSwigluFwd: W = (gate, up); CTA x holds gate rows 64x .. 64x + 63 as A rows 0-63 and the same
+//   up rows as A rows 64-127; the epilogue writes gu = fp16(x [gate|up]^T) and
+//   act = fp16(silu(g) u) to out (mlp.py:31-40 on the GEMM's fp16 output).
+// kSwigluBwd: W = (down,), transposed: the epilogue rounds dact = dy . W_down to fp16 and applies
+//   the in-place SwiGLU backward to gu (mlp.py:43-58).
+constexpr int kPlain = 0, kSwigluFwd = 1, kSwigluBwd = 2;
 
 // ---- tcgen05 / TMA helpers (PTX ISA: tcgen05.mma, cp.async.bulk.tensor) --------------------
 
@@ -205,6 +219,24 @@ __device__ __forceinline__ float ld_cluster(const float *p, uint32_t rank) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
   return v;
+}
+
+// the SwiGLU kernels' formulas (fast exponential and division, as the reference's lower to)
+__device__ __forceinline__ float silu(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+
+__device__ __forceinline__ void swiglu_bwd_one(float dact, float g, float u, float &dg, float &du) {
+  const float sig = __fdividef(1.0f, 1.0f + __expf(-g));
+  const float d_silu = dact * u;
+  dg = d_silu * sig * (1.0f + g * (1.0f - sig));
+  du = dact * (g * sig);
+}
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+
+// barrier of the four epilogue warps (named barrier 1, 128 threads)
+__device__ __forceinline__ void epilogue_sync() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -392,8 +424,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- decoders, then the epilogue --------------------------------------------------------
     const int d = threadIdx.x - 64;  // 0 .. 127
     if (!kTrans) {
-      const int j = weight_of(args, a0);  // a tile lies inside one weight (rows % 128 == 0)
-      const int local = a0 - args.row_start[j] + d;
+      // a tile lies inside one weight (rows % 128 == 0), or holds 64 gate and 64 up rows
+      const bool inter = args.mode == kSwigluFwd;
+      const int j = inter ? (d < 64 ? 0 : 1) : weight_of(args, a0);
+      const int local = inter ? (int)blockIdx.x * 64 + (d & 63) : a0 - args.row_start[j] + d;
       const uint8_t *row_bytes = args.packed[j] + (size_t)local * (size_t)(args.k_dim >> 1);
       const float *row_absmax = args.absmax[j] + (size_t)local * (size_t)(args.k_dim >> 6);
       const uint32_t tab = smem_u32(&sm.table[j][0]);
@@ -440,7 +474,90 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ok = mbar_wait(&sm.acc_full, 0) ? 1 : 0;
     if (!__all_sync(0xffffffffu, ok)) {
       if (lane == 0) sm.error = 1;
-    } else if (!sm.error) {
+    }
+    const bool go = __all_sync(0xffffffffu, ok) && !sm.error;
+    if (args.mode == kSwigluFwd) {
+      // phase 1: every warp stores its fp16 values to gu; the up warps (quarters 2, 3) also to
+      // xch[column][64] in the idle stage buffers. Phase 2 (after the epilogue warps' barrier,
+      // reached by all four whatever happened): the gate warps form act.
+      uint16_t *xch = reinterpret_cast<uint16_t *>(&sm.a[0][0]);
+      const bool up = quarter >= 2;
+      const int fl = (quarter & 1) * 32 + lane;     // feature within the tile's 64
+      const int f = (int)blockIdx.x * 64 + fl;
+      if (go) {
+        tc_fence_after();
+        for (int j = 0; j < args.nsub; ++j)
+          for (int c = 0; c < args.bn; c += 32) {
+            const int tb = t0 + j * args.bn + c;
+            if (tb >= args.tokens) break;
+            uint32_t v[32];
+            tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(j * args.bn + c), v);
+            const int ne = args.tokens - tb < 32 ? args.tokens - tb : 32;
+            uint16_t *o = args.gu + (int64_t)tb * args.ld_gu + (up ? args.inter : 0) + f;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              if (e >= ne) break;
+              const uint16_t x16 = f2h(__uint_as_float(v[e]));
+              o[(int64_t)e * args.ld_gu] = x16;
+              if (up) xch[(j * args.bn + c + e) * 64 + fl] = x16;
+            }
+          }
+      }
+      epilogue_sync();
+      if (go && !up) {
+        for (int j = 0; j < args.nsub; ++j)
+          for (int c = 0; c < args.bn; c += 32) {
+            const int tb = t0 + j * args.bn + c;
+            if (tb >= args.tokens) break;
+            uint32_t v[32];
+            tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(j * args.bn + c), v);
+            const int ne = args.tokens - tb < 32 ? args.tokens - tb : 32;
+            uint16_t *o = args.out + (int64_t)tb * args.ld_out + f;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              if (e >= ne) break;
+              const float g = h2f(f2h(__uint_as_float(v[e])));
+              const float u = h2f(xch[(j * args.bn + c + e) * 64 + fl]);
+              o[(int64_t)e * args.ld_out] = f2h(silu(g) * u);
+            }
+          }
+      }
+    } else if (args.mode == kSwigluBwd) {
+      // dact rounded to fp16 as the unfused GEMM's output; gu's two halves updated in place,
+      // 16 tokens at a time with all their loads issued before the math
+      if (go) {
+        tc_fence_after();
+        const int f = a0 + quarter * 32 + lane;
+        for (int j = 0; j < args.nsub; ++j)
+          for (int c = 0; c < args.bn; c += 32) {
+            const int tb = t0 + j * args.bn + c;
+            if (tb >= args.tokens) break;
+            uint32_t v[32];
+            tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(j * args.bn + c), v);
+            const int ne = args.tokens - tb < 32 ? args.tokens - tb : 32;
+            uint16_t *pg = args.gu + (int64_t)tb * args.ld_gu + f;
+#pragma unroll
+            for (int h = 0; h < 32; h += 16) {
+              uint16_t g16[16], u16[16];
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                const bool in = h + e < ne;
+                g16[e] = in ? pg[(int64_t)(h + e) * args.ld_gu] : (uint16_t)0;
+                u16[e] = in ? pg[(int64_t)(h + e) * args.ld_gu + args.inter] : (uint16_t)0;
+              }
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                if (h + e >= ne) break;
+                float dg, du;
+                swiglu_bwd_one(h2f(f2h(__uint_as_float(v[h + e]))), h2f(g16[e]), h2f(u16[e]), dg,
+                               du);
+                pg[(int64_t)(h + e) * args.ld_gu] = f2h(dg);
+                pg[(int64_t)(h + e) * args.ld_gu + args.inter] = f2h(du);
+              }
+            }
+          }
+      }
+    } else if (go) {
       tc_fence_after();
       const int row = a0 + quarter * 32 + lane;
       const bool add_bias = args.splits == 1 && args.bias != nullptr;
@@ -738,6 +855,10 @@ extern "C" int tb_nf4_gemm(int32_t transpose, const uint16_t *tokens_in, int64_t
   a.ld_out = ld_out;
   a.part = p.splits > 1 && !p.cluster ? workspace : nullptr;
   a.cluster = p.cluster;
+  a.mode = kPlain;
+  a.gu = nullptr;
+  a.ld_gu = 0;
+  a.inter = 0;
 
   CUtensorMap map_b;
   rc = make_map(&map_b, tokens_in, tokens, red_dim, ld_in, p.bn);
@@ -772,6 +893,73 @@ extern "C" int tb_nf4_gemm(int32_t transpose, const uint16_t *tokens_in, int64_t
   return launch("nf4_gemm_reduce", nf4_gemm_reduce, dim3((unsigned)blocks), dim3(256), 0,
                 as_stream(stream), (const float *)workspace, p.splits, tokens, a.a_rows, bias, out,
                 ld_out);
+}
+
+// The MLP's two NF4 GEMMs with SwiGLU in their epilogue (one split each):
+//   forward  (backward == 0): weights (gate, up), each [inter, k_dim]; tokens_in = x
+//            [tokens, k_dim]; writes gu = fp16(x [gate|up]^T) [tokens, 2 inter] (row stride
+//            ld_gu) and act = fp16(silu(g) u) [tokens, inter] (row stride ld_act)
+//   backward (backward == 1): weight (down,) [hidden, inter] (k_dim = inter); tokens_in = dy
+//            [tokens, hidden]; dact = fp16(dy . W_down) stays in the epilogue, which overwrites
+//            gu with d(gate|up) (act unused)
+extern "C" int tb_nf4_gemm_swiglu(int32_t backward, const uint16_t *tokens_in, int64_t tokens,
+                                  int64_t ld_in, int32_t n_weights, const uint8_t *const *packed,
+                                  const float *const *absmax, const float *const *nf4_table,
+                                  const int64_t *rows, int64_t k_dim, uint16_t *gu, int64_t ld_gu,
+                                  uint16_t *act, int64_t ld_act, void *stream) {
+  GemmArgs a;
+  int rc = gemm_args(backward ? 1 : 0, tokens, n_weights, packed, absmax, nf4_table, rows, k_dim,
+                     a);
+  if (rc != TB_OK) return rc;
+  const int64_t inter = backward ? k_dim : rows[0];
+  if (backward ? n_weights != 1 : (n_weights != 2 || rows[1] != rows[0] || rows[0] % 64 != 0))
+    return set_error(TB_EINVAL, "nf4_gemm_swiglu: (gate, up) of equal rows forward, (down,) "
+                     "backward");
+  if (tokens == 0) return TB_OK;
+  const int64_t red_dim = (int64_t)a.red_blocks * kBK;
+  if (!tokens_in || !gu || (!backward && !act))
+    return set_error(TB_EINVAL, "nf4_gemm_swiglu: tokens_in, gu (and act forward) required");
+  if (ld_in < red_dim || ld_in % 8 != 0 || ld_gu < 2 * inter || (!backward && ld_act < inter))
+    return set_error(TB_EINVAL, "nf4_gemm_swiglu: ld_in %lld ld_gu %lld ld_act %lld",
+                     (long long)ld_in, (long long)ld_gu, (long long)ld_act);
+  if (!aligned(tokens_in, 16) || !aligned(gu, 2) || (act && !aligned(act, 2)))
+    return set_error(TB_EALIGN, "nf4_gemm_swiglu: misaligned buffer");
+  int dev = 0, major = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (major != 10) return set_error(TB_EDEVICE, "nf4_gemm_swiglu: needs an sm_100 GPU");
+
+  // forward tiles hold 64 features of each weight; backward tiles 128 features of dact
+  const int a_tiles = backward ? (int)(inter / kBM) : (int)(inter / 64);
+  Plan p = make_plan(tokens, a_tiles, a.red_blocks, a.a_rows, 0, sm_count(), 1);
+  p.splits = 1;
+  p.cluster = 0;
+  a.bn = p.bn;
+  a.nsub = p.nsub;
+  a.span = p.span;
+  a.splits = 1;
+  a.idesc = (1u << 4) | ((uint32_t)(p.bn >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+  a.bias = nullptr;
+  a.out = act;
+  a.ld_out = ld_act;
+  a.part = nullptr;
+  a.cluster = 0;
+  a.mode = backward ? kSwigluBwd : kSwigluFwd;
+  a.gu = gu;
+  a.ld_gu = ld_gu;
+  a.inter = (int)inter;
+
+  CUtensorMap map_b;
+  rc = make_map(&map_b, tokens_in, tokens, red_dim, ld_in, p.bn);
+  if (rc != TB_OK) return rc;
+  const size_t smem = sizeof(Smem) + 1024;
+  auto kernel = backward ? nf4_gemm_kernel<true> : nf4_gemm_kernel<false>;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return check_launch("nf4_gemm_swiglu attribute");
+  const dim3 grid((unsigned)a_tiles, (unsigned)p.groups, 1u);
+  kernel<<<grid, kThreads, smem, as_stream(stream)>>>(map_b, a);
+  return check_launch("nf4_gemm_swiglu");
 }
 
 extern "C" int tb_nf4_gemm_variant(int32_t variant) {

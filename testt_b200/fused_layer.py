@@ -18,13 +18,21 @@ from . import nf4_gemm
 from .mlp import gated_silu, gated_silu_backward_
 
 
-def usable(lw):
+def usable(lw, g_gu=2, g_down=3):
     """True when tb_nf4_gemm is loaded and takes every operand group of the LayerWeights `lw`
-    in both directions."""
+    in both directions (and, with SwiGLU in the epilogues, gate|up as two weights of equal rows
+    and down as one weight)."""
     if not nf4_gemm.available():
         return False
-    return all(nf4_gemm.supported(g) and nf4_gemm.supported(g, transpose=True)
-               for g in lw.groups)
+    if not all(nf4_gemm.supported(g) and nf4_gemm.supported(g, transpose=True)
+               for g in lw.groups):
+        return False
+    if SWIGLU_IN_EPILOGUE:
+        gate_up, down = lw.groups[g_gu], lw.groups[g_down]
+        return len(gate_up) == 2 and len(down) == 1 and \
+            nf4_gemm.weight_shape(gate_up[0])[0] % 64 == 0 and \
+            nf4_gemm.weight_shape(gate_up[0]) == nf4_gemm.weight_shape(gate_up[1])
+    return True
 
 
 class FusedLayerLinear(torch.autograd.Function):
@@ -44,6 +52,10 @@ class FusedLayerLinear(torch.autograd.Function):
         return grad_x, None, None, None
 
 
+# SwiGLU in the GEMMs' epilogues (gate|up forward, down's dX) instead of its own kernels
+SWIGLU_IN_EPILOGUE = True
+
+
 class FusedLayerMLP(torch.autograd.Function):
     """down(SwiGLU(x [gate|up]^T)) with both GEMMs and their dX decoded inside the GEMM."""
 
@@ -51,8 +63,11 @@ class FusedLayerMLP(torch.autograd.Function):
     def forward(ctx, x, lw, g_gu, g_down):
         x = x.contiguous()
         gate_up, down = lw.groups[g_gu], lw.groups[g_down]
-        gu = nf4_gemm.nf4_matmul(x, gate_up)
-        act = gated_silu(gu)
+        if SWIGLU_IN_EPILOGUE:
+            gu, act = nf4_gemm.gate_up_swiglu(x, gate_up)
+        else:
+            gu = nf4_gemm.nf4_matmul(x, gate_up)
+            act = gated_silu(gu)
         out = nf4_gemm.nf4_matmul(act, down)
         ctx.save_for_backward(gu)
         ctx.weights = (gate_up, down)
@@ -64,9 +79,13 @@ class FusedLayerMLP(torch.autograd.Function):
             return None, None, None, None
         (gu,) = ctx.saved_tensors
         gate_up, down = ctx.weights
-        dact = nf4_gemm.nf4_matmul(grad_out.to(torch.float16).contiguous(), down, transpose=True)
-        gated_silu_backward_(dact, gu)  # gu now holds d(gate|up)
-        del dact
+        if SWIGLU_IN_EPILOGUE:
+            nf4_gemm.down_swiglu_backward_(grad_out, down[0], gu)  # gu now holds d(gate|up)
+        else:
+            dact = nf4_gemm.nf4_matmul(grad_out.to(torch.float16).contiguous(), down,
+                                       transpose=True)
+            gated_silu_backward_(dact, gu)  # gu now holds d(gate|up)
+            del dact
         grad_x = nf4_gemm.nf4_matmul(gu, gate_up, transpose=True)
         return grad_x, None, None, None
 

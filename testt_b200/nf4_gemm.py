@@ -136,3 +136,53 @@ def nf4_matmul(x, weights, bias=None, transpose=False):
         msg = _lib.load().tb_last_error().decode(errors="replace")
         raise _lib.KernelError(f"tb_nf4_gemm failed ({rc}): {msg}")
     return out
+
+
+_SWIGLU_SIG = [_lib._I32, _lib._P, _lib._I64, _lib._I64, _lib._I32, _lib._P, _lib._P, _lib._P,
+               _lib._P, _lib._I64, _lib._P, _lib._I64, _lib._P, _lib._I64, _lib._P]
+
+
+def _swiglu_call(backward, x, weights, gu, act):
+    fn = getattr(_lib.load(), "tb_nf4_gemm_swiglu", None)
+    if fn is None:
+        raise RuntimeError("nf4_gemm: tb_nf4_gemm_swiglu is not in the loaded library (staged)")
+    fn.restype, fn.argtypes = ctypes.c_int, _SWIGLU_SIG
+    rows = [weight_shape(w)[0] for w in weights]
+    cols = weight_shape(weights[0])[1]
+    n = len(weights)
+    rc = fn(int(backward), _lib.ptr(x), x.shape[0], x.stride(0), n,
+            _lib.ptr_array([_lib.ptr(w.data) for w in weights]),
+            _lib.ptr_array([_lib.ptr(fp32_absmax(w)) for w in weights]),
+            _lib.ptr_array([_lib.ptr(_quant_state(w).code.to(torch.float32).contiguous())
+                            for w in weights]),
+            (ctypes.c_int64 * n)(*rows), cols, _lib.ptr(gu), gu.stride(0), _lib.ptr(act),
+            act.stride(0) if act is not None else 0, _lib.stream_of(x))
+    if rc != 0:
+        msg = _lib.load().tb_last_error().decode(errors="replace")
+        raise _lib.KernelError(f"tb_nf4_gemm_swiglu failed ({rc}): {msg}")
+
+
+def gate_up_swiglu(x, gate_up):
+    """(gu, act) for x [T, K] and the (gate, up) NF4 weights [I, K] each: gu = fp16(x [gate|up]^T)
+    [T, 2I] and act = fp16(silu(g) u) [T, I], from one GEMM with SwiGLU in its epilogue (the
+    reference: a GEMM, then gated_silu, solution/mlp.py:82-99)."""
+    _lib.require_cuda(x, what="gate_up_swiglu")
+    gate, up = gate_up
+    inter = weight_shape(gate)[0]
+    x = x.contiguous()
+    gu = torch.empty((x.shape[0], 2 * inter), dtype=torch.float16, device=x.device)
+    act = torch.empty((x.shape[0], inter), dtype=torch.float16, device=x.device)
+    if x.shape[0]:
+        _swiglu_call(False, x, (gate, up), gu, act)
+    return gu, act
+
+
+def down_swiglu_backward_(dy, down, gu):
+    """gu <- d(gate|up), in place: dact = fp16(dy . W_down) never leaves the GEMM's epilogue, which
+    applies the SwiGLU backward to gu (the reference: a GEMM, then gated_silu_backward_,
+    solution/mlp.py:103-110). Returns gu."""
+    _lib.require_cuda(dy, gu, what="down_swiglu_backward_")
+    dy = dy.to(torch.float16).contiguous()
+    if dy.shape[0]:
+        _swiglu_call(True, dy, (down,), gu, None)
+    return gu
