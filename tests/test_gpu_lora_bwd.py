@@ -93,3 +93,51 @@ def test_one_adapter_and_determinism(present):
     assert_rel(ad["dh"].float().cpu(), dh.float().cpu(), 1e-3, "dh")
     assert_rel(ad["db"].cpu(), db.cpu(), 1e-4, "dB")
     assert_rel(ad["da"].cpu(), da.cpu(), 1e-4, "dA")
+
+
+@requires_kernel
+@pytest.mark.parametrize("in_bucket", [False, True])
+def test_lora_pair_with_fused_backward_matches_gemm_backward(monkeypatch, in_bucket):
+    """lora_fused.LoraPairFused (tb_lora_backward, then the dropout backward) against
+    lora.LoraPair (six GEMMs, then the same dropout backward) through lora.lora_pair, with the
+    same dropout draws: the padded input's gradient and both adapters' weight gradients,
+    returned to autograd or accumulated into GradBucket views."""
+    from testt_b200 import lora, lora_fused
+    from testt_b200.dist import GradBucket
+    from testt_b200.rope import slot_index
+
+    batch, seq, hidden, r = 3, 40, 256, 16
+    lengths = [33, 7, 40]
+    pos = torch.cat([torch.arange(n) + i * seq for i, n in enumerate(lengths)]).cuda()
+    slot = slot_index(pos, batch * seq)
+    x0 = torch.randn(batch * seq, hidden, device="cuda")
+    gq = (torch.randn(pos.numel(), hidden, device="cuda") * 0.1).half()
+    gv = (torch.randn(pos.numel(), 64, device="cuda") * 0.1).half()
+
+    def run(node):
+        g = torch.Generator().manual_seed(3)
+        parts = []
+        for out, scaling in ((hidden, 2.0), (64, 0.5)):
+            a = torch.nn.Linear(hidden, r, bias=False).cuda()
+            b = torch.nn.Linear(r, out, bias=False).cuda()
+            with torch.no_grad():
+                a.weight.copy_(torch.randn(r, hidden, generator=g) * 0.05)
+                b.weight.copy_(torch.randn(out, r, generator=g) * 0.05)
+            parts.append((torch.nn.Dropout(0.05), a, b, scaling))
+        params = [t.weight for _, a, b, _ in parts for t in (a, b)]
+        if in_bucket:
+            GradBucket(params)
+        monkeypatch.setattr(lora, "LoraPair", node)
+        torch.manual_seed(11)
+        x = x0.clone().requires_grad_(True)
+        with torch.autocast("cuda", dtype=torch.float16):
+            lq, lv = lora.lora_pair(parts[0], parts[1], x, pos, slot)
+        torch.autograd.backward([lq, lv], [gq, gv])
+        torch.cuda.synchronize()
+        return x.grad.clone(), [p.grad.clone() for p in params]
+
+    gx_ref, gw_ref = run(lora.LoraPair)
+    gx, gw = run(lora_fused.LoraPairFused)
+    torch.testing.assert_close(gx, gx_ref, rtol=5e-3, atol=1e-5)
+    for got, ref in zip(gw, gw_ref):
+        torch.testing.assert_close(got, ref, rtol=5e-3, atol=float(ref.abs().max()) * 2e-3)

@@ -1,0 +1,101 @@
+"""The LoRA pair node with its rank-16 backward in two launches (tb_lora_backward: dh, dB and dA
+of both adapters) instead of six cuBLAS GEMMs (reference: solution/model.py:195-206, peft's
+lora_B(lora_A(dropout(x))) * scaling under fp16 autocast).
+
+Staged with the kernel (csrc/next/lora_bwd.cu): nothing imports this module until
+tb_lora_backward is linked into the library; `available()` is False before that. The forward is
+lora.LoraPair's; the backward computes the same quantities as lora.LoraPair.backward:
+    dh = fp16(s * g . fp16(B)), dB = s * g^T . h (fp32), dA = dh^T . x16 (fp32),
+each weight gradient added into its GradBucket view when the parameter has one, then the dropout
+backward with the rank-16 expansion (tb_lora_dropout_grad_expand).
+"""
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .lora import _F16, _RANK, LoraPair, _in_bucket
+
+_SIG = [_lib._P] * 7 + [_lib._I64, _lib._F] + [_lib._P] * 7 + [_lib._I64, _lib._F, _lib._I64,
+                                                                   _lib._I64, _lib._I32, _lib._I32,
+                                                                   _lib._P]
+
+
+def _entry():
+    fn = getattr(_lib.load(), "tb_lora_backward", None)
+    if fn is not None:
+        fn.restype, fn.argtypes = ctypes.c_int, _SIG
+    return fn
+
+
+def available():
+    return _entry() is not None
+
+
+class LoraPairFused(LoraPair):
+    """lora.LoraPair with the two-launch rank-16 backward (falls back to LoraPair.backward for
+    other ranks, a hidden size that is not a multiple of 64, or adapter widths that are not)."""
+
+    @staticmethod
+    def backward(ctx, gq_out, gv_out):
+        pos_idx, slot_tok, mq, mv, xq, hq, aq16, bq16, xv, hv, av16, bv16 = ctx.saved_tensors
+        (pq, on_q, sq), (pv, on_v, sv) = ctx.cfg
+        fn = _entry()
+        adapters = [(gq_out, xq, hq, aq16, bq16, sq), (gv_out, xv, hv, av16, bv16, sv)]
+        ok = fn is not None and ctx.hidden % 64 == 0 and all(
+            x16 is None or (h.shape[1] == _RANK and b16.shape[0] % 64 == 0)
+            for _, x16, h, _, b16, _ in adapters)
+        if not ok:
+            return LoraPair.backward(ctx, gq_out, gv_out)
+        need = ctx.needs_input_grad
+        pa_q, pb_q, pa_v, pb_v = ctx.params
+        rows = pos_idx.numel()
+        args, grads, dhs, a16s, accumulate = [], [], [], [], 0
+        with torch.autocast("cuda", enabled=False):
+            for j, ((g_out, x16, h, a16, b16, s), (pa, pb)) in enumerate(
+                    zip(adapters, ((pa_q, pb_q), (pa_v, pb_v)))):
+                if x16 is None:
+                    args += [None] * 7 + [0, 0.0]
+                    grads += [None, None]
+                    dhs.append(None)
+                    a16s.append(None)
+                    continue
+                width = b16.shape[0]
+                if g_out is None:
+                    g_out = torch.zeros((rows, width), dtype=_F16, device=x16.device)
+                g_out = g_out.to(_F16).contiguous()
+                dh = torch.empty((rows, _RANK), dtype=_F16, device=x16.device)
+                # weight gradients: into the bucket views (accumulated) or fresh fp32 tensors
+                if _in_bucket(pb):
+                    db, out_b = None, pb.grad
+                    accumulate |= 1 << (2 * j)
+                else:
+                    db = out_b = torch.empty((width, _RANK), dtype=torch.float32,
+                                             device=x16.device)
+                if _in_bucket(pa):
+                    da, out_a = None, pa.grad
+                    accumulate |= 1 << (2 * j + 1)
+                else:
+                    da = out_a = torch.empty((_RANK, ctx.hidden), dtype=torch.float32,
+                                             device=x16.device)
+                args += [_lib.ptr(g_out), _lib.ptr(h), _lib.ptr(b16.contiguous()),
+                         _lib.ptr(x16), _lib.ptr(dh), _lib.ptr(out_b), _lib.ptr(out_a), width, s]
+                grads += [da, db]
+                dhs.append(dh)
+                a16s.append(a16.contiguous())
+            rc = fn(*args, rows, ctx.hidden, _RANK, accumulate, _lib.stream_of(pos_idx))
+            if rc != 0:
+                msg = _lib.load().tb_last_error().decode(errors="replace")
+                raise _lib.KernelError(f"tb_lora_backward failed ({rc}): {msg}")
+            gx = None
+            if need[0]:
+                gx = torch.empty((ctx.slots, ctx.hidden), dtype=torch.float32,
+                                 device=slot_tok.device)
+                scale_q = float(1.0 / (1.0 - pq)) if mq is not None else 1.0
+                scale_v = float(1.0 / (1.0 - pv)) if mv is not None else 1.0
+                _lib.call("tb_lora_dropout_grad_expand", _lib.ptr(dhs[0]), _lib.ptr(a16s[0]),
+                          _lib.ptr(dhs[1]), _lib.ptr(a16s[1]), _lib.ptr(mq), _lib.ptr(mv),
+                          _lib.ptr(slot_tok), _lib.ptr(gx), ctx.slots, ctx.hidden, _RANK,
+                          scale_q, scale_v, _lib.stream_of(gx))
+        return (gx, grads[0], grads[1], grads[2], grads[3], None, None, None)
