@@ -76,3 +76,47 @@ def test_host_plan_matches_the_shifted_causal_lm_targets(num_items):
     labelled = sum(1 for y in want_targets if y != -100)
     assert n_labelled == labelled == 6
     assert denom == (float(num_items) if num_items is not None else float(labelled))
+
+
+def test_vocabulary_shards_tile_the_vocabulary():
+    """dist.shard_range: for any vocabulary and world size the ranks' [lo, hi) ranges are
+    contiguous, cover [0, vocab) exactly once, and differ in size by at most one row."""
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    from testt_b200.dist import shard_range
+
+    @settings(max_examples=200, deadline=None)
+    @given(st.integers(1, 300_000), st.integers(1, 64))
+    def check(vocab, world):
+        ranges = [shard_range(vocab, r, world) for r in range(world)]
+        assert ranges[0][0] == 0 and ranges[-1][1] == vocab
+        assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+        sizes = [hi - lo for lo, hi in ranges]
+        assert max(sizes) - min(sizes) <= 1 and min(sizes) >= 0
+
+    check()
+    assert shard_range(151936, 3, 8) == (3 * 18992, 4 * 18992)
+
+
+def test_head_gradient_unit_is_a_power_of_two_near_64_per_token():
+    """head._grad_unit (reference: solution/head.py:79-84): a power of two G with G / denominator
+    within a factor sqrt(2) of 64, clamped to [1, 65536]."""
+    import math
+
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    from testt_b200.head import _grad_unit
+
+    @settings(max_examples=300, deadline=None)
+    @given(st.floats(1e-3, 1e7, allow_nan=False))
+    def check(denom):
+        g = _grad_unit(denom)
+        e = math.log2(g)
+        assert e == int(e) and 0 <= e <= 16
+        if 1 <= e <= 15:
+            assert 64 / math.sqrt(2) * 0.999 <= g / denom <= 64 * math.sqrt(2) * 1.001
+
+    check()
+    assert _grad_unit(1024) == 65536.0 and _grad_unit(0) == 1.0
