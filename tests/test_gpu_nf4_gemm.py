@@ -173,3 +173,34 @@ def test_swiglu_epilogues_match_gemm_then_swiglu_kernels(tokens):
     mlp.gated_silu_backward_(dact, g2)
     torch.cuda.synchronize()
     assert_rel(g1.float().cpu(), g2.float().cpu(), 2e-3, "d(gate|up)")
+
+
+@requires_kernel
+@pytest.mark.parametrize("tokens", [1, 150, 621])
+@pytest.mark.parametrize("lora", [True, False])
+def test_qkv_rope_epilogue_matches_gemm_then_rope_tokens(tokens, lora):
+    """tb_nf4_gemm_qkv_rope (bias, LoRA rows and the rotary embedding in the q|k|v GEMM's
+    finishing phase, one head a tile, the split reduction through the cluster) against the
+    plain GEMM followed by rope.rope_tokens."""
+    from helpers import assert_ulp
+    from oracle import ops
+    from testt_b200 import nf4_gemm, rope
+
+    nh, nkv, hidden, seq = 4, 2, 512, 512
+    _, ws = _weights((nh * 128, nkv * 128, nkv * 128), hidden, True, seed=30)
+    x = _x(tokens, hidden, seed=31)
+    bias = _x(1, (nh + 2 * nkv) * 128, seed=32, std=0.1)[0]
+    lq = _x(tokens, nh * 128, seed=33, std=0.01) if lora else None
+    lv = _x(tokens, nkv * 128, seed=34, std=0.01) if lora else None
+    cos, sin = (t.cuda() for t in ops.rope_tables(seq, 128, 1e6))
+    g = torch.Generator().manual_seed(35)
+    pos = torch.sort(torch.randperm(4 * seq, generator=g)[:tokens]).values.cuda()
+    q, k, v = nf4_gemm.qkv_rope(x, ws, bias, lq, lv, cos, sin, pos, seq, nh, nkv)
+    qkv = nf4_gemm.nf4_matmul(x, ws, bias)
+    rq, rk, rv = rope.rope_tokens(qkv, lq, lv, cos, sin, pos, 4, seq, nh, nkv, 128)
+    torch.cuda.synchronize()
+    # the GEMM halves may round their fp32 sums differently (one fp16 ulp of qkv), then the
+    # same arithmetic: held to the GEMM tolerance, and the v rows (no rotation) to one ulp
+    assert_rel(q.float().cpu(), rq.float().cpu(), RTOL, "q")
+    assert_rel(k.float().cpu(), rk.float().cpu(), RTOL, "k")
+    assert_ulp(v.cpu(), rv.cpu(), 1, "v")

@@ -34,6 +34,8 @@
 // adds column slice r of all of them through distributed shared memory in split order, with
 // the bias; or through fp32 partials [split, token, row] in a caller's workspace, summed in
 // split order by nf4_gemm_reduce (tb_nf4_gemm_variant(1)).
+// tb_nf4_gemm_qkv_rope runs the q|k|v projection with its bias, the LoRA rows and the rotary
+// embedding in the finishing phase (one head a tile), writing token-major q, k, v.
 // tb_nf4_gemm_swiglu runs the MLP's GEMMs with SwiGLU in the epilogue: the gate|up forward
 // (tiles of 64 gate and 64 up rows, act formed from both halves through shared memory) and
 // down's dX (dact never written: the epilogue applies the in-place SwiGLU backward to gu).
@@ -92,10 +94,18 @@ struct GemmArgs {
   float *part;               // [splits, tokens, a_rows] fp32 when splits > 1 (not cluster)
   int cluster;               // splits > 1: the splits are one thread-block cluster and sum
                              // their accumulators through distributed shared memory
-  int mode;                  // kPlain, kSwigluFwd, kSwigluBwd (one split)
+  int mode;                  // kPlain, kSwigluFwd, kSwigluBwd (one split), kQkvRope
   uint16_t *gu;              // SwiGLU modes: fp16 [tokens, 2 * inter] gate | up (row stride ld_gu)
   int64_t ld_gu;
   int inter;
+  // kQkvRope: W = (q, k, v) with heads of 128 rows, one head a tile; the finished values (plus
+  // bias) are rounded to fp16 as the GEMM's output, the LoRA rows added (q, v) and q, k rotated,
+  // then written token-major: q [tokens, nh, 128], k, v [tokens, nkv, 128]
+  const uint16_t *lora_q, *lora_v;  // fp16 [tokens, nh * 128], [tokens, nkv * 128] or NULL
+  const float *cosv, *sinv;         // [seq, 128]
+  const int64_t *pos_idx;           // [tokens]: padded position, t = pos % seq
+  int seq, nh, nkv;
+  uint16_t *q_out, *k_out, *v_out;
 };
 
 // kSwigluFwd: W = (gate, up); CTA x holds gate rows 64x .. 64x + 63 as A rows 0-63 and the same
@@ -103,7 +113,7 @@ struct GemmArgs {
 //   act = fp16(silu(g) u) to out (mlp.py:31-40 on the GEMM's fp16 output).
 // kSwigluBwd: W = (down,), transposed: the epilogue rounds dact = dy . W_down to fp16 and applies
 //   the in-place SwiGLU backward to gu (mlp.py:43-58).
-constexpr int kPlain = 0, kSwigluFwd = 1, kSwigluBwd = 2;
+constexpr int kPlain = 0, kSwigluFwd = 1, kSwigluBwd = 2, kQkvRope = 3;
 
 // ---- tcgen05 / TMA helpers (PTX ISA: tcgen05.mma, cp.async.bulk.tensor) --------------------
 
@@ -569,7 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t v[32];
           tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(j * args.bn + c), v);
           const int ne = args.tokens - tb < 32 ? args.tokens - tb : 32;
-          if (args.cluster) {
+          if (args.cluster || args.mode == kQkvRope) {
             // the stage buffers are free once every MMA has completed: the accumulator goes
             // to red[column][row] (a warp's lanes are consecutive rows: conflict-free)
             float *red = reinterpret_cast<float *>(&sm.a[0][0]);
@@ -598,7 +608,61 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  if (args.cluster) {
+  if (args.mode == kQkvRope) {
+    // one head per tile: CTA r of the cluster (or the CTA alone) finishes columns
+    // [r * per, (r + 1) * per): rows p and p + 64 of a token together (the rotation's pair)
+    if (args.cluster) cluster_sync(); else __syncthreads();
+    const int parts = args.cluster ? args.splits : 1;
+    const int per = (args.span + parts - 1) / parts;
+    const int c_lo = (args.cluster ? (int)cluster_ctarank() : 0) * per;
+    const int c_hi = c_lo + per < args.span ? c_lo + per : args.span;
+    const float *red = reinterpret_cast<const float *>(&sm.a[0][0]);
+    const int hr = blockIdx.x;
+    const int D = kBM, H = kBM / 2;
+    for (int e = threadIdx.x; e < (c_hi - c_lo) * H; e += kThreads) {
+      const int col = c_lo + e / H, pr = e % H;
+      const int tok = t0 + col;
+      if (tok >= args.tokens) break;  // columns ascend with e
+      float s1 = 0.f, s2 = 0.f;
+      for (int q = 0; q < parts; ++q) {
+        const float *base = red + col * kBM;
+        s1 = __fadd_rn(s1, args.cluster ? ld_cluster(base + pr, (uint32_t)q) : base[pr]);
+        s2 = __fadd_rn(s2, args.cluster ? ld_cluster(base + pr + H, (uint32_t)q) : base[pr + H]);
+      }
+      if (args.bias != nullptr) {
+        s1 = __fadd_rn(s1, h2f(__ldg(args.bias + hr * D + pr)));
+        s2 = __fadd_rn(s2, h2f(__ldg(args.bias + hr * D + pr + H)));
+      }
+      float x1 = h2f(f2h(s1)), x2 = h2f(f2h(s2));  // the GEMM's fp16 output
+      const uint16_t *lora = nullptr;
+      uint16_t *dst;
+      if (hr < args.nh) {
+        lora = args.lora_q ? args.lora_q + ((int64_t)tok * args.nh + hr) * D : nullptr;
+        dst = args.q_out + ((int64_t)tok * args.nh + hr) * D;
+      } else if (hr < args.nh + args.nkv) {
+        dst = args.k_out + ((int64_t)tok * args.nkv + hr - args.nh) * D;
+      } else {
+        const int hv = hr - args.nh - args.nkv;
+        lora = args.lora_v ? args.lora_v + ((int64_t)tok * args.nkv + hv) * D : nullptr;
+        dst = args.v_out + ((int64_t)tok * args.nkv + hv) * D;
+      }
+      if (lora != nullptr) {
+        x1 = x1 + h2f(__ldg(lora + pr));
+        x2 = x2 + h2f(__ldg(lora + pr + H));
+      }
+      float o1 = x1, o2 = x2;  // v: LoRA-added, not rotated
+      if (hr < args.nh + args.nkv) {
+        const int64_t t = __ldg(args.pos_idx + tok) % args.seq;
+        const float c1 = __ldg(args.cosv + t * D + pr), c2 = __ldg(args.cosv + t * D + H + pr);
+        const float n1 = __ldg(args.sinv + t * D + pr), n2 = __ldg(args.sinv + t * D + H + pr);
+        o1 = x1 * c1 - x2 * n1;
+        o2 = x2 * c2 + x1 * n2;
+      }
+      dst[pr] = f2h(o1);
+      dst[pr + H] = f2h(o2);
+    }
+    if (args.cluster) cluster_sync();
+  } else if (args.cluster) {
     // the splits' sums: cluster CTA r finishes columns [r * per, (r + 1) * per) of the tile,
     // adding the CTAs' accumulators in rank (= split) order, then the bias; the second barrier
     // keeps every CTA's shared memory alive until all have read it
@@ -859,6 +923,11 @@ extern "C" int tb_nf4_gemm(int32_t transpose, const uint16_t *tokens_in, int64_t
   a.gu = nullptr;
   a.ld_gu = 0;
   a.inter = 0;
+  a.lora_q = a.lora_v = nullptr;
+  a.cosv = a.sinv = nullptr;
+  a.pos_idx = nullptr;
+  a.seq = a.nh = a.nkv = 0;
+  a.q_out = a.k_out = a.v_out = nullptr;
 
   CUtensorMap map_b;
   rc = make_map(&map_b, tokens_in, tokens, red_dim, ld_in, p.bn);
@@ -948,6 +1017,11 @@ extern "C" int tb_nf4_gemm_swiglu(int32_t backward, const uint16_t *tokens_in, i
   a.gu = gu;
   a.ld_gu = ld_gu;
   a.inter = (int)inter;
+  a.lora_q = a.lora_v = nullptr;
+  a.cosv = a.sinv = nullptr;
+  a.pos_idx = nullptr;
+  a.seq = a.nh = a.nkv = 0;
+  a.q_out = a.k_out = a.v_out = nullptr;
 
   CUtensorMap map_b;
   rc = make_map(&map_b, tokens_in, tokens, red_dim, ld_in, p.bn);
@@ -960,6 +1034,93 @@ extern "C" int tb_nf4_gemm_swiglu(int32_t backward, const uint16_t *tokens_in, i
   const dim3 grid((unsigned)a_tiles, (unsigned)p.groups, 1u);
   kernel<<<grid, kThreads, smem, as_stream(stream)>>>(map_b, a);
   return check_launch("nf4_gemm_swiglu");
+}
+
+// The q|k|v projection with its bias, the LoRA rows and the rotary embedding in the epilogue:
+// weights (q, k, v) = [n_heads * 128, k_dim], [n_kv * 128, k_dim] twice; x [tokens, k_dim] (row
+// stride ld_x); out q [tokens, n_heads, 128], k, v [tokens, n_kv, 128] (token-major, contiguous)
+// = what tb_rope_tokens_fwd writes from the GEMM's fp16 output (solution/rope.py:24-75 with the
+// padded scatter replaced by token-major rows). lora_q / lora_v fp16 or NULL; cos, sin fp32
+// [seq, 128]; pos_idx int64 padded positions (t = pos % seq).
+extern "C" int tb_nf4_gemm_qkv_rope(const uint16_t *x, int64_t tokens, int64_t ld_x,
+                                    const uint8_t *const *packed, const float *const *absmax,
+                                    const float *const *nf4_table, int64_t k_dim,
+                                    const uint16_t *bias, const uint16_t *lora_q,
+                                    const uint16_t *lora_v, const float *cos, const float *sin,
+                                    const int64_t *pos_idx, int64_t seq, int32_t n_heads,
+                                    int32_t n_kv, uint16_t *q, uint16_t *k, uint16_t *v,
+                                    void *stream) {
+  if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv != 0 || seq <= 0)
+    return set_error(TB_EINVAL, "nf4_gemm_qkv_rope: heads %d kv %d seq %lld", n_heads, n_kv,
+                     (long long)seq);
+  const int64_t rows[3] = {(int64_t)n_heads * kBM, (int64_t)n_kv * kBM, (int64_t)n_kv * kBM};
+  GemmArgs a;
+  int rc = gemm_args(0, tokens, 3, packed, absmax, nf4_table, rows, k_dim, a);
+  if (rc != TB_OK) return rc;
+  if (tokens == 0) return TB_OK;
+  if (!x || !cos || !sin || !pos_idx || !q || !k || !v)
+    return set_error(TB_EINVAL, "nf4_gemm_qkv_rope: x, cos, sin, pos_idx, q, k, v required");
+  if (ld_x < k_dim || ld_x % 8 != 0 || !aligned(x, 16))
+    return set_error(TB_EINVAL, "nf4_gemm_qkv_rope: x row stride %lld (>= %lld, 16-byte rows)",
+                     (long long)ld_x, (long long)k_dim);
+  int dev = 0, major = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (major != 10) return set_error(TB_EDEVICE, "nf4_gemm_qkv_rope: needs an sm_100 GPU");
+
+  const int a_tiles = a.a_rows / kBM;  // one head a tile
+  const Plan p = make_plan(tokens, a_tiles, a.red_blocks, a.a_rows, 0, sm_count(), 0);
+  a.bn = p.bn;
+  a.nsub = p.nsub;
+  a.span = p.span;
+  a.splits = p.splits;
+  a.cluster = p.cluster;
+  a.idesc = (1u << 4) | ((uint32_t)(p.bn >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+  a.bias = bias;
+  a.out = nullptr;
+  a.ld_out = 0;
+  a.part = nullptr;
+  a.mode = kQkvRope;
+  a.gu = nullptr;
+  a.ld_gu = 0;
+  a.inter = 0;
+  a.lora_q = lora_q;
+  a.lora_v = lora_v;
+  a.cosv = cos;
+  a.sinv = sin;
+  a.pos_idx = pos_idx;
+  a.seq = (int)seq;
+  a.nh = n_heads;
+  a.nkv = n_kv;
+  a.q_out = q;
+  a.k_out = k;
+  a.v_out = v;
+
+  CUtensorMap map_b;
+  rc = make_map(&map_b, x, tokens, k_dim, ld_x, p.bn);
+  if (rc != TB_OK) return rc;
+  const size_t smem = sizeof(Smem) + 1024;
+  if (cudaFuncSetAttribute(nf4_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return check_launch("nf4_gemm_qkv_rope attribute");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)a_tiles, (unsigned)p.groups, (unsigned)p.splits);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = (unsigned)p.splits;
+  cfg.attrs = attr;
+  cfg.numAttrs = p.cluster ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, nf4_gemm_kernel<false>, map_b, a);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return set_error(TB_ELAUNCH, "nf4_gemm_qkv_rope: launch failed: %s", cudaGetErrorString(e));
+  }
+  return TB_OK;
 }
 
 extern "C" int tb_nf4_gemm_variant(int32_t variant) {

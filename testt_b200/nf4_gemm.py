@@ -186,3 +186,43 @@ def down_swiglu_backward_(dy, down, gu):
     if dy.shape[0]:
         _swiglu_call(True, dy, (down,), gu, None)
     return gu
+
+
+_QKV_SIG = [_lib._P, _lib._I64, _lib._I64, _lib._P, _lib._P, _lib._P, _lib._I64, _lib._P, _lib._P,
+            _lib._P, _lib._P, _lib._P, _lib._P, _lib._I64, _lib._I32, _lib._I32, _lib._P, _lib._P,
+            _lib._P, _lib._P]
+
+
+def qkv_rope(x, qkv_weights, bias, lora_q, lora_v, cos, sin, pos_idx, seq, n_heads, n_kv):
+    """(q, k, v) token-major [T, heads, 128] from x [T, K] and the (q, k, v) NF4 weights: the
+    q|k|v GEMM (+ bias), rounded to fp16, the LoRA rows added and the rotary embedding applied in
+    the GEMM's finishing phase (what rope.rope_tokens computes from the GEMM's output,
+    reference: solution/rope.py:24-75). lora_q / lora_v fp16 or None."""
+    fn = getattr(_lib.load(), "tb_nf4_gemm_qkv_rope", None)
+    if fn is None:
+        raise RuntimeError("nf4_gemm: tb_nf4_gemm_qkv_rope is not in the loaded library (staged)")
+    fn.restype, fn.argtypes = ctypes.c_int, _QKV_SIG
+    _lib.require_cuda(x, bias, lora_q, lora_v, cos, sin, pos_idx, what="qkv_rope")
+    x = x.contiguous()
+    t, dev = x.shape[0], x.device
+    q = torch.empty((t, n_heads, 128), dtype=torch.float16, device=dev)
+    k = torch.empty((t, n_kv, 128), dtype=torch.float16, device=dev)
+    v = torch.empty((t, n_kv, 128), dtype=torch.float16, device=dev)
+    if t == 0:
+        return q, k, v
+    ws = tuple(qkv_weights)
+    conv = lambda a: None if a is None else a.to(torch.float16).contiguous()  # noqa: E731
+    bias, lora_q, lora_v = conv(bias), conv(lora_q), conv(lora_v)
+    cos, sin = cos.to(torch.float32).contiguous(), sin.to(torch.float32).contiguous()
+    pos = pos_idx.to(torch.int64).contiguous()
+    rc = fn(_lib.ptr(x), t, x.stride(0), _lib.ptr_array([_lib.ptr(w.data) for w in ws]),
+            _lib.ptr_array([_lib.ptr(fp32_absmax(w)) for w in ws]),
+            _lib.ptr_array([_lib.ptr(_quant_state(w).code.to(torch.float32).contiguous())
+                            for w in ws]),
+            weight_shape(ws[0])[1], _lib.ptr(bias), _lib.ptr(lora_q), _lib.ptr(lora_v),
+            _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(pos), seq, n_heads, n_kv, _lib.ptr(q),
+            _lib.ptr(k), _lib.ptr(v), _lib.stream_of(x))
+    if rc != 0:
+        msg = _lib.load().tb_last_error().decode(errors="replace")
+        raise _lib.KernelError(f"tb_nf4_gemm_qkv_rope failed ({rc}): {msg}")
+    return q, k, v
