@@ -204,3 +204,35 @@ def test_qkv_rope_epilogue_matches_gemm_then_rope_tokens(tokens, lora):
     assert_rel(q.float().cpu(), rq.float().cpu(), RTOL, "q")
     assert_rel(k.float().cpu(), rk.float().cpu(), RTOL, "k")
     assert_ulp(v.cpu(), rv.cpu(), 1, "v")
+
+
+@requires_kernel
+def test_fused_qkv_rope_node_matches_linear_then_rope_tokens():
+    """fused_layer.qkv_rope (forward and the gradients of x and of both LoRA inputs) against
+    nf4.layer_linear followed by rope.rope_tokens on the same LayerWeights."""
+    from oracle import ops
+    from testt_b200 import fused_layer, nf4, rope
+
+    nh, nkv, hidden, seq, tokens = 4, 2, 512, 512, 300
+    _, ws = _weights((nh * 128, nkv * 128, nkv * 128), hidden, True, seed=40)
+    lw = nf4.LayerWeights((tuple(ws),))
+    bias = _x(1, (nh + 2 * nkv) * 128, seed=41, std=0.1)[0]
+    cos, sin = (t.cuda() for t in ops.rope_tables(seq, 128, 1e6))
+    g = torch.Generator().manual_seed(42)
+    pos = torch.sort(torch.randperm(4 * seq, generator=g)[:tokens]).values.cuda()
+    ins = [_x(tokens, hidden, seed=43), _x(tokens, nh * 128, seed=44, std=0.01),
+           _x(tokens, nkv * 128, seed=45, std=0.01)]
+    a = [t.clone().requires_grad_(True) for t in ins]
+    b = [t.clone().requires_grad_(True) for t in ins]
+    out_a = fused_layer.qkv_rope(a[0], lw, 0, bias, a[1], a[2], cos, sin, pos, 4, seq, nh, nkv)
+    qkv = nf4.layer_linear(b[0], lw, 0, bias, last=True)
+    out_b = rope.rope_tokens(qkv, b[1], b[2], cos, sin, pos, 4, seq, nh, nkv, 128)
+    grads = [_x(*o.shape, seed=46 + i, std=0.01) for i, o in enumerate(out_b)]
+    torch.autograd.backward(out_a, grads)
+    torch.autograd.backward(out_b, grads)
+    lw.release()
+    torch.cuda.synchronize()
+    for x, y, name in zip(out_a, out_b, "qkv"):
+        assert_rel(x.detach().float().cpu(), y.detach().float().cpu(), 2e-3, name)
+    for x, y, name in zip(a, b, ("dx", "dlora_q", "dlora_v")):
+        assert_rel(x.grad.float().cpu(), y.grad.float().cpu(), 2e-3, name)

@@ -96,3 +96,49 @@ def layer_linear(x, lw, group, bias=None):
 
 def layer_mlp(x, lw, g_gu, g_down):
     return FusedLayerMLP.apply(x, lw, g_gu, g_down)
+
+
+class FusedQkvRope(torch.autograd.Function):
+    """(q, k, v) token-major from x: the q|k|v GEMM decoded from NF4 with bias, LoRA rows and
+    the rotary embedding in its finishing phase (nf4_gemm.qkv_rope). The backward is
+    rope.RopeTokens' (tb_rope_tokens_bwd: dqkv, the LoRA gradients as its column views) followed
+    by dX = dqkv . W decoded in the GEMM."""
+
+    @staticmethod
+    def forward(ctx, x, bias, lora_q, lora_v, lw, group, cos, sin, pos_idx, batch, seq, n_heads,
+                n_kv):
+        weights = lw.groups[group]
+        q, k, v = nf4_gemm.qkv_rope(x, weights, bias, lora_q, lora_v, cos, sin, pos_idx, seq,
+                                    n_heads, n_kv)
+        cos = cos.to(torch.float32).contiguous()
+        sin = sin.to(torch.float32).contiguous()
+        ctx.save_for_backward(cos, sin, pos_idx.to(torch.int64))
+        ctx.dims = (x.shape[0], batch, seq, n_heads, n_kv, 128)
+        ctx.weights = weights
+        return q, k, v
+
+    @staticmethod
+    def backward(ctx, grad_q, grad_k, grad_v):
+        from . import _lib
+
+        cos, sin, pos_idx = ctx.saved_tensors
+        rows, batch, seq, n_heads, n_kv, head_dim = ctx.dims
+        need_x, _, need_lq, need_lv = ctx.needs_input_grad[:4]
+        dqkv = torch.empty((rows, (n_heads + 2 * n_kv) * head_dim), dtype=torch.float16,
+                           device=pos_idx.device)
+        grads = [g.to(torch.float16).contiguous() if g is not None else None
+                 for g in (grad_q, grad_k, grad_v)]
+        if rows:
+            _lib.call("tb_rope_tokens_bwd", _lib.ptr(grads[0]), _lib.ptr(grads[1]),
+                      _lib.ptr(grads[2]), _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(pos_idx),
+                      _lib.ptr(dqkv), rows, batch, seq, n_heads, n_kv, head_dim,
+                      _lib.stream_of(dqkv))
+        dx = nf4_gemm.nf4_matmul(dqkv, ctx.weights, transpose=True) if need_x else None
+        q_cols, v_start = n_heads * head_dim, (n_heads + n_kv) * head_dim
+        return (dx, None, dqkv[:, :q_cols] if need_lq else None,
+                dqkv[:, v_start:] if need_lv else None) + (None,) * 9
+
+
+def qkv_rope(x, lw, group, bias, lora_q, lora_v, cos, sin, pos_idx, batch, seq, n_heads, n_kv):
+    return FusedQkvRope.apply(x, bias, lora_q, lora_v, lw, group, cos, sin, pos_idx, batch, seq,
+                              n_heads, n_kv)
