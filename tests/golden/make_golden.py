@@ -122,6 +122,22 @@ def case_swiglu(ref):
         save(f"swiglu_{tag}", gu=gu, act=act, dact=dact, dgu=dgu)
 
 
+def case_swiglu_extreme(ref):
+    """Gate values at the ends of the fp16 range (exp overflows to inf, silu(g) -> -0 or g)
+    and around zero, each paired with up = 1 and with a random up."""
+    mlp = ref["mlp"]
+    g = torch.Generator().manual_seed(0)
+    vals = torch.tensor([-65504.0, -100.0, -20.0, -1.0, 0.0, 1.0, 20.0, 65504.0,
+                         -11.0898, 11.0898, -0.0, 88.0, -88.0, 6e-5, -6e-5, 30000.0])
+    inter = vals.numel()
+    up = torch.stack([torch.ones(inter), torch.randn(inter, generator=g) * 4])
+    gu = torch.cat([vals.expand(2, inter), up], 1).to(torch.float16)
+    act = mlp.gated_silu(gu)
+    dact = (torch.randn(2, inter, generator=g) * 0.1).to(torch.float16)
+    dgu = mlp.gated_silu_backward_(dact, gu.clone())
+    save("swiglu_extreme", gu=gu, act=act, dact=dact, dgu=dgu)
+
+
 def case_rope(ref):
     rope = ref["rope"]
     for tag, (batch, seq, nh, nkv, d), lens, lora_dtype in (
@@ -186,19 +202,22 @@ def case_head(ref):
          token_loss=token_loss, correct=correct, dh=h.grad)
 
 
+CASES = dict(nf4=case_nf4, rmsnorm=case_rmsnorm, swiglu=case_swiglu,
+             swiglu_extreme=case_swiglu_extreme, rope=case_rope, head=case_head)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="checkout of the reference repository")
+    ap.add_argument("--cases", default=",".join(CASES),
+                    help="comma-separated subset of: " + ", ".join(CASES))
     args = ap.parse_args()
     sys.path.insert(0, os.path.abspath(args.reference))
     from solution import head, mlp, nf4, rmsnorm, rope
 
     ref = dict(nf4=nf4, rmsnorm=rmsnorm, mlp=mlp, rope=rope, head=head)
-    case_nf4(ref)
-    case_rmsnorm(ref)
-    case_swiglu(ref)
-    case_rope(ref)
-    case_head(ref)
+    for name in args.cases.split(","):
+        CASES[name](ref)
 
 
 if __name__ == "__main__":

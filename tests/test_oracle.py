@@ -80,7 +80,7 @@ def test_rmsnorm_oracle_matches_reference(tag):
         assert_ulp(ddelta, g["ddelta"], 1, "ddelta")
 
 
-@pytest.mark.parametrize("tag", ["odd", "vec"])
+@pytest.mark.parametrize("tag", ["odd", "vec", "extreme"])
 def test_swiglu_oracle_matches_reference(tag):
     g = golden(f"swiglu_{tag}")
     gu = t(g["gu"])
