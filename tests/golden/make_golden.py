@@ -202,8 +202,39 @@ def case_head(ref):
          token_loss=token_loss, correct=correct, dh=h.grad)
 
 
+def case_head_edge(ref):
+    """Head statistics on rows at the edges: all logits equal (zero, and the fp16 maximum), one
+    maximum against the fp16 minimum everywhere else, the label in the last column, an ignored
+    row, and the maximum tied between the label and an earlier column."""
+    head = ref["head"]
+    g = torch.Generator().manual_seed(2)
+    rows, vocab = 7, 3001
+    logits = (torch.randn(rows, vocab, generator=g) * 3).to(torch.float16)
+    logits[0] = 0.0
+    logits[1] = 65504.0
+    logits[2] = -65504.0
+    logits[2, 1234] = 65504.0
+    targets = torch.randint(0, vocab, (rows,), generator=g)
+    targets[0], targets[1], targets[2] = 17, vocab - 1, 1234
+    targets[3] = -100
+    targets[4] = vocab - 1
+    logits[5, 10] = float(logits[5].float().max()) + 2.0
+    logits[5, 2999] = logits[5, 10]
+    targets[5] = 2999                                          # tied, but not the first argmax
+    grad_scale = 0.25
+    work = logits.clone()
+    entropy = torch.empty(rows)
+    loss = torch.empty(rows)
+    correct = torch.empty(rows, dtype=torch.int32)
+    head.head_stats_grad_kernel[(rows,)](work, targets, entropy, loss, correct, grad_scale,
+                                         V=vocab, BLOCK=head.VOCAB_BLOCK, num_warps=8)
+    save("head_edge", logits=logits, targets=targets, grad_scale=np.array(grad_scale),
+         entropy=entropy, loss=loss, correct=correct, dlogits=work)
+
+
 CASES = dict(nf4=case_nf4, rmsnorm=case_rmsnorm, swiglu=case_swiglu,
-             swiglu_extreme=case_swiglu_extreme, rope=case_rope, head=case_head)
+             swiglu_extreme=case_swiglu_extreme, rope=case_rope, head=case_head,
+             head_edge=case_head_edge)
 
 
 def main():

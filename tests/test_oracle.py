@@ -112,6 +112,28 @@ def test_head_stats_oracle_matches_reference():
     assert g["correct"][5] == 0 and g["correct"][6] == 1
 
 
+def test_head_stats_oracle_at_the_edges_matches_reference():
+    """Rows of equal logits (zero and the fp16 maximum), one maximum against the fp16 minimum,
+    the label in the last column, an ignored row and a tie decided by the first argmax. The
+    oracle is exact (fp64). The reference sums online in fp32, so its log-sum-exp carries the
+    fp32 rounding of its magnitude: 65504 + log(3001) becomes 65512.0078 rather than 65512.0067.
+    Loss and entropy are therefore held to that spacing (|lse| 2^-23), and dlogits to two fp16
+    ulps, the effect of that lse error on p = exp(z - lse). Argmax hits are exact, and the
+    ignored row's logits are left untouched."""
+    g = golden("head_edge")
+    logits = t(g["logits"])
+    ent, loss, correct, dlogits = ops.head_stats_exact(logits, t(g["targets"]),
+                                                       float(g["grad_scale"]))
+    lse = torch.logsumexp(logits.double(), -1)
+    tol = lse.abs() * 2.0 ** -23 + 1e-4 * lse.abs().clamp(min=1.0)
+    assert torch.all((loss - torch.from_numpy(g["loss"]).double()).abs() <= tol)
+    assert torch.all((ent - torch.from_numpy(g["entropy"]).double()).abs() <= tol)
+    assert np.array_equal(correct.numpy().astype(np.int32), g["correct"])
+    assert list(g["correct"]) == [0, 0, 1, 0, 0, 0, 0]  # the tie in row 5 is not a hit
+    assert_ulp(dlogits, g["dlogits"], 2, "dlogits")
+    assert_bitexact(dlogits[3], g["logits"][3], "ignored row untouched")
+
+
 def test_head_loss_oracle_matches_reference():
     g = golden("head_loss")
     loss, ent, tok, correct, dh = ops.fused_head_loss(t(g["h"]), t(g["w"]), t(g["targets"]),
