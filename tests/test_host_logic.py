@@ -120,3 +120,65 @@ def test_head_gradient_unit_is_a_power_of_two_near_64_per_token():
 
     check()
     assert _grad_unit(1024) == 65536.0 and _grad_unit(0) == 1.0
+
+
+def test_head_stats_glue_equals_trl_and_soup_formulas_on_logits():
+    """The statistics glue (reference: solution/model.py:36-51, 270-278;
+    solution/trainer_patch.py:121-151): a HeadStats assembled the way fused_forward assembles it
+    (per real token in row-major order, the target the next position's label) gives TRL's
+    entropy and token accuracy and Soup's per-row losses, as computed from the full logits
+    (TRL 0.29.1 entropy_from_logits and accuracy, soup_cli rewind_hf.row_losses, restated).
+    Only real positions are scored, as in the reference's fused path: in a left-padded row whose
+    first real token carried a label, TRL's shifted formula would also count the padding
+    position before it. The batch masks the first real token of every row, as a prompt-masking
+    collator does."""
+    from oracle import ops
+    from testt_b200.model import HeadStats
+    from testt_b200.trainer_patch import _accuracy_counts, _entropy_metric
+
+    g = torch.Generator().manual_seed(4)
+    batch, seq, vocab = 3, 7, 13
+    logits = torch.randn(batch, seq, vocab, generator=g) * 3
+    logits[1, 2, 5] = logits[1, 2].max() + 1.0
+    mask = torch.tensor([[1] * 7, [1] * 5 + [0] * 2, [0] * 2 + [1] * 5])
+    labels = torch.randint(0, vocab, (batch, seq), generator=g)
+    labels[mask == 0] = -100
+    labels[:, :3] = -100                    # prompts: the first real token of every row is unlabelled
+    labels[1, 3] = 5                        # position 2 predicts its own argmax: a hit
+
+    def entropy_from_logits(z):             # TRL: -sum p log p over the vocabulary
+        logp = torch.log_softmax(z.float(), -1)
+        return -(logp.exp() * logp).sum(-1)
+
+    class Out:
+        pass
+
+    out = Out()
+    out.logits = logits
+    want_ent = _entropy_metric(None, out, mask, entropy_from_logits)
+    want_hits, want_total = _accuracy_counts(None, out, labels)
+    shift, tgt = logits[:, :-1], labels[:, 1:]
+    ce = torch.nn.functional.cross_entropy(shift.transpose(1, 2), tgt, ignore_index=-100,
+                                           reduction="none")
+    n = (tgt != -100).sum(1)
+    want_rows = ([float(v) for v in ce.sum(1) / n.clamp(min=1)], [int(v) for v in n])
+
+    pos = mask.reshape(-1).nonzero().squeeze(1)
+    targets = torch.nn.functional.pad(labels, (0, 1), value=-100)[:, 1:].reshape(-1)[pos]
+    z16 = logits.reshape(-1, vocab)[pos]
+    ent, loss, correct, _ = ops.head_stats_exact(z16, targets, 1.0)
+    row = torch.div(pos, seq, rounding_mode="floor")
+    labelled = targets != -100
+    stats = HeadStats(entropy_sum=ent.sum().float(), correct=correct.sum(),
+                      labelled=labelled.sum(),
+                      row_loss_sum=torch.zeros(batch, dtype=torch.float64).index_add_(0, row, loss),
+                      row_tokens=torch.zeros(batch, dtype=torch.long).index_add_(
+                          0, row, labelled.long()))
+    got_ent = _entropy_metric(stats, None, mask, None)
+    got_hits, got_total = _accuracy_counts(stats, None, labels)
+    assert abs(float(got_ent) - float(want_ent)) < 1e-5 * max(1.0, float(want_ent))
+    assert int(got_hits) == int(want_hits) and int(got_total) == int(want_total)
+    assert int(want_hits) >= 1
+    got_rows = stats.row_losses()
+    assert got_rows[1] == want_rows[1]
+    assert all(abs(a - b) < 1e-5 for a, b in zip(got_rows[0], want_rows[0]))
