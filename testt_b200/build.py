@@ -95,5 +95,22 @@ def compile_staged(out_dir):
     return logs
 
 
+def link_staged(out_dir):
+    """A separate test library of the staged kernels (csrc/next/*.cu with csrc/common.cu) in
+    `out_dir`, for exercising their host-side argument checks and planning without a GPU; never
+    loaded by the package. Returns its path."""
+    compile_staged(out_dir)
+    objs = [os.path.join(out_dir, os.path.basename(p)[:-3] + ".o")
+            for p in sorted(glob.glob(os.path.join(CSRC, "next", "*.cu")))]
+    common = os.path.join(out_dir, "common.o")
+    _compile(os.path.join(CSRC, "common.cu"), common, verbose=False)
+    lib = os.path.join(out_dir, "libtestt_b200_staged.so")
+    cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", lib, common, *objs]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"staged link failed:\n{res.stderr}")
+    return lib
+
+
 if __name__ == "__main__":
     print(build(verbose="-v" in sys.argv, force="-f" in sys.argv))
