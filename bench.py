@@ -704,6 +704,53 @@ def _kernel_case(name, device):
         nbytes = 0
         info = {"config": "5 (one layer's gate|up)", "tokens": tokens,
                 "shape": [2 * inter, hidden], "flops": 2 * tokens * 2 * inter * hidden}
+    elif name in ("mlp_fused_fwd", "mlp_unpack_fwd", "qkv_rope_fused", "qkv_unpack_rope"):
+        # a layer's MLP forward (gate|up, SwiGLU, down) or q|k|v projection + RoPE at 621 tokens:
+        # the staged GEMM with its epilogues against unpack + cuBLAS + the separate kernels
+        from oracle import ops
+        from testt_b200 import nf4_gemm
+
+        tokens, hidden, inter = 621, synth.HIDDEN, synth.INTER
+        g = torch.Generator(device=dev).manual_seed(10)
+
+        def nf4w(rows, cols):
+            w = torch.randn((rows, cols), generator=g, device=dev) * 0.02
+            packed, state = quantize_nf4(w, 64, nested=True)
+            return SimpleNamespace(data=packed, quant_state=state)
+
+        x = torch.randn((tokens, hidden), generator=g, device=dev).half()
+        if name.startswith("mlp"):
+            gate_up, down = (nf4w(inter, hidden), nf4w(inter, hidden)), (nf4w(hidden, inter),)
+            if name == "mlp_fused_fwd":
+                if not nf4_gemm.available():
+                    raise SystemExit(f"{name}: tb_nf4_gemm is not in the library (staged kernel)")
+                fn = lambda: nf4_gemm.nf4_matmul(  # noqa: E731
+                    nf4_gemm.gate_up_swiglu(x, gate_up)[1], down)
+            else:
+                fn = lambda: torch.matmul(  # noqa: E731
+                    mlp.gated_silu(torch.matmul(x, nf4.unpack_concat(gate_up, dev).t())),
+                    nf4.unpack_concat(down, dev).t())
+            flops = 6 * tokens * inter * hidden
+        else:
+            nh, nkv, seq = 12, 2, 512
+            qkv_w = (nf4w(nh * 128, hidden), nf4w(nkv * 128, hidden), nf4w(nkv * 128, hidden))
+            bias = (torch.randn((nh + 2 * nkv) * 128, generator=g, device=dev) * 0.1).half()
+            lq = (torch.randn((tokens, nh * 128), generator=g, device=dev) * 0.01).half()
+            lv = (torch.randn((tokens, nkv * 128), generator=g, device=dev) * 0.01).half()
+            cos, sin = (t.to(dev) for t in ops.rope_tables(seq, 128, synth.ROPE_THETA))
+            pos = synth.positions(synth.lengths(seed=0), seq).to(dev)
+            if name == "qkv_rope_fused":
+                if not nf4_gemm.available():
+                    raise SystemExit(f"{name}: tb_nf4_gemm is not in the library (staged kernel)")
+                fn = lambda: nf4_gemm.qkv_rope(x, qkv_w, bias, lq, lv, cos, sin,  # noqa: E731
+                                               pos, seq, nh, nkv)
+            else:
+                fn = lambda: rope.rope_tokens(  # noqa: E731
+                    torch.nn.functional.linear(x, nf4.unpack_concat(qkv_w, dev), bias), lq, lv,
+                    cos, sin, pos, 4, seq, nh, nkv, 128)
+            flops = 2 * tokens * (nh + 2 * nkv) * 128 * hidden
+        nbytes = 0
+        info = {"config": "5 (one layer)", "tokens": tokens, "flops": flops}
     elif name in ("lora_bwd", "lora_bwd_cublas"):  # both adapters' weight and dh gradients
         tokens, hidden, r = 621, synth.HIDDEN, 16
         g = torch.Generator(device=dev).manual_seed(9)
@@ -1055,7 +1102,8 @@ def main():
                          "lora_fwd, attn_fwd, attn_fwd_bwd, "
                          "head_stats, head_tc, head_full, head_cublas, all; staged kernels, "
                          "with what they replace: gate_up_fused_fwd, gate_up_fused_bwd, "
-                         "gate_up_unpack_fwd, gate_up_unpack_bwd, lora_bwd, lora_bwd_cublas)")
+                         "gate_up_unpack_fwd, gate_up_unpack_bwd, mlp_fused_fwd, mlp_unpack_fwd, "
+                         "qkv_rope_fused, qkv_unpack_rope, lora_bwd, lora_bwd_cublas)")
     args = ap.parse_args()
     if args.kernel:
         names = ["nf4", "nf4_nested", "rmsnorm_fwd", "rmsnorm_bwd", "rope_fwd", "rope_bwd",
