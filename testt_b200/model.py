@@ -34,6 +34,7 @@ import threading
 import torch
 
 from . import attention as _own_attn
+from . import fused_layer as _fused_layer
 from .head import IGNORE_INDEX, fused_head_loss
 from .mlp import layer_mlp
 from .nf4 import LayerWeights, layer_linear
@@ -86,6 +87,12 @@ USE_VARLEN_ATTENTION = True
 # unpacks every weight from NF4 (the forward releases the previous step's copies first).
 # False restores the reference's second unpack.
 KEEP_UNPACKED_WEIGHTS = True
+
+# Layers whose every NF4 operand the NF4-decoding GEMM (tb_nf4_gemm) takes run their projections
+# through it (fused_layer: q|k|v with bias, LoRA rows and RoPE in the GEMM's finishing phase, o,
+# the MLP with SwiGLU in the epilogues) and unpack no weight. The kernel is not in the library
+# yet, so fused_layer.usable() is False and every layer takes the unpacking path.
+USE_NF4_GEMM = True
 
 _ALLOWED_KWARGS = {"num_items_in_batch", "output_attentions", "output_hidden_states",
                    "return_dict"}
@@ -356,6 +363,23 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
                                   layer.input_layernorm.variance_epsilon, pos_idx, padded,
                                   zero_padding=False)
         lw = lp.weights
+        if USE_NF4_GEMM and varlen and plan.head_dim == 128 and _fused_layer.usable(lw):
+            lora_q, lora_v = lora_pair(_lora_parts(lp.attn.q_proj), _lora_parts(lp.attn.v_proj),
+                                       y_pad, pos_idx, slot_tok)
+            del y_pad
+            q, k, v = _fused_layer.qkv_rope(y, lw, 0, lp.qkv_bias, lora_q, lora_v, cos, sin,
+                                            pos_idx, batch, seq, plan.n_heads, plan.n_kv)
+            del lora_q, lora_v
+            attn = _varlen_attn(q, k, v, cu_seqlens, max_len, lp.attn.scaling)
+            del q, k, v
+            o = _fused_layer.layer_linear(attn.reshape(tokens, plan.n_heads * plan.head_dim), lw,
+                                          1, lp.o_bias)
+            del attn
+            s, y2, _ = add_rmsnorm(s, o, layer.post_attention_layernorm.weight,
+                                   layer.post_attention_layernorm.variance_epsilon)
+            delta = _fused_layer.layer_mlp(y2, lw, 2, 3)
+            del y2, o
+            continue
         lw.release()
         lw.operands(dev)  # every NF4 weight of the layer, one unpack launch
         qkv = layer_linear(y, lw, 0, lp.qkv_bias, last=True)
