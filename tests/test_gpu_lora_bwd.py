@@ -98,8 +98,9 @@ def test_one_adapter_and_determinism(present):
 @requires_kernel
 @pytest.mark.parametrize("in_bucket", [False, True])
 def test_lora_pair_with_fused_backward_matches_gemm_backward(monkeypatch, in_bucket):
-    """lora_fused.LoraPairFused (tb_lora_backward, then the dropout backward) against
-    lora.LoraPair (six GEMMs, then the same dropout backward) through lora.lora_pair, with the
+    """lora_fused.LoraPairFused (tb_lora_backward, then the dropout backward), which
+    lora.lora_pair takes when the kernel is loaded, against lora.LoraPair (six GEMMs, then the
+    same dropout backward, lora.USE_FUSED_BACKWARD off) through lora.lora_pair, with the
     same dropout draws: the padded input's gradient and both adapters' weight gradients,
     returned to autograd or accumulated into GradBucket views."""
     from testt_b200 import lora, lora_fused
@@ -114,7 +115,7 @@ def test_lora_pair_with_fused_backward_matches_gemm_backward(monkeypatch, in_buc
     gq = (torch.randn(pos.numel(), hidden, device="cuda") * 0.1).half()
     gv = (torch.randn(pos.numel(), 64, device="cuda") * 0.1).half()
 
-    def run(node):
+    def run(fused):
         g = torch.Generator().manual_seed(3)
         parts = []
         for out, scaling in ((hidden, 2.0), (64, 0.5)):
@@ -127,7 +128,8 @@ def test_lora_pair_with_fused_backward_matches_gemm_backward(monkeypatch, in_buc
         params = [t.weight for _, a, b, _ in parts for t in (a, b)]
         if in_bucket:
             GradBucket(params)
-        monkeypatch.setattr(lora, "LoraPair", node)
+        monkeypatch.setattr(lora, "USE_FUSED_BACKWARD", fused)
+        assert lora._node() is (lora_fused.LoraPairFused if fused else lora.LoraPair)
         torch.manual_seed(11)
         x = x0.clone().requires_grad_(True)
         with torch.autocast("cuda", dtype=torch.float16):
@@ -136,8 +138,8 @@ def test_lora_pair_with_fused_backward_matches_gemm_backward(monkeypatch, in_buc
         torch.cuda.synchronize()
         return x.grad.clone(), [p.grad.clone() for p in params]
 
-    gx_ref, gw_ref = run(lora.LoraPair)
-    gx, gw = run(lora_fused.LoraPairFused)
+    gx_ref, gw_ref = run(False)
+    gx, gw = run(True)
     torch.testing.assert_close(gx, gx_ref, rtol=5e-3, atol=1e-5)
     for got, ref in zip(gw, gw_ref):
         torch.testing.assert_close(got, ref, rtol=5e-3, atol=float(ref.abs().max()) * 2e-3)

@@ -200,6 +200,21 @@ class LoraPair(torch.autograd.Function):
         return (gx, grads[0], grads[1], grads[2], grads[3], None, None, None)
 
 
+# The rank-16 backward in two launches (lora_fused.LoraPairFused, tb_lora_backward) instead of
+# six GEMMs, whenever the library has the kernel. It is not in the library yet, so every call
+# takes LoraPair.
+USE_FUSED_BACKWARD = True
+
+
+def _node():
+    if USE_FUSED_BACKWARD:
+        from . import lora_fused
+
+        if lora_fused.available():
+            return lora_fused.LoraPairFused
+    return LoraPair
+
+
 def lora_pair(parts_q, parts_v, x_pad, pos_idx, slot_tok):
     """(lora_q, lora_v) for peft adapter parts (dropout, lora_A, lora_B, scaling) or None per
     projection; None when neither projection has an adapter."""
@@ -216,4 +231,4 @@ def lora_pair(parts_q, parts_v, x_pad, pos_idx, slot_tok):
         p, on = _dropout_of(dropout)
         cfg.append((p, on, float(scaling)))
         weights += [lora_a.weight, lora_b.weight]
-    return LoraPair.apply(x_pad.contiguous(), *weights, pos_idx, slot_tok, tuple(cfg))
+    return _node().apply(x_pad.contiguous(), *weights, pos_idx, slot_tok, tuple(cfg))
