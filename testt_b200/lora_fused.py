@@ -11,6 +11,7 @@ backward with the rank-16 expansion (tb_lora_dropout_grad_expand).
 """
 
 import ctypes
+import functools
 
 import torch
 
@@ -22,7 +23,9 @@ _SIG = [_lib._P] * 7 + [_lib._I64, _lib._F] + [_lib._P] * 7 + [_lib._I64, _lib._
                                                                    _lib._P]
 
 
+@functools.lru_cache(maxsize=None)
 def _entry():
+    """tb_lora_backward of the loaded library, or None (looked up once)."""
     fn = getattr(_lib.load(), "tb_lora_backward", None)
     if fn is not None:
         fn.restype, fn.argtypes = ctypes.c_int, _SIG

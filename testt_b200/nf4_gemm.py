@@ -12,6 +12,7 @@ therefore False with the shipped library, and no training path calls this module
 """
 
 import ctypes
+import functools
 
 import torch
 
@@ -26,8 +27,10 @@ _SIG = [_lib._I32, _lib._P, _lib._I64, _lib._I64, _lib._I32, _lib._P, _lib._P, _
 _WS_SIG = [_lib._I32, _lib._I64, _lib._I32, _lib._P, _lib._I64]
 
 
+@functools.lru_cache(maxsize=None)
 def _entry():
-    """(tb_nf4_gemm, tb_nf4_gemm_workspace) of the loaded library, or None without them."""
+    """(tb_nf4_gemm, tb_nf4_gemm_workspace) of the loaded library, or None without them (looked
+    up once: the library does not change within a process)."""
     lib = _lib.load()
     fn = getattr(lib, "tb_nf4_gemm", None)
     ws = getattr(lib, "tb_nf4_gemm_workspace", None)
