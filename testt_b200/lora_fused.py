@@ -2,8 +2,8 @@
 of both adapters) instead of six cuBLAS GEMMs (reference: solution/model.py:195-206, peft's
 lora_B(lora_A(dropout(x))) * scaling under fp16 autocast).
 
-Staged with the kernel (csrc/next/lora_bwd.cu): nothing imports this module until
-tb_lora_backward is linked into the library; `available()` is False before that. The forward is
+Staged with the kernel (csrc/next/lora_bwd.cu): lora.lora_pair takes this node when the loaded
+library has tb_lora_backward; it is not linked yet, so `available()` is False. The forward is
 lora.LoraPair's; the backward computes the same quantities as lora.LoraPair.backward:
     dh = fp16(s * g . fp16(B)), dB = s * g^T . h (fp32), dA = dh^T . x16 (fp32),
 each weight gradient added into its GradBucket view when the parameter has one, then the dropout
