@@ -8,7 +8,8 @@ the weight and calls cuBLAS in both directions).
 W is the weights stacked by rows (q|k|v, gate|up), each with bitsandbytes' NF4 layout and
 blocksize 64. The kernel, tb_nf4_gemm, is staged: it is built from csrc/next/nf4_gemm.cu and is
 not linked into libtestt_b200.so until its parity tests have run on a B200. `available()` is
-therefore False with the shipped library, and no training path calls this module yet.
+therefore False with the shipped library, and the training step (model.fused_forward, through
+fused_layer) keeps unpacking the weights.
 """
 
 import ctypes
