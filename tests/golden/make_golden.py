@@ -111,6 +111,32 @@ def case_rmsnorm(ref):
              dx=x.grad, ddelta=None if delta is None else delta.grad)
 
 
+def case_rmsnorm_edge(ref):
+    """Rows at the edges of RMSNorm: all zeros (rstd = 1 / sqrt(eps)), large constant values,
+    tiny alternating values, a residual delta at the fp16 maximum, and an ordinary row."""
+    rmsnorm = ref["rmsnorm"]
+    g = torch.Generator().manual_seed(5)
+    rows, hidden, padded = 5, 256, 8
+    x = torch.randn(rows, hidden, generator=g)
+    x[0] = 0.0
+    x[1] = 1.0e4
+    x[2] = 1.0e-3 * (1 - 2 * (torch.arange(hidden) % 2)).float()
+    delta = torch.randn(rows, hidden, generator=g).to(torch.float16)
+    delta[0] = 0.0
+    delta[3, :8] = 65504.0
+    x = x.requires_grad_(True)
+    delta = delta.requires_grad_(True)
+    w = torch.rand(hidden, generator=g) + 0.5
+    pad_idx = torch.randperm(padded, generator=g)[:rows]
+    s, y, ypad = rmsnorm.add_rmsnorm(x, delta, w, 1e-6, pad_idx, padded)
+    gy = torch.randn(rows, hidden, generator=g).to(torch.float16)
+    gpad = torch.randn(padded, hidden, generator=g)
+    gs = torch.randn(rows, hidden, generator=g)
+    torch.autograd.backward([y, ypad, s], [gy, gpad, gs])
+    save("rmsnorm_edge", x=x, delta=delta, w=w, pad_idx=pad_idx, padded_rows=np.array(padded),
+         s=s, y=y, ypad=ypad, gy=gy, gpad=gpad, gs=gs, dx=x.grad, ddelta=delta.grad)
+
+
 def case_swiglu(ref):
     mlp = ref["mlp"]
     for tag, (rows, inter) in (("odd", (5, 1500)), ("vec", (4, 1536))):
@@ -234,7 +260,7 @@ def case_head_edge(ref):
 
 CASES = dict(nf4=case_nf4, rmsnorm=case_rmsnorm, swiglu=case_swiglu,
              swiglu_extreme=case_swiglu_extreme, rope=case_rope, head=case_head,
-             head_edge=case_head_edge)
+             head_edge=case_head_edge, rmsnorm_edge=case_rmsnorm_edge)
 
 
 def main():

@@ -59,7 +59,7 @@ def test_nf4_table_is_normalfloat():
     assert np.all(np.diff(tab) > 0)
 
 
-@pytest.mark.parametrize("tag", ["dp", "d", "p", "wide"])
+@pytest.mark.parametrize("tag", ["dp", "d", "p", "wide", "edge"])
 def test_rmsnorm_oracle_matches_reference(tag):
     g = golden(f"rmsnorm_{tag}")
     x, w = t(g["x"]), t(g["w"])
