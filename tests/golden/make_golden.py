@@ -188,6 +188,27 @@ def case_rope(ref):
              dqkv=qkv.grad)
 
 
+def case_rope_partial(ref):
+    """RoPE pack with no LoRA on q (LoRA on v only), positions in no particular order, and a
+    backward in which k receives no gradient (the reference passes it as None)."""
+    rope = ref["rope"]
+    batch, seq, nh, nkv, d = 3, 6, 4, 2, 16
+    g = torch.Generator().manual_seed(6)
+    pos_idx = torch.tensor([13, 0, 5, 7, 1, 16, 2, 12])
+    rows = pos_idx.numel()
+    qkv = torch.randn(rows, (nh + 2 * nkv) * d, generator=g).to(torch.float16).requires_grad_(True)
+    lv = torch.randn(rows, nkv * d, generator=g).to(torch.float16).requires_grad_(True)
+    inv = 1.0 / (10000 ** (torch.arange(0, d, 2).float() / d))
+    freqs = torch.arange(seq).float()[:, None] * inv[None]
+    emb = torch.cat([freqs, freqs], -1)
+    cos, sin = emb.cos(), emb.sin()
+    q, k, v = rope.rope_pack(qkv, None, lv, cos, sin, pos_idx, batch, seq, nh, nkv, d)
+    gq, gv = [torch.randn(t.shape, generator=g).to(torch.float16) for t in (q, v)]
+    torch.autograd.backward([q, v], [gq, gv])
+    save("rope_partial", qkv=qkv, lv=lv, cos=cos, sin=sin, pos_idx=pos_idx,
+         dims=np.array((batch, seq, nh, nkv, d)), q=q, k=k, v=v, gq=gq, gv=gv, dqkv=qkv.grad)
+
+
 def case_head(ref):
     head = ref["head"]
     g = torch.Generator().manual_seed(0)
@@ -260,7 +281,8 @@ def case_head_edge(ref):
 
 CASES = dict(nf4=case_nf4, rmsnorm=case_rmsnorm, swiglu=case_swiglu,
              swiglu_extreme=case_swiglu_extreme, rope=case_rope, head=case_head,
-             head_edge=case_head_edge, rmsnorm_edge=case_rmsnorm_edge)
+             head_edge=case_head_edge, rmsnorm_edge=case_rmsnorm_edge,
+             rope_partial=case_rope_partial)
 
 
 def main():
