@@ -18,7 +18,7 @@
 // through its own double-buffered shared memory (cp.async, zero-filled past the last row) and
 // reads them with ldmatrix (.trans where the reduction runs along the rows of both operands);
 // the warps' partial sums are added in warp order, so every result is deterministic.
-#include "../common.cuh"
+#include "common.cuh"
 
 namespace tb {
 namespace {

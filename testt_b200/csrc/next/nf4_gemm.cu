@@ -46,7 +46,7 @@
 
 #include <cstddef>
 
-#include "../common.cuh"
+#include "common.cuh"
 
 namespace tb {
 namespace {
