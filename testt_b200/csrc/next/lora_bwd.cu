@@ -313,8 +313,9 @@ extern "C" int tb_lora_backward(const uint16_t *g_q, const uint16_t *h_q, const 
     if (widths[j] <= 0 || widths[j] % kCols != 0 || widths[j] > (1LL << 20))
       return set_error(TB_EINVAL, "lora_backward: adapter %d width %lld (a multiple of %d)", j,
                        (long long)widths[j], kCols);
+    // g, h, B16, x16 and dh (kernel 2 reads it back) go through 16-byte cp.async copies
     if (!aligned(gs[j], 16) || !aligned(hs[j], 16) || !aligned(bs[j], 16) || !aligned(xs[j], 16) ||
-        !aligned(dhs[j], 4) || !aligned(dbs[j], 4) || !aligned(das[j], 4))
+        !aligned(dhs[j], 16) || !aligned(dbs[j], 4) || !aligned(das[j], 4))
       return set_error(TB_EALIGN, "lora_backward: adapter %d has a misaligned buffer", j);
     ad.g = gs[j];
     ad.h = hs[j];
