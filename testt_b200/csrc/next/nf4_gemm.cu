@@ -652,7 +652,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       float o1 = x1, o2 = x2;  // v: LoRA-added, not rotated
       if (hr < args.nh + args.nkv) {
-        const int64_t t = __ldg(args.pos_idx + tok) % args.seq;
+        const int64_t pos = __ldg(args.pos_idx + tok);
+        if (pos < 0) continue;  // no position: nothing written (as tb_rope_tokens_fwd)
+        const int64_t t = pos % args.seq;
         const float c1 = __ldg(args.cosv + t * D + pr), c2 = __ldg(args.cosv + t * D + H + pr);
         const float n1 = __ldg(args.sinv + t * D + pr), n2 = __ldg(args.sinv + t * D + H + pr);
         o1 = x1 * c1 - x2 * n1;
