@@ -107,3 +107,37 @@ def test_staged_entry_points_reject_bad_arguments_before_any_cuda_call(staged):
     assert b"rank 8" in staged.tb_last_error()
     assert lb(*bufs, 100, 2.0, *([None] * 7), 0, 1.0, 10, 128, 16, 0, None) == TB_EINVAL
     assert lb(*bufs, 128, 2.0, *([None] * 7), 0, 1.0, 10, 100, 16, 0, None) == TB_EINVAL
+
+
+def _c_signatures(path):
+    """{name: parameter count} of the extern "C" functions defined in a .cu file."""
+    text = re.sub(r"//[^\n]*", "", open(path).read())
+    out = {}
+    for m in re.finditer(r'extern "C" [\w\s\*]+?\b(tb_\w+)\s*\(([^)]*)\)\s*\{', text):
+        params = m.group(2).strip()
+        out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_staged_python_bindings_match_the_c_signatures():
+    """The ctypes argument lists of the staged wrappers (nf4_gemm, lora_fused, the tests and the
+    bench that bind the entry points themselves) have as many entries as the C functions have
+    parameters: a mismatch would only show on the first call on a GPU."""
+    import os
+
+    from testt_b200 import lora_fused, nf4_gemm
+
+    csrc = os.path.join(os.path.dirname(build.__file__), "csrc", "next")
+    sigs = {}
+    for name in ("nf4_gemm.cu", "lora_bwd.cu"):
+        sigs.update(_c_signatures(os.path.join(csrc, name)))
+    assert set(sigs) == {"tb_nf4_gemm", "tb_nf4_gemm_workspace", "tb_nf4_gemm_swiglu",
+                         "tb_nf4_gemm_qkv_rope", "tb_nf4_gemm_variant", "tb_lora_backward"}
+    assert len(nf4_gemm._SIG) == sigs["tb_nf4_gemm"]
+    assert len(nf4_gemm._WS_SIG) == sigs["tb_nf4_gemm_workspace"]
+    assert len(nf4_gemm._SWIGLU_SIG) == sigs["tb_nf4_gemm_swiglu"]
+    assert len(nf4_gemm._QKV_SIG) == sigs["tb_nf4_gemm_qkv_rope"]
+    assert len(lora_fused._SIG) == sigs["tb_lora_backward"]
+    import test_gpu_lora_bwd
+
+    assert len(test_gpu_lora_bwd._SIG) == sigs["tb_lora_backward"]
