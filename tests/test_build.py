@@ -110,19 +110,27 @@ def test_staged_entry_points_reject_bad_arguments_before_any_cuda_call(staged):
 
 
 def _c_signatures(path):
-    """{name: parameter count} of the extern "C" functions defined in a .cu file."""
+    """{name: [ctypes type of each parameter]} of the extern "C" functions defined in a .cu file
+    (pointers -> c_void_p, int32_t / int64_t / float -> their ctypes)."""
     text = re.sub(r"//[^\n]*", "", open(path).read())
+    kinds = {"int32_t": ctypes.c_int32, "int64_t": ctypes.c_int64, "float": ctypes.c_float}
     out = {}
     for m in re.finditer(r'extern "C" [\w\s\*]+?\b(tb_\w+)\s*\(([^)]*)\)\s*\{', text):
-        params = m.group(2).strip()
-        out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+        params = [p.strip() for p in m.group(2).split(",") if p.strip() not in ("", "void")]
+        types = []
+        for p in params:
+            if "*" in p:
+                types.append(ctypes.c_void_p)
+            else:
+                types.append(kinds[p.split()[-2]])
+        out[m.group(1)] = types
     return out
 
 
 def test_staged_python_bindings_match_the_c_signatures():
-    """The ctypes argument lists of the staged wrappers (nf4_gemm, lora_fused, the tests and the
-    bench that bind the entry points themselves) have as many entries as the C functions have
-    parameters: a mismatch would only show on the first call on a GPU."""
+    """The ctypes argument lists of the staged wrappers (nf4_gemm, lora_fused, and the test that
+    binds the entry point itself) match the C parameter lists type for type: a mismatch would
+    only show on the first call on a GPU."""
     import os
 
     from testt_b200 import lora_fused, nf4_gemm
@@ -133,11 +141,12 @@ def test_staged_python_bindings_match_the_c_signatures():
         sigs.update(_c_signatures(os.path.join(csrc, name)))
     assert set(sigs) == {"tb_nf4_gemm", "tb_nf4_gemm_workspace", "tb_nf4_gemm_swiglu",
                          "tb_nf4_gemm_qkv_rope", "tb_nf4_gemm_variant", "tb_lora_backward"}
-    assert len(nf4_gemm._SIG) == sigs["tb_nf4_gemm"]
-    assert len(nf4_gemm._WS_SIG) == sigs["tb_nf4_gemm_workspace"]
-    assert len(nf4_gemm._SWIGLU_SIG) == sigs["tb_nf4_gemm_swiglu"]
-    assert len(nf4_gemm._QKV_SIG) == sigs["tb_nf4_gemm_qkv_rope"]
-    assert len(lora_fused._SIG) == sigs["tb_lora_backward"]
     import test_gpu_lora_bwd
 
-    assert len(test_gpu_lora_bwd._SIG) == sigs["tb_lora_backward"]
+    for name, bound in (("tb_nf4_gemm", nf4_gemm._SIG),
+                        ("tb_nf4_gemm_workspace", nf4_gemm._WS_SIG),
+                        ("tb_nf4_gemm_swiglu", nf4_gemm._SWIGLU_SIG),
+                        ("tb_nf4_gemm_qkv_rope", nf4_gemm._QKV_SIG),
+                        ("tb_lora_backward", lora_fused._SIG),
+                        ("tb_lora_backward", test_gpu_lora_bwd._SIG)):
+        assert list(bound) == sigs[name], name
