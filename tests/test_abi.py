@@ -48,6 +48,25 @@ def test_binding_signatures_match_header():
     assert not unbound, f"declared but not bound in Python: {sorted(unbound)}"
 
 
+def test_binding_types_match_header():
+    """Type for type: every pointer bound as c_void_p, int32_t / int64_t / float as their
+    ctypes (a swapped 32/64-bit size would only show as garbage on a GPU call)."""
+    import ctypes
+
+    from testt_b200 import _lib
+
+    kinds = {"int32_t": ctypes.c_int32, "int64_t": ctypes.c_int64, "float": ctypes.c_float}
+    for path in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", open(path).read(), flags=re.S)
+        for m in re.finditer(r"\b(tb_\w+)\s*\(([^)]*)\)\s*;", text):
+            name = m.group(1)
+            if name not in _lib.SIGNATURES:
+                continue
+            params = [p.strip() for p in m.group(2).split(",") if p.strip() not in ("", "void")]
+            want = [ctypes.c_void_p if "*" in p else kinds[p.split()[-2]] for p in params]
+            assert list(_lib.SIGNATURES[name]) == want, name
+
+
 def test_version_and_error_text_work_without_gpu():
     from testt_b200 import _lib
 
