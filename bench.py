@@ -155,6 +155,94 @@ class Clocks:
                 "reasons": reasons, "samples": len(sm), "samples_in_region": n_inside}
 
 
+# ---- synthetic workloads ------------------------------------------------------------------------
+# Seeded inputs with the shapes and distributions of the BASELINE configurations. The GPU arm
+# draws them here, not from the oracle package: the oracle is only the checker (and the timed CPU
+# baseline). tests/test_host_logic.py checks that these are the same draws as oracle.synth's,
+# which the parity tests use.
+
+class _Workloads:
+    HIDDEN, INTER, N_HEADS, N_KV, HEAD_DIM, VOCAB, LAYERS = 1536, 8960, 12, 2, 128, 151936, 28
+    BATCH, SEQ = 4, 512
+    ROPE_THETA = 1.0e6
+
+    @staticmethod
+    def _gen(device, seed):
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        return g
+
+    def randn(self, shape, std, dtype, device, seed, mean=0.0):
+        g = self._gen(device, seed)
+        return (torch.randn(shape, generator=g, device=device, dtype=torch.float32) * std
+                + mean).to(dtype)
+
+    def lengths(self, batch=4, seq=512, seed=0):
+        """Sequence lengths ~ lognormal(median 140, sigma 0.5) clipped to [16, seq]."""
+        import math
+
+        import numpy as np
+
+        raw = np.random.default_rng(seed).lognormal(mean=math.log(140), sigma=0.5, size=batch)
+        return [int(v) for v in np.clip(np.round(raw), 16, seq)]
+
+    @staticmethod
+    def positions(lens, seq=512):
+        return torch.cat([b * seq + torch.arange(n, dtype=torch.int64)
+                          for b, n in enumerate(lens)])
+
+    def config1_weight(self, device="cpu", seed=0):
+        return self.randn((self.INTER, self.HIDDEN), 0.02, torch.float16, device, seed)
+
+    def config2(self, device="cpu", seed=0, rows=2048, hidden=1536):
+        r = self.randn
+        d = dict(x=r((rows, hidden), 1.0, torch.float32, device, seed),
+                 delta=r((rows, hidden), 0.5, torch.float16, device, seed + 1),
+                 weight=r((hidden,), 0.1, torch.float32, device, seed + 2, mean=1.0), eps=1e-6,
+                 dy=r((rows, hidden), 1e-2, torch.float16, device, seed + 4),
+                 dypad=r((rows, hidden), 1e-3, torch.float32, device, seed + 5),
+                 ds=r((rows, hidden), 1e-2, torch.float32, device, seed + 6), padded_rows=rows)
+        d["pad_idx"] = torch.randperm(rows, generator=self._gen("cpu", seed + 3)).to(device)
+        return d
+
+    def config3(self, device="cpu", seed=0, batch=4, seq=512):
+        lens = self.lengths(batch, seq, seed)
+        pos = self.positions(lens, seq).to(device)
+        m = pos.numel()
+        nh, nkv, d, r = self.N_HEADS, self.N_KV, self.HEAD_DIM, self.randn
+        cos, sin = self._rope(seq, device)
+        f16, f32 = torch.float16, torch.float32
+        return dict(lengths=lens, pos_idx=pos, rows=m, batch=batch, seq=seq, cos=cos, sin=sin,
+                    qkv=r((m, (nh + 2 * nkv) * d), 1.0, f16, device, seed + 10),
+                    lora_q=r((m, nh * d), 1e-2, f32, device, seed + 11),
+                    lora_v=r((m, nkv * d), 1e-2, f32, device, seed + 12),
+                    dq=r((batch, nh, seq, d), 1.0, f16, device, seed + 13),
+                    dk=r((batch, nkv, seq, d), 1.0, f16, device, seed + 14),
+                    dv=r((batch, nkv, seq, d), 1.0, f16, device, seed + 15),
+                    gu=r((m, 2 * self.INTER), 1.0, f16, device, seed + 16),
+                    dact=r((m, self.INTER), 1e-2, f16, device, seed + 17))
+
+    def _rope(self, seq, device):
+        d = self.HEAD_DIM
+        inv = 1.0 / (self.ROPE_THETA ** (torch.arange(0, d, 2, dtype=torch.int64).float() / d))
+        freqs = torch.arange(seq).float()[:, None] * inv[None]
+        emb = torch.cat([freqs, freqs], -1)
+        return emb.cos().to(device), emb.sin().to(device)
+
+    def config4(self, device="cpu", seed=0, rows=2048, vocab=151936, hidden=1536,
+                masked_frac=0.35):
+        w = self.randn((vocab, hidden), 0.02, torch.float16, device, seed + 20)
+        h = self.randn((rows, hidden), 1.0, torch.float16, device, seed + 21)
+        g = self._gen("cpu", seed + 22)
+        labels = torch.randint(0, vocab, (rows,), generator=g, dtype=torch.int64)
+        n_masked = int(round(masked_frac * rows))
+        labels[torch.randperm(rows, generator=g)[:n_masked]] = -100
+        return dict(weight=w, hidden=h, targets=labels.to(device), n_labelled=rows - n_masked)
+
+
+synth = _Workloads()
+
+
 # ---- the QLoRA step (value, e2e) -------------------------------------------------------------
 
 def make_batch(lengths, seq, vocab, seed, device):
@@ -231,7 +319,6 @@ class HotPath:
     grouped by kernel so each group can be captured and replayed on its own."""
 
     def __init__(self, model, lengths, seq, device):
-        from oracle import synth
         from testt_b200 import _lib, nf4
         from testt_b200.model import USE_VARLEN_ATTENTION as varlen
         from testt_b200.model import model_plan
@@ -471,7 +558,6 @@ def time_graph(graph, reps, world, device, flush=None):
 # ---- the head (config 4) ---------------------------------------------------------------------
 
 def head_bench(device, reps, world):
-    from oracle import synth
     from testt_b200.head import fused_head_loss
 
     c = synth.config4(device)
@@ -505,7 +591,6 @@ def sharded_head_bench(device, reps, world, rank):
     rank's tensor-core logits + statistics over its shard, one all-gather of the folded
     per-row states, dlogits and dh on its shard, one all-reduce of dh): device time per call,
     max over ranks. Every rank holds the same hidden rows and targets (same seed)."""
-    from oracle import synth
     from testt_b200.dist import ShardedHead, shard_range
 
     c = synth.config4(device)
@@ -533,7 +618,6 @@ def sharded_head_bench(device, reps, world, rank):
 def _kernel_case(name, device):
     """(launch closure, algorithmic bytes, info) of one kernel at its configuration, on buffers
     of its own (nbytes 0 for the tensor-core kernels, whose info holds their FLOPs)."""
-    from oracle import synth
     from testt_b200 import _lib, head, mlp, nf4, rmsnorm, rope
     from testt_b200.qlora import quantize_nf4
 
@@ -707,7 +791,6 @@ def _kernel_case(name, device):
     elif name in ("mlp_fused_fwd", "mlp_unpack_fwd", "qkv_rope_fused", "qkv_unpack_rope"):
         # a layer's MLP forward (gate|up, SwiGLU, down) or q|k|v projection + RoPE at 621 tokens:
         # the staged GEMM with its epilogues against unpack + cuBLAS + the separate kernels
-        from oracle import ops
         from testt_b200 import nf4_gemm
 
         tokens, hidden, inter = 621, synth.HIDDEN, synth.INTER
@@ -737,7 +820,7 @@ def _kernel_case(name, device):
             bias = (torch.randn((nh + 2 * nkv) * 128, generator=g, device=dev) * 0.1).half()
             lq = (torch.randn((tokens, nh * 128), generator=g, device=dev) * 0.01).half()
             lv = (torch.randn((tokens, nkv * 128), generator=g, device=dev) * 0.01).half()
-            cos, sin = (t.to(dev) for t in ops.rope_tables(seq, 128, synth.ROPE_THETA))
+            cos, sin = synth._rope(seq, dev)
             pos = synth.positions(synth.lengths(seed=0), seq).to(dev)
             if name == "qkv_rope_fused":
                 if not nf4_gemm.available():
@@ -912,7 +995,6 @@ def reference_arm(args, rank, world):
 
 
 def ours_arm(args, rank, world, local):
-    from oracle import synth
     from testt_b200 import _lib, trainer_patch
     from testt_b200.qlora import build_qlora_model, qwen2_config
 

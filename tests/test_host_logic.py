@@ -182,3 +182,35 @@ def test_head_stats_glue_equals_trl_and_soup_formulas_on_logits():
     got_rows = stats.row_losses()
     assert got_rows[1] == want_rows[1]
     assert all(abs(a - b) < 1e-5 for a, b in zip(got_rows[0], want_rows[0]))
+
+
+def test_bench_workloads_are_the_oracle_workloads():
+    """bench.py draws its inputs itself (its GPU arm does not import the oracle); they are the
+    same seeded draws as oracle.synth's, which the parity tests use: lengths, positions, the
+    rotary tables and every configuration's tensors (small row counts, CPU)."""
+    import bench
+    from oracle import synth
+
+    b = bench.synth
+    for name in ("HIDDEN", "INTER", "N_HEADS", "N_KV", "HEAD_DIM", "VOCAB", "LAYERS", "BATCH",
+                 "SEQ", "ROPE_THETA"):
+        assert getattr(b, name) == getattr(synth, name), name
+    for seed in (0, 1, 7):
+        assert b.lengths(seed=seed) == synth.lengths(seed=seed)
+    lens = synth.lengths(seed=0)
+    assert torch.equal(b.positions(lens), synth.positions(lens))
+    for x, y in zip(b._rope(512, "cpu"), synth._rope(512, "cpu")):
+        assert torch.equal(x, y)
+    assert torch.equal(b.config1_weight(), synth.config1_weight())
+
+    def same(d1, d2):
+        assert d1.keys() == d2.keys()
+        for k in d1:
+            if torch.is_tensor(d1[k]):
+                assert torch.equal(d1[k], d2[k]), k
+            else:
+                assert d1[k] == d2[k], k
+
+    same(b.config2(rows=64), synth.config2(rows=64))
+    same(b.config3(), synth.config3())
+    same(b.config4(rows=32, vocab=1000), synth.config4(rows=32, vocab=1000))
