@@ -316,15 +316,35 @@ def test_nf4_gemm_host_absmax_and_oracle(nested):
     assert torch.equal(ops.nf4_matmul(dy, qs, transpose=True), (dy.double() @ w.double()).half())
 
 
-def test_cpu_step_sample_runs_at_small_shapes():
-    """The timed CPU baseline (oracle.step) end to end at small dimensions: one decoder layer
-    forward and backward with its NF4 weights unpacked by the C oracle, and the head sample."""
+def test_cpu_step_runs_in_full_at_small_shapes():
+    """The timed CPU baseline (oracle.step) end to end at small dimensions: every layer forward
+    and backward (NF4 weights unpacked by the C oracle), the chunked head on every row; the LoRA
+    factors of every layer get gradients, the step is deterministic for a fixed dropout seed,
+    and the head's loss is the fp64 oracle's on the same hidden rows."""
     import math
 
     from oracle import step
 
-    layer = step.CpuLayerSample([5, 9], hidden=128, inter=256, heads=4, kv=2, head_dim=32, seq=16)
-    assert layer.rows == 14
-    assert math.isfinite(layer.run()) and layer.run() > 0
-    head = step.CpuHeadSample(rows=8, vocab=300, hidden=128)
-    assert math.isfinite(head.run())
+    model = step.CpuModel(layers=2, hidden=128, inter=256, heads=4, kv=2, head_dim=32,
+                          vocab=300, seq=16)
+    st = step.CpuStep([5, 9], model=model)
+    assert st.rows == 14
+    torch.manual_seed(3)
+    loss = st.run()
+    grads = [p.grad.clone() for lp in model.lora for ab in lp.values() for p in ab]
+    assert math.isfinite(loss) and loss > 0
+    assert len(grads) == 8 and all(torch.isfinite(g).all() and g.abs().sum() > 0 for g in grads)
+    torch.manual_seed(3)
+    assert st.run() == loss
+    assert all(torch.equal(g, p.grad) for g, p in
+               zip(grads, [p for lp in model.lora for ab in lp.values() for p in ab]))
+    # the head alone against the fp64 statistics of the same fp16 logits
+    g = torch.Generator().manual_seed(0)
+    h16 = torch.randn(300, 128, generator=g).half().float()
+    tg = torch.randint(0, 300, (300,), generator=g)
+    tg[::3] = -100
+    denom = int((tg != -100).sum())
+    got, dh = model._head(h16, tg, denom)
+    _, rloss, _, _ = ops.head_stats_exact((h16 @ model.table32.t()).half(), tg, 1.0)
+    assert abs(got - float(rloss.sum()) / denom) <= 1e-4 * abs(got)
+    assert dh.shape == (300, 128) and bool((dh[tg == -100] == 0).all())
