@@ -20,7 +20,7 @@ Printed on rank 0, one JSON line:
   roofline   the dominant hot-path kernel (NF4 unpack): algorithmic bytes / measured time
   head       the vocabulary head of config 4 (2048 rows, 1331 labelled): TFLOP/s
   head_sharded  (N > 1) config 4 with the head weight vocabulary-sharded over the N GPUs
-  cpu_baseline  the same step on the host cores (oracle.step sample), rank 0 at N = 1
+  cpu_baseline  the same step on the host cores (oracle.step, full steps), rank 0 at N = 1
 The reference arm (--impl reference) times that CPU step alone.
 """
 
@@ -968,17 +968,15 @@ def kernel_bench(name, steps, warmup, device):
 # ---- arms ------------------------------------------------------------------------------------
 
 def reference_arm(args, rank, world):
-    """The reference path on the host cores: the CPU QLoRA step sample (oracle.step)."""
+    """The reference path on the host cores: the full CPU QLoRA step (oracle.step), W untimed
+    and K timed steps, each a complete step of the config-5 batch."""
     if rank != 0:
         return
     from oracle import step, synth
 
     lengths = synth.lengths(seed=0)
     cpu = step.CpuStep(lengths, threads=os.cpu_count())
-    for _ in range(args.warmup):
-        cpu.seconds()
-    secs = [cpu.seconds() for _ in range(args.steps)]
-    s = sum(secs) / len(secs)
+    s = cpu.seconds(repeats=args.steps, warmup=args.warmup)
     sample, thr, rows = cpu.sample, torch.get_num_threads(), cpu.rows
     value = rows / s
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
@@ -986,7 +984,8 @@ def reference_arm(args, rank, world):
             "ms_per_step": s * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "QLoRA step, Qwen2.5-1.5B shape, batch 4/GPU, NF4 dq, "
-                                   "LoRA r16 q/v (CPU sample)", "tokens_per_gpu": rows},
+                                   "LoRA r16 q/v (full step on the host cores)",
+                       "tokens_per_gpu": rows},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": thr, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -1110,10 +1109,11 @@ def ours_arm(args, rank, world, local):
     if rank == 0 and world == 1 and not args.no_cpu:
         from oracle import step as cstep
 
-        s, sample, thr, rows = cstep.cpu_step_seconds(lengths, repeats=1,
+        # the reference arm's measurement (full steps, one untimed first), fewer steps
+        s, sample, thr, rows = cstep.cpu_step_seconds(lengths, repeats=2, warmup=1,
                                                       threads=os.cpu_count())
         cpu = {"value": rows / s, "unit": "tokens/s", "cores": thr, "kind": "port",
-               "sample": sample}
+               "sample": sample + " (1 untimed + 2 timed steps)"}
 
     # graphs that hold NCCL calls are released before the process group goes away
     hp_launches = hp.launches()
