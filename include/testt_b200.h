@@ -37,6 +37,14 @@ int tb_version(void);
  * reference (its Triton kernels do not wait on barriers). */
 int tb_wait_timeouts(int32_t device, uint32_t *count);
 
+/* Self-test of the bounded wait behind tb_wait_timeouts: one thread waits on phase 0 of an
+ * mbarrier in its own shared memory (expecting one arrival) for at most `polls` polls, after
+ * arriving on it itself when `arrive` is nonzero. *status (device int32) = 0 when the phase
+ * completed, 1 when the wait gave up, which also adds 1 to tb_wait_timeouts. Shows that a wait
+ * that runs out returns an error status and leaves the context usable. No counterpart in the
+ * reference (its Triton kernels wait on no barriers). */
+int tb_wait_selftest(int32_t polls, int32_t arrive, int32_t *status, void *stream);
+
 /* ---------------------------------------------------------------------------------------------
  * NF4 unpack (bitsandbytes 4-bit layout). Replaces nf4_unpack_kernel and its launch in
  * unpack_into, solution/nf4.py:27-45 and :72-89.
@@ -68,6 +76,74 @@ int tb_nf4_unpack_multi(int32_t n_weights, const uint8_t *const *packed,
                         const float *const *offset, const float *const *nf4_table,
                         uint16_t *const *out, const int64_t *n_bytes, const int32_t *qblock,
                         const int32_t *qblock2, void *stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * NF4-weight GEMMs on the tensor cores (tcgen05, TMEM accumulator, TMA token tiles) with the NF4
+ * decode in the operand producer: the fp16 copy of the frozen weight is never written. Replaces
+ * FrozenNF4Linear (unpack + cuBLAS in both directions, solution/nf4.py:108-127) and the unpack +
+ * GEMMs of FusedNF4MLP (solution/mlp.py:80-113).
+ *
+ * W is 1..TB_NF4_GEMM_MAX_WEIGHTS weights stacked by rows (q|k|v, gate|up), each in
+ * bitsandbytes' packing (row-major [rows[j], k_dim], blocksize 64, high nibble first) with fp32
+ * absmax per block (a nested state's absmax expanded by the caller:
+ * fp32(code2[c] * absmax2[b / 256]) + offset, each operation rounded on its own). Every decoded
+ * value is fp16(table[q] * absmax), bit-identical to tb_nf4_unpack_*; the products differ from
+ * cuBLAS over the unpacked weight only in the order of the fp32 sums.
+ *   transpose 0: out[t, n] = fp16(sum_k in[t, k] W[n, k] (+ bias[n]))   in [tokens, k_dim]
+ *                rows[j] multiples of 128, k_dim of 64
+ *   transpose 1: out[t, k] = fp16(sum_n in[t, n] W[n, k])               in [tokens, sum rows]
+ *                rows[j] multiples of 64, k_dim of 128, no bias
+ * Arrays packed / absmax / nf4_table / rows are HOST arrays of length n_weights. Row strides
+ * ld_in / ld_out in elements, multiples of 8; in, out, bias 16-byte aligned. When the reduction
+ * is split over several CTAs it is summed within a thread-block cluster (no workspace), unless
+ * tb_nf4_gemm_variant(1) asked for fp32 partials in `workspace`, whose size
+ * tb_nf4_gemm_workspace gives (0: none needed). sm_100 only.
+ * ------------------------------------------------------------------------------------------- */
+#define TB_NF4_GEMM_MAX_WEIGHTS 4
+int tb_nf4_gemm(int32_t transpose, const uint16_t *tokens_in, int64_t tokens, int64_t ld_in,
+                int32_t n_weights, const uint8_t *const *packed, const float *const *absmax,
+                const float *const *nf4_table, const int64_t *rows, int64_t k_dim,
+                const uint16_t *bias, uint16_t *out, int64_t ld_out, float *workspace,
+                int64_t workspace_bytes, void *stream);
+
+/* Bytes of fp32 workspace tb_nf4_gemm needs for these shapes under the current variant (0 when
+ * the reduction is not split or is summed within a cluster). No counterpart in the reference. */
+int64_t tb_nf4_gemm_workspace(int32_t transpose, int64_t tokens, int32_t n_weights,
+                              const int64_t *rows, int64_t k_dim);
+
+/* How tb_nf4_gemm sums a split reduction, process-wide: 0 automatic (within a thread-block
+ * cluster of the splits), 1 fp32 partials in the caller's workspace + a summing kernel, 2 the
+ * cluster always. Same results either way. No counterpart in the reference. */
+int tb_nf4_gemm_variant(int32_t variant);
+
+/* The MLP's NF4 GEMMs with SwiGLU in the epilogue (solution/mlp.py:31-58 applied to the GEMM's
+ * fp16 output, solution/mlp.py:82-113):
+ *   backward 0: weights (gate, up), each [inter, k_dim]; tokens_in = x [tokens, k_dim]; writes
+ *               gu = fp16(x [gate|up]^T) [tokens, 2 inter] (row stride ld_gu) and
+ *               act = fp16(silu(g) u) [tokens, inter] (row stride ld_act)
+ *   backward 1: weight (down,) [hidden, inter] (k_dim = inter); tokens_in = dy [tokens, hidden];
+ *               dact = fp16(dy . W_down) stays in the epilogue, which overwrites gu in place
+ *               with d(gate|up) (act unused, may be NULL). */
+int tb_nf4_gemm_swiglu(int32_t backward, const uint16_t *tokens_in, int64_t tokens, int64_t ld_in,
+                       int32_t n_weights, const uint8_t *const *packed,
+                       const float *const *absmax, const float *const *nf4_table,
+                       const int64_t *rows, int64_t k_dim, uint16_t *gu, int64_t ld_gu,
+                       uint16_t *act, int64_t ld_act, void *stream);
+
+/* The q|k|v projection with its bias, the LoRA rows and the rotary embedding in the GEMM's
+ * finishing phase: weights (q, k, v) = [n_heads * 128, k_dim], [n_kv * 128, k_dim] twice (HOST
+ * arrays of 3); x fp16 [tokens, k_dim] (row stride ld_x); bias fp16 [(n_heads + 2 n_kv) * 128]
+ * or NULL; lora_q fp16 [tokens, n_heads * 128], lora_v fp16 [tokens, n_kv * 128] or NULL; cos,
+ * sin fp32 [seq, 128]; pos_idx int64 [tokens] padded positions (t = pos % seq; a negative
+ * position writes nothing). Writes token-major q [tokens, n_heads, 128], k, v
+ * [tokens, n_kv, 128]: what tb_rope_tokens_fwd writes from the GEMM's fp16 output
+ * (solution/rope.py:24-75 with the padded scatter replaced by token-major rows). */
+int tb_nf4_gemm_qkv_rope(const uint16_t *x, int64_t tokens, int64_t ld_x,
+                         const uint8_t *const *packed, const float *const *absmax,
+                         const float *const *nf4_table, int64_t k_dim, const uint16_t *bias,
+                         const uint16_t *lora_q, const uint16_t *lora_v, const float *cos,
+                         const float *sin, const int64_t *pos_idx, int64_t seq, int32_t n_heads,
+                         int32_t n_kv, uint16_t *q, uint16_t *k, uint16_t *v, void *stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Residual add + RMSNorm. Replaces rmsnorm_fwd_kernel / rmsnorm_bwd_kernel and their launches,
@@ -194,6 +270,23 @@ int tb_lora_dropout_grad_expand(const uint16_t *dh_q, const uint16_t *a16_q, con
                                 int64_t slots, int64_t hidden, int32_t rank, float scale_q,
                                 float scale_v, void *stream);
 
+/* The rank-16 LoRA backward of both adapters (q, then v; an adapter whose g is NULL is skipped)
+ * in two launches, in place of the six cuBLAS GEMMs of peft's lora_B(lora_A(x)) * scaling
+ * backward under fp16 autocast (solution/model.py:195-206). Per adapter: g fp16 [rows, width]
+ * (the output gradient), h fp16 [rows, 16] (lora_A's output), b16 = fp16(lora_B) [width, 16],
+ * x16 fp16 [rows, hidden] (lora_A's input):
+ *   dh = fp16(scale * g . b16)    [rows, 16] fp16
+ *   db = scale * g^T . h          [width, 16] fp32 (added into db when its accumulate bit is set)
+ *   da = dh^T . x16               [16, hidden] fp32 (added into da when its accumulate bit is set)
+ * accumulate: bit 0 db_q, bit 1 da_q, bit 2 db_v, bit 3 da_v. rank must be 16; width and hidden
+ * multiples of 64; g, h, b16, x16, dh 16-byte aligned. Sums in a fixed order (deterministic). */
+int tb_lora_backward(const uint16_t *g_q, const uint16_t *h_q, const uint16_t *b16_q,
+                     const uint16_t *x16_q, uint16_t *dh_q, float *db_q, float *da_q,
+                     int64_t width_q, float scale_q, const uint16_t *g_v, const uint16_t *h_v,
+                     const uint16_t *b16_v, const uint16_t *x16_v, uint16_t *dh_v, float *db_v,
+                     float *da_v, int64_t width_v, float scale_v, int64_t rows, int64_t hidden,
+                     int32_t rank, int32_t accumulate, void *stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Causal attention over packed variable-length sequences with grouped key/value heads. Replaces
  * the decoder layer's SDPA over the padded layout (solution/model.py:242-247) for the real rows:
@@ -309,9 +402,11 @@ int tb_head_gemm_variant(int32_t variant);
  * solution/head.py:34-76, needs no scratch). The scratch it uses (partial states of the split
  * form, 1,179,648 bytes) is a fixed array inside the library: each GPU that loads the library
  * holds it until the process exits. At most 32768 rows per call (larger calls are rejected with
- * TB_EINVAL). The first call on a device looks up the array's device address (once per
- * device), so make that first call before any stream capture. Calls share the array: calls
- * whose kernels overlap on the GPU (different streams, no ordering) race and must not be made. */
+ * TB_EINVAL). Outside stream capture each call looks up the array's device address; during
+ * capture the address an earlier call on that device took is used, so make the first call on
+ * a device before any stream capture (a first call inside capture is rejected). Calls share the
+ * array: calls whose kernels overlap on the GPU (different streams, no ordering) race and must
+ * not be made. */
 int tb_head_stats_grad_noalloc(uint16_t *logits, const int64_t *targets, float *entropy,
                                float *loss, int32_t *correct, int64_t rows, int64_t vocab,
                                int64_t ld, float grad_scale, void *stream);

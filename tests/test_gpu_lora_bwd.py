@@ -1,9 +1,7 @@
 """The rank-16 LoRA backward in two launches (tb_lora_backward: dh, dB, dA of both adapters)
 against fp32 products of the same fp16 operands, with and without in-place accumulation, one
-adapter absent, deterministic. The kernels are staged (not linked into the library yet): these
-tests skip while the loaded library does not export the entry point."""
+adapter absent, deterministic."""
 
-import ctypes
 
 import pytest
 import torch
@@ -12,24 +10,12 @@ from helpers import assert_rel
 
 pytestmark = pytest.mark.gpu
 
-_P, _I64, _I32, _F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float
-_SIG = [_P, _P, _P, _P, _P, _P, _P, _I64, _F, _P, _P, _P, _P, _P, _P, _P, _I64, _F, _I64, _I64,
-        _I32, _I32, _P]
 
 
 def _entry():
-    if not torch.cuda.is_available():
-        return None
     from testt_b200 import _lib
 
-    fn = getattr(_lib.load(), "tb_lora_backward", None)
-    if fn is not None:
-        fn.restype, fn.argtypes = ctypes.c_int, _SIG
-    return fn
-
-
-requires_kernel = pytest.mark.skipif(_entry() is None,
-                                     reason="tb_lora_backward is not in the loaded library (staged)")
+    return _lib.load().tb_lora_backward
 
 
 def _adapter(rows, width, hidden, scale, seed):
@@ -43,11 +29,19 @@ def _adapter(rows, width, hidden, scale, seed):
 
 
 def _reference(ad, acc_db, acc_da):
+    """fp32 products of the same fp16 operands: dh, dB, and a function giving dA from the
+    kernel's own dh (an fp16 dh may differ from this dh by one ulp where the fp32 sum lands
+    near a rounding boundary; dA is held to the product of the dh it was given)."""
     s = ad["scale"]
     dh = (s * (ad["g"].float() @ ad["b16"].float())).half()
     db = s * (ad["g"].float().t() @ ad["h"].float())
-    da = dh.float().t() @ ad["x16"].float()
-    return dh, db + ad["db"] if acc_db else db, da + ad["da"] if acc_da else da
+    old_da = ad["da"].clone()
+
+    def da(dh_used):
+        prod = dh_used.float().t() @ ad["x16"].float()
+        return prod + old_da if acc_da else prod
+
+    return dh, db + ad["db"] if acc_db else db, da
 
 
 def _run(q, v, rows, hidden, accumulate):
@@ -65,7 +59,6 @@ def _run(q, v, rows, hidden, accumulate):
     torch.cuda.synchronize()
 
 
-@requires_kernel
 @pytest.mark.parametrize("rows", [1, 37, 621])
 @pytest.mark.parametrize("accumulate", [0, 0b1111])
 def test_both_adapters_match_fp32_products(rows, accumulate):
@@ -76,10 +69,9 @@ def test_both_adapters_match_fp32_products(rows, accumulate):
     for ad, (dh, db, da), name in zip((q, v), refs, "qv"):
         assert_rel(ad["dh"].float().cpu(), dh.float().cpu(), 1e-3, f"dh {name}")
         assert_rel(ad["db"].cpu(), db.cpu(), 1e-4, f"dB {name}")
-        assert_rel(ad["da"].cpu(), da.cpu(), 1e-4, f"dA {name}")
+        assert_rel(ad["da"].cpu(), da(ad["dh"]).cpu(), 1e-4, f"dA {name}")
 
 
-@requires_kernel
 @pytest.mark.parametrize("present", ["q", "v"])
 def test_one_adapter_and_determinism(present):
     ad = _adapter(300, 1536 if present == "q" else 256, 1536, 2.0, seed=3)
@@ -92,10 +84,9 @@ def test_one_adapter_and_determinism(present):
         assert torch.equal(a, b)
     assert_rel(ad["dh"].float().cpu(), dh.float().cpu(), 1e-3, "dh")
     assert_rel(ad["db"].cpu(), db.cpu(), 1e-4, "dB")
-    assert_rel(ad["da"].cpu(), da.cpu(), 1e-4, "dA")
+    assert_rel(ad["da"].cpu(), da(ad["dh"]).cpu(), 1e-4, "dA")
 
 
-@requires_kernel
 @pytest.mark.parametrize("in_bucket", [False, True])
 def test_lora_pair_with_fused_backward_matches_gemm_backward(monkeypatch, in_bucket):
     """lora_fused.LoraPairFused (tb_lora_backward, then the dropout backward), which

@@ -20,7 +20,8 @@ _I64 = ctypes.c_int64
 _I32 = ctypes.c_int32
 _F = ctypes.c_float
 
-# name -> argument types; every function returns int (0 or a negative TB_E* code).
+# name -> argument types; every function returns int (0 or a negative TB_E* code) unless
+# RESTYPES says otherwise.
 SIGNATURES = {
     "tb_nf4_unpack_nested": [_P, _P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _P],
     "tb_nf4_unpack_plain": [_P, _P, _P, _P, _I64, _I32, _P],
@@ -50,10 +51,23 @@ SIGNATURES = {
     "tb_head_fold": [_P, _P, _I64, _I32, _I64, _I32, _P, _P, _P],
     "tb_head_dlogits": [_P, _P, _P, _I64, _I64, _I64, _I64, _F, _P],
     "tb_wait_timeouts": [_I32, _P],
+    "tb_wait_selftest": [_I32, _I32, _P, _P],
     "tb_head_stats_grad_noalloc": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P],
     "tb_head_logits_stats": [_P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _P],
     "tb_head_gemm_variant": [_I32],
+    "tb_nf4_gemm": [_I32, _P, _I64, _I64, _I32, _P, _P, _P, _P, _I64, _P, _P, _I64, _P, _I64, _P],
+    "tb_nf4_gemm_workspace": [_I32, _I64, _I32, _P, _I64],
+    "tb_nf4_gemm_variant": [_I32],
+    "tb_nf4_gemm_swiglu": [_I32, _P, _I64, _I64, _I32, _P, _P, _P, _P, _I64, _P, _I64, _P, _I64,
+                           _P],
+    "tb_nf4_gemm_qkv_rope": [_P, _I64, _I64, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _P, _I64, _I32,
+                             _I32, _P, _P, _P, _P],
+    "tb_lora_backward": [_P, _P, _P, _P, _P, _P, _P, _I64, _F, _P, _P, _P, _P, _P, _P, _P, _I64,
+                         _F, _I64, _I64, _I32, _I32, _P],
 }
+
+# return types other than int (0 or a negative TB_E* code)
+RESTYPES = {"tb_nf4_gemm_workspace": ctypes.c_int64}
 
 _lib = None
 _calls = 0
@@ -79,7 +93,7 @@ def load():
     lib.tb_version.argtypes = []
     for name, args in SIGNATURES.items():
         fn = getattr(lib, name)
-        fn.restype = ctypes.c_int
+        fn.restype = RESTYPES.get(name, ctypes.c_int)
         fn.argtypes = args
     _lib = lib
     return lib

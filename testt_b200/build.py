@@ -84,32 +84,14 @@ def build(verbose=False, force=False):
     return LIB_PATH
 
 
-def compile_staged(out_dir):
-    """Compile every `csrc/next/*.cu` (kernels not linked into the library until their parity
-    tests have run on a B200) to objects in `out_dir` with the library's flags; returns
-    {file name: ptxas log}."""
+def ptxas_logs(names, out_dir):
+    """Compiles the named `csrc/*.cu` files to objects in `out_dir` with the library's flags and
+    ptxas' resource report; returns {file name: ptxas log} (registers, spills, shared memory)."""
     logs = {}
-    for src in sorted(glob.glob(os.path.join(CSRC, "next", "*.cu"))):
-        obj = os.path.join(out_dir, os.path.basename(src)[:-3] + ".o")
-        logs[os.path.basename(src)] = _compile(src, obj, verbose=True)
+    for name in names:
+        obj = os.path.join(out_dir, name[:-3] + ".o")
+        logs[name] = _compile(os.path.join(CSRC, name), obj, verbose=True)
     return logs
-
-
-def link_staged(out_dir):
-    """A separate test library of the staged kernels (csrc/next/*.cu with csrc/common.cu) in
-    `out_dir`, for exercising their host-side argument checks and planning without a GPU; never
-    loaded by the package. Returns its path."""
-    compile_staged(out_dir)
-    objs = [os.path.join(out_dir, os.path.basename(p)[:-3] + ".o")
-            for p in sorted(glob.glob(os.path.join(CSRC, "next", "*.cu")))]
-    common = os.path.join(out_dir, "common.o")
-    _compile(os.path.join(CSRC, "common.cu"), common, verbose=False)
-    lib = os.path.join(out_dir, "libtestt_b200_staged.so")
-    cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", lib, common, *objs]
-    res = subprocess.run(cmd, capture_output=True, text=True)
-    if res.returncode != 0:
-        raise RuntimeError(f"staged link failed:\n{res.stderr}")
-    return lib
 
 
 if __name__ == "__main__":

@@ -10,9 +10,6 @@
 // "(+ ...)" when the gradient is accumulated in place (a gradient bucket's view), as the GEMMs
 // with beta 1 do. The lora_A input gradient dh . fp16(A) stays in tb_lora_dropout_grad_expand.
 //
-// This file is not linked into libtestt_b200.so: it is compiled on its own
-// (tests/test_build.py) and joins the library once its parity tests have run on a B200.
-//
 // Every product is mma.sync m16n8k16 (fp16 operands, fp32 accumulation). The eight warps of a
 // CTA take alternate 16-wide chunks of the reduction; each warp stages its chunks' operands
 // through its own double-buffered shared memory (cp.async, zero-filled past the last row) and

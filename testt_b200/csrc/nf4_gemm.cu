@@ -6,9 +6,6 @@
 //   backward  out[t, k] = fp16(sum_n dy[t, n] W[n, k])              FrozenNF4Linear.backward,
 //                                                                 solution/nf4.py:121-127
 //
-// This file is not linked into libtestt_b200.so: it is compiled on its own (tests/test_build.py)
-// and joins the library once its parity tests have run on a B200.
-//
 // W is up to four NF4 weights stacked by rows (q|k|v, gate|up), each in bitsandbytes' packing
 // (row-major, blocksize 64, element 2i in the high nibble of byte i) with fp32 absmax per block.
 // A nested state's absmax is expanded once by the caller (code2[c] * absmax2[b / 256] + offset,
@@ -428,7 +425,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       mma_commit(&sm.acc_full);
       mma_commit(&sm.mma_done);
-      mbar_wait(&sm.mma_done, 0);  // no MMA in flight before TMEM is released
+      // no MMA in flight before TMEM is released; a wait that gives up is recorded (the MMAs
+      // depend on nothing that could stall them, so this only guards against the impossible)
+      if (!mbar_wait(&sm.mma_done, 0)) sm.error = 1;
     }
   } else {
     // ---- decoders, then the epilogue --------------------------------------------------------

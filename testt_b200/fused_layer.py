@@ -3,9 +3,9 @@
 every operand of a layer is supported, so the step unpacks no weight at all
 (reference: solution/nf4.py:108-127 FrozenNF4Linear, solution/mlp.py:80-113 FusedNF4MLP).
 
-Staged with the kernel: model.fused_forward takes these nodes for a layer when `usable(lw)`
-holds, which needs tb_nf4_gemm in the loaded library; it is not linked yet, so every layer
-takes the unpacking nodes.
+model.fused_forward takes these nodes for a layer when `usable(lw)` holds (tb_nf4_gemm in the
+loaded library and every operand group of the layer in a shape it takes); other layers take the
+unpacking nodes.
 
 Same operations and roundings as the unpacking path: each GEMM takes fp16 operands, sums in fp32
 and rounds once to fp16 (the bias added before that rounding, as cuBLAS's bias epilogue does),

@@ -2,15 +2,14 @@
 of both adapters) instead of six cuBLAS GEMMs (reference: solution/model.py:195-206, peft's
 lora_B(lora_A(dropout(x))) * scaling under fp16 autocast).
 
-Staged with the kernel (csrc/next/lora_bwd.cu): lora.lora_pair takes this node when the loaded
-library has tb_lora_backward; it is not linked yet, so `available()` is False. The forward is
-lora.LoraPair's; the backward computes the same quantities as lora.LoraPair.backward:
+The kernel is csrc/lora_bwd.cu; lora.lora_pair takes this node when the loaded library has
+tb_lora_backward (lora.USE_FUSED_BACKWARD). The forward is lora.LoraPair's; the backward
+computes the same quantities as lora.LoraPair.backward:
     dh = fp16(s * g . fp16(B)), dB = s * g^T . h (fp32), dA = dh^T . x16 (fp32),
 each weight gradient added into its GradBucket view when the parameter has one, then the dropout
 backward with the rank-16 expansion (tb_lora_dropout_grad_expand).
 """
 
-import ctypes
 import functools
 
 import torch
@@ -18,18 +17,12 @@ import torch
 from . import _lib
 from .lora import _F16, _RANK, LoraPair, _in_bucket
 
-_SIG = [_lib._P] * 7 + [_lib._I64, _lib._F] + [_lib._P] * 7 + [_lib._I64, _lib._F, _lib._I64,
-                                                                   _lib._I64, _lib._I32, _lib._I32,
-                                                                   _lib._P]
-
 
 @functools.lru_cache(maxsize=None)
 def _entry():
-    """tb_lora_backward of the loaded library, or None (looked up once)."""
-    fn = getattr(_lib.load(), "tb_lora_backward", None)
-    if fn is not None:
-        fn.restype, fn.argtypes = ctypes.c_int, _SIG
-    return fn
+    """tb_lora_backward of the loaded library, or None (looked up once; a library built from
+    other sources, TESTT_B200_LIB, may lack it)."""
+    return getattr(_lib.load(), "tb_lora_backward", None)
 
 
 def available():
@@ -54,7 +47,10 @@ class LoraPairFused(LoraPair):
         need = ctx.needs_input_grad
         pa_q, pb_q, pa_v, pb_v = ctx.params
         rows = pos_idx.numel()
-        args, grads, dhs, a16s, accumulate = [], [], [], [], 0
+        # `keep` holds every tensor whose pointer goes into `args` until the launch: a
+        # contiguous copy made for one adapter must not be freed (and its memory handed to the
+        # next adapter's outputs) before the kernel has read it
+        args, keep, grads, dhs, a16s, accumulate = [], [], [], [], [], 0
         with torch.autocast("cuda", enabled=False):
             for j, ((g_out, x16, h, a16, b16, s), (pa, pb)) in enumerate(
                     zip(adapters, ((pa_q, pb_q), (pa_v, pb_v)))):
@@ -82,12 +78,15 @@ class LoraPairFused(LoraPair):
                 else:
                     da = out_a = torch.empty((_RANK, ctx.hidden), dtype=torch.float32,
                                              device=x16.device)
-                args += [_lib.ptr(g_out), _lib.ptr(h), _lib.ptr(b16.contiguous()),
-                         _lib.ptr(x16), _lib.ptr(dh), _lib.ptr(out_b), _lib.ptr(out_a), width, s]
+                b16 = b16.contiguous()
+                keep += [g_out, h, b16, x16, dh, out_b, out_a]
+                args += [_lib.ptr(g_out), _lib.ptr(h), _lib.ptr(b16), _lib.ptr(x16), _lib.ptr(dh),
+                         _lib.ptr(out_b), _lib.ptr(out_a), width, s]
                 grads += [da, db]
                 dhs.append(dh)
                 a16s.append(a16.contiguous())
             rc = fn(*args, rows, ctx.hidden, _RANK, accumulate, _lib.stream_of(pos_idx))
+            del keep
             if rc != 0:
                 msg = _lib.load().tb_last_error().decode(errors="replace")
                 raise _lib.KernelError(f"tb_lora_backward failed ({rc}): {msg}")

@@ -6,10 +6,9 @@ the weight and calls cuBLAS in both directions).
     nf4_matmul(dy, weights, transpose=True)       fp16 [T, K] = dy [T, N] . W
 
 W is the weights stacked by rows (q|k|v, gate|up), each with bitsandbytes' NF4 layout and
-blocksize 64. The kernel, tb_nf4_gemm, is staged: it is built from csrc/next/nf4_gemm.cu and is
-not linked into libtestt_b200.so until its parity tests have run on a B200. `available()` is
-therefore False with the shipped library, and the training step (model.fused_forward, through
-fused_layer) keeps unpacking the weights.
+blocksize 64. The kernels are tb_nf4_gemm, tb_nf4_gemm_swiglu and tb_nf4_gemm_qkv_rope
+(csrc/nf4_gemm.cu); the training step (model.fused_forward, through fused_layer) runs a layer's
+projections through them whenever they take its weights.
 """
 
 import ctypes
@@ -23,22 +22,16 @@ from .nf4 import _quant_state, supports_fast_unpack, weight_shape
 MAX_WEIGHTS = 4
 BLOCKSIZE = 64
 
-_SIG = [_lib._I32, _lib._P, _lib._I64, _lib._I64, _lib._I32, _lib._P, _lib._P, _lib._P, _lib._P,
-        _lib._I64, _lib._P, _lib._P, _lib._I64, _lib._P, _lib._I64, _lib._P]
-_WS_SIG = [_lib._I32, _lib._I64, _lib._I32, _lib._P, _lib._I64]
-
-
 @functools.lru_cache(maxsize=None)
 def _entry():
     """(tb_nf4_gemm, tb_nf4_gemm_workspace) of the loaded library, or None without them (looked
-    up once: the library does not change within a process)."""
+    up once: the library does not change within a process; a library built from other sources,
+    TESTT_B200_LIB, may lack them)."""
     lib = _lib.load()
     fn = getattr(lib, "tb_nf4_gemm", None)
     ws = getattr(lib, "tb_nf4_gemm_workspace", None)
     if fn is None or ws is None:
         return None
-    fn.restype, fn.argtypes = ctypes.c_int, _SIG
-    ws.restype, ws.argtypes = ctypes.c_int64, _WS_SIG
     return fn, ws
 
 
@@ -49,11 +42,7 @@ def available():
 def set_variant(variant):
     """How a split reduction is summed, process-wide: 0 automatic (within a thread-block cluster
     of the splits), 1 fp32 partials in a workspace + a summing kernel, 2 cluster always."""
-    fn = getattr(_lib.load(), "tb_nf4_gemm_variant", None)
-    if fn is None:
-        raise RuntimeError("nf4_gemm: tb_nf4_gemm_variant is not in the loaded library")
-    fn.restype, fn.argtypes = ctypes.c_int, [_lib._I32]
-    if fn(int(variant)) != 0:
+    if _lib.load().tb_nf4_gemm_variant(int(variant)) != 0:
         raise ValueError(_lib.load().tb_last_error().decode(errors="replace"))
 
 
@@ -101,7 +90,7 @@ def nf4_matmul(x, weights, bias=None, transpose=False):
     W = the weights stacked by rows [N, K]."""
     entry = _entry()
     if entry is None:
-        raise RuntimeError("nf4_matmul: tb_nf4_gemm is not in the loaded library (staged kernel)")
+        raise RuntimeError("nf4_matmul: tb_nf4_gemm is not in the loaded library")
     fn, ws_fn = entry
     _lib.require_cuda(x, bias, what="nf4_matmul")
     weights = tuple(weights)
@@ -142,23 +131,17 @@ def nf4_matmul(x, weights, bias=None, transpose=False):
     return out
 
 
-_SWIGLU_SIG = [_lib._I32, _lib._P, _lib._I64, _lib._I64, _lib._I32, _lib._P, _lib._P, _lib._P,
-               _lib._P, _lib._I64, _lib._P, _lib._I64, _lib._P, _lib._I64, _lib._P]
-
-
 def _swiglu_call(backward, x, weights, gu, act):
-    fn = getattr(_lib.load(), "tb_nf4_gemm_swiglu", None)
-    if fn is None:
-        raise RuntimeError("nf4_gemm: tb_nf4_gemm_swiglu is not in the loaded library (staged)")
-    fn.restype, fn.argtypes = ctypes.c_int, _SWIGLU_SIG
+    fn = _lib.load().tb_nf4_gemm_swiglu
     rows = [weight_shape(w)[0] for w in weights]
     cols = weight_shape(weights[0])[1]
     n = len(weights)
+    absmax = [fp32_absmax(w) for w in weights]  # held until the launch is queued
+    tables = [_quant_state(w).code.to(torch.float32).contiguous() for w in weights]
     rc = fn(int(backward), _lib.ptr(x), x.shape[0], x.stride(0), n,
             _lib.ptr_array([_lib.ptr(w.data) for w in weights]),
-            _lib.ptr_array([_lib.ptr(fp32_absmax(w)) for w in weights]),
-            _lib.ptr_array([_lib.ptr(_quant_state(w).code.to(torch.float32).contiguous())
-                            for w in weights]),
+            _lib.ptr_array([_lib.ptr(a) for a in absmax]),
+            _lib.ptr_array([_lib.ptr(t) for t in tables]),
             (ctypes.c_int64 * n)(*rows), cols, _lib.ptr(gu), gu.stride(0), _lib.ptr(act),
             act.stride(0) if act is not None else 0, _lib.stream_of(x))
     if rc != 0:
@@ -192,20 +175,12 @@ def down_swiglu_backward_(dy, down, gu):
     return gu
 
 
-_QKV_SIG = [_lib._P, _lib._I64, _lib._I64, _lib._P, _lib._P, _lib._P, _lib._I64, _lib._P, _lib._P,
-            _lib._P, _lib._P, _lib._P, _lib._P, _lib._I64, _lib._I32, _lib._I32, _lib._P, _lib._P,
-            _lib._P, _lib._P]
-
-
 def qkv_rope(x, qkv_weights, bias, lora_q, lora_v, cos, sin, pos_idx, seq, n_heads, n_kv):
     """(q, k, v) token-major [T, heads, 128] from x [T, K] and the (q, k, v) NF4 weights: the
     q|k|v GEMM (+ bias), rounded to fp16, the LoRA rows added and the rotary embedding applied in
     the GEMM's finishing phase (what rope.rope_tokens computes from the GEMM's output,
     reference: solution/rope.py:24-75). lora_q / lora_v fp16 or None."""
-    fn = getattr(_lib.load(), "tb_nf4_gemm_qkv_rope", None)
-    if fn is None:
-        raise RuntimeError("nf4_gemm: tb_nf4_gemm_qkv_rope is not in the loaded library (staged)")
-    fn.restype, fn.argtypes = ctypes.c_int, _QKV_SIG
+    fn = _lib.load().tb_nf4_gemm_qkv_rope
     _lib.require_cuda(x, bias, lora_q, lora_v, cos, sin, pos_idx, what="qkv_rope")
     x = x.contiguous()
     t, dev = x.shape[0], x.device
@@ -219,10 +194,11 @@ def qkv_rope(x, qkv_weights, bias, lora_q, lora_v, cos, sin, pos_idx, seq, n_hea
     bias, lora_q, lora_v = conv(bias), conv(lora_q), conv(lora_v)
     cos, sin = cos.to(torch.float32).contiguous(), sin.to(torch.float32).contiguous()
     pos = pos_idx.to(torch.int64).contiguous()
+    absmax = [fp32_absmax(w) for w in ws]  # held until the launch is queued
+    tables = [_quant_state(w).code.to(torch.float32).contiguous() for w in ws]
     rc = fn(_lib.ptr(x), t, x.stride(0), _lib.ptr_array([_lib.ptr(w.data) for w in ws]),
-            _lib.ptr_array([_lib.ptr(fp32_absmax(w)) for w in ws]),
-            _lib.ptr_array([_lib.ptr(_quant_state(w).code.to(torch.float32).contiguous())
-                            for w in ws]),
+            _lib.ptr_array([_lib.ptr(a) for a in absmax]),
+            _lib.ptr_array([_lib.ptr(tb) for tb in tables]),
             weight_shape(ws[0])[1], _lib.ptr(bias), _lib.ptr(lora_q), _lib.ptr(lora_v),
             _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(pos), seq, n_heads, n_kv, _lib.ptr(q),
             _lib.ptr(k), _lib.ptr(v), _lib.stream_of(x))
