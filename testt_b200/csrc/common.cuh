@@ -186,10 +186,11 @@ __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// true once the phase with the given parity has completed; false after kWaitLimit polls
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+// true once the phase with the given parity has completed; false after `limit` polls
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
+                                          uint32_t limit = kWaitLimit) {
   const uint32_t addr = smem_u32(bar);
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+  for (uint32_t i = 0; i < limit; ++i) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
