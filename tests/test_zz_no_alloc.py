@@ -2,9 +2,9 @@
 scratch is a fixed array inside the library), for callers that cannot allocate device memory:
 a plain C binding from another runtime that only receives buffers, or a process whose
 framework allocator already holds the device's memory. It must give what tb_head_stats_grad
-gives on the same logits, call after call (the shared scratch keeps the previous call's
-contents), within the head's tolerances: loss and entropy rtol 1e-4, first-argmax hits exact,
-dlogits within 1 fp16 ulp. This file is collected last on purpose."""
+gives on the same logits, and what the fp64 oracle gives, call after call (the shared scratch
+keeps the previous call's contents), within the head's tolerances: loss and entropy rtol 1e-4,
+first-argmax hits exact, dlogits within 1 fp16 ulp. This file is collected last on purpose."""
 
 import numpy as np
 import pytest
@@ -39,6 +39,13 @@ def _run(name, logits, targets, scale):
     return ent, loss, cor, work
 
 
+def _check(got, ref, floor=0.0):
+    assert_rel(got[1], ref[1], 1e-4, "loss", floor=floor)
+    assert_rel(got[0], ref[0], 1e-4, "entropy", floor=floor)
+    assert np.array_equal(got[2].cpu().numpy().astype(bool), ref[2].cpu().numpy().astype(bool))
+    assert_ulp(got[3], ref[3], 1, "dlogits")
+
+
 def test_noalloc_head_stats_matches_allocating_entry_point_twice():
     # two calls in a row with different shapes: the second reuses (and must overwrite) the
     # scratch the first left behind
@@ -47,11 +54,25 @@ def test_noalloc_head_stats_matches_allocating_entry_point_twice():
         scale = 64.0 / 300.0
         ref = _run("tb_head_stats_grad", logits, targets, scale)
         got = _run("tb_head_stats_grad_noalloc", logits, targets, scale)
-        assert_rel(got[1], ref[1], 1e-4, "loss", floor=0.0)
-        assert_rel(got[0], ref[0], 1e-4, "entropy", floor=0.0)
-        assert np.array_equal(got[2].cpu().numpy(), ref[2].cpu().numpy())
+        _check(got, ref)
         assert int(got[2][0]) == 1
-        assert_ulp(got[3], ref[3], 1, "dlogits")
+
+
+def test_noalloc_head_stats_matches_the_oracle_at_its_limits():
+    """Against the fp64 oracle (oracle.ops.head_stats_exact): the scratch's largest call (32768
+    rows, one column range each), then a small call split over many column ranges (more
+    (row, range) states than rows, in the scratch the large call filled)."""
+    from oracle import ops
+
+    for rows, vocab, seed in ((32768, 512, 2), (37, 151936, 3), (2048, 4099, 4)):
+        logits, targets = _case(rows, vocab, seed)
+        scale = 0.5
+        got = _run("tb_head_stats_grad_noalloc", logits, targets, scale)
+        ent, loss, cor, dl = ops.head_stats_exact(logits.cpu(), targets.cpu(), scale)
+        # against fp64, a row whose entropy (or loss) nearly cancels is held to the scale of
+        # the rows (rms floor), as the fp32 sums of the reference's sweep are
+        _check(got, (ent, loss, cor, dl), floor=None)
+        assert bool(got[2][0])
 
 
 def test_noalloc_head_stats_rejects_rows_beyond_its_scratch():

@@ -527,16 +527,27 @@ constexpr size_t kNoAllocBytes = kNoAllocPartBytes + kNoAllocIdxBytes + kNoAlloc
 
 static __device__ __align__(256) unsigned char g_head_scratch[kNoAllocBytes];
 
-// Device address of g_head_scratch on the current device, taken once per device (the host-side
-// name of the array is not a device address).
-int head_scratch(unsigned char **out) {
+// Device address of g_head_scratch on the current device (the host-side name of the array is
+// not a device address). Outside stream capture it is looked up on every call (cheap), so a
+// device reset between calls, which reloads the library's module, never leaves a stale
+// address behind; during capture, where the lookup could load the module, the address taken by
+// an earlier call on the device is used (hence: a first call before any capture).
+int head_scratch(cudaStream_t stream, unsigned char **out) {
   static std::mutex lock;
   static unsigned char *cached[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return set_error(TB_EDEVICE, "head_stats_grad_noalloc: no usable current device");
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &capture) != cudaSuccess) {
+    (void)cudaGetLastError();
+    capture = cudaStreamCaptureStatusActive;  // unknown: do not risk a lookup
+  }
   std::lock_guard<std::mutex> guard(lock);
-  if (cached[dev] == nullptr) {
+  if (capture == cudaStreamCaptureStatusNone || cached[dev] == nullptr) {
+    if (capture != cudaStreamCaptureStatusNone)
+      return set_error(TB_EINVAL, "head_stats_grad_noalloc: the first call on a device must "
+                       "come before any stream capture");
     void *ptr = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&ptr, g_head_scratch);
     if (e != cudaSuccess || ptr == nullptr)
@@ -567,7 +578,7 @@ extern "C" int tb_head_stats_grad_noalloc(uint16_t *logits, const int64_t *targe
   if (!logits || !targets || !entropy || !loss || !correct)
     return set_error(TB_EINVAL, "head_stats_grad_noalloc: all pointers are required");
   unsigned char *scratch = nullptr;
-  int rc = head_scratch(&scratch);
+  int rc = head_scratch(as_stream(stream), &scratch);
   if (rc != TB_OK) return rc;
   float *part = reinterpret_cast<float *>(scratch);
   int64_t *part_idx = reinterpret_cast<int64_t *>(scratch + kNoAllocPartBytes);
