@@ -81,27 +81,16 @@ def run(model, fused):
     return float(out.loss), grads, entropy, accuracy, rows
 
 
-@pytest.mark.parametrize("attention", ["flash_varlen", "torch_varlen", "padded"])
-def test_fused_step_matches_unpatched_model(lora_model, attention):
-    """Every attention form of the fused path: token-major variable-length attention through
-    FlashAttention 2 (the default) or PyTorch's varlen kernels, and the reference's padded layout
-    with the causal + padding mask."""
+def test_fused_step_matches_unpatched_model(lora_model):
+    """Head dimension 64, which the library's attention kernels do not take: the fused path
+    keeps the reference's padded layout and SDPA with the causal + padding mask around the
+    library's other kernels."""
     from testt_b200 import _lib, model
 
-    if attention == "flash_varlen" and model._flash_varlen is None:
-        pytest.skip("flash_attn is not installed")
-    if attention == "torch_varlen" and model._torch_varlen is None:
-        pytest.skip("torch.nn.attention.varlen is not available")
     ref = run(lora_model, fused=False)
     _lib.reset_call_count()
-    saved = model.USE_VARLEN_ATTENTION, model.USE_FLASH_ATTN, model.USE_OWN_ATTENTION
-    model.USE_VARLEN_ATTENTION = attention != "padded" and saved[0]
-    model.USE_FLASH_ATTN = attention == "flash_varlen"
-    model.USE_OWN_ATTENTION = False
-    try:
-        got = run(lora_model, fused=True)
-    finally:
-        model.USE_VARLEN_ATTENTION, model.USE_FLASH_ATTN, model.USE_OWN_ATTENTION = saved
+    assert not model._varlen_available(64, torch.device(DEV))
+    got = run(lora_model, fused=True)
     assert _lib.call_count() > 0, "the fused step must run the native kernels"
     _assert_same_step(got, ref)
 
@@ -133,26 +122,39 @@ def lora_model_d128():
                              norm_jitter=True)
 
 
-def test_fused_step_with_own_attention_matches_unpatched_model(lora_model_d128):
+@pytest.mark.parametrize("nf4_gemm", [False, True], ids=["unpack", "nf4_gemm"])
+def test_fused_step_with_own_attention_matches_unpatched_model(lora_model_d128, nf4_gemm):
     """Head dimension 128: the variable-length attention runs through tb_attn_varlen_fwd / _bwd
-    (checked), and the step matches the unpatched model as with the other attention forms."""
-    from testt_b200 import attention, model
+    (checked), and the step matches the unpatched model, with the layers' projections either
+    over unpacked weights (one unpack launch per layer, cuBLAS) or through the NF4-decoding
+    GEMMs (q|k|v + RoPE, o, the MLP with SwiGLU in the epilogues; checked)."""
+    from testt_b200 import attention, fused_layer, model
 
-    calls = []
-    original = attention.varlen_attention
+    calls, fused_calls = [], []
+    original, original_mlp = attention.varlen_attention, fused_layer.layer_mlp
 
     def counted(*args):
         calls.append(1)
         return original(*args)
 
+    def counted_mlp(*args):
+        fused_calls.append(1)
+        return original_mlp(*args)
+
     ref = run(lora_model_d128, fused=False)
     attention.varlen_attention = counted
+    fused_layer.layer_mlp = counted_mlp
+    saved = model.USE_NF4_GEMM
+    model.USE_NF4_GEMM = nf4_gemm
     try:
-        assert model.USE_OWN_ATTENTION and model.USE_VARLEN_ATTENTION
+        assert model.USE_VARLEN_ATTENTION
         got = run(lora_model_d128, fused=True)
     finally:
         attention.varlen_attention = original
+        fused_layer.layer_mlp = original_mlp
+        model.USE_NF4_GEMM = saved
     assert len(calls) == 2, "each layer's attention must run the library's kernels"
+    assert len(fused_calls) == (2 if nf4_gemm else 0)
     _assert_same_step(got, ref)
 
 

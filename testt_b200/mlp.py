@@ -12,7 +12,7 @@
 import torch
 
 from . import _lib
-from .nf4 import unpack_concat
+from .nf4 import LayerWeights
 
 # Save the fp16 gate|up GEMM output [tokens, 2*inter] for backward (22 MB per Qwen2.5-1.5B
 # layer at 621 tokens) instead of recomputing it there as the reference does to save memory:
@@ -56,81 +56,53 @@ def gated_silu_backward_(dact, gu):
     return gu
 
 
-class FusedNF4MLP(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, x, gate_w, up_w, down_w):
-        gate_up = unpack_concat((gate_w, up_w), x.device)
-        gu = torch.matmul(x, gate_up.t())
-        del gate_up
-        act = gated_silu(gu)
-        if RECOMPUTE_GATE_UP:
-            del gu
-            ctx.save_for_backward(x)
-        else:
-            ctx.save_for_backward(x, gu)
-        down = unpack_concat((down_w,), x.device)
-        out = torch.matmul(act, down.t())
-        ctx.weights = (gate_w, up_w, down_w)
-        return out
-
-    @staticmethod
-    def backward(ctx, grad_out):
-        if not ctx.needs_input_grad[0]:
-            return None, None, None, None
-        gate_w, up_w, down_w = ctx.weights
-        saved = ctx.saved_tensors
-        x = saved[0]
-        grad_out = grad_out.to(torch.float16)
-        down = unpack_concat((down_w,), grad_out.device)
-        dact = torch.matmul(grad_out, down)
-        del down
-        gate_up = unpack_concat((gate_w, up_w), grad_out.device)
-        gu = torch.matmul(x, gate_up.t()) if RECOMPUTE_GATE_UP else saved[1]
-        gated_silu_backward_(dact, gu)
-        del dact
-        grad_x = torch.matmul(gu, gate_up)
-        return grad_x, None, None, None
-
-
 class LayerMLP(torch.autograd.Function):
-    """FusedNF4MLP on the operands of a LayerWeights: gate|up is operand g_gu, down g_down."""
+    """down(silu(gate(x)) * up(x)) on the operands of a LayerWeights: gate|up is operand g_gu
+    ([2 inter, hidden], one GEMM), down g_down. With `own` set the LayerWeights belongs to this
+    node alone: its unpacked copies are dropped after the forward and after the backward, which
+    unpacks them again (in one launch) as the reference's MLP does to hold no fp16 weights
+    between the passes."""
 
     @staticmethod
-    def forward(ctx, x, lw, g_gu, g_down):
-        ops = lw.operands(x.device)
-        gu = torch.matmul(x, ops[g_gu].t())
+    def forward(ctx, x, lw, g_gu, g_down, own):
+        w = lw.operands(x.device)
+        gu = torch.matmul(x, w[g_gu].t())
         act = gated_silu(gu)
-        if RECOMPUTE_GATE_UP:
-            del gu
-            ctx.save_for_backward(x)
-        else:
-            ctx.save_for_backward(x, gu)
-        out = torch.matmul(act, ops[g_down].t())
-        ctx.lw, ctx.groups = lw, (g_gu, g_down)
+        out = torch.matmul(act, w[g_down].t())
+        # backward needs gu (the SwiGLU backward's operand); recomputing it is a third GEMM
+        ctx.save_for_backward(x, None if RECOMPUTE_GATE_UP else gu)
+        ctx.lw, ctx.groups, ctx.own = lw, (g_gu, g_down), own
+        if own:
+            lw.release()
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
         if not ctx.needs_input_grad[0]:
-            return None, None, None, None
-        ops = ctx.lw.operands(grad_out.device)
+            return None, None, None, None, None
+        x, gu = ctx.saved_tensors
         g_gu, g_down = ctx.groups
-        saved = ctx.saved_tensors
-        x = saved[0]
-        grad_out = grad_out.to(torch.float16)
-        dact = torch.matmul(grad_out, ops[g_down])
-        gu = torch.matmul(x, ops[g_gu].t()) if RECOMPUTE_GATE_UP else saved[1]
-        gated_silu_backward_(dact, gu)
-        del dact
-        grad_x = torch.matmul(gu, ops[g_gu])
-        return grad_x, None, None, None
+        w = ctx.lw.operands(grad_out.device)
+        if gu is None:
+            gu = torch.matmul(x, w[g_gu].t())
+        # dact = dy . W_down, then [dgate | dup] in place of gu, then one GEMM back through both
+        gated_silu_backward_(torch.matmul(grad_out.to(torch.float16), w[g_down]), gu)
+        grad_x = torch.matmul(gu, w[g_gu])
+        if ctx.own:
+            ctx.lw.release()
+        return grad_x, None, None, None, None
 
 
 def layer_mlp(x, lw, g_gu, g_down):
+    """The MLP of a decoder layer on its LayerWeights' operands g_gu (gate|up) and g_down."""
     _lib.require_cuda(x, what="layer_mlp")
-    return LayerMLP.apply(x.contiguous(), lw, g_gu, g_down)
+    return LayerMLP.apply(x.contiguous(), lw, g_gu, g_down, False)
 
 
 def fused_mlp(x, gate_w, up_w, down_w):
+    """down(silu(gate(x)) * up(x)) for three frozen NF4 weights (the reference's op,
+    solution/mlp.py:80-118): they form a LayerWeights ((gate, up), (down,)) of their own, unpacked
+    in one launch in the forward and again in the backward."""
     _lib.require_cuda(x, what="fused_mlp")
-    return FusedNF4MLP.apply(x.contiguous(), gate_w, up_w, down_w)
+    lw = LayerWeights(((gate_w, up_w), (down_w,)))
+    return LayerMLP.apply(x.contiguous(), lw, 0, 1, True)

@@ -14,8 +14,7 @@ Per decoder layer, with s the fp32 residual stream of the M real tokens:
                                                       tb_lora_gather, cuBLAS; tb_lora_dropout_grad
     q, k, v    = rope_tokens(qkv, lq, lv)             tb_rope_tokens_fwd, token-major [M, H, 128]
     a          = varlen causal attention(q, k, v)     tb_attn_varlen_fwd / _bwd (sm_100, head
-                                                      dim 128), else FlashAttention 2 varlen,
-                                                      else PyTorch's varlen flash kernels
+                                                      dim 128)
     o          = a @ Wo^T                             cuBLAS
     s, y2, _   = add_rmsnorm(s, o)                    tb_add_rmsnorm_fwd
     d          = mlp(y2)                              cuBLAS + tb_swiglu_fwd
@@ -24,9 +23,9 @@ once, in its first operation)
 then the final norm and the fused head (head.py). Pad tokens never enter the projections, norms,
 MLP, attention or head. Causal attention over each row's real tokens in column order is the
 unpatched model's causal + padding-mask attention restricted to the real query rows (the only
-rows whose outputs are used), with the padded positions never computed. Without
-torch.nn.attention.varlen, attention runs as in the reference: rope_pack into the padded
-[B, H, T, 128] layout and SDPA with the causal + padding mask.
+rows whose outputs are used), with the padded positions never computed. Where those kernels
+do not take the model (another head dimension or GPU), attention runs as in the reference:
+rope_pack into the padded [B, H, T, head_dim] layout and SDPA with the causal + padding mask.
 """
 
 import threading
@@ -42,43 +41,20 @@ from .rmsnorm import add_rmsnorm
 from .lora import lora_pair
 from .rope import rope_pack, rope_tokens, slot_index
 
-try:
-    from torch.nn.attention.varlen import varlen_attn as _torch_varlen
-except ImportError:  # torch < 2.9
-    _torch_varlen = None
-try:  # FlashAttention 2 (library): GQA handled inside its backward, no separate dK/dV sums
-    from flash_attn import flash_attn_varlen_func as _flash_varlen
-except ImportError:
-    _flash_varlen = None
-
-
 def _varlen_attn(q, k, v, cu_seqlens, max_len, scale):
     """Causal attention over the packed sequences of cu_seqlens (token-major q, k, v): this
-    library's kernels (attention.varlen_attention) on sm_100 with head dim 128, else
-    FlashAttention 2's varlen kernels or PyTorch's."""
-    if USE_OWN_ATTENTION and _own_attn.supported(q, k, v):
-        return _own_attn.varlen_attention(q, k, v, cu_seqlens, max_len, scale)
-    if _flash_varlen is not None and USE_FLASH_ATTN:
-        return _flash_varlen(q, k, v, cu_seqlens, cu_seqlens, max_len, max_len,
-                             softmax_scale=scale, causal=True)
-    return _torch_varlen(q, k, v, cu_seqlens, cu_seqlens, max_len, max_len, scale=scale,
-                         window_size=(-1, 0))
-
-
-USE_OWN_ATTENTION = True  # tb_attn_varlen_fwd / _bwd
+    library's kernels (attention.varlen_attention)."""
+    return _own_attn.varlen_attention(q, k, v, cu_seqlens, max_len, scale)
 
 
 def _varlen_available(head_dim, device):
-    """Whether some variable-length attention runs here: the library's kernels (sm_100, head
-    dim 128) or one of the fallbacks."""
-    if USE_OWN_ATTENTION and head_dim == _own_attn.HEAD_DIM and \
-            torch.cuda.get_device_capability(device)[0] == 10:
-        return True
-    return (_flash_varlen is not None and USE_FLASH_ATTN) or _torch_varlen is not None
-USE_FLASH_ATTN = True
+    """Whether the library's variable-length attention kernels take this model (sm_100, head
+    dim 128). Otherwise the step keeps the reference's padded layout and SDPA."""
+    return head_dim == _own_attn.HEAD_DIM and torch.cuda.get_device_capability(device)[0] == 10
 
-# causal attention over each sequence's real tokens (token-major); the library's own kernels
-# need no optional package, the fallbacks for other GPUs or head sizes do
+
+# causal attention over each sequence's real tokens (token-major) through the library's own
+# kernels where they take the model; False keeps the reference's padded layout and SDPA
 USE_VARLEN_ATTENTION = True
 
 # Keep each layer's fp16 weights, unpacked once per step in the forward, for the backward (2.6 GB
@@ -88,11 +64,12 @@ USE_VARLEN_ATTENTION = True
 # False restores the reference's second unpack.
 KEEP_UNPACKED_WEIGHTS = True
 
-# Layers whose every NF4 operand the NF4-decoding GEMM (tb_nf4_gemm) takes run their projections
-# through it (fused_layer: q|k|v with bias, LoRA rows and RoPE in the GEMM's finishing phase, o,
-# the MLP with SwiGLU in the epilogues) and unpack no weight. The kernel is not in the library
-# yet, so fused_layer.usable() is False and every layer takes the unpacking path.
-USE_NF4_GEMM = True
+# True: layers whose every NF4 operand the NF4-decoding GEMM (tb_nf4_gemm) takes run their
+# projections through it (fused_layer: q|k|v with bias, LoRA rows and RoPE in the GEMM's
+# finishing phase, o, the MLP with SwiGLU in the epilogues) and unpack no weight. Off by
+# default: at the config-5 shapes the decoding GEMM is slower than one unpack launch per layer
+# plus cuBLAS (same results either way; the model tests run both).
+USE_NF4_GEMM = False
 
 _ALLOWED_KWARGS = {"num_items_in_batch", "output_attentions", "output_hidden_states",
                    "return_dict"}

@@ -292,12 +292,16 @@ class LayerWeights:
 
 class LayerLinear(torch.autograd.Function):
     """y = x @ W^T (+ b) with W operand `group` of a LayerWeights; `last` marks the layer's
-    operation that runs last in backward (it releases the layer's unpacked weights)."""
+    operation that runs last in backward (it releases the layer's unpacked weights). With `own`
+    the LayerWeights belongs to this node alone and is also released after the forward, so W is
+    unpacked again for the backward (nothing large is held between the passes)."""
 
     @staticmethod
-    def forward(ctx, x, bias, lw, group, last):
+    def forward(ctx, x, bias, lw, group, last, own):
         out = torch.nn.functional.linear(x, lw.operands(x.device)[group], bias)
-        ctx.lw, ctx.group, ctx.last = lw, group, last
+        ctx.lw, ctx.group, ctx.last = lw, group, last or own
+        if own:
+            lw.release()
         return out
 
     @staticmethod
@@ -307,32 +311,15 @@ class LayerLinear(torch.autograd.Function):
             grad_x = grad_out.to(torch.float16) @ ctx.lw.operands(grad_out.device)[ctx.group]
         if ctx.last:
             ctx.lw.release()
-        return grad_x, None, None, None, None
+        return grad_x, None, None, None, None, None
 
 
 def layer_linear(x, lw, group, bias=None, last=False):
-    return LayerLinear.apply(x, bias, lw, group, last)
-
-
-class FrozenNF4Linear(torch.autograd.Function):
-    """y = x @ W^T (+ b) for frozen 4-bit weights stacked by rows, fp16 in and out
-    (reference: nf4.py:108-127). Nothing large is saved: W is unpacked again in backward."""
-
-    @staticmethod
-    def forward(ctx, x, bias, weights):
-        weight = unpack_concat(weights, x.device)
-        out = torch.nn.functional.linear(x, weight, bias)
-        ctx.weights = weights
-        return out
-
-    @staticmethod
-    def backward(ctx, grad_out):
-        grad_x = None
-        if ctx.needs_input_grad[0]:
-            weight = unpack_concat(ctx.weights, grad_out.device)
-            grad_x = grad_out.to(torch.float16) @ weight
-        return grad_x, None, None
+    return LayerLinear.apply(x, bias, lw, group, last, False)
 
 
 def frozen_linear(x, weights, bias=None):
-    return FrozenNF4Linear.apply(x, bias, tuple(weights))
+    """y = x @ W^T (+ b) for frozen NF4 weights stacked by rows, fp16 in and out (the
+    reference's op, solution/nf4.py:108-131): the weights form a LayerWeights of their own,
+    unpacked in one launch for the forward and again for the backward."""
+    return LayerLinear.apply(x, bias, LayerWeights((tuple(weights),)), 0, True, True)
