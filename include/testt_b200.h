@@ -84,36 +84,37 @@ int tb_nf4_unpack_multi(int32_t n_weights, const uint8_t *const *packed,
  * GEMMs of FusedNF4MLP (solution/mlp.py:80-113).
  *
  * W is 1..TB_NF4_GEMM_MAX_WEIGHTS weights stacked by rows (q|k|v, gate|up), each in
- * bitsandbytes' packing (row-major [rows[j], k_dim], blocksize 64, high nibble first) with fp32
- * absmax per block (a nested state's absmax expanded by the caller:
- * fp32(code2[c] * absmax2[b / 256]) + offset, each operation rounded on its own). Every decoded
- * value is fp16(table[q] * absmax), bit-identical to tb_nf4_unpack_*; the products differ from
- * cuBLAS over the unpacked weight only in the order of the fp32 sums.
+ * bitsandbytes' packing (row-major [rows[j], k_dim], blocksize 64, high nibble first) with its
+ * fp32 absmax per block given block-column-major: absmax_t[j] is [k_dim / 64, rows[j]] (a nested
+ * state's absmax expanded by the caller: fp32(code2[c] * absmax2[b / 256]) + offset, each
+ * operation rounded on its own). Every decoded value is fp16(table[q] * absmax), bit-identical
+ * to tb_nf4_unpack_*; the products differ from cuBLAS over the unpacked weight only in the order
+ * of the fp32 sums.
  *   transpose 0: out[t, n] = fp16(sum_k in[t, k] W[n, k] (+ bias[n]))   in [tokens, k_dim]
  *                rows[j] multiples of 128, k_dim of 64
  *   transpose 1: out[t, k] = fp16(sum_n in[t, n] W[n, k])               in [tokens, sum rows]
  *                rows[j] multiples of 64, k_dim of 128, no bias
- * Arrays packed / absmax / nf4_table / rows are HOST arrays of length n_weights. Row strides
- * ld_in / ld_out in elements, multiples of 8; in, out, bias 16-byte aligned. When the reduction
- * is split over several CTAs it is summed within a thread-block cluster (no workspace), unless
- * tb_nf4_gemm_variant(1) asked for fp32 partials in `workspace`, whose size
- * tb_nf4_gemm_workspace gives (0: none needed). sm_100 only.
+ * Arrays packed / absmax_t / nf4_table / rows are HOST arrays of length n_weights. Row strides
+ * ld_in / ld_out in elements, multiples of 8; in, out, bias, packed, absmax_t 16-byte aligned.
+ * Persistent CTAs run the (128-row tile, token group, reduction split) units; when the reduction
+ * is split the fp32 partials go to `workspace` (tb_nf4_gemm_workspace bytes; without it the
+ * reduction is not split) and are summed in split order. sm_100 only.
  * ------------------------------------------------------------------------------------------- */
 #define TB_NF4_GEMM_MAX_WEIGHTS 4
 int tb_nf4_gemm(int32_t transpose, const uint16_t *tokens_in, int64_t tokens, int64_t ld_in,
-                int32_t n_weights, const uint8_t *const *packed, const float *const *absmax,
+                int32_t n_weights, const uint8_t *const *packed, const float *const *absmax_t,
                 const float *const *nf4_table, const int64_t *rows, int64_t k_dim,
                 const uint16_t *bias, uint16_t *out, int64_t ld_out, float *workspace,
                 int64_t workspace_bytes, void *stream);
 
 /* Bytes of fp32 workspace tb_nf4_gemm needs for these shapes under the current variant (0 when
- * the reduction is not split or is summed within a cluster). No counterpart in the reference. */
+ * the reduction is not split). No counterpart in the reference. */
 int64_t tb_nf4_gemm_workspace(int32_t transpose, int64_t tokens, int32_t n_weights,
                               const int64_t *rows, int64_t k_dim);
 
-/* How tb_nf4_gemm sums a split reduction, process-wide: 0 automatic (within a thread-block
- * cluster of the splits), 1 fp32 partials in the caller's workspace + a summing kernel, 2 the
- * cluster always. Same results either way. No counterpart in the reference. */
+/* How tb_nf4_gemm plans the reduction, process-wide: 0 split so that the work units fill the GPU
+ * (fp32 partials in the workspace), 1 never split. Same results either way (up to the order of
+ * the fp32 sums). No counterpart in the reference. */
 int tb_nf4_gemm_variant(int32_t variant);
 
 /* The MLP's NF4 GEMMs with SwiGLU in the epilogue (solution/mlp.py:31-58 applied to the GEMM's
@@ -126,24 +127,30 @@ int tb_nf4_gemm_variant(int32_t variant);
  *               with d(gate|up) (act unused, may be NULL). */
 int tb_nf4_gemm_swiglu(int32_t backward, const uint16_t *tokens_in, int64_t tokens, int64_t ld_in,
                        int32_t n_weights, const uint8_t *const *packed,
-                       const float *const *absmax, const float *const *nf4_table,
+                       const float *const *absmax_t, const float *const *nf4_table,
                        const int64_t *rows, int64_t k_dim, uint16_t *gu, int64_t ld_gu,
                        uint16_t *act, int64_t ld_act, void *stream);
 
-/* The q|k|v projection with its bias, the LoRA rows and the rotary embedding in the GEMM's
- * finishing phase: weights (q, k, v) = [n_heads * 128, k_dim], [n_kv * 128, k_dim] twice (HOST
- * arrays of 3); x fp16 [tokens, k_dim] (row stride ld_x); bias fp16 [(n_heads + 2 n_kv) * 128]
- * or NULL; lora_q fp16 [tokens, n_heads * 128], lora_v fp16 [tokens, n_kv * 128] or NULL; cos,
- * sin fp32 [seq, 128]; pos_idx int64 [tokens] padded positions (t = pos % seq; a negative
- * position writes nothing). Writes token-major q [tokens, n_heads, 128], k, v
- * [tokens, n_kv, 128]: what tb_rope_tokens_fwd writes from the GEMM's fp16 output
- * (solution/rope.py:24-75 with the padded scatter replaced by token-major rows). */
+/* The q|k|v projection with its bias, the LoRA rows and the rotary embedding: weights (q, k, v) =
+ * [n_heads * 128, k_dim], [n_kv * 128, k_dim] twice (HOST arrays of 3); x fp16 [tokens, k_dim]
+ * (row stride ld_x); bias fp16 [(n_heads + 2 n_kv) * 128] or NULL; lora_q fp16
+ * [tokens, n_heads * 128], lora_v fp16 [tokens, n_kv * 128] or NULL; cos, sin fp32 [seq, 128];
+ * pos_idx int64 [tokens] padded positions (t = pos % seq; a negative position writes nothing).
+ * Writes token-major q [tokens, n_heads, 128], k, v [tokens, n_kv, 128]: what
+ * tb_rope_tokens_fwd writes from the GEMM's fp16 output (solution/rope.py:24-75 with the padded
+ * scatter replaced by token-major rows). The GEMM's fp32 partials go to `workspace`
+ * (tb_nf4_gemm_qkv_rope_workspace bytes, 16-byte aligned); a second kernel finishes them. */
 int tb_nf4_gemm_qkv_rope(const uint16_t *x, int64_t tokens, int64_t ld_x,
-                         const uint8_t *const *packed, const float *const *absmax,
+                         const uint8_t *const *packed, const float *const *absmax_t,
                          const float *const *nf4_table, int64_t k_dim, const uint16_t *bias,
                          const uint16_t *lora_q, const uint16_t *lora_v, const float *cos,
                          const float *sin, const int64_t *pos_idx, int64_t seq, int32_t n_heads,
-                         int32_t n_kv, uint16_t *q, uint16_t *k, uint16_t *v, void *stream);
+                         int32_t n_kv, uint16_t *q, uint16_t *k, uint16_t *v, float *workspace,
+                         int64_t workspace_bytes, void *stream);
+
+/* Bytes of workspace tb_nf4_gemm_qkv_rope needs. No counterpart in the reference. */
+int64_t tb_nf4_gemm_qkv_rope_workspace(int64_t tokens, int32_t n_heads, int32_t n_kv,
+                                       int64_t k_dim);
 
 /* ---------------------------------------------------------------------------------------------
  * Residual add + RMSNorm. Replaces rmsnorm_fwd_kernel / rmsnorm_bwd_kernel and their launches,

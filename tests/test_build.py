@@ -41,24 +41,26 @@ def _rows(*rows):
 
 
 def test_nf4_gemm_plan_of_the_step_projections(lib):
-    """The workspace the split reduction asks for (variant 1: fp32 partials in a workspace)
-    shows the plan at the step's 621 tokens on 148 SMs (the count assumed without a GPU): q|k|v
-    and o forward split 4 and 6 ways, down forward 6, gate|up forward none (280 CTAs); backward
-    gate|up 6, down none. The default (cluster reduction) needs no workspace."""
+    """The workspace the split reduction asks for shows the plan at the step's 621 tokens (three
+    token groups of 208) on 148 SMs (the count assumed without a GPU): forward q|k|v split 3
+    ways (48 tiles), o and down 4 (36 tiles), gate|up not at all (420 tiles); backward gate|up's
+    dX 4, down's dX none (210 tiles). Variant 1 never splits."""
     ws = lib.tb_nf4_gemm_workspace
+    t = 621
+    assert ws(0, t, 3, _rows(1536, 256, 256), 1536) == 3 * t * 2048 * 4
+    assert ws(0, t, 1, _rows(1536), 1536) == 4 * t * 1536 * 4
+    assert ws(0, t, 1, _rows(1536), 8960) == 4 * t * 1536 * 4
+    assert ws(0, t, 2, _rows(8960, 8960), 1536) == 0
+    assert ws(1, t, 2, _rows(8960, 8960), 1536) == 4 * t * 1536 * 4
+    assert ws(1, t, 1, _rows(1536), 8960) == 0
+    assert lib.tb_nf4_gemm_qkv_rope_workspace(t, 12, 2, 1536) == 3 * t * 2048 * 4
     assert lib.tb_nf4_gemm_variant(1) == 0
     try:
-        t = 621
-        assert ws(0, t, 3, _rows(1536, 256, 256), 1536) == 4 * t * 2048 * 4
-        assert ws(0, t, 1, _rows(1536), 1536) == 6 * t * 1536 * 4
-        assert ws(0, t, 1, _rows(1536), 8960) == 6 * t * 1536 * 4
-        assert ws(0, t, 2, _rows(8960, 8960), 1536) == 0
-        assert ws(1, t, 2, _rows(8960, 8960), 1536) == 6 * t * 1536 * 4
-        assert ws(1, t, 1, _rows(1536), 8960) == 0
+        assert ws(0, t, 3, _rows(1536, 256, 256), 1536) == 0
+        assert lib.tb_nf4_gemm_qkv_rope_workspace(t, 12, 2, 1536) == t * 2048 * 4
     finally:
         lib.tb_nf4_gemm_variant(0)
-    assert ws(0, 621, 3, _rows(1536, 256, 256), 1536) == 0
-    assert lib.tb_nf4_gemm_variant(3) == TB_EINVAL
+    assert lib.tb_nf4_gemm_variant(2) == TB_EINVAL
 
 
 def test_gemm_entry_points_reject_bad_arguments_before_any_cuda_call(lib):
@@ -83,7 +85,7 @@ def test_gemm_entry_points_reject_bad_arguments_before_any_cuda_call(lib):
     # tb_nf4_gemm_qkv_rope: query heads not a multiple of the key/value heads
     q = lib.tb_nf4_gemm_qkv_rope
     assert q(p(256), 10, 1536, three, three, three, 1536, None, None, None, p(256), p(256),
-             p(256), 512, 12, 5, p(256), p(256), p(256), None) == TB_EINVAL
+             p(256), 512, 12, 5, p(256), p(256), p(256), p(256), 1 << 20, None) == TB_EINVAL
     # tb_lora_backward: rank 8, then widths / hidden that are not multiples of 64
     lb = lib.tb_lora_backward
     bufs = [p(256)] * 7

@@ -40,8 +40,8 @@ def available():
 
 
 def set_variant(variant):
-    """How a split reduction is summed, process-wide: 0 automatic (within a thread-block cluster
-    of the splits), 1 fp32 partials in a workspace + a summing kernel, 2 cluster always."""
+    """How tb_nf4_gemm plans the reduction, process-wide: 0 split so that the work units fill the
+    GPU (fp32 partials in a workspace, summed in split order), 1 never split."""
     if _lib.load().tb_nf4_gemm_variant(int(variant)) != 0:
         raise ValueError(_lib.load().tb_last_error().decode(errors="replace"))
 
@@ -49,7 +49,7 @@ def set_variant(variant):
 def supported(weights, transpose=False):
     """True when tb_nf4_gemm takes these weights: 1-4 NF4 weights with blocksize 64, the same
     column count, rows a multiple of 128 (forward) or 64 (backward), columns a multiple of 64
-    (forward) or 128 (backward)."""
+    (forward) or 128 (backward), packed bytes 16-byte aligned (TMA)."""
     if not 1 <= len(weights) <= MAX_WEIGHTS:
         return False
     if not all(supports_fast_unpack(w) and _quant_state(w).blocksize == BLOCKSIZE for w in weights):
@@ -57,19 +57,18 @@ def supported(weights, transpose=False):
     shapes = [weight_shape(w) for w in weights]
     cols = shapes[0][1]
     row_mult, col_mult = (64, 128) if transpose else (128, 64)
-    return all(s[1] == cols and s[0] % row_mult == 0 for s in shapes) and cols % col_mult == 0
+    return all(s[1] == cols and s[0] % row_mult == 0 for s in shapes) and \
+        cols % col_mult == 0 and all(w.data.data_ptr() % 16 == 0 for w in weights)
 
 
 def fp32_absmax(weight):
-    """The weight's per-block absmax in fp32. A nested state's absmax is expanded once and kept
-    on the state: code2[c] * absmax2[b // blocksize2] + offset, the product and the sum each
-    rounded to fp32 (two kernels, no fused multiply-add), as the unpack kernel computes it."""
+    """The weight's per-block absmax in fp32, in bitsandbytes' block order ([rows, cols / 64]
+    flattened). A nested state's absmax is expanded: code2[c] * absmax2[b // blocksize2] +
+    offset, the product and the sum each rounded to fp32 (two kernels, no fused multiply-add), as
+    the unpack kernel computes it."""
     state = _quant_state(weight)
     if not state.nested:
         return state.absmax
-    cached = getattr(state, "_tb_absmax_f32", None)
-    if cached is not None and cached.device == state.absmax.device:
-        return cached
     dev = state.absmax.device
     code2 = state.state2.code.to(torch.float32)
     absmax2 = state.state2.absmax.to(torch.float32)
@@ -77,12 +76,24 @@ def fp32_absmax(weight):
     prod = code2[state.absmax.long()] * absmax2[blocks]
     off = state.offset
     off = off.to(device=dev, dtype=torch.float32) if torch.is_tensor(off) else float(off)
-    absmax = (prod + off).contiguous()
+    return (prod + off).contiguous()
+
+
+def absmax_t(weight):
+    """The fp32 absmax block-column-major, [cols / 64, rows] (what the GEMM's bulk copies read:
+    the absmax of 64 or 128 consecutive rows of one 64-column block, contiguous), computed once
+    and kept on the quantisation state."""
+    state = _quant_state(weight)
+    cached = getattr(state, "_tb_absmax_t", None)
+    if cached is not None and cached.device == state.absmax.device:
+        return cached
+    rows, cols = weight_shape(weight)
+    out = fp32_absmax(weight).view(rows, cols // BLOCKSIZE).t().contiguous()
     try:
-        state._tb_absmax_f32 = absmax
+        state._tb_absmax_t = out
     except AttributeError:
         pass
-    return absmax
+    return out
 
 
 def nf4_matmul(x, weights, bias=None, transpose=False):
@@ -112,7 +123,7 @@ def nf4_matmul(x, weights, bias=None, transpose=False):
     if x.stride(0) % 8 or x.data_ptr() % 16:
         x = x.contiguous()
     bias = None if bias is None else bias.to(torch.float16).contiguous()
-    absmax = [fp32_absmax(w) for w in weights]
+    absmax = [absmax_t(w) for w in weights]
     tables = [_quant_state(w).code.to(torch.float32).contiguous() for w in weights]
     n = len(weights)
     rows_arr = (ctypes.c_int64 * n)(*rows)
@@ -136,7 +147,7 @@ def _swiglu_call(backward, x, weights, gu, act):
     rows = [weight_shape(w)[0] for w in weights]
     cols = weight_shape(weights[0])[1]
     n = len(weights)
-    absmax = [fp32_absmax(w) for w in weights]  # held until the launch is queued
+    absmax = [absmax_t(w) for w in weights]  # held until the launch is queued
     tables = [_quant_state(w).code.to(torch.float32).contiguous() for w in weights]
     rc = fn(int(backward), _lib.ptr(x), x.shape[0], x.stride(0), n,
             _lib.ptr_array([_lib.ptr(w.data) for w in weights]),
@@ -194,14 +205,17 @@ def qkv_rope(x, qkv_weights, bias, lora_q, lora_v, cos, sin, pos_idx, seq, n_hea
     bias, lora_q, lora_v = conv(bias), conv(lora_q), conv(lora_v)
     cos, sin = cos.to(torch.float32).contiguous(), sin.to(torch.float32).contiguous()
     pos = pos_idx.to(torch.int64).contiguous()
-    absmax = [fp32_absmax(w) for w in ws]  # held until the launch is queued
+    absmax = [absmax_t(w) for w in ws]  # held until the launch is queued
     tables = [_quant_state(w).code.to(torch.float32).contiguous() for w in ws]
+    kdim = weight_shape(ws[0])[1]
+    nbytes = _lib.load().tb_nf4_gemm_qkv_rope_workspace(t, n_heads, n_kv, kdim)
+    work = torch.empty(max(nbytes, 16) // 4, dtype=torch.float32, device=dev)
     rc = fn(_lib.ptr(x), t, x.stride(0), _lib.ptr_array([_lib.ptr(w.data) for w in ws]),
             _lib.ptr_array([_lib.ptr(a) for a in absmax]),
             _lib.ptr_array([_lib.ptr(tb) for tb in tables]),
             weight_shape(ws[0])[1], _lib.ptr(bias), _lib.ptr(lora_q), _lib.ptr(lora_v),
             _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(pos), seq, n_heads, n_kv, _lib.ptr(q),
-            _lib.ptr(k), _lib.ptr(v), _lib.stream_of(x))
+            _lib.ptr(k), _lib.ptr(v), _lib.ptr(work), nbytes, _lib.stream_of(x))
     if rc != 0:
         msg = _lib.load().tb_last_error().decode(errors="replace")
         raise _lib.KernelError(f"tb_nf4_gemm_qkv_rope failed ({rc}): {msg}")
