@@ -418,6 +418,29 @@ int tb_head_stats_grad_noalloc(uint16_t *logits, const int64_t *targets, float *
                                float *loss, int32_t *correct, int64_t rows, int64_t vocab,
                                int64_t ld, float grad_scale, void *stream);
 
+/* The head's hidden-state gradient with the logits gradient formed inside the tensor-core GEMM
+ * (replaces the in-place dlogits of solution/head.py:73-76 followed by the cuBLAS
+ * dh_chunk = dlogits[:lab] @ W of solution/head.py:113). For the first `rows` rows of the fp16
+ * logits slab [rows, cols] (row stride ld, columns col_offset .. of the vocabulary) with lse fp32
+ * [rows] and targets int64 [rows] (global columns; IGNORE_INDEX rows give a zero gradient):
+ *   dl[r, c] = fp16((e^(z[r, c] - lse[r]) - [col_offset + c == targets[r]]) * grad_scale)
+ *              (bit-identical to what tb_head_dlogits writes; never stored)
+ *   dh[r, :] = sum_c dl[r, c] W[c, :]     W fp16 [cols, hidden_dim], fp32 accumulation
+ * written to out row out_rows[r] (out_rows NULL: row r), row stride ld_out: fp32 when out_fp32
+ * (added to what out holds when accumulate is set), else rounded to fp16. The vocabulary is
+ * split over CTAs; their fp32 partials go to `workspace` (tb_head_dh_workspace bytes, 16-byte
+ * aligned) and are summed in a fixed order (deterministic). hidden_dim a multiple of 256, ld a
+ * multiple of 8, ld_out of 4; logits, weight, workspace 16-byte aligned. sm_100 only. */
+int tb_head_dh(const uint16_t *logits, int64_t ld, const int64_t *targets, const float *lse,
+               int64_t rows, int64_t cols, int64_t col_offset, float grad_scale,
+               const uint16_t *weight, int64_t hidden_dim, float *workspace,
+               int64_t workspace_bytes, void *out, int32_t out_fp32, const int64_t *out_rows,
+               int64_t ld_out, int32_t accumulate, void *stream);
+
+/* Bytes of workspace tb_head_dh needs for these sizes on the current device (0 for no rows). No
+ * counterpart in the reference. */
+int64_t tb_head_dh_workspace(int64_t rows, int64_t cols, int64_t hidden_dim);
+
 /* In place over the labelled rows of a [rows, cols] slab (columns col_offset ..):
  * logits <- fp16((exp(z - lse[row]) - [col == target]) * grad_scale); unlabelled rows untouched. */
 int tb_head_dlogits(uint16_t *logits, const int64_t *targets, const float *lse, int64_t rows,

@@ -65,11 +65,15 @@ SIGNATURES = {
     "tb_nf4_gemm_qkv_rope_workspace": [_I64, _I32, _I32, _I64],
     "tb_lora_backward": [_P, _P, _P, _P, _P, _P, _P, _I64, _F, _P, _P, _P, _P, _P, _P, _P, _I64,
                          _F, _I64, _I64, _I32, _I32, _P],
+    "tb_head_dh": [_P, _I64, _P, _P, _I64, _I64, _I64, _F, _P, _I64, _P, _I64, _P, _I32, _P,
+                   _I64, _I32, _P],
+    "tb_head_dh_workspace": [_I64, _I64, _I64],
 }
 
 # return types other than int (0 or a negative TB_E* code)
 RESTYPES = {"tb_nf4_gemm_workspace": ctypes.c_int64,
-            "tb_nf4_gemm_qkv_rope_workspace": ctypes.c_int64}
+            "tb_nf4_gemm_qkv_rope_workspace": ctypes.c_int64,
+            "tb_head_dh_workspace": ctypes.c_int64}
 
 _lib = None
 _calls = 0

@@ -21,8 +21,9 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
+from . import head as _head
 from .head import IGNORE_INDEX, USE_TENSOR_CORE_HEAD, VOCAB_TILE, _grad_unit, _host_counts, \
-    _tensor_core_ok
+    _tensor_core_ok, dh_supported, head_dh
 
 PART_FIELDS = 6
 
@@ -177,7 +178,9 @@ class ShardedHead:
             _lib.call("tb_head_merge", _lib.ptr(gp), _lib.ptr(gi), _lib.ptr(tgt), rows,
                       self.world, 1, _lib.ptr(lse), _lib.ptr(entropy), _lib.ptr(token_loss),
                       _lib.ptr(correct), stream)
-            if n_labelled:
+            if n_labelled and _head.USE_TENSOR_CORE_DH and dh_supported(logits, self.weight):
+                head_dh(logits, tgt, lse, self.weight, dh_sorted, scale, col_offset=self.lo)
+            elif n_labelled:
                 _lib.call("tb_head_dlogits", _lib.ptr(logits), _lib.ptr(tgt), _lib.ptr(lse),
                           n_labelled, cols, cols, self.lo, scale, stream)
                 dh_sorted = torch.mm(logits, self.weight, out_dtype=torch.float32)

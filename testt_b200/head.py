@@ -8,8 +8,10 @@ The head runs over the real (non-pad) tokens, labelled rows first. On B200 (sm_1
    logits are kept only for labelled rows;
 2. tb_head_merge: logsumexp, entropy = lse - sum(p z), token loss lse - z[label] and whether the
    first argmax is the label;
-3. tb_head_dlogits (labelled rows): (softmax - onehot) * scale in fp16, in place; then
-   dh = dlogits @ W (cuBLAS).
+3. the gradient of the labelled rows, dh = dlogits @ W with dlogits = (softmax - onehot) *
+   scale in fp16: tb_head_dlogits in place over the kept logits, then cuBLAS; or, with
+   USE_TENSOR_CORE_DH, tb_head_dh (dlogits formed from the kept logits inside a tcgen05 GEMM,
+   never written).
 Otherwise (hidden not a multiple of 64) the reference's structure runs, in chunks of CHUNK_ROWS
 rows: cuBLAS logits, tb_head_stats_grad (one CTA per row, two sweeps, dlogits in place) and the
 dh GEMM per chunk. The gradient is taken in forward (the head is frozen) and scaled by the loss
@@ -63,27 +65,67 @@ def _tensor_core_ok(h, weight):
     return torch.cuda.get_device_capability(h.device)[0] == 10
 
 
-def _tc_head(h, weight, tgt, entropy, token_loss, correct, grad_sorted, n_labelled, scale,
+def dh_supported(logits, weight):
+    """Whether tb_head_dh takes these operands (hidden a multiple of 256, 16-byte rows)."""
+    return weight.shape[1] % 256 == 0 and logits.stride(0) % 8 == 0 and \
+        logits.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0 and weight.is_contiguous()
+
+
+def head_dh(logits, targets, lse, weight, out, grad_scale, col_offset=0, out_rows=None,
+            accumulate=False, rows=None):
+    """dh = dlogits @ W on the tensor cores for the first `rows` rows of the fp16 logits slab
+    (columns col_offset .. of the vocabulary), dlogits = fp16((softmax - onehot) * grad_scale)
+    formed inside the GEMM from the logits and lse (tb_head_dh; reference: head.py:73-76 and
+    :113). Row r goes to out[out_rows[r]] (or out[r]); out fp32 (accumulated into when asked)
+    or fp16."""
+    rows = logits.shape[0] if rows is None else rows
+    cols, hidden = logits.shape[1], weight.shape[1]
+    dev = logits.device
+    if rows == 0:
+        return out
+    nbytes = _lib.load().tb_head_dh_workspace(rows, cols, hidden)
+    ws = torch.empty(max(nbytes, 16) // 4, dtype=torch.float32, device=dev)
+    rmap = None if out_rows is None else out_rows.to(torch.int64).contiguous()
+    _lib.call("tb_head_dh", _lib.ptr(logits), logits.stride(0), _lib.ptr(targets), _lib.ptr(lse),
+              rows, cols, col_offset, float(grad_scale), _lib.ptr(weight), hidden, _lib.ptr(ws),
+              nbytes, _lib.ptr(out), int(out.dtype == torch.float32), _lib.ptr(rmap),
+              out.stride(0), int(accumulate), _lib.stream_of(logits))
+    return out
+
+
+def _tc_head(h, weight, tgt, entropy, token_loss, correct, grad, order, n_labelled, scale,
              stream):
-    """All rows at once: tensor-core logits + partials, merge, then (labelled rows) dlogits in
-    place over the fp16 logits the GEMM kept and dh = dlogits . W (cuBLAS)."""
+    """All rows at once: tensor-core logits + partials, merge, then (labelled rows) the
+    gradient dh = dlogits . W into grad's unsorted rows."""
     rows, width = h.shape
     vocab = weight.shape[0]
     dev = h.device
     vt = -(-vocab // VOCAB_TILE)
     part = torch.empty((rows, vt, 6), dtype=torch.float32, device=dev)
     pidx = torch.empty((rows, vt), dtype=torch.int64, device=dev)
-    keep = n_labelled if grad_sorted is not None else 0
+    keep = n_labelled if grad is not None else 0
     logits = torch.empty((keep, vocab), dtype=torch.float16, device=dev) if keep else None
     _lib.call("tb_head_logits_stats", _lib.ptr(h), _lib.ptr(weight), _lib.ptr(tgt),
               _lib.ptr(logits), keep, _lib.ptr(part), _lib.ptr(pidx), rows, vocab, width, stream)
     lse = torch.empty(rows, dtype=torch.float32, device=dev)
     _lib.call("tb_head_merge", _lib.ptr(part), _lib.ptr(pidx), _lib.ptr(tgt), rows, 1, vt,
               _lib.ptr(lse), _lib.ptr(entropy), _lib.ptr(token_loss), _lib.ptr(correct), stream)
-    if keep:
-        _lib.call("tb_head_dlogits", _lib.ptr(logits), _lib.ptr(tgt), _lib.ptr(lse), keep, vocab,
-                  vocab, 0, float(scale), stream)
-        torch.matmul(logits, weight, out=grad_sorted)
+    if not keep:
+        return
+    if USE_TENSOR_CORE_DH and dh_supported(logits, weight):
+        head_dh(logits, tgt, lse, weight, grad, scale, out_rows=order[:keep])
+        return
+    _lib.call("tb_head_dlogits", _lib.ptr(logits), _lib.ptr(tgt), _lib.ptr(lse), keep, vocab,
+              vocab, 0, float(scale), stream)
+    grad.index_copy_(0, order[:keep], torch.matmul(logits, weight))
+
+
+# True: dh = dlogits . W through tb_head_dh (dlogits formed inside the tensor-core GEMM, never
+# written). Off by default: at config 4 the fused GEMM measured 1.11 ms against 0.57 ms for the
+# in-place dlogits pass + cuBLAS (it re-reads the fp16 logits once per 512 hidden columns and its
+# pipeline stays latency-bound, tensor pipe 29 % active). Same results either way within the
+# fp32 summation order; the tests run both.
+USE_TENSOR_CORE_DH = False
 
 
 def _grad_unit(denominator):
@@ -133,15 +175,17 @@ class FusedHeadLoss(torch.autograd.Function):
         correct = torch.empty(rows, dtype=torch.int32, device=dev)
         want_grad = ctx.needs_input_grad[0]
         unit = _grad_unit(denom)
-        grad_sorted = torch.empty((n_labelled, width), dtype=torch.float16, device=dev) \
-            if want_grad else None
+        grad = torch.zeros((rows, width), dtype=torch.float16, device=dev) if want_grad else None
+        grad_sorted = None
         stream = _lib.stream_of(hidden)
         if USE_TENSOR_CORE_HEAD and _tensor_core_ok(h, weight):
-            _tc_head(h, weight, tgt, entropy, token_loss, correct, grad_sorted, n_labelled,
+            _tc_head(h, weight, tgt, entropy, token_loss, correct, grad, order, n_labelled,
                      unit / max(denom, 1e-6), stream)
             rows_loop = range(0)
         else:
             rows_loop = range(0, rows, CHUNK_ROWS)
+            if want_grad:
+                grad_sorted = torch.empty((n_labelled, width), dtype=torch.float16, device=dev)
         for start in rows_loop:
             stop = min(rows, start + CHUNK_ROWS)
             logits = torch.matmul(h[start:stop], weight.t())
@@ -159,8 +203,8 @@ class FusedHeadLoss(torch.autograd.Function):
         else:
             loss = total / denominator
         if want_grad:
-            grad = torch.zeros((rows, width), dtype=torch.float16, device=dev)
-            grad.index_copy_(0, order[:n_labelled], grad_sorted)
+            if grad_sorted is not None:
+                grad.index_copy_(0, order[:n_labelled], grad_sorted)
             ctx.save_for_backward(grad)
         ctx.unit = unit
         unsort = torch.empty_like(order)
