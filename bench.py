@@ -266,13 +266,13 @@ class TrainStep:
 
     LOSS_SCALE = 1024.0
 
-    def __init__(self, model, world, bucket=None, opt=None):
+    def __init__(self, model, world, bucket=None, opt=None, dp_groups=0):
         from testt_b200.dist import GradBucket
         from testt_b200.qlora import lora_parameters
 
         self.model = model
         self.params = lora_parameters(model)
-        self.bucket = bucket or GradBucket(self.params)
+        self.bucket = bucket or GradBucket(self.params, overlap_groups=dp_groups)
         self.opt = opt or torch.optim.AdamW(self.params, lr=1e-4, fused=True, capturable=True)
         self.world = world
 
@@ -290,6 +290,7 @@ class TrainStep:
                 out = self.model(input_ids=ids, attention_mask=mask, labels=labels,
                                  num_items_in_batch=n_items)
         (out.loss * self.LOSS_SCALE).backward()
+        self.bucket.finish()
         self.bucket.flat.mul_(1.0 / self.LOSS_SCALE)
         self.post_backward()
         return out
@@ -563,8 +564,12 @@ def head_bench(device, reps, world):
     c = synth.config4(device)
     h = c["hidden"].clone().requires_grad_(True)
 
+    # the counts known on the host (as the captured step passes them): no synchronisation in
+    # the timed region
+    counts = (c["n_labelled"], float(c["n_labelled"]))
+
     def run():
-        loss, *_ = fused_head_loss(h, c["weight"], c["targets"], c["n_labelled"])
+        loss, *_ = fused_head_loss(h, c["weight"], c["targets"], c["n_labelled"], counts=counts)
         return loss
 
     run()
@@ -607,10 +612,22 @@ def sharded_head_bench(device, reps, world, rank):
         run()
     torch.cuda.synchronize()
     ms = time_region(run, reps, world, device) / reps
+    # the same calls once more with an event pair around each phase (untimed as a whole): the
+    # GEMM and each collective apart, mean per call, max over ranks
+    phases = {}
+    for _ in range(reps):
+        head.forward(c["hidden"], c["targets"], n_lab, counts=(n_lab, float(n_lab)),
+                     phases=phases)
+    torch.cuda.synchronize()
+    split = {}
+    for name in ("logits", "all_gather", "dh", "all_reduce"):
+        evs = phases.get(name, [])
+        t = sum(evs[i].elapsed_time(evs[i + 1]) for i in range(0, len(evs) - 1, 2)) / reps
+        split[name + "_ms"] = max_over_ranks(t, world, device)
     rows, hidden, vocab = 2048, synth.HIDDEN, synth.VOCAB
     flops = 2 * rows * hidden * vocab + 2 * n_lab * hidden * vocab
     return {"ms": ms, "tflops": flops / ms / 1e9, "flops": flops, "rows": rows,
-            "labelled": n_lab, "n_gpus": world, "shard_rows": hi - lo}
+            "labelled": n_lab, "n_gpus": world, "shard_rows": hi - lo, "phases": split}
 
 
 # ---- single kernels at configs 1-4 (--kernel) -------------------------------------------------
@@ -1010,7 +1027,7 @@ def ours_arm(args, rank, world, local):
     seq = synth.SEQ
     ids, mask, labels = make_batch(lengths, seq, cfg.vocab_size, 100 + rank, dev)
     tokens = sum(lengths)
-    step = TrainStep(model, world)
+    step = TrainStep(model, world, dp_groups=args.dp_groups if world > 1 else 0)
     from testt_b200.graphs import GraphedTrainStep
 
     graphed = GraphedTrainStep(model, step.bucket, loss_scale=TrainStep.LOSS_SCALE,
@@ -1133,6 +1150,10 @@ def ours_arm(args, rank, world, local):
                                "captured as one CUDA graph (testt_b200.graphs)",
                    "global_batch": 4 * world, "seq_len": seq, "tokens_per_gpu": tokens,
                    "lengths": lengths, "parallelism": f"dp{world}",
+                   "dp_exchange": ("one all-reduce of the LoRA gradients after the backward"
+                                   if world == 1 or args.dp_groups == 0 else
+                                   f"{args.dp_groups} groups of layers, each all-reduced on a "
+                                   "side stream once the backward has written them"),
                    "l2": "inputs larger than L2 (3.4 GB of NF4 weights streamed per step); "
                          "hot-path graphs: L2 flushed (256 MB read) before each replay"},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
@@ -1176,6 +1197,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    ap.add_argument("--dp-groups", type=int, default=4,
+                    help="N > 1: LoRA gradients all-reduced in this many groups of layers during "
+                         "the backward (0: one all-reduce after it)")
     ap.add_argument("--step-only", action="store_true",
                     help="time the captured training step only (for ncu launch lists)")
     ap.add_argument("--kernel", default=None,

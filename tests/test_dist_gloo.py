@@ -46,6 +46,34 @@ def _grad_bucket(rank, world, port, out):
     dist.destroy_process_group()
 
 
+def _grad_bucket_overlap(rank, world, port, out):
+    """Overlap mode: 7 parameters in 3 groups; gradients written in place (as the LoRA node
+    does) and reported in reverse order, a group's exchange starting when its last gradient is
+    reported; one group is never reported and is exchanged by finish(). Two steps in a row."""
+    _init(rank, world, port)
+    from testt_b200.dist import GradBucket
+    from testt_b200.lora import grads_written
+
+    shapes = [(2, 3), (4,), (3, 3), (5,), (2, 2), (6,), (1,)]
+    params = [torch.nn.Parameter(torch.zeros(s)) for s in shapes]
+    bucket = GradBucket(params, overlap_groups=3)
+    assert bucket._groups == [(0, 10), (10, 24), (24, 35)]
+    results = []
+    for step in range(2):
+        bucket.zero()
+        for i, p in enumerate(params):
+            p.grad.add_(float((rank + 1) * (i + 1) * (step + 1)))
+        started = []
+        for i in (6, 5, 4, 3, 2):  # groups 2 and 1 complete; group 0 (params 0, 1) does not
+            grads_written([params[i]])
+            started.append(list(bucket._started))
+        bucket.finish()
+        bucket.all_reduce(average=True)
+        results.append(([p.grad.clone() for p in params], started))
+    torch.save(results, os.path.join(out, f"o{rank}.pt"))
+    dist.destroy_process_group()
+
+
 def _sharded_head(rank, world, port, out):
     _init(rank, world, port)
     from oracle import ops
@@ -107,6 +135,21 @@ def test_grad_bucket_all_reduce_two_ranks(tmp_path):
     for a, b in zip(g0, g1):
         assert torch.equal(a, b)
         assert torch.allclose(a, torch.full_like(a, 1.5))
+
+
+def test_grad_bucket_overlapped_groups_two_ranks(tmp_path):
+    codes = _spawn(_grad_bucket_overlap, tmp_path)
+    assert codes == [0, 0]
+    r0 = torch.load(tmp_path / "o0.pt")
+    r1 = torch.load(tmp_path / "o1.pt")
+    for step, ((g0, started), (g1, _)) in enumerate(zip(r0, r1)):
+        for i, (a, b) in enumerate(zip(g0, g1)):
+            assert torch.equal(a, b)
+            # mean over ranks of (rank + 1) * (i + 1) * (step + 1)
+            assert torch.allclose(a, torch.full_like(a, 1.5 * (i + 1) * (step + 1)))
+        # group 2 (params 4..6) starts once param 4 is reported, group 1 once param 2 is
+        assert started == [[False, False, False], [False, False, False],
+                           [False, False, True], [False, False, True], [False, True, True]]
 
 
 def test_sharded_head_exchange_matches_full_vocab(tmp_path):

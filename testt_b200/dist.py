@@ -4,9 +4,11 @@ The reference runs on one GPU (its harness pins CUDA_VISIBLE_DEVICES=0); the two
 here are this build's:
 
 1. Token-row data parallelism. Every rank runs the whole step on its own batch; the only
-   exchange is one all-reduce of the LoRA gradients. `GradBucket` keeps every trainable gradient
-   as a view into one flat fp32 buffer (autograd accumulates into the views in place), so the
-   exchange is a single NCCL all-reduce of 8.7 MB for Qwen2.5-1.5B with r=16 on q/v.
+   exchange is the all-reduce of the LoRA gradients (8.7 MB for Qwen2.5-1.5B with r=16 on q/v).
+   `GradBucket` keeps every trainable gradient as a view into one flat fp32 buffer (the LoRA
+   node accumulates into the views in place); the exchange is one NCCL all-reduce after the
+   backward, or per group of layers during the backward (overlap_groups), each group's
+   all-reduce starting on a side stream as soon as the LoRA node has written its gradients.
 
 2. A vocabulary-sharded head. Rank r holds rows [lo_r, hi_r) of the tied head weight. Each rank
    computes its logits slab on the tensor cores with the per-row online-softmax state of every
@@ -36,21 +38,49 @@ def shard_range(vocab, rank, world):
 
 
 class GradBucket:
-    """All trainable gradients as views of one flat fp32 buffer, reduced with one all-reduce."""
+    """All trainable gradients as views of one flat fp32 buffer, summed over the ranks.
 
-    def __init__(self, params, group=None):
+    Without overlap (overlap_groups 0) one all-reduce of the whole buffer runs when all_reduce()
+    is called, after the backward. With overlap_groups = G > 0 (and more than one rank) the
+    buffer is cut into G contiguous groups of parameters; the LoRA node reports the gradients it
+    has finished (lora.grads_written) and, as soon as every gradient of a group is final, that
+    group's all-reduce is queued on a side stream behind an event of the current stream, so it
+    runs while the backward of the earlier layers continues. finish() queues the groups not yet
+    started and makes the current stream wait for the side stream. The same calls are captured
+    into a CUDA graph as they are made."""
+
+    def __init__(self, params, group=None, overlap_groups=0):
         self.params = [p for p in params if p.requires_grad]
         self.group = group
         total = sum(p.numel() for p in self.params)
         dev = self.params[0].device if self.params else torch.device("cpu")
         self.flat = torch.zeros(total, dtype=torch.float32, device=dev)
+        self._groups = []       # [lo, hi) element ranges of the flat buffer
+        self._group_of = {}     # id(param) -> group index
+        self._left = []         # per group, parameters still to report this backward
+        self._started = []
+        self._stream = None
+        if overlap_groups > 0 and self.params:
+            n = len(self.params)
+            g = min(overlap_groups, n)
+            bounds = [n * i // g for i in range(g + 1)]
+            off, starts = 0, []
+            for p in self.params:
+                starts.append(off)
+                off += p.numel()
+            starts.append(off)
+            for i in range(g):
+                self._groups.append((starts[bounds[i]], starts[bounds[i + 1]]))
+                for p in self.params[bounds[i]:bounds[i + 1]]:
+                    self._group_of[id(p)] = i
+            self._reset()
         self.attach()
 
     def attach(self):
         """(Re)point every param.grad at its slice of the flat buffer. The parameters are marked
         (lora.GRAD_IN_BUCKET) so the LoRA node accumulates their gradients into these views
-        inside its gradient GEMMs."""
-        from .lora import GRAD_IN_BUCKET
+        inside its gradient GEMMs; with overlap they also carry the bucket (lora.GRAD_BUCKET)."""
+        from .lora import GRAD_BUCKET, GRAD_IN_BUCKET
 
         off = 0
         for p in self.params:
@@ -59,20 +89,78 @@ class GradBucket:
             n = p.numel()
             p.grad = self.flat[off:off + n].view_as(p)
             setattr(p, GRAD_IN_BUCKET, True)
+            if self._groups:
+                setattr(p, GRAD_BUCKET, self)
             off += n
 
     def zero(self):
         self.flat.zero_()
 
+    def _world(self):
+        if not (dist.is_available() and dist.is_initialized()):
+            return 1
+        return dist.get_world_size(self.group)
+
+    def _reset(self):
+        self._left = [set() for _ in self._groups]
+        for p in self.params:
+            self._left[self._group_of[id(p)]].add(id(p))
+        self._started = [False] * len(self._groups)
+
+    def _start(self, i):
+        """Queue group i's all-reduce (on the side stream, after what the current stream has
+        queued so far, when on a GPU)."""
+        self._started[i] = True
+        lo, hi = self._groups[i]
+        part = self.flat[lo:hi]
+        if self.flat.is_cuda:
+            if self._stream is None:
+                self._stream = torch.cuda.Stream(device=self.flat.device)
+            self._stream.wait_stream(torch.cuda.current_stream(self.flat.device))
+            with torch.cuda.stream(self._stream):
+                dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
+        else:
+            dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
+
+    def grads_ready(self, params):
+        """The gradients of `params` are final for this backward: start every group they
+        complete (overlap mode with more than one rank; otherwise nothing happens here)."""
+        if not self._groups or self._world() <= 1:
+            return
+        for p in params:
+            i = self._group_of.get(id(p))
+            if i is None or self._started[i]:
+                continue
+            self._left[i].discard(id(p))
+            if not self._left[i]:
+                self._start(i)
+
+    def finish(self):
+        """Overlap mode: start the groups not started yet and make the current stream wait for
+        the exchange, so that what follows on it (unscaling, the optimizer) sees the sums. Call
+        it right after the backward, before anything else touches the buffer."""
+        if not self._groups or self._world() <= 1:
+            return
+        for i in range(len(self._groups)):
+            if not self._started[i]:
+                self._start(i)
+        if self.flat.is_cuda and self._stream is not None:
+            torch.cuda.current_stream(self.flat.device).wait_stream(self._stream)
+
     def all_reduce(self, average=True):
         """Sum (or average) the gradients over the group; a no-op without a process group."""
-        if not (dist.is_available() and dist.is_initialized()):
+        world = self._world()
+        if world <= 1:
+            if self._groups:
+                self._reset()
             return self.flat
-        world = dist.get_world_size(self.group)
-        if world > 1:
+        if self._groups:
+            self.finish()
+            self._reset()
+        else:
             dist.all_reduce(self.flat, op=dist.ReduceOp.SUM, group=self.group)
-            if average:
-                self.flat.div_(world)
+        if average:
+            self.flat.div_(world)
         return self.flat
 
 
@@ -148,9 +236,18 @@ class ShardedHead:
         self.chunk_rows = chunk_rows
         self.splits = splits
 
-    def forward(self, hidden16, targets, denominator, counts=None):
+    def forward(self, hidden16, targets, denominator, counts=None, phases=None):
         """`counts` = (labelled rows, denominator as a float) when the caller knows them on the
-        host: skips the one synchronisation (the targets are then trusted to be in range)."""
+        host: skips the one synchronisation (the targets are then trusted to be in range).
+        `phases`, a dict, receives a (start, end) pair of recorded CUDA events per phase of the
+        tensor-core path: "logits" (GEMM + statistics + fold), "all_gather" (the partial
+        states), "dh" (merge, dlogits, dh GEMM), "all_reduce" (dh)."""
+
+        def mark(name):
+            if phases is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                phases.setdefault(name, []).append(ev)
         _lib.require_cuda(hidden16, targets, self.weight, what="ShardedHead")
         rows, width = hidden16.shape
         dev = hidden16.device
@@ -173,8 +270,13 @@ class ShardedHead:
         cols = self.hi - self.lo
         stream = _lib.stream_of(hidden16)
         if USE_TENSOR_CORE_HEAD and _tensor_core_ok(h, self.weight):
+            mark("logits")
             folded, fidx, logits = shard_states(h, tgt, self.weight, self.lo, n_labelled, stream)
+            mark("logits")
+            mark("all_gather")
             gp, gi = exchange_partials(folded, fidx, self.group)
+            mark("all_gather")
+            mark("dh")
             _lib.call("tb_head_merge", _lib.ptr(gp), _lib.ptr(gi), _lib.ptr(tgt), rows,
                       self.world, 1, _lib.ptr(lse), _lib.ptr(entropy), _lib.ptr(token_loss),
                       _lib.ptr(correct), stream)
@@ -184,6 +286,7 @@ class ShardedHead:
                 _lib.call("tb_head_dlogits", _lib.ptr(logits), _lib.ptr(tgt), _lib.ptr(lse),
                           n_labelled, cols, cols, self.lo, scale, stream)
                 dh_sorted = torch.mm(logits, self.weight, out_dtype=torch.float32)
+            mark("dh")
             chunks = range(0)
         else:
             chunks = range(0, rows, self.chunk_rows)
@@ -207,7 +310,9 @@ class ShardedHead:
                           stream)
                 dh_sorted[start:start + lab] = torch.mm(logits[:lab], self.weight,
                                                         out_dtype=torch.float32)
+        mark("all_reduce")
         reduce_dh(dh_sorted, self.group)
+        mark("all_reduce")
         dh = torch.zeros((rows, width), dtype=torch.float16, device=dev)
         dh.index_copy_(0, order[:n_labelled], (dh_sorted * (1.0 / unit)).to(torch.float16))
         loss = token_loss.sum() / (denominator.to(dev) if torch.is_tensor(denominator)

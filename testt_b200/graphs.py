@@ -73,6 +73,7 @@ class GraphedTrainStep:
             out = self.model(input_ids=e.ids, attention_mask=e.mask, labels=e.labels,
                              num_items_in_batch=e.n_items)
         (out.loss * self.loss_scale).backward()
+        self.bucket.finish()  # with overlapped exchange: join it before touching the buffer
         self.bucket.flat.mul_(1.0 / self.loss_scale)
         if self.post_backward is not None:
             self.post_backward()

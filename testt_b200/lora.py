@@ -62,6 +62,22 @@ def _in_bucket(param):
         and g.is_contiguous() and g.device == param.device
 
 
+# Attribute a GradBucket that exchanges its gradients during the backward sets on its
+# parameters: the bucket, told by the LoRA node when the gradients it accumulated in place are
+# complete (`grads_written`), so that it can start their all-reduce.
+GRAD_BUCKET = "_testt_grad_bucket"
+
+
+def grads_written(params):
+    """Tells the buckets of `params` (the ones whose gradients this node just accumulated in
+    place) that those gradients are final for this backward."""
+    for p in params:
+        b = getattr(p, GRAD_BUCKET, None) if p is not None else None
+        if b is not None:
+            b.grads_ready([q for q in params if q is not None and _in_bucket(q)])
+            return
+
+
 def _dropout_of(module_dropout):
     """(p, training) of a peft dropout module (nn.Dropout or nn.Identity)."""
     if isinstance(module_dropout, torch.nn.Dropout):
@@ -197,6 +213,7 @@ class LoraPair(torch.autograd.Function):
                     _lib.call("tb_lora_dropout_grad", _lib.ptr(dxs[0]), _lib.ptr(dxs[1]),
                               _lib.ptr(mq), _lib.ptr(mv), _lib.ptr(slot_tok), _lib.ptr(gx),
                               ctx.slots, ctx.hidden, scale_q, scale_v, _lib.stream_of(gx))
+        grads_written([p for p, g in zip(ctx.params, grads) if g is None])
         return (gx, grads[0], grads[1], grads[2], grads[3], None, None, None)
 
 

@@ -15,7 +15,7 @@ import functools
 import torch
 
 from . import _lib
-from .lora import _F16, _RANK, LoraPair, _in_bucket
+from .lora import _F16, _RANK, LoraPair, _in_bucket, grads_written
 
 
 @functools.lru_cache(maxsize=None)
@@ -100,4 +100,5 @@ class LoraPairFused(LoraPair):
                           _lib.ptr(dhs[1]), _lib.ptr(a16s[1]), _lib.ptr(mq), _lib.ptr(mv),
                           _lib.ptr(slot_tok), _lib.ptr(gx), ctx.slots, ctx.hidden, _RANK,
                           scale_q, scale_v, _lib.stream_of(gx))
+        grads_written([p for p, g in zip(ctx.params, grads) if g is None])
         return (gx, grads[0], grads[1], grads[2], grads[3], None, None, None)
