@@ -770,6 +770,29 @@ def _kernel_case(name, device):
         nbytes = 0
         info = {"config": "4", "rows": rows, "labelled": n_lab,
                 "flops": 2 * rows * hidden * vocab + 2 * n_lab * hidden * vocab}
+    elif name in ("head_dh", "head_dh_cublas"):  # config 4's dh: tensor-core vs dlogits + cuBLAS
+        c = synth.config4(dev)
+        hidden, vocab = synth.HIDDEN, synth.VOCAB
+        n_lab = c["n_labelled"]
+        lab = c["targets"] != -100
+        tg = c["targets"][lab][:n_lab].to(torch.int64).contiguous()
+        z = (c["hidden"][lab][:n_lab].float() @ c["weight"].float().t()).half()
+        lse = torch.logsumexp(z.float(), -1)
+        out = torch.empty((n_lab, hidden), dtype=torch.float16, device=dev)
+        scale = 64.0 / n_lab
+        if name == "head_dh":
+            fn = lambda: head.head_dh(z, tg, lse, c["weight"], out, scale)  # noqa: E731
+        else:
+            work = z.clone()
+
+            def fn():
+                # in place: repeated calls rewrite already-converted values, the same work
+                _lib.call("tb_head_dlogits", _lib.ptr(work), _lib.ptr(tg), _lib.ptr(lse), n_lab,
+                          vocab, vocab, 0, scale, _lib.stream_of(work))
+                torch.matmul(work, c["weight"], out=out)
+        nbytes = 0
+        info = {"config": "4 (dh of the labelled rows)", "rows": n_lab,
+                "flops": 2 * n_lab * hidden * vocab}
     elif name == "head_cublas":  # the plain cuBLAS logits GEMM of config 4, for comparison
         c = synth.config4(dev)
         rows, hidden, vocab = 2048, synth.HIDDEN, synth.VOCAB
@@ -1206,7 +1229,8 @@ def main():
                     help="time one kernel at its configuration instead (nf4, nf4_nested, "
                          "rmsnorm_fwd, rmsnorm_bwd, rope_fwd, rope_bwd, swiglu_fwd, swiglu_bwd, "
                          "lora_fwd, attn_fwd, attn_fwd_bwd, "
-                         "head_stats, head_tc, head_full, head_cublas, all; staged kernels, "
+                         "head_stats, head_tc, head_full, head_cublas, head_dh, "
+                         "head_dh_cublas, all; the NF4-decoding GEMMs, "
                          "with what they replace: gate_up_fused_fwd, gate_up_fused_bwd, "
                          "gate_up_unpack_fwd, gate_up_unpack_bwd, mlp_fused_fwd, mlp_unpack_fwd, "
                          "qkv_rope_fused, qkv_unpack_rope, lora_bwd, lora_bwd_cublas)")
