@@ -322,6 +322,21 @@ int tb_attn_varlen_bwd(const uint16_t *q, const uint16_t *k, const uint16_t *v,
                        int64_t max_len, int32_t n_heads, int32_t n_kv, int32_t head_dim,
                        float scale, void *stream);
 
+/* tb_attn_varlen_bwd whose gradients leave through the rotary embedding's backward: instead of
+ * dq, dk, dv it writes dqkv fp16 [total, (n_heads + 2 n_kv) * 128] (row stride ld_qkv) =
+ * [rot^-1(dq) | rot^-1(dk) | dv] per token, what tb_rope_tokens_bwd writes from those fp16
+ * gradients (solution/rope.py:78-128, token-major): each gradient rounded to fp16, then
+ * (g1 c1 + g2 s2, g2 c2 - g1 s1) with cos, sin fp32 [seq, 128] at t = pos_idx[token] % seq; a
+ * position outside [0, slots) gives a zero row. The dq / dk / dv tensors and the separate
+ * rotation pass are never materialised. */
+int tb_attn_varlen_bwd_rope(const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                            const uint16_t *out, const uint16_t *dout, const float *lse,
+                            const int32_t *cu_seqlens, const float *cos, const float *sin,
+                            const int64_t *pos_idx, int64_t seq, int64_t slots, uint16_t *dqkv,
+                            int64_t ld_qkv, float *delta, float *dk_part, float *dv_part,
+                            int64_t batch, int64_t total, int64_t max_len, int32_t n_heads,
+                            int32_t n_kv, int32_t head_dim, float scale, void *stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Gated SiLU. Replaces gated_silu_fwd_kernel / gated_silu_bwd_inplace_kernel,
  * solution/mlp.py:31-58 and :61-77.

@@ -81,3 +81,39 @@ def test_attention_backward_is_deterministic():
         grads.append((qq.grad, kk.grad, vv.grad))
     for a, b in zip(*grads):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("lengths", [[149, 131, 193, 148], [1, 64, 65, 7, 200]])
+def test_attention_backward_through_rope_matches_the_separate_kernels(lengths):
+    """rope_varlen_attention (one node, tb_attn_varlen_bwd_rope: dqkv written through the rotary
+    embedding's backward from inside the attention backward) against rope_tokens followed by
+    varlen_attention (tb_attn_varlen_bwd, then tb_rope_tokens_bwd): the same forward, and the
+    q|k|v and LoRA-row gradients within 1 fp16 ulp."""
+    from helpers import assert_ulp
+    from oracle import ops
+    from testt_b200 import attention, rope
+
+    nh, nkv, seq = 12, 2, 512
+    total = sum(lengths)
+    batch = len(lengths)
+    g = torch.Generator(device=DEV).manual_seed(total)
+    qkv = torch.randn(total, (nh + 2 * nkv) * 128, device=DEV, generator=g).half()
+    lq = (torch.randn(total, nh * 128, device=DEV, generator=g) * 0.01).half()
+    lv = (torch.randn(total, nkv * 128, device=DEV, generator=g) * 0.01).half()
+    pos = torch.cat([torch.arange(n) + b * seq for b, n in enumerate(lengths)]).to(DEV)
+    cos, sin = (t.to(DEV) for t in ops.rope_tables(seq, 128, 1e6))
+    cu = torch.zeros(batch + 1, dtype=torch.int32, device=DEV)
+    cu[1:] = torch.tensor(lengths, device=DEV).cumsum(0)
+    scale = 1.0 / math.sqrt(128)
+    dout = (torch.randn(total, nh, 128, device=DEV, generator=g) * 0.1).half()
+    ins_a = [t.clone().requires_grad_(True) for t in (qkv, lq, lv)]
+    ins_b = [t.clone().requires_grad_(True) for t in (qkv, lq, lv)]
+    out_a = attention.rope_varlen_attention(*ins_a, cos, sin, pos, batch, seq, nh, nkv, cu,
+                                            max(lengths), scale)
+    q, k, v = rope.rope_tokens(*ins_b, cos, sin, pos, batch, seq, nh, nkv, 128)
+    out_b = attention.varlen_attention(q, k, v, cu, max(lengths), scale)
+    assert torch.equal(out_a, out_b)
+    out_a.backward(dout)
+    out_b.backward(dout)
+    for a, b, name in zip(ins_a, ins_b, ("dqkv", "dlora_q", "dlora_v")):
+        assert_ulp(a.grad, b.grad, 1, name)

@@ -43,6 +43,8 @@ SIGNATURES = {
     "tb_attn_varlen_fwd": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _F, _P],
     "tb_attn_varlen_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64,
                            _I32, _I32, _I32, _F, _P],
+    "tb_attn_varlen_bwd_rope": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _P, _I64, _P,
+                                _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _F, _P],
     "tb_swiglu_fwd": [_P, _P, _I64, _I64, _P],
     "tb_swiglu_bwd_inplace": [_P, _P, _I64, _I64, _P],
     "tb_head_stats_grad": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P],

@@ -66,3 +66,57 @@ def varlen_attention(q, k, v, cu_seqlens, max_len, scale):
     """Causal attention over the packed sequences of cu_seqlens (int32 [batch + 1]) for
     token-major fp16 q [T, H, 128], k, v [T, Hkv, 128]; differentiable in q, k, v."""
     return VarlenAttention.apply(q, k, v, cu_seqlens, max_len, scale)
+
+
+class RopeVarlenAttention(torch.autograd.Function):
+    """The token-major rotary pack (rope.rope_tokens) and the attention over it as one node: the
+    forward runs tb_rope_tokens_fwd and tb_attn_varlen_fwd; the backward, tb_attn_varlen_bwd_rope,
+    writes the q|k|v gradient dqkv [T, (H + 2 Hkv) * 128] straight from the attention backward
+    through the rotary embedding's backward (no dq / dk / dv tensors, no tb_rope_tokens_bwd).
+    Returns the gradients rope_tokens' backward returns: dqkv and, for the LoRA rows, views of
+    its q and v columns (solution/rope.py:174-175)."""
+
+    @staticmethod
+    def forward(ctx, qkv, lora_q, lora_v, cos, sin, pos_idx, batch, seq, n_heads, n_kv,
+                cu_seqlens, max_len, scale):
+        from .rope import tokens_forward
+
+        q, k, v, cos, sin, pos_idx = tokens_forward(qkv, lora_q, lora_v, cos, sin, pos_idx,
+                                                    batch, seq, n_heads, n_kv, HEAD_DIM)
+        out, lse = attn_forward(q, k, v, cu_seqlens, max_len, scale)
+        ctx.save_for_backward(q, k, v, out, lse, cu_seqlens, cos, sin, pos_idx)
+        ctx.dims = (batch, seq, n_heads, n_kv, int(max_len), float(scale))
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, out, lse, cu, cos, sin, pos_idx = ctx.saved_tensors
+        batch, seq, nh, nkv, max_len, scale = ctx.dims
+        need_qkv, need_lq, need_lv = ctx.needs_input_grad[:3]
+        none = (None,) * 10
+        if not (need_qkv or need_lq or need_lv):
+            return (None, None, None) + none
+        total, d = q.shape[0], q.shape[2]
+        dout = dout.contiguous().to(torch.float16)
+        dqkv = torch.empty((total, (nh + 2 * nkv) * d), dtype=torch.float16, device=q.device)
+        delta = torch.empty((nh, total), dtype=torch.float32, device=q.device)
+        dk_part = torch.empty((total, nh, d), dtype=torch.float32, device=q.device)
+        dv_part = torch.empty_like(dk_part)
+        _lib.call("tb_attn_varlen_bwd_rope", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(out),
+                  _lib.ptr(dout), _lib.ptr(lse), _lib.ptr(cu), _lib.ptr(cos), _lib.ptr(sin),
+                  _lib.ptr(pos_idx), seq, batch * seq, _lib.ptr(dqkv), dqkv.stride(0),
+                  _lib.ptr(delta), _lib.ptr(dk_part), _lib.ptr(dv_part), cu.numel() - 1, total,
+                  max_len, nh, nkv, d, scale, _lib.stream_of(q))
+        q_cols, v_start = nh * d, (nh + nkv) * d
+        return ((dqkv if need_qkv else None), (dqkv[:, :q_cols] if need_lq else None),
+                (dqkv[:, v_start:] if need_lv else None)) + none
+
+
+def rope_varlen_attention(qkv, lora_q, lora_v, cos, sin, pos_idx, batch, seq, n_heads, n_kv,
+                          cu_seqlens, max_len, scale):
+    """varlen_attention(*rope_tokens(qkv, lora_q, lora_v, ...)) as one node whose backward
+    writes the q|k|v gradient through the rotary embedding's backward directly."""
+    return RopeVarlenAttention.apply(
+        qkv.contiguous(), lora_q.contiguous() if lora_q is not None else None,
+        lora_v.contiguous() if lora_v is not None else None, cos, sin, pos_idx, batch, seq,
+        n_heads, n_kv, cu_seqlens, max_len, scale)

@@ -311,7 +311,35 @@ struct BwdArgs {
   int64_t total;
   int n_heads, n_kv;
   float scale, scale_log2;
+  // With dqkv set (tb_attn_varlen_bwd_rope), the gradients leave through the rotary embedding's
+  // backward instead: dqkv[token] = [rot^-1(dq) | rot^-1(dk) | dv] (row stride ld_qkv), each
+  // gradient rounded to fp16 first, then rotated back with the token's position
+  // (t = pos_idx % seq; a position outside [0, slots) gives a zero row), as tb_rope_tokens_bwd
+  // does with the stored fp16 gradients.
+  uint16_t *dqkv;
+  int64_t ld_qkv;
+  const float *cosv, *sinv;  // [seq, 128]
+  const int64_t *pos_idx;    // [total]
+  int64_t seq, slots;
 };
+
+// The table row of a token's position for the rotary embedding's backward; -1 without one.
+__device__ __forceinline__ int64_t rope_row(const BwdArgs &a, int64_t token) {
+  const int64_t pos = __ldg(a.pos_idx + token);
+  return (pos >= 0 && pos < a.slots) ? pos % a.seq : -1;
+}
+
+// (o1, o2) = (g1 c1 + g2 s2, g2 c2 - g1 s1) for the column pair (p, p + 64) of table row tp,
+// from fp16-rounded gradients (tb_rope_tokens_bwd's arithmetic)
+__device__ __forceinline__ void rope_back(const BwdArgs &a, int64_t tp, int p, float g1, float g2,
+                                          float &o1, float &o2) {
+  g1 = __half2float(__float2half_rn(g1));
+  g2 = __half2float(__float2half_rn(g2));
+  const float c1 = __ldg(a.cosv + tp * kD + p), c2 = __ldg(a.cosv + tp * kD + 64 + p);
+  const float s1 = __ldg(a.sinv + tp * kD + p), s2 = __ldg(a.sinv + tp * kD + 64 + p);
+  o1 = g1 * c1 + g2 * s2;
+  o2 = g2 * c2 - g1 * s1;
+}
 
 __global__ void __launch_bounds__(kCtaThreads) attn_bwd_dq_kernel(const __grid_constant__ BwdArgs a) {
   pdl_wait();
@@ -466,6 +494,31 @@ __global__ void __launch_bounds__(kCtaThreads) attn_bwd_dq_kernel(const __grid_c
   for (int nt = 0; nt < 16; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; ++e) dq[nt][e] += mg[(nt * 4 + e) * 128 + slot];
+  if (a.dqkv != nullptr) {
+    // through the rotary embedding's backward: columns nt * 8 + 2t (+1) and the same + 64
+    // (fragment nt + 8) are a rotation pair, both in this thread
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int row = r == 0 ? row0 : row1;
+      if (row >= len) continue;
+      const int64_t token = start + row;
+      const int64_t tp = rope_row(a, token);
+      uint32_t *op = reinterpret_cast<uint32_t *>(a.dqkv + token * a.ld_qkv + h * kD);
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        float o1[2] = {0.f, 0.f}, o2[2] = {0.f, 0.f};
+        if (tp >= 0) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e)
+            rope_back(a, tp, nt * 8 + 2 * t + e, dq[nt][2 * r + e] * a.scale,
+                      dq[nt + 8][2 * r + e] * a.scale, o1[e], o2[e]);
+        }
+        op[nt * 4 + t] = pack_half2(o1[0], o1[1]);
+        op[(nt + 8) * 4 + t] = pack_half2(o2[0], o2[1]);
+      }
+    }
+    return;
+  }
   if (row0 < len) {
     uint32_t *op = reinterpret_cast<uint32_t *>(a.dq + (int64_t)(start + row0) * ldq + h * kD);
 #pragma unroll
@@ -695,6 +748,57 @@ __global__ void __launch_bounds__(256) attn_bwd_gsum_kernel(const float *__restr
   }
 }
 
+// The same sums, leaving through the rotary embedding's backward into dqkv: a thread takes 4
+// columns c .. c + 3 (c < 64) and their rotation partners c + 64 .. of one (token, key/value
+// head); dK rotated back, dV as it is.
+__global__ void __launch_bounds__(256) attn_bwd_gsum_rope_kernel(const __grid_constant__ BwdArgs a) {
+  pdl_wait();
+  pdl_release();
+  const int group = a.n_heads / a.n_kv;
+  constexpr int kVecs = kD / 8;  // 16 vectors of 4 in the first half of a head
+  const int64_t nvec = a.total * a.n_kv * kVecs;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t tok = i / (a.n_kv * kVecs);
+    const int rem = (int)(i - tok * (a.n_kv * kVecs));
+    const int hk = rem / kVecs, c = (rem % kVecs) * 4;
+    const int64_t src = tok * (int64_t)a.n_heads * kD + (int64_t)hk * group * kD + c;
+    float k1[4] = {0.f, 0.f, 0.f, 0.f}, k2[4] = {0.f, 0.f, 0.f, 0.f};
+    float v1[4] = {0.f, 0.f, 0.f, 0.f}, v2[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < group; ++j) {
+      const int64_t o = src + (int64_t)j * kD;
+      const float4 xk1 = __ldg(reinterpret_cast<const float4 *>(a.dk_part + o));
+      const float4 xk2 = __ldg(reinterpret_cast<const float4 *>(a.dk_part + o + 64));
+      const float4 xv1 = __ldg(reinterpret_cast<const float4 *>(a.dv_part + o));
+      const float4 xv2 = __ldg(reinterpret_cast<const float4 *>(a.dv_part + o + 64));
+      k1[0] += xk1.x; k1[1] += xk1.y; k1[2] += xk1.z; k1[3] += xk1.w;
+      k2[0] += xk2.x; k2[1] += xk2.y; k2[2] += xk2.z; k2[3] += xk2.w;
+      v1[0] += xv1.x; v1[1] += xv1.y; v1[2] += xv1.z; v1[3] += xv1.w;
+      v2[0] += xv2.x; v2[1] += xv2.y; v2[2] += xv2.z; v2[3] += xv2.w;
+    }
+    const int64_t tp = rope_row(a, tok);
+    float o1[4], o2[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (tp >= 0) {
+        rope_back(a, tp, c + e, k1[e], k2[e], o1[e], o2[e]);
+      } else {
+        o1[e] = o2[e] = 0.f;
+        v1[e] = v2[e] = 0.f;
+      }
+    }
+    uint16_t *row = a.dqkv + tok * a.ld_qkv;
+    uint16_t *dk = row + (int64_t)(a.n_heads + hk) * kD + c;
+    uint16_t *dv = row + (int64_t)(a.n_heads + a.n_kv + hk) * kD + c;
+    *reinterpret_cast<uint2 *>(dk) = make_uint2(pack_half2(o1[0], o1[1]), pack_half2(o1[2], o1[3]));
+    *reinterpret_cast<uint2 *>(dk + 64) =
+        make_uint2(pack_half2(o2[0], o2[1]), pack_half2(o2[2], o2[3]));
+    *reinterpret_cast<uint2 *>(dv) = make_uint2(pack_half2(v1[0], v1[1]), pack_half2(v1[2], v1[3]));
+    *reinterpret_cast<uint2 *>(dv + 64) =
+        make_uint2(pack_half2(v2[0], v2[1]), pack_half2(v2[2], v2[3]));
+  }
+}
+
 int check_attn(const char *what, const void *q, const void *k, const void *v, const int32_t *cu,
                int64_t batch, int64_t total, int64_t max_len, int32_t n_heads, int32_t n_kv,
                int32_t head_dim) {
@@ -759,7 +863,7 @@ extern "C" int tb_attn_varlen_bwd(const uint16_t *q, const uint16_t *k, const ui
     return check_launch("attn_varlen_bwd attribute");
   BwdArgs a{q,     k,      v,       out,     dout,    lse,     cu_seqlens,
             delta, dq,     dk_part, dv_part, total,   n_heads, n_kv,
-            scale, scale * 1.4426950408889634f};
+            scale, scale * 1.4426950408889634f, nullptr, 0, nullptr, nullptr, nullptr, 0, 0};
   const dim3 grid((unsigned)((max_len + kBlock - 1) / kBlock), (unsigned)n_heads, (unsigned)batch);
   cudaStream_t st = as_stream(stream);
   rc = launch("attn_varlen_bwd dq", attn_bwd_dq_kernel, grid, kCtaThreads, smem, st, a);
@@ -772,4 +876,51 @@ extern "C" int tb_attn_varlen_bwd(const uint16_t *q, const uint16_t *k, const ui
   return launch("attn_varlen_bwd gsum", attn_bwd_gsum_kernel, (unsigned)blocks, 256, 0, st,
                 (const float *)dk_part, (const float *)dv_part, dk, dv, total, (int)n_heads,
                 (int)n_kv);
+}
+
+// tb_attn_varlen_bwd whose gradients leave through the rotary embedding's backward: writes
+// dqkv [total, (n_heads + 2 n_kv) * 128] (row stride ld_qkv) = what tb_rope_tokens_bwd writes
+// from the dq, dk, dv tb_attn_varlen_bwd would write, without storing those.
+extern "C" int tb_attn_varlen_bwd_rope(const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                                       const uint16_t *out, const uint16_t *dout, const float *lse,
+                                       const int32_t *cu_seqlens, const float *cos,
+                                       const float *sin, const int64_t *pos_idx, int64_t seq,
+                                       int64_t slots, uint16_t *dqkv, int64_t ld_qkv,
+                                       float *delta, float *dk_part, float *dv_part,
+                                       int64_t batch, int64_t total, int64_t max_len,
+                                       int32_t n_heads, int32_t n_kv, int32_t head_dim,
+                                       float scale, void *stream) {
+  int rc = check_attn("attn_varlen_bwd_rope", q, k, v, cu_seqlens, batch, total, max_len,
+                      n_heads, n_kv, head_dim);
+  if (rc != TB_OK) return rc;
+  if (!out || !dout || !lse || !cos || !sin || !pos_idx || !dqkv || !delta || !dk_part ||
+      !dv_part)
+    return set_error(TB_EINVAL, "attn_varlen_bwd_rope: every buffer is required");
+  if (seq <= 0 || slots < 0 || ld_qkv < (int64_t)(n_heads + 2 * n_kv) * kD || ld_qkv % 8 != 0)
+    return set_error(TB_EINVAL, "attn_varlen_bwd_rope: seq %lld slots %lld ld_qkv %lld",
+                     (long long)seq, (long long)slots, (long long)ld_qkv);
+  if (!aligned(out, 16) || !aligned(dout, 16) || !aligned(dqkv, 16) || !aligned(dk_part, 16) ||
+      !aligned(dv_part, 16))
+    return set_error(TB_EALIGN, "attn_varlen_bwd_rope: 16-byte aligned buffers are required");
+  if (batch == 0 || total == 0 || max_len == 0) return TB_OK;
+  const size_t smem = 10 * kTileHalves * sizeof(uint16_t);
+  if (cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess ||
+      cudaFuncSetAttribute(attn_bwd_dkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return check_launch("attn_varlen_bwd_rope attribute");
+  BwdArgs a{q,     k,      v,       out,     dout,    lse,     cu_seqlens,
+            delta, nullptr, dk_part, dv_part, total,  n_heads, n_kv,
+            scale, scale * 1.4426950408889634f, dqkv, ld_qkv, cos, sin, pos_idx, seq, slots};
+  const dim3 grid((unsigned)((max_len + kBlock - 1) / kBlock), (unsigned)n_heads, (unsigned)batch);
+  cudaStream_t st = as_stream(stream);
+  rc = launch("attn_varlen_bwd_rope dq", attn_bwd_dq_kernel, grid, kCtaThreads, smem, st, a);
+  if (rc != TB_OK) return rc;
+  rc = launch("attn_varlen_bwd_rope dkv", attn_bwd_dkv_kernel, grid, kCtaThreads, smem, st, a);
+  if (rc != TB_OK) return rc;
+  const int64_t nvec = total * n_kv * (kD / 8);
+  int64_t blocks = (nvec + 255) / 256;
+  if (blocks > (int64_t)sm_count() * 8) blocks = (int64_t)sm_count() * 8;
+  return launch("attn_varlen_bwd_rope gsum", attn_bwd_gsum_rope_kernel, (unsigned)blocks, 256,
+                0, st, a);
 }

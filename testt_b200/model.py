@@ -13,8 +13,9 @@ Per decoder layer, with s the fp32 residual stream of the M real tokens:
     lq, lv     = LoRA(dropout(y_pad))                 lora.lora_pair: PyTorch dropout (same draws),
                                                       tb_lora_gather, cuBLAS; tb_lora_dropout_grad
     q, k, v    = rope_tokens(qkv, lq, lv)             tb_rope_tokens_fwd, token-major [M, H, 128]
-    a          = varlen causal attention(q, k, v)     tb_attn_varlen_fwd / _bwd (sm_100, head
-                                                      dim 128)
+    a          = varlen causal attention(q, k, v)     tb_attn_varlen_fwd / tb_attn_varlen_bwd_rope
+                                                      (sm_100, head dim 128; the backward writes
+                                                      d(qkv) through the rotation's backward)
     o          = a @ Wo^T                             cuBLAS
     s, y2, _   = add_rmsnorm(s, o)                    tb_add_rmsnorm_fwd
     d          = mlp(y2)                              cuBLAS + tb_swiglu_fwd
@@ -56,6 +57,11 @@ def _varlen_available(head_dim, device):
 # causal attention over each sequence's real tokens (token-major) through the library's own
 # kernels where they take the model; False keeps the reference's padded layout and SDPA
 USE_VARLEN_ATTENTION = True
+
+# With variable-length attention, the rotary pack and the attention as one node whose backward
+# leaves through the rotary embedding's backward (tb_attn_varlen_bwd_rope: no dq / dk / dv
+# tensors, no tb_rope_tokens_bwd launch); False keeps the two nodes (same values).
+USE_ROPE_IN_ATTENTION_BWD = True
 
 # Keep each layer's fp16 weights, unpacked once per step in the forward, for the backward (2.6 GB
 # for Qwen2.5-1.5B, released layer by layer as the backward passes), instead of unpacking them
@@ -363,7 +369,15 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
         lora_q, lora_v = lora_pair(_lora_parts(lp.attn.q_proj), _lora_parts(lp.attn.v_proj),
                                    y_pad, pos_idx, slot_tok)
         del y_pad
-        if varlen:
+        if varlen and USE_ROPE_IN_ATTENTION_BWD:
+            # one node: its backward writes the q|k|v gradient through the rotary embedding's
+            # backward from inside the attention backward
+            attn = _own_attn.rope_varlen_attention(qkv, lora_q, lora_v, cos, sin, pos_idx, batch,
+                                                   seq, plan.n_heads, plan.n_kv, cu_seqlens,
+                                                   max_len, lp.attn.scaling)
+            del qkv, lora_q, lora_v
+            attn = attn.reshape(tokens, plan.n_heads * plan.head_dim)
+        elif varlen:
             q, k, v = rope_tokens(qkv, lora_q, lora_v, cos, sin, pos_idx, batch, seq,
                                   plan.n_heads, plan.n_kv, plan.head_dim)
             del qkv, lora_q, lora_v

@@ -89,6 +89,30 @@ class RopePack(torch.autograd.Function):
                 None, None, None, None, None, None, None, None, None)
 
 
+def tokens_forward(qkv, lora_q, lora_v, cos, sin, pos_idx, batch, seq, n_heads, n_kv, head_dim):
+    """tb_rope_tokens_fwd: (q, k, v) token-major and the fp32 tables / int64 positions it used."""
+    _lib.require_cuda(qkv, lora_q, lora_v, cos, sin, pos_idx, what="rope_tokens")
+    if qkv.dtype != torch.float16:
+        raise TypeError(f"rope_tokens: qkv must be fp16, got {qkv.dtype}")
+    rows = qkv.shape[0]
+    if qkv.shape[1] != (n_heads + 2 * n_kv) * head_dim:
+        raise ValueError(f"rope_tokens: qkv has {qkv.shape[1]} columns")
+    dev = qkv.device
+    cos = cos.to(torch.float32).contiguous()
+    sin = sin.to(torch.float32).contiguous()
+    if pos_idx.dtype != torch.int64:
+        pos_idx = pos_idx.to(torch.int64)
+    q = torch.empty((rows, n_heads, head_dim), dtype=torch.float16, device=dev)
+    k = torch.empty((rows, n_kv, head_dim), dtype=torch.float16, device=dev)
+    v = torch.empty((rows, n_kv, head_dim), dtype=torch.float16, device=dev)
+    lq, lv, fp32 = _lora_pair(lora_q, lora_v)
+    if rows:
+        _lib.call("tb_rope_tokens_fwd", _lib.ptr(qkv), _lib.ptr(lq), _lib.ptr(lv), fp32,
+                  _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(pos_idx), _lib.ptr(q), _lib.ptr(k),
+                  _lib.ptr(v), rows, batch, seq, n_heads, n_kv, head_dim, _lib.stream_of(qkv))
+    return q, k, v, cos, sin, pos_idx
+
+
 class RopeTokens(torch.autograd.Function):
     """rope_pack's arithmetic with token-major outputs: q [rows, n_heads, d], k and v
     [rows, n_kv, d], the packed layout of variable-length attention."""
@@ -96,26 +120,9 @@ class RopeTokens(torch.autograd.Function):
     @staticmethod
     def forward(ctx, qkv, lora_q, lora_v, cos, sin, pos_idx, batch, seq, n_heads, n_kv,
                 head_dim):
-        _lib.require_cuda(qkv, lora_q, lora_v, cos, sin, pos_idx, what="rope_tokens")
-        if qkv.dtype != torch.float16:
-            raise TypeError(f"rope_tokens: qkv must be fp16, got {qkv.dtype}")
         rows = qkv.shape[0]
-        if qkv.shape[1] != (n_heads + 2 * n_kv) * head_dim:
-            raise ValueError(f"rope_tokens: qkv has {qkv.shape[1]} columns")
-        dev = qkv.device
-        cos = cos.to(torch.float32).contiguous()
-        sin = sin.to(torch.float32).contiguous()
-        if pos_idx.dtype != torch.int64:
-            pos_idx = pos_idx.to(torch.int64)
-        q = torch.empty((rows, n_heads, head_dim), dtype=torch.float16, device=dev)
-        k = torch.empty((rows, n_kv, head_dim), dtype=torch.float16, device=dev)
-        v = torch.empty((rows, n_kv, head_dim), dtype=torch.float16, device=dev)
-        lq, lv, fp32 = _lora_pair(lora_q, lora_v)
-        if rows:
-            _lib.call("tb_rope_tokens_fwd", _lib.ptr(qkv), _lib.ptr(lq), _lib.ptr(lv), fp32,
-                      _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(pos_idx), _lib.ptr(q), _lib.ptr(k),
-                      _lib.ptr(v), rows, batch, seq, n_heads, n_kv, head_dim,
-                      _lib.stream_of(qkv))
+        q, k, v, cos, sin, pos_idx = tokens_forward(qkv, lora_q, lora_v, cos, sin, pos_idx,
+                                                    batch, seq, n_heads, n_kv, head_dim)
         ctx.save_for_backward(cos, sin, pos_idx)
         ctx.dims = (rows, batch, seq, n_heads, n_kv, head_dim)
         return q, k, v
