@@ -16,7 +16,8 @@ Printed on rank 0, one JSON line:
   e2e        the same step, the batch copied from pinned host memory every step and the loss
              and statistics read back (the path a training loop takes)
   hot_path   the fused memory-bound kernels of one step (NF4 unpack, add+RMSNorm, RoPE pack,
-             SwiGLU, fwd + bwd, 28 layers), replayed as a CUDA graph: GB/s against HBM peak
+             SwiGLU, fwd + bwd, 28 layers; the RoPE backward only where the step launches it on
+             its own), replayed as a CUDA graph: GB/s against HBM peak
   roofline   the dominant hot-path kernel (NF4 unpack): algorithmic bytes / measured time
   head       the vocabulary head of config 4 (2048 rows, 1331 labelled): TFLOP/s
   head_sharded  (N > 1) config 4 with the head weight vocabulary-sharded over the N GPUs
@@ -321,8 +322,8 @@ class HotPath:
 
     def __init__(self, model, lengths, seq, device):
         from testt_b200 import _lib, nf4
+        from testt_b200.model import USE_ROPE_IN_ATTENTION_BWD, model_plan
         from testt_b200.model import USE_VARLEN_ATTENTION as varlen
-        from testt_b200.model import model_plan
 
         self.lib = _lib
         plan = model_plan(model)
@@ -341,8 +342,12 @@ class HotPath:
         def rnd(shape, dtype, std=1.0):
             return (torch.randn(shape, generator=g, device=dev) * std).to(dtype)
 
+        # the step's variable-length path runs the RoPE backward inside the attention backward
+        # (tb_attn_varlen_bwd_rope), so it has no launch of its own there
+        rope_in_attention = bool(varlen and USE_ROPE_IN_ATTENTION_BWD)
         self.groups = {k: [] for k in ("nf4_unpack", "rmsnorm_fwd", "rmsnorm_bwd", "rope_fwd",
-                                       "rope_bwd", "swiglu_fwd", "swiglu_bwd")}
+                                       "rope_bwd", "swiglu_fwd", "swiglu_bwd")
+                       if not (k == "rope_bwd" and rope_in_attention)}
         self.bytes = {k: 0 for k in self.groups}
         self.keep = []
         cos, sin = (t.to(dev) for t in synth._rope(seq, dev))
@@ -461,13 +466,14 @@ class HotPath:
                 add("rope_fwd", nb, "tb_rope_pack_fwd", _lib.ptr(qkv), _lib.ptr(lq),
                     _lib.ptr(lv), 0, _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(pos),
                     _lib.ptr(slot), _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), m, b, seq, nh, nkv, d)
-            dq, dk, dv = rnd(q.shape, f16), rnd(k.shape, f16), rnd(v.shape, f16)
-            dqkv = torch.empty((m, width), dtype=f16, device=dev)
-            self.keep += [dq, dk, dv, dqkv]
-            nb = m * width * 2 * 2 + m * 8 + 2 * seq * d * 4
-            add("rope_bwd", nb, "tb_rope_tokens_bwd" if varlen else "tb_rope_pack_bwd",
-                _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv), _lib.ptr(cos), _lib.ptr(sin),
-                _lib.ptr(pos), _lib.ptr(dqkv), m, b, seq, nh, nkv, d)
+            if not rope_in_attention:
+                dq, dk, dv = rnd(q.shape, f16), rnd(k.shape, f16), rnd(v.shape, f16)
+                dqkv = torch.empty((m, width), dtype=f16, device=dev)
+                self.keep += [dq, dk, dv, dqkv]
+                nb = m * width * 2 * 2 + m * 8 + 2 * seq * d * 4
+                add("rope_bwd", nb, "tb_rope_tokens_bwd" if varlen else "tb_rope_pack_bwd",
+                    _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv), _lib.ptr(cos), _lib.ptr(sin),
+                    _lib.ptr(pos), _lib.ptr(dqkv), m, b, seq, nh, nkv, d)
             # SwiGLU
             gu = rnd((m, 2 * inter), f16)
             act = torch.empty((m, inter), dtype=f16, device=dev)

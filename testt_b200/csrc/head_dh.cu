@@ -15,20 +15,22 @@
 // 64 x 32), two M128 N256 K16 instructions per 16 columns into two TMEM accumulators (512
 // columns, all of TMEM).
 //
-// Work split: every 128-row tile of dh gets C CTAs (C = SMs / row tiles) that divide its
-// (hidden group of 512, vocabulary block of 32) work units into C contiguous ranges. CTA j of
-// every row tile covers the same units at the same time, so each W block is read from HBM about
-// once and served to the other row tiles from L2. A range crosses at most a few hidden groups;
-// per group it covers, a CTA writes its fp32 partial (128 x 512) to the caller's workspace, and
-// head_dh_reduce sums the partials of each group in CTA order (deterministic), maps rows and
-// writes fp32 or fp16.
+// Work split: CTA (s, t, g) computes the fp32 partial of row tile t and hidden group g (512
+// columns) over the s-th of S contiguous vocabulary ranges (S = SMs / (row tiles x groups), at
+// least 1). Block indices put the group fastest, then the row tile, then the range: the CTAs
+// that read the same logits tile (same row tile and range, every group) and the CTAs that read
+// the same W block (same group and range, every row tile) run side by side at the same pace, so
+// logits and W come from HBM about once and are served to the others from L2. Each CTA writes
+// one partial (128 x 512) to the caller's workspace; head_dh_reduce sums the S partials of each
+// output element in range order (deterministic), maps rows and writes fp32 or fp16.
 //
-// CTA (6 warps):
-//   warp 0      TMA producer: per unit the 128 x 32 fp16 logits tile (no swizzle) and W's
-//               32 x 512 block, into a 4-stage ring
+// CTA (10 warps):
+//   warp 0      TMA producer: per vocabulary block the 128 x 32 fp16 logits tile (no swizzle)
+//               and W's 32 x 512 block, into a 4-stage ring
 //   warp 1      TMEM allocation (512 columns) and the MMA issuer
-//   warps 2..5  producers of A: logits tile -> dl (fp16, swizzled) for the MMA; at the end of a
-//               hidden group the epilogue: TMEM -> fp32 partial in the workspace
+//   warps 2..9  producers of A: logits tile -> dl (fp16, swizzled) for the MMA, 16 rows a warp;
+//               at the end the epilogue: TMEM -> fp32 partial in the workspace (warps w and
+//               w + 4 share TMEM lane quarter w % 4, each reading half the columns)
 // Every mbarrier wait is bounded (mbar_wait); a role that gives up sets the CTA's error flag and
 // leaves its loop, every role meets at the final barrier and TMEM is always released. No
 // multicast is used.
@@ -48,7 +50,8 @@ constexpr int kRawBytes = kBM * kBK * 2;   // 8 KB: fp16 logits, 64-byte rows
 constexpr int kABytes = kBM * kBK * 2;     // 8 KB: fp16 dl, K-major, 64-byte swizzle
 constexpr int kBBytes = kBK * kBN * 2;     // 32 KB: W block, MN-major, 128-byte swizzle
 constexpr int kBoxBytes = kBK * 64 * 2;    // one TMA box of W: 32 rows x 64 columns
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kProducers = 256;            // warps 2..9
 constexpr int kTmemCols = 512;
 constexpr int kMaxGroups = 16;             // hidden <= 8192
 constexpr float kLog2e = 1.4426950408889634f;
@@ -62,7 +65,7 @@ struct Smem {
   alignas(1024) uint8_t a[kStages][kABytes];
   alignas(128) uint8_t raw[kStages][kRawBytes];
   uint64_t full_raw[kStages], full_b[kStages], full_a[kStages], empty[kStages];
-  uint64_t acc_full, acc_empty, mma_done;
+  uint64_t acc_full, mma_done;
   uint32_t tmem_base;
   volatile int error;
 };
@@ -70,13 +73,12 @@ struct Smem {
 struct DhArgs {
   const int64_t *targets;   // [rows], global column of the label (IGNORE_INDEX: none)
   const float *lse;         // [rows]
-  float *ws;                // partials [grid][max_segs][128][512] fp32
+  float *ws;                // partials [S][m_tiles][groups][128][512] fp32, block order
   int rows, cols, hidden;
   int64_t col_offset;
   float grad_scale;
-  int m_tiles, per_tile;    // C CTAs per row tile
-  int groups, kblocks;      // hidden groups of 512; vocabulary blocks of 32
-  int max_segs;
+  int m_tiles, groups;      // row tiles of 128, hidden groups of 512
+  int splits, kblocks;      // S vocabulary ranges; vocabulary blocks of 32
 };
 
 // K-major operand, 64-byte swizzle: SBO 512 bytes between 8-row atoms (LBO unused), sm_100
@@ -151,11 +153,11 @@ __device__ __forceinline__ float ex2f(float x) {
   return y;
 }
 
-// Units [lo, hi) of CTA j of a row tile: (hidden group, vocabulary block) pairs, group-major.
-__device__ __host__ __forceinline__ void unit_range(int j, int per_tile, int64_t units,
-                                                    int64_t &lo, int64_t &hi) {
-  lo = units * j / per_tile;
-  hi = units * (j + 1) / per_tile;
+// Vocabulary blocks [lo, hi) of range s of S.
+__device__ __host__ __forceinline__ void kb_range(int s, int splits, int kblocks, int &lo,
+                                                  int &hi) {
+  lo = (int)((int64_t)kblocks * s / splits);
+  hi = (int)((int64_t)kblocks * (s + 1) / splits);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -165,21 +167,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   Smem &sm = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                         ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mt = blockIdx.x / args.per_tile, j = blockIdx.x % args.per_tile;
-  const int64_t units = (int64_t)args.groups * args.kblocks;
-  int64_t lo, hi;
-  unit_range(j, args.per_tile, units, lo, hi);
-  const int n = (int)(hi - lo);
+  const int g = (int)(blockIdx.x % args.groups);
+  const int mt = (int)((blockIdx.x / args.groups) % args.m_tiles);
+  const int sp = (int)(blockIdx.x / (args.groups * args.m_tiles));
+  int k0, k1;
+  kb_range(sp, args.splits, args.kblocks, k0, k1);
+  const int n = k1 - k0;
+  const int width = min(kBN, args.hidden - g * kBN);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.full_raw[s], 1);
       mbar_init(&sm.full_b[s], 1);
-      mbar_init(&sm.full_a[s], 128);
+      mbar_init(&sm.full_a[s], kProducers);
       mbar_init(&sm.empty[s], 1);
     }
     mbar_init(&sm.acc_full, 1);
-    mbar_init(&sm.acc_empty, 4);
     mbar_init(&sm.mma_done, 1);
     sm.error = 0;
     mbar_init_fence();
@@ -207,9 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           sm.error = 1;
           break;
         }
-        const int64_t u = lo + i;
-        const int g = (int)(u / args.kblocks), kb = (int)(u % args.kblocks);
-        const int width = min(kBN, args.hidden - g * kBN);
+        const int kb = k0 + i;
         mbar_expect_tx(&sm.full_raw[s], kRawBytes);
         tma_load_2d(smem_u32(sm.raw[s]), &map_z, kb * kBK, mt * kBM, &sm.full_raw[s]);
         mbar_expect_tx(&sm.full_b[s], (uint32_t)(width / 64) * kBoxBytes);
@@ -227,22 +228,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---- MMA issuer -------------------------------------------------------------------------
     if (lane == 0) {
-      int seg = 0;
-      int64_t seg_start = lo;
+      const int halves = width / kHalf;
       for (int i = 0; i < n && !sm.error; ++i) {
-        const int64_t u = lo + i;
-        const int g = (int)(u / args.kblocks);
-        if (u != lo && u % args.kblocks == 0) {
-          // a new hidden group: hand the accumulator over, wait until it has been read
-          mma_commit(&sm.acc_full);
-          if (!mbar_wait(&sm.acc_empty, (uint32_t)(seg & 1))) {
-            sm.error = 1;
-            break;
-          }
-          tc_fence_after();
-          ++seg;
-          seg_start = u;
-        }
         const int s = i % kStages;
         const uint32_t parity = (uint32_t)((i / kStages) & 1);
         if (!mbar_wait(&sm.full_b[s], parity) || !mbar_wait(&sm.full_a[s], parity)) {
@@ -250,7 +237,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        const int halves = min(kBN, args.hidden - g * kBN) / kHalf;
         const uint32_t a0 = smem_u32(sm.a[s]), b0 = smem_u32(sm.b[s]);
         for (int h = 0; h < halves; ++h)
 #pragma unroll
@@ -258,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                               // two 8-row groups (2 KB) down B
             mma_f16(tmem + (uint32_t)(h * kHalf), desc_a(a0 + k * 32),
                     desc_b(b0 + (uint32_t)(h * 4 * kBoxBytes) + k * 2048),
-                    (u != seg_start || k != 0) ? 1u : 0u);
+                    (i != 0 || k != 0) ? 1u : 0u);
         mma_commit(&sm.empty[s]);  // the stage is free once these MMAs have read it
       }
       mma_commit(&sm.acc_full);
@@ -266,56 +252,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&sm.mma_done, 0)) sm.error = 1;  // no MMA in flight before TMEM is released
     }
   } else {
-    // ---- producers of A (dl), then the epilogue of each hidden group -----------------------
+    // ---- producers of A (dl), then the epilogue ------------------------------------------------
     const int tw = warp - 2, quarter = warp & 3;
     const int c = lane & 3;  // 16-byte chunk (8 columns) of the 64-byte rows
-    float nl[4];
-    int64_t target[4];
-    bool live[4];
+    float nl[2];
+    int64_t target[2];
+    bool live[2];
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const int r = mt * kBM + p * 32 + tw * 8 + (lane >> 2);
+    for (int p = 0; p < 2; ++p) {
+      const int r = mt * kBM + tw * 16 + p * 8 + (lane >> 2);
       live[p] = r < args.rows;
       target[p] = live[p] ? __ldg(args.targets + r) : -100;
       if (target[p] == -100) live[p] = false;
       nl[p] = live[p] ? -__ldg(args.lse + r) * kLog2e : 0.f;
     }
-    int seg = 0;
-    auto epilogue = [&](int seg_idx, int g) {
-      const int ok = mbar_wait(&sm.acc_full, (uint32_t)(seg_idx & 1)) ? 1 : 0;
-      if (!__all_sync(0xffffffffu, ok)) {
-        if (lane == 0) sm.error = 1;
-        return false;
-      }
-      tc_fence_after();
-      const int width = min(kBN, args.hidden - g * kBN);
-      const int rr = quarter * 32 + lane;
-      float *dst = args.ws + (((int64_t)blockIdx.x * args.max_segs + seg_idx) * kBM + rr) * kBN;
-      for (int col = 0; col < width; col += 32) {
-        uint32_t v[32];
-        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col, v);
-        float4 *d4 = reinterpret_cast<float4 *>(dst + col);
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          d4[q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
-                              __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.acc_empty);
-      return true;
-    };
     bool go = true;
     for (int i = 0; i < n && !sm.error; ++i) {
-      const int64_t u = lo + i;
-      const int g = (int)(u / args.kblocks), kb = (int)(u % args.kblocks);
-      if (u != lo && kb == 0) {  // the previous group is complete: read it out first
-        if (!epilogue(seg, g - 1)) {
-          go = false;
-          break;
-        }
-        ++seg;
-      }
+      const int kb = k0 + i;
       const int s = i % kStages;
       if (!mbar_wait(&sm.full_raw[s], (uint32_t)((i / kStages) & 1))) {
         sm.error = 1;
@@ -324,17 +277,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const uint32_t raw = smem_u32(sm.raw[s]), a = smem_u32(sm.a[s]);
       const int c0 = kb * kBK + c * 8;  // local column of this thread's 8 values
+      const int64_t gc0 = args.col_offset + c0;
+      const bool ragged = kb * kBK + kBK > args.cols;  // the last block of a partial slab
 #pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const int row = p * 32 + tw * 8 + (lane >> 2);
+      for (int p = 0; p < 2; ++p) {
+        const int row = tw * 16 + p * 8 + (lane >> 2);
         uint4 zv;
         asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
                      : "=r"(zv.x), "=r"(zv.y), "=r"(zv.z), "=r"(zv.w)
                      : "r"(raw + (uint32_t)(row * 64 + c * 16)));
         const uint32_t w[4] = {zv.x, zv.y, zv.z, zv.w};
+        // the label's position among this thread's 8 columns, -1 if elsewhere
+        const int tl = (uint64_t)(target[p] - gc0) < 8u ? (int)(target[p] - gc0) : -1;
         float g8[8];
-        const int64_t gc0 = args.col_offset + c0;
-        const bool has_t = (uint64_t)(target[p] - gc0) < 8u;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 z = unpack_half2(w[e]);
@@ -344,9 +299,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           float v = g8[e];
-          if (has_t && gc0 + e == target[p]) v -= 1.f;
+          if (e == tl) v -= 1.f;
           v *= args.grad_scale;
-          g8[e] = (live[p] && c0 + e < args.cols) ? v : 0.f;
+          g8[e] = live[p] ? v : 0.f;
+        }
+        if (ragged) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (c0 + e >= args.cols) g8[e] = 0.f;
         }
         const uint32_t dst = a + (uint32_t)(row * 64) + ((uint32_t)(c ^ ((row >> 1) & 3)) << 4);
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst),
@@ -357,7 +317,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async();  // the generic-proxy stores, visible to the tensor core
       mbar_arrive(&sm.full_a[s]);
     }
-    if (go && n > 0 && !sm.error) epilogue(seg, (int)((hi - 1) / args.kblocks));
+    // epilogue: this warp's lane quarter, columns [half * 256, half * 256 + 256) of the group
+    const int half = tw >> 2;
+    if (go && n > 0 && half * kHalf < width) {
+      const int ok = mbar_wait(&sm.acc_full, 0) ? 1 : 0;
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) sm.error = 1;
+      } else {
+        tc_fence_after();
+        const int rr = quarter * 32 + lane;
+        float *dst = args.ws + ((int64_t)blockIdx.x * kBM + rr) * kBN + half * kHalf;
+        for (int col = 0; col < kHalf; col += 32) {
+          uint32_t v[32];
+          tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * kHalf + col), v);
+          float4 *d4 = reinterpret_cast<float4 *>(dst + col);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            d4[q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+        }
+      }
+    }
   }
 
   tc_fence_before();
@@ -373,36 +353,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 struct ReduceArgs {
   const float *ws;
-  int rows, hidden, m_tiles, per_tile, kblocks, max_segs;
-  int jf[kMaxGroups], jl[kMaxGroups];  // CTAs (within a row tile) covering each hidden group
+  int rows, hidden, m_tiles, groups, splits;
   const int64_t *out_rows;             // nullable: dh row r -> output row out_rows[r]
   void *out;
   int64_t ld_out;
   int out_fp32, accumulate;
 };
 
-// out[row(r), c] (+)= sum over the covering CTAs j (in order) of their partial for (r, c).
+// out[row(r), c] (+)= sum over the vocabulary ranges s (in order) of their partial for (r, c).
 __global__ void __launch_bounds__(256) head_dh_reduce(const __grid_constant__ ReduceArgs a) {
   pdl_wait();
   pdl_release();
   const int64_t vecs = (int64_t)a.rows * (a.hidden / 4);
-  const int64_t units = (int64_t)(a.hidden + kBN - 1) / kBN * a.kblocks;
+  const int64_t split_stride = (int64_t)a.m_tiles * a.groups * kBM * kBN;
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < vecs;
        v += (int64_t)gridDim.x * blockDim.x) {
     const int r = (int)(v / (a.hidden / 4));
     const int col = (int)(v - (int64_t)r * (a.hidden / 4)) * 4;
     const int mt = r / kBM, rr = r % kBM, g = col / kBN, cc = col % kBN;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int jj = a.jf[g]; jj <= a.jl[g]; ++jj) {
-      int64_t lo, hi;
-      unit_range(jj, a.per_tile, units, lo, hi);
-      const int seg = g - (int)(lo / a.kblocks);
-      const float4 p = *reinterpret_cast<const float4 *>(
-          a.ws + ((((int64_t)mt * a.per_tile + jj) * a.max_segs + seg) * kBM + rr) * kBN + cc);
-      acc.x = __fadd_rn(acc.x, p.x);
-      acc.y = __fadd_rn(acc.y, p.y);
-      acc.z = __fadd_rn(acc.z, p.z);
-      acc.w = __fadd_rn(acc.w, p.w);
+    const float *p = a.ws + (((int64_t)mt * a.groups + g) * kBM + rr) * kBN + cc;
+    float4 acc = *reinterpret_cast<const float4 *>(p);
+    for (int s = 1; s < a.splits; ++s) {
+      const float4 q = *reinterpret_cast<const float4 *>(p + s * split_stride);
+      acc.x = __fadd_rn(acc.x, q.x);
+      acc.y = __fadd_rn(acc.y, q.y);
+      acc.z = __fadd_rn(acc.z, q.z);
+      acc.w = __fadd_rn(acc.w, q.w);
     }
     const int64_t orow = a.out_rows ? __ldg(a.out_rows + r) : r;
     if (a.out_fp32) {
@@ -459,41 +435,25 @@ int make_map(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, int
 }
 
 struct Plan {
-  int m_tiles, per_tile, groups, kblocks, max_segs;
-  int jf[kMaxGroups], jl[kMaxGroups];
+  int m_tiles, groups, splits, kblocks;
 };
 
+// S vocabulary ranges per (row tile, hidden group): as many as fill the SMs with one CTA each,
+// at least 1, at most one per vocabulary block.
 Plan make_plan(int64_t rows, int64_t cols, int64_t hidden, int sms) {
   Plan p{};
   p.m_tiles = (int)((rows + kBM - 1) / kBM);
   p.groups = (int)((hidden + kBN - 1) / kBN);
   p.kblocks = (int)((cols + kBK - 1) / kBK);
-  const int64_t units = (int64_t)p.groups * p.kblocks;
-  int per = sms / p.m_tiles;
-  if (per < 1) per = 1;
-  if (per > units) per = (int)units;
-  p.per_tile = per;
-  p.max_segs = 1;
-  for (int g = 0; g < p.groups; ++g) {
-    p.jf[g] = per;
-    p.jl[g] = -1;
-  }
-  for (int j = 0; j < per; ++j) {
-    int64_t lo, hi;
-    unit_range(j, per, units, lo, hi);
-    if (hi <= lo) continue;
-    const int g0 = (int)(lo / p.kblocks), g1 = (int)((hi - 1) / p.kblocks);
-    if (g1 - g0 + 1 > p.max_segs) p.max_segs = g1 - g0 + 1;
-    for (int g = g0; g <= g1; ++g) {
-      if (j < p.jf[g]) p.jf[g] = j;
-      if (j > p.jl[g]) p.jl[g] = j;
-    }
-  }
+  int splits = sms / (p.m_tiles * p.groups);
+  if (splits < 1) splits = 1;
+  if (splits > p.kblocks) splits = p.kblocks;
+  p.splits = splits;
   return p;
 }
 
 int64_t workspace_bytes(const Plan &p) {
-  return (int64_t)p.m_tiles * p.per_tile * p.max_segs * kBM * kBN * 4;
+  return (int64_t)p.splits * p.m_tiles * p.groups * kBM * kBN * 4;
 }
 
 }  // namespace
@@ -561,15 +521,14 @@ extern "C" int tb_head_dh(const uint16_t *logits, int64_t ld, const int64_t *tar
   a.col_offset = col_offset;
   a.grad_scale = grad_scale;
   a.m_tiles = p.m_tiles;
-  a.per_tile = p.per_tile;
   a.groups = p.groups;
+  a.splits = p.splits;
   a.kblocks = p.kblocks;
-  a.max_segs = p.max_segs;
   const size_t smem = sizeof(Smem) + 1024;
   if (cudaFuncSetAttribute(head_dh_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem) != cudaSuccess)
     return check_launch("head_dh attribute");
-  const int64_t grid = (int64_t)p.m_tiles * p.per_tile;
+  const int64_t grid = (int64_t)p.splits * p.m_tiles * p.groups;
   if (grid > 0x7fffffffLL) return set_error(TB_EINVAL, "head_dh: too many rows");
   head_dh_kernel<<<(unsigned)grid, kThreads, smem, as_stream(stream)>>>(map_z, map_w, a);
   rc = check_launch("head_dh");
@@ -579,13 +538,8 @@ extern "C" int tb_head_dh(const uint16_t *logits, int64_t ld, const int64_t *tar
   r.rows = (int)rows;
   r.hidden = (int)hidden_dim;
   r.m_tiles = p.m_tiles;
-  r.per_tile = p.per_tile;
-  r.kblocks = p.kblocks;
-  r.max_segs = p.max_segs;
-  for (int g = 0; g < kMaxGroups; ++g) {
-    r.jf[g] = g < p.groups ? p.jf[g] : 0;
-    r.jl[g] = g < p.groups ? p.jl[g] : -1;
-  }
+  r.groups = p.groups;
+  r.splits = p.splits;
   r.out_rows = out_rows;
   r.out = out;
   r.ld_out = ld_out;
