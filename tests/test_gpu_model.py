@@ -122,20 +122,29 @@ def lora_model_d128():
                              norm_jitter=True)
 
 
-@pytest.mark.parametrize("nf4_gemm", [False, True], ids=["unpack", "nf4_gemm"])
-def test_fused_step_with_own_attention_matches_unpatched_model(lora_model_d128, nf4_gemm):
-    """Head dimension 128: the variable-length attention runs through tb_attn_varlen_fwd / _bwd
+@pytest.mark.parametrize("nf4_gemm,rope_in_bwd", [(False, True), (False, False), (True, True)],
+                         ids=["unpack", "unpack_separate_rope_bwd", "nf4_gemm"])
+def test_fused_step_with_own_attention_matches_unpatched_model(lora_model_d128, nf4_gemm,
+                                                                rope_in_bwd):
+    """Head dimension 128: the variable-length attention runs through this library's kernels
     (checked), and the step matches the unpatched model, with the layers' projections either
     over unpacked weights (one unpack launch per layer, cuBLAS) or through the NF4-decoding
-    GEMMs (q|k|v + RoPE, o, the MLP with SwiGLU in the epilogues; checked)."""
+    GEMMs (q|k|v + RoPE, o, the MLP with SwiGLU in the epilogues; checked). Over unpacked
+    weights the rotary embedding's backward runs inside the attention backward
+    (tb_attn_varlen_bwd_rope) or as its own kernel after tb_attn_varlen_bwd."""
     from testt_b200 import attention, fused_layer, model
 
     calls, fused_calls = [], []
     original, original_mlp = attention.varlen_attention, fused_layer.layer_mlp
+    original_rope = attention.rope_varlen_attention
 
     def counted(*args):
-        calls.append(1)
+        calls.append("varlen")
         return original(*args)
+
+    def counted_rope(*args):
+        calls.append("rope_varlen")
+        return original_rope(*args)
 
     def counted_mlp(*args):
         fused_calls.append(1)
@@ -143,17 +152,22 @@ def test_fused_step_with_own_attention_matches_unpatched_model(lora_model_d128, 
 
     ref = run(lora_model_d128, fused=False)
     attention.varlen_attention = counted
+    attention.rope_varlen_attention = counted_rope
     fused_layer.layer_mlp = counted_mlp
-    saved = model.USE_NF4_GEMM
+    saved = model.USE_NF4_GEMM, model.USE_ROPE_IN_ATTENTION_BWD
     model.USE_NF4_GEMM = nf4_gemm
+    model.USE_ROPE_IN_ATTENTION_BWD = rope_in_bwd
     try:
         assert model.USE_VARLEN_ATTENTION
         got = run(lora_model_d128, fused=True)
     finally:
         attention.varlen_attention = original
+        attention.rope_varlen_attention = original_rope
         fused_layer.layer_mlp = original_mlp
-        model.USE_NF4_GEMM = saved
-    assert len(calls) == 2, "each layer's attention must run the library's kernels"
+        model.USE_NF4_GEMM, model.USE_ROPE_IN_ATTENTION_BWD = saved
+    # the q|k|v GEMM's own RoPE epilogue takes the plain attention entry
+    expect = "rope_varlen" if rope_in_bwd and not nf4_gemm else "varlen"
+    assert calls == [expect] * 2, ("each layer's attention must run the library's kernels", calls)
     assert len(fused_calls) == (2 if nf4_gemm else 0)
     _assert_same_step(got, ref)
 
