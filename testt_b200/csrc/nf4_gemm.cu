@@ -20,19 +20,17 @@
 //   backward  A[k][n] = W[n][k], MN-major (bit 15 of the instruction descriptor): 64 W rows x
 //             128 columns per stage, so W is decoded row by row in its natural order in both
 //             directions (no transposition anywhere).
-// A stage's 64-value row segments are decoded into 128-byte swizzled rows at segment * 128
-// bytes (the same address for both operand majors) by decoder threads that load their packed
-// bytes and absmax straight from global memory into registers, kAhead stages ahead of the
-// stage they decode: the packed tile never passes through shared memory, and a decoder waits
-// only for the MMA to release the stage's A buffer.
+// A stage's 64-value row segments are decoded from packed bytes and absmax that TMA and a bulk
+// copy brought into shared memory, into 128-byte swizzled rows at segment * 128 bytes (the same
+// address for both operand majors).
 //
 // Persistent CTAs (one per SM) loop over work units (128-row tile, token group of <= 256, split of
 // the reduction); token groups are the fastest-varying so the CTAs that decode the same packed
 // tile run side by side and share it through L2. Warps:
-//   warp 0       TMA producer: the tokens tile of each stage
+//   warp 0       TMA producer: tokens tile, packed NF4 tile (TMA), absmax (bulk copy) per stage
 //   warp 1       TMEM allocation (2 x 256 columns) and the MMA issuer
 //   warps 2..5   epilogue (TMEM lane quarters), overlapping the next unit's main loop
-//   warps 6..13  decoders: two threads per 64-value segment, 32 values each
+//   warps 6..13  decoders: two threads per 64-value segment; each warp arrives once per stage
 // A split reduction writes fp32 partials [split][token][row] to the caller's workspace, summed in
 // split order by nf4_gemm_reduce (plain, + bias) or qkv_rope_finish (the q|k|v projection's
 // bias, LoRA rows and rotary embedding, token-major outputs). tb_nf4_gemm_swiglu runs the MLP's
@@ -58,7 +56,8 @@ constexpr int kStages = 4;
 constexpr int kMaxBN = 256;                     // tokens per tile (the MMA's N)
 constexpr int kABytes = kBM * kBK * 2;          // 16 KB decoded tile
 constexpr int kBBytes = kMaxBN * kBK * 2;       // 32 KB tokens tile
-constexpr int kAhead = 3;                       // stages a decoder's global loads run ahead
+constexpr int kPBytes = 4096;                   // packed NF4 of one stage (128 x 64 values)
+constexpr int kSBytes = kBM * 4;                // their 128 absmax
 constexpr int kDecoders = 256;                  // warps 6..13
 constexpr int kThreads = 448;
 constexpr int kTmemCols = 512;                  // two accumulators of 256 columns
@@ -66,8 +65,10 @@ constexpr int kTmemCols = 512;                  // two accumulators of 256 colum
 struct Smem {
   alignas(1024) uint8_t b[kStages][kBBytes];
   alignas(1024) uint8_t a[kStages][kABytes];
+  alignas(128) uint8_t packed[kStages][kPBytes];
+  alignas(128) float scale[kStages][kBM];
   alignas(256) float table[kMaxW][64];          // 16 entries used; 256-byte aligned rows
-  uint64_t full_b[kStages], full_a[kStages], empty[kStages];
+  uint64_t full_b[kStages], full_p[kStages], full_a[kStages], empty[kStages];
   uint64_t acc_full[2], acc_empty[2];
   uint64_t mma_done;
   uint32_t tmem_base;
@@ -78,7 +79,6 @@ struct Smem {
 constexpr int kPlain = 0, kPart = 1, kSwigluFwd = 2, kSwigluBwd = 3;
 
 struct GemmArgs {
-  const uint8_t *packed[kMaxW];  // NF4 [rows_j, k_dim / 2]
   const float *absmax_t[kMaxW];  // fp32 [k_dim / 64, rows_j]
   const float *table[kMaxW];
   int rows[kMaxW];
@@ -177,6 +177,14 @@ __device__ __forceinline__ void st_shared16(uint32_t addr, uint4 v) {
                : "memory");
 }
 
+__device__ __forceinline__ uint4 ld_shared16(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+
 // ---- NF4 decode ------------------------------------------------------------------------------
 
 // Shared-memory address tab | byte b of x (tab 256-byte aligned), one byte permute.
@@ -243,78 +251,61 @@ __device__ __forceinline__ Unit unit_of(const GemmArgs &args, int u) {
   return r;
 }
 
-// Issues the tokens tile of one stage of unit `un`, reduction block kb (absolute).
-__device__ __forceinline__ void issue_stage(const GemmArgs &args, const CUtensorMap *map_b,
-                                            Smem &sm, int s, const Unit &un, int kb) {
-  mbar_expect_tx(&sm.full_b[s], (uint32_t)(args.bn * kBK * 2));
-  tma_load_2d(smem_u32(sm.b[s]), map_b, kb * kBK, un.group * args.bn, &sm.full_b[s]);
-}
-
-// Where decoder thread (seg, half) finds its 16 packed bytes (32 values) and their absmax for
-// reduction block kb of unit `un`, and which weight's table decodes them:
-//   forward        A row seg = stacked W row a_tile * 128 + seg, values kb * 64 + half * 32 ..
-//   SwiGLU forward A row seg = feature a_tile * 64 + seg / 2 of gate (seg even) or up (odd)
-//   backward       A row seg = (M half seg / 64) x (K row seg % 64): W row kb * 64 + seg % 64,
-//                  columns a_tile * 128 + (seg / 64) * 64 + half * 32 ..
-template <int kMode, bool kTrans>
-__device__ __forceinline__ int seg_source(const GemmArgs &args, const Unit &un, int kb, int seg,
-                                          int half, const uint4 *&src, const float *&scale) {
-  const int64_t row_bytes = args.k_dim >> 1;
-  int j, row;
-  int64_t byte, blk;
-  if (kMode == kSwigluFwd) {
-    j = seg & 1;
-    row = un.a_tile * 64 + (seg >> 1);
-    byte = (int64_t)kb * 32 + half * 16;
-    blk = kb;
-  } else if (kTrans) {
-    const int a0 = un.a_tile * kBM, n0 = kb * kBK;
-    j = weight_of(args, n0);
-    row = n0 - args.row_start[j] + (seg & 63);
-    byte = (a0 >> 1) + (seg >> 6) * 32 + half * 16;
-    blk = (a0 >> 6) + (seg >> 6);
-  } else {
-    const int a0 = un.a_tile * kBM;
-    j = weight_of(args, a0);
-    row = a0 - args.row_start[j] + seg;
-    byte = (int64_t)kb * 32 + half * 16;
-    blk = kb;
+// The packed-weight tensor maps of the (up to four) weights, kernel parameters.
+struct PackedMaps {
+  const CUtensorMap *m[kMaxW];
+  __device__ __forceinline__ const CUtensorMap *operator[](int j) const {
+    return j == 0 ? m[0] : j == 1 ? m[1] : j == 2 ? m[2] : m[3];
   }
-  src = reinterpret_cast<const uint4 *>(args.packed[j] + (int64_t)row * row_bytes + byte);
-  scale = args.absmax_t[j] + blk * args.rows[j] + row;
-  return j;
-}
-
-// A position in a CTA's sequence of stages: unit u (blockIdx.x, + gridDim.x, ...), block i.
-struct Cursor {
-  int u, i;
-  Unit un;
 };
 
-__device__ __forceinline__ void cursor_start(const GemmArgs &args, int units, Cursor &c) {
-  c.u = blockIdx.x;
-  c.i = 0;
-  if (c.u < units) c.un = unit_of(args, c.u);
-}
-
-__device__ __forceinline__ void cursor_next(const GemmArgs &args, int units, Cursor &c) {
-  if (++c.i < c.un.nblk) return;
-  c.i = 0;
-  c.u += gridDim.x;
-  if (c.u < units) c.un = unit_of(args, c.u);
-}
-
-__device__ __forceinline__ uint4 ldg_stream(const uint4 *p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
+// Issues the copies of one stage of unit `un`, reduction block kb (absolute): the tokens tile,
+// the weight's packed tile (TMA) and its absmax (bulk copies), all completing on the stage's
+// barriers.
+__device__ __forceinline__ void issue_stage(const GemmArgs &args, const PackedMaps &maps_p,
+                                            const CUtensorMap *map_b, Smem &sm, int s,
+                                            const Unit &un, int kb) {
+  const int t0 = un.group * args.bn;
+  mbar_expect_tx(&sm.full_b[s], (uint32_t)(args.bn * kBK * 2));
+  tma_load_2d(smem_u32(sm.b[s]), map_b, kb * kBK, t0, &sm.full_b[s]);
+  mbar_expect_tx(&sm.full_p[s], (uint32_t)(kPBytes + kSBytes));
+  const uint32_t pk = smem_u32(sm.packed[s]);
+  if (args.mode == kSwigluFwd) {
+    // 64 gate rows, then the same 64 up rows
+    const int f0 = un.a_tile * 64;
+    for (int j = 0; j < 2; ++j) {
+      tma_load_2d(pk + (uint32_t)(j * 2048), maps_p[j], kb * 32, f0, &sm.full_p[s]);
+      bulk_load(&sm.scale[s][j * 64], args.absmax_t[j] + (int64_t)kb * args.rows[j] + f0, 256,
+                &sm.full_p[s]);
+    }
+  } else if (!args.trans) {
+    const int a0 = un.a_tile * kBM;
+    const int j = weight_of(args, a0);
+    const int lr = a0 - args.row_start[j];
+    tma_load_2d(pk, maps_p[j], kb * 32, lr, &sm.full_p[s]);
+    bulk_load(&sm.scale[s][0], args.absmax_t[j] + (int64_t)kb * args.rows[j] + lr, kSBytes,
+              &sm.full_p[s]);
+  } else {
+    // W rows kb*64 .. (within one weight), columns a0 .. a0 + 127
+    const int a0 = un.a_tile * kBM;
+    const int n0 = kb * kBK;
+    const int j = weight_of(args, n0);
+    const int ln = n0 - args.row_start[j];
+    tma_load_2d(pk, maps_p[j], a0 >> 1, ln, &sm.full_p[s]);
+    for (int h = 0; h < 2; ++h)
+      bulk_load(&sm.scale[s][h * 64],
+                args.absmax_t[j] + (int64_t)((a0 >> 6) + h) * args.rows[j] + ln, 256,
+                &sm.full_p[s]);
+  }
 }
 
 template <int kMode, bool kTrans>
 __global__ void __launch_bounds__(kThreads, 1)
     nf4_gemm_kernel(const __grid_constant__ CUtensorMap map_b,
+                    const __grid_constant__ CUtensorMap map_p0,
+                    const __grid_constant__ CUtensorMap map_p1,
+                    const __grid_constant__ CUtensorMap map_p2,
+                    const __grid_constant__ CUtensorMap map_p3,
                     const __grid_constant__ GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   Smem &sm = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -325,7 +316,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.full_b[s], 1);
-      mbar_init(&sm.full_a[s], kDecoders);
+      mbar_init(&sm.full_p[s], 1);
+      mbar_init(&sm.full_a[s], kDecoders / 32);
       mbar_init(&sm.empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -353,6 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---- TMA producer ----------------------------------------------------------------------
     if (lane == 0) {
+      const PackedMaps maps = {{&map_p0, &map_p1, &map_p2, &map_p3}};
       uint32_t ctr = 0;
       for (int u = blockIdx.x; u < units && !sm.error; u += gridDim.x) {
         const Unit un = unit_of(args, u);
@@ -362,13 +355,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             sm.error = 1;
             break;
           }
-          issue_stage(args, &map_b, sm, s, un, un.first + i);
+          issue_stage(args, maps, &map_b, sm, s, un, un.first + i);
         }
       }
       // every copy issued must have landed before the CTA may leave (bounded)
       const uint32_t tail = ctr < kStages ? ctr : kStages;
-      for (uint32_t c = ctr - tail; c < ctr; ++c)
+      for (uint32_t c = ctr - tail; c < ctr; ++c) {
         mbar_wait(&sm.full_b[c % kStages], (c / kStages) & 1);
+        mbar_wait(&sm.full_p[c % kStages], (c / kStages) & 1);
+      }
     }
   } else if (warp == 1) {
     // ---- MMA issuer -------------------------------------------------------------------------
@@ -494,70 +489,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
     }
   } else {
-    // ---- decoders: segment seg = A row (64 values), two threads each --------------------------
+    // ---- decoders: segment s = A row (64 values of one W row), two threads each -----------
     const int d = threadIdx.x - 192;  // 0 .. 255
     const int seg = d >> 1, half = d & 1;
+    // packed bytes and absmax of the segment in the stage buffers
+    uint32_t p_off;
+    int s_idx, jseg;
+    if (kMode == kSwigluFwd) {
+      p_off = (uint32_t)((seg & 1) * 2048 + (seg >> 1) * 32);
+      s_idx = (seg & 1) * 64 + (seg >> 1);
+      jseg = seg & 1;
+    } else if (kTrans) {
+      p_off = (uint32_t)((seg & 63) * 64 + (seg >> 6) * 32);
+      s_idx = seg;
+      jseg = -1;
+    } else {
+      p_off = (uint32_t)(seg * 32);
+      s_idx = seg;
+      jseg = -1;
+    }
+    p_off += (uint32_t)(half * 16);
     const uint32_t a_row = (uint32_t)(seg * 128);
     const uint32_t swz = (uint32_t)(seg & 7);
-    // the packed words and absmax of the next kAhead stages, in flight in registers
-    uint4 pk[kAhead];
-    float sc[kAhead];
-    Cursor ld, dc;
-    cursor_start(args, units, ld);
-    cursor_start(args, units, dc);
-#pragma unroll
-    for (int q = 0; q < kAhead; ++q) {
-      if (ld.u < units) {
-        const uint4 *src;
-        const float *sp;
-        seg_source<kMode, kTrans>(args, ld.un, ld.un.first + ld.i, seg, half, src, sp);
-        pk[q] = ldg_stream(src);
-        sc[q] = __ldg(sp);
-        cursor_next(args, units, ld);
-      }
-    }
     uint32_t ctr = 0;
-    bool run = dc.u < units;
-    while (run) {
-#pragma unroll
-      for (int q = 0; q < kAhead; ++q) {
-        if (dc.u >= units || sm.error) {
-          run = false;
-          break;
-        }
+    bool stop = false;
+    // every exit decision is warp-uniform: the warp arrives once per stage, after __syncwarp
+    for (int u = blockIdx.x; u < units && !stop; u += gridDim.x) {
+      if (__any_sync(0xffffffffu, sm.error != 0)) break;
+      const Unit un = unit_of(args, u);
+      const int jt = kTrans ? 0 : (kMode == kSwigluFwd ? 0 : weight_of(args, un.a_tile * kBM));
+      for (int i = 0; i < un.nblk; ++i, ++ctr) {
         const int s = (int)(ctr % kStages);
-        // the MMA has released this stage's A buffer (kStages stages ago)
-        if (!mbar_wait(&sm.empty[s], ((ctr / kStages) & 1) ^ 1)) {
-          sm.error = 1;
-          run = false;
+        if (!__all_sync(0xffffffffu, mbar_wait(&sm.full_p[s], (ctr / kStages) & 1))) {
+          if (lane == 0) sm.error = 1;
+          stop = true;
           break;
         }
-        const uint4 *unused_src;
-        const float *unused_sp;
-        const int j = seg_source<kMode, kTrans>(args, dc.un, dc.un.first + dc.i, seg, half,
-                                                unused_src, unused_sp);
+        const int j = jseg >= 0 ? jseg : (kTrans ? weight_of(args, (un.first + i) * kBK) : jt);
         const uint32_t tab = smem_u32(&sm.table[j][0]);
+        const uint4 w = ld_shared16(smem_u32(sm.packed[s]) + p_off);
+        const float scale = sm.scale[s][s_idx];
         const uint32_t a_tile = smem_u32(sm.a[s]) + a_row;
-        const uint32_t words[4] = {pk[q].x, pk[q].y, pk[q].z, pk[q].w};
-        const float scale = sc[q];
+        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          const uint32_t c = (uint32_t)(half * 4 + w);  // 16-byte chunk of the 128-byte row
-          st_shared16(a_tile + ((c ^ swz) << 4), decode_word(words[w], scale, tab));
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t c = (uint32_t)(half * 4 + q);  // 16-byte chunk of the 128-byte row
+          st_shared16(a_tile + ((c ^ swz) << 4), decode_word(words[q], scale, tab));
         }
-        fence_proxy_async();  // the generic-proxy stores, visible to the tensor core
-        mbar_arrive(&sm.full_a[s]);
-        // refill this slot with the stage kAhead further on
-        if (ld.u < units) {
-          const uint4 *src;
-          const float *sp;
-          seg_source<kMode, kTrans>(args, ld.un, ld.un.first + ld.i, seg, half, src, sp);
-          pk[q] = ldg_stream(src);
-          sc[q] = __ldg(sp);
-          cursor_next(args, units, ld);
-        }
-        cursor_next(args, units, dc);
-        ++ctr;
+        fence_proxy_async();  // this thread's generic-proxy stores, visible to the tensor core
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.full_a[s]);  // one arrival per decoder warp
       }
     }
   }
@@ -762,7 +743,6 @@ int gemm_args(int32_t transpose, int64_t tokens, int32_t n_weights, const uint8_
                        j, (long long)rows[j], (long long)r_align);
     if (!aligned(packed[j], 16) || !aligned(absmax_t[j], 16) || !aligned(nf4_table[j], 4))
       return set_error(TB_EALIGN, "nf4_gemm: weight %d is not aligned", j);
-    a.packed[j] = packed[j];
     a.absmax_t[j] = absmax_t[j];
     a.table[j] = nf4_table[j];
     a.rows[j] = (int)rows[j];
@@ -771,7 +751,6 @@ int gemm_args(int32_t transpose, int64_t tokens, int32_t n_weights, const uint8_
     a.row_start[j + 1] = (int)total;
   }
   for (int j = n_weights; j < kMaxW; ++j) {
-    a.packed[j] = nullptr;
     a.absmax_t[j] = nullptr;
     a.table[j] = nullptr;
     a.rows[j] = 0;
@@ -801,9 +780,11 @@ int device_ok(const char *what) {
   return TB_OK;
 }
 
-// Launches the GEMM kernel of `mode` over the planned units.
+// Launches the GEMM kernel of `mode` over the planned units. `packed` maps: one per weight,
+// boxes of the mode's packed tile (forward 128 rows x 32 bytes, backward 64 rows x 64 bytes,
+// SwiGLU forward 64 rows x 32 bytes).
 int run_gemm(int mode, GemmArgs &a, const Plan &p, const uint16_t *tokens_in, int64_t ld_in,
-             cudaStream_t stream, const char *what) {
+             const uint8_t *const *packed, cudaStream_t stream, const char *what) {
   a.bn = p.bn;
   a.groups = p.groups;
   a.splits = p.splits;
@@ -811,15 +792,24 @@ int run_gemm(int mode, GemmArgs &a, const Plan &p, const uint16_t *tokens_in, in
   a.idesc = (1u << 4) | ((uint32_t)a.trans << 15) | ((uint32_t)(p.bn >> 3) << 17) |
             ((uint32_t)(kBM >> 4) << 24);
   const int64_t red_dim = (int64_t)a.red_blocks * kBK;
-  CUtensorMap map_b;
+  CUtensorMap map_b, maps_p[kMaxW];
   int rc = make_map(&map_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, tokens_in, a.tokens, red_dim,
                     ld_in, kBK, p.bn, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != TB_OK) return rc;
+  for (int j = 0; j < kMaxW; ++j) {
+    const int jj = j < a.n_w ? j : 0;  // unused maps repeat the first weight's
+    const int box_cols = a.trans ? 64 : 32;
+    const int box_rows = mode == kSwigluFwd ? 64 : (a.trans ? 64 : 128);
+    rc = make_map(&maps_p[j], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, packed[jj], a.rows[jj],
+                  a.k_dim / 2, a.k_dim / 2, box_cols, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != TB_OK) return rc;
+  }
   const int64_t units = (int64_t)a.a_tiles * p.splits * p.groups;
   if (units > 0x7fffffffLL) return set_error(TB_EINVAL, "%s: too many tiles", what);
   const int grid = (int)(units < sm_count() ? units : sm_count());
   const size_t smem = sizeof(Smem) + 1024;
-  void (*kernel)(CUtensorMap, GemmArgs) = nullptr;
+  void (*kernel)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs) =
+      nullptr;
   if (mode == kPlain)
     kernel = a.trans ? nf4_gemm_kernel<kPlain, true> : nf4_gemm_kernel<kPlain, false>;
   else if (mode == kPart)
@@ -831,7 +821,8 @@ int run_gemm(int mode, GemmArgs &a, const Plan &p, const uint16_t *tokens_in, in
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return check_launch(what);
-  kernel<<<(unsigned)grid, kThreads, smem, stream>>>(map_b, a);
+  kernel<<<(unsigned)grid, kThreads, smem, stream>>>(map_b, maps_p[0], maps_p[1], maps_p[2],
+                                                      maps_p[3], a);
   return check_launch(what);
 }
 
@@ -886,10 +877,10 @@ extern "C" int tb_nf4_gemm(int32_t transpose, const uint16_t *tokens_in, int64_t
     a.bias = bias;
     a.out = out;
     a.ld_out = ld_out;
-    return run_gemm(kPlain, a, p, tokens_in, ld_in, st, "nf4_gemm");
+    return run_gemm(kPlain, a, p, tokens_in, ld_in, packed, st, "nf4_gemm");
   }
   a.part = workspace;
-  rc = run_gemm(kPart, a, p, tokens_in, ld_in, st, "nf4_gemm");
+  rc = run_gemm(kPart, a, p, tokens_in, ld_in, packed, st, "nf4_gemm");
   if (rc != TB_OK) return rc;
   const int64_t vecs = tokens * (a.a_rows / 8);
   const int64_t blocks64 = (vecs + 255) / 256;
@@ -939,7 +930,7 @@ extern "C" int tb_nf4_gemm_swiglu(int32_t backward, const uint16_t *tokens_in, i
   a.gu = gu;
   a.ld_gu = ld_gu;
   a.inter = (int)inter;
-  return run_gemm(backward ? kSwigluBwd : kSwigluFwd, a, p, tokens_in, ld_in,
+  return run_gemm(backward ? kSwigluBwd : kSwigluFwd, a, p, tokens_in, ld_in, packed,
                   as_stream(stream), "nf4_gemm_swiglu");
 }
 
@@ -999,7 +990,7 @@ extern "C" int tb_nf4_gemm_qkv_rope(const uint16_t *x, int64_t tokens, int64_t l
                      (long long)workspace_bytes, (long long)p.splits * tokens * a.a_rows * 4);
   a.part = workspace;
   cudaStream_t st = as_stream(stream);
-  rc = run_gemm(kPart, a, p, x, ld_x, st, "nf4_gemm_qkv_rope");
+  rc = run_gemm(kPart, a, p, x, ld_x, packed, st, "nf4_gemm_qkv_rope");
   if (rc != TB_OK) return rc;
   QkvArgs f;
   f.part = workspace;
