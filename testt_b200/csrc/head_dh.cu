@@ -26,7 +26,7 @@
 //
 // CTA (10 warps):
 //   warp 0      TMA producer: per vocabulary block the 128 x 32 fp16 logits tile (no swizzle)
-//               and W's 32 x 512 block, into a 4-stage ring
+//               and W's 32 x 512 block (one 3-D copy), into a 4-stage ring
 //   warp 1      TMEM allocation (512 columns) and the MMA issuer
 //   warps 2..9  producers of A: logits tile -> dl (fp16, swizzled) for the MMA, 16 rows a warp;
 //               at the end the epilogue: TMEM -> fp32 partial in the workspace (warps w and
@@ -108,6 +108,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, "
       "{%2, %3}], [%4];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
+                                            int c2, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -213,10 +222,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kb = k0 + i;
         mbar_expect_tx(&sm.full_raw[s], kRawBytes);
         tma_load_2d(smem_u32(sm.raw[s]), &map_z, kb * kBK, mt * kBM, &sm.full_raw[s]);
-        mbar_expect_tx(&sm.full_b[s], (uint32_t)(width / 64) * kBoxBytes);
-        for (int x = 0; x < width / 64; ++x)
-          tma_load_2d(smem_u32(sm.b[s]) + (uint32_t)(x * kBoxBytes), &map_w, g * kBN + x * 64,
-                      kb * kBK, &sm.full_b[s]);
+        // W's 32 x 512 block as one copy: 8 column blocks of 64 (the map's third dimension),
+        // each a 32 x 64 MN-major atom column; blocks past the hidden size are zero-filled
+        mbar_expect_tx(&sm.full_b[s], (uint32_t)kBBytes);
+        tma_load_3d(smem_u32(sm.b[s]), &map_w, 0, kb * kBK, g * (kBN / 64), &sm.full_b[s]);
         ++issued;
       }
       // every copy issued must have landed before the CTA may leave (bounded)
@@ -434,6 +443,23 @@ int make_map(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, int
   return TB_OK;
 }
 
+// W fp16 [cols, hidden] (row-major) viewed as [hidden / 64][cols][64]: box [8][32][64], so one
+// copy brings a 32 x 512 block as 8 consecutive 4 KB atom columns (128-byte swizzle)
+int make_map_w(CUtensorMap *map, const void *base, int64_t cols, int64_t hidden) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return set_error(TB_EDEVICE, "head_dh: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {64, (cuuint64_t)cols, (cuuint64_t)(hidden / 64)};
+  const cuuint64_t strides[2] = {(cuuint64_t)hidden * 2, 128};
+  const cuuint32_t box[3] = {64, (cuuint32_t)kBK, (cuuint32_t)(kBN / 64)};
+  const cuuint32_t estride[3] = {1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims,
+                        strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(TB_EINVAL, "head_dh: W map encode failed (%d)", (int)r);
+  return TB_OK;
+}
+
 struct Plan {
   int m_tiles, groups, splits, kblocks;
 };
@@ -508,8 +534,7 @@ extern "C" int tb_head_dh(const uint16_t *logits, int64_t ld, const int64_t *tar
   CUtensorMap map_z, map_w;
   rc = make_map(&map_z, logits, rows, cols, ld, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc == TB_OK)
-    rc = make_map(&map_w, weight, cols, hidden_dim, hidden_dim, 64, kBK,
-                  CU_TENSOR_MAP_SWIZZLE_128B);
+    rc = make_map_w(&map_w, weight, cols, hidden_dim);
   if (rc != TB_OK) return rc;
   DhArgs a;
   a.targets = targets;
