@@ -327,8 +327,10 @@ int tb_attn_varlen_bwd(const uint16_t *q, const uint16_t *k, const uint16_t *v,
  * [rot^-1(dq) | rot^-1(dk) | dv] per token, what tb_rope_tokens_bwd writes from those fp16
  * gradients (solution/rope.py:78-128, token-major): each gradient rounded to fp16, then
  * (g1 c1 + g2 s2, g2 c2 - g1 s1) with cos, sin fp32 [seq, 128] at t = pos_idx[token] % seq; a
- * position outside [0, slots) gives a zero row. The dq / dk / dv tensors and the separate
- * rotation pass are never materialised. */
+ * position outside [0, slots) gives a zero row. No dq / dk / dv tensors are materialised: the
+ * dQ kernel writes fp16 dQ into dqkv's q columns, and the last kernel of the call rotates those
+ * in place while it sums, rotates and writes the key/value gradients. cos and sin must be
+ * 16-byte aligned. */
 int tb_attn_varlen_bwd_rope(const uint16_t *q, const uint16_t *k, const uint16_t *v,
                             const uint16_t *out, const uint16_t *dout, const float *lse,
                             const int32_t *cu_seqlens, const float *cos, const float *sin,

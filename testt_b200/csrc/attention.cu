@@ -323,24 +323,6 @@ struct BwdArgs {
   int64_t seq, slots;
 };
 
-// The table row of a token's position for the rotary embedding's backward; -1 without one.
-__device__ __forceinline__ int64_t rope_row(const BwdArgs &a, int64_t token) {
-  const int64_t pos = __ldg(a.pos_idx + token);
-  return (pos >= 0 && pos < a.slots) ? pos % a.seq : -1;
-}
-
-// (o1, o2) = (g1 c1 + g2 s2, g2 c2 - g1 s1) for the column pair (p, p + 64) of table row tp,
-// from fp16-rounded gradients (tb_rope_tokens_bwd's arithmetic)
-__device__ __forceinline__ void rope_back(const BwdArgs &a, int64_t tp, int p, float g1, float g2,
-                                          float &o1, float &o2) {
-  g1 = __half2float(__float2half_rn(g1));
-  g2 = __half2float(__float2half_rn(g2));
-  const float c1 = __ldg(a.cosv + tp * kD + p), c2 = __ldg(a.cosv + tp * kD + 64 + p);
-  const float s1 = __ldg(a.sinv + tp * kD + p), s2 = __ldg(a.sinv + tp * kD + 64 + p);
-  o1 = g1 * c1 + g2 * s2;
-  o2 = g2 * c2 - g1 * s1;
-}
-
 __global__ void __launch_bounds__(kCtaThreads) attn_bwd_dq_kernel(const __grid_constant__ BwdArgs a) {
   pdl_wait();
   pdl_release();
@@ -494,39 +476,18 @@ __global__ void __launch_bounds__(kCtaThreads) attn_bwd_dq_kernel(const __grid_c
   for (int nt = 0; nt < 16; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; ++e) dq[nt][e] += mg[(nt * 4 + e) * 128 + slot];
-  if (a.dqkv != nullptr) {
-    // through the rotary embedding's backward: columns nt * 8 + 2t (+1) and the same + 64
-    // (fragment nt + 8) are a rotation pair, both in this thread
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const int row = r == 0 ? row0 : row1;
-      if (row >= len) continue;
-      const int64_t token = start + row;
-      const int64_t tp = rope_row(a, token);
-      uint32_t *op = reinterpret_cast<uint32_t *>(a.dqkv + token * a.ld_qkv + h * kD);
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        float o1[2] = {0.f, 0.f}, o2[2] = {0.f, 0.f};
-        if (tp >= 0) {
-#pragma unroll
-          for (int e = 0; e < 2; ++e)
-            rope_back(a, tp, nt * 8 + 2 * t + e, dq[nt][2 * r + e] * a.scale,
-                      dq[nt + 8][2 * r + e] * a.scale, o1[e], o2[e]);
-        }
-        op[nt * 4 + t] = pack_half2(o1[0], o1[1]);
-        op[(nt + 8) * 4 + t] = pack_half2(o2[0], o2[1]);
-      }
-    }
-    return;
-  }
+  // with dqkv set (the backward through the rotary embedding), the scaled fp16 dQ goes to
+  // dqkv's q columns unrotated; attn_bwd_gsum_rope_kernel rotates it in place
+  uint16_t *dq_out = a.dqkv != nullptr ? a.dqkv : a.dq;
+  const int64_t ld_out = a.dqkv != nullptr ? a.ld_qkv : ldq;
   if (row0 < len) {
-    uint32_t *op = reinterpret_cast<uint32_t *>(a.dq + (int64_t)(start + row0) * ldq + h * kD);
+    uint32_t *op = reinterpret_cast<uint32_t *>(dq_out + (int64_t)(start + row0) * ld_out + h * kD);
 #pragma unroll
     for (int nt = 0; nt < 16; ++nt)
       op[nt * 4 + t] = pack_half2(dq[nt][0] * a.scale, dq[nt][1] * a.scale);
   }
   if (row1 < len) {
-    uint32_t *op = reinterpret_cast<uint32_t *>(a.dq + (int64_t)(start + row1) * ldq + h * kD);
+    uint32_t *op = reinterpret_cast<uint32_t *>(dq_out + (int64_t)(start + row1) * ld_out + h * kD);
 #pragma unroll
     for (int nt = 0; nt < 16; ++nt)
       op[nt * 4 + t] = pack_half2(dq[nt][2] * a.scale, dq[nt][3] * a.scale);
@@ -748,54 +709,90 @@ __global__ void __launch_bounds__(256) attn_bwd_gsum_kernel(const float *__restr
   }
 }
 
-// The same sums, leaving through the rotary embedding's backward into dqkv: a thread takes 4
-// columns c .. c + 3 (c < 64) and their rotation partners c + 64 .. of one (token, key/value
-// head); dK rotated back, dV as it is.
+// The backward through the rotary embedding, finished in one pass over dqkv: a thread takes 4
+// columns c..c+3 and c+64..c+67 of one head slot of one token. Slots 0 .. n_heads-1 are the q
+// heads: the dQ kernel left fp16 dQ in dqkv's q columns, rotated back here in place. Slots
+// n_heads .. n_heads+n_kv-1 are the key/value heads: the grouped query heads' fp32 dK and dV
+// partials summed in head order, dK rotated back, dV copied. The rotation is
+// tb_rope_tokens_bwd's: each gradient rounded to fp16, then (g1 c1 + g2 s2, g2 c2 - g1 s1) with
+// the table row t = pos_idx[token] % seq; a token without a position gets zeros.
 __global__ void __launch_bounds__(256) attn_bwd_gsum_rope_kernel(const __grid_constant__ BwdArgs a) {
   pdl_wait();
   pdl_release();
   const int group = a.n_heads / a.n_kv;
+  const int slots_per_token = a.n_heads + a.n_kv;
   constexpr int kVecs = kD / 8;  // 16 vectors of 4 in the first half of a head
-  const int64_t nvec = a.total * a.n_kv * kVecs;
+  const int64_t nvec = a.total * slots_per_token * kVecs;
+  const int seq = (int)a.seq, slots = (int)a.slots;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t tok = i / (a.n_kv * kVecs);
-    const int rem = (int)(i - tok * (a.n_kv * kVecs));
-    const int hk = rem / kVecs, c = (rem % kVecs) * 4;
-    const int64_t src = tok * (int64_t)a.n_heads * kD + (int64_t)hk * group * kD + c;
-    float k1[4] = {0.f, 0.f, 0.f, 0.f}, k2[4] = {0.f, 0.f, 0.f, 0.f};
+    const int64_t tok = i / (slots_per_token * kVecs);
+    const int rem = (int)(i - tok * (slots_per_token * kVecs));
+    const int slot = rem / kVecs, c = (rem % kVecs) * 4;
+    const int64_t pos = __ldg(a.pos_idx + tok);
+    const int tp = (pos >= 0 && pos < slots) ? (int)pos % seq : -1;
+    uint16_t *row = a.dqkv + tok * a.ld_qkv;
+    float g1[4], g2[4];
     float v1[4] = {0.f, 0.f, 0.f, 0.f}, v2[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < group; ++j) {
-      const int64_t o = src + (int64_t)j * kD;
-      const float4 xk1 = __ldg(reinterpret_cast<const float4 *>(a.dk_part + o));
-      const float4 xk2 = __ldg(reinterpret_cast<const float4 *>(a.dk_part + o + 64));
-      const float4 xv1 = __ldg(reinterpret_cast<const float4 *>(a.dv_part + o));
-      const float4 xv2 = __ldg(reinterpret_cast<const float4 *>(a.dv_part + o + 64));
-      k1[0] += xk1.x; k1[1] += xk1.y; k1[2] += xk1.z; k1[3] += xk1.w;
-      k2[0] += xk2.x; k2[1] += xk2.y; k2[2] += xk2.z; k2[3] += xk2.w;
-      v1[0] += xv1.x; v1[1] += xv1.y; v1[2] += xv1.z; v1[3] += xv1.w;
-      v2[0] += xv2.x; v2[1] += xv2.y; v2[2] += xv2.z; v2[3] += xv2.w;
-    }
-    const int64_t tp = rope_row(a, tok);
-    float o1[4], o2[4];
+    uint16_t *dst;
+    const bool is_q = slot < a.n_heads;
+    if (is_q) {
+      dst = row + (int64_t)slot * kD + c;
+      const uint2 x1 = *reinterpret_cast<const uint2 *>(dst);
+      const uint2 x2 = *reinterpret_cast<const uint2 *>(dst + 64);
+      const float2 p0 = unpack_half2(x1.x), p1 = unpack_half2(x1.y);
+      const float2 p2 = unpack_half2(x2.x), p3 = unpack_half2(x2.y);
+      g1[0] = p0.x; g1[1] = p0.y; g1[2] = p1.x; g1[3] = p1.y;
+      g2[0] = p2.x; g2[1] = p2.y; g2[2] = p3.x; g2[3] = p3.y;
+    } else {
+      const int hk = slot - a.n_heads;
+      const int64_t src = tok * (int64_t)a.n_heads * kD + (int64_t)hk * group * kD + c;
+      float k1[4] = {0.f, 0.f, 0.f, 0.f}, k2[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < group; ++j) {
+        const int64_t o = src + (int64_t)j * kD;
+        const float4 xk1 = __ldg(reinterpret_cast<const float4 *>(a.dk_part + o));
+        const float4 xk2 = __ldg(reinterpret_cast<const float4 *>(a.dk_part + o + 64));
+        const float4 xv1 = __ldg(reinterpret_cast<const float4 *>(a.dv_part + o));
+        const float4 xv2 = __ldg(reinterpret_cast<const float4 *>(a.dv_part + o + 64));
+        k1[0] += xk1.x; k1[1] += xk1.y; k1[2] += xk1.z; k1[3] += xk1.w;
+        k2[0] += xk2.x; k2[1] += xk2.y; k2[2] += xk2.z; k2[3] += xk2.w;
+        v1[0] += xv1.x; v1[1] += xv1.y; v1[2] += xv1.z; v1[3] += xv1.w;
+        v2[0] += xv2.x; v2[1] += xv2.y; v2[2] += xv2.z; v2[3] += xv2.w;
+      }
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if (tp >= 0) {
-        rope_back(a, tp, c + e, k1[e], k2[e], o1[e], o2[e]);
-      } else {
-        o1[e] = o2[e] = 0.f;
-        v1[e] = v2[e] = 0.f;
+      for (int e = 0; e < 4; ++e) {  // the fp16 gradients the separate rotation would read
+        g1[e] = __half2float(__float2half_rn(k1[e]));
+        g2[e] = __half2float(__float2half_rn(k2[e]));
+      }
+      dst = row + (int64_t)(a.n_heads + hk) * kD + c;
+      uint16_t *dv = row + (int64_t)(a.n_heads + a.n_kv + hk) * kD + c;
+      if (tp < 0) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v1[e] = v2[e] = 0.f;
+      }
+      *reinterpret_cast<uint2 *>(dv) =
+          make_uint2(pack_half2(v1[0], v1[1]), pack_half2(v1[2], v1[3]));
+      *reinterpret_cast<uint2 *>(dv + 64) =
+          make_uint2(pack_half2(v2[0], v2[1]), pack_half2(v2[2], v2[3]));
+    }
+    float o1[4] = {0.f, 0.f, 0.f, 0.f}, o2[4] = {0.f, 0.f, 0.f, 0.f};
+    if (tp >= 0) {
+      const float *cr = a.cosv + (int64_t)tp * kD + c, *sr = a.sinv + (int64_t)tp * kD + c;
+      const float4 c1 = __ldg(reinterpret_cast<const float4 *>(cr));
+      const float4 c2 = __ldg(reinterpret_cast<const float4 *>(cr + 64));
+      const float4 s1 = __ldg(reinterpret_cast<const float4 *>(sr));
+      const float4 s2 = __ldg(reinterpret_cast<const float4 *>(sr + 64));
+      const float cc1[4] = {c1.x, c1.y, c1.z, c1.w}, cc2[4] = {c2.x, c2.y, c2.z, c2.w};
+      const float ss1[4] = {s1.x, s1.y, s1.z, s1.w}, ss2[4] = {s2.x, s2.y, s2.z, s2.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        o1[e] = g1[e] * cc1[e] + g2[e] * ss2[e];
+        o2[e] = g2[e] * cc2[e] - g1[e] * ss1[e];
       }
     }
-    uint16_t *row = a.dqkv + tok * a.ld_qkv;
-    uint16_t *dk = row + (int64_t)(a.n_heads + hk) * kD + c;
-    uint16_t *dv = row + (int64_t)(a.n_heads + a.n_kv + hk) * kD + c;
-    *reinterpret_cast<uint2 *>(dk) = make_uint2(pack_half2(o1[0], o1[1]), pack_half2(o1[2], o1[3]));
-    *reinterpret_cast<uint2 *>(dk + 64) =
+    *reinterpret_cast<uint2 *>(dst) = make_uint2(pack_half2(o1[0], o1[1]), pack_half2(o1[2], o1[3]));
+    *reinterpret_cast<uint2 *>(dst + 64) =
         make_uint2(pack_half2(o2[0], o2[1]), pack_half2(o2[2], o2[3]));
-    *reinterpret_cast<uint2 *>(dv) = make_uint2(pack_half2(v1[0], v1[1]), pack_half2(v1[2], v1[3]));
-    *reinterpret_cast<uint2 *>(dv + 64) =
-        make_uint2(pack_half2(v2[0], v2[1]), pack_half2(v2[2], v2[3]));
   }
 }
 
@@ -896,11 +893,12 @@ extern "C" int tb_attn_varlen_bwd_rope(const uint16_t *q, const uint16_t *k, con
   if (!out || !dout || !lse || !cos || !sin || !pos_idx || !dqkv || !delta || !dk_part ||
       !dv_part)
     return set_error(TB_EINVAL, "attn_varlen_bwd_rope: every buffer is required");
-  if (seq <= 0 || slots < 0 || ld_qkv < (int64_t)(n_heads + 2 * n_kv) * kD || ld_qkv % 8 != 0)
+  if (seq <= 0 || slots < 0 || slots > 0x7fffffffLL || seq > 0x7fffffffLL ||
+      ld_qkv < (int64_t)(n_heads + 2 * n_kv) * kD || ld_qkv % 8 != 0)
     return set_error(TB_EINVAL, "attn_varlen_bwd_rope: seq %lld slots %lld ld_qkv %lld",
                      (long long)seq, (long long)slots, (long long)ld_qkv);
   if (!aligned(out, 16) || !aligned(dout, 16) || !aligned(dqkv, 16) || !aligned(dk_part, 16) ||
-      !aligned(dv_part, 16))
+      !aligned(dv_part, 16) || !aligned(cos, 16) || !aligned(sin, 16))
     return set_error(TB_EALIGN, "attn_varlen_bwd_rope: 16-byte aligned buffers are required");
   if (batch == 0 || total == 0 || max_len == 0) return TB_OK;
   const size_t smem = 10 * kTileHalves * sizeof(uint16_t);
@@ -918,9 +916,9 @@ extern "C" int tb_attn_varlen_bwd_rope(const uint16_t *q, const uint16_t *k, con
   if (rc != TB_OK) return rc;
   rc = launch("attn_varlen_bwd_rope dkv", attn_bwd_dkv_kernel, grid, kCtaThreads, smem, st, a);
   if (rc != TB_OK) return rc;
-  const int64_t nvec = total * n_kv * (kD / 8);
+  const int64_t nvec = total * (n_heads + n_kv) * (kD / 8);
   int64_t blocks = (nvec + 255) / 256;
   if (blocks > (int64_t)sm_count() * 8) blocks = (int64_t)sm_count() * 8;
-  return launch("attn_varlen_bwd_rope gsum", attn_bwd_gsum_rope_kernel, (unsigned)blocks, 256,
+  return launch("attn_varlen_bwd_rope rotate", attn_bwd_gsum_rope_kernel, (unsigned)blocks, 256,
                 0, st, a);
 }
