@@ -280,7 +280,8 @@ int tb_lora_dropout_grad_expand(const uint16_t *dh_q, const uint16_t *a16_q, con
 /* The rank-16 LoRA backward of both adapters (q, then v; an adapter whose g is NULL is skipped)
  * in two launches, in place of the six cuBLAS GEMMs of peft's lora_B(lora_A(x)) * scaling
  * backward under fp16 autocast (solution/model.py:195-206). Per adapter: g fp16 [rows, width]
- * (the output gradient), h fp16 [rows, 16] (lora_A's output), b16 = fp16(lora_B) [width, 16],
+ * with row stride ld_g_q / ld_g_v (>= width, a multiple of 8: the output gradient, for example
+ * the adapter's columns of the q|k|v gradient, read in place), h fp16 [rows, 16] (lora_A's output), b16 = fp16(lora_B) [width, 16],
  * x16 fp16 [rows, hidden] (lora_A's input):
  *   dh = fp16(scale * g . b16)    [rows, 16] fp16
  *   db = scale * g^T . h          [width, 16] fp32 (added into db when its accumulate bit is set)
@@ -292,7 +293,8 @@ int tb_lora_backward(const uint16_t *g_q, const uint16_t *h_q, const uint16_t *b
                      int64_t width_q, float scale_q, const uint16_t *g_v, const uint16_t *h_v,
                      const uint16_t *b16_v, const uint16_t *x16_v, uint16_t *dh_v, float *db_v,
                      float *da_v, int64_t width_v, float scale_v, int64_t rows, int64_t hidden,
-                     int32_t rank, int32_t accumulate, void *stream);
+                     int32_t rank, int32_t accumulate, int64_t ld_g_q, int64_t ld_g_v,
+                     void *stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Causal attention over packed variable-length sequences with grouped key/value heads. Replaces

@@ -53,10 +53,35 @@ def _run(q, v, rows, hidden, accumulate):
         return [_lib.ptr(ad[k]) for k in ("g", "h", "b16", "x16", "dh", "db", "da")] + \
             [ad["g"].shape[1], ad["scale"]]
 
-    rc = _entry()(*parts(q), *parts(v), rows, hidden, 16, accumulate, _lib.stream_of(
-        torch.empty(0, device="cuda")))
+    ld = [0 if ad is None else ad["g"].stride(0) for ad in (q, v)]
+    rc = _entry()(*parts(q), *parts(v), rows, hidden, 16, accumulate, ld[0], ld[1],
+                  _lib.stream_of(torch.empty(0, device="cuda")))
     assert rc == 0, _lib.load().tb_last_error()
     torch.cuda.synchronize()
+
+
+def test_gradients_read_in_place_from_the_qkv_gradient():
+    """g of each adapter given as its columns of one [rows, 2048] q|k|v gradient (row stride
+    2048, v starting at column 1792), as the step passes them: the same results as contiguous
+    copies, bit for bit."""
+    rows, hidden = 621, 1536
+    q = _adapter(rows, 1536, hidden, 2.0, seed=3)
+    v = _adapter(rows, 256, hidden, 2.0, seed=4)
+    dqkv = torch.zeros(rows, 2048, dtype=torch.float16, device="cuda")
+    dqkv[:, :1536] = q["g"]
+    dqkv[:, 1792:] = v["g"]
+    _run(q, v, rows, hidden, 0)
+    dense = [(ad["dh"].clone(), ad["db"].clone(), ad["da"].clone()) for ad in (q, v)]
+    q2 = dict(q, g=dqkv[:, :1536], dh=torch.empty_like(q["dh"]), db=torch.empty_like(q["db"]),
+              da=torch.empty_like(q["da"]))
+    v2 = dict(v, g=dqkv[:, 1792:], dh=torch.empty_like(v["dh"]), db=torch.empty_like(v["db"]),
+              da=torch.empty_like(v["da"]))
+    assert q2["g"].stride(0) == 2048 and not q2["g"].is_contiguous()
+    _run(q2, v2, rows, hidden, 0)
+    for ad, (dh, db, da) in zip((q2, v2), dense):
+        assert torch.equal(ad["dh"], dh)
+        assert torch.equal(ad["db"], db)
+        assert torch.equal(ad["da"], da)
 
 
 @pytest.mark.parametrize("rows", [1, 37, 621])

@@ -12,7 +12,9 @@
 // staged through shared memory (cp.async, the next block copied while one is used) and read
 // with ldmatrix, one CTA per (64-query block, head, sequence), two warp groups per CTA taking
 // alternate key (or query) blocks and merging their partial results at the end, so a CTA's
-// serial chain is half its blocks:
+// serial chain is half its blocks. The grid is (heads, sequences, blocks) with the blocks that
+// have the most work launched first (the last query block; for dK/dV key block 0), so at one
+// CTA per SM the CTAs left for a second wave are the shortest:
 //   forward   S = Q K^T, online softmax in base 2 (the scale folded with log2 e), O += P V;
 //             writes O (fp16) and the base-2 log-sum-exp per (head, query) for the backward.
 // Rows of a sequence's last block past its length are computed but never stored.
@@ -113,7 +115,9 @@ __global__ void __launch_bounds__(kCtaThreads) attn_fwd_kernel(const __grid_cons
   // tile 0: Q; warp group w: tiles 1 + 4w .. 4 + 4w, (K, V) twice: its next key block is
   // copied while it uses one. Group w takes key blocks w, w + 2, ...; the two online-softmax
   // states are merged at the end.
-  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // grid (heads, batch, query blocks), the last query block first: the longest causal blocks
+  // start in the first wave and the shortest fill the tail
+  const int qb = (int)(gridDim.z - 1 - blockIdx.z), h = blockIdx.x, b = blockIdx.y;
   const int start = __ldg(a.cu + b), len = __ldg(a.cu + b + 1) - start;
   const int q0 = qb * kBlock;
   if (q0 >= len) return;
@@ -331,7 +335,9 @@ __global__ void __launch_bounds__(kCtaThreads) attn_bwd_dq_kernel(const __grid_c
   // tiles 0, 1: Q, dO; warp group w: tiles 2 + 4w .. 5 + 4w, (K, V) twice. Group w takes key
   // blocks w, w + 2, ...; the two dQ partials are added at the end (group 0's first).
   uint16_t *Qs = smem, *dOs = smem + kTileHalves;
-  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // grid (heads, batch, query blocks), the last query block first: the longest causal blocks
+  // start in the first wave and the shortest fill the tail
+  const int qb = (int)(gridDim.z - 1 - blockIdx.z), h = blockIdx.x, b = blockIdx.y;
   const int start = __ldg(a.cu + b), len = __ldg(a.cu + b + 1) - start;
   const int q0 = qb * kBlock;
   if (q0 >= len) return;
@@ -503,7 +509,8 @@ __global__ void __launch_bounds__(kCtaThreads) attn_bwd_dkv_kernel(const __grid_
   // blocks kb + w, kb + w + 2, ...; the two dK / dV partials are added at the end (group 0's
   // first).
   uint16_t *Ks = smem, *Vs = smem + kTileHalves;
-  const int kb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // grid (heads, batch, key blocks), key block 0 (which every query block sees) first
+  const int kb = blockIdx.z, h = blockIdx.x, b = blockIdx.y;
   const int start = __ldg(a.cu + b), len = __ldg(a.cu + b + 1) - start;
   const int k0 = kb * kBlock;
   if (k0 >= len) return;
@@ -804,7 +811,8 @@ int check_attn(const char *what, const void *q, const void *k, const void *v, co
   if (batch < 0 || total < 0 || max_len < 0 || n_heads < 1 || n_kv < 1 || n_heads % n_kv)
     return set_error(TB_EINVAL, "%s: batch %lld total %lld max_len %lld heads %d/%d", what,
                      (long long)batch, (long long)total, (long long)max_len, n_heads, n_kv);
-  if (batch > 65535 || n_heads > 65535 || max_len > (1LL << 30) || total > (1LL << 31))
+  if (batch > 65535 || n_heads > 65535 || (max_len + kBlock - 1) / kBlock > 65535 ||
+      total > (1LL << 31))
     return set_error(TB_EINVAL, "%s: sizes too large", what);
   if (!q || !k || !v || !cu) return set_error(TB_EINVAL, "%s: q, k, v, cu_seqlens required", what);
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16))
@@ -833,7 +841,7 @@ extern "C" int tb_attn_varlen_fwd(const uint16_t *q, const uint16_t *k, const ui
                            (int)smem) != cudaSuccess)
     return check_launch("attn_varlen_fwd attribute");
   FwdArgs a{q, k, v, cu_seqlens, out, lse, total, n_heads, n_kv, scale * 1.4426950408889634f};
-  const dim3 grid((unsigned)((max_len + kBlock - 1) / kBlock), (unsigned)n_heads, (unsigned)batch);
+  const dim3 grid((unsigned)n_heads, (unsigned)batch, (unsigned)((max_len + kBlock - 1) / kBlock));
   return launch("attn_varlen_fwd", attn_fwd_kernel, grid, kCtaThreads, smem, as_stream(stream), a);
 }
 
@@ -861,7 +869,7 @@ extern "C" int tb_attn_varlen_bwd(const uint16_t *q, const uint16_t *k, const ui
   BwdArgs a{q,     k,      v,       out,     dout,    lse,     cu_seqlens,
             delta, dq,     dk_part, dv_part, total,   n_heads, n_kv,
             scale, scale * 1.4426950408889634f, nullptr, 0, nullptr, nullptr, nullptr, 0, 0};
-  const dim3 grid((unsigned)((max_len + kBlock - 1) / kBlock), (unsigned)n_heads, (unsigned)batch);
+  const dim3 grid((unsigned)n_heads, (unsigned)batch, (unsigned)((max_len + kBlock - 1) / kBlock));
   cudaStream_t st = as_stream(stream);
   rc = launch("attn_varlen_bwd dq", attn_bwd_dq_kernel, grid, kCtaThreads, smem, st, a);
   if (rc != TB_OK) return rc;
@@ -910,7 +918,7 @@ extern "C" int tb_attn_varlen_bwd_rope(const uint16_t *q, const uint16_t *k, con
   BwdArgs a{q,     k,      v,       out,     dout,    lse,     cu_seqlens,
             delta, nullptr, dk_part, dv_part, total,  n_heads, n_kv,
             scale, scale * 1.4426950408889634f, dqkv, ld_qkv, cos, sin, pos_idx, seq, slots};
-  const dim3 grid((unsigned)((max_len + kBlock - 1) / kBlock), (unsigned)n_heads, (unsigned)batch);
+  const dim3 grid((unsigned)n_heads, (unsigned)batch, (unsigned)((max_len + kBlock - 1) / kBlock));
   cudaStream_t st = as_stream(stream);
   rc = launch("attn_varlen_bwd_rope dq", attn_bwd_dq_kernel, grid, kCtaThreads, smem, st, a);
   if (rc != TB_OK) return rc;

@@ -33,7 +33,7 @@ constexpr int kSmemBytes = kWarps * kWarpHalves * 2;    // 48 KB
 static_assert(kWarps * 16 * kCols * 4 <= kSmemBytes, "the reduction reuses the staging buffers");
 
 struct Adapter {
-  const uint16_t *g;    // fp16 [M, W]
+  const uint16_t *g;    // fp16 [M, W], row stride ld_g
   const uint16_t *h;    // fp16 [M, 16]
   const uint16_t *b16;  // fp16 [W, 16]
   const uint16_t *x16;  // fp16 [M, H]
@@ -41,6 +41,7 @@ struct Adapter {
   float *db;            // fp32 [W, 16]
   float *da;            // fp32 [16, H]
   int width;            // W
+  int64_t ld_g;         // row stride of g (>= W)
   float scale;
   bool acc_db, acc_da;
 };
@@ -95,8 +96,8 @@ __device__ void dh_rows(const Adapter &ad, int rows, int m0, uint16_t *wbuf, flo
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int chunks = ad.width >> 4;
   const bool r0_in = m0 + g < rows, r1_in = m0 + g + 8 < rows;
-  const uint16_t *g0 = ad.g + (int64_t)(r0_in ? m0 + g : 0) * ad.width + 2 * t;
-  const uint16_t *g1 = ad.g + (int64_t)(r1_in ? m0 + g + 8 : 0) * ad.width + 2 * t;
+  const uint16_t *g0 = ad.g + (int64_t)(r0_in ? m0 + g : 0) * ad.ld_g + 2 * t;
+  const uint16_t *g1 = ad.g + (int64_t)(r1_in ? m0 + g + 8 : 0) * ad.ld_g + 2 * t;
   float c[2][4] = {};
   auto stage = [&](int kc, int b) {  // 16 rows x 32 bytes: one 16-byte copy per lane
     const int r = lane >> 1, col = (lane & 1) * 8;
@@ -257,7 +258,7 @@ __global__ void __launch_bounds__(kThreads) lora_bwd_dh_db(const __grid_constant
   const int j = cta < a.nb[0] ? 0 : 1;
   const int blk = j == 0 ? cta : cta - a.nb[0];
   const Adapter &ad = a.ad[j];
-  tn_cols(ad.h, ad.g, ad.width, a.rows, blk * kCols, ad.scale, ad.db, 0, true, ad.acc_db, smem);
+  tn_cols(ad.h, ad.g, ad.ld_g, a.rows, blk * kCols, ad.scale, ad.db, 0, true, ad.acc_db, smem);
 }
 
 // kernel 2: dA of adapter 0 (CTAs [0, hb[0])) and adapter 1
@@ -287,7 +288,8 @@ extern "C" int tb_lora_backward(const uint16_t *g_q, const uint16_t *h_q, const 
                                 const uint16_t *h_v, const uint16_t *b16_v, const uint16_t *x16_v,
                                 uint16_t *dh_v, float *db_v, float *da_v, int64_t width_v,
                                 float scale_v, int64_t rows, int64_t hidden, int32_t rank,
-                                int32_t accumulate, void *stream) {
+                                int32_t accumulate, int64_t ld_g_q, int64_t ld_g_v,
+                                void *stream) {
   if (rank != kRank) return set_error(TB_EINVAL, "lora_backward: rank %d (the kernels take 16)", rank);
   if (rows < 0 || rows > (1LL << 24) || hidden <= 0 || hidden % kCols != 0 || hidden > (1LL << 20))
     return set_error(TB_EINVAL, "lora_backward: rows %lld hidden %lld (a multiple of %d)",
@@ -297,7 +299,7 @@ extern "C" int tb_lora_backward(const uint16_t *g_q, const uint16_t *h_q, const 
                  *xs[2] = {x16_q, x16_v};
   uint16_t *dhs[2] = {dh_q, dh_v};
   float *dbs[2] = {db_q, db_v}, *das[2] = {da_q, da_v};
-  const int64_t widths[2] = {width_q, width_v};
+  const int64_t widths[2] = {width_q, width_v}, lds[2] = {ld_g_q, ld_g_v};
   const float scales[2] = {scale_q, scale_v};
   for (int j = 0; j < 2; ++j) {
     Adapter &ad = a.ad[j];
@@ -310,6 +312,9 @@ extern "C" int tb_lora_backward(const uint16_t *g_q, const uint16_t *h_q, const 
     if (widths[j] <= 0 || widths[j] % kCols != 0 || widths[j] > (1LL << 20))
       return set_error(TB_EINVAL, "lora_backward: adapter %d width %lld (a multiple of %d)", j,
                        (long long)widths[j], kCols);
+    if (lds[j] < widths[j] || lds[j] % 8 != 0)
+      return set_error(TB_EINVAL, "lora_backward: adapter %d row stride %lld (>= width, 16-byte "
+                       "rows)", j, (long long)lds[j]);
     // g, h, B16, x16 and dh (kernel 2 reads it back) go through 16-byte cp.async copies
     if (!aligned(gs[j], 16) || !aligned(hs[j], 16) || !aligned(bs[j], 16) || !aligned(xs[j], 16) ||
         !aligned(dhs[j], 16) || !aligned(dbs[j], 4) || !aligned(das[j], 4))
@@ -322,6 +327,7 @@ extern "C" int tb_lora_backward(const uint16_t *g_q, const uint16_t *h_q, const 
     ad.db = dbs[j];
     ad.da = das[j];
     ad.width = (int)widths[j];
+    ad.ld_g = lds[j];
     ad.scale = scales[j];
     ad.acc_db = (accumulate >> (2 * j)) & 1;
     ad.acc_da = (accumulate >> (2 * j + 1)) & 1;

@@ -50,7 +50,7 @@ class LoraPairFused(LoraPair):
         # `keep` holds every tensor whose pointer goes into `args` until the launch: a
         # contiguous copy made for one adapter must not be freed (and its memory handed to the
         # next adapter's outputs) before the kernel has read it
-        args, keep, grads, dhs, a16s, accumulate = [], [], [], [], [], 0
+        args, keep, grads, dhs, a16s, accumulate, strides = [], [], [], [], [], 0, [0, 0]
         with torch.autocast("cuda", enabled=False):
             for j, ((g_out, x16, h, a16, b16, s), (pa, pb)) in enumerate(
                     zip(adapters, ((pa_q, pb_q), (pa_v, pb_v)))):
@@ -63,7 +63,12 @@ class LoraPairFused(LoraPair):
                 width = b16.shape[0]
                 if g_out is None:
                     g_out = torch.zeros((rows, width), dtype=_F16, device=x16.device)
-                g_out = g_out.to(_F16).contiguous()
+                # read in place when it is a row-strided view (the adapter's columns of the q|k|v
+                # gradient): only the rows need to be 16-byte aligned and dense
+                if not (g_out.dtype == _F16 and g_out.stride(1) == 1 and g_out.stride(0) % 8 == 0
+                        and g_out.data_ptr() % 16 == 0 and g_out.stride(0) >= width):
+                    g_out = g_out.to(_F16).contiguous()
+                strides[j] = g_out.stride(0)
                 dh = torch.empty((rows, _RANK), dtype=_F16, device=x16.device)
                 # weight gradients: into the bucket views (accumulated) or fresh fp32 tensors
                 if _in_bucket(pb):
@@ -85,7 +90,8 @@ class LoraPairFused(LoraPair):
                 grads += [da, db]
                 dhs.append(dh)
                 a16s.append(a16.contiguous())
-            rc = fn(*args, rows, ctx.hidden, _RANK, accumulate, _lib.stream_of(pos_idx))
+            rc = fn(*args, rows, ctx.hidden, _RANK, accumulate, strides[0], strides[1],
+                    _lib.stream_of(pos_idx))
             del keep
             if rc != 0:
                 msg = _lib.load().tb_last_error().decode(errors="replace")
