@@ -28,6 +28,7 @@ The reference arm (--impl reference) times that CPU step alone.
 import argparse
 import ctypes
 import datetime
+import faulthandler
 import json
 import os
 import subprocess
@@ -62,8 +63,13 @@ def setup(args):
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
-        dist.init_process_group("nccl" if args.impl == "ours" else "gloo",
-                                timeout=datetime.timedelta(seconds=300))
+        if args.impl == "ours":
+            # the rank's GPU is current before NCCL sets up, and the group is bound to it
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device(f"cuda:{local}"))
+        else:
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
     return rank, world, local
 
 
@@ -1253,6 +1259,7 @@ def main():
         return
     if args.warmup < 3:
         args.warmup = 3
+    faulthandler.enable()  # a native crash prints the Python stack of every thread
     rank, world, local = setup(args)
     try:
         if args.impl == "reference":

@@ -121,10 +121,10 @@ def _tc_head(h, weight, tgt, entropy, token_loss, correct, grad, order, n_labell
 
 
 # True: dh = dlogits . W through tb_head_dh (dlogits formed inside the tensor-core GEMM, never
-# written). Off by default: at config 4 the fused GEMM measured 1.11 ms against 0.57 ms for the
-# in-place dlogits pass + cuBLAS (it re-reads the fp16 logits once per 512 hidden columns and its
-# pipeline stays latency-bound, tensor pipe 29 % active). Same results either way within the
-# fp32 summation order; the tests run both.
+# written). Off by default: at config 4 it measured 0.66 ms against 0.50 ms for the in-place
+# dlogits pass + cuBLAS, whose GEMM runs at the measured dense peak; the fused kernel reads W and
+# the logits once but stays latency-bound (tensor pipe 55 % active). Same results either way
+# within the fp32 summation order; the tests run both.
 USE_TENSOR_CORE_DH = False
 
 
