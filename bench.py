@@ -735,10 +735,14 @@ def _kernel_case(name, device):
             + (2 * r * hidden + (hidden + 256) * r) * (4 + 2) + m * 8
         info = {"config": "3", "tokens": m, "hidden": hidden, "rank": r,
                 "outputs": [hidden, 256]}
-    elif name in ("attn_fwd", "attn_fwd_bwd"):  # a layer's attention at config 5's lengths
+    elif name in ("attn_fwd", "attn_fwd_tc", "attn_fwd_bwd"):  # a layer's attention, config 5
         import math
 
+        from testt_b200 import attention
         from testt_b200.attention import varlen_attention
+
+        # attn_fwd_tc: the tcgen05 forward (tb_attn_varlen_fwd_tc) on the same inputs
+        attention.USE_TENSOR_CORE_FWD = name == "attn_fwd_tc"
 
         lengths = synth.lengths(seed=0)
         total = sum(lengths)
@@ -749,7 +753,7 @@ def _kernel_case(name, device):
         cu[1:] = torch.tensor(lengths, device=dev).cumsum(0)
         dout = torch.randn((total, 12, 128), generator=g, device=dev).half()
         scale, top = 1.0 / math.sqrt(128), max(lengths)
-        if name == "attn_fwd":
+        if name != "attn_fwd_bwd":
             fn = lambda: varlen_attention(q, k, v, cu, top, scale)  # noqa: E731
         else:
             fn = lambda: torch.autograd.grad(  # noqa: E731
@@ -759,7 +763,7 @@ def _kernel_case(name, device):
         fwd = sum(2 * n * (n + 1) // 2 * 12 * 128 * 2 for n in lengths)
         nbytes = 0
         info = {"config": "5 (one layer)", "lengths": lengths, "heads": [12, 2], "head_dim": 128,
-                "flops": fwd if name == "attn_fwd" else int(3.5 * fwd)}
+                "flops": fwd if name != "attn_fwd_bwd" else int(3.5 * fwd)}
     elif name == "head_tc":
         c = synth.config4(dev)
         rows, hidden, vocab = 2048, synth.HIDDEN, synth.VOCAB
@@ -1242,7 +1246,7 @@ def main():
     ap.add_argument("--kernel", default=None,
                     help="time one kernel at its configuration instead (nf4, nf4_nested, "
                          "rmsnorm_fwd, rmsnorm_bwd, rope_fwd, rope_bwd, swiglu_fwd, swiglu_bwd, "
-                         "lora_fwd, attn_fwd, attn_fwd_bwd, "
+                         "lora_fwd, attn_fwd, attn_fwd_tc, attn_fwd_bwd, "
                          "head_stats, head_tc, head_full, head_cublas, head_dh, "
                          "head_dh_cublas, all; the NF4-decoding GEMMs, "
                          "with what they replace: gate_up_fused_fwd, gate_up_fused_bwd, "

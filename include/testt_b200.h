@@ -312,6 +312,17 @@ int tb_attn_varlen_fwd(const uint16_t *q, const uint16_t *k, const uint16_t *v,
                        int64_t total, int64_t max_len, int32_t n_heads, int32_t n_kv,
                        int32_t head_dim, float scale, void *stream);
 
+/* tb_attn_varlen_fwd on the 5th-generation tensor cores (same arguments, outputs and
+ * tolerances): a CTA per 128 queries of a head of a sequence; S = q k^T and O = P v accumulate
+ * in tensor memory (tcgen05.mma, q / k / v tiles by TMA), P is written to tensor memory as the
+ * A operand of P v; two passes over the key tiles (the row maximum, then P, the row sum and O),
+ * so O is never rescaled. sm_100 only; q, k, v, out 16-byte aligned. Replaces the same SDPA call,
+ * solution/model.py:242-247. */
+int tb_attn_varlen_fwd_tc(const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                          const int32_t *cu_seqlens, uint16_t *out, float *lse, int64_t batch,
+                          int64_t total, int64_t max_len, int32_t n_heads, int32_t n_kv,
+                          int32_t head_dim, float scale, void *stream);
+
 /* tb_attn_varlen_bwd: from the forward's q, k, v, out, lse and the output gradient dout
  *   (fp16 [total, n_heads, head_dim]): dq fp16 [total, n_heads, head_dim], dk, dv fp16
  *   [total, n_kv, head_dim] (the query heads of a group summed in head order in fp32, rounded

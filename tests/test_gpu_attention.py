@@ -31,16 +31,43 @@ def _reference(q, k, v, cu, scale):
     return ops.attention_varlen(q, k, v, cu, scale)
 
 
-@pytest.mark.parametrize("lengths", [[149, 131, 193, 148], [1, 64, 65, 7, 200], [512]])
-def test_attention_forward_matches_reference(lengths):
-    from testt_b200.attention import attn_forward
+@pytest.mark.parametrize("tensor_core", [False, True], ids=["mma_sync", "tcgen05"])
+@pytest.mark.parametrize("lengths", [[149, 131, 193, 148], [1, 64, 65, 7, 200], [512],
+                                     [129, 127, 256, 300, 2]])
+def test_attention_forward_matches_reference(lengths, tensor_core, monkeypatch):
+    """Both forwards (tb_attn_varlen_fwd, tb_attn_varlen_fwd_tc) against the fp64 oracle:
+    outputs within 4e-3, base-2 log-sum-exp within 1e-3, across sequences shorter than, equal
+    to and longer than the 128-row tiles, a one-token sequence and 4 key tiles."""
+    from testt_b200 import _lib, attention
 
+    monkeypatch.setattr(attention, "USE_TENSOR_CORE_FWD", tensor_core)
     q, k, v, cu = _case(lengths, 12, 2, sum(lengths))
     scale = 1.0 / math.sqrt(128)
-    out, lse = attn_forward(q, k, v, cu, max(lengths), scale)
+    out, lse = attention.attn_forward(q, k, v, cu, max(lengths), scale)
     ref, rlse = _reference(q, k, v, cu, scale)
     torch.testing.assert_close(out.double(), ref, rtol=0, atol=4e-3)
     torch.testing.assert_close(lse.double(), rlse, rtol=0, atol=1e-3)
+    assert _lib.wait_timeouts() == 0
+
+
+def test_tensor_core_forward_agrees_with_the_mma_sync_forward_and_other_head_groups():
+    """tb_attn_varlen_fwd_tc against tb_attn_varlen_fwd on the same inputs with 8 query heads
+    per key/value head and 4 per head: outputs within 2 fp16 ulp-scale (2e-3), lse within 1e-4."""
+    from testt_b200 import attention
+
+    for nh, nkv in ((16, 2), (8, 2)):
+        lengths = [77, 260, 131]
+        q, k, v, cu = _case(lengths, nh, nkv, 11 + nh)
+        scale = 1.0 / math.sqrt(128)
+        try:
+            attention.USE_TENSOR_CORE_FWD = True
+            out_tc, lse_tc = attention.attn_forward(q, k, v, cu, max(lengths), scale)
+            attention.USE_TENSOR_CORE_FWD = False
+            out, lse = attention.attn_forward(q, k, v, cu, max(lengths), scale)
+        finally:
+            attention.USE_TENSOR_CORE_FWD = False
+        torch.testing.assert_close(out_tc.float(), out.float(), rtol=0, atol=2e-3)
+        torch.testing.assert_close(lse_tc, lse, rtol=0, atol=1e-4)
 
 
 @pytest.mark.parametrize("lengths", [[149, 131, 193, 148], [1, 64, 65, 7, 200], [512]])

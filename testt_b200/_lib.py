@@ -41,6 +41,7 @@ SIGNATURES = {
     "tb_lora_forward": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _F, _P, _P, _P, _P, _P, _P, _P,
                         _P, _I64, _F, _P, _I64, _I64, _I32, _P],
     "tb_attn_varlen_fwd": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _F, _P],
+    "tb_attn_varlen_fwd_tc": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _F, _P],
     "tb_attn_varlen_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64,
                            _I32, _I32, _I32, _F, _P],
     "tb_attn_varlen_bwd_rope": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _P, _I64, _P,

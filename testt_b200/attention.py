@@ -20,13 +20,20 @@ def supported(q, k, v):
             and torch.cuda.get_device_capability(q.device)[0] == 10)
 
 
+# True: the forward on the 5th-generation tensor cores (tb_attn_varlen_fwd_tc: 128-query tiles,
+# S and O in tensor memory, P written there as the A operand of P V); False: the mma.sync kernel
+# (tb_attn_varlen_fwd). Same contract and tolerances; the tests run both.
+USE_TENSOR_CORE_FWD = False
+
+
 def attn_forward(q, k, v, cu_seqlens, max_len, scale):
     """(out fp16 [T, H, 128], lse fp32 [H, T] base-2) for contiguous token-major q, k, v."""
     _lib.require_cuda(q, k, v, cu_seqlens, what="varlen_attention")
     total, nh, d = q.shape
     out = torch.empty_like(q)
     lse = torch.empty((nh, total), dtype=torch.float32, device=q.device)
-    _lib.call("tb_attn_varlen_fwd", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(cu_seqlens),
+    entry = "tb_attn_varlen_fwd_tc" if USE_TENSOR_CORE_FWD else "tb_attn_varlen_fwd"
+    _lib.call(entry, _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(cu_seqlens),
               _lib.ptr(out), _lib.ptr(lse), cu_seqlens.numel() - 1, total, int(max_len), nh,
               k.shape[1], d, float(scale), _lib.stream_of(q))
     return out, lse

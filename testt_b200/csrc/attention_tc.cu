@@ -1,0 +1,488 @@
+// Variable-length causal attention forward on the 5th-generation tensor cores (tcgen05 with
+// TMEM accumulators, TMA tiles). Same contract as tb_attn_varlen_fwd (attention.cu): the
+// decoder layer's attention of solution/model.py:242-247 restricted to each sequence's real
+// rows, grouped key/value heads, head dim 128, writing O (fp16, token-major) and the base-2
+// log-sum-exp of the scaled scores per (head, query).
+//
+// A CTA takes 128 queries of one head of one sequence; the key tiles (128 keys) up to its own
+// (causal). Warps:
+//   warp 4     TMA producer: the Q tile once, then K and V tiles through a 4-slot ring in the
+//              order the MMA uses them
+//   warp 5     TMEM allocation and the MMA issuer:
+//                S = Q K^T     M128 N128 K128, both operands K-major in shared memory
+//                O += P V      M128 N128 K128, P read from TMEM, V MN-major in shared memory
+//   warps 0-3  softmax and epilogue: thread r owns query row r, the TMEM lane it reads and
+//              writes, so row statistics need no shuffles
+// Two passes over the key tiles: the first computes each row's maximum, the second P =
+// 2^(s - max) (fp16 into TMEM for the P V product) and the row sum from the same fp32 values.
+// O is accumulated with the final maximum, so it is never rescaled in TMEM; the second pass
+// recomputes Q K^T, which at these sizes costs less than moving O through registers.
+// TMEM columns: S 0-127, P 128-191 (fp16 pairs), O 256-383.
+//
+// Every mbarrier wait is bounded (mbar_wait); a role that gives up sets the CTA's error flag and
+// leaves its loop, every role meets at the final barrier and TMEM is always released. No
+// multicast is used.
+#include <cuda.h>
+#include <math_constants.h>
+
+#include "common.cuh"
+
+namespace tb {
+namespace {
+
+constexpr int kD = 128;                       // head dimension
+constexpr int kTile = 128;                    // queries per CTA, keys per tile
+constexpr int kRing = 4;                      // K / V tiles in flight
+constexpr int kBoxBytes = kTile * 64 * 2;     // 16 KB: 128 rows x 64 columns (one TMA box)
+constexpr int kTileBytes = 2 * kBoxBytes;     // 32 KB: 128 rows x 128 columns
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;
+constexpr uint32_t kColS = 0, kColP = 128, kColO = 256;
+
+// M = 128, N = 128, fp16 inputs, fp32 accumulation; S: A and B K-major
+constexpr uint32_t kIdescS = (1u << 4) | ((uint32_t)(kTile >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+// O += P V: A from TMEM (K-major), B = V MN-major (bit 16)
+constexpr uint32_t kIdescO =
+    (1u << 4) | (1u << 16) | ((uint32_t)(kD >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+
+struct Smem {
+  alignas(1024) uint8_t q[kTileBytes];
+  alignas(1024) uint8_t ring[kRing][kTileBytes];
+  uint64_t q_full, ring_full[kRing], ring_empty[kRing];
+  uint64_t s_full, s_read, p_full, p_free, o_full, mma_done;
+  uint32_t tmem_base;
+  volatile int error;
+};
+
+static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory of an attention CTA");
+
+struct TcArgs {
+  const int32_t *cu;
+  uint16_t *out;
+  float *lse;  // [n_heads, total]
+  int64_t total;
+  int n_heads, n_kv;
+  float scale_log2;
+};
+
+// K-major, 128-byte swizzle: SBO 1024 bytes between 8-row atoms, sm_100 descriptor version
+__device__ __forceinline__ uint64_t desc_k(uint32_t addr) {
+  uint64_t d = (uint64_t)((addr >> 4) & 0x3fff);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// MN-major, 128-byte swizzle: LBO = one box between the two 64-column halves of N, SBO 1024
+// bytes between 8-row groups along K
+__device__ __forceinline__ uint64_t desc_mn(uint32_t addr) {
+  uint64_t d = (uint64_t)((addr >> 4) & 0x3fff);
+  d |= (uint64_t)(kBoxBytes >> 4) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                       uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                       uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::
+                   "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
+__device__ __forceinline__ float ex2a(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Tile i of the producer / MMA order: pass 1 K0 .. K(n-1), pass 2 K0, V0, K1, V1, ...
+__device__ __forceinline__ void tile_of(int i, int n, bool &is_v, int &kt) {
+  if (i < n) {
+    is_v = false;
+    kt = i;
+  } else {
+    is_v = ((i - n) & 1) != 0;
+    kt = (i - n) >> 1;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_q,
+                       const __grid_constant__ CUtensorMap map_k,
+                       const __grid_constant__ CUtensorMap map_v, const __grid_constant__ TcArgs a) {
+  pdl_wait();
+  pdl_release();
+  // grid (heads, sequences, query tiles), the last query tile first (the most key tiles)
+  const int qt = (int)(gridDim.z - 1 - blockIdx.z), h = blockIdx.x, b = blockIdx.y;
+  const int start = __ldg(a.cu + b), len = __ldg(a.cu + b + 1) - start;
+  const int q0 = qt * kTile;
+  if (q0 >= len) return;  // the whole CTA, before any barrier or allocation
+  extern __shared__ uint8_t smem_raw[];
+  Smem &sm = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                        ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hk = h / (a.n_heads / a.n_kv);
+  const int n = min(qt, (len - 1) / kTile) + 1;  // key tiles 0 .. n-1 (causal)
+  const int tiles = 3 * n;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    for (int s = 0; s < kRing; ++s) {
+      mbar_init(&sm.ring_full[s], 1);
+      mbar_init(&sm.ring_empty[s], 1);
+    }
+    mbar_init(&sm.s_full, 1);
+    mbar_init(&sm.s_read, 4);  // the 4 softmax warps
+    mbar_init(&sm.p_full, 4);
+    mbar_init(&sm.p_free, 1);
+    mbar_init(&sm.o_full, 1);
+    mbar_init(&sm.mma_done, 1);
+    sm.error = 0;
+    mbar_init_fence();
+  }
+  if (warp == 5) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&sm.tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 4) {
+    // ---- TMA producer -----------------------------------------------------------------------
+    if (lane == 0) {
+      mbar_expect_tx(&sm.q_full, kTileBytes);
+      for (int x = 0; x < 2; ++x)
+        tma_load_2d(smem_u32(sm.q) + (uint32_t)(x * kBoxBytes), &map_q, h * kD + x * 64,
+                    start + q0, &sm.q_full);
+      int issued = 0;
+      for (int i = 0; i < tiles && !sm.error; ++i) {
+        const int s = i % kRing;
+        if (!mbar_wait(&sm.ring_empty[s], (uint32_t)(((i / kRing) & 1) ^ 1))) {
+          sm.error = 1;
+          break;
+        }
+        bool is_v;
+        int kt;
+        tile_of(i, n, is_v, kt);
+        mbar_expect_tx(&sm.ring_full[s], kTileBytes);
+        for (int x = 0; x < 2; ++x)
+          tma_load_2d(smem_u32(sm.ring[s]) + (uint32_t)(x * kBoxBytes), is_v ? &map_v : &map_k,
+                      hk * kD + x * 64, start + kt * kTile, &sm.ring_full[s]);
+        ++issued;
+      }
+      // every copy issued must have landed before the CTA may leave (bounded)
+      mbar_wait(&sm.q_full, 0);
+      for (int i = issued - (issued < kRing ? issued : kRing); i < issued; ++i)
+        mbar_wait(&sm.ring_full[i % kRing], (uint32_t)((i / kRing) & 1));
+    }
+  } else if (warp == 5) {
+    // ---- MMA issuer -------------------------------------------------------------------------
+    if (lane == 0) {
+      uint32_t s_uses = 0, p_uses = 0;
+      bool ok = mbar_wait(&sm.q_full, 0);
+      const uint32_t q_addr = smem_u32(sm.q);
+      for (int i = 0; i < tiles && ok && !sm.error; ++i) {
+        const int s = i % kRing;
+        bool is_v;
+        int kt;
+        tile_of(i, n, is_v, kt);
+        if (!mbar_wait(&sm.ring_full[s], (uint32_t)((i / kRing) & 1))) {
+          ok = false;
+          break;
+        }
+        const uint32_t t_addr = smem_u32(sm.ring[s]);
+        if (!is_v) {
+          // S = Q K^T once the softmax has read the previous S
+          if (!mbar_wait(&sm.s_read, (s_uses & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < kD / 16; ++k) {
+            const uint32_t off = (uint32_t)((k >> 2) * kBoxBytes + (k & 3) * 32);
+            mma_ss(tmem + kColS, desc_k(q_addr + off), desc_k(t_addr + off), kIdescS, k != 0);
+          }
+          mma_commit(&sm.ring_empty[s]);
+          mma_commit(&sm.s_full);
+          ++s_uses;
+        } else {
+          // O += P V once the softmax has written P
+          if (!mbar_wait(&sm.p_full, p_uses & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int j = 0; j < kTile / 16; ++j)
+            mma_ts(tmem + kColO, tmem + kColP + (uint32_t)(8 * j),
+                   desc_mn(t_addr + (uint32_t)(j * 2048)), kIdescO, (kt | j) != 0);
+          mma_commit(&sm.ring_empty[s]);
+          mma_commit(&sm.p_free);
+          ++p_uses;
+        }
+      }
+      if (!ok) sm.error = 1;
+      mma_commit(&sm.o_full);
+      mma_commit(&sm.mma_done);
+      if (!mbar_wait(&sm.mma_done, 0)) sm.error = 1;  // no MMA in flight before TMEM is freed
+    }
+  } else {
+    // ---- softmax (warps 0-3): thread = query row = TMEM lane ---------------------------------
+    const int row = warp * 32 + lane;
+    const int qi = q0 + row;  // query index within the sequence
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    uint32_t s_uses = 0, p_uses = 0;
+    bool go = true;
+    float m = -CUDART_INF_F;
+    // pass 1: the row maximum of the scaled, masked scores
+    for (int kt = 0; kt < n && go; ++kt) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full, s_uses & 1))) {
+        go = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < kTile / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(lane_base + kColS + (uint32_t)(32 * c), v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int key = kt * kTile + 32 * c + e;
+          if (key <= qi && key < len) m = fmaxf(m, __uint_as_float(v[e]) * a.scale_log2);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.s_read);
+      ++s_uses;
+    }
+    // pass 2: P = 2^(s - m) into TMEM, the row sum from the same fp32 values
+    float l = 0.f;
+    for (int kt = 0; kt < n && go; ++kt) {
+      const bool ready = mbar_wait(&sm.s_full, s_uses & 1) &&
+                         mbar_wait(&sm.p_free, (p_uses & 1) ^ 1);  // the last P V has read P
+      if (!__all_sync(0xffffffffu, ready)) {
+        go = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < kTile / 32; ++c) {
+        uint32_t v[32], pk[16];
+        tmem_ld32(lane_base + kColS + (uint32_t)(32 * c), v);
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const int key = kt * kTile + 32 * c + e;
+          const float p0 = (key <= qi && key < len)
+                               ? ex2a(__uint_as_float(v[e]) * a.scale_log2 - m) : 0.f;
+          const float p1 = (key + 1 <= qi && key + 1 < len)
+                               ? ex2a(__uint_as_float(v[e + 1]) * a.scale_log2 - m) : 0.f;
+          l += p0 + p1;
+          pk[e >> 1] = pack_half2(p0, p1);
+        }
+        tmem_st16(lane_base + kColP + (uint32_t)(16 * c), pk);
+      }
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sm.s_read);
+        mbar_arrive(&sm.p_full);
+      }
+      ++s_uses;
+      ++p_uses;
+    }
+    // epilogue: O / l (fp16) and the base-2 log-sum-exp, rows of this sequence only
+    if (go) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.o_full, 0))) {
+        go = false;
+      } else {
+        tc_fence_after();
+        const float inv = 1.f / l;
+        uint16_t *dst = a.out + ((int64_t)start + qi) * ((int64_t)a.n_heads * kD) + (int64_t)h * kD;
+#pragma unroll 1
+        for (int c = 0; c < kD / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(lane_base + kColO + (uint32_t)(32 * c), v);
+          if (qi < len) {
+            uint4 *d4 = reinterpret_cast<uint4 *>(dst + 32 * c);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              d4[q] = make_uint4(
+                  pack_half2(__uint_as_float(v[8 * q]) * inv, __uint_as_float(v[8 * q + 1]) * inv),
+                  pack_half2(__uint_as_float(v[8 * q + 2]) * inv,
+                             __uint_as_float(v[8 * q + 3]) * inv),
+                  pack_half2(__uint_as_float(v[8 * q + 4]) * inv,
+                             __uint_as_float(v[8 * q + 5]) * inv),
+                  pack_half2(__uint_as_float(v[8 * q + 6]) * inv,
+                             __uint_as_float(v[8 * q + 7]) * inv));
+          }
+        }
+        if (qi < len) a.lse[(int64_t)h * a.total + start + qi] = m + __log2f(l);
+      }
+    }
+    if (!go && lane == 0) sm.error = 1;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && sm.error) atomicAdd(&g_wait_timeouts, 1u);
+  if (warp == 5) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// ---- host ---------------------------------------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// token-major fp16 [rows, cols] -> boxes of 128 rows x 64 columns, 128-byte swizzle
+int make_map(CUtensorMap *map, const void *base, int64_t rows, int64_t cols) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr)
+    return set_error(TB_EDEVICE, "attn_varlen_fwd_tc: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)kTile};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims,
+                        strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(TB_EINVAL, "attn_varlen_fwd_tc: tensor map encode failed (%d)", (int)r);
+  return TB_OK;
+}
+
+}  // namespace
+
+TB_REGISTER_TIMEOUT_READER(attention_tc)
+
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" int tb_attn_varlen_fwd_tc(const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                                     const int32_t *cu_seqlens, uint16_t *out, float *lse,
+                                     int64_t batch, int64_t total, int64_t max_len,
+                                     int32_t n_heads, int32_t n_kv, int32_t head_dim, float scale,
+                                     void *stream) {
+  if (head_dim != kD)
+    return set_error(TB_EINVAL, "attn_varlen_fwd_tc: head_dim %d (the kernel takes %d)", head_dim,
+                     kD);
+  if (batch < 0 || total < 0 || max_len < 0 || n_heads < 1 || n_kv < 1 || n_heads % n_kv ||
+      batch > 65535 || n_heads > 65535 || (max_len + kTile - 1) / kTile > 65535 ||
+      total > (1LL << 31))
+    return set_error(TB_EINVAL, "attn_varlen_fwd_tc: batch %lld total %lld max_len %lld heads "
+                     "%d/%d", (long long)batch, (long long)total, (long long)max_len, n_heads, n_kv);
+  if (!q || !k || !v || !cu_seqlens || !out || !lse)
+    return set_error(TB_EINVAL, "attn_varlen_fwd_tc: q, k, v, cu_seqlens, out, lse required");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16))
+    return set_error(TB_EALIGN, "attn_varlen_fwd_tc: q, k, v, out must be 16-byte aligned");
+  if (batch == 0 || total == 0 || max_len == 0) return TB_OK;
+  int dev = 0, major = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (major != 10) return set_error(TB_EDEVICE, "attn_varlen_fwd_tc: needs an sm_100 GPU");
+  CUtensorMap mq, mk, mv;
+  int rc = make_map(&mq, q, total, (int64_t)n_heads * kD);
+  if (rc == TB_OK) rc = make_map(&mk, k, total, (int64_t)n_kv * kD);
+  if (rc == TB_OK) rc = make_map(&mv, v, total, (int64_t)n_kv * kD);
+  if (rc != TB_OK) return rc;
+  const size_t smem = sizeof(Smem) + 1024;
+  if (cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return check_launch("attn_varlen_fwd_tc attribute");
+  TcArgs a{cu_seqlens, out, lse, total, n_heads, n_kv, scale * 1.4426950408889634f};
+  const dim3 grid((unsigned)n_heads, (unsigned)batch, (unsigned)((max_len + kTile - 1) / kTile));
+  attn_fwd_tc_kernel<<<grid, kThreads, smem, as_stream(stream)>>>(mq, mk, mv, a);
+  return check_launch("attn_varlen_fwd_tc");
+}
