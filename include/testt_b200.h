@@ -315,8 +315,9 @@ int tb_attn_varlen_fwd(const uint16_t *q, const uint16_t *k, const uint16_t *v,
 /* tb_attn_varlen_fwd on the 5th-generation tensor cores (same arguments, outputs and
  * tolerances): a CTA per 128 queries of a head of a sequence; S = q k^T and O = P v accumulate
  * in tensor memory (tcgen05.mma, q / k / v tiles by TMA), P is written to tensor memory as the
- * A operand of P v; two passes over the key tiles (the row maximum, then P, the row sum and O),
- * so O is never rescaled. sm_100 only; q, k, v, out 16-byte aligned. Replaces the same SDPA call,
+ * A operand of P v; one pass over the key tiles with the next tile's scores computed while the
+ * current one's softmax runs, and O rescaled in tensor memory only when a row's maximum grows by
+ * more than 2^8. sm_100 only; q, k, v, out 16-byte aligned. Replaces the same SDPA call,
  * solution/model.py:242-247. */
 int tb_attn_varlen_fwd_tc(const uint16_t *q, const uint16_t *k, const uint16_t *v,
                           const int32_t *cu_seqlens, uint16_t *out, float *lse, int64_t batch,

@@ -50,6 +50,29 @@ def test_attention_forward_matches_reference(lengths, tensor_core, monkeypatch):
     assert _lib.wait_timeouts() == 0
 
 
+def test_tensor_core_forward_rescales_when_later_tiles_raise_the_maximum():
+    """Keys of the later 128-key tiles scaled up (scores 6x larger), so the row maximum grows by
+    far more than 2^8 after the first tile and the tcgen05 forward rescales O in tensor memory:
+    outputs and log-sum-exp still held to the fp64 oracle."""
+    from testt_b200 import _lib, attention
+
+    lengths = [300, 140, 390]
+    q, k, v, cu = _case(lengths, 12, 2, 21)
+    starts = [0, 300, 440]
+    for st, n in zip(starts, lengths):
+        k[st + 128:st + n] *= 6.0
+    scale = 1.0 / math.sqrt(128)
+    try:
+        attention.USE_TENSOR_CORE_FWD = True
+        out, lse = attention.attn_forward(q, k, v, cu, max(lengths), scale)
+    finally:
+        attention.USE_TENSOR_CORE_FWD = False
+    ref, rlse = _reference(q, k, v, cu, scale)
+    torch.testing.assert_close(out.double(), ref, rtol=0, atol=4e-3)
+    torch.testing.assert_close(lse.double(), rlse, rtol=0, atol=1e-3)
+    assert _lib.wait_timeouts() == 0
+
+
 def test_tensor_core_forward_agrees_with_the_mma_sync_forward_and_other_head_groups():
     """tb_attn_varlen_fwd_tc against tb_attn_varlen_fwd on the same inputs with 8 query heads
     per key/value head and 4 per head: outputs within 2 fp16 ulp-scale (2e-3), lse within 1e-4."""

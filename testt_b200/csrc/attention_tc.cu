@@ -13,11 +13,14 @@
 //                O += P V      M128 N128 K128, P read from TMEM, V MN-major in shared memory
 //   warps 0-3  softmax and epilogue: thread r owns query row r, the TMEM lane it reads and
 //              writes, so row statistics need no shuffles
-// Two passes over the key tiles: the first computes each row's maximum, the second P =
-// 2^(s - max) (fp16 into TMEM for the P V product) and the row sum from the same fp32 values.
-// O is accumulated with the final maximum, so it is never rescaled in TMEM; the second pass
-// recomputes Q K^T, which at these sizes costs less than moving O through registers.
-// TMEM columns: S 0-127, P 128-191 (fp16 pairs), O 256-383.
+// One pass over the key tiles with an online softmax in base 2. S is double-buffered in TMEM, so
+// the MMA computes the next tile's scores while the softmax warps work on the current one. The
+// row maximum m that P = 2^(s - m) is taken against moves only when a tile's maximum exceeds it
+// by more than 2^8 (then O, in TMEM, is rescaled by the softmax warps once the last P V has
+// finished); otherwise P values up to 256 are used against the older maximum, which changes
+// nothing but rounding: the row sum l is formed from the same fp32 values, and the log-sum-exp
+// is m + log2(l) for whichever m was used.
+// TMEM columns: S0 0-127, S1 128-255, P 256-319 (fp16 pairs), O 384-511.
 //
 // Every mbarrier wait is bounded (mbar_wait); a role that gives up sets the CTA's error flag and
 // leaves its loop, every role meets at the final barrier and TMEM is always released. No
@@ -37,7 +40,8 @@ constexpr int kBoxBytes = kTile * 64 * 2;     // 16 KB: 128 rows x 64 columns (o
 constexpr int kTileBytes = 2 * kBoxBytes;     // 32 KB: 128 rows x 128 columns
 constexpr int kThreads = 192;
 constexpr int kTmemCols = 512;
-constexpr uint32_t kColS = 0, kColP = 128, kColO = 256;
+constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;  // S buffer b at kColS + 128 b
+constexpr float kRescaleAt = 8.f;  // log2 of the largest P the kept maximum may produce
 
 // M = 128, N = 128, fp16 inputs, fp32 accumulation; S: A and B K-major
 constexpr uint32_t kIdescS = (1u << 4) | ((uint32_t)(kTile >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
@@ -49,7 +53,7 @@ struct Smem {
   alignas(1024) uint8_t q[kTileBytes];
   alignas(1024) uint8_t ring[kRing][kTileBytes];
   uint64_t q_full, ring_full[kRing], ring_empty[kRing];
-  uint64_t s_full, s_read, p_full, p_free, o_full, mma_done;
+  uint64_t s_full[2], s_read[2], p_full, p_free, o_full, mma_done;
   uint32_t tmem_base;
   volatile int error;
 };
@@ -158,14 +162,20 @@ __device__ __forceinline__ float ex2a(float x) {
   return y;
 }
 
-// Tile i of the producer / MMA order: pass 1 K0 .. K(n-1), pass 2 K0, V0, K1, V1, ...
+// Tile i of the producer / MMA order: K0, then for each key tile kt the next tile's K (when
+// there is one) before V(kt), so the scores of tile kt + 1 are computed before P(kt) V(kt):
+//   K0, K1, V0, K2, V1, ..., K(n-1), V(n-2), V(n-1)
 __device__ __forceinline__ void tile_of(int i, int n, bool &is_v, int &kt) {
-  if (i < n) {
+  if (i == 0) {
     is_v = false;
-    kt = i;
+    kt = 0;
+  } else if (i == 2 * n - 1) {
+    is_v = true;
+    kt = n - 1;
   } else {
-    is_v = ((i - n) & 1) != 0;
-    kt = (i - n) >> 1;
+    // i = 1, 2 -> K1, V0; i = 3, 4 -> K2, V1; ...
+    is_v = (i & 1) == 0;
+    kt = is_v ? (i >> 1) - 1 : (i + 1) >> 1;
   }
 }
 
@@ -186,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hk = h / (a.n_heads / a.n_kv);
   const int n = min(qt, (len - 1) / kTile) + 1;  // key tiles 0 .. n-1 (causal)
-  const int tiles = 3 * n;
+  const int tiles = 2 * n;
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
@@ -194,8 +204,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.ring_full[s], 1);
       mbar_init(&sm.ring_empty[s], 1);
     }
-    mbar_init(&sm.s_full, 1);
-    mbar_init(&sm.s_read, 4);  // the 4 softmax warps
+    for (int b2 = 0; b2 < 2; ++b2) {
+      mbar_init(&sm.s_full[b2], 1);
+      mbar_init(&sm.s_read[b2], 4);  // the 4 softmax warps
+    }
     mbar_init(&sm.p_full, 4);
     mbar_init(&sm.p_free, 1);
     mbar_init(&sm.o_full, 1);
@@ -246,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 5) {
     // ---- MMA issuer -------------------------------------------------------------------------
     if (lane == 0) {
-      uint32_t s_uses = 0, p_uses = 0;
+      uint32_t p_uses = 0;
       bool ok = mbar_wait(&sm.q_full, 0);
       const uint32_t q_addr = smem_u32(sm.q);
       for (int i = 0; i < tiles && ok && !sm.error; ++i) {
@@ -260,20 +272,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const uint32_t t_addr = smem_u32(sm.ring[s]);
         if (!is_v) {
-          // S = Q K^T once the softmax has read the previous S
-          if (!mbar_wait(&sm.s_read, (s_uses & 1) ^ 1)) {
+          // S(kt) = Q K^T into buffer kt & 1, once the softmax has read that buffer's last use
+          const int bf = kt & 1;
+          if (!mbar_wait(&sm.s_read[bf], (uint32_t)(((kt >> 1) & 1) ^ 1))) {
             ok = false;
             break;
           }
           tc_fence_after();
+          const uint32_t d_s = tmem + kColS + (uint32_t)(128 * bf);
 #pragma unroll
           for (int k = 0; k < kD / 16; ++k) {
             const uint32_t off = (uint32_t)((k >> 2) * kBoxBytes + (k & 3) * 32);
-            mma_ss(tmem + kColS, desc_k(q_addr + off), desc_k(t_addr + off), kIdescS, k != 0);
+            mma_ss(d_s, desc_k(q_addr + off), desc_k(t_addr + off), kIdescS, k != 0);
           }
           mma_commit(&sm.ring_empty[s]);
-          mma_commit(&sm.s_full);
-          ++s_uses;
+          mma_commit(&sm.s_full[bf]);
         } else {
           // O += P V once the softmax has written P
           if (!mbar_wait(&sm.p_full, p_uses & 1)) {
@@ -300,45 +313,62 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = warp * 32 + lane;
     const int qi = q0 + row;  // query index within the sequence
     const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-    uint32_t s_uses = 0, p_uses = 0;
+    uint32_t p_uses = 0;
     bool go = true;
-    float m = -CUDART_INF_F;
-    // pass 1: the row maximum of the scaled, masked scores
+    float m = -CUDART_INF_F, l = 0.f;
     for (int kt = 0; kt < n && go; ++kt) {
-      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full, s_uses & 1))) {
+      const int bf = kt & 1;
+      const uint32_t s_col = kColS + (uint32_t)(128 * bf);
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[bf], (uint32_t)((kt >> 1) & 1)))) {
         go = false;
         break;
       }
       tc_fence_after();
+      // this tile's maximum of the scaled, masked scores
+      float mt = -CUDART_INF_F;
 #pragma unroll 1
       for (int c = 0; c < kTile / 32; ++c) {
         uint32_t v[32];
-        tmem_ld32(lane_base + kColS + (uint32_t)(32 * c), v);
+        tmem_ld32(lane_base + s_col + (uint32_t)(32 * c), v);
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int key = kt * kTile + 32 * c + e;
-          if (key <= qi && key < len) m = fmaxf(m, __uint_as_float(v[e]) * a.scale_log2);
+          if (key <= qi && key < len) mt = fmaxf(mt, __uint_as_float(v[e]) * a.scale_log2);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.s_read);
-      ++s_uses;
-    }
-    // pass 2: P = 2^(s - m) into TMEM, the row sum from the same fp32 values
-    float l = 0.f;
-    for (int kt = 0; kt < n && go; ++kt) {
-      const bool ready = mbar_wait(&sm.s_full, s_uses & 1) &&
-                         mbar_wait(&sm.p_free, (p_uses & 1) ^ 1);  // the last P V has read P
-      if (!__all_sync(0xffffffffu, ready)) {
+      // P must not be overwritten before the last P V has read it (bounded, warp-uniform)
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.p_free, (p_uses & 1) ^ 1))) {
         go = false;
         break;
       }
       tc_fence_after();
+      // a new reference maximum only when this tile's exceeds the kept one by 2^kRescaleAt
+      // (the first tile sets it); O, from earlier tiles, is rescaled in TMEM to match
+      const bool move = kt == 0 || mt > m + kRescaleAt;
+      const float m_new = move ? fmaxf(m, mt) : m;
+      const float f = (kt == 0 || !move) ? 1.f : ex2a(m - m_new);
+      if (kt > 0 && __any_sync(0xffffffffu, move)) {
+#pragma unroll 1
+        for (int c = 0; c < kD / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(lane_base + kColO + (uint32_t)(32 * c), v);
+          uint32_t lo[16], hi[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            lo[e] = __float_as_uint(__uint_as_float(v[e]) * f);
+            hi[e] = __float_as_uint(__uint_as_float(v[16 + e]) * f);
+          }
+          tmem_st16(lane_base + kColO + (uint32_t)(32 * c), lo);
+          tmem_st16(lane_base + kColO + (uint32_t)(32 * c + 16), hi);
+        }
+      }
+      l *= f;
+      m = m_new;
+      // P = 2^(s - m) (fp16 into TMEM) and the row sum from the same fp32 values
 #pragma unroll 1
       for (int c = 0; c < kTile / 32; ++c) {
         uint32_t v[32], pk[16];
-        tmem_ld32(lane_base + kColS + (uint32_t)(32 * c), v);
+        tmem_ld32(lane_base + s_col + (uint32_t)(32 * c), v);
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           const int key = kt * kTile + 32 * c + e;
@@ -355,10 +385,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&sm.s_read);
-        mbar_arrive(&sm.p_full);
+        mbar_arrive(&sm.s_read[bf]);  // this S buffer may take tile kt + 2
+        mbar_arrive(&sm.p_full);      // P (and a rescaled O) ready for P V
       }
-      ++s_uses;
       ++p_uses;
     }
     // epilogue: O / l (fp16) and the base-2 log-sum-exp, rows of this sequence only
