@@ -325,6 +325,7 @@ struct BwdArgs {
   const float *cosv, *sinv;  // [seq, 128]
   const int64_t *pos_idx;    // [total]
   int64_t seq, slots;
+  FastDiv per_token, seq_div;  // (n_heads + n_kv) * 16 vectors a token; seq (the rotation pass)
 };
 
 __global__ void __launch_bounds__(kCtaThreads) attn_bwd_dq_kernel(const __grid_constant__ BwdArgs a) {
@@ -727,17 +728,18 @@ __global__ void __launch_bounds__(256) attn_bwd_gsum_rope_kernel(const __grid_co
   pdl_wait();
   pdl_release();
   const int group = a.n_heads / a.n_kv;
-  const int slots_per_token = a.n_heads + a.n_kv;
-  constexpr int kVecs = kD / 8;  // 16 vectors of 4 in the first half of a head
-  const int64_t nvec = a.total * slots_per_token * kVecs;
-  const int seq = (int)a.seq, slots = (int)a.slots;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t tok = i / (slots_per_token * kVecs);
-    const int rem = (int)(i - tok * (slots_per_token * kVecs));
-    const int slot = rem / kVecs, c = (rem % kVecs) * 4;
+  // 16 vectors of 4 in the first half of a head; 32-bit items (the host keeps their count below 2^31), divisions by invariant divisors
+  const uint32_t nvec = (uint32_t)a.total * a.per_token.d;
+  const int64_t slots = a.slots;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += gridDim.x * blockDim.x) {
+    uint32_t tok32, rem;
+    a.per_token.divmod(i, tok32, rem);
+    const int64_t tok = tok32;
+    const int slot = (int)(rem >> 4), c = (int)(rem & 15) * 4;
     const int64_t pos = __ldg(a.pos_idx + tok);
-    const int tp = (pos >= 0 && pos < slots) ? (int)pos % seq : -1;
+    uint32_t tq, tr;
+    a.seq_div.divmod((uint32_t)pos, tq, tr);
+    const int tp = (pos >= 0 && pos < slots) ? (int)tr : -1;
     uint16_t *row = a.dqkv + tok * a.ld_qkv;
     float g1[4], g2[4];
     float v1[4] = {0.f, 0.f, 0.f, 0.f}, v2[4] = {0.f, 0.f, 0.f, 0.f};
@@ -755,6 +757,7 @@ __global__ void __launch_bounds__(256) attn_bwd_gsum_rope_kernel(const __grid_co
       const int hk = slot - a.n_heads;
       const int64_t src = tok * (int64_t)a.n_heads * kD + (int64_t)hk * group * kD + c;
       float k1[4] = {0.f, 0.f, 0.f, 0.f}, k2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
       for (int j = 0; j < group; ++j) {
         const int64_t o = src + (int64_t)j * kD;
         const float4 xk1 = __ldg(reinterpret_cast<const float4 *>(a.dk_part + o));
@@ -902,7 +905,8 @@ extern "C" int tb_attn_varlen_bwd_rope(const uint16_t *q, const uint16_t *k, con
       !dv_part)
     return set_error(TB_EINVAL, "attn_varlen_bwd_rope: every buffer is required");
   if (seq <= 0 || slots < 0 || slots > 0x7fffffffLL || seq > 0x7fffffffLL ||
-      ld_qkv < (int64_t)(n_heads + 2 * n_kv) * kD || ld_qkv % 8 != 0)
+      ld_qkv < (int64_t)(n_heads + 2 * n_kv) * kD || ld_qkv % 8 != 0 ||
+      total * (n_heads + n_kv) * (kD / 8) >= (1LL << 31))
     return set_error(TB_EINVAL, "attn_varlen_bwd_rope: seq %lld slots %lld ld_qkv %lld",
                      (long long)seq, (long long)slots, (long long)ld_qkv);
   if (!aligned(out, 16) || !aligned(dout, 16) || !aligned(dqkv, 16) || !aligned(dk_part, 16) ||
@@ -927,6 +931,8 @@ extern "C" int tb_attn_varlen_bwd_rope(const uint16_t *q, const uint16_t *k, con
   const int64_t nvec = total * (n_heads + n_kv) * (kD / 8);
   int64_t blocks = (nvec + 255) / 256;
   if (blocks > (int64_t)sm_count() * 8) blocks = (int64_t)sm_count() * 8;
+  a.per_token = FastDiv((uint32_t)((n_heads + n_kv) * (kD / 8)));
+  a.seq_div = FastDiv((uint32_t)seq);
   return launch("attn_varlen_bwd_rope rotate", attn_bwd_gsum_rope_kernel, (unsigned)blocks, 256,
                 0, st, a);
 }
