@@ -324,18 +324,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      // this tile's maximum of the scaled, masked scores
+      // a tile below the diagonal and inside the sequence has no masked key for any row of
+      // this CTA (warp-uniform): its scores need no per-key test
+      const bool full = kt < qt && (kt + 1) * kTile <= len;
+      // this tile's maximum of the scaled, masked scores (scaling by a positive factor is
+      // monotonic, so a full tile takes the maximum of the raw scores and scales it once)
       float mt = -CUDART_INF_F;
 #pragma unroll 1
       for (int c = 0; c < kTile / 32; ++c) {
         uint32_t v[32];
         tmem_ld32(lane_base + s_col + (uint32_t)(32 * c), v);
+        if (full) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int key = kt * kTile + 32 * c + e;
-          if (key <= qi && key < len) mt = fmaxf(mt, __uint_as_float(v[e]) * a.scale_log2);
+          for (int e = 0; e < 32; ++e) mt = fmaxf(mt, __uint_as_float(v[e]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int key = kt * kTile + 32 * c + e;
+            if (key <= qi && key < len) mt = fmaxf(mt, __uint_as_float(v[e]) * a.scale_log2);
+          }
         }
       }
+      if (full) mt *= a.scale_log2;
       // P must not be overwritten before the last P V has read it (bounded, warp-uniform)
       if (!__all_sync(0xffffffffu, mbar_wait(&sm.p_free, (p_uses & 1) ^ 1))) {
         go = false;
@@ -369,15 +379,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < kTile / 32; ++c) {
         uint32_t v[32], pk[16];
         tmem_ld32(lane_base + s_col + (uint32_t)(32 * c), v);
+        if (full) {
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const int key = kt * kTile + 32 * c + e;
-          const float p0 = (key <= qi && key < len)
-                               ? ex2a(__uint_as_float(v[e]) * a.scale_log2 - m) : 0.f;
-          const float p1 = (key + 1 <= qi && key + 1 < len)
-                               ? ex2a(__uint_as_float(v[e + 1]) * a.scale_log2 - m) : 0.f;
-          l += p0 + p1;
-          pk[e >> 1] = pack_half2(p0, p1);
+          for (int e = 0; e < 32; e += 2) {
+            const float p0 = ex2a(__uint_as_float(v[e]) * a.scale_log2 - m);
+            const float p1 = ex2a(__uint_as_float(v[e + 1]) * a.scale_log2 - m);
+            l += p0 + p1;
+            pk[e >> 1] = pack_half2(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const int key = kt * kTile + 32 * c + e;
+            const float p0 = (key <= qi && key < len)
+                                 ? ex2a(__uint_as_float(v[e]) * a.scale_log2 - m) : 0.f;
+            const float p1 = (key + 1 <= qi && key + 1 < len)
+                                 ? ex2a(__uint_as_float(v[e + 1]) * a.scale_log2 - m) : 0.f;
+            l += p0 + p1;
+            pk[e >> 1] = pack_half2(p0, p1);
+          }
         }
         tmem_st16(lane_base + kColP + (uint32_t)(16 * c), pk);
       }
