@@ -910,7 +910,7 @@ def _kernel_case(name, device):
             P, I64, I32, F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float
             entry.restype = ctypes.c_int
             entry.argtypes = [P] * 7 + [I64, F] + [P] * 7 + [I64, F, I64, I64, I32, I32, I64,
-                                                               I64, P]
+                                                               I64, P, P]
 
             def parts(ad):
                 return [_lib.ptr(ad[k]) for k in ("g", "h", "b16", "x16", "dh", "db", "da")] \
@@ -918,7 +918,7 @@ def _kernel_case(name, device):
 
             fn = lambda: entry(*parts(ads[0]), *parts(ads[1]), tokens, hidden, r,  # noqa: E731
                                0b1111, ads[0]["g"].stride(0), ads[1]["g"].stride(0),
-                               _lib.stream_of(ads[0]["dh"]))
+                               _lib.stream_of(ads[0]["dh"]), None)
         else:  # the current backward's six GEMMs (lora.LoraPair.backward, bucket accumulation)
             def fn():
                 for ad in ads:

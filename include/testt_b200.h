@@ -287,14 +287,18 @@ int tb_lora_dropout_grad_expand(const uint16_t *dh_q, const uint16_t *a16_q, con
  *   db = scale * g^T . h          [width, 16] fp32 (added into db when its accumulate bit is set)
  *   da = dh^T . x16               [16, hidden] fp32 (added into da when its accumulate bit is set)
  * accumulate: bit 0 db_q, bit 1 da_q, bit 2 db_v, bit 3 da_v. rank must be 16; width and hidden
- * multiples of 64; g, h, b16, x16, dh 16-byte aligned. Sums in a fixed order (deterministic). */
+ * multiples of 64; g, h, b16, x16, dh 16-byte aligned. Sums in a fixed order (deterministic).
+ * Two launches: dh and db on `stream`, then da. With stream_da non-NULL (and not `stream`), da
+ * runs on stream_da after an event recorded on `stream` behind the first launch, beside what the
+ * caller queues next on `stream`; the caller makes `stream` wait for stream_da before reading
+ * da. */
 int tb_lora_backward(const uint16_t *g_q, const uint16_t *h_q, const uint16_t *b16_q,
                      const uint16_t *x16_q, uint16_t *dh_q, float *db_q, float *da_q,
                      int64_t width_q, float scale_q, const uint16_t *g_v, const uint16_t *h_v,
                      const uint16_t *b16_v, const uint16_t *x16_v, uint16_t *dh_v, float *db_v,
                      float *da_v, int64_t width_v, float scale_v, int64_t rows, int64_t hidden,
                      int32_t rank, int32_t accumulate, int64_t ld_g_q, int64_t ld_g_v,
-                     void *stream);
+                     void *stream, void *stream_da);
 
 /* ---------------------------------------------------------------------------------------------
  * Causal attention over packed variable-length sequences with grouped key/value heads. Replaces

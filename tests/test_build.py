@@ -89,10 +89,10 @@ def test_gemm_entry_points_reject_bad_arguments_before_any_cuda_call(lib):
     # tb_lora_backward: rank 8, then widths / hidden that are not multiples of 64
     lb = lib.tb_lora_backward
     bufs = [p(256)] * 7
-    assert lb(*bufs, 128, 2.0, *([None] * 7), 0, 1.0, 10, 128, 8, 0, 128, 128, None) == TB_EINVAL
+    assert lb(*bufs, 128, 2.0, *([None] * 7), 0, 1.0, 10, 128, 8, 0, 128, 128, None, None) == TB_EINVAL
     assert b"rank 8" in lib.tb_last_error()
-    assert lb(*bufs, 100, 2.0, *([None] * 7), 0, 1.0, 10, 128, 16, 0, 128, 128, None) == TB_EINVAL
-    assert lb(*bufs, 128, 2.0, *([None] * 7), 0, 1.0, 10, 100, 16, 0, 128, 128, None) == TB_EINVAL
+    assert lb(*bufs, 100, 2.0, *([None] * 7), 0, 1.0, 10, 128, 16, 0, 128, 128, None, None) == TB_EINVAL
+    assert lb(*bufs, 128, 2.0, *([None] * 7), 0, 1.0, 10, 100, 16, 0, 128, 128, None, None) == TB_EINVAL
 
 
 def _c_signatures(path):

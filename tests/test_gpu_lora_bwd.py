@@ -55,7 +55,7 @@ def _run(q, v, rows, hidden, accumulate):
 
     ld = [0 if ad is None else ad["g"].stride(0) for ad in (q, v)]
     rc = _entry()(*parts(q), *parts(v), rows, hidden, 16, accumulate, ld[0], ld[1],
-                  _lib.stream_of(torch.empty(0, device="cuda")))
+                  _lib.stream_of(torch.empty(0, device="cuda")), None)
     assert rc == 0, _lib.load().tb_last_error()
     torch.cuda.synchronize()
 
@@ -112,13 +112,16 @@ def test_one_adapter_and_determinism(present):
     assert_rel(ad["da"].cpu(), da(ad["dh"]).cpu(), 1e-4, "dA")
 
 
+@pytest.mark.parametrize("side_stream", [False, True], ids=["one_stream", "da_on_side_stream"])
 @pytest.mark.parametrize("in_bucket", [False, True])
-def test_lora_pair_with_fused_backward_matches_gemm_backward(monkeypatch, in_bucket):
+def test_lora_pair_with_fused_backward_matches_gemm_backward(monkeypatch, in_bucket,
+                                                             side_stream):
     """lora_fused.LoraPairFused (tb_lora_backward, then the dropout backward), which
     lora.lora_pair takes when the kernel is loaded, against lora.LoraPair (six GEMMs, then the
     same dropout backward, lora.USE_FUSED_BACKWARD off) through lora.lora_pair, with the
     same dropout draws: the padded input's gradient and both adapters' weight gradients,
-    returned to autograd or accumulated into GradBucket views."""
+    returned to autograd or accumulated into GradBucket views; the dA launch on the current
+    stream or on the side stream beside the dropout backward (lora_fused.SIDE_STREAM_DA)."""
     from testt_b200 import lora, lora_fused
     from testt_b200.dist import GradBucket
     from testt_b200.rope import slot_index
@@ -145,6 +148,7 @@ def test_lora_pair_with_fused_backward_matches_gemm_backward(monkeypatch, in_buc
         if in_bucket:
             GradBucket(params)
         monkeypatch.setattr(lora, "USE_FUSED_BACKWARD", fused)
+        monkeypatch.setattr(lora_fused, "SIDE_STREAM_DA", side_stream)
         assert lora._node() is (lora_fused.LoraPairFused if fused else lora.LoraPair)
         torch.manual_seed(11)
         x = x0.clone().requires_grad_(True)

@@ -67,7 +67,7 @@ SIGNATURES = {
                              _I32, _P, _P, _P, _P, _I64, _P],
     "tb_nf4_gemm_qkv_rope_workspace": [_I64, _I32, _I32, _I64],
     "tb_lora_backward": [_P, _P, _P, _P, _P, _P, _P, _I64, _F, _P, _P, _P, _P, _P, _P, _P, _I64,
-                         _F, _I64, _I64, _I32, _I32, _I64, _I64, _P],
+                         _F, _I64, _I64, _I32, _I32, _I64, _I64, _P, _P],
     "tb_head_dh": [_P, _I64, _P, _P, _I64, _I64, _I64, _F, _P, _I64, _P, _I64, _P, _I32, _P,
                    _I64, _I32, _P],
     "tb_head_dh_workspace": [_I64, _I64, _I64],

@@ -274,6 +274,18 @@ __global__ void __launch_bounds__(kThreads) lora_bwd_da(const __grid_constant__ 
           smem);
 }
 
+// One event per device for the fork of kernel 2 onto a second stream (created on first use,
+// kept until exit; recording it again, also inside a stream capture, starts a new fork).
+cudaEvent_t fork_event() {
+  static cudaEvent_t events[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (events[dev] == nullptr &&
+      cudaEventCreateWithFlags(&events[dev], cudaEventDisableTiming) != cudaSuccess)
+    return nullptr;
+  return events[dev];
+}
+
 }  // namespace
 }  // namespace tb
 
@@ -289,7 +301,7 @@ extern "C" int tb_lora_backward(const uint16_t *g_q, const uint16_t *h_q, const 
                                 uint16_t *dh_v, float *db_v, float *da_v, int64_t width_v,
                                 float scale_v, int64_t rows, int64_t hidden, int32_t rank,
                                 int32_t accumulate, int64_t ld_g_q, int64_t ld_g_v,
-                                void *stream) {
+                                void *stream, void *stream_da) {
   if (rank != kRank) return set_error(TB_EINVAL, "lora_backward: rank %d (the kernels take 16)", rank);
   if (rows < 0 || rows > (1LL << 24) || hidden <= 0 || hidden % kCols != 0 || hidden > (1LL << 20))
     return set_error(TB_EINVAL, "lora_backward: rows %lld hidden %lld (a multiple of %d)",
@@ -346,6 +358,17 @@ extern "C" int tb_lora_backward(const uint16_t *g_q, const uint16_t *h_q, const 
     rc = launch("lora_bwd_dh_db", lora_bwd_dh_db, dim3((unsigned)grid1), dim3(kThreads),
                 (size_t)kSmemBytes, as_stream(stream), a);
   if (rc != TB_OK) return rc;  // with no rows, kernel 2 still writes (or keeps) zero dA
+  // kernel 2 on the caller's second stream, after kernel 1 (an event of this library's), so it
+  // runs beside whatever the caller queues next on `stream`; the caller joins the two streams
+  cudaStream_t st2 = as_stream(stream);
+  if (stream_da != nullptr && stream_da != stream) {
+    cudaEvent_t ev = fork_event();
+    if (ev == nullptr) return set_error(TB_ELAUNCH, "lora_backward: no fork event");
+    if (cudaEventRecord(ev, as_stream(stream)) != cudaSuccess ||
+        cudaStreamWaitEvent(as_stream(stream_da), ev, 0) != cudaSuccess)
+      return check_launch("lora_backward fork");
+    st2 = as_stream(stream_da);
+  }
   return launch("lora_bwd_da", lora_bwd_da, dim3((unsigned)grid2), dim3(kThreads),
-                (size_t)kSmemBytes, as_stream(stream), a);
+                (size_t)kSmemBytes, st2, a);
 }

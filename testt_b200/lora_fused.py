@@ -19,6 +19,22 @@ from .lora import _F16, _RANK, LoraPair, _in_bucket, grads_written
 
 
 @functools.lru_cache(maxsize=None)
+# True: the dA launch of tb_lora_backward runs on a side stream while the dropout backward
+# (tb_lora_dropout_grad_expand) runs on the current one; both need only dh, so the two short
+# launches overlap. The streams are joined before the node returns (captured as two branches
+# of the step's graph).
+SIDE_STREAM_DA = True
+_SIDE = {}
+
+
+def _side_stream(device):
+    """One side stream per device, made once."""
+    s = _SIDE.get(device)
+    if s is None:
+        s = _SIDE[device] = torch.cuda.Stream(device=device)
+    return s
+
+
 def _entry():
     """tb_lora_backward of the loaded library, or None (looked up once; a library built from
     other sources, TESTT_B200_LIB, may lack it)."""
@@ -90,9 +106,10 @@ class LoraPairFused(LoraPair):
                 grads += [da, db]
                 dhs.append(dh)
                 a16s.append(a16.contiguous())
+            main = torch.cuda.current_stream(pos_idx.device)
+            side = _side_stream(pos_idx.device) if SIDE_STREAM_DA else None
             rc = fn(*args, rows, ctx.hidden, _RANK, accumulate, strides[0], strides[1],
-                    _lib.stream_of(pos_idx))
-            del keep
+                    _lib.stream_of(pos_idx), side.cuda_stream if side is not None else None)
             if rc != 0:
                 msg = _lib.load().tb_last_error().decode(errors="replace")
                 raise _lib.KernelError(f"tb_lora_backward failed ({rc}): {msg}")
@@ -106,5 +123,10 @@ class LoraPairFused(LoraPair):
                           _lib.ptr(dhs[1]), _lib.ptr(a16s[1]), _lib.ptr(mq), _lib.ptr(mv),
                           _lib.ptr(slot_tok), _lib.ptr(gx), ctx.slots, ctx.hidden, _RANK,
                           scale_q, scale_v, _lib.stream_of(gx))
+            # dA ran on the side stream beside the dropout backward: join before anything on
+            # this stream reads it, and only then let its inputs go back to the allocator
+            if side is not None:
+                main.wait_stream(side)
+            del keep
         grads_written([p for p, g in zip(ctx.params, grads) if g is None])
         return (gx, grads[0], grads[1], grads[2], grads[3], None, None, None)
