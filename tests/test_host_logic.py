@@ -214,3 +214,17 @@ def test_bench_workloads_are_the_oracle_workloads():
     same(b.config2(rows=64), synth.config2(rows=64))
     same(b.config3(), synth.config3())
     same(b.config4(rows=32, vocab=1000), synth.config4(rows=32, vocab=1000))
+
+
+def test_every_module_of_the_package_parses():
+    """Every Python file of the package, bench.py and the graft entry compile (a module that
+    only the GPU tests import would otherwise fail there first)."""
+    import glob
+    import os
+    import py_compile
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    files = glob.glob(os.path.join(root, "testt_b200", "*.py")) + [
+        os.path.join(root, "bench.py"), os.path.join(root, "__graft_entry__.py")]
+    for f in files:
+        py_compile.compile(f, doraise=True, cfile=os.devnull)

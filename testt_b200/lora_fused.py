@@ -18,7 +18,6 @@ from . import _lib
 from .lora import _F16, _RANK, LoraPair, _in_bucket, grads_written
 
 
-@functools.lru_cache(maxsize=None)
 # True: the dA launch of tb_lora_backward runs on a side stream while the dropout backward
 # (tb_lora_dropout_grad_expand) runs on the current one; both need only dh, so the two short
 # launches overlap. The streams are joined before the node returns (captured as two branches
@@ -35,6 +34,7 @@ def _side_stream(device):
     return s
 
 
+@functools.lru_cache(maxsize=None)
 def _entry():
     """tb_lora_backward of the loaded library, or None (looked up once; a library built from
     other sources, TESTT_B200_LIB, may lack it)."""
