@@ -221,10 +221,10 @@ def test_every_module_of_the_package_parses():
     only the GPU tests import would otherwise fail there first)."""
     import glob
     import os
-    import py_compile
 
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     files = glob.glob(os.path.join(root, "testt_b200", "*.py")) + [
         os.path.join(root, "bench.py"), os.path.join(root, "__graft_entry__.py")]
     for f in files:
-        py_compile.compile(f, doraise=True, cfile=os.devnull)
+        with open(f) as fh:
+            compile(fh.read(), f, "exec")
