@@ -21,8 +21,10 @@ from .lora import _F16, _RANK, LoraPair, _in_bucket, grads_written
 # True: the dA launch of tb_lora_backward runs on a side stream while the dropout backward
 # (tb_lora_dropout_grad_expand) runs on the current one; both need only dh, so the two short
 # launches overlap. The streams are joined before the node returns (captured as two branches
-# of the step's graph).
-SIDE_STREAM_DA = True
+# of the step's graph). Off: on one B200 the captured step measured 8.58 ms with it against
+# 8.56 ms without (same box, two runs each): the fork and join cost more than the overlap
+# saves, and they break the programmatic-launch chaining of the kernels around them.
+SIDE_STREAM_DA = False
 _SIDE = {}
 
 
