@@ -6,13 +6,15 @@
 //
 // A CTA takes 128 queries of one head of one sequence; the key tiles (128 keys) up to its own
 // (causal). Warps:
-//   warp 4     TMA producer: the Q tile once, then K and V tiles through a 4-slot ring in the
+//   warp 8     TMA producer: the Q tile once, then K and V tiles through a 4-slot ring in the
 //              order the MMA uses them
-//   warp 5     TMEM allocation and the MMA issuer:
+//   warp 9     TMEM allocation and the MMA issuer:
 //                S = Q K^T     M128 N128 K128, both operands K-major in shared memory
 //                O += P V      M128 N128 K128, P read from TMEM, V MN-major in shared memory
-//   warps 0-3  softmax and epilogue: thread r owns query row r, the TMEM lane it reads and
-//              writes, so row statistics need no shuffles
+//   warps 0-7  softmax and epilogue: warps w and w + 4 share TMEM lane quarter w % 4, so a
+//              row's two threads each see the whole row (no shuffles); both take the row
+//              maximum over all 128 keys of a tile, each forms P for its 64 keys and rescales and
+//              writes its 64 columns of O; their row sums are added once, at the end
 // One pass over the key tiles with an online softmax in base 2. S is double-buffered in TMEM, so
 // the MMA computes the next tile's scores while the softmax warps work on the current one. The
 // row maximum m that P = 2^(s - m) is taken against moves only when a tile's maximum exceeds it
@@ -38,7 +40,7 @@ constexpr int kTile = 128;                    // queries per CTA, keys per tile
 constexpr int kRing = 4;                      // K / V tiles in flight
 constexpr int kBoxBytes = kTile * 64 * 2;     // 16 KB: 128 rows x 64 columns (one TMA box)
 constexpr int kTileBytes = 2 * kBoxBytes;     // 32 KB: 128 rows x 128 columns
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr int kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;  // S buffer b at kColS + 128 b
 constexpr float kRescaleAt = 8.f;  // log2 of the largest P the kept maximum may produce
@@ -54,6 +56,7 @@ struct Smem {
   alignas(1024) uint8_t ring[kRing][kTileBytes];
   uint64_t q_full, ring_full[kRing], ring_empty[kRing];
   uint64_t s_full[2], s_read[2], p_full, p_free, o_full, mma_done;
+  float l_pair[2][128];  // the two half-row sums of P (epilogue)
   uint32_t tmem_base;
   volatile int error;
 };
@@ -206,16 +209,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b2 = 0; b2 < 2; ++b2) {
       mbar_init(&sm.s_full[b2], 1);
-      mbar_init(&sm.s_read[b2], 4);  // the 4 softmax warps
+      mbar_init(&sm.s_read[b2], 8);  // the 8 softmax warps
     }
-    mbar_init(&sm.p_full, 4);
+    mbar_init(&sm.p_full, 8);
     mbar_init(&sm.p_free, 1);
     mbar_init(&sm.o_full, 1);
     mbar_init(&sm.mma_done, 1);
     sm.error = 0;
     mbar_init_fence();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&sm.tmem_base)),
                  "r"(kTmemCols)
@@ -227,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---- TMA producer -----------------------------------------------------------------------
     if (lane == 0) {
       mbar_expect_tx(&sm.q_full, kTileBytes);
@@ -255,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = issued - (issued < kRing ? issued : kRing); i < issued; ++i)
         mbar_wait(&sm.ring_full[i % kRing], (uint32_t)((i / kRing) & 1));
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---- MMA issuer -------------------------------------------------------------------------
     if (lane == 0) {
       uint32_t p_uses = 0;
@@ -309,26 +312,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&sm.mma_done, 0)) sm.error = 1;  // no MMA in flight before TMEM is freed
     }
   } else {
-    // ---- softmax (warps 0-3): thread = query row = TMEM lane ---------------------------------
-    const int row = warp * 32 + lane;
+    // ---- softmax (warps 0-7): thread = query row = TMEM lane, two threads a row -------------
+    const int quarter = warp & 3, hcol = warp >> 2;  // lane quarter; key / column half
+    const int row = quarter * 32 + lane;
     const int qi = q0 + row;  // query index within the sequence
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
     uint32_t p_uses = 0;
-    bool go = true;
+    bool go = true;  // false after a wait gave up: the loop still runs to the end (bounded)
     float m = -CUDART_INF_F, l = 0.f;
-    for (int kt = 0; kt < n && go; ++kt) {
+    for (int kt = 0; kt < n; ++kt) {
       const int bf = kt & 1;
       const uint32_t s_col = kColS + (uint32_t)(128 * bf);
-      if (!__all_sync(0xffffffffu, mbar_wait(&sm.s_full[bf], (uint32_t)((kt >> 1) & 1)))) {
-        go = false;
-        break;
-      }
+      go = __all_sync(0xffffffffu, go && mbar_wait(&sm.s_full[bf], (uint32_t)((kt >> 1) & 1)));
       tc_fence_after();
-      // a tile below the diagonal and inside the sequence has no masked key for any row of
-      // this CTA (warp-uniform): its scores need no per-key test
+      // no masked key for any row of this CTA in a tile below the diagonal and inside the
+      // sequence (warp-uniform): the tile maximum is that of the raw scores, scaled once
       const bool full = kt < qt && (kt + 1) * kTile <= len;
-      // this tile's maximum of the scaled, masked scores (scaling by a positive factor is
-      // monotonic, so a full tile takes the maximum of the raw scores and scales it once)
       float mt = -CUDART_INF_F;
 #pragma unroll 1
       for (int c = 0; c < kTile / 32; ++c) {
@@ -346,39 +345,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (full) mt *= a.scale_log2;
-      // P must not be overwritten before the last P V has read it (bounded, warp-uniform)
-      if (!__all_sync(0xffffffffu, mbar_wait(&sm.p_free, (p_uses & 1) ^ 1))) {
-        go = false;
-        break;
-      }
+      // P must not be overwritten before the last P V has read it
+      go = __all_sync(0xffffffffu, go && mbar_wait(&sm.p_free, (p_uses & 1) ^ 1));
       tc_fence_after();
       // a new reference maximum only when this tile's exceeds the kept one by 2^kRescaleAt
-      // (the first tile sets it); O, from earlier tiles, is rescaled in TMEM to match
+      // (the first tile sets it); this thread's half of O is rescaled in TMEM to match
       const bool move = kt == 0 || mt > m + kRescaleAt;
       const float m_new = move ? fmaxf(m, mt) : m;
       const float f = (kt == 0 || !move) ? 1.f : ex2a(m - m_new);
       if (kt > 0 && __any_sync(0xffffffffu, move)) {
 #pragma unroll 1
-        for (int c = 0; c < kD / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
+          const uint32_t o_col = kColO + (uint32_t)(64 * hcol + 32 * c);
           uint32_t v[32];
-          tmem_ld32(lane_base + kColO + (uint32_t)(32 * c), v);
+          tmem_ld32(lane_base + o_col, v);
           uint32_t lo[16], hi[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             lo[e] = __float_as_uint(__uint_as_float(v[e]) * f);
             hi[e] = __float_as_uint(__uint_as_float(v[16 + e]) * f);
           }
-          tmem_st16(lane_base + kColO + (uint32_t)(32 * c), lo);
-          tmem_st16(lane_base + kColO + (uint32_t)(32 * c + 16), hi);
+          tmem_st16(lane_base + o_col, lo);
+          tmem_st16(lane_base + o_col + 16, hi);
         }
       }
       l *= f;
       m = m_new;
-      // P = 2^(s - m) (fp16 into TMEM) and the row sum from the same fp32 values
+      // P = 2^(s - m) for this thread's 64 keys (fp16 into TMEM), the half-row sum from the
+      // same fp32 values
 #pragma unroll 1
-      for (int c = 0; c < kTile / 32; ++c) {
+      for (int c = 0; c < 2; ++c) {
+        const int kc = 64 * hcol + 32 * c;  // first key of the chunk within the tile
         uint32_t v[32], pk[16];
-        tmem_ld32(lane_base + s_col + (uint32_t)(32 * c), v);
+        tmem_ld32(lane_base + s_col + (uint32_t)kc, v);
         if (full) {
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
@@ -390,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
-            const int key = kt * kTile + 32 * c + e;
+            const int key = kt * kTile + kc + e;
             const float p0 = (key <= qi && key < len)
                                  ? ex2a(__uint_as_float(v[e]) * a.scale_log2 - m) : 0.f;
             const float p1 = (key + 1 <= qi && key + 1 < len)
@@ -399,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             pk[e >> 1] = pack_half2(p0, p1);
           }
         }
-        tmem_st16(lane_base + kColP + (uint32_t)(16 * c), pk);
+        tmem_st16(lane_base + kColP + (uint32_t)(kc >> 1), pk);
       }
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
@@ -410,42 +409,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ++p_uses;
     }
-    // epilogue: O / l (fp16) and the base-2 log-sum-exp, rows of this sequence only
-    if (go) {
-      if (!__all_sync(0xffffffffu, mbar_wait(&sm.o_full, 0))) {
-        go = false;
-      } else {
-        tc_fence_after();
-        const float inv = 1.f / l;
-        uint16_t *dst = a.out + ((int64_t)start + qi) * ((int64_t)a.n_heads * kD) + (int64_t)h * kD;
+    // epilogue: the two half-row sums added (first half + second half, in that order), O / l
+    // (fp16) and the base-2 log-sum-exp, rows of this sequence only
+    go = __all_sync(0xffffffffu, go && mbar_wait(&sm.o_full, 0));
+    sm.l_pair[hcol][row] = l;
+    asm volatile("bar.sync 1, 256;" ::: "memory");  // the 8 softmax warps, all of them here
+    tc_fence_after();
+    const float total = sm.l_pair[0][row] + sm.l_pair[1][row];
+    const float inv = 1.f / total;
+    uint16_t *dst =
+        a.out + ((int64_t)start + qi) * ((int64_t)a.n_heads * kD) + (int64_t)h * kD + 64 * hcol;
 #pragma unroll 1
-        for (int c = 0; c < kD / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld32(lane_base + kColO + (uint32_t)(32 * c), v);
-          if (qi < len) {
-            uint4 *d4 = reinterpret_cast<uint4 *>(dst + 32 * c);
+    for (int c = 0; c < 2; ++c) {
+      uint32_t v[32];
+      tmem_ld32(lane_base + kColO + (uint32_t)(64 * hcol + 32 * c), v);
+      if (go && qi < len) {
+        uint4 *d4 = reinterpret_cast<uint4 *>(dst + 32 * c);
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              d4[q] = make_uint4(
-                  pack_half2(__uint_as_float(v[8 * q]) * inv, __uint_as_float(v[8 * q + 1]) * inv),
-                  pack_half2(__uint_as_float(v[8 * q + 2]) * inv,
-                             __uint_as_float(v[8 * q + 3]) * inv),
-                  pack_half2(__uint_as_float(v[8 * q + 4]) * inv,
-                             __uint_as_float(v[8 * q + 5]) * inv),
-                  pack_half2(__uint_as_float(v[8 * q + 6]) * inv,
-                             __uint_as_float(v[8 * q + 7]) * inv));
-          }
-        }
-        if (qi < len) a.lse[(int64_t)h * a.total + start + qi] = m + __log2f(l);
+        for (int q = 0; q < 4; ++q)
+          d4[q] = make_uint4(
+              pack_half2(__uint_as_float(v[8 * q]) * inv, __uint_as_float(v[8 * q + 1]) * inv),
+              pack_half2(__uint_as_float(v[8 * q + 2]) * inv, __uint_as_float(v[8 * q + 3]) * inv),
+              pack_half2(__uint_as_float(v[8 * q + 4]) * inv, __uint_as_float(v[8 * q + 5]) * inv),
+              pack_half2(__uint_as_float(v[8 * q + 6]) * inv, __uint_as_float(v[8 * q + 7]) * inv));
       }
     }
+    if (go && qi < len && hcol == 0) a.lse[(int64_t)h * a.total + start + qi] = m + __log2f(total);
     if (!go && lane == 0) sm.error = 1;
   }
 
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0 && sm.error) atomicAdd(&g_wait_timeouts, 1u);
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kTmemCols)
