@@ -1133,11 +1133,12 @@ def ours_arm(args, rank, world, local):
     if not torch.isfinite(results[:args.steps]).all():
         raise RuntimeError("e2e: a step's loss or statistics read back non-finite")
 
-    # kernels launched per step: counted on one eager step (a replay launches the same kernels)
-    _lib.reset_call_count()
+    # this library's kernel launches per step, counted by the library itself on one eager step
+    # (a replay of the captured step launches the same kernels); the timed region ran K steps
+    before = _lib.launch_count()
     step(ids, mask, labels)
     torch.cuda.synchronize()
-    calls = _lib.call_count()
+    launches_per_step = _lib.launch_count() - before
 
     # hot path: the fused memory-bound kernels of one step as CUDA graphs
     hp = HotPath(model, lengths, seq, dev)
@@ -1204,7 +1205,8 @@ def ours_arm(args, rank, world, local):
         "eager": {"tokens_per_s": tokens * world * args.steps / (eager_ms / 1e3),
                   "ms_per_step": eager_ms / args.steps,
                   "note": "the same step launched op by op from Python (no CUDA graph)"},
-        "gpu_launches": calls,
+        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches_per_step": launches_per_step,
         "clocks": clocks,
         "hot_path": {"gbps": hp_bytes / hp_ms / 1e6, "frac": hp_bytes / hp_ms / 1e6 / pk["hbm_gbs"],
                      "ms_per_step": hp_ms, "bytes_per_step": hp_bytes,

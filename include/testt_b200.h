@@ -45,6 +45,10 @@ int tb_wait_timeouts(int32_t device, uint32_t *count);
  * reference (its Triton kernels wait on no barriers). */
 int tb_wait_selftest(int32_t polls, int32_t arrive, int32_t *status, void *stream);
 
+/* Kernel launches this library has queued since it was loaded, all threads and devices (a
+ * launch captured into a CUDA graph counts once, when captured). No reference counterpart. */
+int64_t tb_launch_count(void);
+
 /* ---------------------------------------------------------------------------------------------
  * NF4 unpack (bitsandbytes 4-bit layout). Replaces nf4_unpack_kernel and its launch in
  * unpack_into, solution/nf4.py:27-45 and :72-89.

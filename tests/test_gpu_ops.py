@@ -574,3 +574,29 @@ def test_split_head_kernels_config4_rows(groups):
     assert_rel(ent, rent, 1e-4, "entropy", floor=0.0)
     assert torch.equal(cor.cpu().bool(), rcor)
     assert_ulp(dl, rdl, 1, "dlogits")
+
+
+def test_launch_count_follows_the_kernels_queued():
+    """tb_launch_count: one more per kernel launch, through the launch helper and through the
+    library's own <<<>>> launches (the tensor-core head GEMM)."""
+    from testt_b200 import _lib, mlp
+
+    gu = torch.randn(64, 2 * 256, device="cuda").half()
+    before = _lib.launch_count()
+    mlp.gated_silu(gu)
+    torch.cuda.synchronize()
+    assert _lib.launch_count() - before == 1
+    from oracle import synth
+    from testt_b200 import head
+
+    c = synth.config4(torch.device("cuda"), rows=256)
+    if head._tensor_core_ok(c["hidden"], c["weight"]):
+        vt = -(-synth.VOCAB // 256)
+        part = torch.empty((256, vt, 6), device="cuda")
+        pidx = torch.empty((256, vt), dtype=torch.int64, device="cuda")
+        before = _lib.launch_count()
+        _lib.call("tb_head_logits_stats", _lib.ptr(c["hidden"]), _lib.ptr(c["weight"]),
+                  _lib.ptr(c["targets"]), None, 0, _lib.ptr(part), _lib.ptr(pidx), 256,
+                  synth.VOCAB, synth.HIDDEN, _lib.stream_of(part))
+        torch.cuda.synchronize()
+        assert _lib.launch_count() - before == 1

@@ -54,6 +54,7 @@ SIGNATURES = {
     "tb_head_fold": [_P, _P, _I64, _I32, _I64, _I32, _P, _P, _P],
     "tb_head_dlogits": [_P, _P, _P, _I64, _I64, _I64, _I64, _F, _P],
     "tb_wait_timeouts": [_I32, _P],
+    "tb_launch_count": [],
     "tb_wait_selftest": [_I32, _I32, _P, _P],
     "tb_head_stats_grad_noalloc": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P],
     "tb_head_logits_stats": [_P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _P],
@@ -76,7 +77,7 @@ SIGNATURES = {
 # return types other than int (0 or a negative TB_E* code)
 RESTYPES = {"tb_nf4_gemm_workspace": ctypes.c_int64,
             "tb_nf4_gemm_qkv_rope_workspace": ctypes.c_int64,
-            "tb_head_dh_workspace": ctypes.c_int64}
+            "tb_head_dh_workspace": ctypes.c_int64, "tb_launch_count": ctypes.c_int64}
 
 _lib = None
 _calls = 0
@@ -116,6 +117,11 @@ def call(name, *args):
     if rc != 0:
         msg = load().tb_last_error().decode(errors="replace")
         raise KernelError(f"{name} failed ({rc}): {msg}")
+
+
+def launch_count():
+    """Kernel launches the library has queued since it was loaded (tb_launch_count)."""
+    return int(load().tb_launch_count())
 
 
 def call_count():

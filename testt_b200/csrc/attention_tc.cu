@@ -529,5 +529,6 @@ extern "C" int tb_attn_varlen_fwd_tc(const uint16_t *q, const uint16_t *k, const
   TcArgs a{cu_seqlens, out, lse, total, n_heads, n_kv, scale * 1.4426950408889634f};
   const dim3 grid((unsigned)n_heads, (unsigned)batch, (unsigned)((max_len + kTile - 1) / kTile));
   attn_fwd_tc_kernel<<<grid, kThreads, smem, as_stream(stream)>>>(mq, mk, mv, a);
+  note_launch();
   return check_launch("attn_varlen_fwd_tc");
 }

@@ -1,4 +1,5 @@
 // C-ABI error reporting and device queries shared by every kernel file.
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 
@@ -7,6 +8,10 @@
 namespace tb {
 
 static thread_local char g_last_error[512] = "";
+
+static std::atomic<long long> g_launches{0};
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int set_error(int code, const char *fmt, ...) {
   va_list ap;
@@ -75,5 +80,7 @@ extern "C" int tb_wait_timeouts(int32_t device, uint32_t *count) {
   *count = total;
   return TB_OK;
 }
+
+extern "C" int64_t tb_launch_count(void) { return tb::g_launches.load(std::memory_order_relaxed); }
 
 extern "C" int tb_version(void) { return (0 << 16) | (1 << 8) | 0; }

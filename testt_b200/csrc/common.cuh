@@ -41,6 +41,10 @@ int resident_blocks(Kernel kernel, int threads, size_t smem = 0) {
   return per_sm * sm_count();
 }
 
+// Counts every kernel launch this library queues (tb_launch_count): called right after each
+// launch, whether it went through launch() or a <<<>>> of its own.
+void note_launch();
+
 // ---- launches with programmatic dependent launch -------------------------------------------
 // The memory-bound kernels are launched with programmatic dependent launch (PDL) allowed: the
 // GPU may schedule a kernel's CTAs while the previous kernel of the stream is still draining,
@@ -79,6 +83,7 @@ int launch(const char *what, void (*kernel)(KArgs...), dim3 grid, dim3 block, si
     (void)cudaGetLastError();
     return set_error(TB_ELAUNCH, "%s: launch failed: %s", what, cudaGetErrorString(e));
   }
+  note_launch();
   return TB_OK;
 }
 

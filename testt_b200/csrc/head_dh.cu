@@ -556,6 +556,7 @@ extern "C" int tb_head_dh(const uint16_t *logits, int64_t ld, const int64_t *tar
   const int64_t grid = (int64_t)p.splits * p.m_tiles * p.groups;
   if (grid > 0x7fffffffLL) return set_error(TB_EINVAL, "head_dh: too many rows");
   head_dh_kernel<<<(unsigned)grid, kThreads, smem, as_stream(stream)>>>(map_z, map_w, a);
+  note_launch();
   rc = check_launch("head_dh");
   if (rc != TB_OK) return rc;
   ReduceArgs r;

@@ -722,6 +722,7 @@ extern "C" int tb_head_logits_stats(const uint16_t *hidden, const uint16_t *weig
     const int64_t pairs = tiles2 < clusters ? tiles2 : clusters;
     head_logits_stats_2sm<<<(unsigned)(2 * pairs), kThreads, smem2, as_stream(stream)>>>(
         map_h2, map_w2, a);
+    note_launch();
     return check_launch("head_logits_stats_2sm");
   }
   const size_t smem = sizeof(Smem) + 1024;
@@ -731,6 +732,7 @@ extern "C" int tb_head_logits_stats(const uint16_t *hidden, const uint16_t *weig
   const int64_t tiles = (int64_t)a.m_tiles * a.v_tiles;
   const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
   head_logits_stats<<<grid, kThreads, smem, as_stream(stream)>>>(map_h, map_w, a);
+  note_launch();
   return check_launch("head_logits_stats");
 }
 

@@ -823,6 +823,7 @@ int run_gemm(int mode, GemmArgs &a, const Plan &p, const uint16_t *tokens_in, in
     return check_launch(what);
   kernel<<<(unsigned)grid, kThreads, smem, stream>>>(map_b, maps_p[0], maps_p[1], maps_p[2],
                                                       maps_p[3], a);
+  note_launch();
   return check_launch(what);
 }
 

@@ -33,5 +33,6 @@ extern "C" int tb_wait_selftest(int32_t polls, int32_t arrive, int32_t *status, 
   if (polls <= 0 || status == nullptr)
     return set_error(TB_EINVAL, "wait_selftest: polls %d (> 0) and a status buffer", polls);
   wait_selftest_kernel<<<1, 32, 0, as_stream(stream)>>>((uint32_t)polls, arrive != 0, status);
+  note_launch();
   return check_launch("wait_selftest");
 }
