@@ -25,12 +25,10 @@
 // output element in range order (deterministic), maps rows and writes fp32 or fp16.
 //
 // CTA (10 warps):
-//   warp 0      TMA producer: per vocabulary block W's 32 x 512 block (one 3-D copy), into a
-//               4-stage ring
+//   warp 0      TMA producer: per vocabulary block the 128 x 32 fp16 logits tile (no swizzle)
+//               and W's 32 x 512 block (one 3-D copy), into a 4-stage ring
 //   warp 1      TMEM allocation (512 columns) and the MMA issuer
-//   warps 2..9  producers of A: each thread loads its 2 rows x 8 logits of a block straight
-//               from global memory, kAhead blocks ahead in registers, and writes dl (fp16,
-//               swizzled) into the A buffer the MMA has released; 16 rows a warp;
+//   warps 2..9  producers of A: logits tile -> dl (fp16, swizzled) for the MMA, 16 rows a warp;
 //               at the end the epilogue: TMEM -> fp32 partial in the workspace (warps w and
 //               w + 4 share TMEM lane quarter w % 4, each reading half the columns)
 // Every mbarrier wait is bounded (mbar_wait); a role that gives up sets the CTA's error flag and
@@ -48,7 +46,7 @@ constexpr int kBN = 512;       // hidden columns per group (two N = 256 accumula
 constexpr int kHalf = 256;
 constexpr int kBK = 32;        // vocabulary columns per unit: 64 bytes of fp16
 constexpr int kStages = 4;
-constexpr int kAhead = 3;      // vocabulary blocks a producer's logits loads run ahead
+constexpr int kRawBytes = kBM * kBK * 2;   // 8 KB: fp16 logits, 64-byte rows
 constexpr int kABytes = kBM * kBK * 2;     // 8 KB: fp16 dl, K-major, 64-byte swizzle
 constexpr int kBBytes = kBK * kBN * 2;     // 32 KB: W block, MN-major, 128-byte swizzle
 constexpr int kBoxBytes = kBK * 64 * 2;    // one TMA box of W: 32 rows x 64 columns
@@ -65,15 +63,14 @@ constexpr uint32_t kIdesc = (1u << 4) | (1u << 16) | ((uint32_t)(kHalf >> 3) << 
 struct Smem {
   alignas(1024) uint8_t b[kStages][kBBytes];
   alignas(1024) uint8_t a[kStages][kABytes];
-  uint64_t full_b[kStages], full_a[kStages], empty[kStages];
+  alignas(128) uint8_t raw[kStages][kRawBytes];
+  uint64_t full_raw[kStages], full_b[kStages], full_a[kStages], empty[kStages];
   uint64_t acc_full, mma_done;
   uint32_t tmem_base;
   volatile int error;
 };
 
 struct DhArgs {
-  const uint16_t *logits;   // fp16 [rows, cols], row stride ld
-  int64_t ld;
   const int64_t *targets;   // [rows], global column of the label (IGNORE_INDEX: none)
   const float *lse;         // [rows]
   float *ws;                // partials [S][m_tiles][groups][128][512] fp32, block order
@@ -103,6 +100,15 @@ __device__ __forceinline__ uint64_t desc_b(uint32_t addr) {
   d |= (uint64_t)1 << 46;
   d |= (uint64_t)2 << 61;
   return d;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
@@ -164,7 +170,8 @@ __device__ __host__ __forceinline__ void kb_range(int s, int splits, int kblocks
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    head_dh_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ DhArgs args) {
+    head_dh_kernel(const __grid_constant__ CUtensorMap map_z,
+                   const __grid_constant__ CUtensorMap map_w, const __grid_constant__ DhArgs args) {
   extern __shared__ uint8_t smem_raw[];
   Smem &sm = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                         ~uintptr_t(1023));
@@ -179,6 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.full_raw[s], 1);
       mbar_init(&sm.full_b[s], 1);
       mbar_init(&sm.full_a[s], kProducers);
       mbar_init(&sm.empty[s], 1);
@@ -212,6 +220,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const int kb = k0 + i;
+        mbar_expect_tx(&sm.full_raw[s], kRawBytes);
+        tma_load_2d(smem_u32(sm.raw[s]), &map_z, kb * kBK, mt * kBM, &sm.full_raw[s]);
         // W's 32 x 512 block as one copy: 8 column blocks of 64 (the map's third dimension),
         // each a 32 x 64 MN-major atom column; blocks past the hidden size are zero-filled
         mbar_expect_tx(&sm.full_b[s], (uint32_t)kBBytes);
@@ -220,6 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // every copy issued must have landed before the CTA may leave (bounded)
       for (int i = issued - (issued < kStages ? issued : kStages); i < issued; ++i) {
+        mbar_wait(&sm.full_raw[i % kStages], (uint32_t)((i / kStages) & 1));
         mbar_wait(&sm.full_b[i % kStages], (uint32_t)((i / kStages) & 1));
       }
     }
@@ -265,86 +276,55 @@ __global__ void __launch_bounds__(kThreads, 1)
       nl[p] = live[p] ? -__ldg(args.lse + r) * kLog2e : 0.f;
     }
     bool go = true;
-    // this thread's 8 logits of each of its 2 rows for vocabulary block kb, straight from global
-    // memory (rows past the end and columns past the slab read as 0)
-    auto load_block = [&](int kb, uint4 (&z)[2]) {
-      const int c0 = kb * kBK + c * 8;
+    for (int i = 0; i < n && !sm.error; ++i) {
+      const int kb = k0 + i;
+      const int s = i % kStages;
+      if (!mbar_wait(&sm.full_raw[s], (uint32_t)((i / kStages) & 1))) {
+        sm.error = 1;
+        go = false;
+        break;
+      }
+      const uint32_t raw = smem_u32(sm.raw[s]), a = smem_u32(sm.a[s]);
+      const int c0 = kb * kBK + c * 8;  // local column of this thread's 8 values
+      const int64_t gc0 = args.col_offset + c0;
+      const bool ragged = kb * kBK + kBK > args.cols;  // the last block of a partial slab
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
-        const int r = mt * kBM + tw * 16 + p * 8 + (lane >> 2);
-        z[p] = make_uint4(0u, 0u, 0u, 0u);
-        if (r >= args.rows) continue;
-        const uint16_t *src = args.logits + (int64_t)r * args.ld + c0;
-        if (c0 + 8 <= args.cols) {
-          z[p] = __ldg(reinterpret_cast<const uint4 *>(src));
-        } else {
-          uint16_t h8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-          for (int e = 0; e < 8 && c0 + e < args.cols; ++e) h8[e] = __ldg(src + e);
-          z[p] = make_uint4(h8[0] | ((uint32_t)h8[1] << 16), h8[2] | ((uint32_t)h8[3] << 16),
-                            h8[4] | ((uint32_t)h8[5] << 16), h8[6] | ((uint32_t)h8[7] << 16));
+        const int row = tw * 16 + p * 8 + (lane >> 2);
+        uint4 zv;
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(zv.x), "=r"(zv.y), "=r"(zv.z), "=r"(zv.w)
+                     : "r"(raw + (uint32_t)(row * 64 + c * 16)));
+        const uint32_t w[4] = {zv.x, zv.y, zv.z, zv.w};
+        // the label's position among this thread's 8 columns, -1 if elsewhere
+        const int tl = (uint64_t)(target[p] - gc0) < 8u ? (int)(target[p] - gc0) : -1;
+        float g8[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 z = unpack_half2(w[e]);
+          g8[2 * e] = ex2f(fmaf(z.x, kLog2e, nl[p]));
+          g8[2 * e + 1] = ex2f(fmaf(z.y, kLog2e, nl[p]));
         }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float v = g8[e];
+          if (e == tl) v -= 1.f;
+          v *= args.grad_scale;
+          g8[e] = live[p] ? v : 0.f;
+        }
+        if (ragged) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (c0 + e >= args.cols) g8[e] = 0.f;
+        }
+        const uint32_t dst = a + (uint32_t)(row * 64) + ((uint32_t)(c ^ ((row >> 1) & 3)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst),
+                     "r"(pack_half2(g8[0], g8[1])), "r"(pack_half2(g8[2], g8[3])),
+                     "r"(pack_half2(g8[4], g8[5])), "r"(pack_half2(g8[6], g8[7]))
+                     : "memory");
       }
-    };
-    uint4 zp[kAhead][2];
-#pragma unroll
-    for (int q = 0; q < kAhead; ++q)
-      if (q < n) load_block(k0 + q, zp[q]);
-    for (int i0 = 0; i0 < n && go; i0 += kAhead) {
-#pragma unroll
-      for (int q = 0; q < kAhead; ++q) {
-        const int i = i0 + q;
-        if (i >= n || sm.error) {
-          go = go && !sm.error;
-          break;
-        }
-        const int kb = k0 + i;
-        const int s = i % kStages;
-        // the MMA has released this stage's A buffer
-        if (!mbar_wait(&sm.empty[s], (uint32_t)(((i / kStages) & 1) ^ 1))) {
-          sm.error = 1;
-          go = false;
-          break;
-        }
-        const uint32_t a = smem_u32(sm.a[s]);
-        const int c0 = kb * kBK + c * 8;  // local column of this thread's 8 values
-        const int64_t gc0 = args.col_offset + c0;
-        const bool ragged = kb * kBK + kBK > args.cols;  // the last block of a partial slab
-#pragma unroll
-        for (int p = 0; p < 2; ++p) {
-          const int row = tw * 16 + p * 8 + (lane >> 2);
-          const uint32_t w[4] = {zp[q][p].x, zp[q][p].y, zp[q][p].z, zp[q][p].w};
-          // the label's position among this thread's 8 columns, -1 if elsewhere
-          const int tl = (uint64_t)(target[p] - gc0) < 8u ? (int)(target[p] - gc0) : -1;
-          float g8[8];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 z = unpack_half2(w[e]);
-            g8[2 * e] = ex2f(fmaf(z.x, kLog2e, nl[p]));
-            g8[2 * e + 1] = ex2f(fmaf(z.y, kLog2e, nl[p]));
-          }
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            float v = g8[e];
-            if (e == tl) v -= 1.f;
-            v *= args.grad_scale;
-            g8[e] = live[p] ? v : 0.f;
-          }
-          if (ragged) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              if (c0 + e >= args.cols) g8[e] = 0.f;
-          }
-          const uint32_t dst = a + (uint32_t)(row * 64) + ((uint32_t)(c ^ ((row >> 1) & 3)) << 4);
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst),
-                       "r"(pack_half2(g8[0], g8[1])), "r"(pack_half2(g8[2], g8[3])),
-                       "r"(pack_half2(g8[4], g8[5])), "r"(pack_half2(g8[6], g8[7]))
-                       : "memory");
-        }
-        fence_proxy_async();  // the generic-proxy stores, visible to the tensor core
-        mbar_arrive(&sm.full_a[s]);
-        // refill this slot with the block kAhead further on
-        if (i + kAhead < n) load_block(k0 + i + kAhead, zp[q]);
-      }
+      fence_proxy_async();  // the generic-proxy stores, visible to the tensor core
+      mbar_arrive(&sm.full_a[s]);
     }
     // epilogue: this warp's lane quarter, columns [half * 256, half * 256 + 256) of the group
     const int half = tw >> 2;
@@ -447,6 +427,22 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// fp16 row-major [rows, cols] (row stride ld elements) -> box [box_rows, box_cols]
+int make_map(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, int64_t ld,
+             int box_cols, int box_rows, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return set_error(TB_EDEVICE, "head_dh: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims,
+                        strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(TB_EINVAL, "head_dh: tensor map encode failed (%d)", (int)r);
+  return TB_OK;
+}
+
 // W fp16 [cols, hidden] (row-major) viewed as [hidden / 64][cols][64]: box [8][32][64], so one
 // copy brings a 32 x 512 block as 8 consecutive 4 KB atom columns (128-byte swizzle)
 int make_map_w(CUtensorMap *map, const void *base, int64_t cols, int64_t hidden) {
@@ -535,12 +531,12 @@ extern "C" int tb_head_dh(const uint16_t *logits, int64_t ld, const int64_t *tar
   if (workspace_bytes_given < workspace_bytes(p))
     return set_error(TB_EINVAL, "head_dh: workspace of %lld bytes, %lld needed",
                      (long long)workspace_bytes_given, (long long)workspace_bytes(p));
-  CUtensorMap map_w;
-  rc = make_map_w(&map_w, weight, cols, hidden_dim);
+  CUtensorMap map_z, map_w;
+  rc = make_map(&map_z, logits, rows, cols, ld, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc == TB_OK)
+    rc = make_map_w(&map_w, weight, cols, hidden_dim);
   if (rc != TB_OK) return rc;
   DhArgs a;
-  a.logits = logits;
-  a.ld = ld;
   a.targets = targets;
   a.lse = lse;
   a.ws = workspace;
@@ -559,7 +555,7 @@ extern "C" int tb_head_dh(const uint16_t *logits, int64_t ld, const int64_t *tar
     return check_launch("head_dh attribute");
   const int64_t grid = (int64_t)p.splits * p.m_tiles * p.groups;
   if (grid > 0x7fffffffLL) return set_error(TB_EINVAL, "head_dh: too many rows");
-  head_dh_kernel<<<(unsigned)grid, kThreads, smem, as_stream(stream)>>>(map_w, a);
+  head_dh_kernel<<<(unsigned)grid, kThreads, smem, as_stream(stream)>>>(map_z, map_w, a);
   note_launch();
   rc = check_launch("head_dh");
   if (rc != TB_OK) return rc;
