@@ -328,7 +328,7 @@ class HotPath:
 
     def __init__(self, model, lengths, seq, device):
         from testt_b200 import _lib, nf4
-        from testt_b200.model import USE_ROPE_IN_ATTENTION_BWD, model_plan
+        from testt_b200.model import FUSE_NORM_LORA_BWD, USE_ROPE_IN_ATTENTION_BWD, model_plan
         from testt_b200.model import USE_VARLEN_ATTENTION as varlen
 
         self.lib = _lib
@@ -351,9 +351,13 @@ class HotPath:
         # the step's variable-length path runs the RoPE backward inside the attention backward
         # (tb_attn_varlen_bwd_rope), so it has no launch of its own there
         rope_in_attention = bool(varlen and USE_ROPE_IN_ATTENTION_BWD)
-        self.groups = {k: [] for k in ("nf4_unpack", "rmsnorm_fwd", "rmsnorm_bwd", "rope_fwd",
-                                       "rope_bwd", "swiglu_fwd", "swiglu_bwd")
-                       if not (k == "rope_bwd" and rope_in_attention)}
+        # the input norms' backward forms the LoRA pair's input gradient itself
+        # (tb_add_rmsnorm_bwd_lora) when the step links them (model.FUSE_NORM_LORA_BWD)
+        self.groups = {k: [] for k in ("nf4_unpack", "rmsnorm_fwd", "rmsnorm_bwd",
+                                       "rmsnorm_bwd_lora", "rope_fwd", "rope_bwd", "swiglu_fwd",
+                                       "swiglu_bwd")
+                       if not (k == "rope_bwd" and rope_in_attention)
+                       and not (k == "rmsnorm_bwd_lora" and not FUSE_NORM_LORA_BWD)}
         self.bytes = {k: 0 for k in self.groups}
         self.keep = []
         cos, sin = (t.to(dev) for t in synth._rope(seq, dev))
@@ -421,19 +425,36 @@ class HotPath:
                 _lib.ptr(w_norm), _lib.ptr(s) if delta is not None else None, _lib.ptr(y),
                 _lib.ptr(ypad), _lib.ptr(pos) if ypad is not None else None, _lib.ptr(rstd),
                 m, h, 1e-6)
+            # backward: layer 0's input (the frozen embedding's output) takes no gradient, so
+            # the step runs no backward for that norm
             dy = rnd((m, h), f16, 1e-2)
-            dypad = rnd((p, h), f32, 1e-3) if ypad is not None else None
             ds = rnd((m, h), f32, 1e-2) if (layer > 0 and not last) else None
             dx = torch.empty((m, h), dtype=f32, device=dev)
             ddelta = torch.empty((m, h), dtype=f16, device=dev) if layer > 0 else None
-            self.keep += [dy, dypad, ds, dx, ddelta]
-            nb = e * (4 + 2 + 4 + (4 if dypad is not None else 0) + (4 if ds is not None else 0)
-                      + (2 if ddelta is not None else 0)) + 4 * h + 4 * m \
-                + (pad_b if dypad is not None else 0)
-            add("rmsnorm_bwd", nb, "tb_add_rmsnorm_bwd", _lib.ptr(s if delta is not None else x),
-                _lib.ptr(rstd), _lib.ptr(w_norm), _lib.ptr(dy), _lib.ptr(dypad),
-                _lib.ptr(pos) if dypad is not None else None, _lib.ptr(ds), _lib.ptr(dx),
-                _lib.ptr(ddelta), m, h)
+            self.keep += [dy, ds, dx, ddelta]
+            if layer > 0 and not last and FUSE_NORM_LORA_BWD:
+                # the LoRA pair's dh (fp16 [m, 16]), fp16 lora_A and dropout masks of q and v
+                lora = []
+                for _ in range(2):
+                    dh, a16 = rnd((m, 16), f16, 0.05), rnd((16, h), f16, 0.05)
+                    mask = torch.rand((p, h), generator=g, device=dev) > 0.05
+                    self.keep += [dh, a16, mask]
+                    lora += [_lib.ptr(dh), _lib.ptr(a16), _lib.ptr(mask), 1.0 / 0.95]
+                nb = e * (4 + 2 + 4 + 4 + 2 + 2 * 1) + 4 * h + 4 * m + 8 * m \
+                    + 2 * (m * 16 * 2 + 16 * h * 2)
+                add("rmsnorm_bwd_lora", nb, "tb_add_rmsnorm_bwd_lora", _lib.ptr(s),
+                    _lib.ptr(rstd), _lib.ptr(w_norm), _lib.ptr(dy), _lib.ptr(pos), _lib.ptr(ds),
+                    *lora, _lib.ptr(dx), _lib.ptr(ddelta), m, h, 16)
+            elif layer > 0:
+                dypad = rnd((p, h), f32, 1e-3) if ypad is not None else None
+                self.keep.append(dypad)
+                nb = e * (4 + 2 + 4 + (4 if dypad is not None else 0)
+                          + (4 if ds is not None else 0) + (2 if ddelta is not None else 0)) \
+                    + 4 * h + 4 * m + (pad_b if dypad is not None else 0)
+                add("rmsnorm_bwd", nb, "tb_add_rmsnorm_bwd", _lib.ptr(s), _lib.ptr(rstd),
+                    _lib.ptr(w_norm), _lib.ptr(dy), _lib.ptr(dypad),
+                    _lib.ptr(pos) if dypad is not None else None, _lib.ptr(ds), _lib.ptr(dx),
+                    _lib.ptr(ddelta), m, h)
             if last:
                 break
             # ... post-attention norm (delta, no padded copy)
@@ -682,6 +703,56 @@ def _kernel_case(name, device):
                                              c["dy"], c["dypad"], True)
             nbytes = 20 * e + 30720
         info = {"config": "2", "rows": 2048, "hidden": 1536}
+    elif name in ("norm_lora_bwd", "norm_lora_bwd_two"):
+        # a layer's input-norm backward with the LoRA pair's input gradient, config 3's tokens:
+        # formed inside the norm's kernel, or written by tb_lora_dropout_grad_expand and read
+        # back by tb_add_rmsnorm_bwd
+        c = synth.config3(dev)
+        m, h, slots = c["rows"], 1536, 2048
+        g = torch.Generator(device=dev).manual_seed(6)
+        f32, f16 = torch.float32, torch.float16
+
+        def rnd(shape, dtype, std=1.0):
+            return (torch.randn(shape, generator=g, device=dev) * std).to(dtype)
+
+        pos = c["pos_idx"]
+        s, dy, ds = rnd((m, h), f32), rnd((m, h), f16, 1e-2), rnd((m, h), f32, 1e-2)
+        rstd = torch.rand(m, generator=g, device=dev) + 0.5
+        w = torch.ones(h, device=dev)
+        dx, dd = torch.empty((m, h), dtype=f32, device=dev), torch.empty((m, h), dtype=f16,
+                                                                        device=dev)
+        ad = [(rnd((m, 16), f16, 0.05), rnd((16, h), f16, 0.05),
+               torch.rand((slots, h), generator=g, device=dev) > 0.05) for _ in range(2)]
+        def st():  # the current stream at launch time (a capture stream inside a graph)
+            return _lib.stream_of(dx)
+
+        if name == "norm_lora_bwd":
+            fn = lambda: _lib.call(  # noqa: E731
+                "tb_add_rmsnorm_bwd_lora", _lib.ptr(s), _lib.ptr(rstd), _lib.ptr(w),
+                _lib.ptr(dy), _lib.ptr(pos), _lib.ptr(ds), *[
+                    v for dh, a16, mk in ad
+                    for v in (_lib.ptr(dh), _lib.ptr(a16), _lib.ptr(mk), 1.0 / 0.95)],
+                _lib.ptr(dx), _lib.ptr(dd), m, h, 16, st())
+            nbytes = m * h * (4 + 2 + 4 + 4 + 2 + 2) + 4 * h + 4 * m + 8 * m \
+                + 2 * (m * 16 * 2 + 16 * h * 2)
+        else:
+            gx = torch.empty((slots, h), dtype=f32, device=dev)
+            slot_tok = rope.slot_index(pos, slots)
+
+            def fn():
+                _lib.call("tb_lora_dropout_grad_expand", _lib.ptr(ad[0][0]), _lib.ptr(ad[0][1]),
+                          _lib.ptr(ad[1][0]), _lib.ptr(ad[1][1]), _lib.ptr(ad[0][2]),
+                          _lib.ptr(ad[1][2]), _lib.ptr(slot_tok), _lib.ptr(gx), slots, h, 16,
+                          1.0 / 0.95, 1.0 / 0.95, st())
+                _lib.call("tb_add_rmsnorm_bwd", _lib.ptr(s), _lib.ptr(rstd), _lib.ptr(w),
+                          _lib.ptr(dy), _lib.ptr(gx), _lib.ptr(pos), _lib.ptr(ds), _lib.ptr(dx),
+                          _lib.ptr(dd), m, h, st())
+
+            # the same algorithmic bytes as the fused launch: the fp32 padded gradient between
+            # the two launches is this path's own overhead
+            nbytes = m * h * (4 + 2 + 4 + 4 + 2 + 2) + 4 * h + 4 * m + 8 * m \
+                + 2 * (m * 16 * 2 + 16 * h * 2)
+        info = {"config": "3", "tokens": m, "hidden": h, "slots": slots, "rank": 16}
     elif name.startswith("rope") or name.startswith("swiglu"):
         c = synth.config3(dev)
         m = c["rows"]
@@ -706,7 +777,9 @@ def _kernel_case(name, device):
             gu = c["gu"].clone()
             fn = lambda: mlp.gated_silu_backward_(c["dact"], gu)  # noqa: E731
             nbytes = m * 89600
-    elif name == "lora_fwd":  # both rank-16 adapters of a layer at config 3's 621 tokens
+    elif name in ("lora_fwd", "lora_fwd_cluster"):
+        # both rank-16 adapters of a layer at config 3's 621 tokens; lora_fwd_cluster: the
+        # 8-CTA cluster kernel (tb_lora_forward_variant 1) instead of the automatic choice
         c = synth.config3(dev)
         m, hidden, r = c["rows"], 1536, 16
         g = torch.Generator(device=dev).manual_seed(5)
@@ -724,12 +797,19 @@ def _kernel_case(name, device):
         oq = torch.empty((m, hidden), dtype=f16, device=dev)
         ov = torch.empty((m, 256), dtype=f16, device=dev)
         pos = c["pos_idx"]
-        fn = lambda: _lib.call(  # noqa: E731
-            "tb_lora_forward", _lib.ptr(dq), _lib.ptr(aq), _lib.ptr(bq), _lib.ptr(w16[0]),
-            _lib.ptr(w16[1]), _lib.ptr(xq), _lib.ptr(hq), _lib.ptr(oq), hidden, 2.0, _lib.ptr(dv),
-            _lib.ptr(av), _lib.ptr(bv), _lib.ptr(w16[2]), _lib.ptr(w16[3]), _lib.ptr(xv),
-            _lib.ptr(hv), _lib.ptr(ov), 256, 2.0, _lib.ptr(pos), m, hidden, r,
-            _lib.stream_of(oq))
+        variant = 1 if name == "lora_fwd_cluster" else 0
+
+        def fn():
+            _lib.load().tb_lora_forward_variant(variant)
+            try:
+                _lib.call("tb_lora_forward", _lib.ptr(dq), _lib.ptr(aq), _lib.ptr(bq),
+                          _lib.ptr(w16[0]), _lib.ptr(w16[1]), _lib.ptr(xq), _lib.ptr(hq),
+                          _lib.ptr(oq), hidden, 2.0, _lib.ptr(dv), _lib.ptr(av), _lib.ptr(bv),
+                          _lib.ptr(w16[2]), _lib.ptr(w16[3]), _lib.ptr(xv), _lib.ptr(hv),
+                          _lib.ptr(ov), 256, 2.0, _lib.ptr(pos), m, hidden, r,
+                          _lib.stream_of(oq))
+            finally:
+                _lib.load().tb_lora_forward_variant(0)
         # x read (fp32) and written (fp16) for both adapters, h16, outputs, weights (fp32 in, fp16 out)
         nbytes = 2 * m * hidden * (4 + 2) + 2 * m * r * 2 + m * (hidden + 256) * 2 \
             + (2 * r * hidden + (hidden + 256) * r) * (4 + 2) + m * 8
@@ -1248,7 +1328,9 @@ def main():
     ap.add_argument("--kernel", default=None,
                     help="time one kernel at its configuration instead (nf4, nf4_nested, "
                          "rmsnorm_fwd, rmsnorm_bwd, rope_fwd, rope_bwd, swiglu_fwd, swiglu_bwd, "
-                         "lora_fwd, attn_fwd, attn_fwd_tc, attn_fwd_bwd, "
+                         "lora_fwd, lora_fwd_cluster, norm_lora_bwd, norm_lora_bwd_two, "
+                         "attn_fwd, attn_fwd_tc, "
+                         "attn_fwd_bwd, "
                          "head_stats, head_tc, head_full, head_cublas, head_dh, "
                          "head_dh_cublas, all; the NF4-decoding GEMMs, "
                          "with what they replace: gate_up_fused_fwd, gate_up_fused_bwd, "

@@ -180,6 +180,26 @@ int tb_add_rmsnorm_bwd(const float *s, const float *rstd, const float *weight, c
                        const float *dypad, const int64_t *pad_idx, const float *ds, float *dx,
                        uint16_t *ddelta, int64_t rows, int64_t hidden, void *stream);
 
+/* The same backward with dypad formed in registers from the rank-16 LoRA pair the padded output
+ * feeds (solution/model.py:195-206 under fp16 autocast: the dropout backward of lora_A's input
+ * gradient), instead of read from a tensor tb_lora_dropout_grad_expand wrote: per row r, slot
+ * p = pad_idx[r] and column c,
+ *   dypad[p, c] = drop_q'(fp16(dh_q[r] . a16_q[:, c])) + drop_v'(fp16(dh_v[r] . a16_v[:, c]))
+ *   drop'(x) = mask[p, c] ? x * scale : 0 (x when mask is NULL)
+ * with tb_lora_dropout_grad_expand's operations and roundings, and tb_add_rmsnorm_bwd's arithmetic
+ * after it. The outputs equal that two-launch path's bit for bit wherever tb_add_rmsnorm_bwd
+ * plans one or two 8-column chunks per thread (for 1536 columns: up to 1381 rows); where it plans
+ * more for a large row count, its row sums run in another order and agree to fp32 rounding.
+ * dh: fp16 [rows, 16]; a16: fp16 [16, hidden]; mask: bool [slots, hidden]; an adapter with dh
+ * NULL is absent. rank must be 16 and hidden a multiple of 8 up to 4096 (TB_EINVAL otherwise);
+ * all buffers 16-byte aligned, masks 8-byte (TB_EALIGN). */
+int tb_add_rmsnorm_bwd_lora(const float *s, const float *rstd, const float *weight,
+                            const uint16_t *dy, const int64_t *pad_idx, const float *ds,
+                            const uint16_t *dh_q, const uint16_t *a16_q, const uint8_t *mask_q,
+                            float scale_q, const uint16_t *dh_v, const uint16_t *a16_v,
+                            const uint8_t *mask_v, float scale_v, float *dx, uint16_t *ddelta,
+                            int64_t rows, int64_t hidden, int32_t rank, void *stream);
+
 /* ---------------------------------------------------------------------------------------------
  * QKV pack: LoRA add + rotary embedding + scatter into the padded attention layout. Replaces
  * rope_pack_fwd_kernel / rope_pack_bwd_kernel and RopePack, solution/rope.py:24-128, :136-176.
@@ -256,6 +276,14 @@ int tb_lora_forward(const float *dropped_q, const float *a_q, const float *b_q, 
                     uint16_t *h16_v, uint16_t *out_v, int64_t hout_v, float scale_v,
                     const int64_t *pos_idx, int64_t rows, int64_t hidden, int32_t rank,
                     void *stream);
+
+/* Which kernel tb_lora_forward runs, process-wide: 0 automatic (the cluster-free kernel, a CTA
+ * per 16 rows, adapter and slice of 384 outputs with the x tile staged in shared memory, where
+ * hidden <= 3192 and the dropout outputs and x16 are 16-byte aligned; else the cluster kernel),
+ * 1 the kernel whose 8-CTA clusters split lora_A's K, 2 the cluster-free kernel (TB_EINVAL from
+ * tb_lora_forward where it does not take the buffers). The two sum lora_A's products in different
+ * orders, so h16 may differ by an fp16 rounding. */
+int tb_lora_forward_variant(int32_t variant);
 
 /* The padded gradient of the dropout input both adapters share, fp32 [slots, hidden]:
  * grad[p] = fp32(dxq[t]) * scale_q * mask_q[p] + fp32(dxv[t]) * scale_v * mask_v[p] for the token

@@ -210,3 +210,48 @@ def test_fused_path_declines_what_it_does_not_run(lora_model):
         assert not isinstance(out.logits, HeadStats)
     finally:
         lora_model.train()
+
+
+@pytest.mark.parametrize("fixture", ["lora_model", "lora_model_d128"])
+def test_norm_backward_with_lora_dropout_backward_gives_the_same_step(request, fixture):
+    """Each layer's input norm forming the LoRA pair's input gradient inside its backward
+    (model.FUSE_NORM_LORA_BWD: tb_add_rmsnorm_bwd_lora, no tb_lora_dropout_grad_expand launch)
+    against the two launches: the same loss and the same gradients, bit for bit."""
+    from testt_b200 import _lib, model
+
+    lm = request.getfixturevalue(fixture)
+    names = []
+    original = _lib.call
+
+    def recorded(name, *args):
+        names.append(name)
+        return original(name, *args)
+
+    saved = model.FUSE_NORM_LORA_BWD
+    _lib.call = recorded
+    try:
+        model.FUSE_NORM_LORA_BWD = False
+        ref = run(lm, fused=True)
+        two = list(names)
+        names.clear()
+        model.FUSE_NORM_LORA_BWD = True
+        got = run(lm, fused=True)
+    finally:
+        _lib.call = original
+        model.FUSE_NORM_LORA_BWD = saved
+    layers = lm.config.num_hidden_layers
+    # layer 0's norm input (the embedding output) takes no gradient, so neither path forms it
+    assert two.count("tb_lora_dropout_grad_expand") == layers - 1
+    assert "tb_add_rmsnorm_bwd_lora" not in two
+    assert names.count("tb_add_rmsnorm_bwd_lora") == layers - 1
+    assert "tb_lora_dropout_grad_expand" not in names
+    assert got[0] == ref[0]
+    assert set(got[1]) == set(ref[1])
+    for name, grad in ref[1].items():
+        assert torch.equal(got[1][name], grad), name
+    # the forward's statistics: the per-row loss sums come from PyTorch's index_add_, whose
+    # atomic float additions run in no fixed order
+    assert got[2] == pytest.approx(ref[2], rel=1e-6)
+    assert got[3] == pytest.approx(ref[3], rel=1e-6)
+    assert got[4][1] == ref[4][1]
+    assert got[4][0] == pytest.approx(ref[4][0], rel=1e-6)

@@ -28,6 +28,8 @@ SIGNATURES = {
     "tb_nf4_unpack_multi": [_I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     "tb_add_rmsnorm_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _F, _P],
     "tb_add_rmsnorm_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _P],
+    "tb_add_rmsnorm_bwd_lora": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _F, _P, _P, _P, _F, _P, _P,
+                                _I64, _I64, _I32, _P],
     "tb_rope_pack_fwd": [_P, _P, _P, _I32, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32,
                          _I32, _I32, _P],
     "tb_rope_pack_bwd": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _P],
@@ -59,6 +61,7 @@ SIGNATURES = {
     "tb_head_stats_grad_noalloc": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P],
     "tb_head_logits_stats": [_P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _P],
     "tb_head_gemm_variant": [_I32],
+    "tb_lora_forward_variant": [_I32],
     "tb_nf4_gemm": [_I32, _P, _I64, _I64, _I32, _P, _P, _P, _P, _I64, _P, _P, _I64, _P, _I64, _P],
     "tb_nf4_gemm_workspace": [_I32, _I64, _I32, _P, _I64],
     "tb_nf4_gemm_variant": [_I32],

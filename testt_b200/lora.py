@@ -23,6 +23,7 @@ backward + the sum of the two in backward.
 import torch
 
 from . import _lib
+from .rmsnorm import lora_link_ok
 
 _F16 = torch.float16
 
@@ -90,7 +91,7 @@ class LoraPair(torch.autograd.Function):
     absent (its weights None)."""
 
     @staticmethod
-    def forward(ctx, x_pad, aq, bq, av, bv, pos_idx, slot_tok, cfg):
+    def forward(ctx, x_pad, aq, bq, av, bv, pos_idx, slot_tok, cfg, link=None):
         (pq, on_q, sq), (pv, on_v, sv) = cfg
         rows = pos_idx.numel()
         hidden = x_pad.shape[1]
@@ -146,6 +147,7 @@ class LoraPair(torch.autograd.Function):
         ctx.cfg = cfg
         ctx.slots = x_pad.shape[0]
         ctx.hidden = hidden
+        ctx.link = link
         return outs[0], outs[1]
 
     @staticmethod
@@ -199,11 +201,11 @@ class LoraPair(torch.autograd.Function):
                 a16s.append(a16.contiguous())
                 grads += [da, db]
             gx = None
-            if need[0]:
+            scale_q = float(1.0 / (1.0 - pq)) if mq is not None else 1.0
+            scale_v = float(1.0 / (1.0 - pv)) if mv is not None else 1.0
+            if need[0] and not (expand and hand_off(ctx, dhs, a16s, mq, mv, scale_q, scale_v)):
                 gx = torch.empty((ctx.slots, ctx.hidden), dtype=torch.float32,
                                  device=slot_tok.device)
-                scale_q = float(1.0 / (1.0 - pq)) if mq is not None else 1.0
-                scale_v = float(1.0 / (1.0 - pv)) if mv is not None else 1.0
                 if expand:
                     _lib.call("tb_lora_dropout_grad_expand", _lib.ptr(dhs[0]), _lib.ptr(a16s[0]),
                               _lib.ptr(dhs[1]), _lib.ptr(a16s[1]), _lib.ptr(mq), _lib.ptr(mv),
@@ -214,7 +216,20 @@ class LoraPair(torch.autograd.Function):
                               _lib.ptr(mq), _lib.ptr(mv), _lib.ptr(slot_tok), _lib.ptr(gx),
                               ctx.slots, ctx.hidden, scale_q, scale_v, _lib.stream_of(gx))
         grads_written([p for p, g in zip(ctx.params, grads) if g is None])
-        return (gx, grads[0], grads[1], grads[2], grads[3], None, None, None)
+        return (gx, grads[0], grads[1], grads[2], grads[3], None, None, None, None)
+
+
+def hand_off(ctx, dhs, a16s, mq, mv, scale_q, scale_v):
+    """Leaves the padded input's gradient to the add+RMSNorm node that produced the input when
+    the forward was given its LoraGradLink (rmsnorm.add_rmsnorm) and its kernel takes the
+    shapes: the factors go into the link and the caller returns no gradient for x_pad. False
+    when the caller has to form the gradient itself."""
+    link = ctx.link
+    if link is None or not lora_link_ok(ctx.hidden, _RANK) or \
+            any(h is not None and h.shape[1] != _RANK for h in dhs):
+        return False
+    link.put(dhs[0], a16s[0], mq, scale_q, dhs[1], a16s[1], mv, scale_v)
+    return True
 
 
 # The rank-16 backward in two launches (lora_fused.LoraPairFused, tb_lora_backward) instead of
@@ -232,9 +247,10 @@ def _node():
     return LoraPair
 
 
-def lora_pair(parts_q, parts_v, x_pad, pos_idx, slot_tok):
+def lora_pair(parts_q, parts_v, x_pad, pos_idx, slot_tok, link=None):
     """(lora_q, lora_v) for peft adapter parts (dropout, lora_A, lora_B, scaling) or None per
-    projection; None when neither projection has an adapter."""
+    projection; None when neither projection has an adapter. `link`: the LoraGradLink given to
+    the add_rmsnorm call that made x_pad, whose backward then forms x_pad's gradient."""
     if parts_q is None and parts_v is None:
         return None, None
     _lib.require_cuda(x_pad, pos_idx, slot_tok, what="lora_pair")
@@ -248,4 +264,4 @@ def lora_pair(parts_q, parts_v, x_pad, pos_idx, slot_tok):
         p, on = _dropout_of(dropout)
         cfg.append((p, on, float(scaling)))
         weights += [lora_a.weight, lora_b.weight]
-    return _node().apply(x_pad.contiguous(), *weights, pos_idx, slot_tok, tuple(cfg))
+    return _node().apply(x_pad.contiguous(), *weights, pos_idx, slot_tok, tuple(cfg), link)

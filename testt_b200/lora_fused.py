@@ -15,7 +15,7 @@ import functools
 import torch
 
 from . import _lib
-from .lora import _F16, _RANK, LoraPair, _in_bucket, grads_written
+from .lora import _F16, _RANK, LoraPair, _in_bucket, grads_written, hand_off
 
 
 # True: the dA launch of tb_lora_backward runs on a side stream while the dropout backward
@@ -116,11 +116,11 @@ class LoraPairFused(LoraPair):
                 msg = _lib.load().tb_last_error().decode(errors="replace")
                 raise _lib.KernelError(f"tb_lora_backward failed ({rc}): {msg}")
             gx = None
-            if need[0]:
+            scale_q = float(1.0 / (1.0 - pq)) if mq is not None else 1.0
+            scale_v = float(1.0 / (1.0 - pv)) if mv is not None else 1.0
+            if need[0] and not hand_off(ctx, dhs, a16s, mq, mv, scale_q, scale_v):
                 gx = torch.empty((ctx.slots, ctx.hidden), dtype=torch.float32,
                                  device=slot_tok.device)
-                scale_q = float(1.0 / (1.0 - pq)) if mq is not None else 1.0
-                scale_v = float(1.0 / (1.0 - pv)) if mv is not None else 1.0
                 _lib.call("tb_lora_dropout_grad_expand", _lib.ptr(dhs[0]), _lib.ptr(a16s[0]),
                           _lib.ptr(dhs[1]), _lib.ptr(a16s[1]), _lib.ptr(mq), _lib.ptr(mv),
                           _lib.ptr(slot_tok), _lib.ptr(gx), ctx.slots, ctx.hidden, _RANK,
@@ -131,4 +131,4 @@ class LoraPairFused(LoraPair):
                 main.wait_stream(side)
             del keep
         grads_written([p for p, g in zip(ctx.params, grads) if g is None])
-        return (gx, grads[0], grads[1], grads[2], grads[3], None, None, None)
+        return (gx, grads[0], grads[1], grads[2], grads[3], None, None, None, None)

@@ -11,7 +11,9 @@ Per decoder layer, with s the fp32 residual stream of the M real tokens:
     W          = unpack(q|k|v, o, gate|up, down)      tb_nf4_unpack_multi, one launch per layer
     qkv        = y @ [Wq; Wk; Wv]^T + b               cuBLAS
     lq, lv     = LoRA(dropout(y_pad))                 lora.lora_pair: PyTorch dropout (same draws),
-                                                      tb_lora_gather, cuBLAS; tb_lora_dropout_grad
+                                                      tb_lora_forward; backward tb_lora_backward,
+                                                      its dropout backward inside the input
+                                                      norm's (tb_add_rmsnorm_bwd_lora)
     q, k, v    = rope_tokens(qkv, lq, lv)             tb_rope_tokens_fwd, token-major [M, H, 128]
     a          = varlen causal attention(q, k, v)     tb_attn_varlen_fwd / tb_attn_varlen_bwd_rope
                                                       (sm_100, head dim 128; the backward writes
@@ -38,7 +40,7 @@ from . import fused_layer as _fused_layer
 from .head import IGNORE_INDEX, fused_head_loss
 from .mlp import layer_mlp
 from .nf4 import LayerWeights, layer_linear
-from .rmsnorm import add_rmsnorm
+from .rmsnorm import LoraGradLink, add_rmsnorm
 from .lora import lora_pair
 from .rope import rope_pack, rope_tokens, slot_index
 
@@ -78,6 +80,13 @@ KEEP_UNPACKED_WEIGHTS = True
 # default: at the config-5 shapes the decoding GEMM is slower than one unpack launch per layer
 # plus cuBLAS (same results either way; the model tests run both).
 USE_NF4_GEMM = False
+
+# True: each layer's input norm and its LoRA pair share a rmsnorm.LoraGradLink, so the norm's
+# backward forms the LoRA branch's input gradient (the dropout backward of dh . fp16(A)) inside
+# its own kernel (tb_add_rmsnorm_bwd_lora) instead of reading the fp32 [slots, hidden] tensor
+# tb_lora_dropout_grad_expand wrote: one launch per layer fewer, same values. False keeps the
+# two launches.
+FUSE_NORM_LORA_BWD = True
 
 _ALLOWED_KWARGS = {"num_items_in_batch", "output_attentions", "output_hidden_states",
                    "return_dict"}
@@ -344,13 +353,14 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
     for lp in plan.layers:
         layer = lp.layer
         # y_pad's padding rows only reach dropout outputs that are never gathered: not zeroed
+        link = LoraGradLink() if FUSE_NORM_LORA_BWD else None
         s, y, y_pad = add_rmsnorm(s, delta, layer.input_layernorm.weight,
                                   layer.input_layernorm.variance_epsilon, pos_idx, padded,
-                                  zero_padding=False)
+                                  zero_padding=False, link=link)
         lw = lp.weights
         if USE_NF4_GEMM and varlen and plan.head_dim == 128 and _fused_layer.usable(lw):
             lora_q, lora_v = lora_pair(_lora_parts(lp.attn.q_proj), _lora_parts(lp.attn.v_proj),
-                                       y_pad, pos_idx, slot_tok)
+                                       y_pad, pos_idx, slot_tok, link)
             del y_pad
             q, k, v = _fused_layer.qkv_rope(y, lw, 0, lp.qkv_bias, lora_q, lora_v, cos, sin,
                                             pos_idx, batch, seq, plan.n_heads, plan.n_kv)
@@ -369,7 +379,7 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
         lw.operands(dev)  # every NF4 weight of the layer, one unpack launch
         qkv = layer_linear(y, lw, 0, lp.qkv_bias, last=True)
         lora_q, lora_v = lora_pair(_lora_parts(lp.attn.q_proj), _lora_parts(lp.attn.v_proj),
-                                   y_pad, pos_idx, slot_tok)
+                                   y_pad, pos_idx, slot_tok, link)
         del y_pad
         if varlen and USE_ROPE_IN_ATTENTION_BWD:
             # one node: its backward writes the q|k|v gradient through the rotary embedding's
