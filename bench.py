@@ -777,9 +777,7 @@ def _kernel_case(name, device):
             gu = c["gu"].clone()
             fn = lambda: mlp.gated_silu_backward_(c["dact"], gu)  # noqa: E731
             nbytes = m * 89600
-    elif name in ("lora_fwd", "lora_fwd_cluster"):
-        # both rank-16 adapters of a layer at config 3's 621 tokens; lora_fwd_cluster: the
-        # 8-CTA cluster kernel (tb_lora_forward_variant 1) instead of the automatic choice
+    elif name == "lora_fwd":  # both rank-16 adapters of a layer at config 3's 621 tokens
         c = synth.config3(dev)
         m, hidden, r = c["rows"], 1536, 16
         g = torch.Generator(device=dev).manual_seed(5)
@@ -797,19 +795,12 @@ def _kernel_case(name, device):
         oq = torch.empty((m, hidden), dtype=f16, device=dev)
         ov = torch.empty((m, 256), dtype=f16, device=dev)
         pos = c["pos_idx"]
-        variant = 1 if name == "lora_fwd_cluster" else 0
-
-        def fn():
-            _lib.load().tb_lora_forward_variant(variant)
-            try:
-                _lib.call("tb_lora_forward", _lib.ptr(dq), _lib.ptr(aq), _lib.ptr(bq),
-                          _lib.ptr(w16[0]), _lib.ptr(w16[1]), _lib.ptr(xq), _lib.ptr(hq),
-                          _lib.ptr(oq), hidden, 2.0, _lib.ptr(dv), _lib.ptr(av), _lib.ptr(bv),
-                          _lib.ptr(w16[2]), _lib.ptr(w16[3]), _lib.ptr(xv), _lib.ptr(hv),
-                          _lib.ptr(ov), 256, 2.0, _lib.ptr(pos), m, hidden, r,
-                          _lib.stream_of(oq))
-            finally:
-                _lib.load().tb_lora_forward_variant(0)
+        fn = lambda: _lib.call(  # noqa: E731
+            "tb_lora_forward", _lib.ptr(dq), _lib.ptr(aq), _lib.ptr(bq), _lib.ptr(w16[0]),
+            _lib.ptr(w16[1]), _lib.ptr(xq), _lib.ptr(hq), _lib.ptr(oq), hidden, 2.0, _lib.ptr(dv),
+            _lib.ptr(av), _lib.ptr(bv), _lib.ptr(w16[2]), _lib.ptr(w16[3]), _lib.ptr(xv),
+            _lib.ptr(hv), _lib.ptr(ov), 256, 2.0, _lib.ptr(pos), m, hidden, r,
+            _lib.stream_of(oq))
         # x read (fp32) and written (fp16) for both adapters, h16, outputs, weights (fp32 in, fp16 out)
         nbytes = 2 * m * hidden * (4 + 2) + 2 * m * r * 2 + m * (hidden + 256) * 2 \
             + (2 * r * hidden + (hidden + 256) * r) * (4 + 2) + m * 8
@@ -1328,8 +1319,7 @@ def main():
     ap.add_argument("--kernel", default=None,
                     help="time one kernel at its configuration instead (nf4, nf4_nested, "
                          "rmsnorm_fwd, rmsnorm_bwd, rope_fwd, rope_bwd, swiglu_fwd, swiglu_bwd, "
-                         "lora_fwd, lora_fwd_cluster, norm_lora_bwd, norm_lora_bwd_two, "
-                         "attn_fwd, attn_fwd_tc, "
+                         "lora_fwd, norm_lora_bwd, norm_lora_bwd_two, attn_fwd, attn_fwd_tc, "
                          "attn_fwd_bwd, "
                          "head_stats, head_tc, head_full, head_cublas, head_dh, "
                          "head_dh_cublas, all; the NF4-decoding GEMMs, "

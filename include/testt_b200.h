@@ -277,14 +277,6 @@ int tb_lora_forward(const float *dropped_q, const float *a_q, const float *b_q, 
                     const int64_t *pos_idx, int64_t rows, int64_t hidden, int32_t rank,
                     void *stream);
 
-/* Which kernel tb_lora_forward runs, process-wide: 0 automatic (the cluster-free kernel, a CTA
- * per 16 rows, adapter and slice of 384 outputs with the x tile staged in shared memory, where
- * hidden <= 3192 and the dropout outputs and x16 are 16-byte aligned; else the cluster kernel),
- * 1 the kernel whose 8-CTA clusters split lora_A's K, 2 the cluster-free kernel (TB_EINVAL from
- * tb_lora_forward where it does not take the buffers). The two sum lora_A's products in different
- * orders, so h16 may differ by an fp16 rounding. */
-int tb_lora_forward_variant(int32_t variant);
-
 /* The padded gradient of the dropout input both adapters share, fp32 [slots, hidden]:
  * grad[p] = fp32(dxq[t]) * scale_q * mask_q[p] + fp32(dxv[t]) * scale_v * mask_v[p] for the token
  * t = slot_tok[p], 0 where slot_tok[p] < 0. dxq / dxv: fp16 [rows, hidden] gradients of the fp16

@@ -61,7 +61,6 @@ SIGNATURES = {
     "tb_head_stats_grad_noalloc": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P],
     "tb_head_logits_stats": [_P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _P],
     "tb_head_gemm_variant": [_I32],
-    "tb_lora_forward_variant": [_I32],
     "tb_nf4_gemm": [_I32, _P, _I64, _I64, _I32, _P, _P, _P, _P, _I64, _P, _P, _I64, _P, _I64, _P],
     "tb_nf4_gemm_workspace": [_I32, _I64, _I32, _P, _I64],
     "tb_nf4_gemm_variant": [_I32],

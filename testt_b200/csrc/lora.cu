@@ -14,8 +14,6 @@
 //             two, five launches and ~100 MB of traffic per layer at 2048 x 1536).
 // Each product and the sum are rounded on their own (no contraction), as the separate PyTorch
 // operations round them.
-#include <atomic>
-
 #include "common.cuh"
 
 namespace tb {
@@ -526,182 +524,6 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kFwdWarps * 3
   }
 }
 
-// ---- the adapters' forward without clusters (rank 16) ----------------------------------------
-// The same operations and roundings as lora_fwd_kernel, laid out for a short serial chain per CTA
-// instead of a cluster-wide reduction. A CTA takes one 16-row tile of one adapter and one slice
-// of kSliceTiles output tiles (8 columns each) of its lora_B; the q adapter's 1536 outputs are 4
-// slices, so its x tile is read by 4 CTAs (from L2 after the first). Per CTA:
-//   - the rows' slots, then the whole fp32 x tile [16, hidden] by cp.async into shared memory
-//     (rows padded by 8 floats against bank conflicts), and this CTA's lora_B fragments, all
-//     issued before anything waits;
-//   - h = x16 . fp16(A)^T on the tensor cores (mma.sync m16n8k16): warp w takes the k-steps
-//     w, w + 8, ..., its x fragments from shared memory and lora_A's straight from L2, both
-//     rounded to fp16 in registers; the 8 warps' 16 x 16 partial sums added in warp order;
-//   - out = fp16(fp32(fp16(h16 . fp16(B)^T)) * scale) for the slice's output tiles;
-//   - slice 0 also stores x16 and h16 for the backward, and the CTAs of tile 0 the fp16 weights
-//     (A by slice 0, each slice its rows of B).
-constexpr int kSplitRows = 16;
-constexpr int kSliceTiles = 48;
-constexpr int kSplitWarps = 8;
-constexpr int kSplitPad = 8;  // floats of padding per x row in shared memory
-constexpr size_t kSplitMaxSmem = 200 * 1024;  // the x tile's bytes: hidden up to 3192
-
-// 0: automatic, 1: the cluster kernel, 2: the cluster-free kernel (process-wide;
-// tb_lora_forward_variant)
-std::atomic<int> g_lora_fwd_variant{0};
-
-__device__ __forceinline__ void cp_async16_lora(void *dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
-               : "memory");
-}
-
-__host__ __device__ constexpr size_t split_smem_bytes(int hidden) {
-  return (size_t)kSplitRows * (hidden + kSplitPad) * sizeof(float);
-}
-
-__global__ void __launch_bounds__(kSplitWarps * 32)
-    lora_fwd_split_kernel(const __grid_constant__ LoraFwdArgs a, int slices_q) {
-  pdl_wait();
-  pdl_release();
-  extern __shared__ __align__(16) float xs[];  // [kSplitRows][hidden + kSplitPad]
-  __shared__ float part[kSplitWarps][kSplitRows][kRank + 1];
-  __shared__ uint32_t h_sh[kSplitRows][kRank / 2];  // h16, fp16x2 pairs
-  __shared__ int64_t slot_sh[kSplitRows];
-  const int adi = (int)blockIdx.y < slices_q ? 0 : 1;
-  const int slice = adi == 0 ? (int)blockIdx.y : (int)blockIdx.y - slices_q;
-  const LoraFwdAdapter &p = a.ad[adi];
-  if (p.a == nullptr) return;  // the whole CTA
-  const int H = a.hidden, HO = p.hout, ld = H + kSplitPad;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const int64_t m0 = (int64_t)blockIdx.x * kSplitRows;
-  const bool writer = blockIdx.x == 0;
-  const int nt_begin = slice * kSliceTiles, nt_end = min(HO / 8, nt_begin + kSliceTiles);
-
-  if (threadIdx.x < kSplitRows) {
-    const int64_t r = m0 + threadIdx.x;
-    slot_sh[threadIdx.x] = r < a.rows ? __ldg(a.pos_idx + r) : -1;
-  }
-  // lora_B fragments of this warp's output tiles (independent of h), loaded while x arrives
-  constexpr int kBPerWarp = (kSliceTiles + kSplitWarps - 1) / kSplitWarps;
-  uint32_t bf[kBPerWarp][2];
-#pragma unroll
-  for (int i = 0; i < kBPerWarp; ++i) {
-    const int nt = nt_begin + warp + i * kSplitWarps;
-    bf[i][0] = bf[i][1] = 0u;
-    if (nt < nt_end) {
-      const int n = nt * 8 + g;  // B[k][n] = lora_B[n][k]
-      bf[i][0] = ld_f16x2(p.b + (int64_t)n * kRank + 2 * t);
-      bf[i][1] = ld_f16x2(p.b + (int64_t)n * kRank + 2 * t + 8);
-    }
-  }
-  __syncthreads();  // slot_sh
-  // the x tile: 16-byte pieces, H / 4 per row; rows past the end are zero
-  const int per_row = H / 4;
-  for (int e = threadIdx.x; e < kSplitRows * per_row; e += blockDim.x) {
-    const int r = e / per_row, c4 = e - r * per_row;
-    float *dst = xs + (size_t)r * ld + 4 * c4;
-    const int64_t slot = slot_sh[r];
-    if (slot >= 0) {
-      cp_async16_lora(dst, p.dropped + slot * H + 4 * c4);
-    } else {
-      *reinterpret_cast<float4 *>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  }
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-  __syncthreads();  // the x tile
-
-  // lora_A: warp w takes k-steps w, w + 8, ...; n-tile 0 = ranks 0..7, n-tile 1 = ranks 8..15
-  float c[2][4] = {};
-  const int ksteps = H / 16;
-#pragma unroll 4
-  for (int ks = warp; ks < ksteps; ks += kSplitWarps) {
-    const int k = ks * 16 + 2 * t;
-    const float2 x00 = *reinterpret_cast<const float2 *>(xs + (size_t)g * ld + k);
-    const float2 x10 = *reinterpret_cast<const float2 *>(xs + (size_t)(g + 8) * ld + k);
-    const float2 x01 = *reinterpret_cast<const float2 *>(xs + (size_t)g * ld + k + 8);
-    const float2 x11 = *reinterpret_cast<const float2 *>(xs + (size_t)(g + 8) * ld + k + 8);
-    const uint32_t a0 = pack_half2(x00.x, x00.y), a1 = pack_half2(x10.x, x10.y);
-    const uint32_t a2 = pack_half2(x01.x, x01.y), a3 = pack_half2(x11.x, x11.y);
-    const uint32_t w00 = ld_f16x2(p.a + (int64_t)g * H + k);
-    const uint32_t w01 = ld_f16x2(p.a + (int64_t)g * H + k + 8);
-    const uint32_t w10 = ld_f16x2(p.a + (int64_t)(g + 8) * H + k);
-    const uint32_t w11 = ld_f16x2(p.a + (int64_t)(g + 8) * H + k + 8);
-    mma_16816(c[0], a0, a1, a2, a3, w00, w01);
-    mma_16816(c[1], a0, a1, a2, a3, w10, w11);
-  }
-#pragma unroll
-  for (int nt = 0; nt < 2; ++nt) {
-    part[warp][g][8 * nt + 2 * t] = c[nt][0];
-    part[warp][g][8 * nt + 2 * t + 1] = c[nt][1];
-    part[warp][g + 8][8 * nt + 2 * t] = c[nt][2];
-    part[warp][g + 8][8 * nt + 2 * t + 1] = c[nt][3];
-  }
-  __syncthreads();
-  if (threadIdx.x < kSplitRows * kRank / 2) {  // one fp16x2 pair of h each, warps in order
-    const int row = threadIdx.x / (kRank / 2), pr = threadIdx.x % (kRank / 2);
-    float h0 = 0.f, h1 = 0.f;
-#pragma unroll
-    for (int w = 0; w < kSplitWarps; ++w) {
-      h0 += part[w][row][2 * pr];
-      h1 += part[w][row][2 * pr + 1];
-    }
-    const uint32_t hv = pack_half2(h0, h1);
-    h_sh[row][pr] = hv;
-    if (slice == 0 && m0 + row < a.rows)
-      reinterpret_cast<uint32_t *>(p.h16)[(m0 + row) * (kRank / 2) + pr] = hv;
-  }
-  __syncthreads();  // h_sh
-
-  // lora_B over this slice's output tiles, A operand = h16
-  const uint32_t ha0 = h_sh[g][t], ha1 = h_sh[g + 8][t], ha2 = h_sh[g][4 + t],
-                 ha3 = h_sh[g + 8][4 + t];
-  const bool rv0 = m0 + g < a.rows, rv1 = m0 + g + 8 < a.rows;
-#pragma unroll
-  for (int i = 0; i < kBPerWarp; ++i) {
-    const int nt = nt_begin + warp + i * kSplitWarps;
-    if (nt >= nt_end) break;
-    if (writer) {
-      uint32_t *w = reinterpret_cast<uint32_t *>(p.b16);
-      const int n = nt * 8 + g;
-      w[((int64_t)n * kRank + 2 * t) / 2] = bf[i][0];
-      w[((int64_t)n * kRank + 2 * t + 8) / 2] = bf[i][1];
-    }
-    float o[4] = {0.f, 0.f, 0.f, 0.f};
-    mma_16816(o, ha0, ha1, ha2, ha3, bf[i][0], bf[i][1]);
-    const int col = nt * 8 + 2 * t;
-    // the GEMM's fp16 output, then * scaling, rounded to fp16 again
-    if (rv0) {
-      const float2 v = unpack_half2(pack_half2(o[0], o[1]));
-      reinterpret_cast<uint32_t *>(p.out)[((m0 + g) * HO + col) / 2] =
-          pack_half2(v.x * p.scale, v.y * p.scale);
-    }
-    if (rv1) {
-      const float2 v = unpack_half2(pack_half2(o[2], o[3]));
-      reinterpret_cast<uint32_t *>(p.out)[((m0 + g + 8) * HO + col) / 2] =
-          pack_half2(v.x * p.scale, v.y * p.scale);
-    }
-  }
-  if (slice != 0) return;
-  // x16 of the tile's real rows, 8 values per 16-byte store
-  const int per_row8 = H / 8;
-  for (int e = threadIdx.x; e < kSplitRows * per_row8; e += blockDim.x) {
-    const int r = e / per_row8, c8 = e - r * per_row8;
-    if (m0 + r >= a.rows) continue;
-    const float *src = xs + (size_t)r * ld + 8 * c8;
-    const float4 u = *reinterpret_cast<const float4 *>(src);
-    const float4 v = *reinterpret_cast<const float4 *>(src + 4);
-    *reinterpret_cast<uint4 *>(p.x16 + (m0 + r) * H + 8 * c8) =
-        make_uint4(pack_half2(u.x, u.y), pack_half2(u.z, u.w), pack_half2(v.x, v.y),
-                   pack_half2(v.z, v.w));
-  }
-  if (writer) {  // fp16(A)
-    uint32_t *w = reinterpret_cast<uint32_t *>(p.a16);
-    for (int e = threadIdx.x; e < kRank * H / 2; e += blockDim.x)
-      w[e] = ld_f16x2(p.a + 2 * (int64_t)e);
-  }
-}
-
 unsigned grid_for(int64_t n) {
   int64_t blocks = (n + kThreads - 1) / kThreads;
   const int64_t cap = (int64_t)sm_count() * 8;
@@ -826,49 +648,10 @@ extern "C" int tb_lora_forward(const float *dropped_q, const float *a_q, const f
   args.pos_idx = pos_idx;
   args.rows = rows;
   args.hidden = (int)hidden;
-  // the cluster-free kernel where its x tile fits in shared memory and the buffers take its
-  // 16-byte copies and stores; else (or when tb_lora_forward_variant says so) the cluster kernel
-  bool split_ok = split_smem_bytes((int)hidden) <= kSplitMaxSmem;
-  for (int i = 0; i < 2; ++i)
-    if (aa[i] != nullptr && rows > 0)
-      split_ok = split_ok && aligned(dr[i], 16) && aligned(xx[i], 16);
-  const int variant = g_lora_fwd_variant.load(std::memory_order_relaxed);
-  if (variant == 2 && !split_ok)
-    return set_error(TB_EINVAL, "lora_forward: the cluster-free kernel does not take these "
-                                "buffers (hidden %lld, 16-byte alignment)", (long long)hidden);
-  if (split_ok && variant != 1) {
-    static std::atomic<int> smem_set{0};
-    if (smem_set.load(std::memory_order_acquire) == 0) {
-      if (cudaFuncSetAttribute(lora_fwd_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)kSplitMaxSmem) != cudaSuccess) {
-        (void)cudaGetLastError();
-        return set_error(TB_ELAUNCH, "lora_forward: shared memory attribute refused");
-      }
-      smem_set.store(1, std::memory_order_release);
-    }
-    // one CTA per 16 rows, adapter and slice of kSliceTiles output tiles (tile 0 also writes
-    // the fp16 weights, so at least one)
-    const int64_t tiles = rows > 0 ? (rows + kSplitRows - 1) / kSplitRows : 1;
-    auto slices = [](int64_t hout) { return (int)((hout / 8 + kSliceTiles - 1) / kSliceTiles); };
-    const int sq = a_q ? slices(hout_q) : 0, sv = a_v ? slices(hout_v) : 0;
-    if (tiles > 0x7fffffffLL || sq + sv > 65535)
-      return set_error(TB_EINVAL, "lora_forward: too many rows or outputs");
-    if (sq + sv == 0) return TB_OK;
-    return launch("lora_forward", lora_fwd_split_kernel, dim3((unsigned)tiles, (unsigned)(sq + sv)),
-                  kSplitWarps * 32, split_smem_bytes((int)hidden), as_stream(stream), args, sq);
-  }
   // one cluster of kCluster CTAs per kTileRows rows and adapter (tile 0 also writes the fp16
   // weights, so at least one)
   const int64_t tiles = rows > 0 ? (rows + kTileRows - 1) / kTileRows : 1;
   if (tiles * kCluster > 0x7fffffffLL) return set_error(TB_EINVAL, "lora_forward: too many rows");
   return launch("lora_forward", lora_fwd_kernel, dim3((unsigned)(tiles * kCluster), 2),
                 kFwdWarps * 32, 0, as_stream(stream), args);
-}
-
-extern "C" int tb_lora_forward_variant(int32_t variant) {
-  if (variant < 0 || variant > 2)
-    return set_error(TB_EINVAL, "lora_forward_variant: %d (0 auto, 1 cluster, 2 cluster-free)",
-                     variant);
-  g_lora_fwd_variant.store(variant, std::memory_order_relaxed);
-  return TB_OK;
 }

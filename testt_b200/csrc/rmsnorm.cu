@@ -337,7 +337,8 @@ __global__ void __maxnreg__((rms_lora_regs<NCH, R>()))
 // loop over rows blockIdx.x, + gridDim.x, ... (about 4 rows per CTA at 621 rows, one CTA per
 // SM). A row's inputs (dy, s, ds, both masks, each thread its own 4 columns; the two dh rows and
 // rstd) are copied by cp.async into a ring of kRowStages shared-memory stages, kRowStages - 1
-// rows ahead of the row being computed; the slot each mask row needs is loaded one copy ahead.
+// rows ahead of the row being computed; the slots of the first kRowStages rows are loaded side
+// by side, and each later row's slot one loop iteration before its copies are issued.
 // Every value is rmsnorm_bwd_lora_vec's: the expansion's fmaf chains per column (fma.rn.f32x2
 // rounds each lane as fmaf), and the row sum in the plain kernel's order: lane 2i + 1 continues
 // lane 2i's FMA chain over the chunk's first 4 columns, the chunk sums go through shared memory,
@@ -409,15 +410,19 @@ __global__ void __launch_bounds__(2 * kRowsMaxChunks, 1)
     cp_async_commit();
   };
 
+  // the slots of the first kRowStages rows, loaded side by side; the first kRowStages - 1 rows'
+  // copies; after that, each row's slot is loaded one loop iteration before its copies
   const int64_t r0 = blockIdx.x;
-  int64_t slot_next = r0 < a.rows ? __ldg(a.pad_idx + r0) : 0;
-  auto issue_ahead = [&](int64_t row, int stage) {  // row's copies; the next row's slot load
-    const int64_t slot = slot_next;
-    slot_next = row + stride < a.rows ? __ldg(a.pad_idx + row + stride) : 0;
-    issue(row, slot, stage);
-  };
+  int64_t slot_ahead;
+  {
+    int64_t sl[kRowStages];
 #pragma unroll
-  for (int k = 0; k < kRowStages - 1; ++k) issue_ahead(r0 + k * stride, k);
+    for (int k = 0; k < kRowStages; ++k)
+      sl[k] = r0 + k * stride < a.rows ? __ldg(a.pad_idx + r0 + k * stride) : 0;
+#pragma unroll
+    for (int k = 0; k < kRowStages - 1; ++k) issue(r0 + k * stride, sl[k], k);
+    slot_ahead = sl[kRowStages - 1];
+  }
 
   // this thread's 4 columns of both fp16(A), as fp32, for every row
   float2 af[2][16][2];
@@ -434,7 +439,11 @@ __global__ void __launch_bounds__(2 * kRowsMaxChunks, 1)
 
   int stage = 0;
   for (int64_t row = r0; row < a.rows; row += stride) {
-    issue_ahead(row + (kRowStages - 1) * stride, stage == 0 ? kRowStages - 1 : stage - 1);
+    {
+      const int64_t ahead = row + (kRowStages - 1) * stride;
+      issue(ahead, slot_ahead, stage == 0 ? kRowStages - 1 : stage - 1);
+      slot_ahead = ahead + stride < a.rows ? __ldg(a.pad_idx + ahead + stride) : 0;
+    }
     cp_async_wait<kRowStages - 1>();  // this thread's copies of `row`
     __syncthreads();                  // and the dh rows and rstd other threads copied
     const uint8_t *st = ring + (size_t)stage * stage_bytes;
