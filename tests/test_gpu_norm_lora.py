@@ -168,3 +168,79 @@ def test_against_the_formula_in_torch():
     # matmul may round a few of them to the neighbouring fp16 value (about 5e-6 here)
     torch.testing.assert_close(got, ref, rtol=1e-4, atol=3e-5)
     torch.testing.assert_close(got16.float(), ref.half().float(), rtol=1e-3, atol=3e-5)
+
+
+@pytest.mark.parametrize("in_bucket", [False, True], ids=["returned_grads", "grad_bucket"])
+def test_linked_norm_and_lora_pair_match_unlinked(in_bucket):
+    """add_rmsnorm -> lora_pair through autograd with a LoraGradLink (the norm's backward forms
+    the padded input's gradient; the LoRA node returns none) against the same chain without it
+    (tb_lora_dropout_grad_expand, then tb_add_rmsnorm_bwd): the residual input's and delta's
+    gradients and the adapters' weight gradients, returned to autograd or accumulated into
+    GradBucket views, bit for bit, with the same dropout draws."""
+    from testt_b200 import _lib, lora
+    from testt_b200.dist import GradBucket
+    from testt_b200.rmsnorm import LoraGradLink, add_rmsnorm
+    from testt_b200.rope import slot_index
+
+    batch, seq, hidden, r = 3, 48, 512, 16
+    lengths = [40, 9, 48]
+    pos = torch.cat([torch.arange(n) + i * seq for i, n in enumerate(lengths)]).to(DEV)
+    slot = slot_index(pos, batch * seq)
+    m = pos.numel()
+    gen = torch.Generator().manual_seed(21)
+    x0 = torch.randn(m, hidden, generator=gen).to(DEV)
+    d0 = (torch.randn(m, hidden, generator=gen) * 0.5).half().to(DEV)
+    w = (torch.randn(hidden, generator=gen) * 0.1 + 1.0).to(DEV)
+    gs = (torch.randn(m, hidden, generator=gen) * 0.01).to(DEV)
+    gy = (torch.randn(m, hidden, generator=gen) * 0.01).half().to(DEV)
+    gq = (torch.randn(m, hidden, generator=gen) * 0.1).half().to(DEV)
+    gv = (torch.randn(m, 128, generator=gen) * 0.1).half().to(DEV)
+
+    def run(linked):
+        g = torch.Generator().manual_seed(3)
+        parts = []
+        for out, scaling in ((hidden, 2.0), (128, 0.5)):
+            a = torch.nn.Linear(hidden, r, bias=False).cuda()
+            b = torch.nn.Linear(r, out, bias=False).cuda()
+            with torch.no_grad():
+                a.weight.copy_(torch.randn(r, hidden, generator=g) * 0.05)
+                b.weight.copy_(torch.randn(out, r, generator=g) * 0.05)
+            parts.append((torch.nn.Dropout(0.1), a, b, scaling))
+        params = [t.weight for _, a, b, _ in parts for t in (a, b)]
+        if in_bucket:
+            GradBucket(params)
+        names = []
+        original = _lib.call
+
+        def recorded(name, *args):
+            names.append(name)
+            return original(name, *args)
+
+        _lib.call = recorded
+        try:
+            torch.manual_seed(17)
+            x = x0.clone().requires_grad_(True)
+            d = d0.clone().requires_grad_(True)
+            link = LoraGradLink() if linked else None
+            with torch.autocast("cuda", dtype=torch.float16):
+                s, y, y_pad = add_rmsnorm(x, d, w, 1e-6, pos, batch * seq, zero_padding=False,
+                                          link=link)
+                lq, lv = lora.lora_pair(parts[0], parts[1], y_pad, pos, slot, link)
+            torch.autograd.backward([s, y, lq, lv], [gs, gy, gq, gv])
+            torch.cuda.synchronize()
+        finally:
+            _lib.call = original
+        if linked:
+            assert "tb_add_rmsnorm_bwd_lora" in names
+            assert "tb_lora_dropout_grad_expand" not in names
+            assert link.factors is None  # taken by the norm's backward
+        else:
+            assert "tb_add_rmsnorm_bwd_lora" not in names
+        return x.grad.clone(), d.grad.clone(), [p.grad.clone() for p in params]
+
+    gx_ref, gd_ref, gw_ref = run(False)
+    gx, gd, gw = run(True)
+    assert torch.equal(gx, gx_ref)
+    assert torch.equal(gd, gd_ref)
+    for got, ref in zip(gw, gw_ref):
+        assert torch.equal(got, ref)
