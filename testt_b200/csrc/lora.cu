@@ -460,11 +460,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kFwdWarps * 3
     hv = pack_half2(h0, h1);
     h_sh[hrow][hpr] = hv;
   }
-  // this CTA is done reading the others' sums: arrive now, and wait only before exiting (no CTA
-  // may leave while another still reads its shared memory), so lora_B and the stores run while
-  // the slower CTAs of the cluster finish their reads
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-  __syncthreads();  // h_sh complete
+  cluster_sync();  // no CTA leaves while another reads its sums; h_sh complete
 
   // lora_B: A operand = h16 (two 16 x 16 m-tiles), one 16 x 8 output tile per mma
   uint32_t ha[2][4];
@@ -526,7 +522,6 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kFwdWarps * 3
       w[((int64_t)row * H + k) / 2] = ld_f16x2(p.a + (int64_t)row * H + k);
     }
   }
-  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every CTA's reads are done
 }
 
 unsigned grid_for(int64_t n) {
