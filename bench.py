@@ -831,16 +831,20 @@ def _kernel_case(name, device):
         nbytes = 0
         info = {"config": "5 (one layer)", "lengths": lengths, "heads": [12, 2], "head_dim": 128,
                 "flops": fwd if name != "attn_fwd_bwd" else int(3.5 * fwd)}
-    elif name == "head_tc":
+    elif name in ("head_tc", "head_tc_keep"):
+        # config 4's logits GEMM with the statistics epilogue; head_tc_keep also stores the
+        # fp16 logits of the labelled rows, as the head does for its dh pass
         c = synth.config4(dev)
         rows, hidden, vocab = 2048, synth.HIDDEN, synth.VOCAB
         vt = -(-vocab // 256)
         part = torch.empty((rows, vt, 6), device=dev)
         pidx = torch.empty((rows, vt), dtype=torch.int64, device=dev)
+        keep = c["n_labelled"] if name == "head_tc_keep" else 0
+        kept = torch.empty((keep, vocab), dtype=torch.float16, device=dev) if keep else None
         fn = lambda: _lib.call(  # noqa: E731
             "tb_head_logits_stats", _lib.ptr(c["hidden"]), _lib.ptr(c["weight"]),
-            _lib.ptr(c["targets"]), None, 0, _lib.ptr(part), _lib.ptr(pidx), rows, vocab, hidden,
-            _lib.stream_of(part))
+            _lib.ptr(c["targets"]), _lib.ptr(kept), keep, _lib.ptr(part), _lib.ptr(pidx), rows,
+            vocab, hidden, _lib.stream_of(part))
         nbytes = 0
         info = {"config": "4", "rows": rows, "flops": 2 * rows * hidden * vocab}
     elif name == "head_full":  # fused_head_loss of config 4: statistics, dlogits and dh
@@ -1317,7 +1321,7 @@ def main():
                          "rmsnorm_fwd, rmsnorm_bwd, rope_fwd, rope_bwd, swiglu_fwd, swiglu_bwd, "
                          "lora_fwd, norm_lora_bwd, norm_lora_bwd_two, attn_fwd, attn_fwd_tc, "
                          "attn_fwd_bwd, "
-                         "head_stats, head_tc, head_full, head_cublas, head_dh, "
+                         "head_stats, head_tc, head_tc_keep, head_full, head_cublas, head_dh, "
                          "head_dh_cublas, all; the NF4-decoding GEMMs, "
                          "with what they replace: gate_up_fused_fwd, gate_up_fused_bwd, "
                          "gate_up_unpack_fwd, gate_up_unpack_bwd, mlp_fused_fwd, mlp_unpack_fwd, "

@@ -115,6 +115,28 @@ def test_tc_head_first_argmax_ties(variant):
     assert_rel(loss, rloss, 1e-4, "loss")
 
 
+@pytest.mark.parametrize("rows,logits_rows", [(300, 77), (129, 33), (256, 31)])
+def test_tc_head_keeps_only_the_asked_rows(rows, logits_rows, variant):
+    """The kept logits go through a per-warp staging tile and leave as 8-row stores: the first
+    logits_rows rows (not a multiple of 32 here, so a warp's 32 rows straddle the end) are the
+    GEMM's fp16 output, and the rows after them in the buffer keep what was there."""
+    from testt_b200 import _lib
+
+    vocab, hidden = 1000, 128
+    h, w, tg = _case(rows, vocab, hidden, rows * 7 + logits_rows)
+    vt = -(-vocab // 256)
+    part = torch.empty((rows, vt, 6), dtype=torch.float32, device=DEV)
+    idx = torch.empty((rows, vt), dtype=torch.int64, device=DEV)
+    sentinel = torch.full((rows, vocab), 1234.0, dtype=torch.float16, device=DEV)
+    buf = sentinel.clone()
+    _lib.call("tb_head_logits_stats", _lib.ptr(h), _lib.ptr(w), _lib.ptr(tg), _lib.ptr(buf),
+              logits_rows, _lib.ptr(part), _lib.ptr(idx), rows, vocab, hidden, _lib.stream_of(h))
+    torch.cuda.synchronize()
+    assert _lib.wait_timeouts() == 0
+    assert_logits(buf[:logits_rows], (h[:logits_rows].float() @ w.float().t()).half())
+    assert torch.equal(buf[logits_rows:], sentinel[logits_rows:])
+
+
 def test_tc_head_config4_against_reference_path(variant):
     """Config 4 (2048 rows, vocab 151936, hidden 1536): the fused statistics against cuBLAS
     logits + tb_head_stats_grad, on the same inputs."""

@@ -37,8 +37,13 @@ constexpr int kPartFields = 6;
 // M=128, N=256, A=B=f16 (K-major), D=f32: the kind::f16 instruction descriptor
 constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
 
+// Each epilogue warp's staging tile for the kept logits: 32 rows of 32 fp16 values in 80-byte
+// rows (the 8 rows a quarter-warp touches at once fall in distinct 16-byte bank groups).
+constexpr int kOutLd = 40;  // halves per staged row
+
 struct Smem {
   alignas(1024) uint8_t stage[kStages][kStageBytes];  // A then B per stage (1024-aligned atoms)
+  alignas(16) uint16_t out_stage[4][32 * kOutLd];
   uint64_t full[kStages], empty[kStages];
   uint64_t acc_full[2], acc_empty[2];
   uint64_t mma_done;
@@ -192,13 +197,20 @@ struct HeadArgs {
 // The epilogue of one tile for one row (one thread): reads the row's 256 fp32 accumulator
 // columns from TMEM (taddr: this warp's lane quarter and the accumulator), rounds them to fp16
 // as the reference's fp16 GEMM output, optionally stores them (kept rows) and returns the
-// tile's state. Every thread of the warp calls it (tcgen05.ld is warp-wide).
+// tile's state. Every thread of the warp calls it (tcgen05.ld is warp-wide). The kept logits of
+// a 32-column chunk go through the warp's staging tile `buf`: each lane writes its row there,
+// then every store instruction writes 8 rows x 64 contiguous bytes (one lane a row would make
+// each 16-byte store land in 32 different rows: 806 against 661 us for config 4's head GEMM
+// with and without the kept logits).
 __device__ __forceinline__ RowTile tile_rows(const HeadArgs &args, uint32_t taddr, int row,
-                                             bool live, int64_t target, int col0) {
+                                             bool live, int64_t target, int col0,
+                                             uint16_t *buf) {
   RowTile st{-CUDART_INF_F, 0.f, 0.f, 0.f, -CUDART_INF_F, -1, false, false};
   const int64_t dt = target - col0;
   const int t_off = (dt >= 0 && dt < kBN) ? (int)dt : -1024;
   const bool keep = live && args.logits != nullptr && row < args.logits_rows;
+  const bool warp_keeps = __any_sync(0xffffffffu, keep);
+  const int lane = threadIdx.x & 31, row0 = row - lane;
 #pragma unroll 1
   for (int c = 0; c < kBN; c += 32) {
     const int nvalid = min(32, args.vocab - (col0 + c));
@@ -211,18 +223,26 @@ __device__ __forceinline__ RowTile tile_rows(const HeadArgs &args, uint32_t tadd
       const __half2 hh = __floats2half2_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
       h[j] = *reinterpret_cast<const uint32_t *>(&hh);
     }
-    if (keep) {
-      uint16_t *dst = args.logits + (int64_t)row * args.vocab + col0 + c;
-      if (nvalid == 32 && (args.vocab & 7) == 0) {
-        uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+    if (warp_keeps && nvalid == 32 && (args.vocab & 7) == 0) {  // warp-uniform
+      uint4 *mine = reinterpret_cast<uint4 *>(buf + lane * kOutLd);
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          d4[q] = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
-      } else {
+      for (int q = 0; q < 4; ++q)
+        mine[q] = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+      __syncwarp();
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < nvalid) dst[i] = (uint16_t)(h[i / 2] >> (16 * (i & 1)));
+      for (int it = 0; it < 4; ++it) {  // rows it*8 + (lane % 8), 16-byte part lane / 8
+        const int r = it * 8 + (lane & 7), part = lane >> 3;
+        const uint4 v = *reinterpret_cast<const uint4 *>(buf + r * kOutLd + part * 8);
+        if (row0 + r < args.logits_rows)
+          *reinterpret_cast<uint4 *>(args.logits + (int64_t)(row0 + r) * args.vocab + col0 + c +
+                                     part * 8) = v;
       }
+      __syncwarp();  // the tile is rewritten by the next chunk
+    } else if (keep) {
+      uint16_t *dst = args.logits + (int64_t)row * args.vocab + col0 + c;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < nvalid) dst[i] = (uint16_t)(h[i / 2] >> (16 * (i & 1)));
     }
     if (nvalid == 32)
       fold_chunk<true>(st, h, c, 32, t_off);
@@ -375,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t target = live ? __ldg(args.targets + row) : -1;
       const int col0 = vt * kBN;
       const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kBN);
-      const RowTile st = tile_rows(args, taddr, row, live, target, col0);
+      const RowTile st = tile_rows(args, taddr, row, live, target, col0, sm.out_stage[quarter]);
       // the accumulator may be overwritten once every epilogue warp has read it
       tc_fence_before();
       __syncwarp();
@@ -413,6 +433,7 @@ constexpr uint32_t kIdesc2 =
 
 struct Smem2 {
   alignas(1024) uint8_t stage[kStages2][kStage2Bytes];
+  alignas(16) uint16_t out_stage[4][32 * kOutLd];
   uint64_t full[kStages2], empty[kStages2];
   uint64_t acc_full[2], acc_empty[2];
   uint64_t mma_done;
@@ -594,7 +615,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int64_t target = live ? __ldg(args.targets + row) : -1;
       const int col0 = vt * kBN;
       const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kBN);
-      const RowTile st = tile_rows(args, taddr, row, live, target, col0);
+      const RowTile st = tile_rows(args, taddr, row, live, target, col0, sm.out_stage[quarter]);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_leader(&sm.acc_empty[acc]);
