@@ -427,6 +427,23 @@ int tb_head_merge(const float *part, const int64_t *part_idx, const int64_t *tar
                   int64_t rows, int32_t n_groups, int32_t splits, float *lse, float *entropy,
                   float *loss, int32_t *correct, void *stream);
 
+/* The head's labelled-first row order (the gather of labelled rows in solution/head.py:87-156,
+ * as a stable partition): order[i] is the row at sorted place i, labelled rows (target !=
+ * ignore_index) first, each group in row order; targets_sorted[i] = targets[order[i]]. One
+ * launch (one CTA), no host synchronisation. */
+int tb_head_order(const int64_t *targets, int64_t rows, int64_t ignore_index, int64_t *order,
+                  int64_t *targets_sorted, void *stream);
+
+/* Back to row order after the head: grad[order[i]] = dh_sorted[i] for i < keep and 0 for the
+ * other rows (fp16 [rows, width], width a multiple of 8, 16-byte aligned; grad NULL: statistics
+ * only), entropy[order[i]] = entropy_sorted[i], loss likewise, correct[order[i]] =
+ * (correct_sorted[i] != 0) as bytes. Replaces the zero fill + index_copy of the gradient and the
+ * inverse permutation + gathers of the statistics (solution/head.py:113-156). */
+int tb_head_unsort(const int64_t *order, int64_t rows, int64_t keep, const uint16_t *dh_sorted,
+                   int64_t width, uint16_t *grad, const float *entropy_sorted,
+                   const float *loss_sorted, const int32_t *correct_sorted, float *entropy,
+                   float *loss, uint8_t *correct, void *stream);
+
 /* Folds partial states: for each row, its splits_in states (part [rows, splits_in, 6],
  * part_idx [rows, splits_in], the layout tb_head_partials and tb_head_logits_stats write) are
  * merged in splits_out contiguous groups into part_out [rows, splits_out, 6] and idx_out

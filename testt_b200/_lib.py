@@ -53,6 +53,8 @@ SIGNATURES = {
     "tb_head_stats_grad": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P],
     "tb_head_partials": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _P],
     "tb_head_merge": [_P, _P, _P, _I64, _I32, _I32, _P, _P, _P, _P, _P],
+    "tb_head_order": [_P, _I64, _I64, _P, _P, _P],
+    "tb_head_unsort": [_P, _I64, _I64, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P],
     "tb_head_fold": [_P, _P, _I64, _I32, _I64, _I32, _P, _P, _P],
     "tb_head_dlogits": [_P, _P, _P, _I64, _I64, _I64, _I64, _F, _P],
     "tb_wait_timeouts": [_I32, _P],

@@ -93,17 +93,18 @@ def head_dh(logits, targets, lse, weight, out, grad_scale, col_offset=0, out_row
     return out
 
 
-def _tc_head(h, weight, tgt, entropy, token_loss, correct, grad, order, n_labelled, scale,
+def _tc_head(h, weight, tgt, entropy, token_loss, correct, want_grad, n_labelled, scale,
              stream):
     """All rows at once: tensor-core logits + partials, merge, then (labelled rows) the
-    gradient dh = dlogits . W into grad's unsorted rows."""
+    gradient dh = dlogits . W of the sorted labelled rows, returned fp16 [n_labelled, width]
+    (None when no gradient is wanted)."""
     rows, width = h.shape
     vocab = weight.shape[0]
     dev = h.device
     vt = -(-vocab // VOCAB_TILE)
     part = torch.empty((rows, vt, 6), dtype=torch.float32, device=dev)
     pidx = torch.empty((rows, vt), dtype=torch.int64, device=dev)
-    keep = n_labelled if grad is not None else 0
+    keep = n_labelled if want_grad else 0
     logits = torch.empty((keep, vocab), dtype=torch.float16, device=dev) if keep else None
     _lib.call("tb_head_logits_stats", _lib.ptr(h), _lib.ptr(weight), _lib.ptr(tgt),
               _lib.ptr(logits), keep, _lib.ptr(part), _lib.ptr(pidx), rows, vocab, width, stream)
@@ -111,13 +112,13 @@ def _tc_head(h, weight, tgt, entropy, token_loss, correct, grad, order, n_labell
     _lib.call("tb_head_merge", _lib.ptr(part), _lib.ptr(pidx), _lib.ptr(tgt), rows, 1, vt,
               _lib.ptr(lse), _lib.ptr(entropy), _lib.ptr(token_loss), _lib.ptr(correct), stream)
     if not keep:
-        return
+        return None
     if USE_TENSOR_CORE_DH and dh_supported(logits, weight):
-        head_dh(logits, tgt, lse, weight, grad, scale, out_rows=order[:keep])
-        return
+        dh = torch.empty((keep, width), dtype=torch.float16, device=dev)
+        return head_dh(logits, tgt, lse, weight, dh, scale)
     _lib.call("tb_head_dlogits", _lib.ptr(logits), _lib.ptr(tgt), _lib.ptr(lse), keep, vocab,
               vocab, 0, float(scale), stream)
-    grad.index_copy_(0, order[:keep], torch.matmul(logits, weight))
+    return torch.matmul(logits, weight)
 
 
 # True: dh = dlogits . W through tb_head_dh (dlogits formed inside the tensor-core GEMM, never
@@ -162,25 +163,28 @@ class FusedHeadLoss(torch.autograd.Function):
         rows, width = hidden.shape
         vocab = weight.shape[0]
         dev = hidden.device
-        labelled = targets != IGNORE_INDEX
-        order = torch.argsort((~labelled).to(torch.int8), stable=True)
         if counts is None:
-            n_labelled, denom = _host_counts(labelled, denominator, dev, targets, vocab)
+            n_labelled, denom = _host_counts(targets != IGNORE_INDEX, denominator, dev, targets,
+                                             vocab)
         else:  # known on the host already (a captured step): no synchronisation here
             n_labelled, denom = int(counts[0]), float(counts[1])
+        stream = _lib.stream_of(hidden)
+        # labelled rows first, each group in row order (tb_head_order: one launch)
+        order = torch.empty(rows, dtype=torch.int64, device=dev)
+        tgt = torch.empty(rows, dtype=torch.int64, device=dev)
+        targets64 = targets.to(torch.int64).contiguous()
+        _lib.call("tb_head_order", _lib.ptr(targets64), rows, IGNORE_INDEX, _lib.ptr(order),
+                  _lib.ptr(tgt), stream)
         h = hidden.index_select(0, order)
-        tgt = targets.index_select(0, order).to(torch.int64).contiguous()
         entropy = torch.empty(rows, dtype=torch.float32, device=dev)
         token_loss = torch.empty(rows, dtype=torch.float32, device=dev)
         correct = torch.empty(rows, dtype=torch.int32, device=dev)
         want_grad = ctx.needs_input_grad[0]
         unit = _grad_unit(denom)
-        grad = torch.zeros((rows, width), dtype=torch.float16, device=dev) if want_grad else None
         grad_sorted = None
-        stream = _lib.stream_of(hidden)
         if USE_TENSOR_CORE_HEAD and _tensor_core_ok(h, weight):
-            _tc_head(h, weight, tgt, entropy, token_loss, correct, grad, order, n_labelled,
-                     unit / max(denom, 1e-6), stream)
+            grad_sorted = _tc_head(h, weight, tgt, entropy, token_loss, correct, want_grad,
+                                   n_labelled, unit / max(denom, 1e-6), stream)
             rows_loop = range(0)
         else:
             rows_loop = range(0, rows, CHUNK_ROWS)
@@ -202,14 +206,31 @@ class FusedHeadLoss(torch.autograd.Function):
             loss = total / denominator.to(dev)
         else:
             loss = total / denominator
+        # back to row order (tb_head_unsort: the gradient rows, zeros for the unlabelled ones,
+        # and the statistics, one launch)
+        keep = n_labelled if want_grad else 0
+        grad = torch.empty((rows, width), dtype=torch.float16, device=dev) if want_grad else None
+        stats = (torch.empty(rows, dtype=torch.float32, device=dev),
+                 torch.empty(rows, dtype=torch.float32, device=dev),
+                 torch.empty(rows, dtype=torch.bool, device=dev))
+        dh = None
+        if keep:
+            dh = grad_sorted.contiguous()
+            if dh.data_ptr() % 16:
+                dh = dh.clone()
+        grad_arg = grad
+        if grad is not None and width % 8:  # rows the 16-byte kernel cannot take
+            grad.zero_()
+            if keep:
+                grad.index_copy_(0, order[:keep], dh)
+            grad_arg = None
+        _lib.call("tb_head_unsort", _lib.ptr(order), rows, keep if grad_arg is not None else 0,
+                  _lib.ptr(dh if grad_arg is not None else None), width, _lib.ptr(grad_arg),
+                  _lib.ptr(entropy), _lib.ptr(token_loss), _lib.ptr(correct),
+                  _lib.ptr(stats[0]), _lib.ptr(stats[1]), _lib.ptr(stats[2]), stream)
         if want_grad:
-            if grad_sorted is not None:
-                grad.index_copy_(0, order[:n_labelled], grad_sorted)
             ctx.save_for_backward(grad)
         ctx.unit = unit
-        unsort = torch.empty_like(order)
-        unsort[order] = torch.arange(rows, device=dev)
-        stats = (entropy[unsort], token_loss[unsort], correct[unsort].bool())
         ctx.mark_non_differentiable(*stats)
         return (loss, *stats)
 
