@@ -328,7 +328,9 @@ class HotPath:
 
     def __init__(self, model, lengths, seq, device):
         from testt_b200 import _lib, nf4
-        from testt_b200.model import FUSE_NORM_LORA_BWD, USE_ROPE_IN_ATTENTION_BWD, model_plan
+        from testt_b200.mlp import SPLIT_PARTS
+        from testt_b200.model import (FUSE_MLP_SPLITK_BWD, FUSE_NORM_LORA_BWD,
+                                      USE_ROPE_IN_ATTENTION_BWD, model_plan)
         from testt_b200.model import USE_VARLEN_ATTENTION as varlen
 
         self.lib = _lib
@@ -353,11 +355,14 @@ class HotPath:
         rope_in_attention = bool(varlen and USE_ROPE_IN_ATTENTION_BWD)
         # the input norms' backward forms the LoRA pair's input gradient itself
         # (tb_add_rmsnorm_bwd_lora) when the step links them (model.FUSE_NORM_LORA_BWD)
+        # and the post-attention norms' backward sums the MLP's K-split gradient partials
+        # (tb_add_rmsnorm_bwd_parts) when the step links those (model.FUSE_MLP_SPLITK_BWD)
         self.groups = {k: [] for k in ("nf4_unpack", "rmsnorm_fwd", "rmsnorm_bwd",
-                                       "rmsnorm_bwd_lora", "rope_fwd", "rope_bwd", "swiglu_fwd",
-                                       "swiglu_bwd")
+                                       "rmsnorm_bwd_lora", "rmsnorm_bwd_parts", "rope_fwd",
+                                       "rope_bwd", "swiglu_fwd", "swiglu_bwd")
                        if not (k == "rope_bwd" and rope_in_attention)
-                       and not (k == "rmsnorm_bwd_lora" and not FUSE_NORM_LORA_BWD)}
+                       and not (k == "rmsnorm_bwd_lora" and not FUSE_NORM_LORA_BWD)
+                       and not (k == "rmsnorm_bwd_parts" and not FUSE_MLP_SPLITK_BWD)}
         self.bytes = {k: 0 for k in self.groups}
         self.keep = []
         cos, sin = (t.to(dev) for t in synth._rope(seq, dev))
@@ -469,9 +474,17 @@ class HotPath:
             add("rmsnorm_fwd", e * 12 + 4 * h + 4 * m, "tb_add_rmsnorm_fwd", _lib.ptr(x2),
                 _lib.ptr(d2), _lib.ptr(w_norm), _lib.ptr(s2), _lib.ptr(y2), None, None,
                 _lib.ptr(r2), m, h, 1e-6)
-            add("rmsnorm_bwd", e * 16 + 4 * h + 4 * m, "tb_add_rmsnorm_bwd", _lib.ptr(s2),
-                _lib.ptr(r2), _lib.ptr(w_norm), _lib.ptr(dy2), None, None, _lib.ptr(ds2),
-                _lib.ptr(dx2), _lib.ptr(dd2), m, h)
+            if FUSE_MLP_SPLITK_BWD:
+                parts = rnd((SPLIT_PARTS, m, h), f32, 1e-2)
+                self.keep.append(parts)
+                add("rmsnorm_bwd_parts", e * (4 + 4 * SPLIT_PARTS + 4 + 4 + 2) + 4 * h + 4 * m,
+                    "tb_add_rmsnorm_bwd_parts", _lib.ptr(s2), _lib.ptr(r2), _lib.ptr(w_norm),
+                    _lib.ptr(parts), SPLIT_PARTS, m * h, _lib.ptr(ds2), _lib.ptr(dx2),
+                    _lib.ptr(dd2), m, h)
+            else:
+                add("rmsnorm_bwd", e * 16 + 4 * h + 4 * m, "tb_add_rmsnorm_bwd", _lib.ptr(s2),
+                    _lib.ptr(r2), _lib.ptr(w_norm), _lib.ptr(dy2), None, None, _lib.ptr(ds2),
+                    _lib.ptr(dx2), _lib.ptr(dd2), m, h)
             # QKV pack + RoPE (LoRA outputs fp16, as under autocast), token-major as the step
             # runs it (model.USE_VARLEN_ATTENTION), else into the padded layout
             qkv = rnd((m, width), f16)

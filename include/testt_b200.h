@@ -180,6 +180,16 @@ int tb_add_rmsnorm_bwd(const float *s, const float *rstd, const float *weight, c
                        const float *dypad, const int64_t *pad_idx, const float *ds, float *dx,
                        uint16_t *ddelta, int64_t rows, int64_t hidden, void *stream);
 
+/* The same backward (no padded gradient) with dy given as the fp32 K-split partial products of
+ * the GEMM that produces it (the MLP's gate|up backward, K = 2 x intermediate, as one batched
+ * GEMM): n_parts arrays [rows, hidden] part_stride elements apart, summed in part order and
+ * rounded to fp16 once (the GEMM's fp16 output), so no split-K reduce launch runs. hidden a
+ * multiple of 8 and every buffer 16-byte aligned (TB_EINVAL / TB_EALIGN otherwise). */
+int tb_add_rmsnorm_bwd_parts(const float *s, const float *rstd, const float *weight,
+                             const float *dy_parts, int32_t n_parts, int64_t part_stride,
+                             const float *ds, float *dx, uint16_t *ddelta, int64_t rows,
+                             int64_t hidden, void *stream);
+
 /* The same backward with dypad formed in registers from the rank-16 LoRA pair the padded output
  * feeds (solution/model.py:195-206 under fp16 autocast: the dropout backward of lora_A's input
  * gradient), instead of read from a tensor tb_lora_dropout_grad_expand wrote: per row r, slot

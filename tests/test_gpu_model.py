@@ -255,3 +255,36 @@ def test_norm_backward_with_lora_dropout_backward_gives_the_same_step(request, f
     assert got[3] == pytest.approx(ref[3], rel=1e-6)
     assert got[4][1] == ref[4][1]
     assert got[4][0] == pytest.approx(ref[4][0], rel=1e-6)
+
+
+def test_mlp_gradient_as_partials_gives_the_same_step(lora_model_d128):
+    """The MLP's gate|up backward as one batched GEMM of fp32 K-split partials summed by the
+    post-attention norm's backward (model.FUSE_MLP_SPLITK_BWD, tb_add_rmsnorm_bwd_parts) against
+    one fp16 GEMM: the same loss (the forward is untouched) and the same gradients up to the
+    order of the fp32 sums behind one fp16 rounding."""
+    from testt_b200 import _lib, model
+
+    names = []
+    original = _lib.call
+
+    def recorded(name, *args):
+        names.append(name)
+        return original(name, *args)
+
+    saved = model.FUSE_MLP_SPLITK_BWD
+    _lib.call = recorded
+    try:
+        model.FUSE_MLP_SPLITK_BWD = False
+        ref = run(lora_model_d128, fused=True)
+        assert "tb_add_rmsnorm_bwd_parts" not in names
+        names.clear()
+        model.FUSE_MLP_SPLITK_BWD = True
+        got = run(lora_model_d128, fused=True)
+    finally:
+        _lib.call = original
+        model.FUSE_MLP_SPLITK_BWD = saved
+    assert names.count("tb_add_rmsnorm_bwd_parts") == lora_model_d128.config.num_hidden_layers
+    assert got[0] == ref[0]
+    for name, grad in ref[1].items():
+        rel = (got[1][name] - grad).norm() / grad.norm().clamp(min=1e-12)
+        assert rel < 2e-3, (name, float(rel))

@@ -244,3 +244,29 @@ def test_linked_norm_and_lora_pair_match_unlinked(in_bucket):
     assert torch.equal(gd, gd_ref)
     for got, ref in zip(gw, gw_ref):
         assert torch.equal(got, ref)
+
+
+@pytest.mark.parametrize("rows,hidden,parts", [(621, 1536, 4), (37, 1536, 4), (300, 2560, 3),
+                                               (5, 896, 1)])
+def test_partials_form_matches_the_plain_backward(rows, hidden, parts):
+    """tb_add_rmsnorm_bwd_parts (dy as fp32 K-split partials, summed in part order and rounded to
+    fp16 in the kernel) against tb_add_rmsnorm_bwd fed that fp16 sum: bit for bit."""
+    from testt_b200 import _lib
+
+    c = _case(rows, hidden, 0, "", False, seed=rows * parts)
+    g = torch.Generator().manual_seed(hidden)
+    p = (torch.randn(parts, rows, hidden, generator=g) * 0.01).to(DEV)
+    total = p[0].clone()
+    for i in range(1, parts):
+        total = total + p[i]
+    dy16 = total.half()
+    ref_dx, ref_dd = torch.empty_like(c["s"]), torch.empty(rows, hidden, dtype=torch.float16,
+                                                           device=DEV)
+    _lib.call("tb_add_rmsnorm_bwd", _ptr(c["s"]), _ptr(c["rstd"]), _ptr(c["w"]), _ptr(dy16),
+              None, None, _ptr(c["ds"]), _ptr(ref_dx), _ptr(ref_dd), rows, hidden, _stream())
+    dx, dd = torch.empty_like(ref_dx), torch.empty_like(ref_dd)
+    _lib.call("tb_add_rmsnorm_bwd_parts", _ptr(c["s"]), _ptr(c["rstd"]), _ptr(c["w"]), _ptr(p),
+              parts, rows * hidden, _ptr(c["ds"]), _ptr(dx), _ptr(dd), rows, hidden, _stream())
+    torch.cuda.synchronize()
+    assert torch.equal(dx, ref_dx)
+    assert torch.equal(dd, ref_dd)

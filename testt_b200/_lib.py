@@ -28,6 +28,7 @@ SIGNATURES = {
     "tb_nf4_unpack_multi": [_I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     "tb_add_rmsnorm_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _F, _P],
     "tb_add_rmsnorm_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _P],
+    "tb_add_rmsnorm_bwd_parts": [_P, _P, _P, _P, _I32, _I64, _P, _P, _P, _I64, _I64, _P],
     "tb_add_rmsnorm_bwd_lora": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _F, _P, _P, _P, _F, _P, _P,
                                 _I64, _I64, _I32, _P],
     "tb_rope_pack_fwd": [_P, _P, _P, _I32, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32,

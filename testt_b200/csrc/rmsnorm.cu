@@ -73,9 +73,13 @@ __global__ void rmsnorm_fwd_vec(const float *__restrict__ x, const uint16_t *__r
   if (threadIdx.x == 0) rstd_out[row] = rstd;
 }
 
+// dy is fp16 [rows, hidden], or (dyp non-NULL) the fp32 K-split partial products of the GEMM
+// that produces it, nparts of them pstride elements apart: summed in part order and rounded to
+// fp16 once, the GEMM's fp16 output (the split-K reduction folded into this kernel).
 template <int NCH>
 __global__ void rmsnorm_bwd_vec(const float *__restrict__ s, const float *__restrict__ rstd_in,
                                 const float *__restrict__ w, const uint16_t *__restrict__ dy,
+                                const float *__restrict__ dyp, int nparts, int64_t pstride,
                                 const float *__restrict__ dypad,
                                 const int64_t *__restrict__ pad_idx, const float *__restrict__ ds,
                                 float *__restrict__ dx, uint16_t *__restrict__ ddelta,
@@ -96,7 +100,17 @@ __global__ void rmsnorm_bwd_vec(const float *__restrict__ s, const float *__rest
     const int c = threadIdx.x + i * blockDim.x;
     if (c < nch) {
       float wv[8];
-      if (dy != nullptr) {
+      if (dyp != nullptr) {
+        load8f(dyp + base + c * 8, g[i]);
+        for (int p = 1; p < nparts; ++p) {
+          float q[8];
+          load8f(dyp + p * pstride + base + c * 8, q);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) g[i][k] = g[i][k] + q[k];
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) g[i][k] = __half2float(__float2half_rn(g[i][k]));
+      } else if (dy != nullptr) {
         load8h(dy + base + c * 8, g[i]);
       } else {
 #pragma unroll
@@ -689,33 +703,67 @@ extern "C" int tb_add_rmsnorm_fwd(const float *x, const uint16_t *delta, const f
   return rc;
 }
 
+namespace tb {
+namespace {
+
+// tb_add_rmsnorm_bwd with dy given either as fp16 or as nparts fp32 K-split partials
+int rmsnorm_bwd_launch(const char *what, const float *s, const float *rstd, const float *weight,
+                       const uint16_t *dy, const float *dyp, int nparts, int64_t pstride,
+                       const float *dypad, const int64_t *pad_idx, const float *ds, float *dx,
+                       uint16_t *ddelta, int64_t rows, int64_t hidden, void *stream) {
+  if (rows < 0 || hidden <= 0)
+    return set_error(TB_EINVAL, "%s: rows %lld hidden %lld", what, (long long)rows,
+                     (long long)hidden);
+  if (!s || !rstd || !weight || !dx)
+    return set_error(TB_EINVAL, "%s: s, rstd, weight and dx are required", what);
+  if (dypad && !pad_idx) return set_error(TB_EINVAL, "%s: dypad given without pad_idx", what);
+  if (rows == 0) return TB_OK;
+  if (rows > 0x7fffffffLL) return set_error(TB_EINVAL, "%s: too many rows", what);
+  const bool vec_ok = aligned(s, 16) && aligned(weight, 16) && aligned(dx, 16) &&
+                      (!dy || aligned(dy, 16)) && (!dyp || aligned(dyp, 16)) &&
+                      (!dypad || aligned(dypad, 16)) && (!ds || aligned(ds, 16)) &&
+                      (!ddelta || aligned(ddelta, 16));
+  int threads, nch;
+  plan_rows(hidden, rows, vec_ok, threads, nch);
+  if (dyp != nullptr && nch == 0)
+    return set_error(vec_ok ? TB_EINVAL : TB_EALIGN,
+                     "%s: the partial-sum form needs hidden a multiple of 8 and 16-byte aligned "
+                     "buffers", what);
+  cudaStream_t st = as_stream(stream);
+  const dim3 grid((unsigned)rows);
+  switch (nch) {
+    case 1: return launch(what, rmsnorm_bwd_vec<1>, grid, threads, 0, st, s, rstd, weight, dy, dyp, nparts, pstride, dypad, pad_idx, ds, dx, ddelta, hidden);
+    case 2: return launch(what, rmsnorm_bwd_vec<2>, grid, threads, 0, st, s, rstd, weight, dy, dyp, nparts, pstride, dypad, pad_idx, ds, dx, ddelta, hidden);
+    case 4: return launch(what, rmsnorm_bwd_vec<4>, grid, threads, 0, st, s, rstd, weight, dy, dyp, nparts, pstride, dypad, pad_idx, ds, dx, ddelta, hidden);
+    case 8: return launch(what, rmsnorm_bwd_vec<8>, grid, threads, 0, st, s, rstd, weight, dy, dyp, nparts, pstride, dypad, pad_idx, ds, dx, ddelta, hidden);
+    default: return launch(what, rmsnorm_bwd_any, grid, threads, 0, st, s, rstd, weight, dy, dypad, pad_idx, ds, dx, ddelta, hidden);
+  }
+}
+
+}  // namespace
+}  // namespace tb
+
 extern "C" int tb_add_rmsnorm_bwd(const float *s, const float *rstd, const float *weight,
                                   const uint16_t *dy, const float *dypad, const int64_t *pad_idx,
                                   const float *ds, float *dx, uint16_t *ddelta, int64_t rows,
                                   int64_t hidden, void *stream) {
-  if (rows < 0 || hidden <= 0) return set_error(TB_EINVAL, "add_rmsnorm_bwd: rows %lld hidden %lld",
-                                                (long long)rows, (long long)hidden);
-  if (!s || !rstd || !weight || !dx)
-    return set_error(TB_EINVAL, "add_rmsnorm_bwd: s, rstd, weight and dx are required");
-  if (dypad && !pad_idx) return set_error(TB_EINVAL, "add_rmsnorm_bwd: dypad given without pad_idx");
-  if (rows == 0) return TB_OK;
-  if (rows > 0x7fffffffLL) return set_error(TB_EINVAL, "add_rmsnorm_bwd: too many rows");
-  const bool vec_ok = aligned(s, 16) && aligned(weight, 16) && aligned(dx, 16) &&
-                      (!dy || aligned(dy, 16)) && (!dypad || aligned(dypad, 16)) &&
-                      (!ds || aligned(ds, 16)) && (!ddelta || aligned(ddelta, 16));
-  int threads, nch;
-  plan_rows(hidden, rows, vec_ok, threads, nch);
-  cudaStream_t st = as_stream(stream);
-  const dim3 grid((unsigned)rows);
-  int rc;
-  switch (nch) {
-    case 1: rc = launch("add_rmsnorm_bwd", rmsnorm_bwd_vec<1>, grid, threads, 0, st, s, rstd, weight, dy, dypad, pad_idx, ds, dx, ddelta, hidden); break;
-    case 2: rc = launch("add_rmsnorm_bwd", rmsnorm_bwd_vec<2>, grid, threads, 0, st, s, rstd, weight, dy, dypad, pad_idx, ds, dx, ddelta, hidden); break;
-    case 4: rc = launch("add_rmsnorm_bwd", rmsnorm_bwd_vec<4>, grid, threads, 0, st, s, rstd, weight, dy, dypad, pad_idx, ds, dx, ddelta, hidden); break;
-    case 8: rc = launch("add_rmsnorm_bwd", rmsnorm_bwd_vec<8>, grid, threads, 0, st, s, rstd, weight, dy, dypad, pad_idx, ds, dx, ddelta, hidden); break;
-    default: rc = launch("add_rmsnorm_bwd", rmsnorm_bwd_any, grid, threads, 0, st, s, rstd, weight, dy, dypad, pad_idx, ds, dx, ddelta, hidden); break;
-  }
-  return rc;
+  return rmsnorm_bwd_launch("add_rmsnorm_bwd", s, rstd, weight, dy, nullptr, 0, 0, dypad, pad_idx,
+                            ds, dx, ddelta, rows, hidden, stream);
+}
+
+extern "C" int tb_add_rmsnorm_bwd_parts(const float *s, const float *rstd, const float *weight,
+                                        const float *dy_parts, int32_t n_parts,
+                                        int64_t part_stride, const float *ds, float *dx,
+                                        uint16_t *ddelta, int64_t rows, int64_t hidden,
+                                        void *stream) {
+  if (!dy_parts || n_parts < 1 || n_parts > 64 || part_stride < rows * hidden)
+    return set_error(TB_EINVAL, "add_rmsnorm_bwd_parts: %d parts %lld elements apart", n_parts,
+                     (long long)part_stride);
+  if (part_stride % 4)
+    return set_error(TB_EALIGN, "add_rmsnorm_bwd_parts: part stride %lld not a multiple of 4",
+                     (long long)part_stride);
+  return rmsnorm_bwd_launch("add_rmsnorm_bwd_parts", s, rstd, weight, nullptr, dy_parts, n_parts,
+                            part_stride, nullptr, nullptr, ds, dx, ddelta, rows, hidden, stream);
 }
 
 extern "C" int tb_add_rmsnorm_bwd_lora(const float *s, const float *rstd, const float *weight,

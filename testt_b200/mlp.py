@@ -13,12 +13,19 @@ import torch
 
 from . import _lib
 from .nf4 import LayerWeights
+from .rmsnorm import split_link_ok
 
 # Save the fp16 gate|up GEMM output [tokens, 2*inter] for backward (22 MB per Qwen2.5-1.5B
 # layer at 621 tokens) instead of recomputing it there as the reference does to save memory:
 # on a 180 GB B200 the memory is free and the recompute is a third of the layer's MLP GEMMs.
 # True restores the reference's recompute.
 RECOMPUTE_GATE_UP = False
+
+# K-split parts of the gate|up backward GEMM when its input's norm is linked (rmsnorm.
+# SplitGradLink): one batched GEMM writing 4 fp32 partials took 34.8 us for config 5's
+# [621 x 17920] x [17920 x 1536], against 47.1 us for cuBLAS's split-K GEMM and its reduce launch
+# (2 parts: 41.0, 5: 38.9, 7: 38.9 us; one B200, CUDA graphs, L2 flushed)
+SPLIT_PARTS = 4
 
 
 def _check_gu(gu, what):
@@ -64,14 +71,14 @@ class LayerMLP(torch.autograd.Function):
     between the passes."""
 
     @staticmethod
-    def forward(ctx, x, lw, g_gu, g_down, own):
+    def forward(ctx, x, lw, g_gu, g_down, own, link=None):
         w = lw.operands(x.device)
         gu = torch.matmul(x, w[g_gu].t())
         act = gated_silu(gu)
         out = torch.matmul(act, w[g_down].t())
         # backward needs gu (the SwiGLU backward's operand); recomputing it is a third GEMM
         ctx.save_for_backward(x, None if RECOMPUTE_GATE_UP else gu)
-        ctx.lw, ctx.groups, ctx.own = lw, (g_gu, g_down), own
+        ctx.lw, ctx.groups, ctx.own, ctx.link = lw, (g_gu, g_down), own, link
         if own:
             lw.release()
         return out
@@ -79,7 +86,7 @@ class LayerMLP(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_out):
         if not ctx.needs_input_grad[0]:
-            return None, None, None, None, None
+            return None, None, None, None, None, None
         x, gu = ctx.saved_tensors
         g_gu, g_down = ctx.groups
         w = ctx.lw.operands(grad_out.device)
@@ -87,16 +94,31 @@ class LayerMLP(torch.autograd.Function):
             gu = torch.matmul(x, w[g_gu].t())
         # dact = dy . W_down, then [dgate | dup] in place of gu, then one GEMM back through both
         gated_silu_backward_(torch.matmul(grad_out.to(torch.float16), w[g_down]), gu)
-        grad_x = torch.matmul(gu, w[g_gu])
+        rows, k = gu.shape
+        hidden = w[g_gu].shape[1]
+        if ctx.link is not None and k % SPLIT_PARTS == 0 and (k // SPLIT_PARTS) % 8 == 0 \
+                and split_link_ok(hidden) and w[g_gu].is_contiguous():
+            # x's gradient as SPLIT_PARTS fp32 K-split products in one batched GEMM; the norm that
+            # produced x sums them in its backward (rmsnorm.SplitGradLink)
+            kp = k // SPLIT_PARTS
+            parts = torch.empty((SPLIT_PARTS, rows, hidden), dtype=torch.float32, device=gu.device)
+            torch.bmm(gu.view(rows, SPLIT_PARTS, kp).transpose(0, 1),
+                      w[g_gu].view(SPLIT_PARTS, kp, hidden), out_dtype=torch.float32, out=parts)
+            ctx.link.put(parts)
+            grad_x = None
+        else:
+            grad_x = torch.matmul(gu, w[g_gu])
         if ctx.own:
             ctx.lw.release()
-        return grad_x, None, None, None, None
+        return grad_x, None, None, None, None, None
 
 
-def layer_mlp(x, lw, g_gu, g_down):
-    """The MLP of a decoder layer on its LayerWeights' operands g_gu (gate|up) and g_down."""
+def layer_mlp(x, lw, g_gu, g_down, link=None):
+    """The MLP of a decoder layer on its LayerWeights' operands g_gu (gate|up) and g_down.
+    `link`: the rmsnorm.SplitGradLink given to the add_rmsnorm call that made x (x's only
+    consumer here), whose backward then sums x's gradient from K-split partials."""
     _lib.require_cuda(x, what="layer_mlp")
-    return LayerMLP.apply(x.contiguous(), lw, g_gu, g_down, False)
+    return LayerMLP.apply(x.contiguous(), lw, g_gu, g_down, False, link)
 
 
 def fused_mlp(x, gate_w, up_w, down_w):

@@ -40,7 +40,7 @@ from . import fused_layer as _fused_layer
 from .head import IGNORE_INDEX, fused_head_loss
 from .mlp import layer_mlp
 from .nf4 import LayerWeights, layer_linear
-from .rmsnorm import LoraGradLink, add_rmsnorm
+from .rmsnorm import LoraGradLink, SplitGradLink, add_rmsnorm
 from .lora import lora_pair
 from .rope import rope_pack, rope_tokens, slot_index
 
@@ -87,6 +87,12 @@ USE_NF4_GEMM = False
 # tb_lora_dropout_grad_expand wrote: one launch per layer fewer, same values. False keeps the
 # two launches.
 FUSE_NORM_LORA_BWD = True
+
+# True: each layer's post-attention norm and its MLP share a rmsnorm.SplitGradLink, so the MLP's
+# gate|up backward GEMM writes the norm output's gradient as fp32 K-split partials (one batched
+# GEMM, mlp.SPLIT_PARTS) and the norm's backward sums them (tb_add_rmsnorm_bwd_parts) instead of
+# cuBLAS's split-K GEMM followed by its reduce launch. False: one torch.matmul.
+FUSE_MLP_SPLITK_BWD = True
 
 _ALLOWED_KWARGS = {"num_items_in_batch", "output_attentions", "output_hidden_states",
                    "return_dict"}
@@ -405,9 +411,10 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
             attn = attn.reshape(padded, plan.n_heads * plan.head_dim).index_select(0, pos_idx)
         o = layer_linear(attn, lw, 1, lp.o_bias)
         del attn
+        link2 = SplitGradLink() if FUSE_MLP_SPLITK_BWD else None
         s, y2, _ = add_rmsnorm(s, o, layer.post_attention_layernorm.weight,
-                               layer.post_attention_layernorm.variance_epsilon)
-        delta = layer_mlp(y2, lw, 2, 3)
+                               layer.post_attention_layernorm.variance_epsilon, link=link2)
+        delta = layer_mlp(y2, lw, 2, 3, link2)
         if not KEEP_UNPACKED_WEIGHTS:
             lw.release()  # backward unpacks the layer again
         del y2, o

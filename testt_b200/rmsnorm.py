@@ -120,7 +120,56 @@ def _launch_bwd_lora(s, rstd, weight, pad_idx, grad_s, grad_y, factors, want_del
     return dx, ddelta
 
 
+class SplitGradLink:
+    """The hand-off between this norm's autograd node and the node that reads its fp16 output y
+    through a GEMM with a long reduction (the MLP's gate|up, K = 2 x intermediate): that node's
+    backward leaves y's gradient as fp32 K-split partial products [parts, rows, hidden] here and
+    returns none; the norm backward sums them in its own kernel (tb_add_rmsnorm_bwd_parts) in
+    place of cuBLAS's split-K reduce launch."""
+
+    __slots__ = ("parts",)
+
+    def __init__(self):
+        self.parts = None
+
+    def put(self, parts):
+        self.parts = parts
+
+    def take(self):
+        p, self.parts = self.parts, None
+        return p
+
+
+def split_link_ok(hidden):
+    """Whether tb_add_rmsnorm_bwd_parts takes this row width (a multiple of 8)."""
+    return hidden > 0 and hidden % 8 == 0
+
+
+def _launch_bwd_parts(s, rstd, weight, grad_s, parts, want_delta):
+    """_launch_bwd with dy as fp32 K-split partials [parts, rows, hidden]."""
+    rows, hidden = s.shape
+    weight = _f32(weight).contiguous()
+    dx = torch.empty_like(s)
+    ddelta = torch.empty((rows, hidden), dtype=torch.float16, device=s.device) \
+        if want_delta else None
+    ds = _aligned(_f32(grad_s)) if grad_s is not None else None
+    parts = _aligned(parts)
+    if rows:
+        _lib.call("tb_add_rmsnorm_bwd_parts", _lib.ptr(s), _lib.ptr(rstd), _lib.ptr(weight),
+                  _lib.ptr(parts), parts.shape[0], rows * hidden, _lib.ptr(ds), _lib.ptr(dx),
+                  _lib.ptr(ddelta), rows, hidden, _lib.stream_of(s))
+    return dx, ddelta
+
+
 def _backward(ctx, x_or_s, rstd, weight, pad_idx, grad_s, grad_y, grad_ypad, want_delta):
+    if isinstance(ctx.link, SplitGradLink):
+        parts = ctx.link.take()
+        if parts is not None:
+            if grad_y is not None or grad_ypad is not None:
+                raise RuntimeError("add_rmsnorm: y has a consumer besides the linked GEMM; a "
+                                   "SplitGradLink requires y to feed that node alone")
+            return _launch_bwd_parts(x_or_s, rstd, weight, grad_s, parts, want_delta)
+        return _launch_bwd(x_or_s, rstd, weight, pad_idx, grad_s, grad_y, grad_ypad, want_delta)
     factors = ctx.link.take() if ctx.link is not None else None
     if factors is not None:
         if grad_ypad is not None:
@@ -184,7 +233,9 @@ def add_rmsnorm(x, delta, weight, eps, pad_idx=None, padded_rows=0, zero_padding
     """Returns (s, y16, ypad32); with delta=None, s is x itself (reference: rmsnorm.py:152-158).
     zero_padding=False leaves the rows of ypad that pad_idx does not name unwritten (for a
     caller that never reads them). `link` (a LoraGradLink shared with the lora_pair call that
-    reads ypad, and ypad's only consumer) lets the backward form ypad's gradient itself."""
+    reads ypad, and ypad's only consumer) lets the backward form ypad's gradient itself; a
+    SplitGradLink shared with the layer_mlp call that alone reads y lets it sum y's K-split
+    gradient partials."""
     x = x.contiguous()
     ypad = None
     if pad_idx is not None and not zero_padding:
