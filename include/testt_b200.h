@@ -441,6 +441,18 @@ int tb_head_merge(const float *part, const int64_t *part_idx, const int64_t *tar
  * as a stable partition): order[i] is the row at sorted place i, labelled rows (target !=
  * ignore_index) first, each group in row order; targets_sorted[i] = targets[order[i]]. One
  * launch (one CTA), no host synchronisation. */
+/* The token embedding of the real tokens: out[r] = fp32(table[ids[pos_idx[r]]]) (the fused path
+ * of solution/model.py:220-225: index_select of the ids, the embedding gather and the cast to the
+ * fp32 residual stream in one launch). ids int64 [slots] (the padded batch, flattened); table
+ * fp16 [vocab, hidden], hidden a multiple of 8, table and out 16-byte aligned. An id outside
+ * [0, vocab) reads nothing: its row is written as zeros and counted (tb_embed_invalid_ids). */
+int tb_embed_rows(const int64_t *ids, const int64_t *pos_idx, const uint16_t *table, float *out,
+                  int64_t rows, int64_t hidden, int64_t vocab, void *stream);
+
+/* Token ids tb_embed_rows found outside [0, vocab) since the library was loaded (-1 when the
+ * counter cannot be read). */
+int64_t tb_embed_invalid_ids(void);
+
 int tb_head_order(const int64_t *targets, int64_t rows, int64_t ignore_index, int64_t *order,
                   int64_t *targets_sorted, void *stream);
 

@@ -55,11 +55,13 @@ SIGNATURES = {
     "tb_head_partials": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _P],
     "tb_head_merge": [_P, _P, _P, _I64, _I32, _I32, _P, _P, _P, _P, _P],
     "tb_head_order": [_P, _I64, _I64, _P, _P, _P],
+    "tb_embed_rows": [_P, _P, _P, _P, _I64, _I64, _I64, _P],
     "tb_head_unsort": [_P, _I64, _I64, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P],
     "tb_head_fold": [_P, _P, _I64, _I32, _I64, _I32, _P, _P, _P],
     "tb_head_dlogits": [_P, _P, _P, _I64, _I64, _I64, _I64, _F, _P],
     "tb_wait_timeouts": [_I32, _P],
     "tb_launch_count": [],
+    "tb_embed_invalid_ids": [],
     "tb_wait_selftest": [_I32, _I32, _P, _P],
     "tb_head_stats_grad_noalloc": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _F, _P],
     "tb_head_logits_stats": [_P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _P],
@@ -82,7 +84,8 @@ SIGNATURES = {
 # return types other than int (0 or a negative TB_E* code)
 RESTYPES = {"tb_nf4_gemm_workspace": ctypes.c_int64,
             "tb_nf4_gemm_qkv_rope_workspace": ctypes.c_int64,
-            "tb_head_dh_workspace": ctypes.c_int64, "tb_launch_count": ctypes.c_int64}
+            "tb_head_dh_workspace": ctypes.c_int64, "tb_launch_count": ctypes.c_int64,
+            "tb_embed_invalid_ids": ctypes.c_int64}
 
 _lib = None
 _calls = 0

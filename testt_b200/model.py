@@ -35,6 +35,7 @@ import threading
 
 import torch
 
+from . import _lib
 from . import attention as _own_attn
 from . import fused_layer as _fused_layer
 from .head import IGNORE_INDEX, fused_head_loss
@@ -43,6 +44,23 @@ from .nf4 import LayerWeights, layer_linear
 from .rmsnorm import LoraGradLink, SplitGradLink, add_rmsnorm
 from .lora import lora_pair
 from .rope import rope_pack, rope_tokens, slot_index
+
+def embed_rows(input_ids, pos_idx, table):
+    """fp32 [rows, hidden]: the embedding of the real tokens (input_ids flattened, at pos_idx),
+    one tb_embed_rows launch for an fp16 table whose rows are 16-byte vectors; else PyTorch's
+    index_select + embedding + cast (reference: solution/model.py:220-225)."""
+    ids = input_ids.reshape(-1)
+    rows, (vocab, hidden) = pos_idx.numel(), table.shape
+    if table.dtype == torch.float16 and table.is_contiguous() and hidden % 8 == 0 and \
+            table.data_ptr() % 16 == 0 and ids.dtype == torch.int64 and \
+            pos_idx.dtype == torch.int64:
+        ids = ids.contiguous()
+        out = torch.empty((rows, hidden), dtype=torch.float32, device=table.device)
+        _lib.call("tb_embed_rows", _lib.ptr(ids), _lib.ptr(pos_idx.contiguous()), _lib.ptr(table),
+                  _lib.ptr(out), rows, hidden, vocab, _lib.stream_of(out))
+        return out
+    return torch.nn.functional.embedding(ids.index_select(0, pos_idx), table).float()
+
 
 def _varlen_attn(q, k, v, cu_seqlens, max_len, scale):
     """Causal attention over the packed sequences of cu_seqlens (token-major q, k, v): this
@@ -339,8 +357,7 @@ def fused_forward(causal_lm, input_ids, attention_mask, labels, num_items_in_bat
 
     # Embeddings of the real tokens (the table may be held in fp16 with exact values, see
     # trainer_patch.prepare_model); the residual stream is fp32.
-    ids = input_ids.reshape(-1).index_select(0, pos_idx)
-    s = torch.nn.functional.embedding(ids, plan.embed.weight).float()
+    s = embed_rows(input_ids, pos_idx, plan.embed.weight)
 
     shape_ref = s.new_empty((1, 1, 1)).expand(batch, seq, plan.hidden)
     position_ids = torch.arange(seq, device=dev).unsqueeze(0)
