@@ -290,7 +290,34 @@ __global__ void head_merge_kernel(const float *__restrict__ part,
   Online o{-CUDART_INF_F, 0.f, 0.f, -CUDART_INF_F, 0x7fffffffffffffffLL};
   float zt = 0.f, found = 0.f;
   const int n = n_groups * splits;
-  for (int p = lane; p < n; p += 32) {
+  // a lane merges states lane, lane + 32, ... in that order; four states' loads are issued
+  // before they are merged (a row has hundreds of states: one load round trip per state made
+  // this a chain of latencies)
+  constexpr int kAhead = 4;
+  int p = lane;
+  for (; p + 32 * (kAhead - 1) < n; p += 32 * kAhead) {
+    Online b[kAhead];
+    float zq[kAhead], fq[kAhead];
+#pragma unroll
+    for (int k = 0; k < kAhead; ++k) {
+      const int pk = p + 32 * k;
+      const int g = pk / splits, sp = pk - g * splits;
+      const int64_t at = ((int64_t)g * rows + row) * splits + sp;
+      const float *q = part + at * kPartFields;
+      b[k] = Online{__ldg(q), __ldg(q + 1), __ldg(q + 2), __ldg(q + 3), __ldg(part_idx + at)};
+      zq[k] = __ldg(q + 4);
+      fq[k] = __ldg(q + 5);
+    }
+#pragma unroll
+    for (int k = 0; k < kAhead; ++k) {
+      o = online_merge(o, b[k]);
+      if (fq[k] != 0.f && found == 0.f) {
+        zt = zq[k];
+        found = 1.f;
+      }
+    }
+  }
+  for (; p < n; p += 32) {
     const int g = p / splits, sp = p - g * splits;
     const int64_t at = ((int64_t)g * rows + row) * splits + sp;
     const float *q = part + at * kPartFields;
