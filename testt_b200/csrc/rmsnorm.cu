@@ -11,7 +11,6 @@
 // (IEEE sqrt and division); y = (s * rstd) * w. Backward: g = (dy + dypad) * w; n = s * rstd;
 // dx = (g - n * sum(g n) / H) * rstd + ds.
 #include <algorithm>
-#include <atomic>
 
 #include "common.cuh"
 
@@ -651,17 +650,14 @@ int launch_rms_lora(const RmsLoraArgs &a, int threads, cudaStream_t st) {
 // the row-loop kernel: its shared-memory ring (once per process: the attribute is the
 // function's), and one CTA per resident slot, at most one per row
 int launch_rms_lora_rows(const RmsLoraArgs &a, cudaStream_t st) {
-  static std::atomic<int> smem_set{0};
   const int threads = (int)((2 * (a.hidden / 8) + 31) / 32 * 32);  // two threads a chunk
   const size_t smem = (size_t)kRowStages * row_stage_bytes(threads);
-  if (smem_set.load(std::memory_order_acquire) == 0) {
-    if (cudaFuncSetAttribute(rmsnorm_bwd_lora_rows, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)((size_t)kRowStages * row_stage_bytes(2 * kRowsMaxChunks))) !=
-        cudaSuccess) {
-      (void)cudaGetLastError();
-      return set_error(TB_ELAUNCH, "add_rmsnorm_bwd_lora: shared memory attribute refused");
-    }
-    smem_set.store(1, std::memory_order_release);
+  // set on every call: the attribute belongs to the current device
+  if (cudaFuncSetAttribute(rmsnorm_bwd_lora_rows, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)((size_t)kRowStages * row_stage_bytes(2 * kRowsMaxChunks))) !=
+      cudaSuccess) {
+    (void)cudaGetLastError();
+    return set_error(TB_ELAUNCH, "add_rmsnorm_bwd_lora: shared memory attribute refused");
   }
   const int64_t grid = std::min<int64_t>(a.rows, resident_blocks(rmsnorm_bwd_lora_rows, threads, smem));
   return launch("add_rmsnorm_bwd_lora", rmsnorm_bwd_lora_rows, dim3((unsigned)grid), threads, smem,
